@@ -1,0 +1,56 @@
+"""Build and load the in-tree sm_100a extension (`_bdh_cuda`).
+
+The extension is compiled with nvcc for `sm_100a` only (tcgen05 / TMA / TMEM are
+architecture-specific features) into ``burn_dragon_b200/csrc/build`` so the shared
+object lives inside the repository tree. ``load()`` never silently falls back: the
+caller gets the compiled module or an exception.
+"""
+
+from __future__ import annotations
+
+import os
+import threading
+
+_LOCK = threading.Lock()
+_MOD = None
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+BUILD_DIR = os.path.join(CSRC, "build")
+
+SOURCES = ["bindings.cpp", "gemm_host.cu", "rowwise.cu"]
+
+NVCC_FLAGS = [
+    "-gencode=arch=compute_100a,code=sm_100a",
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "--expt-relaxed-constexpr",
+]
+if os.environ.get("BDH_PTXAS_VERBOSE"):
+    NVCC_FLAGS.append("-Xptxas=-v")
+
+
+def load(verbose: bool = False):
+    """Compile (if stale) and import the extension. Thread-safe, cached."""
+    global _MOD
+    if _MOD is not None:
+        return _MOD
+    with _LOCK:
+        if _MOD is not None:
+            return _MOD
+        # Pin the arch list so torch adds no -gencode flags of its own.
+        os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+        from torch.utils.cpp_extension import load as _load
+
+        os.makedirs(BUILD_DIR, exist_ok=True)
+        _MOD = _load(
+            name="_bdh_cuda",
+            sources=[os.path.join(CSRC, s) for s in SOURCES],
+            extra_cflags=["-O3", "-std=c++17"],
+            extra_cuda_cflags=NVCC_FLAGS,
+            extra_include_paths=[CSRC],
+            build_directory=BUILD_DIR,
+            verbose=verbose,
+        )
+        return _MOD

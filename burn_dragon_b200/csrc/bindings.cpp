@@ -1,0 +1,55 @@
+// bindings.cpp — Python bindings of the sm_100a extension `_bdh_cuda`.
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace bd {
+void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<int64_t> a_geom,
+          const at::Tensor& b, bool b_mn, std::vector<int64_t> b_geom, int64_t M, int64_t N, int64_t K,
+          int64_t Z1, int64_t Z2, int64_t splits, bool causal_skip, const at::Tensor& out0,
+          const c10::optional<at::Tensor>& out1, const c10::optional<at::Tensor>& aux0,
+          const c10::optional<at::Tensor>& aux1, int64_t ld, int64_t sz1, int64_t sz2, int64_t split_stride,
+          double alpha, double thr, const c10::optional<at::Tensor>& freq,
+          const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh, bool accumulate,
+          const at::Tensor& err);
+void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_t rows, int64_t D,
+            const at::Tensor& gamma, const at::Tensor& beta, double eps, const c10::optional<at::Tensor>& y32,
+            const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd);
+at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
+                  int64_t rows, int64_t D, const at::Tensor& gamma, int64_t remap_T, int64_t remap_H,
+                  const c10::optional<at::Tensor>& dx16, const c10::optional<at::Tensor>& dx32);
+void tail_fwd(const at::Tensor& partial, int64_t nsplit, int64_t split_stride, const at::Tensor& v, int64_t rows,
+              int64_t D, const at::Tensor& gamma, const at::Tensor& beta, double eps,
+              const c10::optional<at::Tensor>& m_out, const at::Tensor& vout32,
+              const c10::optional<at::Tensor>& vout16, const c10::optional<at::Tensor>& st);
+at::Tensor tail_bwd(const at::Tensor& gin, const at::Tensor& v, const at::Tensor& m, const at::Tensor& st,
+                    int64_t rows, int64_t D, const at::Tensor& gamma, const at::Tensor& beta, const at::Tensor& dm16,
+                    const at::Tensor& dv_res);
+void sum_rows(const at::Tensor& out, const c10::optional<at::Tensor>& base, const at::Tensor& p0, int64_t n0,
+              int64_t s0, const c10::optional<at::Tensor>& p1, int64_t n1, int64_t s1, int64_t total);
+void cross_entropy(const at::Tensor& logits, const at::Tensor& target, const c10::optional<at::Tensor>& mask,
+                   const at::Tensor& inv_count, int64_t rows, int64_t V, const at::Tensor& loss_rows,
+                   const at::Tensor& dlogits);
+void symmetrize(const at::Tensor& P, const at::Tensor& G, int64_t BH, int64_t T, int64_t H,
+                const c10::optional<at::Tensor>& log2_decay);
+void adamw(const at::Tensor& p, const at::Tensor& g, const at::Tensor& m, const at::Tensor& v,
+           const c10::optional<at::Tensor>& shadow, double lr, double b1, double b2, double eps, double wd,
+           double bc1, double bc2, const c10::optional<at::Tensor>& gscale);
+void grad_clip_coef(const at::Tensor& g, const at::Tensor& scratch3, double max_norm);
+void cast_bf16(const at::Tensor& x, const at::Tensor& y);
+}  // namespace bd
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "burn_dragon_b200 sm_100a kernels (tcgen05 GEMM engine + row kernels)";
+  m.def("gemm", &bd::gemm);
+  m.def("ln_fwd", &bd::ln_fwd);
+  m.def("ln_bwd", &bd::ln_bwd);
+  m.def("tail_fwd", &bd::tail_fwd);
+  m.def("tail_bwd", &bd::tail_bwd);
+  m.def("sum_rows", &bd::sum_rows);
+  m.def("cross_entropy", &bd::cross_entropy);
+  m.def("symmetrize", &bd::symmetrize);
+  m.def("adamw", &bd::adamw);
+  m.def("grad_clip_coef", &bd::grad_clip_coef);
+  m.def("cast_bf16", &bd::cast_bf16);
+}

@@ -1,0 +1,202 @@
+// gemm_host.cu — host side of the tcgen05 GEMM engine: TMA tensor-map encoding,
+// tile-grid sizing for a persistent launch over all SMs, and the instantiation table.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <vector>
+
+#include "gemm_sm100.cuh"
+
+namespace bd {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t st = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    TORCH_CHECK(st == cudaSuccess && q == cudaDriverEntryPointSuccess && ptr != nullptr,
+                "burn_dragon_b200: cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Operand geometry, in elements: a 4-D view (inner, outer, z1, z2) of bf16 memory.
+struct Geom {
+  int64_t inner, outer, outer_stride, z1c, z1s, z2c, z2s;
+  bool use_z1, use_z2;
+};
+
+Geom parse_geom(const std::vector<int64_t>& g) {
+  TORCH_CHECK(g.size() == 9, "operand geometry needs 9 entries");
+  return Geom{g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7] != 0, g[8] != 0};
+}
+
+CUtensorMap encode_map(const at::Tensor& t, const Geom& g, uint32_t box_inner, uint32_t box_outer) {
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, "GEMM operands must be bf16");
+  TORCH_CHECK(t.is_cuda(), "GEMM operands must be CUDA tensors");
+  const uintptr_t base = reinterpret_cast<uintptr_t>(t.data_ptr());
+  TORCH_CHECK(base % 16 == 0, "GEMM operand base must be 16-byte aligned");
+  auto chk16 = [](int64_t elems) {
+    TORCH_CHECK((elems * 2) % 16 == 0, "GEMM operand strides must be multiples of 16 bytes");
+  };
+  chk16(g.outer_stride);
+  TORCH_CHECK(g.inner % 8 == 0, "GEMM operand inner extent must be a multiple of 8 elements");
+  cuuint64_t dims[4] = {(cuuint64_t)g.inner, (cuuint64_t)g.outer, (cuuint64_t)(g.use_z1 ? g.z1c : 1),
+                        (cuuint64_t)(g.use_z2 ? g.z2c : 1)};
+  const int64_t fallback = ((g.outer * g.outer_stride * 2 + 15) / 16) * 16;
+  const int64_t s1 = g.outer_stride * 2;
+  const int64_t s2 = g.use_z1 ? g.z1s * 2 : fallback;
+  const int64_t s3 = g.use_z2 ? g.z2s * 2 : fallback;
+  if (g.use_z1) chk16(g.z1s);
+  if (g.use_z2) chk16(g.z2s);
+  cuuint64_t strides[3] = {(cuuint64_t)s1, (cuuint64_t)s2, (cuuint64_t)s3};
+  cuuint32_t box[4] = {box_inner, box_outer, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMap m;
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.data_ptr(), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  return m;
+}
+
+int num_sms(int dev) {
+  static int cached[64] = {0};
+  if (cached[dev] == 0) {
+    int n = 0;
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+void launch_one(const GemmParams& p, cudaStream_t stream, int dev) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, EPI>;
+  static bool attr_set[64] = {false};
+  if (!attr_set[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    attr_set[dev] = true;
+  }
+  const long long total = (long long)p.tiles_m * p.tiles_n * p.splits * p.Z1 * p.Z2;
+  const int grid = (int)std::min<long long>(total, num_sms(dev));
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+using LaunchFn = void (*)(const GemmParams&, cudaStream_t, int);
+
+struct Entry {
+  int bn;
+  bool a_mn, b_mn;
+  int epi;
+  LaunchFn fn;
+};
+
+#define BD_ENTRY(BN, AMN, BMN, EPI) Entry{BN, AMN, BMN, EPI, &launch_one<BN, AMN, BMN, EPI>}
+
+// Every (tile N, A major, B major, epilogue) combination the BDH stack uses.
+const Entry kTable[] = {
+    BD_ENTRY(256, false, false, EPI_BF16), BD_ENTRY(128, false, false, EPI_BF16),
+    BD_ENTRY(64, false, false, EPI_BF16), BD_ENTRY(256, false, true, EPI_BF16),
+    BD_ENTRY(64, false, true, EPI_BF16),
+    BD_ENTRY(256, false, false, EPI_F32), BD_ENTRY(128, false, false, EPI_F32),
+    BD_ENTRY(64, false, false, EPI_F32), BD_ENTRY(256, false, true, EPI_F32),
+    BD_ENTRY(128, false, true, EPI_F32), BD_ENTRY(64, false, true, EPI_F32),
+    BD_ENTRY(256, true, true, EPI_F32), BD_ENTRY(128, true, true, EPI_F32),
+    BD_ENTRY(64, true, true, EPI_F32), BD_ENTRY(256, true, false, EPI_F32),
+    BD_ENTRY(256, false, true, EPI_RELU_ROPE), BD_ENTRY(128, false, true, EPI_RELU_ROPE),
+    BD_ENTRY(64, false, true, EPI_RELU_ROPE),
+    BD_ENTRY(128, false, false, EPI_SCORES), BD_ENTRY(64, false, false, EPI_SCORES),
+    BD_ENTRY(256, false, true, EPI_GATE), BD_ENTRY(128, false, true, EPI_GATE),
+    BD_ENTRY(64, false, true, EPI_GATE),
+    BD_ENTRY(256, false, false, EPI_DEC_BWD), BD_ENTRY(128, false, false, EPI_DEC_BWD),
+    BD_ENTRY(64, false, false, EPI_DEC_BWD),
+    BD_ENTRY(256, false, true, EPI_DQ), BD_ENTRY(128, false, true, EPI_DQ),
+    BD_ENTRY(64, false, true, EPI_DQ),
+};
+
+}  // namespace
+
+// Generic entry: C[z1,z2] = epilogue(A[z1,z2] (M x K) * B[z1,z2]^T (N x K)).
+void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<int64_t> a_geom,
+          const at::Tensor& b, bool b_mn, std::vector<int64_t> b_geom, int64_t M, int64_t N, int64_t K,
+          int64_t Z1, int64_t Z2, int64_t splits, bool causal_skip, const at::Tensor& out0,
+          const c10::optional<at::Tensor>& out1, const c10::optional<at::Tensor>& aux0,
+          const c10::optional<at::Tensor>& aux1, int64_t ld, int64_t sz1, int64_t sz2, int64_t split_stride,
+          double alpha, double thr, const c10::optional<at::Tensor>& freq,
+          const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh,
+          bool accumulate, const at::Tensor& err) {
+  const Entry* hit = nullptr;
+  for (const Entry& en : kTable)
+    if (en.bn == bn && en.a_mn == a_mn && en.b_mn == b_mn && en.epi == epi) hit = &en;
+  TORCH_CHECK(hit != nullptr, "no GEMM instantiation for bn=", bn, " a_mn=", a_mn, " b_mn=", b_mn,
+              " epi=", epi);
+  TORCH_CHECK(M > 0 && N > 0 && K > 0 && Z1 > 0 && Z2 > 0 && splits > 0, "bad GEMM sizes");
+  TORCH_CHECK(N % 32 == 0, "GEMM N must be a multiple of 32");
+  TORCH_CHECK(ld % 8 == 0 && sz1 % 8 == 0 && sz2 % 8 == 0 && split_stride % 8 == 0,
+              "output strides must be multiples of 8 elements");
+  TORCH_CHECK(err.scalar_type() == at::kInt && err.is_cuda(), "err must be an int32 CUDA tensor");
+  const Geom ga = parse_geom(a_geom), gb = parse_geom(b_geom);
+  const int dev = a.get_device();
+  c10::cuda::CUDAGuard guard(dev);
+
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.ta = a_mn ? encode_map(a, ga, 64, 64) : encode_map(a, ga, 64, 128);
+  p.tb = b_mn ? encode_map(b, gb, 64, 64) : encode_map(b, gb, 64, (uint32_t)bn);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.Z1 = (int)Z1;
+  p.Z2 = (int)Z2;
+  p.tiles_m = (int)((M + 127) / 128);
+  p.tiles_n = (int)((N + bn - 1) / bn);
+  const int KB = (int)((K + 63) / 64);
+  p.kb_per_split = (KB + (int)splits - 1) / (int)splits;
+  p.splits = (KB + p.kb_per_split - 1) / p.kb_per_split;
+  TORCH_CHECK(p.splits == splits, "split-K count ", splits, " does not fit ", KB, " K-blocks");
+  p.a_z1 = ga.use_z1;
+  p.a_z2 = ga.use_z2;
+  p.b_z1 = gb.use_z1;
+  p.b_z2 = gb.use_z2;
+  p.causal_skip = causal_skip ? 1 : 0;
+  p.err = err.data_ptr<int>();
+  EpiParams& e = p.e;
+  e.out0 = out0.data_ptr();
+  e.out1 = out1 ? out1->data_ptr() : nullptr;
+  e.aux0 = aux0 ? reinterpret_cast<const __nv_bfloat16*>(aux0->data_ptr()) : nullptr;
+  e.aux1 = aux1 ? reinterpret_cast<const __nv_bfloat16*>(aux1->data_ptr()) : nullptr;
+  e.ld = ld;
+  e.sz1 = sz1;
+  e.sz2 = sz2;
+  e.split_stride = split_stride;
+  e.alpha = (float)alpha;
+  e.thr = (float)thr;
+  e.freq = freq ? freq->data_ptr<float>() : nullptr;
+  e.log2_decay = log2_decay ? log2_decay->data_ptr<float>() : nullptr;
+  e.T = (int)T;
+  e.pos0 = (int)pos0;
+  e.Nh = (int)Nh;
+  e.accumulate = accumulate ? 1 : 0;
+  if (epi == EPI_F32)
+    TORCH_CHECK(out0.scalar_type() == at::kFloat, "EPI_F32 output must be fp32");
+  else
+    TORCH_CHECK(out0.scalar_type() == at::kBFloat16, "bf16 epilogue output must be bf16");
+  if (epi == EPI_RELU_ROPE && e.freq) TORCH_CHECK(e.out1, "RoPE epilogue needs out1");
+  if (epi == EPI_GATE) TORCH_CHECK(e.aux0, "gate epilogue needs aux0 (x)");
+  if (epi == EPI_DEC_BWD) TORCH_CHECK(e.aux0 && e.aux1 && e.out1, "decoder backward epilogue needs x, yn, out1");
+  if (epi == EPI_DQ) TORCH_CHECK(e.aux0 && e.aux1, "dq epilogue needs dx_part and x");
+  hit->fn(p, at::cuda::getCurrentCUDAStream(dev).stream(), dev);
+}
+
+}  // namespace bd

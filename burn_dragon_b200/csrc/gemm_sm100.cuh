@@ -1,0 +1,256 @@
+// gemm_sm100.cuh — the one tensor-core engine every BDH contraction runs on.
+//
+// A persistent, warp-specialised tcgen05 GEMM for sm_100a:
+//   warp 0        : TMA producer (one elected lane) filling a STAGES-deep smem ring
+//   warp 1        : TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..9    : epilogue (two warps per TMEM lane quadrant, each owning half of the
+//                   tile's columns), reading fp32 accumulators with tcgen05.ld and
+//                   applying a fused, mode-specific epilogue before the global store.
+// Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the mainloop
+// of tile i+1. Tile M is 128, K-block 64 (one 128-byte swizzle atom of bf16), tile N is
+// a template parameter (64/128/256). A and B may each be K-major or MN-major in global
+// memory; TMA writes them into the canonical 128B-swizzled layouts that the smem
+// descriptors describe, so no operand is ever transposed in HBM.
+//
+// Batching: two batch coordinates (z1, z2) index the 4-D tensor maps of A and B (each
+// operand can ignore either coordinate, e.g. the value matrix V shared by all heads)
+// and the outputs through element strides. Split-K writes fp32 partials at
+// `split * split_stride`; the consumer reduces them.
+//
+// The reference computes these contractions as scalar FP32 CubeCL/WGSL kernels
+// (burn_dragon_kernel/src/relu_lowrank.wgsl:40-82, dense_causal_attention.wgsl:53-106)
+// or Burn library matmuls (burn_dragon_core/src/model/dragon/residual_stream.rs:309-321).
+#pragma once
+#include "sm100_ptx.cuh"
+
+namespace bd {
+
+enum EpiMode : int {
+  EPI_BF16 = 0,       // out0 = alpha*acc (bf16)
+  EPI_F32 = 1,        // out0 (+)= alpha*acc (fp32); split-K partials
+  EPI_RELU_ROPE = 2,  // x = relu(acc - thr) -> out0; q = rope(x, pos) -> out1
+  EPI_SCORES = 3,     // strictly-causal masked (and decayed) scores -> out0 (bf16)
+  EPI_GATE = 4,       // yn = relu(acc - thr) * x(aux0) -> out0 (bf16)
+  EPI_DEC_BWD = 5,    // acc = d(yn): dx_part -> out0, dy_pre -> out1 (aux0 = x, aux1 = yn)
+  EPI_DQ = 6,         // acc = d(q): dx_pre = (aux0 + rope^T(acc)) * [x(aux1) > 0] -> out0
+};
+
+struct EpiParams {
+  void* out0;
+  void* out1;
+  const __nv_bfloat16* aux0;
+  const __nv_bfloat16* aux1;
+  long long ld;            // row stride of outputs/aux (elements)
+  long long sz1, sz2;      // batch strides of outputs/aux (elements)
+  long long split_stride;  // split-K partial stride (elements)
+  float alpha;
+  float thr;
+  const float* freq;       // RoPE frequency per latent column (cycles / position), or null
+  const float* log2_decay; // per-z1 log2(gamma) for decayed scores, or null
+  int T;                   // rows per sequence (position = pos0 + row % T)
+  int pos0;
+  int Nh;                  // latent per head (column -> in-head index for RoPE)
+  int accumulate;          // EPI_F32: add into the existing output
+};
+
+struct alignas(64) GemmParams {
+  CUtensorMap ta;
+  CUtensorMap tb;
+  int M, N, K;
+  int Z1, Z2;
+  int tiles_m, tiles_n, splits, kb_per_split;
+  int a_z1, a_z2, b_z1, b_z2;  // does the operand's tensor map use z1 / z2?
+  int causal_skip;             // tiles with n0 >= m0 + 128 are zero tiles (no MMA)
+  int* err;
+  EpiParams e;
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int THREADS = 320;
+};
+
+struct TileCoord {
+  int z1, z2, split, m0, n0, kb0, kb1;
+  bool zero;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(const GemmParams& p, int t, int BN) {
+  TileCoord c;
+  int n_blk = t % p.tiles_n;
+  int r = t / p.tiles_n;
+  int m_blk = r % p.tiles_m;
+  r /= p.tiles_m;
+  c.split = r % p.splits;
+  r /= p.splits;
+  c.z1 = r % p.Z1;
+  c.z2 = r / p.Z1;
+  c.m0 = m_blk * 128;
+  c.n0 = n_blk * BN;
+  const int KB = (p.K + 63) / 64;
+  c.kb0 = c.split * p.kb_per_split;
+  c.kb1 = min(c.kb0 + p.kb_per_split, KB);
+  c.zero = (p.causal_skip && c.n0 >= c.m0 + 128) || (c.kb1 <= c.kb0);
+  return c;
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    __nv_bfloat162 h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[q * 8 + 2 * i], v[q * 8 + 2 * i + 1]);
+    d[q] = *reinterpret_cast<uint4*>(h);
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v)[32]) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u = s[q];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(h[i]);
+      v[q * 8 + 2 * i] = f.x;
+      v[q * 8 + 2 * i + 1] = f.y;
+    }
+  }
+}
+
+// cos/sin of the RoPE phase 2*pi*frac(pos*freq) (phase wrapped as in
+// burn_dragon_core/src/model/attention.rs:540-550), evaluated with CUDA's __sincosf on
+// the argument reduced to [-pi, pi).
+__device__ __forceinline__ void rope_cs(float pos, float freq, float& c, float& s) {
+  float raw = pos * freq;
+  float ph = (raw - floorf(raw)) * 6.283185307179586f;
+  if (ph > 3.14159265358979f) ph -= 6.283185307179586f;
+  __sincosf(ph, &s, &c);
+}
+
+// Apply the epilogue for one thread's 32 consecutive columns of one output row.
+// `row`, `col` are coordinates inside the (z1, z2) batch matrix.
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const TileCoord& tc,
+                                               float (&v)[32], int row, int col) {
+  const EpiParams& e = p.e;
+  if (row >= p.M || col >= p.N) return;
+  const long long off = (long long)tc.z2 * e.sz2 + (long long)tc.z1 * e.sz1 + (long long)row * e.ld + col;
+  if constexpr (EPI == EPI_F32) {
+    float* o = reinterpret_cast<float*>(e.out0) + off + (long long)tc.split * e.split_stride;
+    float4* o4 = reinterpret_cast<float4*>(o);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 w = make_float4(e.alpha * v[4 * q], e.alpha * v[4 * q + 1], e.alpha * v[4 * q + 2],
+                             e.alpha * v[4 * q + 3]);
+      if (e.accumulate) {
+        float4 old = o4[q];
+        w.x += old.x; w.y += old.y; w.z += old.z; w.w += old.w;
+      }
+      o4[q] = w;
+    }
+    return;
+  } else {
+    if constexpr (EPI == EPI_BF16) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] *= e.alpha;
+    } else if constexpr (EPI == EPI_RELU_ROPE) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i] - e.thr, 0.0f);
+    } else if constexpr (EPI == EPI_SCORES) {
+      const float l2g = e.log2_decay ? e.log2_decay[tc.z1] : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int c = col + i;
+        float w = (c < row) ? v[i] : 0.0f;
+        if (e.log2_decay && c < row) w *= exp2f((float)(row - c) * l2g);
+        v[i] = w;
+      }
+    } else if constexpr (EPI == EPI_GATE) {
+      float xv[32];
+      load_bf16x32(e.aux0 + off, xv);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i] - e.thr, 0.0f) * xv[i];
+    } else if constexpr (EPI == EPI_DEC_BWD) {
+      float xv[32], yv[32], dy[32];
+      load_bf16x32(e.aux0 + off, xv);
+      load_bf16x32(e.aux1 + off, yv);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float g = v[i];
+        const float y = (xv[i] > 0.0f) ? __fdividef(yv[i], xv[i]) : 0.0f;
+        dy[i] = (yv[i] > 0.0f) ? g * xv[i] : 0.0f;
+        v[i] = g * y;
+      }
+      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(e.out1) + off, dy);
+    } else if constexpr (EPI == EPI_DQ) {
+      float base[32], xv[32];
+      load_bf16x32(e.aux0 + off, base);
+      load_bf16x32(e.aux1 + off, xv);
+      if (e.freq) {
+        const float pos = (float)(e.pos0 + row);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float c, s;
+          rope_cs(pos, e.freq[col + i], c, s);
+          const float ge = v[i], go = v[i + 1];
+          v[i] = ge * c + go * s;
+          v[i + 1] = go * c - ge * s;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = (xv[i] > 0.0f) ? (v[i] + base[i]) : 0.0f;
+    }
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(e.out0) + off;
+    store_bf16x32(o, v);
+    if constexpr (EPI == EPI_RELU_ROPE) {
+      if (e.freq) {
+        const float pos = (float)(e.pos0 + row % e.T);
+        const int j0 = col % e.Nh;
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float c, s;
+          rope_cs(pos, e.freq[j0 + i], c, s);
+          const float xe = v[i], xo = v[i + 1];
+          v[i] = xe * c - xo * s;
+          v[i + 1] = xo * c + xe * s;
+        }
+        store_bf16x32(reinterpret_cast<__nv_bfloat16*>(e.out1) + off, v);
+      }
+    }
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_zero_chunk(const GemmParams& p, const TileCoord& tc,
+                                                    int row, int col) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+  if (row >= p.M || col >= p.N) return;
+  const EpiParams& e = p.e;
+  const long long off = (long long)tc.z2 * e.sz2 + (long long)tc.z1 * e.sz1 + (long long)row * e.ld + col;
+  if constexpr (EPI == EPI_F32) {
+    if (e.accumulate) return;
+    float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out0) + off +
+                                           (long long)tc.split * e.split_stride);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    store_bf16x32(reinterpret_cast<__nv_bfloat16*>(e.out0) + off, v);
+  }
+}
+
+}  // namespace bd
+
+#include "gemm_sm100_kernel.cuh"

@@ -1,0 +1,199 @@
+// gemm_sm100_kernel.cuh — the persistent warp-specialised tcgen05 GEMM kernel body.
+// Included from gemm_sm100.cuh (parameter structs and epilogues live there).
+#pragma once
+
+namespace bd {
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t full_bar[STAGES];
+  __shared__ uint64_t empty_bar[STAGES];
+  __shared__ uint64_t tfull_bar[2];
+  __shared__ uint64_t tempty_bar[2];
+  __shared__ uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 8);
+    }
+    mbar_init(&drain_bar, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&p.ta);
+    tma_prefetch_desc(&p.tb);
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_s, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_s;
+
+  const int total = p.tiles_m * p.tiles_n * p.splits * p.Z1 * p.Z2;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const TileCoord tc = decode_tile(p, t, BN);
+        if (tc.zero) continue;
+        const int za1 = p.a_z1 ? tc.z1 : 0, za2 = p.a_z2 ? tc.z2 : 0;
+        const int zb1 = p.b_z1 ? tc.z1 : 0, zb2 = p.b_z2 ? tc.z2 : 0;
+        for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, &abort_flag, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * Cfg::A_BYTES;
+          uint8_t* b_dst = sB + stage * Cfg::B_BYTES;
+          const int k0 = kb * 64;
+          if constexpr (A_MN) {
+            tma_load_4d(a_dst, &p.ta, &full_bar[stage], tc.m0, k0, za1, za2);
+            tma_load_4d(a_dst + 8192, &p.ta, &full_bar[stage], tc.m0 + 64, k0, za1, za2);
+          } else {
+            tma_load_4d(a_dst, &p.ta, &full_bar[stage], k0, tc.m0, za1, za2);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i)
+              tma_load_4d(b_dst + i * 8192, &p.tb, &full_bar[stage], tc.n0 + 64 * i, k0, zb1, zb2);
+          } else {
+            tma_load_4d(b_dst, &p.tb, &full_bar[stage], k0, tc.n0, zb1, zb2);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: wait (bounded, ignoring the abort flag) for the loads still in flight.
+        int dummy_abort = 0;
+        const long long inflight = issued < STAGES ? issued : STAGES;
+        int s = stage;
+        uint32_t ph = phase;
+        for (long long i = 0; i < inflight; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait_bounded(&full_bar[s], ph, (volatile int*)&dummy_abort, p.err, kErrTimeoutDrain);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = make_idesc_bf16(128, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const TileCoord tc = decode_tile(p, t, BN);
+        if (tc.zero) continue;
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1, &abort_flag, p.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, &abort_flag, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = A_MN ? make_sdesc_sw128(a_base + kk * 2048, 8192, 1024)
+                                     : make_sdesc_sw128(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sdesc_sw128(b_base + kk * 2048, 8192, 1024)
+                                     : make_sdesc_sw128(b_base + kk * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb > tc.kb0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // Wait for every MMA this thread issued before TMEM can be released.
+      umma_commit(&drain_bar);
+      int dummy_abort = 0;
+      mbar_wait_bounded(&drain_bar, 0, (volatile int*)&dummy_abort, p.err, kErrTimeoutDrain);
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..9)
+    const int ew = warp - 2;    // 0..7
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int half = ew >> 2;   // column half of the tile
+    const int r_local = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const TileCoord tc = decode_tile(p, t, BN);
+      const int row = tc.m0 + r_local;
+      if (tc.zero) {
+        for (int c = 0; c < BN / 2; c += 32) epilogue_zero_chunk<EPI>(p, tc, row, tc.n0 + half * (BN / 2) + c);
+        continue;
+      }
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t t_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + half * (BN / 2);
+#pragma unroll 1
+      for (int c = 0; c < BN / 2; c += 32) {
+        float v[32];
+        tmem_ld32(t_addr + c, v);
+        epilogue_chunk<EPI>(p, tc, v, row, tc.n0 + half * (BN / 2) + c);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace bd

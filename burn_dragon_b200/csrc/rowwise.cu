@@ -1,0 +1,516 @@
+// rowwise.cu — memory-bound row kernels of the BDH step, one warp per row.
+//
+// LayerNorm here is the reference's shared `DragonNorm` (LayerNorm with gamma/beta,
+// eps 1e-5; burn_dragon_core/src/model/norm.rs:302-327). Each lane holds D/32 values
+// (lane-strided, so loads are coalesced); statistics are fp32.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_bf16.h>
+#include <torch/extension.h>
+
+namespace bd {
+namespace {
+
+constexpr int kWarps = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int VPL>
+__device__ __forceinline__ void ln_stats(const float (&x)[VPL], int D, float eps, float& mean, float& rstd) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) s += x[i];
+  mean = warp_sum(s) / D;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const float d = x[i] - mean;
+    q += d * d;
+  }
+  rstd = rsqrtf(warp_sum(q) / D + eps);
+}
+
+// dx of y = xhat*gamma + beta given dy; accumulates dgamma/dbeta lane partials.
+template <int VPL>
+__device__ __forceinline__ void ln_backward_row(const float (&g)[VPL], const float (&xhat)[VPL],
+                                                const float (&gam)[VPL], float rstd, int D, float (&dx)[VPL],
+                                                float (&dg)[VPL], float (&db)[VPL]) {
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const float gy = g[i] * gam[i];
+    s1 += gy;
+    s2 += gy * xhat[i];
+    dg[i] += g[i] * xhat[i];
+    db[i] += g[i];
+  }
+  s1 = warp_sum(s1) / D;
+  s2 = warp_sum(s2) / D;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) dx[i] = rstd * (g[i] * gam[i] - s1 - xhat[i] * s2);
+}
+
+// Reduce per-lane dgamma/dbeta partials over the block's warps and write one partial
+// row per block: part[block, 0, :] = dgamma, part[block, 1, :] = dbeta.
+template <int VPL>
+__device__ void block_write_partials(const float (&dg)[VPL], const float (&db)[VPL], int D, float* part) {
+  extern __shared__ float sh[];  // [kWarps][2][D]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    sh[(warp * 2 + 0) * D + lane + 32 * i] = dg[i];
+    sh[(warp * 2 + 1) * D + lane + 32 * i] = db[i];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < 2 * D; c += blockDim.x) {
+    const int which = c / D, col = c % D;
+    float s = 0.f;
+    for (int w = 0; w < kWarps; ++w) s += sh[(w * 2 + which) * D + col];
+    part[(size_t)blockIdx.x * 2 * D + c] = s;
+  }
+}
+
+// y = LN(x) for rows of x (fp32); optional fp32 / bf16 outputs and saved stats.
+// When `tokens` is given the row is gathered from an embedding table first.
+template <int VPL>
+__global__ void ln_fwd_kernel(const float* __restrict__ x, const int64_t* __restrict__ tokens, long long rows, int D,
+                              const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
+                              float* __restrict__ y32, __nv_bfloat16* __restrict__ y16, float* __restrict__ mean_out,
+                              float* __restrict__ rstd_out) {
+  const int lane = threadIdx.x % 32;
+  const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
+  if (row >= rows) return;
+  const float* src = tokens ? x + (size_t)tokens[row] * D : x + (size_t)row * D;
+  float v[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) v[i] = src[lane + 32 * i];
+  float mean, rstd;
+  ln_stats<VPL>(v, D, eps, mean, rstd);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    const float y = (v[i] - mean) * rstd * gamma[c] + beta[c];
+    if (y32) y32[(size_t)row * D + c] = y;
+    if (y16) y16[(size_t)row * D + c] = __float2bfloat16_rn(y);
+  }
+  if (lane == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
+// dx = LN^T(dy), with an optional output row remap: input row r = m*H + h with
+// m = b*T + t is written to row (b*H + h)*T + t (the [B,H,T,D] layout the attention
+// backward GEMMs read). Output bf16 and/or fp32.
+template <int VPL>
+__global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                              const float* __restrict__ mean_in, const float* __restrict__ rstd_in, long long rows,
+                              int D, const float* __restrict__ gamma, int remap_T, int remap_H,
+                              __nv_bfloat16* __restrict__ dx16, float* __restrict__ dx32, float* __restrict__ part) {
+  const int lane = threadIdx.x % 32;
+  float gam[VPL], dg[VPL], db[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    gam[i] = gamma[lane + 32 * i];
+    dg[i] = 0.f;
+    db[i] = 0.f;
+  }
+  for (long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32; row < rows;
+       row += (long long)gridDim.x * kWarps) {
+    float g[VPL], xh[VPL], dx[VPL];
+    const float mean = mean_in[row], rstd = rstd_in[row];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      g[i] = dy[(size_t)row * D + lane + 32 * i];
+      xh[i] = (x[(size_t)row * D + lane + 32 * i] - mean) * rstd;
+    }
+    ln_backward_row<VPL>(g, xh, gam, rstd, D, dx, dg, db);
+    long long orow = row;
+    if (remap_T > 0) {
+      const long long m = row / remap_H, h = row % remap_H;
+      const long long b = m / remap_T, t = m % remap_T;
+      orow = (b * remap_H + h) * remap_T + t;
+    }
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      if (dx16) dx16[(size_t)orow * D + lane + 32 * i] = __float2bfloat16_rn(dx[i]);
+      if (dx32) dx32[(size_t)orow * D + lane + 32 * i] = dx[i];
+    }
+  }
+  block_write_partials<VPL>(dg, db, D, part);
+}
+
+// Forward of the residual merge (burn_dragon_core/src/model/residual_stream.rs:511-535):
+//   m = sum_s partial[s]  (split-K / per-head partial products of yn @ E)
+//   u = LN(m);  v' = LN(v + u)
+// Saves m (fp32) and both LN statistics for the backward.
+template <int VPL>
+__global__ void tail_fwd_kernel(const float* __restrict__ partial, int nsplit, long long split_stride,
+                                const float* __restrict__ v, long long rows, int D, const float* __restrict__ gamma,
+                                const float* __restrict__ beta, float eps, float* __restrict__ m_out,
+                                float* __restrict__ vout32, __nv_bfloat16* __restrict__ vout16,
+                                float* __restrict__ st) {
+  const int lane = threadIdx.x % 32;
+  const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
+  if (row >= rows) return;
+  float m[VPL], z[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    float s = 0.f;
+    for (int k = 0; k < nsplit; ++k) s += partial[k * split_stride + (size_t)row * D + lane + 32 * i];
+    m[i] = s;
+    if (m_out) m_out[(size_t)row * D + lane + 32 * i] = s;
+  }
+  float mean1, rstd1, mean2, rstd2;
+  ln_stats<VPL>(m, D, eps, mean1, rstd1);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    z[i] = v[(size_t)row * D + c] + (m[i] - mean1) * rstd1 * gamma[c] + beta[c];
+  }
+  ln_stats<VPL>(z, D, eps, mean2, rstd2);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    const float y = (z[i] - mean2) * rstd2 * gamma[c] + beta[c];
+    vout32[(size_t)row * D + c] = y;
+    if (vout16) vout16[(size_t)row * D + c] = __float2bfloat16_rn(y);
+  }
+  if (lane == 0 && st) {
+    st[row * 4 + 0] = mean1;
+    st[row * 4 + 1] = rstd1;
+    st[row * 4 + 2] = mean2;
+    st[row * 4 + 3] = rstd2;
+  }
+}
+
+// Backward of the residual merge. g = d(v'). Writes dm (bf16, operand of the decoder
+// backward GEMMs) and dv_res = d(v) through the residual path (fp32).
+template <int VPL>
+__global__ void tail_bwd_kernel(const float* __restrict__ g_in, const float* __restrict__ v,
+                                const float* __restrict__ m_in, const float* __restrict__ st, long long rows, int D,
+                                const float* __restrict__ gamma, const float* __restrict__ beta,
+                                __nv_bfloat16* __restrict__ dm16, float* __restrict__ dv_res,
+                                float* __restrict__ part) {
+  const int lane = threadIdx.x % 32;
+  float gam[VPL], bet[VPL], dg[VPL], db[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    gam[i] = gamma[lane + 32 * i];
+    bet[i] = beta[lane + 32 * i];
+    dg[i] = 0.f;
+    db[i] = 0.f;
+  }
+  for (long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32; row < rows;
+       row += (long long)gridDim.x * kWarps) {
+    const float mean1 = st[row * 4 + 0], rstd1 = st[row * 4 + 1];
+    const float mean2 = st[row * 4 + 2], rstd2 = st[row * 4 + 3];
+    float g[VPL], mh[VPL], zh[VPL], dz[VPL], dm[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const size_t o = (size_t)row * D + lane + 32 * i;
+      g[i] = g_in[o];
+      mh[i] = (m_in[o] - mean1) * rstd1;
+      const float z = v[o] + mh[i] * gam[i] + bet[i];
+      zh[i] = (z - mean2) * rstd2;
+    }
+    ln_backward_row<VPL>(g, zh, gam, rstd2, D, dz, dg, db);
+    ln_backward_row<VPL>(dz, mh, gam, rstd1, D, dm, dg, db);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const size_t o = (size_t)row * D + lane + 32 * i;
+      dm16[o] = __float2bfloat16_rn(dm[i]);
+      dv_res[o] = dz[i];
+    }
+  }
+  block_write_partials<VPL>(dg, db, D, part);
+}
+
+// out[i] = base[i] (optional) + sum_k p0[k*s0 + i] + sum_k p1[k*s1 + i].
+__global__ void sum_rows_kernel(float* __restrict__ out, const float* __restrict__ base, const float* __restrict__ p0,
+                                int n0, long long s0, const float* __restrict__ p1, int n1, long long s1,
+                                long long total) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float s = base ? base[i] : 0.f;
+    for (int k = 0; k < n0; ++k) s += p0[k * s0 + i];
+    for (int k = 0; k < n1; ++k) s += p1[k * s1 + i];
+    out[i] = s;
+  }
+}
+
+// Per row: loss = logsumexp(z) - z[target]; dz = (softmax(z) - onehot) * w * inv_count,
+// w the optional loss mask (burn_dragon_core/src/model/dragon/language_head.rs:549-572).
+template <int VPL>
+__global__ void ce_kernel(const float* __restrict__ logits, const int64_t* __restrict__ target,
+                          const float* __restrict__ mask, const float* __restrict__ inv_count, long long rows, int V,
+                          float* __restrict__ loss_rows, __nv_bfloat16* __restrict__ dlogits) {
+  const int lane = threadIdx.x % 32;
+  const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
+  if (row >= rows) return;
+  float z[VPL];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    z[i] = logits[(size_t)row * V + lane + 32 * i];
+    mx = fmaxf(mx, z[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) s += expf(z[i] - mx);
+  s = warp_sum(s);
+  const float lse = mx + logf(s);
+  const int64_t tg = target[row];
+  const float w = mask ? mask[row] : 1.0f;
+  const float sc = w * inv_count[0];
+  float zt = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c == tg) zt = z[i];
+    const float pr = expf(z[i] - lse);
+    dlogits[(size_t)row * V + c] = __float2bfloat16_rn((pr - (c == tg ? 1.f : 0.f)) * sc);
+  }
+  zt = warp_sum(zt);
+  if (lane == 0) loss_rows[row] = (lse - zt) * w;
+}
+
+// G[i,j] = P[i,j]*g^(i-j) (j<i) + P[j,i]*g^(j-i) (j>i), 0 on the diagonal, per (b,h)
+// T x T block: dS + dS^T of the strictly-causal score matrix, the left factor of
+// dQ = (dS + dS^T) Q (the keys equal the queries).
+__global__ void symmetrize_kernel(const float* __restrict__ P, __nv_bfloat16* __restrict__ G, int T, int H,
+                                  const float* __restrict__ log2_decay) {
+  __shared__ float tile[32][33];
+  const int bh = blockIdx.z;
+  const float* Pb = P + (size_t)bh * T * T;
+  __nv_bfloat16* Gb = G + (size_t)bh * T * T;
+  const float l2g = log2_decay ? log2_decay[bh % H] : 0.f;
+  const int i0 = blockIdx.y * 32, j0 = blockIdx.x * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) tile[r][threadIdx.x] = Pb[(size_t)(j0 + r) * T + i0 + threadIdx.x];
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int i = i0 + r, j = j0 + threadIdx.x;
+    float val = 0.f;
+    if (j < i) {
+      val = Pb[(size_t)i * T + j];
+      if (log2_decay) val *= exp2f((float)(i - j) * l2g);
+    } else if (j > i) {
+      val = tile[threadIdx.x][r];
+      if (log2_decay) val *= exp2f((float)(j - i) * l2g);
+    }
+    Gb[(size_t)i * T + j] = __float2bfloat16_rn(val);
+  }
+}
+
+// AdamW (decoupled weight decay) over a flat fp32 buffer, optional device-side gradient
+// scale (clipping coefficient) and a bf16 shadow copy for the GEMMs.
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, long long n, float lr,
+                             float b1, float b2, float eps, float wd, float bc1, float bc2,
+                             const float* __restrict__ gscale) {
+  const float gs = gscale ? gscale[0] : 1.0f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float gi = g[i] * gs;
+    const float mi = b1 * m[i] + (1.f - b1) * gi;
+    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    float pi = p[i] * (1.f - lr * wd);
+    pi -= lr * (mi / bc1) / (sqrtf(vi / bc2) + eps);
+    p[i] = pi;
+    if (shadow) shadow[i] = __float2bfloat16_rn(pi);
+  }
+}
+
+__global__ void sumsq_kernel(const float* __restrict__ x, long long n, float* __restrict__ out) {
+  float s = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    s += x[i] * x[i];
+  s = warp_sum(s);
+  __shared__ float sh[32];
+  if (threadIdx.x % 32 == 0) sh[threadIdx.x / 32] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? sh[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) atomicAdd(out, t);
+  }
+}
+
+// [sumsq] -> [sumsq, norm, min(1, max_norm / (norm + 1e-6))]
+__global__ void clip_coef_kernel(float* s, float max_norm) {
+  const float norm = sqrtf(s[0]);
+  s[1] = norm;
+  s[2] = fminf(1.0f, max_norm / (norm + 1e-6f));
+}
+
+__global__ void cast_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = __float2bfloat16_rn(x[i]);
+}
+
+}  // namespace
+
+// ====================================================================== host wrappers
+namespace {
+
+cudaStream_t cur_stream(const at::Tensor& t) { return at::cuda::getCurrentCUDAStream(t.get_device()).stream(); }
+
+template <typename F>
+void dispatch_vpl(int D, F&& f) {
+  TORCH_CHECK(D % 32 == 0, "row width ", D, " must be a multiple of 32");
+  switch (D / 32) {
+    case 1: f(std::integral_constant<int, 1>{}); break;
+    case 2: f(std::integral_constant<int, 2>{}); break;
+    case 4: f(std::integral_constant<int, 4>{}); break;
+    case 8: f(std::integral_constant<int, 8>{}); break;
+    case 16: f(std::integral_constant<int, 16>{}); break;
+    case 32: f(std::integral_constant<int, 32>{}); break;
+    default: TORCH_CHECK(false, "row width ", D, " must be 32 * {1,2,4,8,16,32}");
+  }
+}
+
+template <typename T>
+T* opt_ptr(const c10::optional<at::Tensor>& t) {
+  return t ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+int part_blocks(long long rows) {
+  const long long need = (rows + kWarps - 1) / kWarps;
+  return (int)std::min<long long>(need, 148 * 8);
+}
+
+}  // namespace
+
+void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_t rows, int64_t D,
+            const at::Tensor& gamma, const at::Tensor& beta, double eps, const c10::optional<at::Tensor>& y32,
+            const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd) {
+  c10::cuda::CUDAGuard g(x.get_device());
+  const int blocks = (int)((rows + kWarps - 1) / kWarps);
+  dispatch_vpl((int)D, [&](auto vpl) {
+    ln_fwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(x)>>>(
+        x.data_ptr<float>(), tokens ? tokens->data_ptr<int64_t>() : nullptr, rows, (int)D, gamma.data_ptr<float>(),
+        beta.data_ptr<float>(), (float)eps, opt_ptr<float>(y32), opt_ptr<__nv_bfloat16>(y16), mean.data_ptr<float>(),
+        rstd.data_ptr<float>());
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Returns the [blocks, 2, D] dgamma/dbeta partials.
+at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
+                  int64_t rows, int64_t D, const at::Tensor& gamma, int64_t remap_T, int64_t remap_H,
+                  const c10::optional<at::Tensor>& dx16, const c10::optional<at::Tensor>& dx32) {
+  c10::cuda::CUDAGuard g(x.get_device());
+  const int blocks = part_blocks(rows);
+  auto part = at::empty({blocks, 2, D}, x.options().dtype(at::kFloat));
+  dispatch_vpl((int)D, [&](auto vpl) {
+    ln_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * 2 * D * sizeof(float), cur_stream(x)>>>(
+        dy.data_ptr<float>(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, (int)D,
+        gamma.data_ptr<float>(), (int)remap_T, (int)remap_H, opt_ptr<__nv_bfloat16>(dx16), opt_ptr<float>(dx32),
+        part.data_ptr<float>());
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return part;
+}
+
+void tail_fwd(const at::Tensor& partial, int64_t nsplit, int64_t split_stride, const at::Tensor& v, int64_t rows,
+              int64_t D, const at::Tensor& gamma, const at::Tensor& beta, double eps,
+              const c10::optional<at::Tensor>& m_out, const at::Tensor& vout32,
+              const c10::optional<at::Tensor>& vout16, const c10::optional<at::Tensor>& st) {
+  c10::cuda::CUDAGuard g(v.get_device());
+  const int blocks = (int)((rows + kWarps - 1) / kWarps);
+  dispatch_vpl((int)D, [&](auto vpl) {
+    tail_fwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(v)>>>(
+        partial.data_ptr<float>(), (int)nsplit, split_stride, v.data_ptr<float>(), rows, (int)D,
+        gamma.data_ptr<float>(), beta.data_ptr<float>(), (float)eps, opt_ptr<float>(m_out), vout32.data_ptr<float>(),
+        opt_ptr<__nv_bfloat16>(vout16), opt_ptr<float>(st));
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+at::Tensor tail_bwd(const at::Tensor& gin, const at::Tensor& v, const at::Tensor& m, const at::Tensor& st,
+                    int64_t rows, int64_t D, const at::Tensor& gamma, const at::Tensor& beta, const at::Tensor& dm16,
+                    const at::Tensor& dv_res) {
+  c10::cuda::CUDAGuard g(v.get_device());
+  const int blocks = part_blocks(rows);
+  auto part = at::empty({blocks, 2, D}, v.options().dtype(at::kFloat));
+  dispatch_vpl((int)D, [&](auto vpl) {
+    tail_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * 2 * D * sizeof(float), cur_stream(v)>>>(
+        gin.data_ptr<float>(), v.data_ptr<float>(), m.data_ptr<float>(), st.data_ptr<float>(), rows, (int)D,
+        gamma.data_ptr<float>(), beta.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dm16.data_ptr()),
+        dv_res.data_ptr<float>(), part.data_ptr<float>());
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return part;
+}
+
+void sum_rows(const at::Tensor& out, const c10::optional<at::Tensor>& base, const at::Tensor& p0, int64_t n0,
+              int64_t s0, const c10::optional<at::Tensor>& p1, int64_t n1, int64_t s1, int64_t total) {
+  c10::cuda::CUDAGuard g(out.get_device());
+  sum_rows_kernel<<<148 * 4, 256, 0, cur_stream(out)>>>(out.data_ptr<float>(), opt_ptr<const float>(base),
+                                                        p0.data_ptr<float>(), (int)n0, s0, opt_ptr<const float>(p1),
+                                                        (int)n1, s1, total);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void cross_entropy(const at::Tensor& logits, const at::Tensor& target, const c10::optional<at::Tensor>& mask,
+                   const at::Tensor& inv_count, int64_t rows, int64_t V, const at::Tensor& loss_rows,
+                   const at::Tensor& dlogits) {
+  c10::cuda::CUDAGuard g(logits.get_device());
+  const int blocks = (int)((rows + kWarps - 1) / kWarps);
+  dispatch_vpl((int)V, [&](auto vpl) {
+    ce_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(logits)>>>(
+        logits.data_ptr<float>(), target.data_ptr<int64_t>(), opt_ptr<const float>(mask), inv_count.data_ptr<float>(),
+        rows, (int)V, loss_rows.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dlogits.data_ptr()));
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void symmetrize(const at::Tensor& P, const at::Tensor& G, int64_t BH, int64_t T, int64_t H,
+                const c10::optional<at::Tensor>& log2_decay) {
+  c10::cuda::CUDAGuard g(P.get_device());
+  TORCH_CHECK(T % 32 == 0, "symmetrize needs T % 32 == 0");
+  dim3 grid((unsigned)(T / 32), (unsigned)(T / 32), (unsigned)BH);
+  symmetrize_kernel<<<grid, dim3(32, 8), 0, cur_stream(P)>>>(
+      P.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(G.data_ptr()), (int)T, (int)H,
+      opt_ptr<const float>(log2_decay));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void adamw(const at::Tensor& p, const at::Tensor& g, const at::Tensor& m, const at::Tensor& v,
+           const c10::optional<at::Tensor>& shadow, double lr, double b1, double b2, double eps, double wd,
+           double bc1, double bc2, const c10::optional<at::Tensor>& gscale) {
+  c10::cuda::CUDAGuard gd(p.get_device());
+  adamw_kernel<<<148 * 8, 256, 0, cur_stream(p)>>>(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
+                                                   v.data_ptr<float>(), opt_ptr<__nv_bfloat16>(shadow), p.numel(),
+                                                   (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
+                                                   (float)bc1, (float)bc2, opt_ptr<const float>(gscale));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Writes [sumsq, norm, clip_coef] into `scratch3` (3 floats).
+void grad_clip_coef(const at::Tensor& g, const at::Tensor& scratch3, double max_norm) {
+  c10::cuda::CUDAGuard gd(g.get_device());
+  C10_CUDA_CHECK(cudaMemsetAsync(scratch3.data_ptr(), 0, sizeof(float), cur_stream(g)));
+  sumsq_kernel<<<148 * 4, 256, 0, cur_stream(g)>>>(g.data_ptr<float>(), g.numel(), scratch3.data_ptr<float>());
+  clip_coef_kernel<<<1, 1, 0, cur_stream(g)>>>(scratch3.data_ptr<float>(), (float)max_norm);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void cast_bf16(const at::Tensor& x, const at::Tensor& y) {
+  c10::cuda::CUDAGuard gd(x.get_device());
+  cast_bf16_kernel<<<148 * 8, 256, 0, cur_stream(x)>>>(x.data_ptr<float>(),
+                                                       reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), x.numel());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace bd
