@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "gemm_sm100.cuh"
+#include "gemm_table.h"
 
 namespace bd {
 
@@ -78,53 +79,21 @@ int num_sms(int dev) {
   return cached[dev];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
-void launch_one(const GemmParams& p, cudaStream_t stream, int dev) {
-  using Cfg = GemmCfg<BN>;
-  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, EPI>;
-  static bool attr_set[64] = {false};
-  if (!attr_set[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    attr_set[dev] = true;
-  }
-  const long long total = (long long)p.tiles_m * p.tiles_n * p.splits * p.Z1 * p.Z2;
-  const int grid = (int)std::min<long long>(total, num_sms(dev));
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}  // namespace
+
+int num_sms_of(int dev) { return num_sms(dev); }
+
+namespace {
+const Entry* find_entry(int bn, bool a_mn, bool b_mn, int epi) {
+  const Entry* tables[3] = {kGemmTableA, kGemmTableB, kGemmTableC};
+  const int sizes[3] = {kGemmTableASize, kGemmTableBSize, kGemmTableCSize};
+  for (int t = 0; t < 3; ++t)
+    for (int i = 0; i < sizes[t]; ++i) {
+      const Entry& en = tables[t][i];
+      if (en.bn == bn && en.a_mn == a_mn && en.b_mn == b_mn && en.epi == epi) return &en;
+    }
+  return nullptr;
 }
-
-using LaunchFn = void (*)(const GemmParams&, cudaStream_t, int);
-
-struct Entry {
-  int bn;
-  bool a_mn, b_mn;
-  int epi;
-  LaunchFn fn;
-};
-
-#define BD_ENTRY(BN, AMN, BMN, EPI) Entry{BN, AMN, BMN, EPI, &launch_one<BN, AMN, BMN, EPI>}
-
-// Every (tile N, A major, B major, epilogue) combination the BDH stack uses.
-const Entry kTable[] = {
-    BD_ENTRY(256, false, false, EPI_BF16), BD_ENTRY(128, false, false, EPI_BF16),
-    BD_ENTRY(64, false, false, EPI_BF16), BD_ENTRY(256, false, true, EPI_BF16),
-    BD_ENTRY(64, false, true, EPI_BF16),
-    BD_ENTRY(256, false, false, EPI_F32), BD_ENTRY(128, false, false, EPI_F32),
-    BD_ENTRY(64, false, false, EPI_F32), BD_ENTRY(256, false, true, EPI_F32),
-    BD_ENTRY(128, false, true, EPI_F32), BD_ENTRY(64, false, true, EPI_F32),
-    BD_ENTRY(256, true, true, EPI_F32), BD_ENTRY(128, true, true, EPI_F32),
-    BD_ENTRY(64, true, true, EPI_F32), BD_ENTRY(256, true, false, EPI_F32),
-    BD_ENTRY(256, false, true, EPI_RELU_ROPE), BD_ENTRY(128, false, true, EPI_RELU_ROPE),
-    BD_ENTRY(64, false, true, EPI_RELU_ROPE),
-    BD_ENTRY(128, false, false, EPI_SCORES), BD_ENTRY(64, false, false, EPI_SCORES),
-    BD_ENTRY(256, false, true, EPI_GATE), BD_ENTRY(128, false, true, EPI_GATE),
-    BD_ENTRY(64, false, true, EPI_GATE),
-    BD_ENTRY(256, false, false, EPI_DEC_BWD), BD_ENTRY(128, false, false, EPI_DEC_BWD),
-    BD_ENTRY(64, false, false, EPI_DEC_BWD),
-    BD_ENTRY(256, false, true, EPI_DQ), BD_ENTRY(128, false, true, EPI_DQ),
-    BD_ENTRY(64, false, true, EPI_DQ),
-};
-
 }  // namespace
 
 // Generic entry: C[z1,z2] = epilogue(A[z1,z2] (M x K) * B[z1,z2]^T (N x K)).
@@ -136,9 +105,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           double alpha, double thr, const c10::optional<at::Tensor>& freq,
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh,
           bool accumulate, const at::Tensor& err) {
-  const Entry* hit = nullptr;
-  for (const Entry& en : kTable)
-    if (en.bn == bn && en.a_mn == a_mn && en.b_mn == b_mn && en.epi == epi) hit = &en;
+  const Entry* hit = find_entry((int)bn, a_mn, b_mn, (int)epi);
   TORCH_CHECK(hit != nullptr, "no GEMM instantiation for bn=", bn, " a_mn=", a_mn, " b_mn=", b_mn,
               " epi=", epi);
   TORCH_CHECK(M > 0 && N > 0 && K > 0 && Z1 > 0 && Z2 > 0 && splits > 0, "bad GEMM sizes");
@@ -188,10 +155,11 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   e.pos0 = (int)pos0;
   e.Nh = (int)Nh;
   e.accumulate = accumulate ? 1 : 0;
-  if (epi == EPI_F32)
+  if (epi == EPI_F32) {
     TORCH_CHECK(out0.scalar_type() == at::kFloat, "EPI_F32 output must be fp32");
-  else
+  } else {
     TORCH_CHECK(out0.scalar_type() == at::kBFloat16, "bf16 epilogue output must be bf16");
+  }
   if (epi == EPI_RELU_ROPE && e.freq) TORCH_CHECK(e.out1, "RoPE epilogue needs out1");
   if (epi == EPI_GATE) TORCH_CHECK(e.aux0, "gate epilogue needs aux0 (x)");
   if (epi == EPI_DEC_BWD) TORCH_CHECK(e.aux0 && e.aux1 && e.out1, "decoder backward epilogue needs x, yn, out1");
