@@ -1,0 +1,293 @@
+"""Configuration: model hyper-parameters and the training TOML schema.
+
+The key names follow the reference's serde schema so a reference TOML file loads here:
+``DragonConfig`` (burn_dragon_core/src/model/config.rs:979-1063), ``FusedKernelConfig``
+(config.rs:51-85; it carries ``rope_theta``, ``relu_threshold``, ``rotary_embedding``),
+``DragonRandomScaffoldConfig`` (config.rs:884-962) and the language ``TrainingConfig``
+sections ``[dataset] [model] [training] [optimizer] [parallel] [generation]``
+(burn_dragon_language/src/config/train/schema.rs:1209-2224). ``extends = "base.toml"``
+inheritance and ordered ``--config`` overlays merge tables recursively, later files
+winning (burn_dragon_language/src/config/merge.rs:8-164). Keys this framework does not
+implement are kept in ``extras`` and reported once as a warning.
+"""
+
+from __future__ import annotations
+
+import copy
+import dataclasses
+import math
+import os
+import tomllib
+import warnings
+from dataclasses import dataclass, field
+from typing import Any
+
+ROTARY_KINDS = ("rope", "alibi", "pope")
+
+
+@dataclass
+class RandomScaffoldConfig:
+    """Frozen seeded projection + trainable low-rank adapter (config.rs:884-906)."""
+
+    enabled: bool = False
+    seed: int = 1337
+    distribution: str = "gaussian_clt12"  # or "rademacher"
+    rank: int = 8
+    alpha: float = 16.0
+    scaling: str = "standard"  # or "rank_stabilized"
+    trainable_gain: bool = True
+
+    def adapter_scale(self) -> float:
+        if self.scaling == "rank_stabilized":
+            return self.alpha / math.sqrt(self.rank)
+        return self.alpha / self.rank
+
+
+@dataclass
+class DragonConfig:
+    """BDH model hyper-parameters (defaults as in config.rs:1030-1063)."""
+
+    n_layer: int = 6
+    n_embd: int = 256
+    dropout: float = 0.1
+    n_head: int = 4
+    mlp_internal_dim_multiplier: int = 4
+    vocab_size: int = 256
+    n_expert: int = 1
+    tie_input_output_embeddings: bool = False
+    rollout_fast_steps_per_slow_step: int = 1
+    # FusedKernelConfig fields that change the math
+    rotary_embedding: str = "alibi"
+    rope_theta: float = 65536.0
+    relu_threshold: float = 0.0
+    alibi_slopes: list[float] | None = None
+    # DragonNorm
+    norm_eps: float = 1e-5
+    # initialization (SimpleNormal std, init.rs:10,810)
+    init_std: float = 0.02
+    # dense-score row chunk (sequence/config.rs)
+    dense_score_row_chunk: int = 512
+    random_scaffold: RandomScaffoldConfig = field(default_factory=RandomScaffoldConfig)
+
+    @property
+    def latent_total(self) -> int:
+        return self.mlp_internal_dim_multiplier * self.n_embd
+
+    @property
+    def latent_per_head(self) -> int:
+        total = self.latent_total
+        if total % self.n_head:
+            raise ValueError("latent size must be divisible by the number of heads")
+        return total // self.n_head
+
+    def validate(self) -> None:
+        if self.rotary_embedding not in ROTARY_KINDS:
+            raise ValueError(f"rotary_embedding must be one of {ROTARY_KINDS}")
+        if self.rollout_fast_steps_per_slow_step not in (1, 2, 4, 8, 16):
+            raise ValueError("rollout_fast_steps_per_slow_step must be one of [1, 2, 4, 8, 16]")
+        if self.rotary_embedding == "rope" and self.latent_per_head % 2:
+            raise ValueError("RoPE needs an even latent per head")
+        _ = self.latent_per_head
+
+    def decay_slopes(self) -> list[float]:
+        """ALiBi slopes 1/2^(h/H) (burn_dragon_core/src/kernel/linear_attention.rs:149-160)."""
+        if self.alibi_slopes is not None:
+            return list(self.alibi_slopes)
+        return [1.0 / (2.0 ** (h / self.n_head)) for h in range(self.n_head)]
+
+    def uses_decay(self) -> bool:
+        return self.rotary_embedding == "alibi"
+
+    def param_count(self) -> int:
+        d, n, v = self.n_embd, self.latent_total, self.vocab_size
+        head = 0 if self.tie_input_output_embeddings else d * v
+        return 3 * d * n + v * d + head + 2 * d
+
+    @staticmethod
+    def bdh_gpu() -> "DragonConfig":
+        """BDH-GPU: d=256, n=32768, h=4, L=6, RoPE, byte vocab (the flagship config)."""
+        return DragonConfig(n_layer=6, n_embd=256, n_head=4, mlp_internal_dim_multiplier=128,
+                            dropout=0.0, rotary_embedding="rope")
+
+    @staticmethod
+    def tiny() -> "DragonConfig":
+        """Tiny CPU config: d=64, n=2048, h=4, L=2."""
+        return DragonConfig(n_layer=2, n_embd=64, n_head=4, mlp_internal_dim_multiplier=32,
+                            dropout=0.0, rotary_embedding="rope")
+
+
+@dataclass
+class OptimizerConfig:
+    name: str = "adamw"
+    learning_rate: float = 1e-3
+    weight_decay: float = 0.1
+    beta1: float = 0.9
+    beta2: float = 0.999
+    eps: float = 1e-8
+    grad_clip_norm: float | None = None
+    lr_schedule: dict[str, Any] = field(default_factory=lambda: {"type": "constant"})
+
+
+@dataclass
+class ParallelConfig:
+    mode: str = "single"  # single | ddp | fsdp | tensor_parallel_neuron | hybrid_2d | pipeline
+    world_size: int | None = None
+    data: dict[str, Any] = field(default_factory=dict)
+    tensor: dict[str, Any] = field(default_factory=dict)
+    pipeline: dict[str, Any] = field(default_factory=dict)
+    fsdp: dict[str, Any] = field(default_factory=dict)
+    checkpoint: dict[str, Any] = field(default_factory=dict)
+
+
+@dataclass
+class TrainingSection:
+    block_size: int = 512
+    batch_size: int = 32
+    max_iters: int = 1000
+    tbptt_chunk_size: int | None = None
+    tbptt_persist_across_steps: bool = False
+    sequence_batching: str = "random"  # random | streaming
+    gradient_accumulation_steps: int = 1
+    seed: int = 1337
+    log_frequency: int = 10
+    checkpoint_interval_iters: int | None = None
+    validation_interval_iters: int | None = None
+
+
+@dataclass
+class DatasetConfig:
+    type: str = "synthetic_bytes"
+    cache_dir: str = "data"
+    train_split_ratio: float = 0.9
+    path: str | None = None
+
+
+@dataclass
+class GenerationConfig:
+    max_tokens: int = 256
+    temperature: float = 1.0
+    top_k: int | None = None
+    device_buffer_tokens: int = 64
+
+
+@dataclass
+class TrainingConfig:
+    dataset: DatasetConfig = field(default_factory=DatasetConfig)
+    model: DragonConfig = field(default_factory=DragonConfig)
+    training: TrainingSection = field(default_factory=TrainingSection)
+    optimizer: OptimizerConfig = field(default_factory=OptimizerConfig)
+    parallel: ParallelConfig = field(default_factory=ParallelConfig)
+    generation: GenerationConfig = field(default_factory=GenerationConfig)
+    extras: dict[str, Any] = field(default_factory=dict)
+
+    def validate(self) -> None:
+        self.model.validate()
+        p = self.parallel.mode
+        if p not in ("single", "ddp", "fsdp", "tensor_parallel_neuron", "hybrid_2d", "pipeline"):
+            raise ValueError(f"unknown parallel.mode {p!r}")
+        if p == "pipeline" and self.training.tbptt_chunk_size:
+            raise ValueError("pipeline parallelism does not support TBPTT chunking")
+        if self.training.tbptt_persist_across_steps and self.training.sequence_batching != "streaming":
+            raise ValueError("tbptt_persist_across_steps requires sequence_batching = \"streaming\"")
+        if self.training.tbptt_chunk_size is not None:
+            if self.training.tbptt_chunk_size <= 0 or self.training.block_size % self.training.tbptt_chunk_size:
+                raise ValueError("tbptt_chunk_size must divide block_size")
+
+
+# ------------------------------------------------------------------ TOML loading
+
+
+def merge_tables(base: dict, overlay: dict) -> dict:
+    """Recursive table merge; overlay scalars and arrays replace base values."""
+    out = copy.deepcopy(base)
+    for k, v in overlay.items():
+        if isinstance(v, dict) and isinstance(out.get(k), dict):
+            out[k] = merge_tables(out[k], v)
+        else:
+            out[k] = copy.deepcopy(v)
+    return out
+
+
+def load_toml_with_extends(path: str, _seen: tuple[str, ...] = ()) -> dict:
+    path = os.path.abspath(path)
+    if path in _seen:
+        raise ValueError(f"circular extends: {' -> '.join(_seen + (path,))}")
+    with open(path, "rb") as f:
+        data = tomllib.load(f)
+    parent = data.pop("extends", None)
+    if parent is None:
+        return data
+    parents = parent if isinstance(parent, list) else [parent]
+    merged: dict = {}
+    for p in parents:
+        p_path = p if os.path.isabs(p) else os.path.join(os.path.dirname(path), p)
+        merged = merge_tables(merged, load_toml_with_extends(p_path, _seen + (path,)))
+    return merge_tables(merged, data)
+
+
+def _fill(cls, table: dict, extras: dict, prefix: str):
+    names = {f.name: f for f in dataclasses.fields(cls)}
+    kwargs = {}
+    for k, v in table.items():
+        if k in names:
+            f = names[k]
+            if dataclasses.is_dataclass(f.default_factory() if callable(f.default_factory) else None) \
+                    and isinstance(v, dict):
+                sub_cls = type(f.default_factory())
+                kwargs[k] = _fill(sub_cls, v, extras, f"{prefix}{k}.")
+            else:
+                kwargs[k] = v
+        else:
+            extras[f"{prefix}{k}"] = v
+    return cls(**kwargs)
+
+
+def _model_table(table: dict) -> dict:
+    """Flatten the reference's nested [model.fused_kernels] keys into DragonConfig fields."""
+    t = dict(table)
+    fk = t.pop("fused_kernels", None)
+    if isinstance(fk, dict):
+        for k in ("rope_theta", "relu_threshold", "alibi_slopes", "rotary_embedding"):
+            if k in fk:
+                t[k] = fk[k]
+    if "rotary_embedding" in t and isinstance(t["rotary_embedding"], str):
+        t["rotary_embedding"] = t["rotary_embedding"].lower()
+    if "latent_total" in t:
+        lt = t.pop("latent_total")
+        d = t.get("n_embd", DragonConfig.n_embd)
+        if lt % d:
+            raise ValueError("latent_total must be a multiple of n_embd")
+        t["mlp_internal_dim_multiplier"] = lt // d
+    return t
+
+
+def training_config_from_dict(data: dict) -> TrainingConfig:
+    extras: dict = {}
+    cfg = TrainingConfig()
+    for section, cls in (("dataset", DatasetConfig), ("training", TrainingSection),
+                         ("optimizer", OptimizerConfig), ("parallel", ParallelConfig),
+                         ("generation", GenerationConfig)):
+        if section in data:
+            setattr(cfg, section, _fill(cls, data[section], extras, f"{section}."))
+    if "model" in data:
+        cfg.model = _fill(DragonConfig, _model_table(data["model"]), extras, "model.")
+    for k, v in data.items():
+        if k not in ("dataset", "training", "optimizer", "parallel", "generation", "model"):
+            extras[k] = v
+    cfg.extras = extras
+    if extras:
+        warnings.warn(f"ignoring config keys not implemented here: {sorted(extras)}", stacklevel=2)
+    cfg.validate()
+    return cfg
+
+
+def load_training_config(paths: list[str] | str, overrides: dict | None = None) -> TrainingConfig:
+    """Load one or more TOML files (each may `extends` others), merged in order."""
+    if isinstance(paths, str):
+        paths = [paths]
+    merged: dict = {}
+    for p in paths:
+        merged = merge_tables(merged, load_toml_with_extends(p))
+    if overrides:
+        merged = merge_tables(merged, overrides)
+    return training_config_from_dict(merged)

@@ -1,0 +1,224 @@
+"""The BDH training step on the sm_100a kernels: forward, loss and hand-written backward.
+
+Every contraction of the shared-weight layer stack runs on the tcgen05 engine with its
+elementwise work fused into the epilogue; the row-wise LayerNorm / residual-merge /
+cross-entropy work runs in one-warp-per-row kernels. Activations of every layer are
+kept resident in HBM (about 3.4 GB per layer at BDH-GPU batch 32 x 512), so the backward
+recomputes nothing.
+
+Layouts (M = B*T token rows, N = H*Nh neurons):
+  v      [M, D]     fp32 residual stream (+ bf16 copy as GEMM operand)
+  x, q   [M, N]     bf16 relu(v Dx) and rope(x)  (column = h*Nh + j)
+  S      [B,H,T,T]  bf16 strictly-causal scores q q^T (zeros on and above the diagonal)
+  a      [M, H, D]  fp32 attention output before its LayerNorm; an = LN(a) in bf16
+  yn     [M, N]     bf16 x * relu(an Dy)
+Parameters keep the reference layouts: encoder / encoder_v [H, D, Nh], decoder [N, D],
+embed [V, D], lm_head [D, V] (burn_dragon_core/src/model/dragon.rs:240-272).
+
+Reference call stack mirrored: dragon/language_pipeline.rs:55-411 (embedding LN, layer
+loop), dragon/residual_stream.rs:323-572 (layer), dragon/language_head.rs:549-572 (CE).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import _ext
+from ..ops import gemm as G
+from ..ops.gemm import Operand
+from .reference import rope_freqs
+
+
+class FusedWorkspace:
+    """Activation and gradient buffers for one (B, T) shape, allocated once."""
+
+    def __init__(self, cfg, B: int, T: int, device: torch.device):
+        self.cfg = cfg
+        self.B, self.T = B, T
+        D, H, Nh, V = cfg.n_embd, cfg.n_head, cfg.latent_per_head, cfg.vocab_size
+        N, M, L = H * Nh, B * T, cfg.n_layer
+        self.D, self.H, self.Nh, self.N, self.M, self.L, self.V = D, H, Nh, N, M, L, V
+        if T % 128 or M % 128 or Nh % 64 or D % 32 or V % 32:
+            raise ValueError("fused BDH path needs T % 128 == 0, Nh % 64 == 0, D % 32 == 0, V % 32 == 0")
+        dev = device
+        f32, bf16 = torch.float32, torch.bfloat16
+        e = lambda *s, dt=f32: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
+        self.v32 = [e(M, D) for _ in range(L + 1)]
+        self.v16 = [e(M, D, dt=bf16) for _ in range(L + 1)]
+        self.x16 = [e(M, N, dt=bf16) for _ in range(L)]
+        self.q16 = [e(M, N, dt=bf16) for _ in range(L)] if cfg.rotary_embedding == "rope" else self.x16
+        self.S16 = [e(B, H, T, T, dt=bf16) for _ in range(L)]
+        self.a32 = [e(M, H, D) for _ in range(L)]
+        self.amean = [e(M * H) for _ in range(L)]
+        self.arstd = [e(M * H) for _ in range(L)]
+        self.an16 = [e(M, H, D, dt=bf16) for _ in range(L)]
+        self.yn16 = [e(M, N, dt=bf16) for _ in range(L)]
+        self.m32 = [e(M, D) for _ in range(L)]
+        self.tst = [e(M, 4) for _ in range(L)]
+        self.emb_rows = e(M, D)
+        self.emean, self.erstd = e(M), e(M)
+        self.logits = e(M, V)
+        self.dlogits16 = e(M, V, dt=bf16)
+        self.loss_rows = e(M)
+        self.inv_count = torch.full((1,), 1.0 / M, dtype=f32, device=dev)
+        # split-K for the decoder product (K = N is long, only M/128 output tiles)
+        kb = -(-N // 64)
+        tiles = -(-M // 128) * -(-D // G.pick_bn(D))
+        self.dec_splits = G.fit_splits(kb, max(1, -(-2 * 148 // tiles)))
+        self.partial = e(self.dec_splits, M, D)
+        # backward temporaries (shared across layers)
+        self.dx16 = e(M, N, dt=bf16)
+        self.dy16 = e(M, N, dt=bf16)
+        self.dm16 = e(M, D, dt=bf16)
+        self.dv_res = e(M, D)
+        self.dan32 = e(M, H, D)
+        self.dC16 = e(B, H, T, D, dt=bf16)
+        self.P32 = e(B, H, T, T)
+        self.G16 = e(B, H, T, T, dt=bf16)
+        self.dva32 = e(M, D)
+        self.dvx32 = e(H, M, D)
+        self.dv = [e(M, D), e(M, D)]
+        self.freq = rope_freqs(Nh, cfg.rope_theta, device=dev) if cfg.rotary_embedding == "rope" else None
+        if cfg.uses_decay():
+            g = torch.tensor(cfg.decay_slopes(), dtype=torch.float64)
+            self.log2_decay = (-g / math.log(2.0)).to(torch.float32).to(dev)  # log2(exp(-s))
+        else:
+            self.log2_decay = None
+        self.norm_parts: list[torch.Tensor] = []
+
+
+def _bn(n: int) -> int:
+    return G.pick_bn(n)
+
+
+class FusedBDH:
+    """Runs forward + CE + backward of the BDH stack for a fixed workspace."""
+
+    def __init__(self, cfg, ws: FusedWorkspace):
+        if cfg.dropout != 0.0:
+            raise ValueError("the fused path implements dropout = 0 (as the BDH-GPU profiles use)")
+        if cfg.tie_input_output_embeddings:
+            raise ValueError("the fused path needs an untied lm_head")
+        self.cfg = cfg
+        self.ws = ws
+        self.mod = _ext.load()
+
+    # ---------------------------------------------------------------- forward
+    def forward(self, p16: dict, p32: dict, tokens: torch.Tensor, pos0: int = 0) -> None:
+        ws, cfg, mod = self.ws, self.cfg, self.mod
+        B, T, D, H, Nh, N, M, L = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L
+        eps, thr = cfg.norm_eps, cfg.relu_threshold
+        tok = tokens.reshape(-1)
+        torch.index_select(p32["embed"], 0, tok, out=ws.emb_rows)
+        mod.ln_fwd(ws.emb_rows, None, M, D, p32["norm_gamma"], p32["norm_beta"], eps, ws.v32[0], ws.v16[0],
+                   ws.emean, ws.erstd)
+        enc, encv, dec = p16["encoder"], p16["encoder_v"], p16["decoder"]
+        B_enc = Operand(enc, True, Nh, D, Nh, z1=(H, D * Nh))
+        B_encv = Operand(encv, True, Nh, D, Nh, z1=(H, D * Nh))
+        B_dec = Operand(dec, True, D, N, D)
+        for l in range(L):
+            v16 = ws.v16[l]
+            # x = relu(v Dx - thr), q = rope(x)       (K = D)
+            G.gemm(G.EPI_RELU_ROPE, Operand(v16, False, D, M, D), B_enc, M, Nh, D, ws.x16[l], Z1=H,
+                   out1=ws.q16[l] if ws.freq is not None else None, ld=N, sz1=Nh, thr=thr, freq=ws.freq,
+                   T=T, pos0=pos0, Nh=Nh)
+            # S = tril_{-1}(q q^T) (* gamma^(i-j))      (K = Nh), upper tiles skipped
+            qop = Operand(ws.q16[l], False, Nh, T, N, z1=(H, Nh), z2=(B, T * N))
+            G.gemm(G.EPI_SCORES, qop, qop, T, T, Nh, ws.S16[l], Z1=H, Z2=B, bn=128 if T % 128 == 0 else 64,
+                   causal_skip=True, ld=T, sz1=T * T, sz2=H * T * T, log2_decay=ws.log2_decay)
+            # a = S V                                   (K = T), V shared by the heads
+            G.gemm(G.EPI_F32, Operand(ws.S16[l], False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
+                   Operand(v16, True, D, T, D, z2=(B, T * D)), T, D, T, ws.a32[l], Z1=H, Z2=B,
+                   ld=H * D, sz1=D, sz2=T * H * D)
+            mod.ln_fwd(ws.a32[l], None, M * H, D, p32["norm_gamma"], p32["norm_beta"], eps, None, ws.an16[l],
+                       ws.amean[l], ws.arstd[l])
+            # yn = relu(an Dy - thr) * x                (K = D)
+            G.gemm(G.EPI_GATE, Operand(ws.an16[l], False, D, M, H * D, z1=(H, D)), B_encv, M, Nh, D, ws.yn16[l],
+                   Z1=H, aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr)
+            # m = yn E (split-K partials), v' = LN(v + LN(m))
+            G.gemm(G.EPI_F32, Operand(ws.yn16[l], False, N, M, N), B_dec, M, D, N, ws.partial,
+                   splits=ws.dec_splits, ld=D, split_stride=M * D)
+            mod.tail_fwd(ws.partial, ws.dec_splits, M * D, ws.v32[l], M, D, p32["norm_gamma"], p32["norm_beta"],
+                         eps, ws.m32[l], ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
+        G.gemm(G.EPI_F32, Operand(ws.v16[L], False, D, M, D), Operand(p16["lm_head"], True, ws.V, D, ws.V),
+               M, ws.V, D, ws.logits, ld=ws.V)
+
+    def loss(self, targets: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
+        ws = self.ws
+        if mask is not None:
+            ws.inv_count.copy_(1.0 / mask.float().sum().clamp_min(1.0))
+            m = mask.reshape(-1).float().contiguous()
+        else:
+            ws.inv_count.fill_(1.0 / ws.M)
+            m = None
+        self.mod.cross_entropy(ws.logits, targets.reshape(-1), m, ws.inv_count, ws.M, ws.V, ws.loss_rows,
+                               ws.dlogits16)
+        return ws.loss_rows.sum() * ws.inv_count[0]
+
+    # ---------------------------------------------------------------- backward
+    def backward(self, p16: dict, p32: dict, g32: dict, tokens: torch.Tensor, pos0: int = 0) -> None:
+        """Writes parameter gradients into g32 (overwrites)."""
+        ws, cfg, mod = self.ws, self.cfg, self.mod
+        B, T, D, H, Nh, N, M, L, V = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L, ws.V
+        gam, bet = p32["norm_gamma"], p32["norm_beta"]
+        for k in ("encoder", "encoder_v", "decoder"):
+            g32[k].zero_()
+        parts = []
+        # lm head
+        G.gemm(G.EPI_F32, Operand(ws.v16[L], True, D, M, D), Operand(ws.dlogits16, True, V, M, V), D, V, M,
+               g32["lm_head"], ld=V)
+        dv = ws.dv[0]
+        G.gemm(G.EPI_F32, Operand(ws.dlogits16, False, V, M, V), Operand(p16["lm_head"], False, V, D, V), M, D, V,
+               dv, ld=D)
+        enc, encv, dec = p16["encoder"], p16["encoder_v"], p16["decoder"]
+        for l in reversed(range(L)):
+            v16 = ws.v16[l]
+            parts.append(mod.tail_bwd(dv, ws.v32[l], ws.m32[l], ws.tst[l], M, D, gam, bet, ws.dm16, ws.dv_res))
+            # d(yn) = dm E^T -> dx_part = d(yn)*y, dy_pre = d(yn)*x*[y>0]
+            G.gemm(G.EPI_DEC_BWD, Operand(ws.dm16, False, D, M, D), Operand(dec, False, D, N, D), M, N, D, ws.dx16,
+                   out1=ws.dy16, aux0=ws.x16[l], aux1=ws.yn16[l], ld=N)
+            # dE += yn^T dm
+            G.gemm(G.EPI_F32, Operand(ws.yn16[l], True, N, M, N), Operand(ws.dm16, True, D, M, D), N, D, M,
+                   g32["decoder"], ld=D, accumulate=True)
+            # dDy_h += an_h^T dy_h
+            G.gemm(G.EPI_F32, Operand(ws.an16[l], True, D, M, H * D, z1=(H, D)),
+                   Operand(ws.dy16, True, Nh, M, N, z1=(H, Nh)), D, Nh, M, g32["encoder_v"], Z1=H, ld=Nh,
+                   sz1=D * Nh, accumulate=True)
+            # d(an)_h = dy_h Dy_h^T
+            G.gemm(G.EPI_F32, Operand(ws.dy16, False, Nh, M, N, z1=(H, Nh)),
+                   Operand(encv, False, Nh, D, Nh, z1=(H, D * Nh)), M, D, Nh, ws.dan32, Z1=H, ld=H * D, sz1=D)
+            # dC = LN^T(d an), written as [B,H,T,D]
+            parts.append(mod.ln_bwd(ws.dan32, ws.a32[l], ws.amean[l], ws.arstd[l], M * H, D, gam, T, H, ws.dC16,
+                                    None))
+            # P = dC V^T ; G = mask(P) + mask(P)^T
+            dcop = Operand(ws.dC16, False, D, T, D, z1=(H, T * D), z2=(B, H * T * D))
+            G.gemm(G.EPI_F32, dcop, Operand(v16, False, D, T, D, z2=(B, T * D)), T, T, D, ws.P32, Z1=H, Z2=B,
+                   bn=128 if T % 128 == 0 else 64, ld=T, sz1=T * T, sz2=H * T * T)
+            mod.symmetrize(ws.P32, ws.G16, B * H, T, H, ws.log2_decay)
+            # dx_pre = (dx_part + rope^T(G q)) * [x > 0]   (in place over dx_part)
+            G.gemm(G.EPI_DQ, Operand(ws.G16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
+                   Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B,
+                   aux0=ws.dx16, aux1=ws.x16[l], ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh)
+            # dV = sum_h S_h^T dC_h  (K = (h, i))
+            G.gemm(G.EPI_F32, Operand(ws.S16[l], True, T, H * T, T, z2=(B, H * T * T)),
+                   Operand(ws.dC16, True, D, H * T, D, z2=(B, H * T * D)), T, D, H * T, ws.dva32, Z2=B, ld=D,
+                   sz2=T * D)
+            # dDx_h += v^T dx_h
+            G.gemm(G.EPI_F32, Operand(v16, True, D, M, D), Operand(ws.dx16, True, Nh, M, N, z1=(H, Nh)), D, Nh, M,
+                   g32["encoder"], Z1=H, ld=Nh, sz1=D * Nh, accumulate=True)
+            # dv_x per head = dx_h Dx_h^T
+            G.gemm(G.EPI_F32, Operand(ws.dx16, False, Nh, M, N, z1=(H, Nh)),
+                   Operand(enc, False, Nh, D, Nh, z1=(H, D * Nh)), M, D, Nh, ws.dvx32, Z1=H, ld=D, sz1=M * D)
+            dv_next = ws.dv[1] if dv is ws.dv[0] else ws.dv[0]
+            mod.sum_rows(dv_next, ws.dv_res, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)
+            dv = dv_next
+        # embedding LayerNorm and gather
+        demb = ws.dv_res  # reuse as fp32 [M, D] scratch
+        parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb))
+        g32["embed"].zero_()
+        g32["embed"].index_add_(0, tokens.reshape(-1), demb)
+        allp = torch.cat(parts, 0).sum(0)
+        g32["norm_gamma"].copy_(allp[0])
+        g32["norm_beta"].copy_(allp[1])

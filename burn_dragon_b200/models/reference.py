@@ -1,0 +1,167 @@
+"""Pure-PyTorch statement of the BDH math: the oracle every kernel is tested against,
+and the CPU execution path.
+
+Everything here follows the reference's own reference math:
+
+* linear attention, strictly causal, read-before-update recurrence
+  ``a_t = rho^T q_t ; rho <- (rho + q_t (x) v_t) * gamma``
+  (burn_dragon_core/src/model/sequence/linear.rs:18-60) and its dense-score form
+  ``S = tril_{-1}(Q Q^T) * gamma^(i-j)``, ``C = gamma^i Q rho0 + S V``,
+  ``rho_T = gamma^T rho0 + (Q * gamma^(T-i))^T V`` (linear.rs:105-430);
+* RoPE with frequencies ``theta^(-2 floor(i/2)/Nh) / 2pi``, wrapped phase
+  ``frac(pos*freq)*2pi`` and adjacent (even, odd) pairs (attention.rs:488-575);
+* the low-rank residual step (residual_stream.rs:323-572): x = relu(v W_x - thr),
+  a = LN(LinAttn(rope(x), v)), y = relu(a W_y - thr), yn = x*y, m = LN(yn_flat E),
+  v' = LN(v + m), with the single shared LayerNorm (norm.rs:302-327).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def rope_freqs(latent: int, theta: float, device=None, dtype=torch.float32) -> torch.Tensor:
+    """Per-column frequency in cycles per position (attention.rs:553-575)."""
+    idx = torch.arange(latent, dtype=torch.float64)
+    exponent = (torch.floor(idx / 2.0) * 2.0) / latent
+    f = 1.0 / torch.pow(torch.tensor(theta, dtype=torch.float64), exponent) / (2.0 * math.pi)
+    return f.to(dtype=torch.float32).to(device=device, dtype=dtype)
+
+
+def rope_phases(positions: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """phase[t, j] = frac(pos_t * f_j) * 2pi, computed in fp32 like the reference."""
+    raw = positions.to(torch.float32)[:, None] * freqs.to(torch.float32)[None, :]
+    return (raw - torch.floor(raw)) * (2.0 * math.pi)
+
+
+def rope_apply(x: torch.Tensor, phases: torch.Tensor) -> torch.Tensor:
+    """x * cos + rot(x) * sin with rot(x)[2i] = -x[2i+1], rot(x)[2i+1] = x[2i]."""
+    cos = torch.cos(phases).to(x.dtype)
+    sin = torch.sin(phases).to(x.dtype)
+    pairs = x.reshape(*x.shape[:-1], x.shape[-1] // 2, 2)
+    rot = torch.stack((-pairs[..., 1], pairs[..., 0]), dim=-1).reshape(x.shape)
+    return x * cos + rot * sin
+
+
+def decay_vector(slopes: list[float], device=None, dtype=torch.float32) -> torch.Tensor:
+    """gamma_h = exp(-slope_h)."""
+    return torch.exp(-torch.tensor(slopes, dtype=torch.float64)).to(device=device, dtype=dtype)
+
+
+def linear_attention_recurrent(q, v, rho0=None, decay=None):
+    """Time-step recurrence. q [B,H,T,N], v [B,1|H,T,D], rho0 [B,H,N,D], decay [H]."""
+    B, H, T, N = q.shape
+    D = v.shape[-1]
+    v = v.expand(B, H, T, D)
+    rho = rho0.clone() if rho0 is not None else q.new_zeros(B, H, N, D)
+    outs = []
+    g = decay.view(1, H, 1, 1) if decay is not None else None
+    for t in range(T):
+        qt = q[:, :, t, :]
+        outs.append(torch.einsum("bhn,bhnd->bhd", qt, rho))
+        rho = rho + qt[..., :, None] * v[:, :, t, None, :]
+        if g is not None:
+            rho = rho * g
+    return torch.stack(outs, dim=2), rho
+
+
+def _decay_powers(T: int, decay: torch.Tensor | None, device, dtype):
+    """Gamma matrix gamma^(i-j) for j<i (0 elsewhere), and the gamma^i / gamma^(T-i) vectors."""
+    i = torch.arange(T, device=device)
+    diff = (i[:, None] - i[None, :]).to(dtype)
+    mask = (i[None, :] < i[:, None]).to(dtype)
+    if decay is None:
+        return mask[None], None, None
+    lg = torch.log(decay.to(dtype))[:, None, None]  # [H,1,1]
+    gam = torch.exp(lg * diff[None]) * mask[None]
+    pow_i = torch.exp(torch.log(decay.to(dtype))[:, None] * i.to(dtype)[None, :])  # [H,T]
+    pow_ti = torch.exp(torch.log(decay.to(dtype))[:, None] * (T - i).to(dtype)[None, :])
+    return gam, pow_i, pow_ti
+
+
+def linear_attention_dense(q, v, rho0=None, decay=None, need_state: bool = True):
+    """Dense-score form (the reference's CUDA training executor)."""
+    B, H, T, N = q.shape
+    D = v.shape[-1]
+    v = v.expand(B, H, T, D)
+    gam, pow_i, pow_ti = _decay_powers(T, decay, q.device, q.dtype)
+    s = torch.matmul(q, q.transpose(-1, -2)) * gam[None]
+    c = torch.matmul(s, v)
+    if rho0 is not None:
+        init = torch.matmul(q, rho0)
+        if pow_i is not None:
+            init = init * pow_i[None, :, :, None]
+        c = c + init
+    rho = None
+    if need_state:
+        qw = q * pow_ti[None, :, :, None] if pow_ti is not None else q
+        rho = torch.matmul(qw.transpose(-1, -2), v)
+        if rho0 is not None:
+            base = rho0 * (decay.view(1, H, 1, 1) ** T if decay is not None else 1.0)
+            rho = rho + base
+    return c, rho
+
+
+def layer_norm(x, gamma, beta, eps):
+    return F.layer_norm(x, (x.shape[-1],), gamma, beta, eps)
+
+
+def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, decay, rho0=None,
+              need_state=False, dropout=0.0, training=False):
+    """One shared-weight BDH layer. v [B,T,D]; enc/enc_v [H,D,Nh]; dec [N,D].
+
+    Returns (v', rho_T or None, aux dict of the intermediate activations).
+    """
+    B, T, D = v.shape
+    H, _, Nh = enc.shape
+    x = torch.relu(torch.einsum("btd,hdn->bhtn", v, enc) - thr)  # [B,H,T,Nh]
+    q = rope_apply(x, rope_phases(positions, freqs)[None, None]) if freqs is not None else x
+    a, rho = linear_attention_dense(q, v[:, None], rho0=rho0, decay=decay, need_state=need_state)
+    a = layer_norm(a, gamma, beta, eps)  # [B,H,T,D]
+    y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr)
+    yn = x * y
+    if dropout > 0.0 and training:
+        yn = F.dropout(yn, dropout, training=True)
+    m = yn.permute(0, 2, 1, 3).reshape(B, T, H * Nh) @ dec
+    m = layer_norm(m, gamma, beta, eps)
+    v_next = layer_norm(v + m, gamma, beta, eps)
+    return v_next, rho, {"x": x, "q": q, "a": a, "y": y, "yn": yn}
+
+
+def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state=False, training=False):
+    """Full BDH forward (logits). params: embed [V,D], encoder, encoder_v, decoder,
+    lm_head [D,V] (or None for tied), norm_gamma, norm_beta."""
+    B, T = tokens.shape
+    gamma, beta = params["norm_gamma"], params["norm_beta"]
+    v = layer_norm(params["embed"][tokens], gamma, beta, cfg.norm_eps)
+    Nh = cfg.latent_per_head
+    freqs = None
+    if cfg.rotary_embedding == "rope":
+        freqs = rope_freqs(Nh, cfg.rope_theta, device=v.device, dtype=v.dtype)
+    decay = decay_vector(cfg.decay_slopes(), device=v.device, dtype=v.dtype) if cfg.uses_decay() else None
+    positions = torch.arange(pos0, pos0 + T, device=v.device)
+    rhos = []
+    for layer in range(cfg.n_layer):
+        r0 = rho0s[layer] if rho0s is not None else None
+        v, rho, _ = bdh_layer(v, params["encoder"], params["encoder_v"], params["decoder"], gamma, beta,
+                              eps=cfg.norm_eps, thr=cfg.relu_threshold, freqs=freqs, positions=positions,
+                              decay=decay, rho0=r0, need_state=need_state, dropout=cfg.dropout,
+                              training=training)
+        rhos.append(rho)
+    head = params["embed"].t() if params.get("lm_head") is None else params["lm_head"]
+    logits = v @ head
+    return logits, rhos
+
+
+def cross_entropy(logits, targets, mask=None):
+    """Token-mean CE (language_head.rs:549-572), optional loss mask."""
+    V = logits.shape[-1]
+    lp = F.log_softmax(logits.reshape(-1, V).float(), dim=-1)
+    nll = -lp.gather(1, targets.reshape(-1, 1)).squeeze(1)
+    if mask is None:
+        return nll.mean()
+    w = mask.reshape(-1).to(nll.dtype)
+    return (nll * w).sum() / w.sum().clamp_min(1.0)

@@ -1,0 +1,108 @@
+"""Python front of the tcgen05 GEMM engine (``csrc/gemm_sm100.cuh``).
+
+Each BDH contraction is expressed as one engine call: an operand is described by a
+4-D geometry ``(inner, outer, outer_stride, z1, z2)`` of bf16 memory and a majorness
+(K-major = the reduction index is contiguous; MN-major = the output row/column index
+is contiguous), so every operand is read in place — no transposed copies in HBM.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _ext
+
+EPI_BF16, EPI_F32, EPI_RELU_ROPE, EPI_SCORES, EPI_GATE, EPI_DEC_BWD, EPI_DQ = range(7)
+
+
+@dataclass(frozen=True)
+class Operand:
+    t: torch.Tensor
+    mn: bool
+    inner: int
+    outer: int
+    stride: int
+    z1: tuple[int, int] | None = None  # (count, stride) or None when unused
+    z2: tuple[int, int] | None = None
+
+    def geom(self) -> list[int]:
+        z1c, z1s = self.z1 if self.z1 else (1, 0)
+        z2c, z2s = self.z2 if self.z2 else (1, 0)
+        return [self.inner, self.outer, self.stride, z1c, z1s, z2c, z2s,
+                int(self.z1 is not None), int(self.z2 is not None)]
+
+
+_ERR: dict[int, torch.Tensor] = {}
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 the kernels set when a bounded wait times out (0 = healthy)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _ERR:
+        _ERR[idx] = torch.zeros(1, dtype=torch.int32, device=device)
+    return _ERR[idx]
+
+
+def check_errors(device: torch.device) -> None:
+    """Raise if any engine launch on `device` recorded a timeout (synchronizes)."""
+    e = error_word(device)
+    code = int(e.item())
+    if code:
+        e.zero_()
+        raise RuntimeError(f"tcgen05 GEMM engine reported a bounded-wait timeout (code {code})")
+
+
+def pick_bn(n: int) -> int:
+    for bn in (256, 128, 64):
+        if n % bn == 0:
+            return bn
+    return 64
+
+
+def fit_splits(kb: int, want: int) -> int:
+    """Largest split count <= want that the engine's even K partition reproduces."""
+    want = max(1, min(want, kb))
+    per = -(-kb // want)
+    return -(-kb // per)
+
+
+def gemm(epi: int, a: Operand, b: Operand, M: int, N: int, K: int, out0: torch.Tensor, *,
+         Z1: int = 1, Z2: int = 1, bn: int | None = None, splits: int = 1, causal_skip: bool = False,
+         out1=None, aux0=None, aux1=None, ld: int, sz1: int = 0, sz2: int = 0, split_stride: int = 0,
+         alpha: float = 1.0, thr: float = 0.0, freq=None, log2_decay=None, T: int = 1, pos0: int = 0,
+         Nh: int = 1, accumulate: bool = False) -> None:
+    mod = _ext.load()
+    bn = bn or pick_bn(N)
+    mod.gemm(epi, bn, a.t, a.mn, a.geom(), b.t, b.mn, b.geom(), M, N, K, Z1, Z2, splits, causal_skip,
+             out0, out1, aux0, aux1, ld, sz1, sz2, split_stride, alpha, thr, freq, log2_decay, T, pos0, Nh,
+             accumulate, error_word(out0.device))
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, a_t: bool = False,
+           b_t: bool = False) -> torch.Tensor:
+    """C = op(a) @ op(b) for 2-D bf16 tensors on the engine (op = transpose if *_t).
+
+    a is [M,K] (or [K,M] with a_t), b is [K,N] (or [N,K] with b_t). Used by tests and
+    small contractions; the BDH stack calls ``gemm`` directly.
+    """
+    assert a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16
+    a = a.contiguous()
+    b = b.contiguous()
+    if a_t:
+        K, M = a.shape
+        A = Operand(a, True, M, K, M)
+    else:
+        M, K = a.shape
+        A = Operand(a, False, K, M, K)
+    if b_t:
+        N, K2 = b.shape
+        B = Operand(b, False, K2, N, K2)
+    else:
+        K2, N = b.shape
+        B = Operand(b, True, N, K2, N)
+    assert K2 == K
+    out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    gemm(EPI_F32 if out_dtype == torch.float32 else EPI_BF16, A, B, M, N, K, out, ld=N)
+    return out
