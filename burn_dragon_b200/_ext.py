@@ -31,6 +31,35 @@ if os.environ.get("BDH_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
 
 
+# Kernels launched by one call of each binding (for the bench's launch count).
+_LAUNCHES_PER_CALL = {"grad_clip_coef": 2}
+
+
+class _Counted:
+    """Proxy over the extension module that counts kernel launches."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.launches = 0
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+        per = _LAUNCHES_PER_CALL.get(name, 1)
+
+        def call(*args, **kwargs):
+            self.launches += per
+            return fn(*args, **kwargs)
+
+        return call
+
+
+def launch_count() -> int:
+    """Kernels of this package launched so far in this process."""
+    return _MOD.launches if _MOD is not None else 0
+
+
 def load(verbose: bool = False):
     """Compile (if stale) and import the extension. Thread-safe, cached."""
     global _MOD
@@ -44,7 +73,7 @@ def load(verbose: bool = False):
         from torch.utils.cpp_extension import load as _load
 
         os.makedirs(BUILD_DIR, exist_ok=True)
-        _MOD = _load(
+        raw = _load(
             name="_bdh_cuda",
             sources=[os.path.join(CSRC, s) for s in SOURCES],
             extra_cflags=["-O3", "-std=c++17"],
@@ -53,4 +82,5 @@ def load(verbose: bool = False):
             build_directory=BUILD_DIR,
             verbose=verbose,
         )
+        _MOD = _Counted(raw)
         return _MOD

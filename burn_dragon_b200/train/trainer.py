@@ -1,0 +1,86 @@
+"""Training driver: one process per GPU, fused BDH step, DDP gradient all-reduce, AdamW.
+
+``Trainer.step(tokens, targets)`` is the public per-step call: it copies the batch to
+the device (non-blocking from pinned memory), runs forward + CE + backward (the fused
+sm_100a path on CUDA, the PyTorch path on CPU), averages the flat gradient buffer over
+the data-parallel group, applies AdamW and returns the loss as a device tensor.
+
+DDP mirrors the reference's process-group data parallelism (WORLD_SIZE / RANK /
+LOCAL_RANK, gradient mean over ranks; burn_dragon_language/src/train/schedule.rs:
+10348-10457), but the all-reduce is one collective over the single flat gradient
+buffer instead of one per parameter tensor.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..config import DragonConfig
+from ..models.bdh import BDH
+from .optim import FusedAdamW, lr_at
+
+
+def init_distributed() -> tuple[int, int, int]:
+    """Initialise torch.distributed from the torchrun environment; returns (rank, world, local)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend=backend)
+    return rank, world, local
+
+
+class Trainer:
+    def __init__(self, cfg: DragonConfig, device, lr=1e-3, weight_decay=0.1, betas=(0.9, 0.999), eps=1e-8,
+                 grad_clip_norm=None, seed=1337, lr_schedule=None, max_iters=1000, comm=None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.model = BDH(cfg, device=self.device, seed=seed)
+        self.opt = FusedAdamW(self.model.store, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
+                              grad_clip_norm=grad_clip_norm)
+        self.lr_schedule = lr_schedule
+        self.max_iters = max_iters
+        self.base_lr = lr
+        self.step_idx = 0
+        self.world = dist.get_world_size() if dist.is_initialized() else 1
+        self.comm = comm  # optional custom gradient communicator (parallel.ddp)
+        self.fused = self.device.type == "cuda"
+
+    def compute_grads(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None) -> torch.Tensor:
+        if self.fused:
+            return self.model.fused_step(tokens, targets, mask)
+        self.model.zero_grad(set_to_none=False)
+        loss = self.model.loss(tokens, targets, mask)
+        grads = torch.autograd.grad(loss, [p for p in self.model.parameters()])
+        for p, g in zip(self.model.parameters(), grads):
+            p.grad.copy_(g)
+        return loss.detach()
+
+    def allreduce_grads(self) -> None:
+        if self.world == 1:
+            return
+        if self.comm is not None:
+            self.comm.allreduce_mean(self.model.store.grad)
+            return
+        op = dist.ReduceOp.AVG if dist.get_backend() == "nccl" else dist.ReduceOp.SUM
+        dist.all_reduce(self.model.store.grad, op=op)
+        if op == dist.ReduceOp.SUM:
+            self.model.store.grad.div_(self.world)
+
+    def step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None) -> torch.Tensor:
+        tokens = tokens.to(self.device, non_blocking=True)
+        targets = targets.to(self.device, non_blocking=True)
+        if mask is not None:
+            mask = mask.to(self.device, non_blocking=True)
+        loss = self.compute_grads(tokens, targets, mask)
+        self.allreduce_grads()
+        lr = lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters)
+        self.opt.step(lr)
+        self.step_idx += 1
+        return loss

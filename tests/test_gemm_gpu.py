@@ -1,0 +1,81 @@
+"""tcgen05 GEMM engine vs a plain PyTorch fp32 reference of the same op."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from burn_dragon_b200.ops import gemm as G
+
+    return G
+
+
+def _ref(a, b, a_t, b_t):
+    A = a.float().t() if a_t else a.float()
+    B = b.float().t() if b_t else b.float()
+    return A @ B
+
+
+def _close(got, ref, tol=2e-2):
+    err = (got.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err / scale < tol, f"max rel err {err / scale:.3e}"
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 128, 192), (384, 64, 1024), (200, 96, 136)])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+def test_matmul_layouts(M, N, K, a_t, b_t):
+    G = _ops()
+    torch.manual_seed(0)
+    dev = "cuda"
+    a = torch.randn((K, M) if a_t else (M, K), device=dev).bfloat16()
+    b = torch.randn((N, K) if b_t else (K, N), device=dev).bfloat16()
+    if a_t and not b_t and N % 256:
+        pytest.skip("no instantiation for this (bn, MN-A, K-B) combination")
+    got = G.matmul(a, b, a_t=a_t, b_t=b_t)
+    torch.cuda.synchronize()
+    G.check_errors(torch.device(dev))
+    _close(got, _ref(a, b, a_t, b_t))
+
+
+def test_split_k_partials_sum():
+    G = _ops()
+    torch.manual_seed(1)
+    M, N, K, S = 256, 256, 2048, 4
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = torch.randn(K, N, device="cuda").bfloat16()
+    out = torch.empty(S, M, N, device="cuda")
+    G.gemm(G.EPI_F32, G.Operand(a, False, K, M, K), G.Operand(b, True, N, K, N), M, N, K, out, splits=S, ld=N,
+           split_stride=M * N)
+    torch.cuda.synchronize()
+    _close(out.sum(0), _ref(a, b, False, False))
+
+
+def test_batched_z_coordinates_and_accumulate():
+    G = _ops()
+    torch.manual_seed(2)
+    Z, M, N, K = 3, 128, 128, 256
+    a = torch.randn(Z, M, K, device="cuda").bfloat16()
+    b = torch.randn(Z, N, K, device="cuda").bfloat16()
+    out = torch.ones(Z, M, N, device="cuda")
+    G.gemm(G.EPI_F32, G.Operand(a, False, K, M, K, z1=(Z, M * K)), G.Operand(b, False, K, N, K, z1=(Z, N * K)),
+           M, N, K, out, Z1=Z, ld=N, sz1=M * N, accumulate=True)
+    torch.cuda.synchronize()
+    _close(out - 1.0, torch.bmm(a.float(), b.float().transpose(1, 2)))
+
+
+def test_causal_scores_epilogue():
+    G = _ops()
+    torch.manual_seed(3)
+    B, H, T, Nh = 2, 2, 256, 128
+    q = torch.randn(B, T, H, Nh, device="cuda").bfloat16()
+    S = torch.full((B, H, T, T), 7.0, device="cuda").bfloat16()
+    op = G.Operand(q, False, Nh, T, H * Nh, z1=(H, Nh), z2=(B, T * H * Nh))
+    G.gemm(G.EPI_SCORES, op, op, T, T, Nh, S, Z1=H, Z2=B, bn=128, causal_skip=True, ld=T, sz1=T * T,
+           sz2=H * T * T)
+    torch.cuda.synchronize()
+    qf = q.float().permute(0, 2, 1, 3)
+    ref = torch.tril(qf @ qf.transpose(-1, -2), diagonal=-1)
+    _close(S, ref)
+    assert (S.float().triu() == 0).all()
