@@ -6,6 +6,8 @@
 #include <torch/extension.h>
 
 #include <mutex>
+#include <stdexcept>
+#include <string>
 #include <vector>
 
 #include "gemm_sm100.cuh"
@@ -106,8 +108,11 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh,
           bool accumulate, const at::Tensor& err) {
   const Entry* hit = find_entry((int)bn, a_mn, b_mn, (int)epi);
-  TORCH_CHECK(hit != nullptr, "no GEMM instantiation for bn=", bn, " a_mn=", a_mn, " b_mn=", b_mn,
-              " epi=", epi);
+  if (hit == nullptr) {
+    throw std::invalid_argument("burn_dragon_b200: no GEMM instantiation for bn=" + std::to_string(bn) +
+                                " a_mn=" + std::to_string((int)a_mn) + " b_mn=" + std::to_string((int)b_mn) +
+                                " epi=" + std::to_string(epi));
+  }
   TORCH_CHECK(M > 0 && N > 0 && K > 0 && Z1 > 0 && Z2 > 0 && splits > 0, "bad GEMM sizes");
   TORCH_CHECK(N % 32 == 0, "GEMM N must be a multiple of 32");
   TORCH_CHECK(ld % 8 == 0 && sz1 % 8 == 0 && sz2 % 8 == 0 && split_stride % 8 == 0,

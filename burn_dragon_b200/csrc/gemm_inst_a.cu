@@ -4,7 +4,7 @@ namespace bd {
 const Entry kGemmTableA[] = {
     BD_ENTRY(256, false, false, EPI_BF16), BD_ENTRY(128, false, false, EPI_BF16),
     BD_ENTRY(64, false, false, EPI_BF16),  BD_ENTRY(256, false, true, EPI_BF16),
-    BD_ENTRY(64, false, true, EPI_BF16),   BD_ENTRY(256, false, false, EPI_F32),
+    BD_ENTRY(64, false, true, EPI_BF16),   BD_ENTRY(128, false, true, EPI_BF16),   BD_ENTRY(256, false, false, EPI_F32),
     BD_ENTRY(128, false, false, EPI_F32),  BD_ENTRY(64, false, false, EPI_F32),
 };
 const int kGemmTableASize = sizeof(kGemmTableA) / sizeof(Entry);

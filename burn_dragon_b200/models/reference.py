@@ -76,7 +76,7 @@ def _decay_powers(T: int, decay: torch.Tensor | None, device, dtype):
     if decay is None:
         return mask[None], None, None
     lg = torch.log(decay.to(dtype))[:, None, None]  # [H,1,1]
-    gam = torch.exp(lg * diff[None]) * mask[None]
+    gam = torch.exp(lg * diff.clamp_min(0)[None]) * mask[None]
     pow_i = torch.exp(torch.log(decay.to(dtype))[:, None] * i.to(dtype)[None, :])  # [H,T]
     pow_ti = torch.exp(torch.log(decay.to(dtype))[:, None] * (T - i).to(dtype)[None, :])
     return gam, pow_i, pow_ti
