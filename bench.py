@@ -89,6 +89,7 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=32, help="sequences per GPU")
     ap.add_argument("--seq", type=int, default=512)
     ap.add_argument("--layers", type=int, default=6)
+    ap.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per step")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -119,6 +120,14 @@ def main() -> None:
 
     for i in range(args.warmup):
         trainer.step(*dev_batches[i % 2])
+    torch.cuda.synchronize()
+    if not args.no_graph:
+        trainer.enable_cuda_graph(*dev_batches[0], warmup=1)
+    # host-side enqueue time of one step (diagnostic)
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    trainer.step(*dev_batches[1])
+    host_ms = (time.perf_counter() - h0) * 1e3
     torch.cuda.synchronize()
     check_errors(dev)
 
@@ -186,6 +195,8 @@ def main() -> None:
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 2 * B * T * 8,
                     "d2h_bytes_per_step": 4},
             "gpu_launches": launches,
+            "cuda_graph": not args.no_graph,
+            "host_enqueue_ms_per_step": round(host_ms, 3),
             "final_loss": losses[-1] if losses else float(loss.item()),
         }
         print(json.dumps(out))

@@ -55,6 +55,12 @@ class _Counted:
         return call
 
 
+def add_launches(n: int) -> None:
+    """Account for kernels launched by replaying a captured CUDA graph."""
+    if _MOD is not None:
+        _MOD.launches += n
+
+
 def launch_count() -> int:
     """Kernels of this package launched so far in this process."""
     return _MOD.launches if _MOD is not None else 0

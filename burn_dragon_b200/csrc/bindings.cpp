@@ -34,7 +34,8 @@ void symmetrize(const at::Tensor& P, const at::Tensor& G, int64_t BH, int64_t T,
                 const c10::optional<at::Tensor>& log2_decay);
 void adamw(const at::Tensor& p, const at::Tensor& g, const at::Tensor& m, const at::Tensor& v,
            const c10::optional<at::Tensor>& shadow, double lr, double b1, double b2, double eps, double wd,
-           double bc1, double bc2, const c10::optional<at::Tensor>& gscale);
+           double bc1, double bc2, const c10::optional<at::Tensor>& gscale,
+           const c10::optional<at::Tensor>& hyper);
 void grad_clip_coef(const at::Tensor& g, const at::Tensor& scratch3, double max_norm);
 void cast_bf16(const at::Tensor& x, const at::Tensor& y);
 }  // namespace bd

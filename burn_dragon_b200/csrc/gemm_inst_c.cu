@@ -5,6 +5,7 @@ namespace bd {
 const Entry kGemmTableC[] = {
     BD_ENTRY(256, false, true, EPI_RELU_ROPE), BD_ENTRY(128, false, true, EPI_RELU_ROPE),
     BD_ENTRY(64, false, true, EPI_RELU_ROPE),  BD_ENTRY(128, false, false, EPI_SCORES),
+    BD_ENTRY(256, false, false, EPI_SCORES),
     BD_ENTRY(64, false, false, EPI_SCORES),    BD_ENTRY(256, false, true, EPI_GATE),
     BD_ENTRY(128, false, true, EPI_GATE),      BD_ENTRY(64, false, true, EPI_GATE),
     BD_ENTRY(256, false, false, EPI_DEC_BWD),  BD_ENTRY(128, false, false, EPI_DEC_BWD),

@@ -313,8 +313,13 @@ __global__ void symmetrize_kernel(const float* __restrict__ P, __nv_bfloat16* __
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ shadow, long long n, float lr,
                              float b1, float b2, float eps, float wd, float bc1, float bc2,
-                             const float* __restrict__ gscale) {
+                             const float* __restrict__ gscale, const float* __restrict__ hyper) {
   const float gs = gscale ? gscale[0] : 1.0f;
+  if (hyper) {  // device-resident {lr, bc1, bc2}: lets a captured CUDA graph replay every step
+    lr = hyper[0];
+    bc1 = hyper[1];
+    bc2 = hyper[2];
+  }
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
     const float gi = g[i] * gs;
@@ -488,12 +493,13 @@ void symmetrize(const at::Tensor& P, const at::Tensor& G, int64_t BH, int64_t T,
 
 void adamw(const at::Tensor& p, const at::Tensor& g, const at::Tensor& m, const at::Tensor& v,
            const c10::optional<at::Tensor>& shadow, double lr, double b1, double b2, double eps, double wd,
-           double bc1, double bc2, const c10::optional<at::Tensor>& gscale) {
+           double bc1, double bc2, const c10::optional<at::Tensor>& gscale,
+           const c10::optional<at::Tensor>& hyper) {
   c10::cuda::CUDAGuard gd(p.get_device());
   adamw_kernel<<<148 * 8, 256, 0, cur_stream(p)>>>(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
                                                    v.data_ptr<float>(), opt_ptr<__nv_bfloat16>(shadow), p.numel(),
                                                    (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
-                                                   (float)bc1, (float)bc2, opt_ptr<const float>(gscale));
+                                                   (float)bc1, (float)bc2, opt_ptr<const float>(gscale), opt_ptr<const float>(hyper));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -59,6 +59,11 @@ class FusedAdamW:
         self.v = torch.zeros_like(store.data)
         self.t = 0
         self._scratch = torch.zeros(4, dtype=torch.float32, device=store.data.device)
+        # {lr, 1-b1^t, 1-b2^t} on the device, so a captured step reads this step's values
+        self._hyper = torch.zeros(4, dtype=torch.float32, device=store.data.device)
+        # pageable on purpose: the copy from pageable memory is staged before copy_ returns,
+        # so the next step may overwrite this buffer while the GPU still lags behind
+        self._hyper_host = torch.zeros(4, dtype=torch.float32)
 
     def state_dict(self) -> dict:
         return {"m": self.m, "v": self.v, "t": self.t, "lr": self.lr}
@@ -71,12 +76,19 @@ class FusedAdamW:
     def grad_norm(self) -> torch.Tensor:
         return self._scratch[1]
 
-    @torch.no_grad()
-    def step(self, lr: float | None = None) -> None:
+    def prepare(self, lr: float | None = None) -> None:
+        """Advance the step counter and stage this step's scalars on the device."""
         self.t += 1
-        lr = self.lr if lr is None else lr
-        bc1 = 1.0 - self.b1 ** self.t
-        bc2 = 1.0 - self.b2 ** self.t
+        self._lr_now = self.lr if lr is None else lr
+        self._hyper_host[0] = self._lr_now
+        self._hyper_host[1] = 1.0 - self.b1 ** self.t
+        self._hyper_host[2] = 1.0 - self.b2 ** self.t
+        if self.store.data.is_cuda:
+            self._hyper.copy_(self._hyper_host, non_blocking=True)
+
+    @torch.no_grad()
+    def apply(self) -> None:
+        """The update itself (device work only on CUDA; safe to capture in a CUDA graph)."""
         s = self.store
         if s.data.is_cuda:
             mod = _ext.load()
@@ -84,9 +96,11 @@ class FusedAdamW:
             if self.clip is not None:
                 mod.grad_clip_coef(s.grad, self._scratch, float(self.clip))
                 gscale = self._scratch[2:3]
-            mod.adamw(s.data, s.grad, self.m, self.v, s.shadow, lr, self.b1, self.b2, self.eps, self.wd, bc1, bc2,
-                      gscale)
+            mod.adamw(s.data, s.grad, self.m, self.v, s.shadow, 0.0, self.b1, self.b2, self.eps, self.wd, 1.0, 1.0,
+                      gscale, self._hyper)
             return
+        lr = self._lr_now
+        bc1, bc2 = float(self._hyper_host[1]), float(self._hyper_host[2])
         g = s.grad
         if self.clip is not None:
             norm = g.norm()
@@ -96,3 +110,8 @@ class FusedAdamW:
         self.v.mul_(self.b2).addcmul_(g, g, value=1 - self.b2)
         s.data.mul_(1 - lr * self.wd)
         s.data.addcdiv_(self.m / bc1, (self.v / bc2).sqrt_().add_(self.eps), value=-lr)
+
+    @torch.no_grad()
+    def step(self, lr: float | None = None) -> None:
+        self.prepare(lr)
+        self.apply()

@@ -51,6 +51,50 @@ class Trainer:
         self.world = dist.get_world_size() if dist.is_initialized() else 1
         self.comm = comm  # optional custom gradient communicator (parallel.ddp)
         self.fused = self.device.type == "cuda"
+        self._graph = None
+        self._graph_shape = None
+        self._graph_launches = 0
+
+    def enable_cuda_graph(self, tokens: torch.Tensor, targets: torch.Tensor, warmup: int = 2) -> None:
+        """Capture forward + backward + all-reduce + AdamW of one step into a CUDA graph.
+
+        The graph replays on static input buffers; ``step`` copies each batch into them.
+        Shapes are fixed at capture; a different batch shape falls back to eager steps.
+        Warm-up steps run (and train) before the capture.
+        """
+        from .. import _ext
+
+        assert self.fused, "CUDA graphs need the CUDA path"
+        self._sx = torch.empty_like(tokens, device=self.device)
+        self._sy = torch.empty_like(targets, device=self.device)
+        self._sx.copy_(tokens)
+        self._sy.copy_(targets)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._eager_device_step(self._sx, self._sy)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
+        before = _ext.launch_count()
+        with torch.cuda.graph(g):
+            self._sloss = self.compute_grads(self._sx, self._sy)
+            self.allreduce_grads()
+            self.opt.apply()
+        self._graph_launches = _ext.launch_count() - before
+        self.opt.t -= 1  # the capture itself did not update anything
+        self._graph = g
+        self._graph_shape = (tuple(tokens.shape), tuple(targets.shape))
+
+    def _eager_device_step(self, tokens, targets, mask=None) -> torch.Tensor:
+        loss = self.compute_grads(tokens, targets, mask)
+        self.allreduce_grads()
+        self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
+        self.opt.apply()
+        self.step_idx += 1
+        return loss
 
     def compute_grads(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None) -> torch.Tensor:
         if self.fused:
@@ -74,6 +118,17 @@ class Trainer:
             self.model.store.grad.div_(self.world)
 
     def step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None) -> torch.Tensor:
+        if (self._graph is not None and mask is None
+                and (tuple(tokens.shape), tuple(targets.shape)) == self._graph_shape):
+            from .. import _ext
+
+            self._sx.copy_(tokens, non_blocking=True)
+            self._sy.copy_(targets, non_blocking=True)
+            self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
+            self._graph.replay()
+            _ext.add_launches(self._graph_launches)
+            self.step_idx += 1
+            return self._sloss
         tokens = tokens.to(self.device, non_blocking=True)
         targets = targets.to(self.device, non_blocking=True)
         if mask is not None:
