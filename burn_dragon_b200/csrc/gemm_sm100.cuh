@@ -65,15 +65,19 @@ struct alignas(64) GemmParams {
   EpiParams e;
 };
 
-template <int BN>
+// STAGED: bf16-output epilogues that stage through two 4 KB smem tiles per epilogue
+// warp (64 KB), paid for with fewer mainloop stages.
+template <int BN, bool STAGED = false>
 struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int STAGES = STAGED ? ((BN == 256) ? 3 : (BN == 128 ? 4 : 5))
+                                       : ((BN == 256) ? 4 : (BN == 128 ? 6 : 8));
+  static constexpr int EPI_BYTES = STAGED ? 8 * 2 * 4096 : 0;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int THREADS = 320;
 };
@@ -253,4 +257,5 @@ __device__ __forceinline__ void epilogue_zero_chunk(const GemmParams& p, const T
 
 }  // namespace bd
 
+#include "gemm_epilogue_staged.cuh"
 #include "gemm_sm100_kernel.cuh"

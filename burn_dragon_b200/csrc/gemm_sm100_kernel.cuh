@@ -6,7 +6,8 @@ namespace bd {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
-  using Cfg = GemmCfg<BN>;
+  constexpr bool STAGED = (EPI != EPI_F32);
+  using Cfg = GemmCfg<BN, STAGED>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[STAGES];
@@ -22,6 +23,7 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+  uint8_t* sEpi = smem + STAGES * Cfg::STAGE_BYTES;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -160,23 +162,46 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int half = ew >> 2;   // column half of the tile
     const int r_local = quad * 32 + lane;
+    uint8_t* buf0 = sEpi + ew * 2 * kStageTileBytes;
+    uint8_t* buf1 = buf0 + kStageTileBytes;
+    // Columns this warp owns: half of the tile (for BN = 64 with staging, warps of the
+    // second half idle: a staged chunk is 64 columns wide).
+    constexpr int COLS = STAGED ? (BN >= 128 ? BN / 2 : (BN == 64 ? 64 : 0)) : BN / 2;
+    const bool active = !(STAGED && BN == 64 && half == 1);
+    const int col_off = STAGED && BN == 64 ? 0 : half * (BN / 2);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const TileCoord tc = decode_tile(p, t, BN);
       const int row = tc.m0 + r_local;
       if (tc.zero) {
-        for (int c = 0; c < BN / 2; c += 32) epilogue_zero_chunk<EPI>(p, tc, row, tc.n0 + half * (BN / 2) + c);
+        if constexpr (STAGED) {
+          if (active)
+            for (int c = 0; c < COLS; c += 64) epilogue_zero64<EPI>(p, tc, tc.m0 + quad * 32, tc.n0 + col_off + c, lane);
+        } else {
+          for (int c = 0; c < COLS; c += 32) epilogue_zero_chunk<EPI>(p, tc, row, tc.n0 + col_off + c);
+        }
         continue;
       }
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-      const uint32_t t_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + half * (BN / 2);
+      const uint32_t t_addr = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off;
+      if constexpr (STAGED) {
+        if (active) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 2; c += 32) {
-        float v[32];
-        tmem_ld32(t_addr + c, v);
-        epilogue_chunk<EPI>(p, tc, v, row, tc.n0 + half * (BN / 2) + c);
+          for (int c = 0; c < COLS; c += 64) {
+            float v[64];
+            tmem_ld64(t_addr + c, v);
+            epilogue_chunk64<EPI>(p, tc, v, tc.m0 + quad * 32, tc.n0 + col_off + c, buf0, buf1, lane);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < COLS; c += 32) {
+          float v[32];
+          tmem_ld32(t_addr + c, v);
+          epilogue_chunk<EPI>(p, tc, v, row, tc.n0 + col_off + c);
+        }
       }
       tc_fence_before();
       __syncwarp();
