@@ -1,0 +1,99 @@
+// gemm_epilogue_tma.cuh — asynchronous epilogue for the memory-bound BDH modes
+// (x-projection + RoPE, gate, decoder backward, dQ), tile N = 128.
+//
+// Each epilogue warp owns a 32-row x 64-column chunk of every tile. Its auxiliary
+// operands (x, yn, dx_part) are fetched by TMA one tile ahead into a double-buffered,
+// 128B-swizzled smem tile pair, so the fetch overlaps the current tile's math and
+// store; results are written over the aux tile in place and leave through TMA bulk
+// stores. No warp ever waits on a global load of its own, and the accumulator is handed
+// back to the MMA warp right after tcgen05.ld, before the math.
+#pragma once
+
+namespace bd {
+
+template <int EPI>
+constexpr int epi_naux() {
+  return EPI == EPI_GATE ? 1 : ((EPI == EPI_DEC_BWD || EPI == EPI_DQ) ? 2 : 0);
+}
+
+// In-place math on the smem tiles b0 (and b1) for this thread's row.
+template <int EPI>
+__device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoord& tc, float (&v)[64], int row,
+                                             int col0, uint8_t* b0, uint8_t* b1, int lane) {
+  const EpiParams& e = p.e;
+  float pos = 0.f;
+  int j0 = 0;
+  if constexpr (EPI == EPI_RELU_ROPE) {
+    pos = (float)(e.pos0 + row % e.T);
+    j0 = col0 % e.Nh;
+  } else if constexpr (EPI == EPI_DQ) {
+    pos = (float)(e.pos0 + row);
+    j0 = col0;
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    float* w = v + 8 * c;
+    uint4* s0 = reinterpret_cast<uint4*>(b0 + stg_off(lane, c));
+    uint4* s1 = reinterpret_cast<uint4*>(b1 + stg_off(lane, c));
+    if constexpr (EPI == EPI_RELU_ROPE) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = fmaxf(w[i] - e.thr, 0.0f);
+      *s0 = pack8(w);
+      if (e.freq) {
+        const float4 fa = *reinterpret_cast<const float4*>(e.freq + j0 + 8 * c);
+        const float4 fb = *reinterpret_cast<const float4*>(e.freq + j0 + 8 * c + 4);
+        const float f[4] = {fa.x, fa.z, fb.x, fb.z};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float cs, sn;
+          rope_cs(pos, f[i], cs, sn);
+          const float xe = w[2 * i], xo = w[2 * i + 1];
+          w[2 * i] = xe * cs - xo * sn;
+          w[2 * i + 1] = xo * cs + xe * sn;
+        }
+        *s1 = pack8(w);
+      }
+    } else if constexpr (EPI == EPI_GATE) {
+      float xv[8];
+      unpack8(*s0, xv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = fmaxf(w[i] - e.thr, 0.0f) * xv[i];
+      *s0 = pack8(w);
+    } else if constexpr (EPI == EPI_DEC_BWD) {
+      float xv[8], yv[8], dy[8];
+      unpack8(*s0, xv);
+      unpack8(*s1, yv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float g = w[i];
+        const float y = (xv[i] > 0.0f) ? __fdividef(yv[i], xv[i]) : 0.0f;
+        dy[i] = (yv[i] > 0.0f) ? g * xv[i] : 0.0f;
+        w[i] = g * y;
+      }
+      *s0 = pack8(w);
+      *s1 = pack8(dy);
+    } else if constexpr (EPI == EPI_DQ) {
+      float bv[8], xv[8];
+      unpack8(*s0, bv);
+      unpack8(*s1, xv);
+      if (e.freq) {
+        const float4 fa = *reinterpret_cast<const float4*>(e.freq + j0 + 8 * c);
+        const float4 fb = *reinterpret_cast<const float4*>(e.freq + j0 + 8 * c + 4);
+        const float f[4] = {fa.x, fa.z, fb.x, fb.z};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float cs, sn;
+          rope_cs(pos, f[i], cs, sn);
+          const float ge = w[2 * i], go = w[2 * i + 1];
+          w[2 * i] = ge * cs + go * sn;
+          w[2 * i + 1] = go * cs - ge * sn;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = (xv[i] > 0.0f) ? (w[i] + bv[i]) : 0.0f;
+      *s0 = pack8(w);
+    }
+  }
+}
+
+}  // namespace bd

@@ -11,7 +11,7 @@ namespace bd {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 void launch_one(const GemmParams& p, cudaStream_t stream, int dev) {
-  using Cfg = GemmCfg<BN, EPI != EPI_F32>;
+  using Cfg = GemmCfg<BN, epi_kind<EPI>()>;
   auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, EPI>;
   static bool attr_set[64] = {false};
   if (!attr_set[dev]) {

@@ -56,6 +56,9 @@ struct EpiParams {
 struct alignas(64) GemmParams {
   CUtensorMap ta;
   CUtensorMap tb;
+  // TMA-epilogue modes: 32 x 64 boxes (128B swizzle) of the auxiliary inputs / outputs,
+  // as 4-D maps (cols, rows, z1, z2) of the output geometry.
+  CUtensorMap tx0, tx1, to0, to1;
   int M, N, K;
   int Z1, Z2;
   int tiles_m, tiles_n, splits, kb_per_split;
@@ -65,18 +68,28 @@ struct alignas(64) GemmParams {
   EpiParams e;
 };
 
-// STAGED: bf16-output epilogues that stage through two 4 KB smem tiles per epilogue
-// warp (64 KB), paid for with fewer mainloop stages.
-template <int BN, bool STAGED = false>
+// Epilogue kinds: 0 = fp32 row stores, 1 = register-computed bf16 tiles staged through
+// smem (two 4 KB tiles per epilogue warp), 2 = TMA epilogue (aux operands prefetched by
+// TMA one tile ahead into double-buffered smem, results stored by TMA; BN = 128 only).
+template <int EPI>
+constexpr int epi_kind() {
+  return EPI == EPI_F32 ? 0
+         : ((EPI == EPI_RELU_ROPE || EPI == EPI_GATE || EPI == EPI_DEC_BWD || EPI == EPI_DQ) ? 2 : 1);
+}
+
+template <int BN, int KIND = 0>
 struct GemmCfg {
+  static constexpr bool STAGED = KIND != 0;
   static constexpr int BM = 128;
   static constexpr int BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = STAGED ? ((BN == 256) ? 3 : (BN == 128 ? 4 : 5))
-                                       : ((BN == 256) ? 4 : (BN == 128 ? 6 : 8));
-  static constexpr int EPI_BYTES = STAGED ? 8 * 2 * 4096 : 0;
+  static constexpr int STAGES = KIND == 2 ? 3
+                               : (STAGED ? ((BN == 256) ? 3 : (BN == 128 ? 4 : 5))
+                                         : ((BN == 256) ? 4 : (BN == 128 ? 6 : 8)));
+  // kind 2: 8 warps x 2 tile buffers x 2 tensors x 4 KB
+  static constexpr int EPI_BYTES = KIND == 2 ? 8 * 2 * 2 * 4096 : (STAGED ? 8 * 2 * 4096 : 0);
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int THREADS = 320;
@@ -258,4 +271,5 @@ __device__ __forceinline__ void epilogue_zero_chunk(const GemmParams& p, const T
 }  // namespace bd
 
 #include "gemm_epilogue_staged.cuh"
+#include "gemm_epilogue_tma.cuh"
 #include "gemm_sm100_kernel.cuh"

@@ -6,8 +6,10 @@ namespace bd {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
-  constexpr bool STAGED = (EPI != EPI_F32);
-  using Cfg = GemmCfg<BN, STAGED>;
+  constexpr int KIND = epi_kind<EPI>();
+  constexpr bool STAGED = KIND == 1;
+  static_assert(KIND != 2 || BN == 128, "the TMA epilogue is built for tile N = 128");
+  using Cfg = GemmCfg<BN, KIND>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t full_bar[STAGES];
@@ -17,6 +19,7 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_flag;
+  __shared__ uint64_t aux_bar[8][2];
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -36,6 +39,10 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
       mbar_init(&tempty_bar[a], 8);
     }
     mbar_init(&drain_bar, 1);
+    for (int w = 0; w < 8; ++w) {
+      mbar_init(&aux_bar[w][0], 1);
+      mbar_init(&aux_bar[w][1], 1);
+    }
     fence_barrier_init();
     tma_prefetch_desc(&p.ta);
     tma_prefetch_desc(&p.tb);
@@ -162,6 +169,82 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int half = ew >> 2;   // column half of the tile
     const int r_local = quad * 32 + lane;
+    if constexpr (KIND == 2) {
+      // ---------------- TMA epilogue (see gemm_epilogue_tma.cuh)
+      constexpr int NAUX = epi_naux<EPI>();
+      uint8_t* wbuf = sEpi + ew * 4 * kStageTileBytes;  // [tile parity][tensor] 4 KB tiles
+      const int col_off = half * 64;
+      // Per-buffer issue / wait counters keep the mbarrier parities exact (uniform
+      // across the warp; only lane 0 issues).
+      int n_issued[2] = {0, 0}, n_waited[2] = {0, 0};
+      auto issue_aux = [&](int t, int b) {
+        if constexpr (NAUX > 0) {
+          if (t >= total) return;
+          const TileCoord n = decode_tile(p, t, BN);
+          if (n.zero) return;
+          ++n_issued[b];
+          if (lane != 0) return;
+          uint8_t* dst = wbuf + b * 2 * kStageTileBytes;
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(&aux_bar[ew][b], NAUX * kStageTileBytes);
+          tma_load_4d(dst, &p.tx0, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1, n.z2);
+          if constexpr (NAUX > 1)
+            tma_load_4d(dst + kStageTileBytes, &p.tx1, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1,
+                        n.z2);
+        }
+      };
+      issue_aux(blockIdx.x, 0);
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+        const TileCoord tc = decode_tile(p, t, BN);
+        const int b = it & 1;
+        uint8_t* b0 = wbuf + b * 2 * kStageTileBytes;
+        uint8_t* b1 = b0 + kStageTileBytes;
+        // the other buffer was last read by this warp's stores of the previous tile
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+        issue_aux(t + gridDim.x, b ^ 1);
+        if (tc.zero) continue;  // (no zero tiles in these modes unless K is empty)
+        if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        tc_fence_after();
+        float v[64];
+        tmem_ld64(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        if constexpr (NAUX > 0) {
+          if (!mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
+          ++n_waited[b];
+        }
+        tma_epi_math<EPI>(p, tc, v, tc.m0 + r_local, tc.n0 + col_off, b0, b1, lane);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int c0 = tc.n0 + col_off, c1 = tc.m0 + quad * 32;
+          tma_store_4d(&p.to0, b0, c0, c1, tc.z1, tc.z2);
+          if (EPI == EPI_DEC_BWD || (EPI == EPI_RELU_ROPE && p.e.freq != nullptr))
+            tma_store_4d(&p.to1, b1, c0, c1, tc.z1, tc.z2);
+          bulk_commit_group();
+        }
+      }
+      if (lane == 0) {
+        bulk_wait_group0();
+        // On an abort, loads may still be landing in smem: wait for them (bounded).
+        int dummy_abort = 0;
+        for (int b = 0; b < 2; ++b)
+          while (n_waited[b] < n_issued[b]) {
+            mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, (volatile int*)&dummy_abort, p.err, kErrTimeoutDrain);
+            ++n_waited[b];
+          }
+      }
+      __syncwarp();
+    } else {
     uint8_t* buf0 = sEpi + ew * 2 * kStageTileBytes;
     uint8_t* buf1 = buf0 + kStageTileBytes;
     // Columns this warp owns: half of the tile (for BN = 64 with staging, warps of the
@@ -213,6 +296,7 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
     }
   }
 
+    }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

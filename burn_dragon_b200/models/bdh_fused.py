@@ -121,7 +121,7 @@ class FusedBDH:
         for l in range(L):
             v16 = ws.v16[l]
             # x = relu(v Dx - thr), q = rope(x)       (K = D)
-            G.gemm(G.EPI_RELU_ROPE, Operand(v16, False, D, M, D), B_enc, M, Nh, D, ws.x16[l], Z1=H,
+            G.gemm(G.EPI_RELU_ROPE, Operand(v16, False, D, M, D), B_enc, M, Nh, D, ws.x16[l], Z1=H, bn=128,
                    out1=ws.q16[l] if ws.freq is not None else None, ld=N, sz1=Nh, thr=thr, freq=ws.freq,
                    T=T, pos0=pos0, Nh=Nh)
             # S = tril_{-1}(q q^T) (* gamma^(i-j))      (K = Nh), upper tiles skipped
@@ -136,7 +136,7 @@ class FusedBDH:
                        ws.amean[l], ws.arstd[l])
             # yn = relu(an Dy - thr) * x                (K = D)
             G.gemm(G.EPI_GATE, Operand(ws.an16[l], False, D, M, H * D, z1=(H, D)), B_encv, M, Nh, D, ws.yn16[l],
-                   Z1=H, aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr)
+                   Z1=H, bn=128, aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr)
             # m = yn E (split-K partials), v' = LN(v + LN(m))
             G.gemm(G.EPI_F32, Operand(ws.yn16[l], False, N, M, N), B_dec, M, D, N, ws.partial,
                    splits=ws.dec_splits, ld=D, split_stride=M * D)
@@ -177,7 +177,7 @@ class FusedBDH:
             v16 = ws.v16[l]
             parts.append(mod.tail_bwd(dv, ws.v32[l], ws.m32[l], ws.tst[l], M, D, gam, bet, ws.dm16, ws.dv_res))
             # d(yn) = dm E^T -> dx_part = d(yn)*y, dy_pre = d(yn)*x*[y>0]
-            G.gemm(G.EPI_DEC_BWD, Operand(ws.dm16, False, D, M, D), Operand(dec, False, D, N, D), M, N, D, ws.dx16,
+            G.gemm(G.EPI_DEC_BWD, Operand(ws.dm16, False, D, M, D), Operand(dec, False, D, N, D), M, N, D, ws.dx16, bn=128,
                    out1=ws.dy16, aux0=ws.x16[l], aux1=ws.yn16[l], ld=N)
             # dE += yn^T dm
             G.gemm(G.EPI_F32, Operand(ws.yn16[l], True, N, M, N), Operand(ws.dm16, True, D, M, D), N, D, M,
@@ -199,7 +199,7 @@ class FusedBDH:
             mod.symmetrize(ws.P32, ws.G16, B * H, T, H, ws.log2_decay)
             # dx_pre = (dx_part + rope^T(G q)) * [x > 0]   (in place over dx_part)
             G.gemm(G.EPI_DQ, Operand(ws.G16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
-                   Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B,
+                   Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B, bn=128,
                    aux0=ws.dx16, aux1=ws.x16[l], ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh)
             # dV = sum_h S_h^T dC_h  (K = (h, i))
             G.gemm(G.EPI_F32, Operand(ws.S16[l], True, T, H * T, T, z2=(B, H * T * T)),

@@ -28,7 +28,7 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
     if case == "xproj":
         v, enc, x, q = r(M, D), r(H, D, Nh), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_RELU_ROPE, Operand(v, False, D, M, D),  # noqa: E731
-                              Operand(enc, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, x, Z1=H, out1=q, ld=N,
+                              Operand(enc, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, x, Z1=H, bn=128, out1=q, ld=N,
                               sz1=Nh, freq=freq, T=T, Nh=Nh)
         return call, 2 * M * N * D, (M * D + D * N + 2 * M * N) * 2
     if case == "scores":
@@ -40,18 +40,18 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
     if case == "gate":
         an, encv, x, yn = r(M, H, D), r(H, D, Nh), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_GATE, Operand(an, False, D, M, H * D, z1=(H, D)),  # noqa: E731
-                              Operand(encv, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, yn, Z1=H, aux0=x, ld=N,
+                              Operand(encv, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, yn, Z1=H, bn=128, aux0=x, ld=N,
                               sz1=Nh)
         return call, 2 * M * N * D, (M * H * D + D * N + 2 * M * N) * 2
     if case == "dec_bwd":
         dm, dec, x, yn, dx, dy = r(M, D), r(N, D), r(M, N), r(M, N), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_DEC_BWD, Operand(dm, False, D, M, D), Operand(dec, False, D, N, D),  # noqa: E731
-                              M, N, D, dx, out1=dy, aux0=x, aux1=yn, ld=N)
+                              M, N, D, dx, bn=128, out1=dy, aux0=x, aux1=yn, ld=N)
         return call, 2 * M * N * D, (M * D + N * D + 4 * M * N) * 2
     if case == "dq":
         g16, q, dx, x = r(B, H, T, T), r(M, N), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_DQ, Operand(g16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),  # noqa: E731
-                              Operand(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B,
+                              Operand(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B, bn=128,
                               aux0=dx, aux1=x, ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh)
         return call, 2 * B * H * T * T * Nh, (B * H * T * T + 4 * M * N) * 2
     if case == "wgrad":
