@@ -199,9 +199,17 @@ def main() -> None:
             "host_enqueue_ms_per_step": round(host_ms, 3),
             "final_loss": losses[-1] if losses else float(loss.item()),
         }
-        print(json.dumps(out))
+        print(json.dumps(out), flush=True)
+    # Teardown: a CUDA graph that captured NCCL collectives must be released before the
+    # process group; a final barrier keeps ranks together, then exit without the
+    # interpreter's slow (and, with live graphs, hang-prone) finalizers.
+    trainer._graph = None
+    torch.cuda.synchronize()
     if world > 1:
-        dist.destroy_process_group()
+        dist.barrier()
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 if __name__ == "__main__":
