@@ -29,6 +29,11 @@ __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoor
   } else if constexpr (EPI == EPI_DQ) {
     pos = (float)(e.pos0 + row);
     j0 = col0;
+    if (e.row_decay) {
+      const float a = exp2f((float)row * e.log2_decay[tc.z1]);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) v[i] *= a;
+    }
   }
 #pragma unroll
   for (int c = 0; c < 8; ++c) {

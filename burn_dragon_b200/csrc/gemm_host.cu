@@ -125,7 +125,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           const c10::optional<at::Tensor>& aux1, int64_t ld, int64_t sz1, int64_t sz2, int64_t split_stride,
           double alpha, double thr, const c10::optional<at::Tensor>& freq,
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh,
-          bool accumulate, const at::Tensor& err) {
+          bool accumulate, bool row_decay, const at::Tensor& err) {
   const Entry* hit = find_entry((int)bn, a_mn, b_mn, (int)epi);
   if (hit == nullptr) {
     throw std::invalid_argument("burn_dragon_b200: no GEMM instantiation for bn=" + std::to_string(bn) +
@@ -179,6 +179,8 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   e.pos0 = (int)pos0;
   e.Nh = (int)Nh;
   e.accumulate = accumulate ? 1 : 0;
+  e.row_decay = row_decay ? 1 : 0;
+  if (row_decay) TORCH_CHECK(e.log2_decay != nullptr, "row_decay needs log2_decay");
   if (epi == EPI_F32) {
     TORCH_CHECK(out0.scalar_type() == at::kFloat, "EPI_F32 output must be fp32");
   } else {

@@ -51,6 +51,7 @@ struct EpiParams {
   int pos0;
   int Nh;                  // latent per head (column -> in-head index for RoPE)
   int accumulate;          // EPI_F32: add into the existing output
+  int row_decay;           // EPI_F32 / EPI_DQ: scale row r by 2^(r * log2_decay[z1])
 };
 
 struct alignas(64) GemmParams {
@@ -166,10 +167,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const TileCo
   if constexpr (EPI == EPI_F32) {
     float* o = reinterpret_cast<float*>(e.out0) + off + (long long)tc.split * e.split_stride;
     float4* o4 = reinterpret_cast<float4*>(o);
+    const float a = e.row_decay ? e.alpha * exp2f((float)row * e.log2_decay[tc.z1]) : e.alpha;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      float4 w = make_float4(e.alpha * v[4 * q], e.alpha * v[4 * q + 1], e.alpha * v[4 * q + 2],
-                             e.alpha * v[4 * q + 3]);
+      float4 w = make_float4(a * v[4 * q], a * v[4 * q + 1], a * v[4 * q + 2], a * v[4 * q + 3]);
       if (e.accumulate) {
         float4 old = o4[q];
         w.x += old.x; w.y += old.y; w.z += old.z; w.w += old.w;

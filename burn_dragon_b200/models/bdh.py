@@ -147,9 +147,13 @@ class BDH(nn.Module):
         return R.cross_entropy(self.forward(tokens, state=state), targets, mask)
 
     # ---------------------------------------------------------------- fused path
-    def fused_step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None) -> torch.Tensor:
+    def fused_step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None, state=None) -> torch.Tensor:
         """Forward + CE + backward on the sm_100a kernels. Writes ``.grad`` of every
-        parameter (the flat grad buffer) and returns the loss as a device scalar."""
+        parameter (the flat grad buffer) and returns the loss as a device scalar.
+
+        With a ``ModelState`` the chunk continues that state (stateful TBPTT: the state
+        enters detached and leaves detached, burn_dragon_language/src/train/steps.rs:
+        2698-2731) and the state is advanced in place."""
         from .bdh_fused import FusedBDH, FusedWorkspace
 
         B, T = tokens.shape
@@ -160,7 +164,12 @@ class BDH(nn.Module):
         f = self._fused
         p32 = self.store.views(self.store.data)
         p16 = self.shadow_dict()
-        f.forward(p16, p32, tokens)
+        pos0 = state.position if state is not None else 0
+        rho0s = state.rhos if state is not None else None
+        outs = f.forward(p16, p32, tokens, pos0=pos0, rho0s=rho0s, want_state=state is not None)
         loss = f.loss(targets, mask)
-        f.backward(p16, p32, self.grad_dict(), tokens)
+        f.backward(p16, p32, self.grad_dict(), tokens, pos0=pos0)
+        if state is not None:
+            state.rhos = outs
+            state.position += T
         return loss

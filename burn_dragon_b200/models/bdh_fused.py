@@ -86,7 +86,22 @@ class FusedWorkspace:
             self.log2_decay = (-g / math.log(2.0)).to(torch.float32).to(dev)  # log2(exp(-s))
         else:
             self.log2_decay = None
-        self.norm_parts: list[torch.Tensor] = []
+        # stateful (TBPTT / streaming) buffers, allocated on first use: the bf16 operand
+        # copy of the incoming state and two ping-pong sets of outgoing fp32 states
+        self.rho16: list[torch.Tensor] | None = None
+        self.rho_sets: list[list[torch.Tensor]] | None = None
+        self.rho_flip = 0
+        self.has_rho0 = False
+        self.qscaled: torch.Tensor | None = None
+
+    def ensure_state_buffers(self) -> None:
+        if self.rho16 is not None:
+            return
+        B, H, Nh, D, L = self.B, self.H, self.Nh, self.D, self.L
+        dev = self.v32[0].device
+        self.rho16 = [torch.empty(B, H, Nh, D, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+        self.rho_sets = [[torch.empty(B, H, Nh, D, dtype=torch.float32, device=dev) for _ in range(L)]
+                         for _ in range(2)]
 
 
 def _bn(n: int) -> int:
@@ -106,8 +121,21 @@ class FusedBDH:
         self.mod = _ext.load()
 
     # ---------------------------------------------------------------- forward
-    def forward(self, p16: dict, p32: dict, tokens: torch.Tensor, pos0: int = 0) -> None:
+    def forward(self, p16: dict, p32: dict, tokens: torch.Tensor, pos0: int = 0, rho0s=None,
+                want_state: bool = False):
+        """Forward of the stack. With ``rho0s`` (per-layer fp32 [B,H,Nh,D]) the carried
+        linear-attention state enters every layer (C += gamma^t q rho0); with
+        ``want_state`` the per-layer final states are returned (fp32, owned by the
+        workspace: valid until the step after next)."""
         ws, cfg, mod = self.ws, self.cfg, self.mod
+        decay = ws.log2_decay is not None
+        ws.has_rho0 = rho0s is not None
+        out_states = None
+        if rho0s is not None or want_state:
+            ws.ensure_state_buffers()
+        if want_state:
+            out_states = ws.rho_sets[ws.rho_flip]
+            ws.rho_flip ^= 1
         B, T, D, H, Nh, N, M, L = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L
         eps, thr = cfg.norm_eps, cfg.relu_threshold
         tok = tokens.reshape(-1)
@@ -132,6 +160,31 @@ class FusedBDH:
             G.gemm(G.EPI_F32, Operand(ws.S16[l], False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
                    Operand(v16, True, D, T, D, z2=(B, T * D)), T, D, T, ws.a32[l], Z1=H, Z2=B,
                    ld=H * D, sz1=D, sz2=T * H * D)
+            if rho0s is not None:
+                # a += gamma^t q rho0                    (K = Nh)
+                ws.rho16[l].copy_(rho0s[l])
+                G.gemm(G.EPI_F32, qop, Operand(ws.rho16[l], True, D, Nh, D, z1=(H, Nh * D), z2=(B, H * Nh * D)),
+                       T, D, Nh, ws.a32[l], Z1=H, Z2=B, ld=H * D, sz1=D, sz2=T * H * D, accumulate=True,
+                       log2_decay=ws.log2_decay, row_decay=decay)
+            if want_state:
+                # rho_T = gamma^T rho0 + (q * gamma^(T-t))^T v      (K = T)
+                ro = out_states[l]
+                qsrc = ws.q16[l]
+                if decay:
+                    g = torch.exp2(ws.log2_decay.double())  # gamma per head
+                    tt = torch.arange(T, device=ro.device, dtype=torch.float64)
+                    sc = (g[None, :] ** (T - tt)[:, None]).float()  # [T, H]
+                    if ws.qscaled is None:
+                        ws.qscaled = torch.empty_like(ws.q16[l])
+                    qv = ws.q16[l].view(B, T, H, Nh).float() * sc[None, :, :, None]
+                    ws.qscaled.view(B, T, H, Nh).copy_(qv)
+                    qsrc = ws.qscaled
+                if rho0s is not None:
+                    gT = torch.exp2(ws.log2_decay * T).view(1, H, 1, 1) if decay else 1.0
+                    ro.copy_(rho0s[l] * gT)
+                G.gemm(G.EPI_F32, Operand(qsrc, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)),
+                       Operand(v16, True, D, T, D, z2=(B, T * D)), Nh, D, T, ro, Z1=H, Z2=B, ld=D, sz1=Nh * D,
+                       sz2=H * Nh * D, accumulate=rho0s is not None)
             mod.ln_fwd(ws.a32[l], None, M * H, D, p32["norm_gamma"], p32["norm_beta"], eps, None, ws.an16[l],
                        ws.amean[l], ws.arstd[l])
             # yn = relu(an Dy - thr) * x                (K = D)
@@ -144,6 +197,7 @@ class FusedBDH:
                          eps, ws.m32[l], ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
         G.gemm(G.EPI_F32, Operand(ws.v16[L], False, D, M, D), Operand(p16["lm_head"], True, ws.V, D, ws.V),
                M, ws.V, D, ws.logits, ld=ws.V)
+        return out_states
 
     def loss(self, targets: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
         ws = self.ws
@@ -201,6 +255,12 @@ class FusedBDH:
             G.gemm(G.EPI_DQ, Operand(ws.G16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
                    Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B, bn=128,
                    aux0=ws.dx16, aux1=ws.x16[l], ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh)
+            if ws.has_rho0:
+                # + rope^T(gamma^t dC rho0^T) (the carried state is detached: no grad to rho0)
+                G.gemm(G.EPI_DQ, dcop, Operand(ws.rho16[l], False, D, Nh, D, z1=(H, Nh * D), z2=(B, H * Nh * D)),
+                       T, Nh, D, ws.dx16, Z1=H, Z2=B, bn=128, aux0=ws.dx16, aux1=ws.x16[l], ld=N, sz1=Nh,
+                       sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh, log2_decay=ws.log2_decay,
+                       row_decay=ws.log2_decay is not None)
             # dV = sum_h S_h^T dC_h  (K = (h, i))
             G.gemm(G.EPI_F32, Operand(ws.S16[l], True, T, H * T, T, z2=(B, H * T * T)),
                    Operand(ws.dC16, True, D, H * T, D, z2=(B, H * T * D)), T, D, H * T, ws.dva32, Z2=B, ld=D,

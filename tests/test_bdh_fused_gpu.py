@@ -52,3 +52,49 @@ def test_fused_step_matches_reference(rotary):
     for n in ("lm_head", "decoder", "encoder_v", "encoder", "embed", "norm_gamma", "norm_beta"):
         r = _rel(grads[n], ref_params[n].grad)
         assert r < 0.08, f"{n}: rel err {r:.3e}"
+
+
+@pytest.mark.parametrize("rotary", ["rope", "alibi"])
+def test_fused_stateful_chunks_match_reference(rotary):
+    """Stateful TBPTT: chunk 2 continues chunk 1's detached state (loss, grads, state)."""
+    from burn_dragon_b200.models.state import ModelState
+
+    cfg = DragonConfig(n_layer=2, n_embd=64, n_head=2, mlp_internal_dim_multiplier=8, dropout=0.0,
+                       rotary_embedding=rotary)
+    model = BDH(cfg, device="cuda", seed=7)
+    with torch.no_grad():
+        for n in ("encoder", "encoder_v", "decoder"):
+            getattr(model, n).mul_(5.0)
+    model.store.refresh_shadow()
+    torch.manual_seed(1)
+    B, T = 2, 128
+    toks = torch.randint(0, 256, (B, 2 * T), device="cuda")
+    tgts = torch.randint(0, 256, (B, 2 * T), device="cuda")
+
+    ref_params = {}
+    for n, p in model.param_dict().items():
+        q = p.detach().clone()
+        if n in ("encoder", "encoder_v", "decoder", "lm_head"):
+            q = q.bfloat16().float()
+        ref_params[n] = q.requires_grad_(True)
+    with torch.no_grad():
+        _, rhos1 = R.bdh_forward(toks[:, :T], ref_params, cfg, need_state=True)
+    logits2, rhos2 = R.bdh_forward(toks[:, T:], ref_params, cfg, rho0s=[r.detach() for r in rhos1], pos0=T,
+                                   need_state=True)
+    ref_loss = R.cross_entropy(logits2, tgts[:, T:])
+    ref_loss.backward()
+
+    st = ModelState.empty()
+    model.fused_step(toks[:, :T], tgts[:, :T], state=st)
+    for r_ref, r_got in zip(rhos1, st.rhos):
+        assert _rel(r_got, r_ref) < 0.03
+    loss = model.fused_step(toks[:, T:], tgts[:, T:], state=st)
+    torch.cuda.synchronize()
+    assert st.position == 2 * T
+    assert abs(loss.item() - ref_loss.item()) < 2e-2 * abs(ref_loss.item())
+    grads = model.grad_dict()
+    for n in ("lm_head", "decoder", "encoder_v", "encoder", "embed"):
+        r = _rel(grads[n], ref_params[n].grad)
+        assert r < 0.08, f"{n}: rel err {r:.3e}"
+    for r_ref, r_got in zip(rhos2, st.rhos):
+        assert _rel(r_got, r_ref.detach()) < 0.03
