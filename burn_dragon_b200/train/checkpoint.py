@@ -1,0 +1,260 @@
+"""Checkpoints and run directories.
+
+Run layout (burn_dragon_language/src/checkpoint.rs:27-85,712-735; run_dirs.rs:37-46):
+
+    <root>/<backend>/<run-name>/
+        config.json                     model / optimizer / parallel / kernel spec
+        training_config.json            the resolved training configuration
+        tokenizer.json                  byte tokenizer description
+        random_scaffold_manifest.json   (random-scaffold runs only)
+        checkpoint/model-<step>.bin     parameters
+        checkpoint/optim-<step>.bin     optimizer moments + step
+        checkpoint/scheduler-<step>.bin learning-rate schedule position
+        checkpoint/runtime-state-<step>.bin  streaming rho state, position, ...
+        latest                          name of the newest checkpoint step
+
+The root comes from ``BURN_DRAGON_RUN_ROOT`` (default ``runs``); ``BURN_DRAGON_RUN_DIR``
+overrides the whole path and ``BURN_DRAGON_RUN_NAME`` the run name.
+
+Tensor payloads use the safetensors container (8-byte little-endian header length, a
+JSON header of ``{name: {dtype, shape, data_offsets}}`` plus ``__metadata__``, then the
+raw little-endian data), implemented here. Record names mirror the reference's Burn
+record paths (``encoder``, ``embed.weight``, ``norm.gamma``, ...). Large files can be
+split into parts with a manifest (burn_dragon_checkpoint/src/parts.rs) and exported at
+reduced precision (f16 / bf16; burn_dragon_checkpoint/src/precision.rs). Retention keeps
+the newest two checkpoints plus the best-validation one (schedule.rs:25,848-900).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import re
+import shutil
+import struct
+from dataclasses import asdict, is_dataclass
+
+import torch
+
+SCHEMA_VERSION = 4  # burn_dragon_core/src/lib.rs:7
+
+_DT = {
+    torch.float32: "F32", torch.float16: "F16", torch.bfloat16: "BF16", torch.int64: "I64",
+    torch.int32: "I32", torch.uint8: "U8", torch.float64: "F64", torch.bool: "BOOL",
+}
+_DT_INV = {v: k for k, v in _DT.items()}
+
+
+# ------------------------------------------------------------------ tensor files
+def save_tensors(path: str, tensors: dict[str, torch.Tensor], metadata: dict | None = None) -> None:
+    header: dict = {}
+    blobs = []
+    off = 0
+    for name in sorted(tensors):
+        t = tensors[name].detach().contiguous().cpu()
+        raw = t.view(torch.uint8).numpy().tobytes() if t.numel() else b""
+        header[name] = {"dtype": _DT[t.dtype], "shape": list(t.shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    if metadata:
+        header["__metadata__"] = {k: json.dumps(v) for k, v in metadata.items()}
+    h = json.dumps(header, separators=(",", ":")).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    tmp = path + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
+    os.replace(tmp, path)
+
+
+def load_tensors(path: str, device=None) -> tuple[dict[str, torch.Tensor], dict]:
+    with open(path, "rb") as f:
+        n = struct.unpack("<Q", f.read(8))[0]
+        header = json.loads(f.read(n))
+        data = f.read()
+    meta = {k: json.loads(v) for k, v in header.pop("__metadata__", {}).items()}
+    out = {}
+    for name, info in header.items():
+        a, b = info["data_offsets"]
+        dt = _DT_INV[info["dtype"]]
+        buf = bytearray(data[a:b])
+        t = torch.frombuffer(buf, dtype=torch.uint8) if b > a else torch.empty(0, dtype=torch.uint8)
+        t = t.view(dt).reshape(info["shape"]) if b > a else torch.empty(info["shape"], dtype=dt)
+        out[name] = t.to(device) if device is not None else t
+    return out, meta
+
+
+def convert_precision(tensors: dict[str, torch.Tensor], dtype: torch.dtype) -> dict[str, torch.Tensor]:
+    """Float tensors to `dtype` (f16 / bf16 export); integers are kept."""
+    return {k: (v.to(dtype) if v.is_floating_point() else v) for k, v in tensors.items()}
+
+
+def save_parts(path: str, tensors: dict[str, torch.Tensor], max_part_bytes: int, metadata=None) -> dict:
+    """Split a record over ``<path>.part-<i>`` files of at most ``max_part_bytes`` each
+    (a tensor larger than the limit gets a part of its own) plus ``<path>.parts.json``."""
+    parts: list[list[str]] = [[]]
+    size = 0
+    for name in sorted(tensors):
+        nb = tensors[name].numel() * tensors[name].element_size()
+        if parts[-1] and size + nb > max_part_bytes:
+            parts.append([])
+            size = 0
+        parts[-1].append(name)
+        size += nb
+    manifest = {"schema_version": SCHEMA_VERSION, "parts": []}
+    for i, names in enumerate(parts):
+        fname = f"{os.path.basename(path)}.part-{i:04d}"
+        save_tensors(os.path.join(os.path.dirname(path), fname), {n: tensors[n] for n in names}, metadata)
+        manifest["parts"].append({"file": fname, "tensors": names})
+    with open(path + ".parts.json", "w") as f:
+        json.dump(manifest, f, indent=2)
+    return manifest
+
+
+def load_parts(path: str, device=None) -> dict[str, torch.Tensor]:
+    with open(path + ".parts.json") as f:
+        manifest = json.load(f)
+    out: dict[str, torch.Tensor] = {}
+    for part in manifest["parts"]:
+        t, _ = load_tensors(os.path.join(os.path.dirname(path), part["file"]), device)
+        out.update(t)
+    return out
+
+
+# ------------------------------------------------------------------ run directories
+def resolve_run_dir(backend: str = "cuda", run_name: str | None = None, root: str | None = None) -> str:
+    if os.environ.get("BURN_DRAGON_RUN_DIR"):
+        return os.environ["BURN_DRAGON_RUN_DIR"]
+    root = root or os.environ.get("BURN_DRAGON_RUN_ROOT", "runs")
+    name = run_name or os.environ.get("BURN_DRAGON_RUN_NAME") or "run"
+    return os.path.join(root, backend, name)
+
+
+def _jsonable(x):
+    if is_dataclass(x):
+        return {k: _jsonable(v) for k, v in asdict(x).items()}
+    if isinstance(x, dict):
+        return {k: _jsonable(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return [_jsonable(v) for v in x]
+    return x
+
+
+class RunDir:
+    def __init__(self, path: str):
+        self.path = path
+        self.ckpt = os.path.join(path, "checkpoint")
+        os.makedirs(self.ckpt, exist_ok=True)
+
+    def write_json(self, name: str, obj) -> None:
+        with open(os.path.join(self.path, name), "w") as f:
+            json.dump(_jsonable(obj), f, indent=2, sort_keys=True)
+
+    def read_json(self, name: str):
+        with open(os.path.join(self.path, name)) as f:
+            return json.load(f)
+
+    def write_run_config(self, train_cfg) -> None:
+        """config.json (RunConfigOutput-like spec) and training_config.json."""
+        self.write_json("config.json", {
+            "schema_version": SCHEMA_VERSION,
+            "model_spec": train_cfg.model,
+            "optimizer_spec": train_cfg.optimizer,
+            "parallel_spec": train_cfg.parallel,
+            "kernel_spec": {"backend": "sm_100a tcgen05", "dtype": "bf16 operands, fp32 accumulate/master"},
+            "state_layout": {"rho": "[B, H, Nh, D] fp32 per layer"},
+        })
+        self.write_json("training_config.json", train_cfg)
+        self.write_json("tokenizer.json", {"type": "byte", "vocab_size": train_cfg.model.vocab_size})
+
+    # ---- checkpoints
+    def _p(self, kind: str, step: int) -> str:
+        return os.path.join(self.ckpt, f"{kind}-{step}.bin")
+
+    def save(self, step: int, model, optimizer=None, scheduler: dict | None = None, runtime: dict | None = None,
+             keep_last: int = 2, best_step: int | None = None) -> None:
+        from ..models.bdh import RECORD_NAMES
+
+        params = {RECORD_NAMES[n]: t.detach() for n, t in model.store.views(model.store.data).items()}
+        save_tensors(self._p("model", step), params, {"schema_version": SCHEMA_VERSION, "step": step})
+        if optimizer is not None:
+            save_tensors(self._p("optim", step), {"m": optimizer.m, "v": optimizer.v},
+                         {"t": optimizer.t, "lr": optimizer.lr})
+        with open(self._p("scheduler", step), "w") as f:
+            json.dump(scheduler or {}, f)
+        if runtime is not None:
+            rt = {}
+            meta = {k: v for k, v in runtime.items() if k != "rhos"}
+            for i, r in enumerate(runtime.get("rhos") or []):
+                rt[f"rho.{i}"] = r
+            save_tensors(self._p("runtime-state", step), rt, meta)
+        with open(os.path.join(self.path, "latest"), "w") as f:
+            f.write(str(step))
+        self._retain(keep_last, best_step)
+
+    def steps(self) -> list[int]:
+        out = []
+        for fn in os.listdir(self.ckpt):
+            m = re.fullmatch(r"model-(\d+)\.bin", fn)
+            if m:
+                out.append(int(m.group(1)))
+        return sorted(out)
+
+    def latest(self) -> int | None:
+        p = os.path.join(self.path, "latest")
+        if os.path.exists(p):
+            return int(open(p).read().strip())
+        s = self.steps()
+        return s[-1] if s else None
+
+    def _retain(self, keep_last: int, best_step: int | None) -> None:
+        steps = self.steps()
+        keep = set(steps[-keep_last:]) | ({best_step} if best_step is not None else set())
+        for s in steps:
+            if s in keep:
+                continue
+            for kind in ("model", "optim", "scheduler", "runtime-state"):
+                p = self._p(kind, s)
+                if os.path.exists(p):
+                    os.remove(p)
+
+    def load(self, step: int | None, model, optimizer=None, device=None) -> dict:
+        """Restore model (and optimizer) state; returns {'scheduler', 'runtime'}."""
+        from ..models.bdh import RECORD_NAMES
+
+        step = self.latest() if step is None else step
+        if step is None:
+            raise FileNotFoundError(f"no checkpoint in {self.ckpt}")
+        tensors, meta = load_tensors(self._p("model", step))
+        if int(meta.get("schema_version", SCHEMA_VERSION)) != SCHEMA_VERSION:
+            raise ValueError("checkpoint schema version mismatch")
+        views = model.store.views(model.store.data)
+        with torch.no_grad():
+            for n, v in views.items():
+                src = tensors[RECORD_NAMES[n]]
+                if tuple(src.shape) != tuple(v.shape):
+                    raise ValueError(f"{RECORD_NAMES[n]}: checkpoint shape {tuple(src.shape)} != {tuple(v.shape)}")
+                v.copy_(src.to(v.device, v.dtype))
+        model.store.refresh_shadow()
+        if optimizer is not None and os.path.exists(self._p("optim", step)):
+            o, ometa = load_tensors(self._p("optim", step))
+            optimizer.m.copy_(o["m"].to(optimizer.m.device))
+            optimizer.v.copy_(o["v"].to(optimizer.v.device))
+            optimizer.t = int(ometa["t"])
+        out = {"step": step, "scheduler": {}, "runtime": None}
+        sp = self._p("scheduler", step)
+        if os.path.exists(sp):
+            out["scheduler"] = json.load(open(sp))
+        rp = self._p("runtime-state", step)
+        if os.path.exists(rp):
+            rt, rmeta = load_tensors(rp, device)
+            rhos = [rt[f"rho.{i}"] for i in range(len(rt))] or None
+            runtime = dict(rmeta)
+            runtime["rhos"] = rhos
+            out["runtime"] = runtime
+        return out
+
+    def remove(self) -> None:
+        shutil.rmtree(self.path, ignore_errors=True)

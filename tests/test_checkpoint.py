@@ -1,0 +1,71 @@
+"""Checkpoint round trips (CPU): tensor files, parts, precision, run dir, resume."""
+import os
+
+import torch
+
+from burn_dragon_b200.config import DragonConfig, TrainingConfig
+from burn_dragon_b200.models.bdh import BDH
+from burn_dragon_b200.train import checkpoint as C
+from burn_dragon_b200.train.optim import FusedAdamW
+
+
+def _cfg():
+    return DragonConfig(n_layer=2, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0,
+                        rotary_embedding="rope")
+
+
+def test_tensor_file_round_trip(tmp_path):
+    t = {"a": torch.randn(3, 4), "b": torch.arange(5), "c": torch.randn(2).bfloat16(), "e": torch.empty(0)}
+    p = str(tmp_path / "x.bin")
+    C.save_tensors(p, t, {"step": 7, "name": "x"})
+    back, meta = C.load_tensors(p)
+    assert meta == {"step": 7, "name": "x"}
+    for k in t:
+        assert back[k].dtype == t[k].dtype and torch.equal(back[k], t[k])
+
+
+def test_parts_and_precision(tmp_path):
+    t = {f"w{i}": torch.randn(64, 64) for i in range(5)}
+    p = str(tmp_path / "model.bin")
+    man = C.save_parts(p, t, max_part_bytes=2 * 64 * 64 * 4)
+    assert len(man["parts"]) == 3
+    back = C.load_parts(p)
+    assert all(torch.equal(back[k], t[k]) for k in t)
+    h = C.convert_precision(t, torch.float16)
+    assert all(v.dtype == torch.float16 for v in h.values())
+
+
+def test_run_dir_resume_preserves_logits_and_optimizer(tmp_path):
+    cfg = _cfg()
+    model = BDH(cfg, seed=3)
+    opt = FusedAdamW(model.store, lr=1e-2)
+    x = torch.randint(0, 256, (2, 8))
+    y = torch.randint(0, 256, (2, 8))
+    for _ in range(2):
+        loss = model.loss(x, y)
+        grads = torch.autograd.grad(loss, list(model.parameters()))
+        for p, g in zip(model.parameters(), grads):
+            p.grad.copy_(g)
+        opt.step()
+    run = C.RunDir(C.resolve_run_dir("cpu", "t", root=str(tmp_path)))
+    tc = TrainingConfig(model=cfg)
+    run.write_run_config(tc)
+    rho = [torch.randn(2, 2, 32, 32) for _ in range(2)]
+    run.save(2, model, opt, {"step": 2}, {"position": 8, "rhos": rho})
+    assert os.path.exists(os.path.join(run.path, "config.json"))
+    model2 = BDH(cfg, seed=99)
+    opt2 = FusedAdamW(model2.store, lr=1e-2)
+    info = run.load(None, model2, opt2)
+    assert info["step"] == 2 and info["runtime"]["position"] == 8
+    assert torch.equal(info["runtime"]["rhos"][1], rho[1])
+    assert torch.allclose(model(x), model2(x))
+    assert opt2.t == opt.t and torch.equal(opt2.m, opt.m)
+
+
+def test_retention_keeps_last_two_and_best(tmp_path):
+    model = BDH(_cfg(), seed=1)
+    run = C.RunDir(str(tmp_path / "r"))
+    for s in (1, 2, 3, 4):
+        run.save(s, model, best_step=1)
+    assert run.steps() == [1, 3, 4]
+    assert run.latest() == 4
