@@ -38,6 +38,9 @@ void adamw(const at::Tensor& p, const at::Tensor& g, const at::Tensor& m, const 
            const c10::optional<at::Tensor>& hyper);
 void grad_clip_coef(const at::Tensor& g, const at::Tensor& scratch3, double max_norm);
 void cast_bf16(const at::Tensor& x, const at::Tensor& y);
+void rho_step(const at::Tensor& rho, const at::Tensor& q, int64_t q_row_stride, const at::Tensor& v,
+              const c10::optional<at::Tensor>& gamma, const at::Tensor& a, int64_t B, int64_t H, int64_t Nh,
+              int64_t D);
 }  // namespace bd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -53,4 +56,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &bd::adamw);
   m.def("grad_clip_coef", &bd::grad_clip_coef);
   m.def("cast_bf16", &bd::cast_bf16);
+  m.def("rho_step", &bd::rho_step);
 }

@@ -1,0 +1,108 @@
+// decode.cu — one-token recurrent attention step for generation.
+//
+// For each (b, h): a[b,h,:] = rho[b,h]^T q[b,h,:]   (read BEFORE the update)
+//                  rho[b,h] <- (rho[b,h] + q[b,h,:] (x) v[b,:]) * gamma_h
+// (burn_dragon_core/src/model/sequence/linear.rs:18-60 with T = 1). The state is the
+// whole cost of a decode token: it is read and written exactly once here, in place.
+// Grid: (row chunks of Nh, B*H); 256 threads = 64 column groups of 4 floats x 4 row
+// phases; the 4 phases reduce through smem and one atomicAdd per column lands in `a`
+// (which the caller zeroes).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_bf16.h>
+#include <torch/extension.h>
+
+namespace bd {
+namespace {
+
+constexpr int kRows = 64;  // latent rows per CTA
+
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename QT>
+__global__ void rho_step_kernel(float* __restrict__ rho, const QT* __restrict__ q, long long q_row_stride,
+                                const float* __restrict__ v, const float* __restrict__ gamma, float* __restrict__ a,
+                                int H, int Nh, int D) {
+  __shared__ float4 red[4][64];
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const int j0 = blockIdx.x * kRows;
+  const int c4 = threadIdx.x & 63;  // column group (4 floats)
+  const int ph = threadIdx.x >> 6;  // row phase 0..3
+  const float g = gamma ? gamma[h] : 1.0f;
+  float4* R = reinterpret_cast<float4*>(rho + ((size_t)bh * Nh) * D);
+  const QT* qb = q + (size_t)b * q_row_stride + (size_t)h * Nh;
+  float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int D4 = D / 4;
+  for (int cb = 0; cb < D4; cb += 64) {
+    const int c = cb + c4;
+    const bool on = c < D4;
+    acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (on) {
+      vv = reinterpret_cast<const float4*>(v + (size_t)b * D)[c];
+      for (int j = j0 + ph; j < min(j0 + kRows, Nh); j += 4) {
+        const float qj = to_f(qb[j]);
+        float4 r = R[(size_t)j * D4 + c];
+        acc.x += qj * r.x;
+        acc.y += qj * r.y;
+        acc.z += qj * r.z;
+        acc.w += qj * r.w;
+        r.x = (r.x + qj * vv.x) * g;
+        r.y = (r.y + qj * vv.y) * g;
+        r.z = (r.z + qj * vv.z) * g;
+        r.w = (r.w + qj * vv.w) * g;
+        R[(size_t)j * D4 + c] = r;
+      }
+    }
+    red[ph][c4] = acc;
+    __syncthreads();
+    if (ph == 0 && on) {
+      float4 s = red[0][c4];
+#pragma unroll
+      for (int k = 1; k < 4; ++k) {
+        s.x += red[k][c4].x;
+        s.y += red[k][c4].y;
+        s.z += red[k][c4].z;
+        s.w += red[k][c4].w;
+      }
+      float* dst = a + (size_t)bh * D + 4 * c;
+      atomicAdd(dst + 0, s.x);
+      atomicAdd(dst + 1, s.y);
+      atomicAdd(dst + 2, s.z);
+      atomicAdd(dst + 3, s.w);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+// rho [B,H,Nh,D] fp32 (updated in place); q rows [B, >= H*Nh] (bf16 or fp32, row stride
+// q_row_stride elements); v [B,D] fp32; gamma [H] or None; a [B,H,D] fp32, pre-zeroed.
+void rho_step(const at::Tensor& rho, const at::Tensor& q, int64_t q_row_stride, const at::Tensor& v,
+              const c10::optional<at::Tensor>& gamma, const at::Tensor& a, int64_t B, int64_t H, int64_t Nh,
+              int64_t D) {
+  c10::cuda::CUDAGuard g(rho.get_device());
+  TORCH_CHECK(rho.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat && a.scalar_type() == at::kFloat,
+              "rho_step: rho, v and a must be fp32");
+  TORCH_CHECK(D % 4 == 0, "rho_step: D must be a multiple of 4");
+  dim3 grid((unsigned)((Nh + kRows - 1) / kRows), (unsigned)(B * H));
+  auto st = at::cuda::getCurrentCUDAStream(rho.get_device()).stream();
+  const float* gp = gamma ? gamma->data_ptr<float>() : nullptr;
+  if (q.scalar_type() == at::kBFloat16) {
+    rho_step_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(rho.data_ptr<float>(),
+                                                         reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
+                                                         q_row_stride, v.data_ptr<float>(), gp, a.data_ptr<float>(),
+                                                         (int)H, (int)Nh, (int)D);
+  } else {
+    TORCH_CHECK(q.scalar_type() == at::kFloat, "rho_step: q must be bf16 or fp32");
+    rho_step_kernel<float><<<grid, 256, 0, st>>>(rho.data_ptr<float>(), q.data_ptr<float>(), q_row_stride,
+                                                 v.data_ptr<float>(), gp, a.data_ptr<float>(), (int)H, (int)Nh,
+                                                 (int)D);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace bd

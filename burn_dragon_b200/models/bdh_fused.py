@@ -34,8 +34,11 @@ from .reference import rope_freqs
 class FusedWorkspace:
     """Activation and gradient buffers for one (B, T) shape, allocated once."""
 
-    def __init__(self, cfg, B: int, T: int, device: torch.device):
+    def __init__(self, cfg, B: int, T: int, device: torch.device, inference: bool = False):
+        """``inference``: forward-only workspace (one set of per-layer activation buffers
+        reused by every layer, outgoing state written in place over the incoming one)."""
         self.cfg = cfg
+        self.inference = inference
         self.B, self.T = B, T
         D, H, Nh, V = cfg.n_embd, cfg.n_head, cfg.latent_per_head, cfg.vocab_size
         N, M, L = H * Nh, B * T, cfg.n_layer
@@ -45,18 +48,25 @@ class FusedWorkspace:
         dev = device
         f32, bf16 = torch.float32, torch.bfloat16
         e = lambda *s, dt=f32: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
-        self.v32 = [e(M, D) for _ in range(L + 1)]
-        self.v16 = [e(M, D, dt=bf16) for _ in range(L + 1)]
-        self.x16 = [e(M, N, dt=bf16) for _ in range(L)]
-        self.q16 = [e(M, N, dt=bf16) for _ in range(L)] if cfg.rotary_embedding == "rope" else self.x16
-        self.S16 = [e(B, H, T, T, dt=bf16) for _ in range(L)]
-        self.a32 = [e(M, H, D) for _ in range(L)]
-        self.amean = [e(M * H) for _ in range(L)]
-        self.arstd = [e(M * H) for _ in range(L)]
-        self.an16 = [e(M, H, D, dt=bf16) for _ in range(L)]
-        self.yn16 = [e(M, N, dt=bf16) for _ in range(L)]
-        self.m32 = [e(M, D) for _ in range(L)]
-        self.tst = [e(M, 4) for _ in range(L)]
+        def per_layer(make, count=L):
+            if inference:
+                one = make()
+                return [one] * count
+            return [make() for _ in range(count)]
+
+        self.v32 = per_layer(lambda: e(M, D), L + 1) if not inference else [e(M, D), e(M, D)] * (L // 2 + 1)
+        self.v16 = per_layer(lambda: e(M, D, dt=bf16), L + 1) if not inference else \
+            [e(M, D, dt=bf16), e(M, D, dt=bf16)] * (L // 2 + 1)
+        self.x16 = per_layer(lambda: e(M, N, dt=bf16))
+        self.q16 = per_layer(lambda: e(M, N, dt=bf16)) if cfg.rotary_embedding == "rope" else self.x16
+        self.S16 = per_layer(lambda: e(B, H, T, T, dt=bf16))
+        self.a32 = per_layer(lambda: e(M, H, D))
+        self.amean = per_layer(lambda: e(M * H))
+        self.arstd = per_layer(lambda: e(M * H))
+        self.an16 = per_layer(lambda: e(M, H, D, dt=bf16))
+        self.yn16 = per_layer(lambda: e(M, N, dt=bf16))
+        self.m32 = per_layer(lambda: e(M, D))
+        self.tst = per_layer(lambda: e(M, 4))
         self.emb_rows = e(M, D)
         self.emean, self.erstd = e(M), e(M)
         self.logits = e(M, V)
@@ -68,6 +78,18 @@ class FusedWorkspace:
         tiles = -(-M // 128) * -(-D // G.pick_bn(D))
         self.dec_splits = G.fit_splits(kb, max(1, -(-2 * 148 // tiles)))
         self.partial = e(self.dec_splits, M, D)
+        if inference:
+            self.rho16 = None
+            self.rho_sets = None
+            self.rho_flip = 0
+            self.has_rho0 = False
+            self.qscaled = None
+            self.freq = rope_freqs(Nh, cfg.rope_theta, device=dev) if cfg.rotary_embedding == "rope" else None
+            self.log2_decay = None
+            if cfg.uses_decay():
+                g = torch.tensor(cfg.decay_slopes(), dtype=torch.float64)
+                self.log2_decay = (-g / math.log(2.0)).to(torch.float32).to(dev)
+            return
         # backward temporaries (shared across layers)
         self.dx16 = e(M, N, dt=bf16)
         self.dy16 = e(M, N, dt=bf16)
@@ -99,9 +121,14 @@ class FusedWorkspace:
             return
         B, H, Nh, D, L = self.B, self.H, self.Nh, self.D, self.L
         dev = self.v32[0].device
-        self.rho16 = [torch.empty(B, H, Nh, D, dtype=torch.bfloat16, device=dev) for _ in range(L)]
-        self.rho_sets = [[torch.empty(B, H, Nh, D, dtype=torch.float32, device=dev) for _ in range(L)]
-                         for _ in range(2)]
+        one16 = torch.empty(B, H, Nh, D, dtype=torch.bfloat16, device=dev) if self.inference else None
+        self.rho16 = [one16 if self.inference else torch.empty(B, H, Nh, D, dtype=torch.bfloat16, device=dev)
+                      for _ in range(L)]
+        if self.inference:
+            self.rho_sets = None  # inference: outgoing state overwrites the incoming one
+        else:
+            self.rho_sets = [[torch.empty(B, H, Nh, D, dtype=torch.float32, device=dev) for _ in range(L)]
+                             for _ in range(2)]
 
 
 def _bn(n: int) -> int:
@@ -134,8 +161,15 @@ class FusedBDH:
         if rho0s is not None or want_state:
             ws.ensure_state_buffers()
         if want_state:
-            out_states = ws.rho_sets[ws.rho_flip]
-            ws.rho_flip ^= 1
+            if ws.inference:
+                if rho0s is None:
+                    rho0s_buf = [torch.empty(ws.B, ws.H, ws.Nh, ws.D, device=ws.v32[0].device) for _ in range(ws.L)]
+                    out_states = rho0s_buf
+                else:
+                    out_states = list(rho0s)  # updated in place
+            else:
+                out_states = ws.rho_sets[ws.rho_flip]
+                ws.rho_flip ^= 1
         B, T, D, H, Nh, N, M, L = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L
         eps, thr = cfg.norm_eps, cfg.relu_threshold
         tok = tokens.reshape(-1)
@@ -181,7 +215,11 @@ class FusedBDH:
                     qsrc = ws.qscaled
                 if rho0s is not None:
                     gT = torch.exp2(ws.log2_decay * T).view(1, H, 1, 1) if decay else 1.0
-                    ro.copy_(rho0s[l] * gT)
+                    if ro.data_ptr() == rho0s[l].data_ptr():
+                        if decay:
+                            ro.mul_(gT)
+                    else:
+                        ro.copy_(rho0s[l] * gT)
                 G.gemm(G.EPI_F32, Operand(qsrc, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)),
                        Operand(v16, True, D, T, D, z2=(B, T * D)), Nh, D, T, ro, Z1=H, Z2=B, ld=D, sz1=Nh * D,
                        sz2=H * Nh * D, accumulate=rho0s is not None)
