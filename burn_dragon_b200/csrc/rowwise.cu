@@ -400,6 +400,7 @@ void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_
             const at::Tensor& gamma, const at::Tensor& beta, double eps, const c10::optional<at::Tensor>& y32,
             const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd) {
   c10::cuda::CUDAGuard g(x.get_device());
+  TORCH_CHECK(x.is_contiguous() && (!tokens || tokens->is_contiguous()), "ln_fwd: inputs must be contiguous");
   const int blocks = (int)((rows + kWarps - 1) / kWarps);
   dispatch_vpl((int)D, [&](auto vpl) {
     ln_fwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(x)>>>(
@@ -471,6 +472,7 @@ void cross_entropy(const at::Tensor& logits, const at::Tensor& target, const c10
                    const at::Tensor& inv_count, int64_t rows, int64_t V, const at::Tensor& loss_rows,
                    const at::Tensor& dlogits) {
   c10::cuda::CUDAGuard g(logits.get_device());
+  TORCH_CHECK(logits.is_contiguous() && target.is_contiguous(), "cross_entropy: inputs must be contiguous");
   const int blocks = (int)((rows + kWarps - 1) / kWarps);
   dispatch_vpl((int)V, [&](auto vpl) {
     ce_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(logits)>>>(

@@ -114,6 +114,7 @@ class Generator:
             state.detach_in_place()
             return logits[:, -1].float()
         cfg = self.cfg
+        tokens = tokens.contiguous()
         B = tokens.shape[0]
         if self._dws is None or self._dws.B != B:
             self._dws = _DecodeWorkspace(cfg, B, tokens.device)
