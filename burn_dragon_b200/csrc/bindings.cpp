@@ -41,6 +41,11 @@ void cast_bf16(const at::Tensor& x, const at::Tensor& y);
 void rho_step(const at::Tensor& rho, const at::Tensor& q, int64_t q_row_stride, const at::Tensor& v,
               const c10::optional<at::Tensor>& gamma, const at::Tensor& a, int64_t B, int64_t H, int64_t Nh,
               int64_t D);
+void scaffold_effective(int64_t key, double stdv, int64_t dist, int64_t rows, int64_t I, int64_t O, int64_t R,
+                        const c10::optional<at::Tensor>& A, const c10::optional<at::Tensor>& B,
+                        const c10::optional<at::Tensor>& gain, double scale, const c10::optional<at::Tensor>& out16,
+                        const c10::optional<at::Tensor>& out32, const c10::optional<at::Tensor>& base32);
+void scaffold_gain_grad(int64_t key, double stdv, int64_t dist, const at::Tensor& dW, const at::Tensor& out);
 }  // namespace bd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -57,4 +62,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_clip_coef", &bd::grad_clip_coef);
   m.def("cast_bf16", &bd::cast_bf16);
   m.def("rho_step", &bd::rho_step);
+  m.def("scaffold_effective", &bd::scaffold_effective);
+  m.def("scaffold_gain_grad", &bd::scaffold_gain_grad);
 }

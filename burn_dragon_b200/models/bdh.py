@@ -37,20 +37,36 @@ RECORD_NAMES = {
 }
 
 
+SCAFFOLD_RECORD = "random_scaffold_adapters.fast"
+
+
 def param_shapes(cfg: DragonConfig) -> dict[str, tuple[int, ...]]:
     D, H, Nh, V = cfg.n_embd, cfg.n_head, cfg.latent_per_head, cfg.vocab_size
-    shapes = {
-        "encoder": (H, D, Nh),
-        "encoder_v": (H, D, Nh),
-        "decoder": (H * Nh, D),
-        "embed": (V, D),
-        "lm_head": (D, V),
-        "norm_gamma": (D,),
-        "norm_beta": (D,),
-    }
+    if cfg.random_scaffold.enabled:
+        from .scaffold import adapter_shapes
+
+        shapes = {}
+        for k, shp in adapter_shapes(cfg).items():
+            if k.endswith(".gain") and not cfg.random_scaffold.trainable_gain:
+                continue
+            shapes[k.replace(".", "_")] = shp
+    else:
+        shapes = {"encoder": (H, D, Nh), "encoder_v": (H, D, Nh), "decoder": (H * Nh, D)}
+    shapes.update({"embed": (V, D), "lm_head": (D, V), "norm_gamma": (D,), "norm_beta": (D,)})
     if cfg.tie_input_output_embeddings:
         del shapes["lm_head"]
     return shapes
+
+
+def record_name(name: str) -> str:
+    """Reference record path of a parameter (scaffold adapters under
+    ``random_scaffold_adapters.fast.<proj>.<a|b|gain>``)."""
+    if name in RECORD_NAMES:
+        return RECORD_NAMES[name]
+    for proj in ("encoder_v", "encoder", "decoder"):
+        if name.startswith(proj + "_"):
+            return f"{SCAFFOLD_RECORD}.{proj}.{name[len(proj) + 1:]}"
+    return name
 
 
 class ParamStore:
@@ -100,26 +116,98 @@ class BDH(nn.Module):
             self.register_parameter(name, p)
         self.store.refresh_shadow()
         self._fused = None
+        self.scaffold = cfg.random_scaffold.enabled
+        if self.scaffold:
+            self._init_scaffold(device)
 
     # SimpleNormal(0.02) for every projection and the embedding, LayerNorm gamma=1,
-    # beta=0 (burn_dragon_core/src/model/init.rs:10,448-520,593-650).
+    # beta=0 (burn_dragon_core/src/model/init.rs:10,448-520,593-650); scaffold adapters:
+    # A from the scaffold generator, B = 0, gain = 1 (scaffold.rs:31-55).
     def _init_weights(self, gen: torch.Generator) -> None:
+        from .scaffold import PATHS, adapter_a_init
+
         std = self.cfg.init_std
+        rs = self.cfg.random_scaffold
         for name, shp in self.store.shapes.items():
             view = self.store.view(self.store.data, name)
-            if name == "norm_gamma":
+            if name == "norm_gamma" or name.endswith("_gain"):
                 view.fill_(1.0)
-            elif name == "norm_beta":
+            elif name == "norm_beta" or name.endswith("_b"):
                 view.zero_()
+            elif name.endswith("_a") and rs.enabled:
+                proj = name[:-2]
+                fan_in = shp[-2]
+                view.copy_(adapter_a_init(rs.seed, PATHS[proj], shp, fan_in))
             else:
                 view.copy_(torch.randn(shp, generator=gen, dtype=torch.float32) * std)
 
+    def _init_scaffold(self, device) -> None:
+        """Frozen bases: kept on the host (CPU path) or regenerated by the device kernel."""
+        from .scaffold import PATHS, base_shape, dist_code, scaffold_tensor_cpu, signed64, tensor_key
+
+        rs = self.cfg.random_scaffold
+        self.scaffold_keys = {n: signed64(tensor_key(rs.seed, PATHS[n])) for n in PATHS}
+        self.scaffold_dist = dist_code(rs.distribution)
+        self._bases: dict[str, torch.Tensor] = {}
+        if device.type != "cuda":
+            for n in PATHS:
+                self._bases[n] = scaffold_tensor_cpu(rs.seed, PATHS[n], base_shape(self.cfg, n), self.cfg.init_std,
+                                                     rs.distribution)
+        self._eff16 = None
+        self._geff = None
+
+    def scaffold_base(self, name: str) -> torch.Tensor:
+        """W_seed of a projection (fp32), regenerated on the device when needed."""
+        if name not in self._bases:
+            from .. import _ext
+            from .scaffold import base_shape
+
+            shp = base_shape(self.cfg, name)
+            out = torch.empty(shp, device=self.store.data.device)
+            rows = shp[0] * shp[1] if len(shp) == 3 else shp[0]
+            _ext.load().scaffold_effective(self.scaffold_keys[name], self.cfg.init_std, self.scaffold_dist, rows,
+                                           shp[-2] if len(shp) == 3 else rows, shp[-1], 0, None, None, None, 0.0,
+                                           None, None, out)
+            self._bases[name] = out
+        return self._bases[name]
+
+    def _scaffold_parts(self, name: str):
+        a = getattr(self, f"{name}_a")
+        b = getattr(self, f"{name}_b")
+        g = getattr(self, f"{name}_gain") if self.cfg.random_scaffold.trainable_gain else \
+            torch.ones(1, device=a.device, dtype=a.dtype)
+        return a, b, g
+
     # ---------------------------------------------------------------- helpers
     def param_dict(self) -> dict[str, torch.Tensor]:
-        d = {n: getattr(self, n) for n in self.store.shapes}
+        """The BDH weights the math consumes (effective projections for scaffold runs)."""
+        d = {n: getattr(self, n) for n in ("embed", "lm_head", "norm_gamma", "norm_beta") if n in self.store.shapes}
+        if self.scaffold:
+            from .scaffold import effective_weight
+
+            for n in ("encoder", "encoder_v", "decoder"):
+                a, b, g = self._scaffold_parts(n)
+                d[n] = effective_weight(self.cfg, n, a, b, g, self.scaffold_base(n).to(a.dtype))
+        else:
+            for n in ("encoder", "encoder_v", "decoder"):
+                d[n] = getattr(self, n)
         if "lm_head" not in d:
             d["lm_head"] = None
         return d
+
+    def fold_scaffold_for_inference(self) -> "BDH":
+        """Dense model with W = gain*W_seed + s*A@B folded in (dragon.rs:1126-1180)."""
+        import copy
+
+        cfg = copy.deepcopy(self.cfg)
+        cfg.random_scaffold.enabled = False
+        dense = BDH(cfg, device=self.store.data.device)
+        with torch.no_grad():
+            src = self.param_dict()
+            for n in dense.store.shapes:
+                getattr(dense, n).copy_(src[n].detach())
+        dense.store.refresh_shadow()
+        return dense
 
     def shadow_dict(self) -> dict[str, torch.Tensor]:
         assert self.store.shadow is not None
@@ -146,6 +234,51 @@ class BDH(nn.Module):
     def loss(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None, state=None) -> torch.Tensor:
         return R.cross_entropy(self.forward(tokens, state=state), targets, mask)
 
+    # ---------------------------------------------------------------- scaffold (fused path)
+    def _scaffold_prepare(self, p16: dict, g32: dict) -> None:
+        """Fold gain*W_seed + s*A@B into bf16 GEMM operands (W_seed regenerated in the
+        kernel, never stored) and point the projection grads at fp32 scratch buffers."""
+        from .. import _ext
+        from .scaffold import base_shape
+
+        mod = _ext.load()
+        dev = self.store.data.device
+        if self._eff16 is None:
+            self._eff16 = {n: torch.empty(base_shape(self.cfg, n), dtype=torch.bfloat16, device=dev)
+                           for n in ("encoder", "encoder_v", "decoder")}
+            self._geff = {n: torch.empty(base_shape(self.cfg, n), device=dev) for n in ("encoder", "encoder_v", "decoder")}
+        s = self.cfg.random_scaffold.adapter_scale()
+        r = self.cfg.random_scaffold.rank
+        for n in ("encoder", "encoder_v", "decoder"):
+            shp = base_shape(self.cfg, n)
+            a, b, g = self._scaffold_parts(n)
+            rows = shp[0] * shp[1] if len(shp) == 3 else shp[0]
+            I = shp[1] if len(shp) == 3 else shp[0]
+            mod.scaffold_effective(self.scaffold_keys[n], self.cfg.init_std, self.scaffold_dist, rows, I, shp[-1], r,
+                                   a.detach().reshape(rows, r), b.detach(), g.detach(), s, self._eff16[n], None, None)
+            p16[n] = self._eff16[n]
+            g32[n] = self._geff[n]
+
+    def _scaffold_backward(self, g32: dict) -> None:
+        """Adapter grads from d(W_eff): dA = s dW B^T, dB = s A^T dW, dgain = sum(dW * W_seed)."""
+        from .. import _ext
+
+        mod = _ext.load()
+        s = self.cfg.random_scaffold.adapter_scale()
+        for n in ("encoder", "encoder_v", "decoder"):
+            dW = self._geff[n]
+            a, b, _ = self._scaffold_parts(n)
+            ga = self.store.view(self.store.grad, f"{n}_a")
+            gb = self.store.view(self.store.grad, f"{n}_b")
+            torch.matmul(dW, b.detach().transpose(-1, -2), out=ga)
+            ga.mul_(s)
+            torch.matmul(a.detach().transpose(-1, -2), dW, out=gb)
+            gb.mul_(s)
+            if self.cfg.random_scaffold.trainable_gain:
+                gg = self.store.view(self.store.grad, f"{n}_gain")
+                gg.zero_()
+                mod.scaffold_gain_grad(self.scaffold_keys[n], self.cfg.init_std, self.scaffold_dist, dW, gg)
+
     # ---------------------------------------------------------------- fused path
     def fused_step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None, state=None) -> torch.Tensor:
         """Forward + CE + backward on the sm_100a kernels. Writes ``.grad`` of every
@@ -164,11 +297,16 @@ class BDH(nn.Module):
         f = self._fused
         p32 = self.store.views(self.store.data)
         p16 = self.shadow_dict()
+        g32 = self.grad_dict()
+        if self.scaffold:
+            self._scaffold_prepare(p16, g32)
         pos0 = state.position if state is not None else 0
         rho0s = state.rhos if state is not None else None
         outs = f.forward(p16, p32, tokens, pos0=pos0, rho0s=rho0s, want_state=state is not None)
         loss = f.loss(targets, mask)
-        f.backward(p16, p32, self.grad_dict(), tokens, pos0=pos0)
+        f.backward(p16, p32, g32, tokens, pos0=pos0)
+        if self.scaffold:
+            self._scaffold_backward(g32)
         if state is not None:
             state.rhos = outs
             state.position += T

@@ -175,9 +175,9 @@ class RunDir:
 
     def save(self, step: int, model, optimizer=None, scheduler: dict | None = None, runtime: dict | None = None,
              keep_last: int = 2, best_step: int | None = None) -> None:
-        from ..models.bdh import RECORD_NAMES
+        from ..models.bdh import record_name
 
-        params = {RECORD_NAMES[n]: t.detach() for n, t in model.store.views(model.store.data).items()}
+        params = {record_name(n): t.detach() for n, t in model.store.views(model.store.data).items()}
         save_tensors(self._p("model", step), params, {"schema_version": SCHEMA_VERSION, "step": step})
         if optimizer is not None:
             save_tensors(self._p("optim", step), {"m": optimizer.m, "v": optimizer.v},
@@ -222,7 +222,7 @@ class RunDir:
 
     def load(self, step: int | None, model, optimizer=None, device=None) -> dict:
         """Restore model (and optimizer) state; returns {'scheduler', 'runtime'}."""
-        from ..models.bdh import RECORD_NAMES
+        from ..models.bdh import record_name
 
         step = self.latest() if step is None else step
         if step is None:
@@ -233,9 +233,9 @@ class RunDir:
         views = model.store.views(model.store.data)
         with torch.no_grad():
             for n, v in views.items():
-                src = tensors[RECORD_NAMES[n]]
+                src = tensors[record_name(n)]
                 if tuple(src.shape) != tuple(v.shape):
-                    raise ValueError(f"{RECORD_NAMES[n]}: checkpoint shape {tuple(src.shape)} != {tuple(v.shape)}")
+                    raise ValueError(f"{record_name(n)}: checkpoint shape {tuple(src.shape)} != {tuple(v.shape)}")
                 v.copy_(src.to(v.device, v.dtype))
         model.store.refresh_shadow()
         if optimizer is not None and os.path.exists(self._p("optim", step)):
