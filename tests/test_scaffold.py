@@ -107,13 +107,39 @@ def test_fused_scaffold_step_matches_reference():
     ref = BDH(cfg, device="cuda", seed=3)
     with torch.no_grad():
         ref.store.data.copy_(model.store.data)
-    loss_ref = ref.loss(x, y)
+    pd = ref.param_dict()
+    logits, _ = R.bdh_forward(x, pd, cfg)
+    loss_ref = R.cross_entropy(logits, y)
     names = [n for n, _ in ref.named_parameters()]
-    grads = dict(zip(names, torch.autograd.grad(loss_ref, [p for _, p in ref.named_parameters()])))
+    params = [p for _, p in ref.named_parameters()]
+    effs = [pd["encoder"], pd["encoder_v"], pd["decoder"]]
+    out = torch.autograd.grad(loss_ref, params + effs)
+    grads = dict(zip(names, out[:len(params)]))
+    d_eff = dict(zip(("encoder", "encoder_v", "decoder"), out[len(params):]))
     loss = model.fused_step(x, y)
     torch.cuda.synchronize()
     assert abs(loss.item() - loss_ref.item()) < 2e-2 * loss_ref.item()
     g = model.grad_dict()
-    for n in ("encoder_a", "encoder_b", "decoder_a", "decoder_b", "encoder_v_b", "encoder_gain", "embed"):
+    for n in ("encoder_a", "encoder_b", "decoder_a", "decoder_b", "encoder_v_b", "embed"):
         rel = ((g[n] - grads[n]).norm() / (grads[n].norm() + 1e-12)).item()
         assert rel < 0.1, f"{n}: {rel:.3e}"
+    for n in ("encoder", "encoder_v", "decoder"):
+        rel = ((model._geff[n] - d_eff[n]).norm() / d_eff[n].norm()).item()
+        assert rel < 0.08, f"d{n}: {rel:.3e}"
+        # the gain gradient is a cancelling sum: judge it against the scale of its terms
+        base = model.scaffold_base(n)
+        scale = (d_eff[n] * base).abs().sum().item()
+        assert abs(g[f"{n}_gain"].item() - grads[f"{n}_gain"].item()) < 0.05 * scale
+
+
+@pytest.mark.gpu
+def test_gain_grad_kernel_matches_host_sum():
+    from burn_dragon_b200 import _ext
+
+    cfg = _cfg()
+    model = BDH(cfg, device="cuda", seed=1)
+    dW = torch.randn(S.base_shape(cfg, "encoder"), device="cuda")
+    out = torch.zeros(1, device="cuda")
+    _ext.load().scaffold_gain_grad(model.scaffold_keys["encoder"], cfg.init_std, 0, dW, out)
+    ref = (dW.double() * model.scaffold_base("encoder").double()).sum().item()
+    assert abs(out.item() - ref) < 1e-4 * (dW.abs() * model.scaffold_base("encoder").abs()).sum().item()
