@@ -90,6 +90,9 @@ def main() -> None:
     ap.add_argument("--seq", type=int, default=512)
     ap.add_argument("--layers", type=int, default=6)
     ap.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per step")
+    ap.add_argument("--comm", default="nccl", choices=["nccl", "nvlink"],
+                    help="gradient step for N > 1: NCCL all-reduce + AdamW, or the NVLink peer-memory "
+                         "reduce-scatter + sharded AdamW + all-gather kernel")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -109,7 +112,7 @@ def main() -> None:
     cfg = DragonConfig.bdh_gpu()
     cfg.n_layer = args.layers
     B, T = args.batch, args.seq
-    trainer = Trainer(cfg, dev, lr=1e-3, weight_decay=0.1, seed=1337)
+    trainer = Trainer(cfg, dev, lr=1e-3, weight_decay=0.1, seed=1337, comm=args.comm)
     data = RandomBytes(B, T, seed=20260729, rank=rank, world=world, pin=True)
     # Device-resident batches for the kernel-only timing (inputs staged before the clock).
     dev_batches = [tuple(t.to(dev) for t in data.next()) for _ in range(2)]
@@ -188,7 +191,7 @@ def main() -> None:
             "dtype": "bf16",
             "data": "synthetic (seeded uniform random bytes), random-init weights",
             "config": {"model": "BDH-GPU d256 n32768 h4 L%d RoPE vocab256" % cfg.n_layer, "global_batch": B * world,
-                       "seq_len": T, "parallelism": f"dp{world}", "optimizer": "AdamW (fused, fp32 master)",
+                       "seq_len": T, "parallelism": f"dp{world}", "comm": args.comm if world > 1 else "none", "optimizer": "AdamW (fused, fp32 master)",
                        "l2": "inputs larger than L2 (~20 GB activations per step)",
                        "baseline_ref": "P1: 23,311 wall tok/s on GB10 (L4 d256 latent4096)"},
             "clocks": clocks,

@@ -46,6 +46,20 @@ void scaffold_effective(int64_t key, double stdv, int64_t dist, int64_t rows, in
                         const c10::optional<at::Tensor>& gain, double scale, const c10::optional<at::Tensor>& out16,
                         const c10::optional<at::Tensor>& out32, const c10::optional<at::Tensor>& base32);
 void scaffold_gain_grad(int64_t key, double stdv, int64_t dist, const at::Tensor& dW, const at::Tensor& out);
+int64_t sym_alloc(int64_t bytes, int64_t device);
+void sym_free(int64_t ptr, int64_t device);
+std::vector<int64_t> ipc_handle(int64_t ptr, int64_t device);
+int64_t ipc_open(std::vector<int64_t> handle, int64_t device);
+void ipc_close(int64_t ptr, int64_t device);
+at::Tensor wrap_ptr(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
+void peer_barrier(std::vector<int64_t> grad, std::vector<int64_t> param, std::vector<int64_t> shadow,
+                  std::vector<int64_t> flags, int64_t rank, int64_t phase, const at::Tensor& err);
+void reduce_adamw(std::vector<int64_t> grad, std::vector<int64_t> param, std::vector<int64_t> shadow,
+                  std::vector<int64_t> flags, int64_t rank, int64_t lo, int64_t hi, const at::Tensor& m,
+                  const at::Tensor& v, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
+                  const c10::optional<at::Tensor>& hyper);
+void reduce_mean(std::vector<int64_t> grad, std::vector<int64_t> flags, int64_t rank, int64_t lo, int64_t hi,
+                 const at::Tensor& err);
 }  // namespace bd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -64,4 +78,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rho_step", &bd::rho_step);
   m.def("scaffold_effective", &bd::scaffold_effective);
   m.def("scaffold_gain_grad", &bd::scaffold_gain_grad);
+  m.def("sym_alloc", &bd::sym_alloc);
+  m.def("sym_free", &bd::sym_free);
+  m.def("ipc_handle", &bd::ipc_handle);
+  m.def("ipc_open", &bd::ipc_open);
+  m.def("ipc_close", &bd::ipc_close);
+  m.def("wrap_ptr", &bd::wrap_ptr);
+  m.def("peer_barrier", &bd::peer_barrier);
+  m.def("reduce_adamw", &bd::reduce_adamw);
+  m.def("reduce_mean", &bd::reduce_mean);
 }

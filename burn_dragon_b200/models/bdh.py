@@ -99,6 +99,17 @@ class ParamStore:
         if self.shadow is not None:
             self.shadow.copy_(self.data)
 
+    def rebind(self, data: torch.Tensor, grad: torch.Tensor, shadow: torch.Tensor | None) -> None:
+        """Move the flat buffers into caller-owned memory (e.g. symmetric IPC memory);
+        the new buffers may be longer than ``numel`` (the tail stays zero)."""
+        with torch.no_grad():
+            data[:self.numel].copy_(self.data)
+            grad[:self.numel].copy_(self.grad)
+            if shadow is not None:
+                shadow[:self.numel].copy_(self.data)
+        self.data, self.grad = data, grad
+        self.shadow = shadow if shadow is not None else self.shadow
+
 
 class BDH(nn.Module):
     def __init__(self, cfg: DragonConfig, device=None, seed: int | None = None):
@@ -177,6 +188,15 @@ class BDH(nn.Module):
         g = getattr(self, f"{name}_gain") if self.cfg.random_scaffold.trainable_gain else \
             torch.ones(1, device=a.device, dtype=a.dtype)
         return a, b, g
+
+    def attach_buffers(self, data: torch.Tensor, grad: torch.Tensor, shadow: torch.Tensor | None) -> None:
+        """Re-home parameters, grads and the bf16 shadow (see ``ParamStore.rebind``)."""
+        self.store.rebind(data, grad, shadow)
+        for name in self.store.shapes:
+            p = nn.Parameter(self.store.view(self.store.data, name))
+            p.grad = self.store.view(self.store.grad, name)
+            setattr(self, name, p)
+        self._fused = None
 
     # ---------------------------------------------------------------- helpers
     def param_dict(self) -> dict[str, torch.Tensor]:

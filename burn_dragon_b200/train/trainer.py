@@ -49,8 +49,17 @@ class Trainer:
         self.base_lr = lr
         self.step_idx = 0
         self.world = dist.get_world_size() if dist.is_initialized() else 1
-        self.comm = comm  # optional custom gradient communicator (parallel.ddp)
         self.fused = self.device.type == "cuda"
+        # comm: None / "nccl" (all-reduce + full AdamW on every rank) or "nvlink"
+        # (symmetric-memory reduce-scatter + sharded AdamW + all-gather, parallel.ddp)
+        self.comm = None
+        if comm == "nvlink" and self.world > 1:
+            from ..parallel.ddp import NVLinkDDP
+
+            if grad_clip_norm is not None:
+                raise ValueError("the NVLink DDP step does not implement global-norm clipping; use comm='nccl'")
+            self.comm = NVLinkDDP(self.model.store.numel, self.device)
+            self.model.attach_buffers(self.comm.param, self.comm.grad, self.comm.shadow)
         self._graph = None
         self._graph_shape = None
         self._graph_launches = 0
@@ -81,18 +90,24 @@ class Trainer:
         before = _ext.launch_count()
         with torch.cuda.graph(g):
             self._sloss = self.compute_grads(self._sx, self._sy)
-            self.allreduce_grads()
-            self.opt.apply()
+            self._update()
         self._graph_launches = _ext.launch_count() - before
         self.opt.t -= 1  # the capture itself did not update anything
         self._graph = g
         self._graph_shape = (tuple(tokens.shape), tuple(targets.shape))
 
+    def _update(self) -> None:
+        """Gradient reduction + optimizer update (device work only; capturable)."""
+        if self.comm is not None:
+            self.comm.step_adamw(self.opt)
+        else:
+            self.allreduce_grads()
+            self.opt.apply()
+
     def _eager_device_step(self, tokens, targets, mask=None) -> torch.Tensor:
         loss = self.compute_grads(tokens, targets, mask)
-        self.allreduce_grads()
         self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
-        self.opt.apply()
+        self._update()
         self.step_idx += 1
         return loss
 
@@ -107,11 +122,8 @@ class Trainer:
         return loss.detach()
 
     def allreduce_grads(self) -> None:
-        if self.world == 1:
-            return
-        if self.comm is not None:
-            self.comm.allreduce_mean(self.model.store.grad)
-            return
+        if self.world == 1 or self.comm is not None:
+            return  # the NVLink communicator reduces inside its fused optimizer step
         op = dist.ReduceOp.AVG if dist.get_backend() == "nccl" else dist.ReduceOp.SUM
         dist.all_reduce(self.model.store.grad, op=op)
         if op == dist.ReduceOp.SUM:
@@ -134,8 +146,7 @@ class Trainer:
         if mask is not None:
             mask = mask.to(self.device, non_blocking=True)
         loss = self.compute_grads(tokens, targets, mask)
-        self.allreduce_grads()
-        lr = lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters)
-        self.opt.step(lr)
+        self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
+        self._update()
         self.step_idx += 1
         return loss

@@ -1,0 +1,60 @@
+"""NVLink peer-memory DDP step (symmetric IPC buffers, fused reduce-scatter + sharded
+AdamW + all-gather) vs the NCCL all-reduce + AdamW path, on 2 GPUs as child processes.
+Skipped unless at least 2 GPUs are visible."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, out):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    from burn_dragon_b200.config import DragonConfig
+    from burn_dragon_b200.train.trainer import Trainer
+
+    cfg = DragonConfig(n_layer=2, n_embd=64, n_head=2, mlp_internal_dim_multiplier=8, dropout=0.0,
+                       rotary_embedding="rope")
+    dev = torch.device("cuda", rank)
+    g = torch.Generator().manual_seed(10 + rank)
+    batches = [(torch.randint(0, 256, (2, 128), generator=g), torch.randint(0, 256, (2, 128), generator=g))
+               for _ in range(3)]
+    res = {}
+    for comm in ("nccl", "nvlink"):
+        tr = Trainer(cfg, dev, lr=1e-3, seed=3, comm=comm)
+        for x, y in batches:
+            tr.step(x.to(dev), y.to(dev))
+        torch.cuda.synchronize()
+        if tr.comm is not None:
+            tr.comm.check()
+        res[comm] = tr.model.store.data[:tr.model.store.numel].cpu().clone()
+        if tr.comm is not None:
+            tr.comm.close()
+    out[rank] = res
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_nvlink_step_matches_nccl_step():
+    out = mp.Manager().dict()
+    mp.spawn(_worker, args=(2, _port(), out), nprocs=2, join=True)
+    a, b = out[0], out[1]
+    assert torch.equal(a["nvlink"], b["nvlink"])  # replicas identical
+    assert torch.allclose(a["nvlink"], a["nccl"], atol=1e-6, rtol=1e-5)
