@@ -127,6 +127,7 @@ class BDH(nn.Module):
             self.register_parameter(name, p)
         self.store.refresh_shadow()
         self._fused = None
+        self.tp = None  # parallel.tp.TensorParallel when this model holds a head shard
         self.scaffold = cfg.random_scaffold.enabled
         if self.scaffold:
             self._init_scaffold(device)
@@ -300,7 +301,8 @@ class BDH(nn.Module):
                 mod.scaffold_gain_grad(self.scaffold_keys[n], self.cfg.init_std, self.scaffold_dist, dW, gg)
 
     # ---------------------------------------------------------------- fused path
-    def fused_step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None, state=None) -> torch.Tensor:
+    def fused_step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None, state=None,
+                   accumulate: bool = False, loss_scale: float = 1.0) -> torch.Tensor:
         """Forward + CE + backward on the sm_100a kernels. Writes ``.grad`` of every
         parameter (the flat grad buffer) and returns the loss as a device scalar.
 
@@ -313,7 +315,7 @@ class BDH(nn.Module):
         if self._fused is None or self._fused.ws.B != B or self._fused.ws.T != T:
             self._fused = None
             torch.cuda.empty_cache()
-            self._fused = FusedBDH(self.cfg, FusedWorkspace(self.cfg, B, T, tokens.device))
+            self._fused = FusedBDH(self.cfg, FusedWorkspace(self.cfg, B, T, tokens.device), tp=self.tp)
         f = self._fused
         p32 = self.store.views(self.store.data)
         p16 = self.shadow_dict()
@@ -323,8 +325,8 @@ class BDH(nn.Module):
         pos0 = state.position if state is not None else 0
         rho0s = state.rhos if state is not None else None
         outs = f.forward(p16, p32, tokens, pos0=pos0, rho0s=rho0s, want_state=state is not None)
-        loss = f.loss(targets, mask)
-        f.backward(p16, p32, g32, tokens, pos0=pos0)
+        loss = f.loss(targets, mask, scale=loss_scale)
+        f.backward(p16, p32, g32, tokens, pos0=pos0, accumulate=accumulate)
         if self.scaffold:
             self._scaffold_backward(g32)
         if state is not None:

@@ -138,7 +138,11 @@ def _bn(n: int) -> int:
 class FusedBDH:
     """Runs forward + CE + backward of the BDH stack for a fixed workspace."""
 
-    def __init__(self, cfg, ws: FusedWorkspace):
+    def __init__(self, cfg, ws: FusedWorkspace, tp=None):
+        """``tp``: optional ``parallel.tp.TensorParallel``; the workspace then holds this
+        rank's heads only and the decoder / residual-gradient partials are summed over
+        the tensor-parallel group."""
+        self.tp = tp
         if cfg.dropout != 0.0:
             raise ValueError("the fused path implements dropout = 0 (as the BDH-GPU profiles use)")
         if cfg.tie_input_output_embeddings:
@@ -231,36 +235,54 @@ class FusedBDH:
             # m = yn E (split-K partials), v' = LN(v + LN(m))
             G.gemm(G.EPI_F32, Operand(ws.yn16[l], False, N, M, N), B_dec, M, D, N, ws.partial,
                    splits=ws.dec_splits, ld=D, split_stride=M * D)
-            mod.tail_fwd(ws.partial, ws.dec_splits, M * D, ws.v32[l], M, D, p32["norm_gamma"], p32["norm_beta"],
-                         eps, ws.m32[l], ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
+            if self.tp is not None and self.tp.world > 1:
+                # sum this rank's split-K partials, then over the tensor-parallel group
+                msum = ws.partial[0]
+                if ws.dec_splits > 1:
+                    mod.sum_rows(ws.m32[l], msum, ws.partial[1:], ws.dec_splits - 1, M * D, None, 0, 0, M * D)
+                else:
+                    ws.m32[l].copy_(msum)
+                self.tp.all_reduce(ws.m32[l])
+                mod.tail_fwd(ws.m32[l], 1, M * D, ws.v32[l], M, D, p32["norm_gamma"], p32["norm_beta"], eps, None,
+                             ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
+            else:
+                mod.tail_fwd(ws.partial, ws.dec_splits, M * D, ws.v32[l], M, D, p32["norm_gamma"],
+                             p32["norm_beta"], eps, ws.m32[l], ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
         G.gemm(G.EPI_F32, Operand(ws.v16[L], False, D, M, D), Operand(p16["lm_head"], True, ws.V, D, ws.V),
                M, ws.V, D, ws.logits, ld=ws.V)
         return out_states
 
-    def loss(self, targets: torch.Tensor, mask: torch.Tensor | None = None) -> torch.Tensor:
+    def loss(self, targets: torch.Tensor, mask: torch.Tensor | None = None, scale: float = 1.0) -> torch.Tensor:
+        """Token-mean CE; ``scale`` multiplies the loss and its gradient (1/n for an
+        n-micro-batch accumulation)."""
         ws = self.ws
         if mask is not None:
-            ws.inv_count.copy_(1.0 / mask.float().sum().clamp_min(1.0))
+            ws.inv_count.copy_(scale / mask.float().sum().clamp_min(1.0))
             m = mask.reshape(-1).float().contiguous()
         else:
-            ws.inv_count.fill_(1.0 / ws.M)
+            ws.inv_count.fill_(scale / ws.M)
             m = None
-        self.mod.cross_entropy(ws.logits, targets.reshape(-1), m, ws.inv_count, ws.M, ws.V, ws.loss_rows,
+        self.mod.cross_entropy(ws.logits, targets.reshape(-1).contiguous(), m, ws.inv_count, ws.M, ws.V, ws.loss_rows,
                                ws.dlogits16)
         return ws.loss_rows.sum() * ws.inv_count[0]
 
     # ---------------------------------------------------------------- backward
-    def backward(self, p16: dict, p32: dict, g32: dict, tokens: torch.Tensor, pos0: int = 0) -> None:
-        """Writes parameter gradients into g32 (overwrites)."""
+    def backward(self, p16: dict, p32: dict, g32: dict, tokens: torch.Tensor, pos0: int = 0,
+                 accumulate: bool = False) -> None:
+        """Writes parameter gradients into g32 (``accumulate``: adds to them, for
+        gradient accumulation over micro-batches)."""
         ws, cfg, mod = self.ws, self.cfg, self.mod
         B, T, D, H, Nh, N, M, L, V = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L, ws.V
         gam, bet = p32["norm_gamma"], p32["norm_beta"]
-        for k in ("encoder", "encoder_v", "decoder"):
-            g32[k].zero_()
-        parts = []
+        tp = self.tp if self.tp is not None and self.tp.world > 1 else None
+        if not accumulate:
+            for k in ("encoder", "encoder_v", "decoder"):
+                g32[k].zero_()
+        parts = []       # norm-grad partials identical on every tensor-parallel rank
+        head_parts = []  # norm-grad partials of this rank's heads (summed over the group)
         # lm head
         G.gemm(G.EPI_F32, Operand(ws.v16[L], True, D, M, D), Operand(ws.dlogits16, True, V, M, V), D, V, M,
-               g32["lm_head"], ld=V)
+               g32["lm_head"], ld=V, accumulate=accumulate)
         dv = ws.dv[0]
         G.gemm(G.EPI_F32, Operand(ws.dlogits16, False, V, M, V), Operand(p16["lm_head"], False, V, D, V), M, D, V,
                dv, ld=D)
@@ -282,7 +304,7 @@ class FusedBDH:
             G.gemm(G.EPI_F32, Operand(ws.dy16, False, Nh, M, N, z1=(H, Nh)),
                    Operand(encv, False, Nh, D, Nh, z1=(H, D * Nh)), M, D, Nh, ws.dan32, Z1=H, ld=H * D, sz1=D)
             # dC = LN^T(d an), written as [B,H,T,D]
-            parts.append(mod.ln_bwd(ws.dan32, ws.a32[l], ws.amean[l], ws.arstd[l], M * H, D, gam, T, H, ws.dC16,
+            head_parts.append(mod.ln_bwd(ws.dan32, ws.a32[l], ws.amean[l], ws.arstd[l], M * H, D, gam, T, H, ws.dC16,
                                     None))
             # P = dC V^T ; G = mask(P) + mask(P)^T
             dcop = Operand(ws.dC16, False, D, T, D, z1=(H, T * D), z2=(B, H * T * D))
@@ -310,13 +332,27 @@ class FusedBDH:
             G.gemm(G.EPI_F32, Operand(ws.dx16, False, Nh, M, N, z1=(H, Nh)),
                    Operand(enc, False, Nh, D, Nh, z1=(H, D * Nh)), M, D, Nh, ws.dvx32, Z1=H, ld=D, sz1=M * D)
             dv_next = ws.dv[1] if dv is ws.dv[0] else ws.dv[0]
-            mod.sum_rows(dv_next, ws.dv_res, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)
+            if tp is not None:
+                mod.sum_rows(dv_next, None, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)
+                tp.all_reduce(dv_next)
+                dv_next.add_(ws.dv_res)
+            else:
+                mod.sum_rows(dv_next, ws.dv_res, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)
             dv = dv_next
         # embedding LayerNorm and gather
         demb = ws.dv_res  # reuse as fp32 [M, D] scratch
         parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb))
-        g32["embed"].zero_()
+        if not accumulate:
+            g32["embed"].zero_()
         g32["embed"].index_add_(0, tokens.reshape(-1), demb)
         allp = torch.cat(parts, 0).sum(0)
-        g32["norm_gamma"].copy_(allp[0])
-        g32["norm_beta"].copy_(allp[1])
+        hp = torch.cat(head_parts, 0).sum(0)
+        if tp is not None:
+            tp.all_reduce(hp)
+        allp = allp + hp
+        if accumulate:
+            g32["norm_gamma"].add_(allp[0])
+            g32["norm_beta"].add_(allp[1])
+        else:
+            g32["norm_gamma"].copy_(allp[0])
+            g32["norm_beta"].copy_(allp[1])

@@ -38,17 +38,36 @@ def init_distributed() -> tuple[int, int, int]:
 
 class Trainer:
     def __init__(self, cfg: DragonConfig, device, lr=1e-3, weight_decay=0.1, betas=(0.9, 0.999), eps=1e-8,
-                 grad_clip_norm=None, seed=1337, lr_schedule=None, max_iters=1000, comm=None):
+                 grad_clip_norm=None, seed=1337, lr_schedule=None, max_iters=1000, comm=None,
+                 tensor_parallel: bool = False, micro_batches: int = 1):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.model = BDH(cfg, device=self.device, seed=seed)
+        self.micro_batches = micro_batches
+        self.tp = None
+        if tensor_parallel:
+            from ..parallel.tp import TensorParallel
+
+            self.tp = TensorParallel()
+            local = self.tp.local_config(cfg)
+            self.model = BDH(local, device=self.device, seed=seed)
+            # replicated tensors share the seed; each rank's heads get their own stream
+            g = torch.Generator().manual_seed(seed * 1009 + 17 + self.tp.rank)
+            with torch.no_grad():
+                for n in ("encoder", "encoder_v", "decoder"):
+                    p = getattr(self.model, n)
+                    p.copy_(torch.randn(p.shape, generator=g) * cfg.init_std)
+            self.model.store.refresh_shadow()
+            self.model.tp = self.tp
+        else:
+            self.model = BDH(cfg, device=self.device, seed=seed)
         self.opt = FusedAdamW(self.model.store, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                               grad_clip_norm=grad_clip_norm)
         self.lr_schedule = lr_schedule
         self.max_iters = max_iters
         self.base_lr = lr
         self.step_idx = 0
-        self.world = dist.get_world_size() if dist.is_initialized() else 1
+        # data-parallel world (tensor parallelism alone replicates the batch)
+        self.world = 1 if self.tp is not None else (dist.get_world_size() if dist.is_initialized() else 1)
         self.fused = self.device.type == "cuda"
         # comm: None / "nccl" (all-reduce + full AdamW on every rank) or "nvlink"
         # (symmetric-memory reduce-scatter + sharded AdamW + all-gather, parallel.ddp)
@@ -112,6 +131,18 @@ class Trainer:
         return loss
 
     def compute_grads(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None) -> torch.Tensor:
+        n = self.micro_batches
+        if self.fused and n > 1:
+            B = tokens.shape[0]
+            assert B % n == 0, "batch must split evenly into micro-batches"
+            b = B // n
+            total = None
+            for i in range(n):
+                sl = slice(i * b, (i + 1) * b)
+                li = self.model.fused_step(tokens[sl], targets[sl], None if mask is None else mask[sl],
+                                           accumulate=i > 0, loss_scale=1.0 / n)
+                total = li if total is None else total + li
+            return total
         if self.fused:
             return self.model.fused_step(tokens, targets, mask)
         self.model.zero_grad(set_to_none=False)
