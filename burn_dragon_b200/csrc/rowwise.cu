@@ -389,6 +389,13 @@ T* opt_ptr(const c10::optional<at::Tensor>& t) {
   return t ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
 }
 
+// The dgamma/dbeta block reduction needs kWarps * 2 * D floats of dynamic smem (64 KB at
+// D = 1024): opt in above the 48 KB default once per kernel.
+template <typename K>
+void allow_smem(K kern, size_t bytes) {
+  if (bytes > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+}
+
 int part_blocks(long long rows) {
   const long long need = (rows + kWarps - 1) / kWarps;
   return (int)std::min<long long>(need, 148 * 8);
@@ -419,6 +426,7 @@ at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& m
   const int blocks = part_blocks(rows);
   auto part = at::empty({blocks, 2, D}, x.options().dtype(at::kFloat));
   dispatch_vpl((int)D, [&](auto vpl) {
+    allow_smem(ln_bwd_kernel<decltype(vpl)::value>, kWarps * 2 * D * sizeof(float));
     ln_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * 2 * D * sizeof(float), cur_stream(x)>>>(
         dy.data_ptr<float>(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, (int)D,
         gamma.data_ptr<float>(), (int)remap_T, (int)remap_H, opt_ptr<__nv_bfloat16>(dx16), opt_ptr<float>(dx32),
@@ -450,6 +458,7 @@ at::Tensor tail_bwd(const at::Tensor& gin, const at::Tensor& v, const at::Tensor
   const int blocks = part_blocks(rows);
   auto part = at::empty({blocks, 2, D}, v.options().dtype(at::kFloat));
   dispatch_vpl((int)D, [&](auto vpl) {
+    allow_smem(tail_bwd_kernel<decltype(vpl)::value>, kWarps * 2 * D * sizeof(float));
     tail_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * 2 * D * sizeof(float), cur_stream(v)>>>(
         gin.data_ptr<float>(), v.data_ptr<float>(), m.data_ptr<float>(), st.data_ptr<float>(), rows, (int)D,
         gamma.data_ptr<float>(), beta.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dm16.data_ptr()),
