@@ -152,12 +152,15 @@ class FusedBDH:
         self.mod = _ext.load()
 
     # ---------------------------------------------------------------- forward
-    def forward(self, p16: dict, p32: dict, tokens: torch.Tensor, pos0: int = 0, rho0s=None,
-                want_state: bool = False):
+    def forward(self, p16: dict, p32: dict, tokens: torch.Tensor | None, pos0: int = 0, rho0s=None,
+                want_state: bool = False, v_in: torch.Tensor | None = None, with_head: bool = True):
         """Forward of the stack. With ``rho0s`` (per-layer fp32 [B,H,Nh,D]) the carried
         linear-attention state enters every layer (C += gamma^t q rho0); with
         ``want_state`` the per-layer final states are returned (fp32, owned by the
-        workspace: valid until the step after next)."""
+        workspace: valid until the step after next).
+
+        Pipeline stages: ``v_in`` ([M, D] fp32) replaces the embedding (a later stage),
+        ``with_head=False`` stops after this stage's layers (the output is ``ws.v32[L]``)."""
         ws, cfg, mod = self.ws, self.cfg, self.mod
         decay = ws.log2_decay is not None
         ws.has_rho0 = rho0s is not None
@@ -176,10 +179,14 @@ class FusedBDH:
                 ws.rho_flip ^= 1
         B, T, D, H, Nh, N, M, L = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L
         eps, thr = cfg.norm_eps, cfg.relu_threshold
-        tok = tokens.reshape(-1)
-        torch.index_select(p32["embed"], 0, tok, out=ws.emb_rows)
-        mod.ln_fwd(ws.emb_rows, None, M, D, p32["norm_gamma"], p32["norm_beta"], eps, ws.v32[0], ws.v16[0],
-                   ws.emean, ws.erstd)
+        if v_in is None:
+            tok = tokens.reshape(-1)
+            torch.index_select(p32["embed"], 0, tok, out=ws.emb_rows)
+            mod.ln_fwd(ws.emb_rows, None, M, D, p32["norm_gamma"], p32["norm_beta"], eps, ws.v32[0], ws.v16[0],
+                       ws.emean, ws.erstd)
+        else:
+            ws.v32[0].copy_(v_in.reshape(M, D))
+            ws.v16[0].copy_(ws.v32[0])
         enc, encv, dec = p16["encoder"], p16["encoder_v"], p16["decoder"]
         B_enc = Operand(enc, True, Nh, D, Nh, z1=(H, D * Nh))
         B_encv = Operand(encv, True, Nh, D, Nh, z1=(H, D * Nh))
@@ -248,8 +255,9 @@ class FusedBDH:
             else:
                 mod.tail_fwd(ws.partial, ws.dec_splits, M * D, ws.v32[l], M, D, p32["norm_gamma"],
                              p32["norm_beta"], eps, ws.m32[l], ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
-        G.gemm(G.EPI_F32, Operand(ws.v16[L], False, D, M, D), Operand(p16["lm_head"], True, ws.V, D, ws.V),
-               M, ws.V, D, ws.logits, ld=ws.V)
+        if with_head:
+            G.gemm(G.EPI_F32, Operand(ws.v16[L], False, D, M, D), Operand(p16["lm_head"], True, ws.V, D, ws.V),
+                   M, ws.V, D, ws.logits, ld=ws.V)
         return out_states
 
     def loss(self, targets: torch.Tensor, mask: torch.Tensor | None = None, scale: float = 1.0) -> torch.Tensor:
@@ -267,10 +275,14 @@ class FusedBDH:
         return ws.loss_rows.sum() * ws.inv_count[0]
 
     # ---------------------------------------------------------------- backward
-    def backward(self, p16: dict, p32: dict, g32: dict, tokens: torch.Tensor, pos0: int = 0,
-                 accumulate: bool = False) -> None:
+    def backward(self, p16: dict, p32: dict, g32: dict, tokens: torch.Tensor | None, pos0: int = 0,
+                 accumulate: bool = False, dv_out: torch.Tensor | None = None, with_embed: bool = True):
         """Writes parameter gradients into g32 (``accumulate``: adds to them, for
-        gradient accumulation over micro-batches)."""
+        gradient accumulation over micro-batches).
+
+        Pipeline stages: ``dv_out`` ([M, D] fp32, the gradient of this stage's output)
+        replaces the LM head / CE backward; ``with_embed=False`` stops at this stage's
+        input and returns its gradient (a view of a workspace buffer)."""
         ws, cfg, mod = self.ws, self.cfg, self.mod
         B, T, D, H, Nh, N, M, L, V = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L, ws.V
         gam, bet = p32["norm_gamma"], p32["norm_beta"]
@@ -280,12 +292,17 @@ class FusedBDH:
                 g32[k].zero_()
         parts = []       # norm-grad partials identical on every tensor-parallel rank
         head_parts = []  # norm-grad partials of this rank's heads (summed over the group)
-        # lm head
-        G.gemm(G.EPI_F32, Operand(ws.v16[L], True, D, M, D), Operand(ws.dlogits16, True, V, M, V), D, V, M,
-               g32["lm_head"], ld=V, accumulate=accumulate)
         dv = ws.dv[0]
-        G.gemm(G.EPI_F32, Operand(ws.dlogits16, False, V, M, V), Operand(p16["lm_head"], False, V, D, V), M, D, V,
-               dv, ld=D)
+        if dv_out is None:
+            # lm head
+            G.gemm(G.EPI_F32, Operand(ws.v16[L], True, D, M, D), Operand(ws.dlogits16, True, V, M, V), D, V, M,
+                   g32["lm_head"], ld=V, accumulate=accumulate)
+            G.gemm(G.EPI_F32, Operand(ws.dlogits16, False, V, M, V), Operand(p16["lm_head"], False, V, D, V), M, D,
+                   V, dv, ld=D)
+        else:
+            if not accumulate and "lm_head" in g32:
+                g32["lm_head"].zero_()
+            dv.copy_(dv_out.reshape(M, D))
         enc, encv, dec = p16["encoder"], p16["encoder_v"], p16["decoder"]
         for l in reversed(range(L)):
             v16 = ws.v16[l]
@@ -339,12 +356,15 @@ class FusedBDH:
             else:
                 mod.sum_rows(dv_next, ws.dv_res, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)
             dv = dv_next
-        # embedding LayerNorm and gather
-        demb = ws.dv_res  # reuse as fp32 [M, D] scratch
-        parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb))
-        if not accumulate:
+        if with_embed:
+            # embedding LayerNorm and gather
+            demb = ws.dv_res  # reuse as fp32 [M, D] scratch
+            parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb))
+            if not accumulate:
+                g32["embed"].zero_()
+            g32["embed"].index_add_(0, tokens.reshape(-1), demb)
+        elif not accumulate:
             g32["embed"].zero_()
-        g32["embed"].index_add_(0, tokens.reshape(-1), demb)
         allp = torch.cat(parts, 0).sum(0)
         hp = torch.cat(head_parts, 0).sum(0)
         if tp is not None:
@@ -356,3 +376,4 @@ class FusedBDH:
         else:
             g32["norm_gamma"].copy_(allp[0])
             g32["norm_beta"].copy_(allp[1])
+        return None if with_embed else dv
