@@ -1,0 +1,164 @@
+"""Top-level training driver: ``train(TrainingConfig)``.
+
+Mirrors the reference's ``train_backend`` flow (burn_dragon_language/src/train/
+backend.rs:1187-1915): resolve the parallel runtime from WORLD_SIZE / RANK / LOCAL_RANK,
+seed, create the run directory and write ``config.json`` / ``training_config.json`` /
+``tokenizer.json`` (and ``random_scaffold_manifest.json``), build the model and AdamW,
+resume from the newest checkpoint, then run the step loop with metrics, periodic
+validation and checkpoints, the non-finite-loss interrupter and peer heartbeats.
+
+Parallel modes (``[parallel] mode``): ``single``; ``ddp`` (NVLink peer-memory step on
+CUDA, gloo/NCCL all-reduce otherwise); ``tensor_parallel_neuron`` (head-aligned neuron
+sharding); ``pipeline`` (``[parallel.pipeline] schedule / micro_batches``); ``fsdp`` maps
+to ``ddp`` with the partitioned (sharded-moment) optimizer step.
+
+Sequence batching: ``random`` windows, or ``streaming`` with stateful TBPTT
+(``tbptt_chunk_size``, ``tbptt_persist_across_steps``): every step trains the next chunk
+of each stream with the linear-attention state carried (detached) from the previous
+chunk, reset at stream starts (burn_dragon_language/src/train/steps.rs:2698-2731,
+11860-11960); the state is saved in ``runtime-state-<step>.bin``.
+"""
+
+from __future__ import annotations
+
+import os
+import time
+
+import torch
+import torch.distributed as dist
+
+from ..config import TrainingConfig
+from ..models.state import ModelState
+from ..parallel.fault import Heartbeat, NonFiniteGuard, PeerFailure
+from . import checkpoint as C
+from .data import RandomBytes, StreamingBytes
+from .metrics import MetricsLogger, StageProfiler
+from .trainer import Trainer, init_distributed
+
+
+def _device(local: int) -> torch.device:
+    return torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+
+
+def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True) -> dict:
+    rank, world, local = init_distributed()
+    dev = _device(local)
+    if dev.type == "cuda":
+        torch.cuda.set_device(dev)
+    t = cfg.training
+    mode = cfg.parallel.mode
+    torch.manual_seed(t.seed + rank)
+    run = C.RunDir(C.resolve_run_dir(dev.type, run_name))
+    if rank == 0:
+        run.write_run_config(cfg)
+        if cfg.model.random_scaffold.enabled:
+            from ..models import scaffold as S
+
+            man_path = os.path.join(run.path, "random_scaffold_manifest.json")
+            if os.path.exists(man_path):
+                import json
+
+                S.check_manifest(json.load(open(man_path)), cfg.model)
+            else:
+                S.write_manifest(man_path, cfg.model)
+    o = cfg.optimizer
+    comm = None
+    if mode in ("ddp", "fsdp") and world > 1 and dev.type == "cuda":
+        comm = "nvlink" if o.grad_clip_norm is None else "nccl"
+    micro = int(cfg.parallel.tensor.get("micro_batches", t.gradient_accumulation_steps))
+    trainer = Trainer(cfg.model, dev, lr=o.learning_rate, weight_decay=o.weight_decay, betas=(o.beta1, o.beta2),
+                      eps=o.eps, grad_clip_norm=o.grad_clip_norm, seed=t.seed, lr_schedule=o.lr_schedule,
+                      max_iters=t.max_iters, comm=comm, tensor_parallel=mode == "tensor_parallel_neuron",
+                      micro_batches=micro if mode != "pipeline" else 1)
+    runner = None
+    if mode == "pipeline":
+        from ..parallel.pipeline import PipelineRunner, plan
+
+        pp = cfg.parallel.pipeline
+        pl = plan(cfg.model.n_layer, world, int(pp.get("micro_batches", 4)), pp.get("schedule", "1f1b"))
+        runner = PipelineRunner(trainer.model, pl, rank, t.batch_size // pl.micro, t.block_size)
+
+    start = 0
+    state = None
+    if resume and run.latest() is not None:
+        info = run.load(None, trainer.model, trainer.opt, device=dev)
+        start = info["step"]
+        trainer.step_idx = start
+        rt = info.get("runtime")
+        if rt and rt.get("rhos") is not None:
+            state = ModelState(rt["rhos"], int(rt.get("position", 0)))
+    streaming = t.sequence_batching == "streaming" or t.tbptt_persist_across_steps
+    data_rank = 0 if mode in ("tensor_parallel_neuron", "pipeline") else rank
+    data_world = 1 if mode in ("tensor_parallel_neuron", "pipeline") else world
+    if streaming:
+        chunk = t.tbptt_chunk_size or t.block_size
+        data = StreamingBytes(t.batch_size, t.block_size, chunk, seed=t.seed, rank=data_rank)
+        data.pos = (start * chunk) % max(1, t.block_size - chunk + 1) if t.block_size > chunk else 0
+    else:
+        data = RandomBytes(t.batch_size, t.block_size, seed=t.seed, rank=data_rank, world=data_world)
+        data.step = start
+    valid = RandomBytes(t.batch_size, t.block_size, seed=t.seed + 7919, rank=data_rank, world=data_world)
+
+    log = MetricsLogger(run.path, rank, every=t.log_frequency)
+    prof = StageProfiler(dev)
+    guard = NonFiniteGuard(every=t.log_frequency)
+    hb = Heartbeat(timeout=float(os.environ.get("BDH_HEARTBEAT_TIMEOUT", "60"))) if world > 1 else None
+    last_loss = None
+    step = start
+    try:
+        for step in range(start, t.max_iters):
+            if hb is not None:
+                hb.check()
+            prof.start("dataloader")
+            if streaming:
+                x, y, reset = data.next()
+                if reset or state is None:
+                    state = ModelState.empty()
+            else:
+                x, y = data.next()
+            prof.stop("dataloader")
+            t0 = time.perf_counter()
+            prof.start("forward_backward")
+            if runner is not None:
+                loss = runner.step(x.to(dev), y.to(dev))
+                prof.stop("forward_backward")
+                prof.start("optimizer")
+                trainer.opt.step()
+                trainer.step_idx += 1
+                prof.stop("optimizer")
+                loss = loss if loss is not None else torch.zeros(())
+            elif streaming:
+                loss = trainer.step_stream(x, y, state)
+                prof.stop("forward_backward")
+            else:
+                loss = trainer.step(x, y)
+                prof.stop("forward_backward")
+            prof.tokens += x.numel() * (world if mode in ("ddp", "fsdp") else 1)
+            if (step + 1) % t.log_frequency == 0 or step + 1 == t.max_iters:
+                lv = float(loss)
+                guard.check(0, lv)
+                log.log(step + 1, loss=lv, lr=trainer.opt._lr_now if hasattr(trainer.opt, "_lr_now") else o.learning_rate,
+                        step_ms=(time.perf_counter() - t0) * 1e3, force=True)
+                last_loss = lv
+            if t.validation_interval_iters and (step + 1) % t.validation_interval_iters == 0 and runner is None:
+                vx, vy = valid.next()
+                with torch.no_grad():
+                    vl = float(trainer.model.loss(vx.to(dev), vy.to(dev)))
+                log.log(step + 1, valid_loss=vl, force=True)
+            if t.checkpoint_interval_iters and (step + 1) % t.checkpoint_interval_iters == 0 and rank == 0:
+                rt = None
+                if state is not None and state.rhos is not None:
+                    rt = {"position": state.position, "rhos": [r.detach() for r in state.rhos]}
+                run.save(step + 1, trainer.model, trainer.opt, {"step": step + 1}, rt)
+        if rank == 0 and t.checkpoint_interval_iters:
+            run.save(t.max_iters, trainer.model, trainer.opt, {"step": t.max_iters})
+    except PeerFailure:
+        if hb is not None:
+            hb.stop()
+        raise
+    finally:
+        log.close()
+        if hb is not None:
+            hb.stop()
+    summary = prof.summary() if prof.enabled else {}
+    return {"final_loss": last_loss, "steps": t.max_iters - start, "run_dir": run.path, "profile": summary}

@@ -160,6 +160,27 @@ class Trainer:
         if op == dist.ReduceOp.SUM:
             self.model.store.grad.div_(self.world)
 
+    def step_stream(self, tokens: torch.Tensor, targets: torch.Tensor, state) -> torch.Tensor:
+        """Stateful TBPTT step: the chunk continues ``state`` (detached) and advances it."""
+        tokens = tokens.to(self.device, non_blocking=True)
+        targets = targets.to(self.device, non_blocking=True)
+        if self.fused:
+            loss = self.model.fused_step(tokens, targets, state=state)
+        else:
+            self.model.zero_grad(set_to_none=False)
+            if state.rhos is not None:
+                state.rhos = [r.detach() for r in state.rhos]
+            loss = self.model.loss(tokens, targets, state=state)
+            grads = torch.autograd.grad(loss, list(self.model.parameters()))
+            for p, g in zip(self.model.parameters(), grads):
+                p.grad.copy_(g)
+            state.detach_in_place()
+            loss = loss.detach()
+        self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
+        self._update()
+        self.step_idx += 1
+        return loss
+
     def step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None) -> torch.Tensor:
         if (self._graph is not None and mask is None
                 and (tuple(tokens.shape), tuple(targets.shape)) == self._graph_shape):

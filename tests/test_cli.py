@@ -1,0 +1,77 @@
+"""Config loading and the CPU training CLI on BASELINE config 1 (tiny BDH, 20 steps)."""
+import json
+import os
+
+import pytest
+
+from burn_dragon_b200.cli.train import main, parse_set
+from burn_dragon_b200.config import load_training_config
+
+CFG = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs")
+
+
+def test_extends_and_overlays():
+    cfg = load_training_config([os.path.join(CFG, "bdh_gpu_scaffold.toml")])
+    assert cfg.model.random_scaffold.enabled and cfg.model.random_scaffold.rank == 16
+    assert cfg.parallel.mode == "ddp" and cfg.model.latent_total == 32768
+    assert cfg.model.rotary_embedding == "rope"
+    cfg = load_training_config([os.path.join(CFG, "tiny_cpu.toml")], parse_set(["training.max_iters=3"]))
+    assert cfg.training.max_iters == 3 and cfg.model.n_embd == 64
+
+
+def test_invalid_parallel_combination_rejected(tmp_path):
+    p = tmp_path / "bad.toml"
+    p.write_text('extends = "%s"\n[parallel]\nmode = "pipeline"\n[training]\ntbptt_chunk_size = 64\n'
+                 % os.path.join(CFG, "tiny_cpu.toml").replace("\\", "/"))
+    with pytest.raises(ValueError):
+        load_training_config([str(p)])
+
+
+def test_tiny_cpu_training_run_and_resume(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.checkpoint_interval_iters=10",
+          "--run-name", "tiny"])
+    out = capsys.readouterr().out
+    res = json.loads(out.strip().splitlines()[-1])
+    losses = [json.loads(line)["loss"] for line in open(os.path.join(res["run_dir"], "events", "metrics.jsonl"))
+              if "loss" in line]
+    import math
+
+    # uniform random bytes: the loss stays at the entropy floor ln(256)
+    assert len(losses) == 4 and all(abs(v - math.log(256)) < 0.05 for v in losses)
+    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "model-20.bin"))
+    # resume: nothing left to do at max_iters
+    main(["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.checkpoint_interval_iters=10",
+          "--run-name", "tiny"])
+    res2 = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res2["steps"] == 0
+
+
+def test_streaming_tbptt_cpu(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.block_size=64",
+          "--set", "training.tbptt_chunk_size=16", "--set", "training.tbptt_persist_across_steps=true",
+          "--set", 'training.sequence_batching="streaming"', "--set", "training.max_iters=6",
+          "--set", "training.log_frequency=3", "--run-name", "tb"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None
+
+
+def test_tiny_model_learns_a_periodic_stream():
+    """The CPU path actually learns: a period-4 byte stream drops well below ln(256)."""
+    import torch
+
+    from burn_dragon_b200.config import DragonConfig
+    from burn_dragon_b200.train.trainer import Trainer
+
+    cfg = DragonConfig(n_layer=2, n_embd=64, n_head=4, mlp_internal_dim_multiplier=32, dropout=0.0,
+                       rotary_embedding="rope")
+    tr = Trainer(cfg, "cpu", lr=3e-3, weight_decay=0.0, seed=1)
+    base = torch.tensor([7, 100, 42, 200])
+    seq = base.repeat(8 * 33 // 4 + 1)[: 8 * 33].view(8, 33)
+    first = last = None
+    for i in range(20):
+        loss = float(tr.step(seq[:, :-1], seq[:, 1:]))
+        first = first if first is not None else loss
+        last = loss
+    assert last < 0.5 * first
