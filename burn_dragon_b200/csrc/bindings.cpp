@@ -11,7 +11,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           const c10::optional<at::Tensor>& aux1, int64_t ld, int64_t sz1, int64_t sz2, int64_t split_stride,
           double alpha, double thr, const c10::optional<at::Tensor>& freq,
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh, bool accumulate,
-          bool row_decay, const at::Tensor& err);
+          bool row_decay, int64_t pair, const at::Tensor& err);
 void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_t rows, int64_t D,
             const at::Tensor& gamma, const at::Tensor& beta, double eps, const c10::optional<at::Tensor>& y32,
             const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd);

@@ -105,13 +105,13 @@ int num_sms(int dev) {
 int num_sms_of(int dev) { return num_sms(dev); }
 
 namespace {
-const Entry* find_entry(int bn, bool a_mn, bool b_mn, int epi) {
-  const Entry* tables[3] = {kGemmTableA, kGemmTableB, kGemmTableC};
-  const int sizes[3] = {kGemmTableASize, kGemmTableBSize, kGemmTableCSize};
-  for (int t = 0; t < 3; ++t)
+const Entry* find_entry(int bn, bool a_mn, bool b_mn, int epi, bool pair) {
+  const Entry* tables[4] = {kGemmTableA, kGemmTableB, kGemmTableC, kGemmTableD};
+  const int sizes[4] = {kGemmTableASize, kGemmTableBSize, kGemmTableCSize, kGemmTableDSize};
+  for (int t = 0; t < 4; ++t)
     for (int i = 0; i < sizes[t]; ++i) {
       const Entry& en = tables[t][i];
-      if (en.bn == bn && en.a_mn == a_mn && en.b_mn == b_mn && en.epi == epi) return &en;
+      if (en.bn == bn && en.a_mn == a_mn && en.b_mn == b_mn && en.epi == epi && en.pair == pair) return &en;
     }
   return nullptr;
 }
@@ -125,8 +125,11 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           const c10::optional<at::Tensor>& aux1, int64_t ld, int64_t sz1, int64_t sz2, int64_t split_stride,
           double alpha, double thr, const c10::optional<at::Tensor>& freq,
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh,
-          bool accumulate, bool row_decay, const at::Tensor& err) {
-  const Entry* hit = find_entry((int)bn, a_mn, b_mn, (int)epi);
+          bool accumulate, bool row_decay, int64_t pair, const at::Tensor& err) {
+  // pair: 0 = 1-CTA kernel, 1 = CTA-pair kernel when instantiated and M >= 256
+  const Entry* hit = nullptr;
+  if (pair && M >= 256) hit = find_entry((int)bn, a_mn, b_mn, (int)epi, true);
+  if (hit == nullptr) hit = find_entry((int)bn, a_mn, b_mn, (int)epi, false);
   if (hit == nullptr) {
     throw std::invalid_argument("burn_dragon_b200: no GEMM instantiation for bn=" + std::to_string(bn) +
                                 " a_mn=" + std::to_string((int)a_mn) + " b_mn=" + std::to_string((int)b_mn) +
@@ -150,7 +153,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   p.K = (int)K;
   p.Z1 = (int)Z1;
   p.Z2 = (int)Z2;
-  p.tiles_m = (int)((M + 127) / 128);
+  p.tiles_m = (int)((M + (hit->pair ? 255 : 127)) / (hit->pair ? 256 : 128));
   p.tiles_n = (int)((N + bn - 1) / bn);
   const int KB = (int)((K + 63) / 64);
   p.kb_per_split = (KB + (int)splits - 1) / (int)splits;

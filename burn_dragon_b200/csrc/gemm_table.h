@@ -15,6 +15,7 @@ struct Entry {
   bool a_mn, b_mn;
   int epi;
   LaunchFn fn;
+  bool pair = false;  // 2-CTA (cta_group::2) kernel: 256-row tiles on a CTA pair
 };
 
 int num_sms_of(int dev);
@@ -25,5 +26,7 @@ extern const Entry kGemmTableB[];
 extern const int kGemmTableBSize;
 extern const Entry kGemmTableC[];
 extern const int kGemmTableCSize;
+extern const Entry kGemmTableD[];
+extern const int kGemmTableDSize;
 
 }  // namespace bd

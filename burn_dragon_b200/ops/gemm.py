@@ -8,6 +8,7 @@ is contiguous), so every operand is read in place — no transposed copies in HB
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -35,6 +36,9 @@ class Operand:
 
 
 _ERR: dict[int, torch.Tensor] = {}
+
+# CTA-pair (cta_group::2) kernels for the MMA-bound contractions: on unless BDH_GEMM_PAIR=0.
+PAIR = os.environ.get("BDH_GEMM_PAIR", "1") != "0"
 
 
 def error_word(device: torch.device) -> torch.Tensor:
@@ -72,12 +76,12 @@ def gemm(epi: int, a: Operand, b: Operand, M: int, N: int, K: int, out0: torch.T
          Z1: int = 1, Z2: int = 1, bn: int | None = None, splits: int = 1, causal_skip: bool = False,
          out1=None, aux0=None, aux1=None, ld: int, sz1: int = 0, sz2: int = 0, split_stride: int = 0,
          alpha: float = 1.0, thr: float = 0.0, freq=None, log2_decay=None, T: int = 1, pos0: int = 0,
-         Nh: int = 1, accumulate: bool = False, row_decay: bool = False) -> None:
+         Nh: int = 1, accumulate: bool = False, row_decay: bool = False, pair: bool | None = None) -> None:
     mod = _ext.load()
     bn = bn or pick_bn(N)
     mod.gemm(epi, bn, a.t, a.mn, a.geom(), b.t, b.mn, b.geom(), M, N, K, Z1, Z2, splits, causal_skip,
              out0, out1, aux0, aux1, ld, sz1, sz2, split_stride, alpha, thr, freq, log2_decay, T, pos0, Nh,
-             accumulate, row_decay, error_word(out0.device))
+             accumulate, row_decay, int(PAIR if pair is None else pair), error_word(out0.device))
 
 
 def matmul(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, a_t: bool = False,

@@ -77,3 +77,40 @@ def test_causal_scores_epilogue():
     ref = torch.tril(qf @ qf.transpose(-1, -2), diagonal=-1)
     _close(S, ref)
     assert (S.float().triu() == 0).all()
+
+
+@pytest.mark.parametrize("a_t,b_t,N", [(True, False, 256), (False, False, 256), (False, True, 256),
+                                       (False, True, 128)])
+@pytest.mark.parametrize("M,K", [(256, 512), (640, 1024)])
+def test_cta_pair_kernel_matches_single_cta(a_t, b_t, N, M, K):
+    """The cta_group::2 kernel (256-row tiles on a CTA pair) equals the 1-CTA kernel."""
+    G = _ops()
+    torch.manual_seed(5)
+    a = torch.randn((K, M) if a_t else (M, K), device="cuda").bfloat16()
+    b = torch.randn((N, K) if b_t else (K, N), device="cuda").bfloat16()
+    A = G.Operand(a, True, M, K, M) if a_t else G.Operand(a, False, K, M, K)
+    B = G.Operand(b, False, K, N, K) if b_t else G.Operand(b, True, N, K, N)
+    o1 = torch.empty(M, N, device="cuda")
+    o2 = torch.empty(M, N, device="cuda")
+    G.gemm(G.EPI_F32, A, B, M, N, K, o1, ld=N, pair=False)
+    G.gemm(G.EPI_F32, A, B, M, N, K, o2, ld=N, pair=True)
+    torch.cuda.synchronize()
+    G.check_errors(torch.device("cuda"))
+    assert torch.allclose(o1, o2, rtol=1e-5, atol=1e-3)
+    _close(o2, _ref(a, b, a_t, b_t))
+
+
+def test_cta_pair_causal_scores():
+    G = _ops()
+    torch.manual_seed(6)
+    B, H, T, Nh = 2, 2, 512, 256
+    q = torch.randn(B, T, H, Nh, device="cuda").bfloat16()
+    op = G.Operand(q, False, Nh, T, H * Nh, z1=(H, Nh), z2=(B, T * H * Nh))
+    outs = []
+    for pair in (False, True):
+        S = torch.full((B, H, T, T), 3.0, device="cuda").bfloat16()
+        G.gemm(G.EPI_SCORES, op, op, T, T, Nh, S, Z1=H, Z2=B, bn=256, causal_skip=True, ld=T, sz1=T * T,
+               sz2=H * T * T, pair=pair)
+        outs.append(S)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
