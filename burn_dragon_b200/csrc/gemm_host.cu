@@ -147,7 +147,8 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   GemmParams p;
   memset(&p, 0, sizeof(p));
   p.ta = a_mn ? encode_map(a, ga, 64, 64) : encode_map(a, ga, 64, 128);
-  p.tb = b_mn ? encode_map(b, gb, 64, 64) : encode_map(b, gb, 64, (uint32_t)bn);
+  // a CTA of a pair stages half of the B tile (BN/2 rows)
+  p.tb = b_mn ? encode_map(b, gb, 64, 64) : encode_map(b, gb, 64, (uint32_t)(hit->pair ? bn / 2 : bn));
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
