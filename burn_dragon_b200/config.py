@@ -63,8 +63,15 @@ class DragonConfig:
     alibi_slopes: list[float] | None = None
     # DragonNorm
     norm_eps: float = 1e-5
-    # initialization (SimpleNormal std, init.rs:10,810)
+    # initialization family (init.rs:18-25; the reference defaults to near_critical) and
+    # the SimpleNormal std (init.rs:810)
+    initialization: str = "near_critical"
     init_std: float = 0.02
+    reservoir_density: float = 0.1
+    # DragonNormConfig (norm.rs:11-125): layer_norm | rms_norm | dynamic_tanh | derf
+    norm_kind: str = "layer_norm"
+    norm_alpha_init: float | None = None
+    norm_shift_init: float = 0.0
     # dense-score row chunk (sequence/config.rs)
     dense_score_row_chunk: int = 512
     random_scaffold: RandomScaffoldConfig = field(default_factory=RandomScaffoldConfig)
@@ -80,7 +87,17 @@ class DragonConfig:
             raise ValueError("latent size must be divisible by the number of heads")
         return total // self.n_head
 
+    def norm_alpha(self) -> float:
+        if self.norm_alpha_init is not None:
+            return self.norm_alpha_init
+        return {"dynamic_tanh": 0.5, "derf": 0.88622695}.get(self.norm_kind, 1.0)
+
     def validate(self) -> None:
+        if self.norm_kind not in ("layer_norm", "rms_norm", "dynamic_tanh", "derf"):
+            raise ValueError(f"unknown normalization kind {self.norm_kind!r}")
+        if self.initialization not in ("simple_normal", "near_critical", "he_glorot", "headwise_semi_orthogonal",
+                                       "reservoir"):
+            raise ValueError(f"unknown initialization kind {self.initialization!r}")
         if self.rotary_embedding not in ROTARY_KINDS:
             raise ValueError(f"rotary_embedding must be one of {ROTARY_KINDS}")
         if self.rollout_fast_steps_per_slow_step not in (1, 2, 4, 8, 16):
@@ -107,13 +124,13 @@ class DragonConfig:
     def bdh_gpu() -> "DragonConfig":
         """BDH-GPU: d=256, n=32768, h=4, L=6, RoPE, byte vocab (the flagship config)."""
         return DragonConfig(n_layer=6, n_embd=256, n_head=4, mlp_internal_dim_multiplier=128,
-                            dropout=0.0, rotary_embedding="rope")
+                            dropout=0.0, rotary_embedding="rope", initialization="simple_normal")
 
     @staticmethod
     def tiny() -> "DragonConfig":
         """Tiny CPU config: d=64, n=2048, h=4, L=2."""
         return DragonConfig(n_layer=2, n_embd=64, n_head=4, mlp_internal_dim_multiplier=32,
-                            dropout=0.0, rotary_embedding="rope")
+                            dropout=0.0, rotary_embedding="rope", initialization="simple_normal")
 
 
 @dataclass
@@ -252,6 +269,21 @@ def _model_table(table: dict) -> dict:
                 t[k] = fk[k]
     if "rotary_embedding" in t and isinstance(t["rotary_embedding"], str):
         t["rotary_embedding"] = t["rotary_embedding"].lower()
+    norm = t.pop("normalization", None)
+    if isinstance(norm, dict):
+        kind = norm.get("kind", "layer_norm").lower()
+        t["norm_kind"] = {"rmsnorm": "rms_norm", "dyt": "dynamic_tanh"}.get(kind, kind)
+        if "eps" in norm:
+            t["norm_eps"] = norm["eps"]
+        if norm.get("alpha_init") is not None:
+            t["norm_alpha_init"] = norm["alpha_init"]
+        if norm.get("shift_init") is not None:
+            t["norm_shift_init"] = norm["shift_init"]
+    ini = t.get("initialization")
+    if isinstance(ini, dict):
+        t["initialization"] = ini.get("kind", "near_critical")
+        if "simple_normal_std" in ini:
+            t["init_std"] = ini["simple_normal_std"]
     if "latent_total" in t:
         lt = t.pop("latent_total")
         d = t.get("n_embd", DragonConfig.n_embd)

@@ -34,6 +34,8 @@ RECORD_NAMES = {
     "lm_head": "lm_head",
     "norm_gamma": "norm.gamma",
     "norm_beta": "norm.beta",
+    "norm_alpha": "norm.alpha",
+    "norm_shift": "norm.shift",
 }
 
 
@@ -52,7 +54,8 @@ def param_shapes(cfg: DragonConfig) -> dict[str, tuple[int, ...]]:
             shapes[k.replace(".", "_")] = shp
     else:
         shapes = {"encoder": (H, D, Nh), "encoder_v": (H, D, Nh), "decoder": (H * Nh, D)}
-    shapes.update({"embed": (V, D), "lm_head": (D, V), "norm_gamma": (D,), "norm_beta": (D,)})
+    shapes.update({"embed": (V, D), "lm_head": (D, V), "norm_gamma": (D,), "norm_beta": (D,),
+                   "norm_alpha": (1,), "norm_shift": (1,)})
     if cfg.tie_input_output_embeddings:
         del shapes["lm_head"]
     return shapes
@@ -136,14 +139,23 @@ class BDH(nn.Module):
     # beta=0 (burn_dragon_core/src/model/init.rs:10,448-520,593-650); scaffold adapters:
     # A from the scaffold generator, B = 0, gain = 1 (scaffold.rs:31-55).
     def _init_weights(self, gen: torch.Generator) -> None:
+        from .init import init_tensor
         from .scaffold import PATHS, adapter_a_init
 
-        std = self.cfg.init_std
-        rs = self.cfg.random_scaffold
+        cfg = self.cfg
+        rs = cfg.random_scaffold
+        D, N, V = cfg.n_embd, cfg.latent_total, cfg.vocab_size
+        fans = {"encoder": (D, cfg.latent_per_head), "encoder_v": (D, cfg.latent_per_head), "decoder": (N, D),
+                "embed": (V, D), "lm_head": (D, V)}
+        depth = cfg.n_layer * cfg.rollout_fast_steps_per_slow_step
         for name, shp in self.store.shapes.items():
             view = self.store.view(self.store.data, name)
             if name == "norm_gamma" or name.endswith("_gain"):
                 view.fill_(1.0)
+            elif name == "norm_alpha":
+                view.fill_(cfg.norm_alpha())
+            elif name == "norm_shift":
+                view.fill_(cfg.norm_shift_init)
             elif name == "norm_beta" or name.endswith("_b"):
                 view.zero_()
             elif name.endswith("_a") and rs.enabled:
@@ -151,7 +163,9 @@ class BDH(nn.Module):
                 fan_in = shp[-2]
                 view.copy_(adapter_a_init(rs.seed, PATHS[proj], shp, fan_in))
             else:
-                view.copy_(torch.randn(shp, generator=gen, dtype=torch.float32) * std)
+                fi, fo = fans[name]
+                view.copy_(init_tensor(cfg.initialization, name, shp, fi, fo, depth, gen, cfg.init_std,
+                                       cfg.reservoir_density))
 
     def _init_scaffold(self, device) -> None:
         """Frozen bases: kept on the host (CPU path) or regenerated by the device kernel."""
@@ -202,7 +216,8 @@ class BDH(nn.Module):
     # ---------------------------------------------------------------- helpers
     def param_dict(self) -> dict[str, torch.Tensor]:
         """The BDH weights the math consumes (effective projections for scaffold runs)."""
-        d = {n: getattr(self, n) for n in ("embed", "lm_head", "norm_gamma", "norm_beta") if n in self.store.shapes}
+        d = {n: getattr(self, n) for n in ("embed", "lm_head", "norm_gamma", "norm_beta", "norm_alpha", "norm_shift")
+             if n in self.store.shapes}
         if self.scaffold:
             from .scaffold import effective_weight
 

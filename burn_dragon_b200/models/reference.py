@@ -31,6 +31,37 @@ def rope_freqs(latent: int, theta: float, device=None, dtype=torch.float32) -> t
     return f.to(dtype=torch.float32).to(device=device, dtype=dtype)
 
 
+def pope_freqs(latent: int, theta: float, device=None, dtype=torch.float32) -> torch.Tensor:
+    """PoPE frequencies theta^(-i/Nh) / 2pi (attention.rs:561-564)."""
+    idx = torch.arange(latent, dtype=torch.float64)
+    f = 1.0 / torch.pow(torch.tensor(theta, dtype=torch.float64), idx / latent) / (2.0 * math.pi)
+    return f.to(dtype=torch.float32).to(device=device, dtype=dtype)
+
+
+def pope_apply(x: torch.Tensor, phases: torch.Tensor) -> torch.Tensor:
+    """softplus(x) as magnitude of a complex embedding: [|x| cos, |x| sin] (2 Nh wide;
+    attention.rs:503-510)."""
+    mag = F.softplus(x)
+    return torch.cat([mag * torch.cos(phases).to(x.dtype), mag * torch.sin(phases).to(x.dtype)], dim=-1)
+
+
+def make_norm(kind: str, gamma, beta, eps: float, alpha=None, shift=None):
+    """DragonNorm (norm.rs:302-327): LayerNorm / RMSNorm / DynamicTanh / Derf, then x*gamma+beta."""
+    def f(x):
+        if kind == "layer_norm":
+            return F.layer_norm(x, (x.shape[-1],), gamma, beta, eps)
+        if kind == "rms_norm":
+            y = x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+        elif kind == "dynamic_tanh":
+            y = torch.tanh(x * alpha)
+        elif kind == "derf":
+            y = torch.erf(x * alpha + shift)
+        else:
+            raise ValueError(kind)
+        return y * gamma + beta
+    return f
+
+
 def rope_phases(positions: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
     """phase[t, j] = frac(pos_t * f_j) * 2pi, computed in fp32 like the reference."""
     raw = positions.to(torch.float32)[:, None] * freqs.to(torch.float32)[None, :]
@@ -110,24 +141,32 @@ def layer_norm(x, gamma, beta, eps):
 
 
 def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, decay, rho0=None,
-              need_state=False, dropout=0.0, training=False):
+              need_state=False, dropout=0.0, training=False, norm=None, pope=False):
     """One shared-weight BDH layer. v [B,T,D]; enc/enc_v [H,D,Nh]; dec [N,D].
+    ``norm`` overrides the LayerNorm (other DragonNorm kinds); ``pope`` switches the
+    query embedding to PoPE (``freqs`` then holds the PoPE frequencies).
 
     Returns (v', rho_T or None, aux dict of the intermediate activations).
     """
     B, T, D = v.shape
     H, _, Nh = enc.shape
+    nf = norm if norm is not None else (lambda z: layer_norm(z, gamma, beta, eps))
     x = torch.relu(torch.einsum("btd,hdn->bhtn", v, enc) - thr)  # [B,H,T,Nh]
-    q = rope_apply(x, rope_phases(positions, freqs)[None, None]) if freqs is not None else x
+    if freqs is None:
+        q = x
+    elif pope:
+        q = pope_apply(x, rope_phases(positions, freqs)[None, None])
+    else:
+        q = rope_apply(x, rope_phases(positions, freqs)[None, None])
     a, rho = linear_attention_dense(q, v[:, None], rho0=rho0, decay=decay, need_state=need_state)
-    a = layer_norm(a, gamma, beta, eps)  # [B,H,T,D]
+    a = nf(a)  # [B,H,T,D]
     y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr)
     yn = x * y
     if dropout > 0.0 and training:
         yn = F.dropout(yn, dropout, training=True)
     m = yn.permute(0, 2, 1, 3).reshape(B, T, H * Nh) @ dec
-    m = layer_norm(m, gamma, beta, eps)
-    v_next = layer_norm(v + m, gamma, beta, eps)
+    m = nf(m)
+    v_next = nf(v + m)
     return v_next, rho, {"x": x, "q": q, "a": a, "y": y, "yn": yn}
 
 
@@ -136,11 +175,15 @@ def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state
     lm_head [D,V] (or None for tied), norm_gamma, norm_beta."""
     B, T = tokens.shape
     gamma, beta = params["norm_gamma"], params["norm_beta"]
-    v = layer_norm(params["embed"][tokens], gamma, beta, cfg.norm_eps)
+    norm = make_norm(getattr(cfg, "norm_kind", "layer_norm"), gamma, beta, cfg.norm_eps, params.get("norm_alpha"),
+                     params.get("norm_shift"))
+    v = norm(params["embed"][tokens])
     Nh = cfg.latent_per_head
     freqs = None
     if cfg.rotary_embedding == "rope":
         freqs = rope_freqs(Nh, cfg.rope_theta, device=v.device, dtype=v.dtype)
+    elif cfg.rotary_embedding == "pope":
+        freqs = pope_freqs(Nh, cfg.rope_theta, device=v.device, dtype=v.dtype)
     decay = decay_vector(cfg.decay_slopes(), device=v.device, dtype=v.dtype) if cfg.uses_decay() else None
     positions = torch.arange(pos0, pos0 + T, device=v.device)
     rhos = []
@@ -149,7 +192,7 @@ def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state
         v, rho, _ = bdh_layer(v, params["encoder"], params["encoder_v"], params["decoder"], gamma, beta,
                               eps=cfg.norm_eps, thr=cfg.relu_threshold, freqs=freqs, positions=positions,
                               decay=decay, rho0=r0, need_state=need_state, dropout=cfg.dropout,
-                              training=training)
+                              training=training, norm=norm, pope=cfg.rotary_embedding == "pope")
         rhos.append(rho)
     head = params["embed"].t() if params.get("lm_head") is None else params["lm_head"]
     logits = v @ head

@@ -147,9 +147,12 @@ class Trainer:
             return self.model.fused_step(tokens, targets, mask)
         self.model.zero_grad(set_to_none=False)
         loss = self.model.loss(tokens, targets, mask)
-        grads = torch.autograd.grad(loss, [p for p in self.model.parameters()])
+        grads = torch.autograd.grad(loss, [p for p in self.model.parameters()], allow_unused=True)
         for p, g in zip(self.model.parameters(), grads):
-            p.grad.copy_(g)
+            if g is None:
+                p.grad.zero_()
+            else:
+                p.grad.copy_(g)
         return loss.detach()
 
     def allreduce_grads(self) -> None:
@@ -171,9 +174,12 @@ class Trainer:
             if state.rhos is not None:
                 state.rhos = [r.detach() for r in state.rhos]
             loss = self.model.loss(tokens, targets, state=state)
-            grads = torch.autograd.grad(loss, list(self.model.parameters()))
+            grads = torch.autograd.grad(loss, list(self.model.parameters()), allow_unused=True)
             for p, g in zip(self.model.parameters(), grads):
-                p.grad.copy_(g)
+                if g is None:
+                    p.grad.zero_()
+                else:
+                    p.grad.copy_(g)
             state.detach_in_place()
             loss = loss.detach()
         self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))

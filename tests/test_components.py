@@ -1,0 +1,62 @@
+"""Model components beyond the BDH-GPU defaults: norm kinds, PoPE, initialisers."""
+import math
+
+import pytest
+import torch
+
+from burn_dragon_b200.config import DragonConfig
+from burn_dragon_b200.models import reference as R
+from burn_dragon_b200.models.bdh import BDH
+from burn_dragon_b200.models.init import init_tensor, near_critical_projection_std
+
+
+@pytest.mark.parametrize("kind", ["layer_norm", "rms_norm", "dynamic_tanh", "derf"])
+def test_norm_kinds_run_and_train(kind):
+    cfg = DragonConfig(n_layer=2, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0,
+                       rotary_embedding="rope", norm_kind=kind)
+    model = BDH(cfg, seed=1)
+    x = torch.randint(0, 256, (2, 8))
+    loss = model.loss(x, x)
+    assert torch.isfinite(loss)
+    g = torch.autograd.grad(loss, [model.norm_alpha, model.encoder], allow_unused=True)
+    assert g[1] is not None and g[1].abs().sum() > 0
+    assert (g[0] is not None) == (kind in ("dynamic_tanh", "derf"))
+
+
+def test_norm_formulas():
+    x = torch.randn(3, 8, dtype=torch.float64)
+    g, b = torch.ones(8, dtype=torch.float64), torch.zeros(8, dtype=torch.float64)
+    rms = R.make_norm("rms_norm", g, b, 0.0)(x)
+    assert torch.allclose(rms.pow(2).mean(-1), torch.ones(3, dtype=torch.float64))
+    a = torch.tensor([0.5], dtype=torch.float64)
+    assert torch.allclose(R.make_norm("dynamic_tanh", g, b, 0.0, a)(x), torch.tanh(0.5 * x))
+    s = torch.tensor([0.1], dtype=torch.float64)
+    assert torch.allclose(R.make_norm("derf", g, b, 0.0, a, s)(x), torch.erf(0.5 * x + 0.1))
+
+
+def test_pope_doubles_latent_and_is_causal_recurrent():
+    cfg = DragonConfig(n_layer=1, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0,
+                       rotary_embedding="pope")
+    model = BDH(cfg, seed=2).double()
+    x = torch.randint(0, 256, (1, 6))
+    from burn_dragon_b200.models.state import ModelState
+
+    full = model(x)
+    st = ModelState.empty()
+    parts = [model(x[:, :3], state=st), model(x[:, 3:], state=st)]
+    assert torch.allclose(torch.cat(parts, 1), full, atol=1e-9)
+    assert st.rhos[0].shape[-2] == 2 * cfg.latent_per_head
+
+
+@pytest.mark.parametrize("kind", ["simple_normal", "near_critical", "he_glorot", "headwise_semi_orthogonal",
+                                  "reservoir"])
+def test_initializers(kind):
+    g = torch.Generator().manual_seed(0)
+    w = init_tensor(kind, "encoder", (2, 64, 256), 64, 256, 6, g)
+    assert w.shape == (2, 64, 256) and torch.isfinite(w).all()
+    if kind in ("near_critical", "headwise_semi_orthogonal", "reservoir"):
+        want = near_critical_projection_std(64, 256) / math.sqrt(6)
+        assert abs(float(w.pow(2).mean().sqrt()) - want) < 0.1 * want
+    if kind == "headwise_semi_orthogonal":
+        m = w[0] / w[0].norm(dim=1, keepdim=True)
+        assert torch.allclose(m @ m.t(), torch.eye(64), atol=1e-4)
