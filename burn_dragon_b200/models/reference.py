@@ -141,7 +141,7 @@ def layer_norm(x, gamma, beta, eps):
 
 
 def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, decay, rho0=None,
-              need_state=False, dropout=0.0, training=False, norm=None, pope=False):
+              need_state=False, dropout=0.0, training=False, norm=None, pope=False, attention=None):
     """One shared-weight BDH layer. v [B,T,D]; enc/enc_v [H,D,Nh]; dec [N,D].
     ``norm`` overrides the LayerNorm (other DragonNorm kinds); ``pope`` switches the
     query embedding to PoPE (``freqs`` then holds the PoPE frequencies).
@@ -158,7 +158,10 @@ def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, de
         q = pope_apply(x, rope_phases(positions, freqs)[None, None])
     else:
         q = rope_apply(x, rope_phases(positions, freqs)[None, None])
-    a, rho = linear_attention_dense(q, v[:, None], rho0=rho0, decay=decay, need_state=need_state)
+    if attention is not None:  # e.g. context parallelism: the sequence is split over ranks
+        a, rho = attention(q, v[:, None])
+    else:
+        a, rho = linear_attention_dense(q, v[:, None], rho0=rho0, decay=decay, need_state=need_state)
     a = nf(a)  # [B,H,T,D]
     y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr)
     yn = x * y

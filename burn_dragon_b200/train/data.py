@@ -54,3 +54,31 @@ class StreamingBytes:
         if self.pos + self.chunk > self.stream_len:
             self.pos = 0
         return x.contiguous(), y.contiguous(), reset
+
+
+class FileBytes:
+    """Random [B, T+1] windows of a byte file (memory-mapped), split into train / valid
+    by ``train_split_ratio`` (the reference's file-backed corpora, dataset/mod.rs)."""
+
+    def __init__(self, path: str, batch: int, block: int, split: str = "train", ratio: float = 0.9,
+                 seed: int = 1337, rank: int = 0, world: int = 1):
+        import numpy as np
+
+        data = np.memmap(path, dtype=np.uint8, mode="r")
+        cut = int(len(data) * ratio)
+        self.data = data[:cut] if split == "train" else data[cut:]
+        if len(self.data) <= block + 1:
+            raise ValueError(f"{path}: {split} split has only {len(self.data)} bytes for block {block}")
+        self.batch, self.block = batch, block
+        self.seed, self.rank, self.world = seed, rank, world
+        self.step = 0
+
+    def next(self) -> tuple[torch.Tensor, torch.Tensor]:
+        import numpy as np
+
+        g = np.random.default_rng(self.seed * 1_000_003 + self.step * self.world + self.rank)
+        self.step += 1
+        starts = g.integers(0, len(self.data) - self.block - 1, size=self.batch)
+        w = np.stack([np.asarray(self.data[s:s + self.block + 1], dtype=np.int64) for s in starts])
+        t = torch.from_numpy(w)
+        return t[:, :-1].contiguous(), t[:, 1:].contiguous()

@@ -31,7 +31,7 @@ from ..config import TrainingConfig
 from ..models.state import ModelState
 from ..parallel.fault import Heartbeat, NonFiniteGuard, PeerFailure
 from . import checkpoint as C
-from .data import RandomBytes, StreamingBytes
+from .data import FileBytes, RandomBytes, StreamingBytes
 from .metrics import MetricsLogger, StageProfiler
 from .trainer import Trainer, init_distributed
 
@@ -94,10 +94,18 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         chunk = t.tbptt_chunk_size or t.block_size
         data = StreamingBytes(t.batch_size, t.block_size, chunk, seed=t.seed, rank=data_rank)
         data.pos = (start * chunk) % max(1, t.block_size - chunk + 1) if t.block_size > chunk else 0
+    elif cfg.dataset.type == "file":
+        data = FileBytes(cfg.dataset.path, t.batch_size, t.block_size, "train", cfg.dataset.train_split_ratio,
+                         seed=t.seed, rank=data_rank, world=data_world)
+        data.step = start
     else:
         data = RandomBytes(t.batch_size, t.block_size, seed=t.seed, rank=data_rank, world=data_world)
         data.step = start
-    valid = RandomBytes(t.batch_size, t.block_size, seed=t.seed + 7919, rank=data_rank, world=data_world)
+    if cfg.dataset.type == "file":
+        valid = FileBytes(cfg.dataset.path, t.batch_size, t.block_size, "valid", cfg.dataset.train_split_ratio,
+                          seed=t.seed + 7919, rank=data_rank, world=data_world)
+    else:
+        valid = RandomBytes(t.batch_size, t.block_size, seed=t.seed + 7919, rank=data_rank, world=data_world)
 
     log = MetricsLogger(run.path, rank, every=t.log_frequency)
     prof = StageProfiler(dev)
