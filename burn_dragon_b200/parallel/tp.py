@@ -19,6 +19,17 @@ import torch
 import torch.distributed as dist
 
 
+def hybrid_layout(world: int, tp: int) -> tuple[list[list[int]], list[list[int]]]:
+    """2-D DP x TP layout (the reference's hybrid_2d, validate.rs:1492-1503): tensor-parallel
+    groups are consecutive ranks (one NVSwitch node holds them), data-parallel groups
+    stride over them. Returns (tp_groups, dp_groups)."""
+    if world % tp:
+        raise ValueError(f"world {world} not divisible by tensor-parallel size {tp}")
+    tp_groups = [list(range(d * tp, (d + 1) * tp)) for d in range(world // tp)]
+    dp_groups = [list(range(i, world, tp)) for i in range(tp)]
+    return tp_groups, dp_groups
+
+
 class TensorParallel:
     def __init__(self, group=None):
         self.group = group

@@ -1,0 +1,81 @@
+"""EGGROLL: evolution strategies with antithetic low-rank perturbations of the matrix
+parameters, the whole population evaluated in one batched forward
+(burn_dragon_eggroll/src/lib.rs:96-238; population forward dragon.rs:1555-1646).
+
+Member i of a population of 2P uses ``W + s_i * sigma * A_i B_i^T / sqrt(r)`` with
+s_i = +-1 (antithetic pairs share A_i, B_i), A_i, B_i Gaussian of rank r, for the three
+shared projections. Fitness is minus the CE loss on the batch; the update is
+``W += lr / (2 P sigma) * sum_i (f_i^+ - f_i^-) E_i`` (the antithetic ES estimator).
+All members run in one forward: the population is a leading batch dimension of the
+weights (``torch.func.vmap`` over members).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ..models import reference as R
+
+MATRIX = ("encoder", "encoder_v", "decoder")
+
+
+def _noise(shape, rank: int, gen: torch.Generator, device):
+    if len(shape) == 3:
+        H, a, b = shape
+        A = torch.randn(H, a, rank, generator=gen).to(device)
+        B = torch.randn(H, rank, b, generator=gen).to(device)
+    else:
+        a, b = shape
+        A = torch.randn(a, rank, generator=gen).to(device)
+        B = torch.randn(rank, b, generator=gen).to(device)
+    return torch.matmul(A, B) / math.sqrt(rank)
+
+
+@torch.no_grad()
+def population_losses(model, tokens, targets, noises: dict, sigma: float) -> torch.Tensor:
+    """Losses of the 2P antithetic members (order: +1..+P, -1..-P), one batched forward."""
+    base = model.param_dict()
+    cfg = model.cfg
+    P = next(iter(noises.values())).shape[0]
+
+    def member_loss(sign, *eps):
+        p = dict(base)
+        for n, e in zip(MATRIX, eps):
+            p[n] = base[n] + sign * sigma * e
+        logits, _ = R.bdh_forward(tokens, p, cfg)
+        return R.cross_entropy(logits, targets)
+
+    signs = torch.cat([torch.ones(P), -torch.ones(P)]).to(tokens.device)
+    eps = [torch.cat([noises[n], noises[n]], 0) for n in MATRIX]
+    return torch.func.vmap(member_loss)(signs, *eps)
+
+
+@torch.no_grad()
+def es_step(model, tokens, targets, population: int = 8, sigma: float = 0.01, lr: float = 0.01, rank: int = 4,
+            seed: int = 0) -> dict:
+    """One antithetic ES update of the three shared projections; returns diagnostics."""
+    gen = torch.Generator().manual_seed(seed)
+    params = model.param_dict()
+    noises = {n: torch.stack([_noise(params[n].shape, rank, gen, tokens.device) for _ in range(population)])
+              for n in MATRIX}
+    losses = population_losses(model, tokens, targets, noises, sigma)
+    fp, fm = -losses[:population], -losses[population:]
+    coef = (fp - fm) / (2 * population * sigma)
+    for n in MATRIX:
+        upd = torch.tensordot(coef, noises[n], dims=1)
+        getattr(model, n).add_(lr * upd)
+    model.store.refresh_shadow()
+    return {"mean_loss": float(losses.mean()), "best_loss": float(losses.min())}
+
+
+def es_gradient_estimate(model, tokens, targets, population: int, sigma: float, rank: int, seed: int = 0) -> dict:
+    """The ES estimate of -dL/dW (for diagnostics / tests)."""
+    gen = torch.Generator().manual_seed(seed)
+    params = model.param_dict()
+    noises = {n: torch.stack([_noise(params[n].shape, rank, gen, tokens.device) for _ in range(population)])
+              for n in MATRIX}
+    losses = population_losses(model, tokens, targets, noises, sigma)
+    coef = (-losses[:population] + losses[population:]) / (2 * population * sigma)
+    return {n: torch.tensordot(coef, noises[n], dims=1) for n in MATRIX}

@@ -66,9 +66,17 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     if mode in ("ddp", "fsdp") and world > 1 and dev.type == "cuda":
         comm = "nvlink" if o.grad_clip_norm is None else "nccl"
     micro = int(cfg.parallel.tensor.get("micro_batches", t.gradient_accumulation_steps))
+    tp_arg: bool | int = mode == "tensor_parallel_neuron"
+    if mode == "hybrid_2d":
+        tp_arg = int(cfg.parallel.tensor.get("size", 8))
+        comm = "nvlink" if o.grad_clip_norm is None and dev.type == "cuda" else None
+    if cfg.parallel.tensor.get("sequence_parallel"):
+        # the residual stream is replicated across the tensor-parallel group; the sum is an
+        # all-reduce of [M, D] per layer (a reduce-scatter + all-gather moves the same bytes)
+        pass
     trainer = Trainer(cfg.model, dev, lr=o.learning_rate, weight_decay=o.weight_decay, betas=(o.beta1, o.beta2),
                       eps=o.eps, grad_clip_norm=o.grad_clip_norm, seed=t.seed, lr_schedule=o.lr_schedule,
-                      max_iters=t.max_iters, comm=comm, tensor_parallel=mode == "tensor_parallel_neuron",
+                      max_iters=t.max_iters, comm=comm, tensor_parallel=tp_arg,
                       micro_batches=micro if mode != "pipeline" else 1)
     runner = None
     if mode == "pipeline":
@@ -90,6 +98,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     streaming = t.sequence_batching == "streaming" or t.tbptt_persist_across_steps
     data_rank = 0 if mode in ("tensor_parallel_neuron", "pipeline") else rank
     data_world = 1 if mode in ("tensor_parallel_neuron", "pipeline") else world
+    if mode == "hybrid_2d":
+        tp_size = int(cfg.parallel.tensor.get("size", 8))
+        data_rank, data_world = rank // tp_size, world // tp_size
     if streaming:
         chunk = t.tbptt_chunk_size or t.block_size
         data = StreamingBytes(t.batch_size, t.block_size, chunk, seed=t.seed, rank=data_rank)

@@ -44,10 +44,24 @@ class Trainer:
         self.device = torch.device(device)
         self.micro_batches = micro_batches
         self.tp = None
+        self.dp_group = None
+        dp_world = None
         if tensor_parallel:
-            from ..parallel.tp import TensorParallel
+            from ..parallel.tp import TensorParallel, hybrid_layout
 
-            self.tp = TensorParallel()
+            world_all = dist.get_world_size() if dist.is_initialized() else 1
+            tp_size = world_all if tensor_parallel is True else int(tensor_parallel)
+            if tp_size < world_all:
+                # hybrid 2-D: tensor parallel inside groups of tp_size, data parallel across
+                tp_groups, dp_groups = hybrid_layout(world_all, tp_size)
+                pg_tp = [dist.new_group(g) for g in tp_groups]
+                pg_dp = [dist.new_group(g) for g in dp_groups]
+                r = dist.get_rank()
+                self.tp = TensorParallel(pg_tp[r // tp_size])
+                self.dp_group = pg_dp[r % tp_size]
+                dp_world = world_all // tp_size
+            else:
+                self.tp = TensorParallel()
             local = self.tp.local_config(cfg)
             self.model = BDH(local, device=self.device, seed=seed)
             # replicated tensors share the seed; each rank's heads get their own stream
@@ -67,7 +81,10 @@ class Trainer:
         self.base_lr = lr
         self.step_idx = 0
         # data-parallel world (tensor parallelism alone replicates the batch)
-        self.world = 1 if self.tp is not None else (dist.get_world_size() if dist.is_initialized() else 1)
+        if dp_world is not None:
+            self.world = dp_world
+        else:
+            self.world = 1 if self.tp is not None else (dist.get_world_size() if dist.is_initialized() else 1)
         self.fused = self.device.type == "cuda"
         # comm: None / "nccl" (all-reduce + full AdamW on every rank) or "nvlink"
         # (symmetric-memory reduce-scatter + sharded AdamW + all-gather, parallel.ddp)
@@ -77,7 +94,7 @@ class Trainer:
 
             if grad_clip_norm is not None:
                 raise ValueError("the NVLink DDP step does not implement global-norm clipping; use comm='nccl'")
-            self.comm = NVLinkDDP(self.model.store.numel, self.device)
+            self.comm = NVLinkDDP(self.model.store.numel, self.device, group=self.dp_group)
             self.model.attach_buffers(self.comm.param, self.comm.grad, self.comm.shadow)
         self._graph = None
         self._graph_shape = None
@@ -159,7 +176,7 @@ class Trainer:
         if self.world == 1 or self.comm is not None:
             return  # the NVLink communicator reduces inside its fused optimizer step
         op = dist.ReduceOp.AVG if dist.get_backend() == "nccl" else dist.ReduceOp.SUM
-        dist.all_reduce(self.model.store.grad, op=op)
+        dist.all_reduce(self.model.store.grad, op=op, group=self.dp_group)
         if op == dist.ReduceOp.SUM:
             self.model.store.grad.div_(self.world)
 
