@@ -60,6 +60,7 @@ void reduce_adamw(std::vector<int64_t> grad, std::vector<int64_t> param, std::ve
                   const c10::optional<at::Tensor>& hyper);
 void reduce_mean(std::vector<int64_t> grad, std::vector<int64_t> flags, int64_t rank, int64_t lo, int64_t hi,
                  const at::Tensor& err);
+void percentile_thresholds(const at::Tensor& values, double q, const at::Tensor& out);
 }  // namespace bd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -87,4 +88,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &bd::peer_barrier);
   m.def("reduce_adamw", &bd::reduce_adamw);
   m.def("reduce_mean", &bd::reduce_mean);
+  m.def("percentile_thresholds", &bd::percentile_thresholds);
 }

@@ -60,3 +60,16 @@ def test_initializers(kind):
     if kind == "headwise_semi_orthogonal":
         m = w[0] / w[0].norm(dim=1, keepdim=True)
         assert torch.allclose(m @ m.t(), torch.eye(64), atol=1e-4)
+
+
+def test_widen_preserves_function_with_alibi():
+    from burn_dragon_b200.models.widen import widen
+
+    cfg = DragonConfig(n_layer=2, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0,
+                       rotary_embedding="alibi")
+    model = BDH(cfg, seed=5).double()
+    wide = widen(model.float(), 8).double()
+    model = model.double()
+    x = torch.randint(0, 256, (2, 9))
+    assert wide.cfg.latent_total == 2 * cfg.latent_total
+    assert torch.allclose(model(x), wide(x), atol=1e-6)
