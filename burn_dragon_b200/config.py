@@ -72,6 +72,10 @@ class DragonConfig:
     norm_kind: str = "layer_norm"
     norm_alpha_init: float | None = None
     norm_shift_init: float = 0.0
+    # ManifoldHyperConnectionsConfig (mhc/config.rs): 1 stream = vanilla residual
+    mhc_streams: int = 1
+    mhc_tau: float = 1.0
+    mhc_iters: int = 10
     # dense-score row chunk (sequence/config.rs)
     dense_score_row_chunk: int = 512
     random_scaffold: RandomScaffoldConfig = field(default_factory=RandomScaffoldConfig)
@@ -279,6 +283,11 @@ def _model_table(table: dict) -> dict:
             t["norm_alpha_init"] = norm["alpha_init"]
         if norm.get("shift_init") is not None:
             t["norm_shift_init"] = norm["shift_init"]
+    mhc = t.pop("mhc", None)
+    if isinstance(mhc, dict) and mhc.get("enabled"):
+        t["mhc_streams"] = int(mhc.get("num_streams", 4))
+        t["mhc_tau"] = float(mhc.get("mhc_tau", 1.0))
+        t["mhc_iters"] = int(mhc.get("mhc_iters", 10))
     ini = t.get("initialization")
     if isinstance(ini, dict):
         t["initialization"] = ini.get("kind", "near_critical")

@@ -58,6 +58,9 @@ def param_shapes(cfg: DragonConfig) -> dict[str, tuple[int, ...]]:
                    "norm_alpha": (1,), "norm_shift": (1,)})
     if cfg.tie_input_output_embeddings:
         del shapes["lm_head"]
+    if cfg.mhc_streams > 1:
+        S, L = cfg.mhc_streams, cfg.n_layer
+        shapes.update({"mhc_res": (L, S, S), "mhc_pre": (L, 1, S), "mhc_post": (L, 1, S)})
     return shapes
 
 
@@ -158,6 +161,10 @@ class BDH(nn.Module):
                 view.fill_(cfg.norm_shift_init)
             elif name == "norm_beta" or name.endswith("_b"):
                 view.zero_()
+            elif name.startswith("mhc_"):
+                from .mhc import init_logits
+
+                view.copy_(init_logits(cfg.n_layer, cfg.mhc_streams)[name])
             elif name.endswith("_a") and rs.enabled:
                 proj = name[:-2]
                 fan_in = shp[-2]
@@ -216,7 +223,8 @@ class BDH(nn.Module):
     # ---------------------------------------------------------------- helpers
     def param_dict(self) -> dict[str, torch.Tensor]:
         """The BDH weights the math consumes (effective projections for scaffold runs)."""
-        d = {n: getattr(self, n) for n in ("embed", "lm_head", "norm_gamma", "norm_beta", "norm_alpha", "norm_shift")
+        d = {n: getattr(self, n) for n in ("embed", "lm_head", "norm_gamma", "norm_beta", "norm_alpha", "norm_shift",
+                                           "mhc_res", "mhc_pre", "mhc_post")
              if n in self.store.shapes}
         if self.scaffold:
             from .scaffold import effective_weight

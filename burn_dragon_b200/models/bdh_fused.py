@@ -145,7 +145,8 @@ class FusedBDH:
         self.tp = tp
         if cfg.dropout != 0.0:
             raise ValueError("the fused path implements dropout = 0 (as the BDH-GPU profiles use)")
-        if getattr(cfg, "norm_kind", "layer_norm") != "layer_norm" or cfg.rotary_embedding == "pope":
+        if getattr(cfg, "norm_kind", "layer_norm") != "layer_norm" or cfg.rotary_embedding == "pope" \
+                or getattr(cfg, "mhc_streams", 1) > 1:
             raise ValueError("the fused path implements LayerNorm and RoPE / ALiBi (use the PyTorch path)")
         if cfg.tie_input_output_embeddings:
             raise ValueError("the fused path needs an untied lm_head")

@@ -190,13 +190,24 @@ def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state
     decay = decay_vector(cfg.decay_slopes(), device=v.device, dtype=v.dtype) if cfg.uses_decay() else None
     positions = torch.arange(pos0, pos0 + T, device=v.device)
     rhos = []
+    streams = getattr(cfg, "mhc_streams", 1)
+    if streams > 1:
+        from . import mhc as MHC
+
+        R = v[:, None].expand(B, streams, T, v.shape[-1])
     for layer in range(cfg.n_layer):
         r0 = rho0s[layer] if rho0s is not None else None
+        if streams > 1:
+            v, R = MHC.layer_split(R, params["mhc_res"][layer], params["mhc_pre"][layer], cfg.mhc_tau, cfg.mhc_iters)
         v, rho, _ = bdh_layer(v, params["encoder"], params["encoder_v"], params["decoder"], gamma, beta,
                               eps=cfg.norm_eps, thr=cfg.relu_threshold, freqs=freqs, positions=positions,
                               decay=decay, rho0=r0, need_state=need_state, dropout=cfg.dropout,
                               training=training, norm=norm, pope=cfg.rotary_embedding == "pope")
+        if streams > 1:
+            R = MHC.layer_merge(R, v, params["mhc_post"][layer])
         rhos.append(rho)
+    if streams > 1:
+        v = R.mean(dim=1)
     head = params["embed"].t() if params.get("lm_head") is None else params["lm_head"]
     logits = v @ head
     return logits, rhos

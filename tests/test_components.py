@@ -73,3 +73,17 @@ def test_widen_preserves_function_with_alibi():
     x = torch.randint(0, 256, (2, 9))
     assert wide.cfg.latent_total == 2 * cfg.latent_total
     assert torch.allclose(model(x), wide(x), atol=1e-6)
+
+
+def test_mhc_sinkhorn_and_training():
+    from burn_dragon_b200.models.mhc import sinkhorn
+
+    h = sinkhorn(torch.randn(4, 4), 1.0, 30)
+    assert torch.allclose(h.sum(0), torch.ones(4), atol=1e-4) and torch.allclose(h.sum(1), torch.ones(4), atol=1e-4)
+    cfg = DragonConfig(n_layer=2, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0,
+                       rotary_embedding="rope", mhc_streams=3)
+    model = BDH(cfg, seed=1)
+    x = torch.randint(0, 256, (2, 8))
+    loss = model.loss(x, x)
+    g = torch.autograd.grad(loss, [model.mhc_res, model.mhc_post, model.encoder], allow_unused=True)
+    assert all(t is not None and torch.isfinite(t).all() for t in g)
