@@ -44,6 +44,143 @@ class RandomScaffoldConfig:
 
 
 @dataclass
+class YNeuronRecurrenceConfig:
+    """Token-wise carry of the y-neuron activity into the next token's x-neurons
+    (config.rs:196-224, defaults config.rs:594-612)."""
+
+    enabled: bool = False
+    carry_in_scale: float = 0.125
+    last_layers: int | None = None
+    chunk_tokens: int = 1
+    state_decay: float = 0.5
+    state_update_scale: float = 1.0
+    state_rms_cap: float | None = 1.0
+
+
+@dataclass
+class ClockedSlowMemoryConfig:
+    """A second low-rank step on chunk means, broadcast back to the chunk (config.rs:226-260)."""
+
+    enabled: bool = False
+    last_layers: int | None = None
+    chunk_tokens: int = 4
+    residual_scale: float = 1.0
+
+
+@dataclass
+class SummaryMemoryConfig:
+    """Surprise-gated running summary of chunk means added to later chunks (config.rs:318-380)."""
+
+    enabled: bool = False
+    last_layers: int | None = None
+    chunk_tokens: int = 32
+    residual_scale: float = 0.25
+    state_decay: float = 0.75
+    state_update_scale: float = 0.5
+    surprise_gate_threshold: float = 0.0
+    surprise_gate_sharpness: float = 8.0
+    write_trigger_text: str | None = None
+    write_trigger_token_ids: list[int] | None = None
+
+
+@dataclass
+class HierarchicalDragonConfig:
+    """Fast/slow cycles per layer with shared or split rho / weights (config.rs:452-520)."""
+
+    enabled: bool = False
+    last_layers: int | None = None
+    fast_cycles: int = 3
+    slow_cycles: int = 2
+    rho_sharing: str = "shared"  # or "split"
+    weight_sharing: str = "shared"  # or "split"
+    slow_to_fast_scale: float = 0.25
+    fast_to_slow_scale: float = 0.25
+
+
+@dataclass
+class AttentionResidualConfig:
+    """Softmax attention over the history of layer deltas as the branch input
+    (attention_residual/config.rs:70-116)."""
+
+    enabled: bool = False
+    last_layers: int | None = None
+    num_heads: int = 4
+    history_window: int | None = None
+    dropout: float = 0.0
+    recency_bias: float = 2.0
+
+
+@dataclass
+class BlockAttentionResidualConfig:
+    """Attention residual over block summaries plus the recent raw deltas
+    (attention_residual/config.rs:240-305)."""
+
+    enabled: bool = False
+    last_layers: int | None = None
+    num_heads: int = 4
+    layers_per_block: int = 2
+    block_history_window: int | None = None
+    intra_block_history_window: int | None = None
+    summary_mode: str = "learned_projection"  # or "mean_pool"
+    dropout: float = 0.0
+    recency_bias: float = 2.0
+    cache_block_summaries: bool = True
+    two_phase_compute: bool = True
+
+
+@dataclass
+class LatentReasoningConfig:
+    """Iterated latent refiner with optional adaptive halting (config.rs:744-843)."""
+
+    enabled: bool = False
+    max_steps: int = 1
+    min_steps: int = 1
+    adaptive_halting: bool = False
+    halt_threshold: float = 0.55
+    refiner_hidden_multiplier: int = 1
+    normalize_steps: bool = False
+    residual_refinement_gate: bool = False
+    residual_refinement_gate_init: float = 0.25
+    energy_head: bool = False
+    step_conditioned_decoder: bool = False
+    step_conditioned_decoder_scale: float = 1.0
+    stop_bias_init: float = -2.0
+    energy_margin: float = 1.0
+
+    def validate(self) -> None:
+        if not self.enabled:
+            return
+        if self.max_steps < 1 or self.min_steps < 1 or self.min_steps > self.max_steps:
+            raise ValueError("latent_reasoning needs 1 <= min_steps <= max_steps")
+        if self.adaptive_halting and not 0.0 <= self.halt_threshold <= 1.0:
+            raise ValueError("latent_reasoning.halt_threshold must be in [0, 1]")
+        if self.refiner_hidden_multiplier < 1:
+            raise ValueError("latent_reasoning.refiner_hidden_multiplier must be > 0")
+        if not 0.0 < self.residual_refinement_gate_init < 1.0:
+            raise ValueError("latent_reasoning.residual_refinement_gate_init must be in (0, 1)")
+        if self.step_conditioned_decoder_scale < 0 or self.energy_margin < 0:
+            raise ValueError("latent_reasoning scales must be >= 0")
+
+
+@dataclass
+class NextLatentTransitionConfig:
+    """Action-conditioned next-latent predictor (config.rs:845-883)."""
+
+    enabled: bool = False
+    hidden_multiplier: int = 2
+    normalize_input: bool = True
+    zero_init_output: bool = True
+
+
+@dataclass
+class SequenceScoreHeadConfig:
+    """Low-rank prompt/candidate compatibility score head (config.rs:963-978)."""
+
+    enabled: bool = False
+    projection_dim: int = 64
+
+
+@dataclass
 class DragonConfig:
     """BDH model hyper-parameters (defaults as in config.rs:1030-1063)."""
 
@@ -79,6 +216,17 @@ class DragonConfig:
     # dense-score row chunk (sequence/config.rs)
     dense_score_row_chunk: int = 512
     random_scaffold: RandomScaffoldConfig = field(default_factory=RandomScaffoldConfig)
+    # residual connector: vanilla | mhc | attention_residual | block_attention_residual
+    residual_connector: str = "vanilla"
+    attention_residual: AttentionResidualConfig = field(default_factory=AttentionResidualConfig)
+    block_attention_residual: BlockAttentionResidualConfig = field(default_factory=BlockAttentionResidualConfig)
+    y_neuron_recurrence: YNeuronRecurrenceConfig = field(default_factory=YNeuronRecurrenceConfig)
+    clocked_slow_memory: ClockedSlowMemoryConfig = field(default_factory=ClockedSlowMemoryConfig)
+    summary_memory: SummaryMemoryConfig = field(default_factory=SummaryMemoryConfig)
+    hierarchical_dragon: HierarchicalDragonConfig = field(default_factory=HierarchicalDragonConfig)
+    latent_reasoning: LatentReasoningConfig = field(default_factory=LatentReasoningConfig)
+    next_latent_transition: NextLatentTransitionConfig = field(default_factory=NextLatentTransitionConfig)
+    sequence_score_head: SequenceScoreHeadConfig = field(default_factory=SequenceScoreHeadConfig)
 
     @property
     def latent_total(self) -> int:
@@ -109,6 +257,32 @@ class DragonConfig:
         if self.rotary_embedding == "rope" and self.latent_per_head % 2:
             raise ValueError("RoPE needs an even latent per head")
         _ = self.latent_per_head
+        if self.residual_connector not in ("vanilla", "mhc", "attention_residual", "block_attention_residual"):
+            raise ValueError(f"unknown residual_connector {self.residual_connector!r}")
+        self.latent_reasoning.validate()
+        for name in ("rho_sharing", "weight_sharing"):
+            if getattr(self.hierarchical_dragon, name) not in ("shared", "split"):
+                raise ValueError(f"hierarchical_dragon.{name} must be 'shared' or 'split'")
+
+    def resolved_residual_connector(self) -> str:
+        """``vanilla`` defers to the enabled sub-config (config.rs:1067-1086)."""
+        if self.residual_connector != "vanilla":
+            return self.residual_connector
+        if self.block_attention_residual.enabled:
+            return "block_attention_residual"
+        if self.attention_residual.enabled:
+            return "attention_residual"
+        if self.mhc_streams > 1:
+            return "mhc"
+        return "vanilla"
+
+    def uses_extended_runtime(self) -> bool:
+        """True when a feature outside the fused BDH step is on (these run on the PyTorch
+        layer path of ``models.dragon_runtime``)."""
+        return (self.resolved_residual_connector() in ("attention_residual", "block_attention_residual")
+                or self.y_neuron_recurrence.enabled or self.clocked_slow_memory.enabled
+                or self.summary_memory.enabled or self.hierarchical_dragon.enabled
+                or self.latent_reasoning.enabled or self.rollout_fast_steps_per_slow_step > 1)
 
     def decay_slopes(self) -> list[float]:
         """ALiBi slopes 1/2^(h/H) (burn_dragon_core/src/kernel/linear_attention.rs:149-160)."""

@@ -174,7 +174,9 @@ class RunDir:
         return os.path.join(self.ckpt, f"{kind}-{step}.bin")
 
     def save(self, step: int, model, optimizer=None, scheduler: dict | None = None, runtime: dict | None = None,
-             keep_last: int = 2, best_step: int | None = None) -> None:
+             keep_last: int = 2, best_step: int | None = None, extra: dict | None = None) -> None:
+        """``extra``: further named tensors (the optional modules of ``DragonRuntime`` and
+        their optimizer moments), stored as ``extra-<step>.bin``."""
         from ..models.bdh import record_name
 
         params = {record_name(n): t.detach() for n, t in model.store.views(model.store.data).items()}
@@ -190,6 +192,8 @@ class RunDir:
             for i, r in enumerate(runtime.get("rhos") or []):
                 rt[f"rho.{i}"] = r
             save_tensors(self._p("runtime-state", step), rt, meta)
+        if extra:
+            save_tensors(self._p("extra", step), extra, {"schema_version": SCHEMA_VERSION})
         with open(os.path.join(self.path, "latest"), "w") as f:
             f.write(str(step))
         self._retain(keep_last, best_step)
@@ -215,7 +219,7 @@ class RunDir:
         for s in steps:
             if s in keep:
                 continue
-            for kind in ("model", "optim", "scheduler", "runtime-state"):
+            for kind in ("model", "optim", "scheduler", "runtime-state", "extra"):
                 p = self._p(kind, s)
                 if os.path.exists(p):
                     os.remove(p)
@@ -243,7 +247,10 @@ class RunDir:
             optimizer.m.copy_(o["m"].to(optimizer.m.device))
             optimizer.v.copy_(o["v"].to(optimizer.v.device))
             optimizer.t = int(ometa["t"])
-        out = {"step": step, "scheduler": {}, "runtime": None}
+        out = {"step": step, "scheduler": {}, "runtime": None, "extra": None}
+        ep = self._p("extra", step)
+        if os.path.exists(ep):
+            out["extra"] = load_tensors(ep, device)[0]
         sp = self._p("scheduler", step)
         if os.path.exists(sp):
             out["scheduler"] = json.load(open(sp))

@@ -74,10 +74,20 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         # the residual stream is replicated across the tensor-parallel group; the sum is an
         # all-reduce of [M, D] per layer (a reduce-scatter + all-gather moves the same bytes)
         pass
-    trainer = Trainer(cfg.model, dev, lr=o.learning_rate, weight_decay=o.weight_decay, betas=(o.beta1, o.beta2),
-                      eps=o.eps, grad_clip_norm=o.grad_clip_norm, seed=t.seed, lr_schedule=o.lr_schedule,
-                      max_iters=t.max_iters, comm=comm, tensor_parallel=tp_arg,
-                      micro_batches=micro if mode != "pipeline" else 1)
+    extended = cfg.model.uses_extended_runtime()
+    if extended and mode not in ("single", "ddp", "fsdp"):
+        raise ValueError(f"parallel mode {mode!r} does not support the layer-loop variants this model enables")
+    if extended:
+        from .runtime_trainer import RuntimeTrainer
+
+        trainer = RuntimeTrainer(cfg.model, dev, lr=o.learning_rate, weight_decay=o.weight_decay,
+                                 betas=(o.beta1, o.beta2), eps=o.eps, grad_clip_norm=o.grad_clip_norm, seed=t.seed,
+                                 lr_schedule=o.lr_schedule, max_iters=t.max_iters)
+    else:
+        trainer = Trainer(cfg.model, dev, lr=o.learning_rate, weight_decay=o.weight_decay,
+                          betas=(o.beta1, o.beta2), eps=o.eps, grad_clip_norm=o.grad_clip_norm, seed=t.seed,
+                          lr_schedule=o.lr_schedule, max_iters=t.max_iters, comm=comm, tensor_parallel=tp_arg,
+                          micro_batches=micro if mode != "pipeline" else 1)
     runner = None
     if mode == "pipeline":
         from ..parallel.pipeline import PipelineRunner, plan
@@ -89,11 +99,13 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     start = 0
     state = None
     if resume and run.latest() is not None:
-        info = run.load(None, trainer.model, trainer.opt, device=dev)
+        info = run.load(None, trainer.core if extended else trainer.model, trainer.opt, device=dev)
         start = info["step"]
         trainer.step_idx = start
+        if extended and info.get("extra"):
+            trainer.load_extra_state(info["extra"])
         rt = info.get("runtime")
-        if rt and rt.get("rhos") is not None:
+        if rt and rt.get("rhos") is not None and not extended:
             state = ModelState(rt["rhos"], int(rt.get("position", 0)))
     streaming = t.sequence_batching == "streaming" or t.tbptt_persist_across_steps
     data_rank = 0 if mode in ("tensor_parallel_neuron", "pipeline") else rank
@@ -132,7 +144,12 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
             if streaming:
                 x, y, reset = data.next()
                 if reset or state is None:
-                    state = ModelState.empty()
+                    if extended:
+                        from ..models.dragon_runtime import RuntimeState
+
+                        state = RuntimeState.new(cfg.model.n_layer)
+                    else:
+                        state = ModelState.empty()
             else:
                 x, y = data.next()
             prof.stop("dataloader")
@@ -162,15 +179,17 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
             if t.validation_interval_iters and (step + 1) % t.validation_interval_iters == 0 and runner is None:
                 vx, vy = valid.next()
                 with torch.no_grad():
-                    vl = float(trainer.model.loss(vx.to(dev), vy.to(dev)))
+                    vl = float(trainer.model.loss(vx.to(dev), vy.to(dev)))  # fresh state per window
                 log.log(step + 1, valid_loss=vl, force=True)
             if t.checkpoint_interval_iters and (step + 1) % t.checkpoint_interval_iters == 0 and rank == 0:
                 rt = None
-                if state is not None and state.rhos is not None:
+                if state is not None and not extended and state.rhos is not None:
                     rt = {"position": state.position, "rhos": [r.detach() for r in state.rhos]}
-                run.save(step + 1, trainer.model, trainer.opt, {"step": step + 1}, rt)
+                run.save(step + 1, trainer.core if extended else trainer.model, trainer.opt, {"step": step + 1}, rt,
+                         extra=trainer.extra_state() if extended else None)
         if rank == 0 and t.checkpoint_interval_iters:
-            run.save(t.max_iters, trainer.model, trainer.opt, {"step": t.max_iters})
+            run.save(t.max_iters, trainer.core if extended else trainer.model, trainer.opt, {"step": t.max_iters},
+                     extra=trainer.extra_state() if extended else None)
     except PeerFailure:
         if hb is not None:
             hb.stop()

@@ -75,3 +75,21 @@ def test_tiny_model_learns_a_periodic_stream():
         first = first if first is not None else loss
         last = loss
     assert last < 0.5 * first
+
+
+def test_layer_loop_variants_train_checkpoint_resume(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    args = ["--config", os.path.join(CFG, "tiny_cpu_variants.toml"), "--set", "training.checkpoint_interval_iters=2",
+            "--run-name", "var"]
+    main(args)
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None and res["steps"] == 4
+    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "extra-4.bin"))
+    main(args[:3] + ["training.max_iters=6", "--run-name", "var"])
+    res2 = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res2["steps"] == 2
+    # streaming TBPTT carries the runtime state (rho + y-neuron state) across chunks
+    main(["--config", os.path.join(CFG, "tiny_cpu_variants.toml"), "--set", "training.block_size=32",
+          "--set", "training.tbptt_chunk_size=8", "--set", 'training.sequence_batching="streaming"',
+          "--run-name", "var_tb"])
+    assert json.loads(capsys.readouterr().out.strip().splitlines()[-1])["final_loss"] is not None
