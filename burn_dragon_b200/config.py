@@ -335,6 +335,27 @@ class ParallelConfig:
 
 
 @dataclass
+class ContinualBackpropConfig:
+    """Utility-based replacement of shared low-rank features (burn_dragon_train/src/
+    config/continual_backprop.rs:1-120; defaults as there)."""
+
+    enabled: bool = False
+    target: str = "shared_lowrank_latents"
+    utility_decay: float = 0.99
+    replacement_rate: float = 1.0e-5
+    maturity_steps: int = 1024
+    sample_interval_steps: int = 8
+    replace_interval_steps: int = 256
+    utility_epsilon: float = 1.0e-6
+    lr_coupling: str = "global_ratio"  # none | global_ratio | target_group_ratio
+    lr_coupling_power: float = 1.0
+    warmup_steps: int = 1024
+    cooldown_steps: int = 256
+    max_replacements_per_interval: int = 1
+    regression_pause_steps: int = 1024
+
+
+@dataclass
 class TrainingSection:
     block_size: int = 512
     batch_size: int = 32
@@ -347,6 +368,7 @@ class TrainingSection:
     log_frequency: int = 10
     checkpoint_interval_iters: int | None = None
     validation_interval_iters: int | None = None
+    continual_backprop: ContinualBackpropConfig = field(default_factory=ContinualBackpropConfig)
 
 
 @dataclass

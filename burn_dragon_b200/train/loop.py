@@ -96,6 +96,15 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         pl = plan(cfg.model.n_layer, world, int(pp.get("micro_batches", 4)), pp.get("schedule", "1f1b"))
         runner = PipelineRunner(trainer.model, pl, rank, t.batch_size // pl.micro, t.block_size)
 
+    cbp = None
+    if t.continual_backprop.enabled:
+        m = cfg.model
+        if extended or m.random_scaffold.enabled or mode not in ("single", "ddp", "fsdp"):
+            raise ValueError("continual_backprop needs the plain shared low-rank model (no scaffold or "
+                             "layer-loop variants) in single / ddp mode")
+        from .continual_backprop import ContinualBackprop
+
+        cbp = ContinualBackprop(t.continual_backprop, m, o.learning_rate, seed=t.seed)
     start = 0
     state = None
     if resume and run.latest() is not None:
@@ -167,8 +176,17 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 loss = trainer.step_stream(x, y, state)
                 prof.stop("forward_backward")
             else:
+                sample = cbp is not None and cbp.should_sample()
+                if sample and not getattr(trainer, "fused", False):
+                    cbp.record_reference(trainer.model, x.to(dev))
                 loss = trainer.step(x, y)
                 prof.stop("forward_backward")
+                if cbp is not None:
+                    if sample and getattr(trainer, "fused", False):
+                        cbp.record_fused(trainer.model)
+                    lr_now = getattr(trainer.opt, "_lr_now", o.learning_rate)
+                    if cbp.after_optimizer_step(trainer.model, trainer.opt, lr_now):
+                        log.log(step + 1, cbp_replaced=cbp.last.replacement_count, force=True)
             prof.tokens += x.numel() * (world if mode in ("ddp", "fsdp") else 1)
             if (step + 1) % t.log_frequency == 0 or step + 1 == t.max_iters:
                 lv = float(loss)

@@ -93,3 +93,16 @@ def test_layer_loop_variants_train_checkpoint_resume(tmp_path, monkeypatch, caps
           "--set", "training.tbptt_chunk_size=8", "--set", 'training.sequence_batching="streaming"',
           "--run-name", "var_tb"])
     assert json.loads(capsys.readouterr().out.strip().splitlines()[-1])["final_loss"] is not None
+
+
+def test_continual_backprop_in_training_loop(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.max_iters=8",
+          "--set", "training.continual_backprop.enabled=true", "--set", "training.continual_backprop.warmup_steps=0",
+          "--set", "training.continual_backprop.maturity_steps=1", "--set",
+          "training.continual_backprop.replace_interval_steps=4", "--set",
+          "training.continual_backprop.replacement_rate=0.01", "--set",
+          "training.continual_backprop.sample_interval_steps=2", "--run-name", "cbp"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    events = [json.loads(line) for line in open(os.path.join(res["run_dir"], "events", "metrics.jsonl"))]
+    assert any("cbp_replaced" in e for e in events)
