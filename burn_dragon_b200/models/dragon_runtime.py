@@ -360,7 +360,9 @@ class DragonRuntime(nn.Module):
         cap = self.cfg.y_neuron_recurrence.state_rms_cap
         if cap is None:
             return s
-        rms = s.pow(2).mean(-1, keepdim=True).sqrt().clamp_min(1e-6)
+        # clamp before the square root (same value as clamping the rms at 1e-6) so an
+        # all-zero row has a finite gradient
+        rms = s.pow(2).mean(-1, keepdim=True).clamp_min(1e-12).sqrt()
         return s / (rms / cap).clamp_min(1.0)
 
     def _y_recurrent_layer(self, v, ls: LayerState, start_pos: int, fixed: bool):

@@ -1,5 +1,6 @@
 """Continual backprop: statistics, selection, feature re-initialisation and moment resets (CPU)."""
 
+import pytest
 import torch
 
 from burn_dragon_b200.config import ContinualBackpropConfig, DragonConfig
@@ -80,3 +81,20 @@ def test_reference_statistics_from_model_forward():
     cbp.record_reference(model, torch.randint(0, 32, (2, 8)))
     cbp._fold_batch()
     assert cbp.samples == m.n_layer and float(cbp.avg_abs.sum()) > 0
+
+
+@pytest.mark.gpu
+def test_statistics_from_fused_step_buffers():
+    m = DragonConfig(n_layer=2, n_embd=64, n_head=2, mlp_internal_dim_multiplier=16, dropout=0.0,
+                     rotary_embedding="rope", initialization="simple_normal", vocab_size=256)
+    model = BDH(m, device="cuda", seed=0)
+    t = torch.randint(0, 256, (2, 128), device="cuda")
+    model.fused_step(t, t)
+    cbp = ContinualBackprop(ContinualBackpropConfig(enabled=True, utility_decay=0.0), m, 1e-3)
+    cbp.record_fused(model)
+    cbp._fold_batch()
+    ref = ContinualBackprop(ContinualBackpropConfig(enabled=True, utility_decay=0.0), m, 1e-3)
+    ref.record_reference(model, t)
+    ref._fold_batch()
+    assert cbp.samples == m.n_layer
+    torch.testing.assert_close(cbp.avg_abs, ref.avg_abs, rtol=0.05, atol=1e-4)

@@ -258,3 +258,28 @@ def test_toml_sections_for_runtime_features():
     with pytest.raises(ValueError):
         training_config_from_dict({"model": {"latent_reasoning": {"enabled": True, "max_steps": 1,
                                                                   "min_steps": 2}}})
+
+
+@pytest.mark.gpu
+def test_runtime_variants_on_cuda_match_cpu():
+    cfg = tiny()
+    cfg.y_neuron_recurrence.enabled = True
+    cfg.summary_memory.enabled = True
+    cfg.summary_memory.chunk_tokens = 4
+    cpu = DragonRuntime(cfg, seed=13)
+    gpu = DragonRuntime(copy.deepcopy(cfg), device="cuda", seed=13)
+    t = toks(T=8)
+    ref = cpu.forward(t)
+    got = gpu.forward(t.cuda())
+    torch.testing.assert_close(got.cpu(), ref, rtol=2e-3, atol=2e-3)
+    gpu.loss(t.cuda(), t.cuda()).backward()
+    assert torch.isfinite(gpu.core.encoder.grad).all()
+
+
+def test_y_neuron_recurrence_gradients_finite_with_silent_rows():
+    cfg = tiny(relu_threshold=0.05)
+    cfg.y_neuron_recurrence.enabled = True
+    rt = DragonRuntime(cfg, seed=14)
+    rt.loss(toks(T=6), toks(T=6, seed=3)).backward()
+    for p in rt.parameters():
+        assert p.grad is None or torch.isfinite(p.grad).all()
