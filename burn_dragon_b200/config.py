@@ -181,6 +181,65 @@ class SequenceScoreHeadConfig:
 
 
 @dataclass
+class GatedDeltaNet2Config:
+    """Gated DeltaNet-2 memory (burn_dragon_core/src/model/sequence/gdn2.rs:28-80)."""
+
+    chunk_size: int = 64
+    implementation: str = "bdh_adapter_legacy"
+    qk_l2_norm: bool = True
+    allow_neg_eigval: bool = False
+    erase_gate: str = "channel"  # channel | scalar | disabled
+    write_gate: str = "channel"
+    decay_gate: str = "channel"
+    state_precision: str = "f32"
+    state_epsilon: float = 1.0e-6
+    output_scale: float = 1.0
+
+
+@dataclass
+class MambaSequenceConfig:
+    """Mamba-3 SISO memory (burn_dragon_core/src/model/sequence/mamba.rs:60-130)."""
+
+    d_state: int = 16
+    d_conv: int = 4
+    expand: int = 2
+    dt_rank: int | None = None
+    dt_min: float = 1.0e-3
+    dt_max: float = 1.0e-1
+    dt_scale: float = 1.0
+    conv_bias: bool = True
+    use_fast_path: bool = True
+    headdim: int = 128
+    ngroups: int = 1
+    a_init_min: float = 1.0
+    a_init_max: float = 16.0
+    norm_eps: float = 1.0e-5
+    rope_fraction: float = 0.5
+    dt_init_floor: float = 1.0e-4
+    a_floor: float = 1.0e-4
+    chunk_size: int = 64
+    is_outproj_norm: bool = False
+    is_mimo: bool = False
+    mimo_rank: int = 1
+
+    def validate(self, d_model: int) -> None:
+        d_inner = d_model * self.expand
+        if self.headdim <= 0 or d_inner % self.headdim:
+            raise ValueError(f"mamba: d_inner {d_inner} must be divisible by headdim {self.headdim}")
+        if (d_inner // self.headdim) % self.ngroups:
+            raise ValueError("mamba: nheads must be divisible by ngroups")
+        if abs(self.rope_fraction - 0.5) > 1e-6 and abs(self.rope_fraction - 1.0) > 1e-6:
+            raise ValueError("mamba: rope_fraction must be 0.5 or 1.0")
+        split = int(self.d_state * self.rope_fraction)
+        if split - split % 2 < 2:
+            raise ValueError("mamba: d_state * rope_fraction needs at least one rotary pair")
+        if self.is_mimo:
+            raise ValueError("mamba: MIMO is not implemented (set is_mimo = false)")
+        if self.chunk_size <= 0 or self.dt_min <= 0 or self.dt_max < self.dt_min:
+            raise ValueError("mamba: invalid chunk_size / dt range")
+
+
+@dataclass
 class DragonConfig:
     """BDH model hyper-parameters (defaults as in config.rs:1030-1063)."""
 
@@ -216,6 +275,13 @@ class DragonConfig:
     # dense-score row chunk (sequence/config.rs)
     dense_score_row_chunk: int = 512
     random_scaffold: RandomScaffoldConfig = field(default_factory=RandomScaffoldConfig)
+    # sequence memory system (sequence/config.rs:12-120): linear_attention |
+    # mamba3_state_space_duality | gated_deltanet2; executor reference |
+    # dense_score_short_context | gated_delta_chunk_wy
+    sequence_memory_system: str = "linear_attention"
+    sequence_executor: str = "reference"
+    mamba: MambaSequenceConfig = field(default_factory=MambaSequenceConfig)
+    gated_deltanet2: GatedDeltaNet2Config = field(default_factory=GatedDeltaNet2Config)
     # residual connector: vanilla | mhc | attention_residual | block_attention_residual
     residual_connector: str = "vanilla"
     attention_residual: AttentionResidualConfig = field(default_factory=AttentionResidualConfig)
@@ -260,6 +326,14 @@ class DragonConfig:
         if self.residual_connector not in ("vanilla", "mhc", "attention_residual", "block_attention_residual"):
             raise ValueError(f"unknown residual_connector {self.residual_connector!r}")
         self.latent_reasoning.validate()
+        ok = {("linear_attention", "reference"), ("linear_attention", "dense_score_short_context"),
+              ("mamba3_state_space_duality", "reference"), ("gated_deltanet2", "reference"),
+              ("gated_deltanet2", "gated_delta_chunk_wy")}
+        if (self.sequence_memory_system, self.sequence_executor) not in ok:
+            raise ValueError(f"sequence kernel family {self.sequence_memory_system!r} with executor "
+                             f"{self.sequence_executor!r} is not supported")
+        if self.sequence_memory_system == "mamba3_state_space_duality":
+            self.mamba.validate(self.n_embd)
         for name in ("rho_sharing", "weight_sharing"):
             if getattr(self.hierarchical_dragon, name) not in ("shared", "split"):
                 raise ValueError(f"hierarchical_dragon.{name} must be 'shared' or 'split'")
@@ -279,7 +353,8 @@ class DragonConfig:
     def uses_extended_runtime(self) -> bool:
         """True when a feature outside the fused BDH step is on (these run on the PyTorch
         layer path of ``models.dragon_runtime``)."""
-        return (self.resolved_residual_connector() in ("attention_residual", "block_attention_residual")
+        return (self.sequence_memory_system != "linear_attention"
+                or self.resolved_residual_connector() in ("attention_residual", "block_attention_residual")
                 or self.y_neuron_recurrence.enabled or self.clocked_slow_memory.enabled
                 or self.summary_memory.enabled or self.hierarchical_dragon.enabled
                 or self.latent_reasoning.enabled or self.rollout_fast_steps_per_slow_step > 1)
@@ -484,6 +559,17 @@ def _model_table(table: dict) -> dict:
         t["mhc_streams"] = int(mhc.get("num_streams", 4))
         t["mhc_tau"] = float(mhc.get("mhc_tau", 1.0))
         t["mhc_iters"] = int(mhc.get("mhc_iters", 10))
+    sk = t.pop("sequence_kernel", None)
+    if isinstance(sk, str):
+        sk = {"memory_system": sk}
+    if isinstance(sk, dict):
+        fam = str(sk.get("memory_system", sk.get("family", "linear_attention"))).lower()
+        fam = {"gdn2": "gated_deltanet2"}.get(fam, fam)
+        t["sequence_memory_system"] = fam
+        ex = str(sk.get("executor") or "reference").lower()
+        t["sequence_executor"] = {"gdn2_chunk_wy": "gated_delta_chunk_wy"}.get(ex, ex)
+        if "dense_score_row_chunk" in sk:
+            t["dense_score_row_chunk"] = sk["dense_score_row_chunk"]
     ini = t.get("initialization")
     if isinstance(ini, dict):
         t["initialization"] = ini.get("kind", "near_critical")

@@ -51,11 +51,15 @@ class LayerState:
     clocked_hidden: torch.Tensor | None = None  # [B, 1, D]
     summary_hidden: torch.Tensor | None = None  # [B, 1, D]
     hier_slow: torch.Tensor | None = None  # [B, 1, D]
+    mamba: dict | None = None  # Mamba-3 ssm / angle / k / v
+    slow_mamba: dict | None = None
 
     def detach(self) -> None:
         for k, v in vars(self).items():
             if isinstance(v, torch.Tensor):
                 setattr(self, k, v.detach())
+            elif isinstance(v, dict):
+                setattr(self, k, {n: t.detach() for n, t in v.items()})
 
 
 @dataclass
@@ -244,6 +248,14 @@ class DragonRuntime(nn.Module):
                 mod.to(dev)
         for name, p in list(self._parameters.items()):
             self._parameters[name] = nn.Parameter(p.data.to(dev))
+        if cfg.sequence_memory_system == "gated_deltanet2":
+            from .sequence import GDN2Params
+
+            self.gdn2 = GDN2Params(cfg.n_head, D, cfg.latent_per_head, cfg.gated_deltanet2, gen).to(dev)
+        elif cfg.sequence_memory_system == "mamba3_state_space_duality":
+            from .sequence import Mamba3Params
+
+            self.mamba = Mamba3Params(D, cfg.mamba, gen).to(dev)
         Nh = cfg.latent_per_head
         self._freqs = None
         if cfg.rotary_embedding in ("rope", "pope"):
@@ -263,19 +275,43 @@ class DragonRuntime(nn.Module):
         return R.make_norm(c.norm_kind, p["norm_gamma"], p["norm_beta"], c.norm_eps, p.get("norm_alpha"),
                            p.get("norm_shift"))
 
-    def _attend(self, x, v, ls: LayerState, pos: int, fixed: bool, slot: str = "fast"):
-        """Linear attention reading and writing the layer's rho (slot ``slow`` = split rho)."""
+    def _rotate(self, x, pos: int, fixed: bool):
         T = x.shape[2]
-        positions = torch.full((T,), pos, device=x.device) if fixed else torch.arange(pos, pos + T, device=x.device)
         if self._freqs is None:
-            q = x
-        else:
-            ph = R.rope_phases(positions, self._freqs)[None, None]
-            q = R.pope_apply(x, ph) if self.cfg.rotary_embedding == "pope" else R.rope_apply(x, ph)
+            return x
+        positions = torch.full((T,), pos, device=x.device) if fixed else torch.arange(pos, pos + T, device=x.device)
+        ph = R.rope_phases(positions, self._freqs)[None, None]
+        return R.pope_apply(x, ph) if self.cfg.rotary_embedding == "pope" else R.rope_apply(x, ph)
+
+    def _attend(self, x, v, ls: LayerState, pos: int, fixed: bool, slot: str = "fast"):
+        """The sequence memory read / write (sequence_dispatch.rs:83-403): linear
+        attention on rho, Gated DeltaNet-2 on its delta-rule state, or Mamba-3 on the
+        dense stream. Slot ``slow`` uses the split (hierarchical slow) state."""
+        fam = self.cfg.sequence_memory_system
         attr = "slow_rho" if slot == "slow" else "rho"
         rho0 = getattr(ls, attr)
         if rho0 is not None and rho0.shape[0] != x.shape[0]:
             rho0 = None
+        if fam == "mamba3_state_space_duality":
+            mattr = "slow_mamba" if slot == "slow" else "mamba"
+            ctx, st = self.mamba(v, getattr(ls, mattr))
+            setattr(ls, mattr, st)
+            return ctx[:, None]
+        if fam == "gated_deltanet2":
+            from .sequence import gdn2_chunk_wy, gdn2_recurrent, l2_normalize
+
+            c = self.cfg.gated_deltanet2
+            key, erase, write, log_decay = self.gdn2.project(v)
+            q, k = self._rotate(x, pos, fixed), self._rotate(key, pos, fixed)
+            if c.qk_l2_norm:
+                q, k = l2_normalize(q, c.state_epsilon), l2_normalize(k, c.state_epsilon)
+            if self.cfg.sequence_executor == "gated_delta_chunk_wy":
+                out, S = gdn2_chunk_wy(q, k, v[:, None], erase, write, log_decay, rho0, c.chunk_size)
+            else:
+                out, S = gdn2_recurrent(q, k, v[:, None], erase, write, log_decay, rho0)
+            setattr(ls, attr, S)
+            return out * self.gdn2.output_scale
+        q = self._rotate(x, pos, fixed)
         a, rho = R.linear_attention_dense(q, v[:, None], rho0=rho0, decay=self._decay, need_state=True)
         setattr(ls, attr, rho)
         return a
