@@ -272,6 +272,10 @@ class DragonConfig:
     mhc_streams: int = 1
     mhc_tau: float = 1.0
     mhc_iters: int = 10
+    # latent block pattern (kernel/block_sparse.rs): None = dense; otherwise the active
+    # latent blocks (of latent_block_size neurons within each head)
+    latent_block_size: int = 64
+    latent_active_blocks: list[int] | None = None
     # dense-score row chunk (sequence/config.rs)
     dense_score_row_chunk: int = 512
     random_scaffold: RandomScaffoldConfig = field(default_factory=RandomScaffoldConfig)
@@ -353,7 +357,7 @@ class DragonConfig:
     def uses_extended_runtime(self) -> bool:
         """True when a feature outside the fused BDH step is on (these run on the PyTorch
         layer path of ``models.dragon_runtime``)."""
-        return (self.sequence_memory_system != "linear_attention"
+        return (self.sequence_memory_system != "linear_attention" or self.latent_active_blocks is not None
                 or self.resolved_residual_connector() in ("attention_residual", "block_attention_residual")
                 or self.y_neuron_recurrence.enabled or self.clocked_slow_memory.enabled
                 or self.summary_memory.enabled or self.hierarchical_dragon.enabled
@@ -542,6 +546,11 @@ def _model_table(table: dict) -> dict:
         for k in ("rope_theta", "relu_threshold", "alibi_slopes", "rotary_embedding"):
             if k in fk:
                 t[k] = fk[k]
+        lat = (fk.get("block_sparse") or {}).get("latent") if isinstance(fk.get("block_sparse"), dict) else None
+        if isinstance(lat, dict):
+            t["latent_block_size"] = int(lat.get("block_size", 64))
+            if lat.get("active_blocks") is not None:
+                t["latent_active_blocks"] = sorted(int(b) for b in lat["active_blocks"])
     if "rotary_embedding" in t and isinstance(t["rotary_embedding"], str):
         t["rotary_embedding"] = t["rotary_embedding"].lower()
     norm = t.pop("normalization", None)

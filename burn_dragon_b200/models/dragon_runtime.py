@@ -261,6 +261,12 @@ class DragonRuntime(nn.Module):
         if cfg.rotary_embedding in ("rope", "pope"):
             f = R.rope_freqs if cfg.rotary_embedding == "rope" else R.pope_freqs
             self._freqs = f(Nh, cfg.rope_theta, device=dev)
+        self._latent_mask = None
+        if cfg.latent_active_blocks is not None:
+            from .legacy_attention import BlockPattern1d
+
+            pat = BlockPattern1d(cfg.latent_block_size, set(cfg.latent_active_blocks))
+            self._latent_mask = pat.mask(cfg.latent_per_head, device=dev)
         self._decay = R.decay_vector(cfg.decay_slopes(), device=dev) if cfg.uses_decay() else None
 
     # ------------------------------------------------------------------ pieces
@@ -320,11 +326,16 @@ class DragonRuntime(nn.Module):
         enc, enc_v, dec, p = self._weights(slow_weights)
         nf = self._norm(p)
         thr = self.cfg.relu_threshold
+        lm = self._latent_mask
         x = torch.relu(torch.einsum("btd,hdn->bhtn", v, enc) - thr)
+        if lm is not None:
+            x = x * lm
         if x_inject is not None:
             x = x + x_inject
         a = nf(self._attend(x, v, ls, pos, fixed, slot))
         y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr)
+        if lm is not None:
+            y = y * lm
         yn = x * y
         if self.cfg.dropout > 0 and self.training:
             yn = F.dropout(yn, self.cfg.dropout, True)
@@ -411,6 +422,8 @@ class DragonRuntime(nn.Module):
         st = ls.y_state
         st = self._stabilize(st) if st is not None and st.shape == (B, H, Nh) else v.new_zeros(B, H, Nh)
         x_base = torch.relu(torch.einsum("btd,hdn->bhtn", v, enc) - thr)
+        if self._latent_mask is not None:
+            x_base = x_base * self._latent_mask
         ck = max(1, min(c.chunk_tokens, T))
         outs = []
         for s in range(0, T, ck):
@@ -421,6 +434,8 @@ class DragonRuntime(nn.Module):
             tok = v[:, s:e]
             a = nf(self._attend(x, tok, ls, start_pos if fixed else start_pos + s, fixed))
             y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr)
+            if self._latent_mask is not None:
+                y = y * self._latent_mask
             yn = x * y
             if self.cfg.dropout > 0 and self.training:
                 yn = F.dropout(yn, self.cfg.dropout, True)
