@@ -435,6 +435,28 @@ class ContinualBackpropConfig:
 
 
 @dataclass
+class PCInferenceConfig:
+    """Activity-inference rule of local predictive coding (burn_pc PcInferenceConfig;
+    defaults burn_dragon_language/src/config/train/schema.rs:621-639)."""
+
+    steps: int = 4
+    step_size: float = 0.05
+    latent_decay: float = 0.0
+    max_grad_norm: float | None = 1.0
+    gradient_norm_scope: str = "per_row"  # per_row | global
+    eps: float = 1.0e-8
+
+
+@dataclass
+class LocalPredictiveCodingConfig:
+    solver: str = "synchronous_equilibrium"  # | reverse_gauss_seidel | fixed_prediction
+    inference: PCInferenceConfig = field(default_factory=PCInferenceConfig)
+    prediction_precision: float = 1.0
+    factor_reduction: str = "sum"  # sum | mean
+    sync_diagnostics: bool = False
+
+
+@dataclass
 class TrainingSection:
     block_size: int = 512
     batch_size: int = 32
@@ -448,6 +470,9 @@ class TrainingSection:
     checkpoint_interval_iters: int | None = None
     validation_interval_iters: int | None = None
     continual_backprop: ContinualBackpropConfig = field(default_factory=ContinualBackpropConfig)
+    # auto | backpropagation | predictive_coding | eggroll (schema.rs:569-577)
+    algorithm: str = "auto"
+    local_predictive_coding: LocalPredictiveCodingConfig = field(default_factory=LocalPredictiveCodingConfig)
 
 
 @dataclass

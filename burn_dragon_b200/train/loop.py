@@ -96,6 +96,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         pl = plan(cfg.model.n_layer, world, int(pp.get("micro_batches", 4)), pp.get("schedule", "1f1b"))
         runner = PipelineRunner(trainer.model, pl, rank, t.batch_size // pl.micro, t.block_size)
 
+    pc = t.algorithm == "predictive_coding"
+    if pc and (extended or mode not in ("single", "ddp", "fsdp")):
+        raise ValueError("predictive_coding training needs the plain BDH model in single / ddp mode")
     cbp = None
     if t.continual_backprop.enabled:
         m = cfg.model
@@ -174,6 +177,15 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 loss = loss if loss is not None else torch.zeros(())
             elif streaming:
                 loss = trainer.step_stream(x, y, state)
+                prof.stop("forward_backward")
+            elif pc:
+                from .optim import lr_at
+                from .predictive_coding import local_pc_step
+
+                loss, _ = local_pc_step(trainer.model, x.to(dev), y.to(dev), t.local_predictive_coding)
+                trainer.opt.prepare(lr_at(trainer.step_idx, trainer.base_lr, trainer.lr_schedule, trainer.max_iters))
+                trainer._update()
+                trainer.step_idx += 1
                 prof.stop("forward_backward")
             else:
                 sample = cbp is not None and cbp.should_sample()

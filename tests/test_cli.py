@@ -106,3 +106,12 @@ def test_continual_backprop_in_training_loop(tmp_path, monkeypatch, capsys):
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     events = [json.loads(line) for line in open(os.path.join(res["run_dir"], "events", "metrics.jsonl"))]
     assert any("cbp_replaced" in e for e in events)
+
+
+def test_predictive_coding_training_run(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.max_iters=4",
+          "--set", 'training.algorithm="predictive_coding"', "--set", "training.block_size=32",
+          "--set", "training.local_predictive_coding.inference.steps=2", "--run-name", "pc"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None and res["steps"] == 4
