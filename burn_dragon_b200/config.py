@@ -473,6 +473,9 @@ class TrainingSection:
     # auto | backpropagation | predictive_coding | eggroll (schema.rs:569-577)
     algorithm: str = "auto"
     local_predictive_coding: LocalPredictiveCodingConfig = field(default_factory=LocalPredictiveCodingConfig)
+    # training objective table (objective.rs TrainingObjectiveConfig): {type = "next_token"
+    # | "sdft" | "sdpo" | "sdft_sdpo", sdft = {...}, sdpo = {...}, sdft_weight, sdpo_weight}
+    objective: dict[str, Any] = field(default_factory=lambda: {"type": "next_token"})
 
 
 @dataclass

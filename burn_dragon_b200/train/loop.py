@@ -99,6 +99,21 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     pc = t.algorithm == "predictive_coding"
     if pc and (extended or mode not in ("single", "ddp", "fsdp")):
         raise ValueError("predictive_coding training needs the plain BDH model in single / ddp mode")
+    objective = None
+    if t.objective.get("type", "next_token") != "next_token":
+        from . import objectives as OBJ
+        from ..config import _fill
+
+        sub = dict(t.objective)
+        oc = OBJ.ObjectiveConfig(type=sub.pop("type"),
+                                 sdft=_fill(OBJ.SdftObjectiveConfig, sub.pop("sdft", {}), {}, ""),
+                                 sdpo=_fill(OBJ.SdpoObjectiveConfig, sub.pop("sdpo", {}), {}, ""),
+                                 **{k: v for k, v in sub.items() if k in ("sdft_weight", "sdpo_weight")})
+        oc.validate()
+        if extended or pc or mode not in ("single", "ddp", "fsdp"):
+            raise ValueError("self-distillation objectives need the plain BDH model in single / ddp mode")
+        rate = oc.sdpo.teacher_update_rate if oc.type == "sdpo" else oc.sdft.teacher_update_rate
+        objective = (oc, OBJ.EMATeacher(trainer.model, rate))
     cbp = None
     if t.continual_backprop.enabled:
         m = cfg.model
@@ -177,6 +192,23 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 loss = loss if loss is not None else torch.zeros(())
             elif streaming:
                 loss = trainer.step_stream(x, y, state)
+                prof.stop("forward_backward")
+            elif objective is not None:
+                from . import objectives as OBJ
+                from .optim import lr_at
+
+                oc, teacher = objective
+                m = trainer.model
+                lo = OBJ.window_objective_loss(m, teacher.model, x.to(dev), y.to(dev), oc)
+                gr = torch.autograd.grad(lo, list(m.parameters()), allow_unused=True)
+                for (n, _), g in zip(m.named_parameters(), gr):
+                    view = m.store.view(m.store.grad, n)
+                    view.zero_() if g is None else view.copy_(g)
+                trainer.opt.prepare(lr_at(trainer.step_idx, trainer.base_lr, trainer.lr_schedule, trainer.max_iters))
+                trainer._update()
+                trainer.step_idx += 1
+                teacher.update(m)
+                loss = lo.detach()
                 prof.stop("forward_backward")
             elif pc:
                 from .optim import lr_at

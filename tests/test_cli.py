@@ -115,3 +115,11 @@ def test_predictive_coding_training_run(tmp_path, monkeypatch, capsys):
           "--set", "training.local_predictive_coding.inference.steps=2", "--run-name", "pc"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res["final_loss"] is not None and res["steps"] == 4
+
+
+def test_self_distillation_objective_training_run(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.max_iters=3",
+          "--set", "training.block_size=32", "--set", 'training.objective.type="sdft_sdpo"', "--run-name", "sd"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None
