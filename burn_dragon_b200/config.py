@@ -457,6 +457,24 @@ class LocalPredictiveCodingConfig:
 
 
 @dataclass
+class AutoBatchSizeConfig:
+    """Startup batch-size selection (burn_dragon_language/src/config/train/schema.rs:
+    209-255; defaults :179-205)."""
+
+    enabled: bool = False
+    max_batch_size: int | None = None
+    max_probe_batch_size: int | None = None
+    min_batch_size: int = 1
+    target_device_memory_mb: int = 0
+    probe_steps: int = 1
+    binary_search: bool = True
+    recompute_on_neuron_scale: bool = True
+    scale_memory_exponent: float = 1.0
+    max_system_memory_fraction: float = 0.9
+    probe_safety_margin: float = 1.15
+
+
+@dataclass
 class TrainingSection:
     block_size: int = 512
     batch_size: int = 32
@@ -470,6 +488,8 @@ class TrainingSection:
     checkpoint_interval_iters: int | None = None
     validation_interval_iters: int | None = None
     continual_backprop: ContinualBackpropConfig = field(default_factory=ContinualBackpropConfig)
+    auto_batch_size: AutoBatchSizeConfig = field(default_factory=AutoBatchSizeConfig)
+    target_effective_batch_size: int | None = None
     # auto | backpropagation | predictive_coding | eggroll (schema.rs:569-577)
     algorithm: str = "auto"
     local_predictive_coding: LocalPredictiveCodingConfig = field(default_factory=LocalPredictiveCodingConfig)

@@ -74,6 +74,15 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         # the residual stream is replicated across the tensor-parallel group; the sum is an
         # all-reduce of [M, D] per layer (a reduce-scatter + all-gather moves the same bytes)
         pass
+    if t.auto_batch_size.enabled:
+        from .autotune import choose_batch_size
+
+        res = choose_batch_size(cfg.model, t.block_size, t.auto_batch_size,
+                                target_effective_batch=t.target_effective_batch_size)
+        t.batch_size = res.batch_size * res.gradient_accumulation_steps
+        cfg.parallel.tensor["micro_batches"] = res.gradient_accumulation_steps
+        if rank == 0:
+            run.write_json("auto_batch_size.json", vars(res))
     extended = cfg.model.uses_extended_runtime()
     if extended and mode not in ("single", "ddp", "fsdp"):
         raise ValueError(f"parallel mode {mode!r} does not support the layer-loop variants this model enables")
