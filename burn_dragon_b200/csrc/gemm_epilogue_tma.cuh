@@ -1,15 +1,22 @@
 // gemm_epilogue_tma.cuh — asynchronous epilogue for the memory-bound BDH modes
 // (x-projection + RoPE, gate, decoder backward, dQ), tile N = 128.
 //
-// Each epilogue warp owns a 32-row x 64-column chunk of every tile. Its auxiliary
-// operands (x, yn, dx_part) are fetched by TMA one tile ahead into a double-buffered,
-// 128B-swizzled smem tile pair, so the fetch overlaps the current tile's math and
-// store; results are written over the aux tile in place and leave through TMA bulk
-// stores. No warp ever waits on a global load of its own, and the accumulator is handed
+// Each epilogue warp owns a 32-row x CW-column chunk of every tile: CW = 64 with 8
+// warps (128-byte rows, 128B swizzle) or CW = 32 with 16 warps (64-byte rows, 64B
+// swizzle). A warp's auxiliary operands (x, yn, dx_part) are fetched by TMA one tile
+// ahead into a double-buffered smem tile pair, so the fetch overlaps the current tile's
+// math and store; results are written over the aux tile in place and leave through TMA
+// bulk stores. No warp ever waits on a global load of its own, and the accumulator is handed
 // back to the MMA warp right after tcgen05.ld, before the math.
 #pragma once
 
 namespace bd {
+
+// Byte offset of 16-byte chunk `chunk` (0..3) of row `row` in a 32 x 32 bf16 tile laid
+// out by a TMA SWIZZLE_64B box: 64-byte rows, chunk index XOR address bits 7..8.
+__device__ __forceinline__ uint32_t sw64_off(int row, int chunk) {
+  return (uint32_t)(row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
+}
 
 template <int EPI>
 constexpr int epi_naux() {
@@ -17,8 +24,16 @@ constexpr int epi_naux() {
 }
 
 // In-place math on the smem tiles b0 (and b1) for this thread's row.
-template <int EPI>
-__device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoord& tc, float (&v)[64], int row,
+template <int CW>
+__device__ __forceinline__ uint32_t epi_off(int row, int chunk) {
+  if constexpr (CW == 32)
+    return sw64_off(row, chunk);
+  else
+    return stg_off(row, chunk);
+}
+
+template <int EPI, int CW>
+__device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoord& tc, float (&v)[CW], int row,
                                              int col0, uint8_t* b0, uint8_t* b1, int lane) {
   const EpiParams& e = p.e;
   float pos = 0.f;
@@ -32,14 +47,14 @@ __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoor
     if (e.row_decay) {
       const float a = exp2f((float)row * e.log2_decay[tc.z1]);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] *= a;
+      for (int i = 0; i < CW; ++i) v[i] *= a;
     }
   }
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
+  for (int c = 0; c < CW / 8; ++c) {
     float* w = v + 8 * c;
-    uint4* s0 = reinterpret_cast<uint4*>(b0 + stg_off(lane, c));
-    uint4* s1 = reinterpret_cast<uint4*>(b1 + stg_off(lane, c));
+    uint4* s0 = reinterpret_cast<uint4*>(b0 + epi_off<CW>(lane, c));
+    uint4* s1 = reinterpret_cast<uint4*>(b1 + epi_off<CW>(lane, c));
     if constexpr (EPI == EPI_RELU_ROPE) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) w[i] = fmaxf(w[i] - e.thr, 0.0f);

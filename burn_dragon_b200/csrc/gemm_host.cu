@@ -71,20 +71,21 @@ CUtensorMap encode_map(const at::Tensor& t, const Geom& g, uint32_t box_inner, u
   return m;
 }
 
-// 32 x 64 box map over an output-shaped bf16 matrix (cols, rows, z1, z2) for the TMA
-// epilogue; strides in elements.
+// 32-row box map over an output-shaped bf16 matrix (cols, rows, z1, z2) for the TMA
+// epilogue, `cols` = 64 (128-byte swizzle) or 32 (64-byte swizzle); strides in elements.
 CUtensorMap encode_out_map(const void* ptr, int64_t N, int64_t M, int64_t ld, int64_t Z1, int64_t sz1, int64_t Z2,
-                           int64_t sz2) {
+                           int64_t sz2, uint32_t cols) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA epilogue tensors must be 16-byte aligned");
   const int64_t fallback = ((M * ld * 2 + 15) / 16) * 16;
   cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)Z1, (cuuint64_t)Z2};
   cuuint64_t strides[3] = {(cuuint64_t)(ld * 2), (cuuint64_t)(Z1 > 1 ? sz1 * 2 : fallback),
                            (cuuint64_t)(Z2 > 1 ? sz2 * 2 : fallback)};
-  cuuint32_t box[4] = {64, 32, 1, 1};
+  cuuint32_t box[4] = {cols, 32, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUtensorMap m;
   CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (epilogue map) failed with code ", (int)r);
   return m;
@@ -196,10 +197,12 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   if (epi == EPI_DQ) TORCH_CHECK(e.aux0 && e.aux1, "dq epilogue needs dx_part and x");
   if (epi == EPI_RELU_ROPE || epi == EPI_GATE || epi == EPI_DEC_BWD || epi == EPI_DQ) {
     TORCH_CHECK(bn == 128, "TMA-epilogue modes use tile N = 128");
-    p.to0 = encode_out_map(e.out0, N, M, ld, Z1, sz1, Z2, sz2);
-    if (e.out1) p.to1 = encode_out_map(e.out1, N, M, ld, Z1, sz1, Z2, sz2);
-    if (e.aux0) p.tx0 = encode_out_map(e.aux0, N, M, ld, Z1, sz1, Z2, sz2);
-    if (e.aux1) p.tx1 = encode_out_map(e.aux1, N, M, ld, Z1, sz1, Z2, sz2);
+    // columns per epilogue warp: 32 for the 16-warp x-projection epilogue, else 64
+    const uint32_t cw = epi == EPI_RELU_ROPE ? 32 : 64;
+    p.to0 = encode_out_map(e.out0, N, M, ld, Z1, sz1, Z2, sz2, cw);
+    if (e.out1) p.to1 = encode_out_map(e.out1, N, M, ld, Z1, sz1, Z2, sz2, cw);
+    if (e.aux0) p.tx0 = encode_out_map(e.aux0, N, M, ld, Z1, sz1, Z2, sz2, cw);
+    if (e.aux1) p.tx1 = encode_out_map(e.aux1, N, M, ld, Z1, sz1, Z2, sz2, cw);
   }
   hit->fn(p, at::cuda::getCurrentCUDAStream(dev).stream(), dev);
 }

@@ -74,8 +74,12 @@ struct alignas(64) GemmParams {
 // TMA one tile ahead into double-buffered smem, results stored by TMA; BN = 128 only).
 template <int EPI>
 constexpr int epi_kind() {
+  // 0: fp32 row stores; 1: staged bf16; 2: TMA epilogue, 8 warps x 64 columns;
+  // 3: TMA epilogue, 16 warps x 32 columns (the store-only x-projection, where more
+  // concurrent warps beat wider boxes)
   return EPI == EPI_F32 ? 0
-         : ((EPI == EPI_RELU_ROPE || EPI == EPI_GATE || EPI == EPI_DEC_BWD || EPI == EPI_DQ) ? 2 : 1);
+         : EPI == EPI_RELU_ROPE ? 3
+                                : ((EPI == EPI_GATE || EPI == EPI_DEC_BWD || EPI == EPI_DQ) ? 2 : 1);
 }
 
 template <int BN, int KIND = 0>
@@ -86,14 +90,17 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = KIND == 2 ? 3
+  static constexpr int STAGES = KIND >= 2 ? 3
                                : (STAGED ? ((BN == 256) ? 3 : (BN == 128 ? 4 : 5))
                                          : ((BN == 256) ? 4 : (BN == 128 ? 6 : 8)));
-  // kind 2: 8 warps x 2 tile buffers x 2 tensors x 4 KB
-  static constexpr int EPI_BYTES = KIND == 2 ? 8 * 2 * 2 * 4096 : (STAGED ? 8 * 2 * 4096 : 0);
+  // epilogue warps: kind 3 runs 16 (four per TMEM lane quadrant, 32 columns each),
+  // the others 8 (two per quadrant, 64 columns each)
+  static constexpr int NEPI = KIND == 3 ? 16 : 8;
+  // kinds 2 / 3: warps x 2 tile buffers x 2 tensors x (32 rows x columns-per-warp bf16)
+  static constexpr int EPI_BYTES = KIND >= 2 ? 128 * 1024 : (STAGED ? 8 * 2 * 4096 : 0);
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 64 + 32 * NEPI;
 };
 
 struct TileCoord {

@@ -53,7 +53,7 @@ __device__ __forceinline__ TileCoord decode_tile_pair(const GemmParams& p, int t
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(320, 1) gemm_sm100_2cta_kernel(const __grid_constant__ GemmParams p) {
   constexpr int KIND = epi_kind<EPI>();
-  static_assert(KIND != 2, "the pair kernel serves the fp32 and staged-bf16 epilogues");
+  static_assert(KIND < 2, "the pair kernel serves the fp32 and staged-bf16 epilogues");
   constexpr bool STAGED = KIND == 1;
   using Cfg = Gemm2Cfg<BN, KIND>;
   constexpr int STAGES = Cfg::STAGES;

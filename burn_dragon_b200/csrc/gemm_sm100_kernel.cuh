@@ -5,10 +5,11 @@
 namespace bd {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
+    gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
   constexpr int KIND = epi_kind<EPI>();
   constexpr bool STAGED = KIND == 1;
-  static_assert(KIND != 2 || BN == 128, "the TMA epilogue is built for tile N = 128");
+  static_assert(KIND < 2 || BN == 128, "the TMA epilogue is built for tile N = 128");
   using Cfg = GemmCfg<BN, KIND>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -19,7 +20,7 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_flag;
-  __shared__ uint64_t aux_bar[8][2];
+  __shared__ uint64_t aux_bar[16][2];
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -36,10 +37,10 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 8);
+      mbar_init(&tempty_bar[a], Cfg::NEPI);
     }
     mbar_init(&drain_bar, 1);
-    for (int w = 0; w < 8; ++w) {
+    for (int w = 0; w < Cfg::NEPI; ++w) {
       mbar_init(&aux_bar[w][0], 1);
       mbar_init(&aux_bar[w][1], 1);
     }
@@ -164,16 +165,18 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
       mbar_wait_bounded(&drain_bar, 0, (volatile int*)&dummy_abort, p.err, kErrTimeoutDrain);
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 2..9)
-    const int ew = warp - 2;    // 0..7
+    // ------------------------------------------------ epilogue (warps 2..)
+    const int ew = warp - 2;    // 0..NEPI-1
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-    const int half = ew >> 2;   // column half of the tile
+    const int half = ew >> 2;   // column group of the tile
     const int r_local = quad * 32 + lane;
-    if constexpr (KIND == 2) {
-      // ---------------- TMA epilogue (see gemm_epilogue_tma.cuh)
+    if constexpr (KIND >= 2) {
+      // ---------------- TMA epilogue (see gemm_epilogue_tma.cuh): 32 rows x CW columns
       constexpr int NAUX = epi_naux<EPI>();
-      uint8_t* wbuf = sEpi + ew * 4 * kStageTileBytes;  // [tile parity][tensor] 4 KB tiles
-      const int col_off = half * 64;
+      constexpr int CW = KIND == 3 ? 32 : 64;
+      constexpr int kTmaTileBytes = 32 * CW * 2;
+      uint8_t* wbuf = sEpi + ew * 4 * kTmaTileBytes;  // [tile parity][tensor] tiles
+      const int col_off = half * CW;
       // Per-buffer issue / wait counters keep the mbarrier parities exact (uniform
       // across the warp; only lane 0 issues).
       int n_issued[2] = {0, 0}, n_waited[2] = {0, 0};
@@ -184,12 +187,12 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
           if (n.zero) return;
           ++n_issued[b];
           if (lane != 0) return;
-          uint8_t* dst = wbuf + b * 2 * kStageTileBytes;
+          uint8_t* dst = wbuf + b * 2 * kTmaTileBytes;
           fence_proxy_async_smem();
-          mbar_arrive_expect_tx(&aux_bar[ew][b], NAUX * kStageTileBytes);
+          mbar_arrive_expect_tx(&aux_bar[ew][b], NAUX * kTmaTileBytes);
           tma_load_4d(dst, &p.tx0, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1, n.z2);
           if constexpr (NAUX > 1)
-            tma_load_4d(dst + kStageTileBytes, &p.tx1, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1,
+            tma_load_4d(dst + kTmaTileBytes, &p.tx1, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1,
                         n.z2);
         }
       };
@@ -200,8 +203,8 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
         const TileCoord tc = decode_tile(p, t, BN);
         const int b = it & 1;
-        uint8_t* b0 = wbuf + b * 2 * kStageTileBytes;
-        uint8_t* b1 = b0 + kStageTileBytes;
+        uint8_t* b0 = wbuf + b * 2 * kTmaTileBytes;
+        uint8_t* b1 = b0 + kTmaTileBytes;
         // the other buffer was last read by this warp's stores of the previous tile
         if (lane == 0) bulk_wait_group_read0();
         __syncwarp();
@@ -209,8 +212,11 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
         if (tc.zero) continue;  // (no zero tiles in these modes unless K is empty)
         if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
         tc_fence_after();
-        float v[64];
-        tmem_ld64(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
+        float v[CW];
+        if constexpr (CW == 32)
+          tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
+        else
+          tmem_ld64(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -222,7 +228,7 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_kernel(const __grid_constan
           if (!mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
           ++n_waited[b];
         }
-        tma_epi_math<EPI>(p, tc, v, tc.m0 + r_local, tc.n0 + col_off, b0, b1, lane);
+        tma_epi_math<EPI, CW>(p, tc, v, tc.m0 + r_local, tc.n0 + col_off, b0, b1, lane);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
