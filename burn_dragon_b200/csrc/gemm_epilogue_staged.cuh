@@ -87,10 +87,8 @@ __device__ __forceinline__ void epilogue_chunk64(const GemmParams& p, const Tile
 
   if constexpr (EPI == EPI_GATE) {
     coop_load(e.aux0 + base, e.ld, rows_valid, cols_valid, buf0, lane);
-  } else if constexpr (EPI == EPI_DEC_BWD || EPI == EPI_DQ) {
-    coop_load(e.aux0 + base, e.ld, rows_valid, cols_valid, buf0, lane);
-    coop_load(e.aux1 + base, e.ld, rows_valid, cols_valid, buf1, lane);
   }
+  static_assert(EPI != EPI_DEC_BWD && EPI != EPI_DQ, "decoder-backward and dQ use the TMA epilogue");
   __syncwarp();
 
   float pos = 0.f;
@@ -98,9 +96,6 @@ __device__ __forceinline__ void epilogue_chunk64(const GemmParams& p, const Tile
   if constexpr (EPI == EPI_RELU_ROPE) {
     pos = (float)(e.pos0 + row % e.T);
     j0 = col0 % e.Nh;
-  } else if constexpr (EPI == EPI_DQ) {
-    pos = (float)(e.pos0 + row);
-    j0 = col0;
   }
   float l2g = 0.f;
   if constexpr (EPI == EPI_SCORES) {
@@ -146,39 +141,6 @@ __device__ __forceinline__ void epilogue_chunk64(const GemmParams& p, const Tile
       unpack8(*reinterpret_cast<const uint4*>(buf0 + stg_off(lane, c)), xv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) w[i] = fmaxf(w[i] - e.thr, 0.0f) * xv[i];
-      *reinterpret_cast<uint4*>(buf0 + stg_off(lane, c)) = pack8(w);
-    } else if constexpr (EPI == EPI_DEC_BWD) {
-      float xv[8], yv[8], dy[8];
-      unpack8(*reinterpret_cast<const uint4*>(buf0 + stg_off(lane, c)), xv);
-      unpack8(*reinterpret_cast<const uint4*>(buf1 + stg_off(lane, c)), yv);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float g = w[i];
-        const float y = (xv[i] > 0.0f) ? __fdividef(yv[i], xv[i]) : 0.0f;
-        dy[i] = (yv[i] > 0.0f) ? g * xv[i] : 0.0f;
-        w[i] = g * y;
-      }
-      *reinterpret_cast<uint4*>(buf0 + stg_off(lane, c)) = pack8(w);
-      *reinterpret_cast<uint4*>(buf1 + stg_off(lane, c)) = pack8(dy);
-    } else if constexpr (EPI == EPI_DQ) {
-      float bv[8], xv[8];
-      unpack8(*reinterpret_cast<const uint4*>(buf0 + stg_off(lane, c)), bv);
-      unpack8(*reinterpret_cast<const uint4*>(buf1 + stg_off(lane, c)), xv);
-      if (e.freq) {
-        const float4 fa = *reinterpret_cast<const float4*>(e.freq + j0 + 8 * c);
-        const float4 fb = *reinterpret_cast<const float4*>(e.freq + j0 + 8 * c + 4);
-        const float f[4] = {fa.x, fa.z, fb.x, fb.z};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float cs, sn;
-          rope_cs(pos, f[i], cs, sn);
-          const float ge = w[2 * i], go = w[2 * i + 1];
-          w[2 * i] = ge * cs + go * sn;
-          w[2 * i + 1] = go * cs - ge * sn;
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = (xv[i] > 0.0f) ? (w[i] + bv[i]) : 0.0f;
       *reinterpret_cast<uint4*>(buf0 + stg_off(lane, c)) = pack8(w);
     }
   }

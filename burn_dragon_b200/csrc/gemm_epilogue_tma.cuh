@@ -20,8 +20,16 @@ __device__ __forceinline__ uint32_t sw64_off(int row, int chunk) {
 
 template <int EPI>
 constexpr int epi_naux() {
-  return EPI == EPI_GATE ? 1 : ((EPI == EPI_DEC_BWD || EPI == EPI_DQ) ? 2 : 0);
+  return (EPI == EPI_GATE || EPI == EPI_DQ) ? 1 : (EPI == EPI_DEC_BWD ? 2 : 0);
 }
+
+// The x > 0 mask rides in dx_part: the decoder backward writes -0.0 (bf16 0x8000) where
+// x <= 0 and flushes |value| < 1e-30 to +0.0 elsewhere, so no live entry carries the
+// 0x8000 pattern; dQ reads the mask from those bits instead of re-reading x, and keeps
+// the marker in its output for a second dQ pass over the same buffer.
+constexpr unsigned short kMaskedBits = 0x8000u;
+
+__device__ __forceinline__ float flush_live(float v) { return fabsf(v) < 1e-30f ? 0.0f : v; }
 
 // In-place math on the smem tiles b0 (and b1) for this thread's row.
 template <int CW>
@@ -86,16 +94,18 @@ __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoor
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float g = w[i];
-        const float y = (xv[i] > 0.0f) ? __fdividef(yv[i], xv[i]) : 0.0f;
+        const bool live = xv[i] > 0.0f;
+        const float y = live ? __fdividef(yv[i], xv[i]) : 0.0f;
         dy[i] = (yv[i] > 0.0f) ? g * xv[i] : 0.0f;
-        w[i] = g * y;
+        w[i] = live ? flush_live(g * y) : -0.0f;
       }
       *s0 = pack8(w);
       *s1 = pack8(dy);
     } else if constexpr (EPI == EPI_DQ) {
-      float bv[8], xv[8];
-      unpack8(*s0, bv);
-      unpack8(*s1, xv);
+      float bv[8];
+      const uint4 raw = *s0;
+      const unsigned short* bits = reinterpret_cast<const unsigned short*>(&raw);
+      unpack8(raw, bv);
       if (e.freq) {
         const float4 fa = *reinterpret_cast<const float4*>(e.freq + j0 + 8 * c);
         const float4 fb = *reinterpret_cast<const float4*>(e.freq + j0 + 8 * c + 4);
@@ -110,7 +120,7 @@ __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoor
         }
       }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = (xv[i] > 0.0f) ? (w[i] + bv[i]) : 0.0f;
+      for (int i = 0; i < 8; ++i) w[i] = bits[i] == kMaskedBits ? -0.0f : flush_live(w[i] + bv[i]);
       *s0 = pack8(w);
     }
   }

@@ -194,7 +194,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   if (epi == EPI_RELU_ROPE && e.freq) TORCH_CHECK(e.out1, "RoPE epilogue needs out1");
   if (epi == EPI_GATE) TORCH_CHECK(e.aux0, "gate epilogue needs aux0 (x)");
   if (epi == EPI_DEC_BWD) TORCH_CHECK(e.aux0 && e.aux1 && e.out1, "decoder backward epilogue needs x, yn, out1");
-  if (epi == EPI_DQ) TORCH_CHECK(e.aux0 && e.aux1, "dq epilogue needs dx_part and x");
+  if (epi == EPI_DQ) TORCH_CHECK(e.aux0, "dq epilogue needs dx_part (carrying the x mask)");
   if (epi == EPI_RELU_ROPE || epi == EPI_GATE || epi == EPI_DEC_BWD || epi == EPI_DQ) {
     TORCH_CHECK(bn == 128, "TMA-epilogue modes use tile N = 128");
     // columns per epilogue warp: 32 for the 16-warp x-projection epilogue, else 64

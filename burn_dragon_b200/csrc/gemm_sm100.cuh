@@ -31,8 +31,9 @@ enum EpiMode : int {
   EPI_RELU_ROPE = 2,  // x = relu(acc - thr) -> out0; q = rope(x, pos) -> out1
   EPI_SCORES = 3,     // strictly-causal masked (and decayed) scores -> out0 (bf16)
   EPI_GATE = 4,       // yn = relu(acc - thr) * x(aux0) -> out0 (bf16)
-  EPI_DEC_BWD = 5,    // acc = d(yn): dx_part -> out0, dy_pre -> out1 (aux0 = x, aux1 = yn)
-  EPI_DQ = 6,         // acc = d(q): dx_pre = (aux0 + rope^T(acc)) * [x(aux1) > 0] -> out0
+  EPI_DEC_BWD = 5,    // acc = d(yn): dx_part -> out0, dy_pre -> out1 (aux0 = x, aux1 = yn);
+                      // dx_part carries the x <= 0 mask as -0.0
+  EPI_DQ = 6,         // acc = d(q): dx_pre = (aux0 + rope^T(acc)), masked by aux0's -0.0 -> out0
 };
 
 struct EpiParams {
@@ -74,12 +75,16 @@ struct alignas(64) GemmParams {
 // TMA one tile ahead into double-buffered smem, results stored by TMA; BN = 128 only).
 template <int EPI>
 constexpr int epi_kind() {
-  // 0: fp32 row stores; 1: staged bf16; 2: TMA epilogue, 8 warps x 64 columns;
-  // 3: TMA epilogue, 16 warps x 32 columns (the store-only x-projection, where more
-  // concurrent warps beat wider boxes)
+  // 0: fp32 row stores; 1: staged bf16; 2: TMA epilogue, 8 warps x 64 columns, two
+  // tile buffers of two tensors; 3: TMA epilogue, 16 warps x 32 columns (the store-only
+  // x-projection, where more concurrent warps beat wider boxes); 4: TMA epilogue,
+  // 8 warps x 64 columns, a ring of three single-tensor buffers (the gate and dQ: a
+  // buffer's store has two tiles to drain before the buffer is refilled)
   return EPI == EPI_F32 ? 0
-         : EPI == EPI_RELU_ROPE ? 3
-                                : ((EPI == EPI_GATE || EPI == EPI_DEC_BWD || EPI == EPI_DQ) ? 2 : 1);
+         : EPI == EPI_RELU_ROPE                  ? 3
+         : (EPI == EPI_GATE || EPI == EPI_DQ)    ? 4
+         : EPI == EPI_DEC_BWD                    ? 2
+                                                 : 1;
 }
 
 template <int BN, int KIND = 0>
@@ -90,14 +95,14 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = KIND >= 2 ? 3
+  static constexpr int STAGES = KIND == 4 ? 4 : KIND >= 2 ? 3
                                : (STAGED ? ((BN == 256) ? 3 : (BN == 128 ? 4 : 5))
                                          : ((BN == 256) ? 4 : (BN == 128 ? 6 : 8)));
   // epilogue warps: kind 3 runs 16 (four per TMEM lane quadrant, 32 columns each),
   // the others 8 (two per quadrant, 64 columns each)
   static constexpr int NEPI = KIND == 3 ? 16 : 8;
   // kinds 2 / 3: warps x 2 tile buffers x 2 tensors x (32 rows x columns-per-warp bf16)
-  static constexpr int EPI_BYTES = KIND >= 2 ? 128 * 1024 : (STAGED ? 8 * 2 * 4096 : 0);
+  static constexpr int EPI_BYTES = KIND == 4 ? 96 * 1024 : KIND >= 2 ? 128 * 1024 : (STAGED ? 8 * 2 * 4096 : 0);
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int THREADS = 64 + 32 * NEPI;
@@ -206,35 +211,6 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const TileCo
       load_bf16x32(e.aux0 + off, xv);
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i] - e.thr, 0.0f) * xv[i];
-    } else if constexpr (EPI == EPI_DEC_BWD) {
-      float xv[32], yv[32], dy[32];
-      load_bf16x32(e.aux0 + off, xv);
-      load_bf16x32(e.aux1 + off, yv);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float g = v[i];
-        const float y = (xv[i] > 0.0f) ? __fdividef(yv[i], xv[i]) : 0.0f;
-        dy[i] = (yv[i] > 0.0f) ? g * xv[i] : 0.0f;
-        v[i] = g * y;
-      }
-      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(e.out1) + off, dy);
-    } else if constexpr (EPI == EPI_DQ) {
-      float base[32], xv[32];
-      load_bf16x32(e.aux0 + off, base);
-      load_bf16x32(e.aux1 + off, xv);
-      if (e.freq) {
-        const float pos = (float)(e.pos0 + row);
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float c, s;
-          rope_cs(pos, e.freq[col + i], c, s);
-          const float ge = v[i], go = v[i + 1];
-          v[i] = ge * c + go * s;
-          v[i + 1] = go * c - ge * s;
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = (xv[i] > 0.0f) ? (v[i] + base[i]) : 0.0f;
     }
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(e.out0) + off;
     store_bf16x32(o, v);

@@ -20,7 +20,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_flag;
-  __shared__ uint64_t aux_bar[16][2];
+  __shared__ uint64_t aux_bar[16][3];
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -43,6 +43,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
     for (int w = 0; w < Cfg::NEPI; ++w) {
       mbar_init(&aux_bar[w][0], 1);
       mbar_init(&aux_bar[w][1], 1);
+      mbar_init(&aux_bar[w][2], 1);
     }
     fence_barrier_init();
     tma_prefetch_desc(&p.ta);
@@ -175,11 +176,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
       constexpr int NAUX = epi_naux<EPI>();
       constexpr int CW = KIND == 3 ? 32 : 64;
       constexpr int kTmaTileBytes = 32 * CW * 2;
-      uint8_t* wbuf = sEpi + ew * 4 * kTmaTileBytes;  // [tile parity][tensor] tiles
+      constexpr int NBUF = KIND == 4 ? 3 : 2;  // ring of tile buffers
+      constexpr int TENS = KIND == 4 ? 1 : 2;  // tensors per buffer
+      uint8_t* wbuf = sEpi + ew * NBUF * TENS * kTmaTileBytes;  // [buffer][tensor] tiles
       const int col_off = half * CW;
       // Per-buffer issue / wait counters keep the mbarrier parities exact (uniform
       // across the warp; only lane 0 issues).
-      int n_issued[2] = {0, 0}, n_waited[2] = {0, 0};
+      int n_issued[3] = {0, 0, 0}, n_waited[3] = {0, 0, 0};
       auto issue_aux = [&](int t, int b) {
         if constexpr (NAUX > 0) {
           if (t >= total) return;
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
           if (n.zero) return;
           ++n_issued[b];
           if (lane != 0) return;
-          uint8_t* dst = wbuf + b * 2 * kTmaTileBytes;
+          uint8_t* dst = wbuf + b * TENS * kTmaTileBytes;
           fence_proxy_async_smem();
           mbar_arrive_expect_tx(&aux_bar[ew][b], NAUX * kTmaTileBytes);
           tma_load_4d(dst, &p.tx0, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1, n.z2);
@@ -202,13 +205,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
       int it = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
         const TileCoord tc = decode_tile(p, t, BN);
-        const int b = it & 1;
-        uint8_t* b0 = wbuf + b * 2 * kTmaTileBytes;
-        uint8_t* b1 = b0 + kTmaTileBytes;
-        // the other buffer was last read by this warp's stores of the previous tile
-        if (lane == 0) bulk_wait_group_read0();
+        const int b = it % NBUF;
+        const int bn = (it + 1) % NBUF;
+        uint8_t* b0 = wbuf + b * TENS * kTmaTileBytes;
+        uint8_t* b1 = TENS > 1 ? b0 + kTmaTileBytes : b0;
+        // the next buffer was last read by this warp's stores NBUF - 1 tiles ago
+        if (lane == 0) {
+          if constexpr (NBUF == 3)
+            bulk_wait_group_read1();
+          else
+            bulk_wait_group_read0();
+        }
         __syncwarp();
-        issue_aux(t + gridDim.x, b ^ 1);
+        issue_aux(t + gridDim.x, bn);
         if (tc.zero) continue;  // (no zero tiles in these modes unless K is empty)
         if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
         tc_fence_after();
@@ -243,7 +252,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
         bulk_wait_group0();
         // On an abort, loads may still be landing in smem: wait for them (bounded).
         int dummy_abort = 0;
-        for (int b = 0; b < 2; ++b)
+        for (int b = 0; b < NBUF; ++b)
           while (n_waited[b] < n_issued[b]) {
             mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, (volatile int*)&dummy_abort, p.err, kErrTimeoutDrain);
             ++n_waited[b];

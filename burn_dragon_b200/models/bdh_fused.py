@@ -331,14 +331,15 @@ class FusedBDH:
             G.gemm(G.EPI_F32, dcop, Operand(v16, False, D, T, D, z2=(B, T * D)), T, T, D, ws.P32, Z1=H, Z2=B,
                    bn=128 if T % 128 == 0 else 64, ld=T, sz1=T * T, sz2=H * T * T)
             mod.symmetrize(ws.P32, ws.G16, B * H, T, H, ws.log2_decay)
-            # dx_pre = (dx_part + rope^T(G q)) * [x > 0]   (in place over dx_part)
+            # dx_pre = (dx_part + rope^T(G q)) * [x > 0]   (in place over dx_part, which
+            # carries the x <= 0 mask as -0.0 from the decoder backward)
             G.gemm(G.EPI_DQ, Operand(ws.G16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
                    Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B, bn=128,
-                   aux0=ws.dx16, aux1=ws.x16[l], ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh)
+                   aux0=ws.dx16, ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh)
             if ws.has_rho0:
                 # + rope^T(gamma^t dC rho0^T) (the carried state is detached: no grad to rho0)
                 G.gemm(G.EPI_DQ, dcop, Operand(ws.rho16[l], False, D, Nh, D, z1=(H, Nh * D), z2=(B, H * Nh * D)),
-                       T, Nh, D, ws.dx16, Z1=H, Z2=B, bn=128, aux0=ws.dx16, aux1=ws.x16[l], ld=N, sz1=Nh,
+                       T, Nh, D, ws.dx16, Z1=H, Z2=B, bn=128, aux0=ws.dx16, ld=N, sz1=Nh,
                        sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh, log2_decay=ws.log2_decay,
                        row_decay=ws.log2_decay is not None)
             # dV = sum_h S_h^T dC_h  (K = (h, i))

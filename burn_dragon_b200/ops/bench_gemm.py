@@ -49,11 +49,11 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
                               M, N, D, dx, bn=128, out1=dy, aux0=x, aux1=yn, ld=N)
         return call, 2 * M * N * D, (M * D + N * D + 4 * M * N) * 2
     if case == "dq":
-        g16, q, dx, x = r(B, H, T, T), r(M, N), r(M, N), r(M, N)
+        g16, q, dx = r(B, H, T, T), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_DQ, Operand(g16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),  # noqa: E731
                               Operand(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B, bn=128,
-                              aux0=dx, aux1=x, ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh)
-        return call, 2 * B * H * T * T * Nh, (B * H * T * T + 4 * M * N) * 2
+                              aux0=dx, ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh)
+        return call, 2 * B * H * T * T * Nh, (B * H * T * T + 3 * M * N) * 2
     if case == "wgrad":
         a, dy, out = r(M, D), r(M, N), torch.zeros(H, D, Nh, device=dev)
         call = lambda: G.gemm(G.EPI_F32, Operand(a, True, D, M, D), Operand(dy, True, Nh, M, N, z1=(H, Nh)),  # noqa: E731
