@@ -254,6 +254,30 @@ __device__ __forceinline__ void epilogue_zero_chunk(const GemmParams& p, const T
 
 }  // namespace bd
 
+namespace bd {
+
+// Tile of a CTA pair: rows [m0, m0 + 256); the caller adds 128 * cta_rank.
+__device__ __forceinline__ TileCoord decode_tile_pair(const GemmParams& p, int t, int BN) {
+  TileCoord c;
+  int n_blk = t % p.tiles_n;
+  int r = t / p.tiles_n;
+  int m_blk = r % p.tiles_m;
+  r /= p.tiles_m;
+  c.split = r % p.splits;
+  r /= p.splits;
+  c.z1 = r % p.Z1;
+  c.z2 = r / p.Z1;
+  c.m0 = m_blk * 256;
+  c.n0 = n_blk * BN;
+  const int KB = (p.K + 63) / 64;
+  c.kb0 = c.split * p.kb_per_split;
+  c.kb1 = min(c.kb0 + p.kb_per_split, KB);
+  c.zero = (p.causal_skip && c.n0 >= c.m0 + 256) || (c.kb1 <= c.kb0);
+  return c;
+}
+
+}  // namespace bd
+
 #include "gemm_epilogue_staged.cuh"
 #include "gemm_epilogue_tma.cuh"
 #include "gemm_sm100_kernel.cuh"

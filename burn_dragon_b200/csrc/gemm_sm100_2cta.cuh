@@ -12,8 +12,13 @@
 //   leader     warp 1     TMEM (pair allocation) + single-thread MMA issuer; commits
 //                         multicast to both CTAs' empty / tmem-full barriers
 //   both CTAs  warps 2-9  epilogue on their own 128 rows; release the accumulator on
-//                         the leader's tmem-empty barrier (16 arrivals: 8 local, 8 remote)
-// Epilogue kinds 0 (fp32) and 1 (staged bf16) only. Bounded waits as in the 1-CTA kernel.
+//                         the leader's tmem-empty barrier (one arrival per epilogue warp of both CTAs)
+// All epilogue kinds: fp32, staged bf16 and the TMA epilogues (each CTA runs the same
+// per-warp TMA epilogue loop as the 1-CTA kernel on its own 128 rows). The TMA-epilogue
+// modes are not instantiated on pairs: measured at BDH-GPU batch 32 they ran 25-45%
+// slower than the 1-CTA kernel (the pair couples two CTAs' epilogues through the shared
+// accumulator release, and these modes are bound by the epilogue, not operand bytes).
+// Bounded waits as in the 1-CTA kernel.
 #pragma once
 
 namespace bd {
@@ -23,37 +28,23 @@ struct Gemm2Cfg {
   static constexpr int A_BYTES = 128 * 64 * 2;
   static constexpr int B_BYTES = (BN / 2) * 64 * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = KIND == 1 ? (BN == 256 ? 5 : 6) : (BN == 256 ? 6 : 8);
-  static constexpr int EPI_BYTES = KIND == 1 ? 8 * 2 * 4096 : 0;
+  // TMA-epilogue kinds: the 1-CTA kernel's warp counts and tile buffers (GemmCfg)
+  static constexpr int NEPI = GemmCfg<BN, KIND>::NEPI;
+  static constexpr int EPI_BYTES = KIND >= 2 ? GemmCfg<BN, KIND>::EPI_BYTES : (KIND == 1 ? 8 * 2 * 4096 : 0);
+  static constexpr int STAGES = KIND == 4   ? 5
+                                : KIND >= 2 ? 4
+                                : KIND == 1 ? (BN == 256 ? 5 : 6)
+                                            : (BN == 256 ? 6 : 8);
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 64 + 32 * NEPI;
 };
 
-// Tile of a CTA pair: rows [m0, m0 + 256); the caller adds 128 * cta_rank.
-__device__ __forceinline__ TileCoord decode_tile_pair(const GemmParams& p, int t, int BN) {
-  TileCoord c;
-  int n_blk = t % p.tiles_n;
-  int r = t / p.tiles_n;
-  int m_blk = r % p.tiles_m;
-  r /= p.tiles_m;
-  c.split = r % p.splits;
-  r /= p.splits;
-  c.z1 = r % p.Z1;
-  c.z2 = r / p.Z1;
-  c.m0 = m_blk * 256;
-  c.n0 = n_blk * BN;
-  const int KB = (p.K + 63) / 64;
-  c.kb0 = c.split * p.kb_per_split;
-  c.kb1 = min(c.kb0 + p.kb_per_split, KB);
-  c.zero = (p.causal_skip && c.n0 >= c.m0 + 256) || (c.kb1 <= c.kb0);
-  return c;
-}
-
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(320, 1) gemm_sm100_2cta_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(Gemm2Cfg<BN, epi_kind<EPI>()>::THREADS, 1)
+    gemm_sm100_2cta_kernel(const __grid_constant__ GemmParams p) {
   constexpr int KIND = epi_kind<EPI>();
-  static_assert(KIND < 2, "the pair kernel serves the fp32 and staged-bf16 epilogues");
+  static_assert(KIND < 2 || BN == 128, "the TMA epilogue is built for tile N = 128");
   constexpr bool STAGED = KIND == 1;
   using Cfg = Gemm2Cfg<BN, KIND>;
   constexpr int STAGES = Cfg::STAGES;
@@ -66,6 +57,7 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_2cta_kernel(const __grid_co
   __shared__ uint64_t drain_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ volatile int abort_flag;
+  __shared__ uint64_t aux_bar[16][3];
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -84,9 +76,11 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_2cta_kernel(const __grid_co
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 16);
+      mbar_init(&tempty_bar[a], 2 * Cfg::NEPI);
     }
     mbar_init(&drain_bar, 1);
+    for (int w = 0; w < Cfg::NEPI; ++w)
+      for (int b = 0; b < 3; ++b) mbar_init(&aux_bar[w][b], 1);
     fence_barrier_init();
     tma_prefetch_desc(&p.ta);
     tma_prefetch_desc(&p.tb);
@@ -210,6 +204,11 @@ __global__ void __launch_bounds__(320, 1) gemm_sm100_2cta_kernel(const __grid_co
       int dummy_abort = 0;
       mbar_wait_bounded(&drain_bar, 0, (volatile int*)&dummy_abort, p.err, kErrTimeoutDrain);
     }
+  } else if constexpr (KIND >= 2) {
+    // ------------------------------------------------ TMA epilogue (both CTAs, own 128 rows)
+    tma_epilogue_loop<BN, EPI, KIND, true>(p, total, cluster_id, n_clusters, 128 * (int)crank, sEpi, aux_bar,
+                                           tfull_bar, tempty_bar, map_to_cta(&tempty_bar[0], 0),
+                                           map_to_cta(&tempty_bar[1], 0), leader, tmem_base, &abort_flag, warp, lane);
   } else {
     // ------------------------------------------------ epilogue (both CTAs, own 128 rows)
     const int ew = warp - 2;

@@ -172,93 +172,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
     const int half = ew >> 2;   // column group of the tile
     const int r_local = quad * 32 + lane;
     if constexpr (KIND >= 2) {
-      // ---------------- TMA epilogue (see gemm_epilogue_tma.cuh): 32 rows x CW columns
-      constexpr int NAUX = epi_naux<EPI>();
-      constexpr int CW = KIND == 3 ? 32 : 64;
-      constexpr int kTmaTileBytes = 32 * CW * 2;
-      constexpr int NBUF = KIND == 4 ? 3 : 2;  // ring of tile buffers
-      constexpr int TENS = KIND == 4 ? 1 : 2;  // tensors per buffer
-      uint8_t* wbuf = sEpi + ew * NBUF * TENS * kTmaTileBytes;  // [buffer][tensor] tiles
-      const int col_off = half * CW;
-      // Per-buffer issue / wait counters keep the mbarrier parities exact (uniform
-      // across the warp; only lane 0 issues).
-      int n_issued[3] = {0, 0, 0}, n_waited[3] = {0, 0, 0};
-      auto issue_aux = [&](int t, int b) {
-        if constexpr (NAUX > 0) {
-          if (t >= total) return;
-          const TileCoord n = decode_tile(p, t, BN);
-          if (n.zero) return;
-          ++n_issued[b];
-          if (lane != 0) return;
-          uint8_t* dst = wbuf + b * TENS * kTmaTileBytes;
-          fence_proxy_async_smem();
-          mbar_arrive_expect_tx(&aux_bar[ew][b], NAUX * kTmaTileBytes);
-          tma_load_4d(dst, &p.tx0, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1, n.z2);
-          if constexpr (NAUX > 1)
-            tma_load_4d(dst + kTmaTileBytes, &p.tx1, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1,
-                        n.z2);
-        }
-      };
-      issue_aux(blockIdx.x, 0);
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      int it = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
-        const TileCoord tc = decode_tile(p, t, BN);
-        const int b = it % NBUF;
-        const int bn = (it + 1) % NBUF;
-        uint8_t* b0 = wbuf + b * TENS * kTmaTileBytes;
-        uint8_t* b1 = TENS > 1 ? b0 + kTmaTileBytes : b0;
-        // the next buffer was last read by this warp's stores NBUF - 1 tiles ago
-        if (lane == 0) {
-          if constexpr (NBUF == 3)
-            bulk_wait_group_read1();
-          else
-            bulk_wait_group_read0();
-        }
-        __syncwarp();
-        issue_aux(t + gridDim.x, bn);
-        if (tc.zero) continue;  // (no zero tiles in these modes unless K is empty)
-        if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
-        tc_fence_after();
-        float v[CW];
-        if constexpr (CW == 32)
-          tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
-        else
-          tmem_ld64(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1;
-        }
-        if constexpr (NAUX > 0) {
-          if (!mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, &abort_flag, p.err, kErrTimeoutEpilogue)) break;
-          ++n_waited[b];
-        }
-        tma_epi_math<EPI, CW>(p, tc, v, tc.m0 + r_local, tc.n0 + col_off, b0, b1, lane);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          const int c0 = tc.n0 + col_off, c1 = tc.m0 + quad * 32;
-          tma_store_4d(&p.to0, b0, c0, c1, tc.z1, tc.z2);
-          if (EPI == EPI_DEC_BWD || (EPI == EPI_RELU_ROPE && p.e.freq != nullptr))
-            tma_store_4d(&p.to1, b1, c0, c1, tc.z1, tc.z2);
-          bulk_commit_group();
-        }
-      }
-      if (lane == 0) {
-        bulk_wait_group0();
-        // On an abort, loads may still be landing in smem: wait for them (bounded).
-        int dummy_abort = 0;
-        for (int b = 0; b < NBUF; ++b)
-          while (n_waited[b] < n_issued[b]) {
-            mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, (volatile int*)&dummy_abort, p.err, kErrTimeoutDrain);
-            ++n_waited[b];
-          }
-      }
-      __syncwarp();
+      tma_epilogue_loop<BN, EPI, KIND, false>(p, total, blockIdx.x, gridDim.x, 0, sEpi, aux_bar, tfull_bar,
+                                              tempty_bar, 0u, 0u, true, tmem_base, &abort_flag, warp, lane);
     } else {
     uint8_t* buf0 = sEpi + ew * 2 * kStageTileBytes;
     uint8_t* buf1 = buf0 + kStageTileBytes;
