@@ -82,12 +82,24 @@ class Generator:
         dev = prompt.device
         fused_ok = dev.type == "cuda" and self.cfg.dropout == 0.0 and not self.cfg.tie_input_output_embeddings
         chunk = self.prefill_chunk if fused_ok else T
-        if fused_ok and (T % chunk or chunk % 128):
-            chunk = T if T % 128 == 0 else 0
-        if not fused_ok or chunk == 0:
-            logits = self.model(prompt, state=state)
-            state.detach_in_place()
-            return logits[:, -1].float(), state
+        main = (T // 128) * 128 if fused_ok else 0
+        if fused_ok and 0 < main < T:
+            # the fused prefill takes whole 128-token blocks; the tail runs as decode steps
+            logits, state = self.prefill(prompt[:, :main], state)
+            for t in range(main, T):
+                logits = self.decode_step(prompt[:, t].contiguous(), state)
+            return logits, state
+        if fused_ok and main:
+            chunk = math.gcd(main, chunk) if chunk % 128 == 0 else 128
+        if not fused_ok or main == 0:
+            if not fused_ok:
+                logits = self.model(prompt, state=state)
+                state.detach_in_place()
+                return logits[:, -1].float(), state
+            logits = None
+            for t in range(T):
+                logits = self.decode_step(prompt[:, t].contiguous(), state)
+            return logits, state
         from .bdh_fused import FusedBDH, FusedWorkspace
 
         if self._pws is None or self._pws.B != B or self._pws.T != chunk:
@@ -151,6 +163,106 @@ class Generator:
                w.logits, ld=V)
         state.position += 1
         return w.logits
+
+    # ---------------------------------------------------------------- ragged batches
+    @torch.no_grad()
+    def generate_ragged(self, prompts: list[list[int]], max_new_tokens: list[int], stop_token: int | None = None,
+                        device_buffer_tokens: int = 64, device=None) -> list[list[int]]:
+        """Exact greedy continuations of prompts of different lengths in one batch
+        (burn_dragon_language/src/generation.rs:296-560): every row advances at the same
+        absolute position; a row still inside its prompt consumes its next prompt token,
+        a finished one its argmax. Tokens stay on the device for ``device_buffer_tokens``
+        steps; the host then applies budgets and the stop token (kept in the output)
+        and drops finished rows from the batch (the recurrent state is row-separable)."""
+        if len(prompts) != len(max_new_tokens):
+            raise ValueError("one token budget per prompt")
+        if any(len(p) == 0 for p in prompts):
+            raise ValueError("prompts must be non-empty")
+        dev = torch.device(device) if device is not None else self.model.store.data.device
+        out: list[list[int]] = [[] for _ in prompts]
+        rows = [r for r, b in enumerate(max_new_tokens) if b > 0]
+        if not rows:
+            return out
+        lens = torch.tensor([len(prompts[r]) for r in rows], device=dev)
+        width = int(lens.max())
+        table = torch.zeros(len(rows), width, dtype=torch.long, device=dev)
+        for i, r in enumerate(rows):
+            table[i, :len(prompts[r])] = torch.tensor(prompts[r], device=dev)
+        shared = int(lens.min())
+        logits, state = self.prefill(table[:, :shared].contiguous())
+        nbuf = max(1, device_buffer_tokens)
+        while rows:
+            toks = torch.empty(len(rows), nbuf, dtype=torch.long, device=dev)
+            gen = torch.empty(len(rows), nbuf, dtype=torch.bool, device=dev)
+            for k in range(nbuf):
+                pos = state.position
+                in_prompt = lens > pos
+                prompt_tok = table[:, min(pos, width - 1)]
+                nxt = torch.where(in_prompt, prompt_tok, logits.argmax(-1))
+                toks[:, k] = nxt
+                gen[:, k] = ~in_prompt
+                logits = self.decode_step(nxt.contiguous(), state)
+            host_t, host_g = toks.cpu().tolist(), gen.cpu().tolist()
+            keep = []
+            for i, r in enumerate(rows):
+                stopped = False
+                for t, g in zip(host_t[i], host_g[i]):
+                    if not g or len(out[r]) >= max_new_tokens[r]:
+                        continue
+                    out[r].append(t)
+                    if stop_token is not None and t == stop_token:
+                        stopped = True
+                        break
+                if not stopped and len(out[r]) < max_new_tokens[r]:
+                    keep.append(i)
+            if len(keep) < len(rows):
+                idx = torch.tensor(keep, device=dev, dtype=torch.long)
+                rows = [rows[i] for i in keep]
+                if not rows:
+                    break
+                state.rhos = [r_.index_select(0, idx).contiguous() for r_ in state.rhos]
+                lens, table, logits = lens[idx], table[idx], logits[idx]
+        return out
+
+    # ---------------------------------------------------------------- streaming
+    @torch.no_grad()
+    def generate_stream(self, prompt: list[int], max_new_tokens: int, chunk_tokens: int = 16,
+                        temperature: float = 0.0, top_k: int | None = None, stop_token: int | None = None,
+                        sliding_window: int | None = None, on_chunk=None, seed: int | None = None,
+                        device=None) -> list[int]:
+        """One sequence, tokens handed to ``on_chunk`` every ``chunk_tokens`` steps
+        (generation.rs:1174-1275). ``sliding_window`` keeps only the last ``window``
+        prompt tokens (the recurrent state needs no trimming afterwards)."""
+        dev = torch.device(device) if device is not None else self.model.store.data.device
+        if sliding_window and len(prompt) > sliding_window:
+            prompt = prompt[-sliding_window:]
+        gen = None
+        if seed is not None:
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(seed)
+        logits, state = self.prefill(torch.tensor([prompt], device=dev))
+        full = list(prompt)
+        pending = []
+        done = 0
+        while done < max_new_tokens:
+            nxt = sample_next(logits, temperature, top_k, gen)
+            pending.append(nxt)
+            done += 1
+            if done < max_new_tokens:
+                logits = self.decode_step(nxt.contiguous(), state)
+            if len(pending) >= chunk_tokens or done == max_new_tokens:
+                chunk = torch.cat(pending).cpu().tolist()
+                pending.clear()
+                if stop_token is not None and stop_token in chunk:
+                    chunk = chunk[:chunk.index(stop_token) + 1]
+                    full.extend(chunk)
+                    if on_chunk:
+                        on_chunk(chunk)
+                    break
+                full.extend(chunk)
+                if on_chunk:
+                    on_chunk(chunk)
+        return full
 
     # ---------------------------------------------------------------- loop
     @torch.no_grad()

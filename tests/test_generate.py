@@ -85,3 +85,66 @@ def test_gpu_prefill_and_decode_match_reference(rotary):
     for i in range(T, T + 4):
         logits = g.decode_step(toks[:, i], st)
         assert rel(logits, full[:, i]) < 0.03, i
+
+
+def test_ragged_batch_matches_serial_greedy():
+    import torch
+
+    from burn_dragon_b200.config import DragonConfig
+    from burn_dragon_b200.models.bdh import BDH
+    from burn_dragon_b200.models.generate import Generator
+
+    cfg = DragonConfig(n_layer=2, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0,
+                       rotary_embedding="rope", initialization="simple_normal", vocab_size=64)
+    m = BDH(cfg, seed=0)
+    g = Generator(m)
+    prompts = [[1, 2, 3], [4, 5, 6, 7, 8, 9], [10], [11, 12]]
+    budgets = [5, 3, 0, 7]
+    out = g.generate_ragged(prompts, budgets, device_buffer_tokens=4, device="cpu")
+    for p, b, o in zip(prompts, budgets, out):
+        if b == 0:
+            assert o == []
+            continue
+        ref = g.generate(torch.tensor([p]), b)[0].tolist()
+        assert o == ref
+    # a stop token ends a row early (and is kept)
+    first = out[0][1]
+    stopped = g.generate_ragged([prompts[0]], [5], stop_token=first, device="cpu")[0]
+    assert stopped == out[0][:2]
+
+
+def test_stream_chunks_and_sliding_window():
+    import torch
+
+    from burn_dragon_b200.config import DragonConfig
+    from burn_dragon_b200.models.bdh import BDH
+    from burn_dragon_b200.models.generate import Generator
+
+    cfg = DragonConfig(n_layer=1, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0,
+                       rotary_embedding="rope", initialization="simple_normal", vocab_size=64)
+    g = Generator(BDH(cfg, seed=1))
+    chunks = []
+    full = g.generate_stream([1, 2, 3, 4, 5], 7, chunk_tokens=3, on_chunk=chunks.append, device="cpu")
+    assert [len(c) for c in chunks] == [3, 3, 1] and full[5:] == sum(chunks, [])
+    ref = g.generate(torch.tensor([[1, 2, 3, 4, 5]]), 7)[0].tolist()
+    assert full[5:] == ref
+    win = g.generate_stream([9, 9, 1, 2, 3, 4, 5], 7, sliding_window=5, device="cpu")
+    assert win == full
+
+
+@pytest.mark.gpu
+def test_ragged_batch_on_cuda_matches_serial():
+    import torch
+
+    from burn_dragon_b200.config import DragonConfig
+    from burn_dragon_b200.models.bdh import BDH
+    from burn_dragon_b200.models.generate import Generator
+
+    cfg = DragonConfig(n_layer=2, n_embd=64, n_head=2, mlp_internal_dim_multiplier=16, dropout=0.0,
+                       rotary_embedding="rope", initialization="simple_normal", vocab_size=256)
+    g = Generator(BDH(cfg, device="cuda", seed=0), prefill_chunk=128)
+    gen = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, 256, (n,), generator=gen).tolist() for n in (130, 256, 7)]
+    out = g.generate_ragged(prompts, [6, 4, 9], device_buffer_tokens=4)
+    for p, b, o in zip(prompts, [6, 4, 9], out):
+        assert o == g.generate(torch.tensor([p], device="cuda"), b)[0].tolist()
