@@ -490,6 +490,8 @@ class TrainingSection:
     continual_backprop: ContinualBackpropConfig = field(default_factory=ContinualBackpropConfig)
     auto_batch_size: AutoBatchSizeConfig = field(default_factory=AutoBatchSizeConfig)
     target_effective_batch_size: int | None = None
+    # initialise the weights from this run directory's newest checkpoint (a fresh run only)
+    init_checkpoint_path: str | None = None
     # auto | backpropagation | predictive_coding | eggroll (schema.rs:569-577)
     algorithm: str = "auto"
     local_predictive_coding: LocalPredictiveCodingConfig = field(default_factory=LocalPredictiveCodingConfig)

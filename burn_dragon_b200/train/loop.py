@@ -143,6 +143,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         rt = info.get("runtime")
         if rt and rt.get("rhos") is not None and not extended:
             state = ModelState(rt["rhos"], int(rt.get("position", 0)))
+    if start == 0 and t.init_checkpoint_path:
+        src = C.RunDir(t.init_checkpoint_path)
+        src.load(None, trainer.core if extended else trainer.model, None, device=dev)
     streaming = t.sequence_batching == "streaming" or t.tbptt_persist_across_steps
     data_rank = 0 if mode in ("tensor_parallel_neuron", "pipeline") else rank
     data_world = 1 if mode in ("tensor_parallel_neuron", "pipeline") else world
