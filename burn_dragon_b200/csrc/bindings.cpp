@@ -11,7 +11,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           const c10::optional<at::Tensor>& aux1, int64_t ld, int64_t sz1, int64_t sz2, int64_t split_stride,
           double alpha, double thr, const c10::optional<at::Tensor>& freq,
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh, bool accumulate,
-          bool row_decay, int64_t pair, const at::Tensor& err);
+          bool row_decay, int64_t pair, const at::Tensor& err, const c10::optional<std::vector<int64_t>>& scatter);
 void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_t rows, int64_t D,
             const at::Tensor& gamma, const at::Tensor& beta, double eps, const c10::optional<at::Tensor>& y32,
             const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd);
@@ -58,6 +58,8 @@ void reduce_adamw(std::vector<int64_t> grad, std::vector<int64_t> param, std::ve
                   std::vector<int64_t> flags, int64_t rank, int64_t lo, int64_t hi, const at::Tensor& m,
                   const at::Tensor& v, double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
                   const c10::optional<at::Tensor>& hyper);
+void tp_reduce_gather(const at::Tensor& slots, std::vector<int64_t> dst, int64_t rank, int64_t rows, int64_t M,
+                      int64_t D, int64_t slot_stride);
 void reduce_mean(std::vector<int64_t> grad, std::vector<int64_t> flags, int64_t rank, int64_t lo, int64_t hi,
                  const at::Tensor& err);
 void percentile_thresholds(const at::Tensor& values, double q, const at::Tensor& out);
@@ -88,5 +90,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &bd::peer_barrier);
   m.def("reduce_adamw", &bd::reduce_adamw);
   m.def("reduce_mean", &bd::reduce_mean);
+  m.def("tp_reduce_gather", &bd::tp_reduce_gather);
   m.def("percentile_thresholds", &bd::percentile_thresholds);
 }

@@ -21,6 +21,7 @@
 #include <cuda_bf16.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <vector>
 
 namespace bd {
@@ -156,6 +157,35 @@ __global__ void reduce_mean_kernel(PeerPtrs pp, int rank, int world, long long l
   }
 }
 
+// Tensor-parallel sum, second half: every rank's GEMM epilogue stored its partial rows
+// of owner o into o's slot buffer (slot s = source rank, [rows, D] each). The owner
+// sums its W slots and stores the total into every rank's destination rows (an
+// all-gather by P2P stores).
+struct DstPtrs {
+  float* dst[kMaxRanks];
+};
+
+__global__ void tp_reduce_gather_kernel(const float* __restrict__ slots, DstPtrs dp, int world, int rank,
+                                        long long rows, long long valid_rows, int D, long long slot_stride) {
+  const long long n4 = valid_rows * D / 4;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const long long e = 4 * i;
+    float4 acc = *reinterpret_cast<const float4*>(slots + e);
+    for (int s = 1; s < world; ++s) {
+      const float4 x = *reinterpret_cast<const float4*>(slots + s * slot_stride + e);
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    const long long o = rank * rows * D + e;
+    for (int r = 0; r < world; ++r) {
+      const int t = (rank + r) % world;  // stagger the destinations
+      *reinterpret_cast<float4*>(dp.dst[t] + o) = acc;
+    }
+  }
+}
+
 PeerPtrs make_ptrs(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
                    const std::vector<int64_t>& shadow, const std::vector<int64_t>& flags) {
   PeerPtrs pp;
@@ -241,6 +271,21 @@ void reduce_adamw(std::vector<int64_t> grad, std::vector<int64_t> param, std::ve
                                                (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1,
                                                (float)bc2, hyper ? hyper->data_ptr<float>() : nullptr,
                                                1.0f / (float)world);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void tp_reduce_gather(const at::Tensor& slots, std::vector<int64_t> dst, int64_t rank, int64_t rows, int64_t M,
+                      int64_t D, int64_t slot_stride) {
+  const int world = (int)dst.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks, "1..8 ranks");
+  TORCH_CHECK(slots.scalar_type() == at::kFloat && slots.is_contiguous() && D % 4 == 0, "fp32 slots, D % 4 == 0");
+  DstPtrs dp;
+  memset(&dp, 0, sizeof(dp));
+  for (int r = 0; r < world; ++r) dp.dst[r] = reinterpret_cast<float*>(dst[r]);
+  const long long valid = std::max<long long>(0, std::min<long long>(rows, M - rank * rows));
+  auto st = at::cuda::getCurrentCUDAStream(slots.get_device()).stream();
+  tp_reduce_gather_kernel<<<148 * 2, 256, 0, st>>>(slots.data_ptr<float>(), dp, world, (int)rank, rows, valid,
+                                                   (int)D, slot_stride);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

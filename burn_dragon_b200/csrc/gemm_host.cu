@@ -126,7 +126,8 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           const c10::optional<at::Tensor>& aux1, int64_t ld, int64_t sz1, int64_t sz2, int64_t split_stride,
           double alpha, double thr, const c10::optional<at::Tensor>& freq,
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh,
-          bool accumulate, bool row_decay, int64_t pair, const at::Tensor& err) {
+          bool accumulate, bool row_decay, int64_t pair, const at::Tensor& err,
+          const c10::optional<std::vector<int64_t>>& scatter) {
   // pair: 0 = 1-CTA kernel, 1 = CTA-pair kernel when instantiated and M >= 256
   const Entry* hit = nullptr;
   if (pair && M >= 256) hit = find_entry((int)bn, a_mn, b_mn, (int)epi, true);
@@ -186,7 +187,22 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   e.accumulate = accumulate ? 1 : 0;
   e.row_decay = row_decay ? 1 : 0;
   if (row_decay) TORCH_CHECK(e.log2_decay != nullptr, "row_decay needs log2_decay");
-  if (epi == EPI_F32) {
+  if (epi == EPI_F32_SCATTER) {
+    // scatter = [world, rows per owner, this rank, slot stride (elements), slot pointer per rank]
+    TORCH_CHECK(scatter && scatter->size() >= 5, "EPI_F32_SCATTER needs the scatter description");
+    const auto& sc = *scatter;
+    const int64_t W = sc[0];
+    TORCH_CHECK(W >= 1 && W <= 8 && (int64_t)sc.size() == 4 + W, "scatter: world in [1, 8], one pointer per rank");
+    TORCH_CHECK(sc[1] > 0 && sc[1] * W >= M && Z1 == 1 && Z2 == 1 && splits == 1 && !causal_skip && !accumulate,
+                "scatter: plain 2-D GEMM, rows covered by the owners");
+    e.scatter_rows = (int)sc[1];
+    e.scatter_rank = (int)sc[2];
+    e.slot_stride = sc[3];
+    for (int64_t r = 0; r < W; ++r) {
+      e.peer[r] = reinterpret_cast<float*>(sc[4 + r]);
+      TORCH_CHECK(sc[4 + r] % 16 == 0, "scatter slots must be 16-byte aligned");
+    }
+  } else if (epi == EPI_F32) {
     TORCH_CHECK(out0.scalar_type() == at::kFloat, "EPI_F32 output must be fp32");
   } else {
     TORCH_CHECK(out0.scalar_type() == at::kBFloat16, "bf16 epilogue output must be bf16");

@@ -34,6 +34,8 @@ enum EpiMode : int {
   EPI_DEC_BWD = 5,    // acc = d(yn): dx_part -> out0, dy_pre -> out1 (aux0 = x, aux1 = yn);
                       // dx_part carries the x <= 0 mask as -0.0
   EPI_DQ = 6,         // acc = d(q): dx_pre = (aux0 + rope^T(acc)), masked by aux0's -0.0 -> out0
+  EPI_F32_SCATTER = 7,  // fp32 rows stored straight into their owner rank's slot over NVLink
+                        // (the reduce-scatter half of a tensor-parallel sum, fused into the GEMM)
 };
 
 struct EpiParams {
@@ -53,6 +55,13 @@ struct EpiParams {
   int Nh;                  // latent per head (column -> in-head index for RoPE)
   int accumulate;          // EPI_F32: add into the existing output
   int row_decay;           // EPI_F32 / EPI_DQ: scale row r by 2^(r * log2_decay[z1])
+  // EPI_F32_SCATTER: row r belongs to rank r / scatter_rows; it is stored at
+  // peer[owner] + scatter_rank * slot_stride + (r % scatter_rows) * ld + col, where
+  // peer[] are the (IPC-mapped) slot buffers of every rank. Plain st.global over NVLink.
+  float* peer[8];
+  int scatter_rows;
+  int scatter_rank;
+  long long slot_stride;
 };
 
 struct alignas(64) GemmParams {
@@ -80,7 +89,7 @@ constexpr int epi_kind() {
   // x-projection, where more concurrent warps beat wider boxes); 4: TMA epilogue,
   // 8 warps x 64 columns, a ring of three single-tensor buffers (the gate and dQ: a
   // buffer's store has two tiles to drain before the buffer is refilled)
-  return EPI == EPI_F32 ? 0
+  return (EPI == EPI_F32 || EPI == EPI_F32_SCATTER) ? 0
          : EPI == EPI_RELU_ROPE                  ? 3
          : (EPI == EPI_GATE || EPI == EPI_DQ)    ? 4
          : EPI == EPI_DEC_BWD                    ? 2
@@ -176,7 +185,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const TileCo
   const EpiParams& e = p.e;
   if (row >= p.M || col >= p.N) return;
   const long long off = (long long)tc.z2 * e.sz2 + (long long)tc.z1 * e.sz1 + (long long)row * e.ld + col;
-  if constexpr (EPI == EPI_F32) {
+  if constexpr (EPI == EPI_F32_SCATTER) {
+    const int owner = row / e.scatter_rows;
+    float4* o4 = reinterpret_cast<float4*>(e.peer[owner] + (long long)e.scatter_rank * e.slot_stride +
+                                           (long long)(row - owner * e.scatter_rows) * e.ld + col);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    return;
+  } else if constexpr (EPI == EPI_F32) {
     float* o = reinterpret_cast<float*>(e.out0) + off + (long long)tc.split * e.split_stride;
     float4* o4 = reinterpret_cast<float4*>(o);
     const float a = e.row_decay ? e.alpha * exp2f((float)row * e.log2_decay[tc.z1]) : e.alpha;
@@ -241,7 +257,9 @@ __device__ __forceinline__ void epilogue_zero_chunk(const GemmParams& p, const T
   if (row >= p.M || col >= p.N) return;
   const EpiParams& e = p.e;
   const long long off = (long long)tc.z2 * e.sz2 + (long long)tc.z1 * e.sz1 + (long long)row * e.ld + col;
-  if constexpr (EPI == EPI_F32) {
+  if constexpr (EPI == EPI_F32_SCATTER) {
+    return;  // the scattered GEMM has no zero tiles (no causal skip, K > 0)
+  } else if constexpr (EPI == EPI_F32) {
     if (e.accumulate) return;
     float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out0) + off +
                                            (long long)tc.split * e.split_stride);

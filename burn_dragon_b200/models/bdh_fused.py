@@ -181,6 +181,11 @@ class FusedBDH:
                 out_states = ws.rho_sets[ws.rho_flip]
                 ws.rho_flip ^= 1
         B, T, D, H, Nh, N, M, L = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L
+        peer = None
+        if self.tp is not None and self.tp.world > 1 and not ws.inference:
+            peer = self.tp.attach_peer(M, D, L, ws.v32[0].device)
+            if peer is not None:
+                ws.m32 = peer.sum_views  # the all-gathered decoder sums land here
         eps, thr = cfg.norm_eps, cfg.relu_threshold
         if v_in is None:
             tok = tokens.reshape(-1)
@@ -243,6 +248,15 @@ class FusedBDH:
             G.gemm(G.EPI_GATE, Operand(ws.an16[l], False, D, M, H * D, z1=(H, D)), B_encv, M, Nh, D, ws.yn16[l],
                    Z1=H, bn=128, aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr)
             # m = yn E (split-K partials), v' = LN(v + LN(m))
+            if peer is not None:
+                # decoder product with the reduce-scatter fused into its epilogue, then the
+                # owners' sums all-gathered by peer stores (parallel.tp.PeerSum)
+                G.gemm(G.EPI_F32_SCATTER, Operand(ws.yn16[l], False, N, M, N), B_dec, M, D, N, ws.m32[l], ld=D,
+                       scatter=peer.scatter_args())
+                peer.finish(l)
+                mod.tail_fwd(ws.m32[l], 1, M * D, ws.v32[l], M, D, p32["norm_gamma"], p32["norm_beta"], eps, None,
+                             ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
+                continue
             G.gemm(G.EPI_F32, Operand(ws.yn16[l], False, N, M, N), B_dec, M, D, N, ws.partial,
                    splits=ws.dec_splits, ld=D, split_stride=M * D)
             if self.tp is not None and self.tp.world > 1:

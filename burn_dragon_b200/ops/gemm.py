@@ -15,7 +15,7 @@ import torch
 
 from .. import _ext
 
-EPI_BF16, EPI_F32, EPI_RELU_ROPE, EPI_SCORES, EPI_GATE, EPI_DEC_BWD, EPI_DQ = range(7)
+EPI_BF16, EPI_F32, EPI_RELU_ROPE, EPI_SCORES, EPI_GATE, EPI_DEC_BWD, EPI_DQ, EPI_F32_SCATTER = range(8)
 
 
 @dataclass(frozen=True)
@@ -76,12 +76,15 @@ def gemm(epi: int, a: Operand, b: Operand, M: int, N: int, K: int, out0: torch.T
          Z1: int = 1, Z2: int = 1, bn: int | None = None, splits: int = 1, causal_skip: bool = False,
          out1=None, aux0=None, aux1=None, ld: int, sz1: int = 0, sz2: int = 0, split_stride: int = 0,
          alpha: float = 1.0, thr: float = 0.0, freq=None, log2_decay=None, T: int = 1, pos0: int = 0,
-         Nh: int = 1, accumulate: bool = False, row_decay: bool = False, pair: bool | None = None) -> None:
+         Nh: int = 1, accumulate: bool = False, row_decay: bool = False, pair: bool | None = None,
+         scatter: list[int] | None = None) -> None:
+    """``scatter`` (EPI_F32_SCATTER): [world, rows per owner, rank, slot stride, slot
+    pointer of every rank] — rows go straight to their owner's slot over NVLink."""
     mod = _ext.load()
     bn = bn or pick_bn(N)
     mod.gemm(epi, bn, a.t, a.mn, a.geom(), b.t, b.mn, b.geom(), M, N, K, Z1, Z2, splits, causal_skip,
              out0, out1, aux0, aux1, ld, sz1, sz2, split_stride, alpha, thr, freq, log2_decay, T, pos0, Nh,
-             accumulate, row_decay, int(PAIR if pair is None else pair), error_word(out0.device))
+             accumulate, row_decay, int(PAIR if pair is None else pair), error_word(out0.device), scatter)
 
 
 def matmul(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, a_t: bool = False,

@@ -30,11 +30,99 @@ def hybrid_layout(world: int, tp: int) -> tuple[list[list[int]], list[list[int]]
     return tp_groups, dp_groups
 
 
+class PeerSum:
+    """The per-layer decoder sum of tensor parallelism over NVLink peer memory.
+
+    The decoder GEMM of every rank stores each output row straight into the slot of the
+    rank that owns that row (``EPI_F32_SCATTER``: the reduce-scatter happens in the
+    GEMM epilogue, tile by tile, while the tensor cores keep running); after a peer
+    barrier each owner sums its W slots and stores the total rows into every rank's
+    per-layer sum buffer (``tp_reduce_gather``, an all-gather by P2P stores), and a
+    second barrier publishes them. The slot and sum buffers live in symmetric device
+    memory shared through CUDA IPC, like the data-parallel communicator's.
+    """
+
+    FLAG_WORDS = 64
+
+    def __init__(self, tp: "TensorParallel", M: int, D: int, L: int, device: torch.device):
+        from .. import _ext
+
+        W = tp.world
+        if M % W:
+            raise ValueError(f"token rows {M} must split evenly over {W} tensor-parallel ranks")
+        mod = _ext.load()
+        self.tp, self.M, self.D, self.L = tp, M, D, L
+        self.rows = M // W
+        self.dev = device.index if device.index is not None else torch.cuda.current_device()
+        sizes = {"slots": W * self.rows * D * 4, "sum": L * M * D * 4, "flags": self.FLAG_WORDS * 4}
+        self._own = {k: mod.sym_alloc(b, self.dev) for k, b in sizes.items()}
+        handles = {k: mod.ipc_handle(v, self.dev) for k, v in self._own.items()}
+        gathered: list = [None] * W
+        dist.all_gather_object(gathered, handles, group=tp.group)
+        self.ptrs: dict[str, list[int]] = {k: [] for k in sizes}
+        self._opened: list[int] = []
+        for r in range(W):
+            for k in sizes:
+                if r == tp.rank:
+                    self.ptrs[k].append(self._own[k])
+                else:
+                    h = mod.ipc_open(gathered[r][k], self.dev)
+                    self._opened.append(h)
+                    self.ptrs[k].append(h)
+        self.slots = mod.wrap_ptr(self._own["slots"], W * self.rows * D, 0, self.dev)
+        sums = mod.wrap_ptr(self._own["sum"], L * M * D, 0, self.dev).view(L, M, D)
+        self.sum_views = [sums[l] for l in range(L)]
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.barrier(group=tp.group)
+
+    def scatter_args(self) -> list[int]:
+        W = self.tp.world
+        return [W, self.rows, self.tp.rank, self.rows * self.D] + list(self.ptrs["slots"])
+
+    def _barrier(self, phase: int) -> None:
+        from .. import _ext
+
+        f = self.ptrs["flags"]
+        _ext.load().peer_barrier(f, f, f, f, self.tp.rank, phase, self.err)
+
+    def finish(self, layer: int) -> None:
+        """After the scattered GEMM: sum this rank's rows, all-gather them into every
+        rank's sum buffer of ``layer``."""
+        from .. import _ext
+
+        self._barrier(0)
+        base = self.ptrs["sum"]
+        dst = [b + layer * self.M * self.D * 4 for b in base]
+        _ext.load().tp_reduce_gather(self.slots, dst, self.tp.rank, self.rows, self.M, self.D, self.rows * self.D)
+        self._barrier(1)
+
+    def check(self) -> None:
+        if int(self.err.item()):
+            raise RuntimeError(f"tensor-parallel peer barrier timed out (code {int(self.err.item())})")
+
+
 class TensorParallel:
-    def __init__(self, group=None):
+    def __init__(self, group=None, fused_comm: bool | None = None):
+        """``fused_comm``: run the forward decoder sums through ``PeerSum`` (default on
+        CUDA unless BDH_TP_FUSED=0); otherwise NCCL all-reduce."""
+        import os
+
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if fused_comm is None:
+            fused_comm = os.environ.get("BDH_TP_FUSED", "1") != "0" and torch.cuda.is_available()
+        self.fused_comm = fused_comm and self.world > 1
+        self.peer: PeerSum | None = None
+
+    def attach_peer(self, M: int, D: int, L: int, device: torch.device) -> PeerSum | None:
+        """Symmetric buffers for a workspace shape (re-created when the shape changes)."""
+        if not self.fused_comm:
+            return None
+        p = self.peer
+        if p is None or (p.M, p.D, p.L) != (M, D, L):
+            self.peer = PeerSum(self, M, D, L, device)
+        return self.peer
 
     def all_reduce(self, t: torch.Tensor) -> None:
         if self.world > 1:

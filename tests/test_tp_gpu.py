@@ -25,11 +25,11 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, fused="1"):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0", BDH_TP_FUSED=fused)
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world)
     from burn_dragon_b200.models.bdh import BDH
@@ -66,9 +66,11 @@ def _worker(rank, world, port, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_matches_unsharded():
+@pytest.mark.parametrize("fused", ["1", "0"])
+def test_tensor_parallel_matches_unsharded(fused):
+    """fused = "1": decoder sums through the scattered GEMM + peer all-gather; "0": NCCL."""
     out = mp.Manager().dict()
-    mp.spawn(_worker, args=(2, _port(), out), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _port(), out, fused), nprocs=2, join=True)
     for r in (0, 1):
         res = out[r]
         a, b = res.pop("loss")
