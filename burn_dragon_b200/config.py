@@ -261,9 +261,28 @@ class DragonConfig:
     norm_eps: float = 1e-5
     # initialization family (init.rs:18-25; the reference defaults to near_critical) and
     # the SimpleNormal std (init.rs:810)
-    initialization: str = "near_critical"
+    initialization: str = "simple_normal"
     init_std: float = 0.02
     reservoir_density: float = 0.1
+    # DragonInitializationConfig sub-tables (init.rs:24-190). Without an
+    # [model.initialization] table the reference uses its promoted default: simple_normal
+    # with depth-scaled residual projections and heavy-tailed log-normal neuron gains.
+    residual_scaling: str = "depth_scaled"  # family_default | disabled | depth_scaled
+    residual_scaling_gain: float = 1.0
+    neuron_gains: str = "heavy_tailed_log_normal"  # iid | heavy_tailed_log_normal
+    neuron_gain_log_sigma: float = 0.75
+    neuron_gain_max: float = 4.0
+    topology_prior: str = "iid"  # iid | modular_bridges
+    topology_community_count: int = 4
+    topology_bridge_fraction: float = 0.05
+    topology_intra_community_gain: float = 1.5
+    topology_inter_community_gain: float = 0.5
+    topology_bridge_gain: float = 1.0
+    firing_targets: str = "disabled"  # disabled | gaussian_estimate | explicit_thresholds
+    x_firing_target: float = 0.15
+    y_firing_target: float = 0.05
+    x_firing_threshold: float = 0.0
+    y_firing_threshold: float = 0.0
     # DragonNormConfig (norm.rs:11-125): layer_norm | rms_norm | dynamic_tanh | derf
     norm_kind: str = "layer_norm"
     norm_alpha_init: float | None = None
@@ -309,6 +328,28 @@ class DragonConfig:
             raise ValueError("latent size must be divisible by the number of heads")
         return total // self.n_head
 
+    def residual_depth(self) -> int:
+        return max(self.n_layer, 1) * max(self.rollout_fast_steps_per_slow_step, 1)
+
+    def thresholds(self) -> tuple[float, float]:
+        """(x, y) ReLU thresholds: the shared ``relu_threshold`` unless firing targets set
+        them (init.rs:544-580): ``gaussian_estimate`` places each threshold at the
+        (1 - target) quantile of the estimated pre-activation N(0, sqrt(D) * std)."""
+        if self.firing_targets == "disabled":
+            return self.relu_threshold, self.relu_threshold
+        if self.firing_targets == "explicit_thresholds":
+            return self.x_firing_threshold, self.y_firing_threshold
+        from statistics import NormalDist
+
+        from .models.init import projection_std
+
+        out = []
+        for role, target in (("encoder", self.x_firing_target), ("encoder_v", self.y_firing_target)):
+            sigma = math.sqrt(max(self.n_embd, 1)) * projection_std(self, role, self.n_embd, self.latent_per_head)
+            p = min(max(1.0 - target, 1e-12), 1.0 - 1e-12)
+            out.append(sigma * NormalDist().inv_cdf(p))
+        return out[0], out[1]
+
     def norm_alpha(self) -> float:
         if self.norm_alpha_init is not None:
             return self.norm_alpha_init
@@ -320,6 +361,22 @@ class DragonConfig:
         if self.initialization not in ("simple_normal", "near_critical", "he_glorot", "headwise_semi_orthogonal",
                                        "reservoir"):
             raise ValueError(f"unknown initialization kind {self.initialization!r}")
+        if self.residual_scaling not in ("family_default", "disabled", "depth_scaled") or \
+                not self.residual_scaling_gain > 0:
+            raise ValueError("initialization.residual_scaling: kind family_default | disabled | depth_scaled, gain > 0")
+        if self.neuron_gains not in ("iid", "heavy_tailed_log_normal") or self.neuron_gain_log_sigma < 0 or \
+                not self.neuron_gain_max > 0:
+            raise ValueError("initialization.neuron_gains: kind iid | heavy_tailed_log_normal, log_sigma >= 0, "
+                             "max_gain > 0")
+        if self.topology_prior not in ("iid", "modular_bridges") or self.topology_community_count < 1 or \
+                not 0 <= self.topology_bridge_fraction <= 1:
+            raise ValueError("initialization.topology_prior: kind iid | modular_bridges, community_count > 0, "
+                             "bridge_fraction in [0, 1]")
+        if self.firing_targets not in ("disabled", "gaussian_estimate", "explicit_thresholds"):
+            raise ValueError("initialization.firing_targets.kind: disabled | gaussian_estimate | explicit_thresholds")
+        if self.firing_targets == "gaussian_estimate" and not (0 < self.x_firing_target < 1
+                                                               and 0 < self.y_firing_target < 1):
+            raise ValueError("initialization.firing_targets: targets must be probabilities in (0, 1)")
         if self.rotary_embedding not in ROTARY_KINDS:
             raise ValueError(f"rotary_embedding must be one of {ROTARY_KINDS}")
         if self.rollout_fast_steps_per_slow_step not in (1, 2, 4, 8, 16):
@@ -631,9 +688,31 @@ def _model_table(table: dict) -> dict:
             t["dense_score_row_chunk"] = sk["dense_score_row_chunk"]
     ini = t.get("initialization")
     if isinstance(ini, dict):
+        # a present table takes each sub-table's own defaults (init.rs:24-160)
         t["initialization"] = ini.get("kind", "near_critical")
         if "simple_normal_std" in ini:
             t["init_std"] = ini["simple_normal_std"]
+        rs = ini.get("residual_scaling", {})
+        t["residual_scaling"] = rs.get("kind", "family_default")
+        t["residual_scaling_gain"] = rs.get("gain", 1.0)
+        ng = ini.get("neuron_gains", {})
+        t["neuron_gains"] = ng.get("kind", "iid")
+        t["neuron_gain_log_sigma"] = ng.get("log_sigma", 0.75)
+        t["neuron_gain_max"] = ng.get("max_gain", 4.0)
+        tp = ini.get("topology_prior", {})
+        t["topology_prior"] = tp.get("kind", "iid")
+        for k in ("community_count", "bridge_fraction", "intra_community_gain", "inter_community_gain",
+                  "bridge_gain"):
+            if k in tp:
+                t["topology_" + k] = tp[k]
+        ft = ini.get("firing_targets", {})
+        t["firing_targets"] = ft.get("kind", "disabled")
+        for a, b in (("x_target", "x_firing_target"), ("y_target", "y_firing_target"),
+                     ("x_threshold", "x_firing_threshold"), ("y_threshold", "y_firing_threshold")):
+            if a in ft:
+                t[b] = ft[a]
+        if isinstance(ini.get("reservoir"), dict) and "density" in ini["reservoir"]:
+            t["reservoir_density"] = ini["reservoir"]["density"]
     if "latent_total" in t:
         lt = t.pop("latent_total")
         d = t.get("n_embd", DragonConfig.n_embd)

@@ -142,15 +142,11 @@ class BDH(nn.Module):
     # beta=0 (burn_dragon_core/src/model/init.rs:10,448-520,593-650); scaffold adapters:
     # A from the scaffold generator, B = 0, gain = 1 (scaffold.rs:31-55).
     def _init_weights(self, gen: torch.Generator) -> None:
-        from .init import init_tensor
+        from .init import init_param
         from .scaffold import PATHS, adapter_a_init
 
         cfg = self.cfg
         rs = cfg.random_scaffold
-        D, N, V = cfg.n_embd, cfg.latent_total, cfg.vocab_size
-        fans = {"encoder": (D, cfg.latent_per_head), "encoder_v": (D, cfg.latent_per_head), "decoder": (N, D),
-                "embed": (V, D), "lm_head": (D, V)}
-        depth = cfg.n_layer * cfg.rollout_fast_steps_per_slow_step
         for name, shp in self.store.shapes.items():
             view = self.store.view(self.store.data, name)
             if name == "norm_gamma" or name.endswith("_gain"):
@@ -170,9 +166,7 @@ class BDH(nn.Module):
                 fan_in = shp[-2]
                 view.copy_(adapter_a_init(rs.seed, PATHS[proj], shp, fan_in))
             else:
-                fi, fo = fans[name]
-                view.copy_(init_tensor(cfg.initialization, name, shp, fi, fo, depth, gen, cfg.init_std,
-                                       cfg.reservoir_density))
+                view.copy_(init_param(cfg, name, shp, gen))
 
     def _init_scaffold(self, device) -> None:
         """Frozen bases: kept on the host (CPU path) or regenerated by the device kernel."""

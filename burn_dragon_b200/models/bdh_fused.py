@@ -186,7 +186,8 @@ class FusedBDH:
             peer = self.tp.attach_peer(M, D, L, ws.v32[0].device)
             if peer is not None:
                 ws.m32 = peer.sum_views  # the all-gathered decoder sums land here
-        eps, thr = cfg.norm_eps, cfg.relu_threshold
+        eps = cfg.norm_eps
+        thr, thr_y = cfg.thresholds()
         if v_in is None:
             tok = tokens.reshape(-1)
             torch.index_select(p32["embed"], 0, tok, out=ws.emb_rows)
@@ -246,7 +247,7 @@ class FusedBDH:
                        ws.amean[l], ws.arstd[l])
             # yn = relu(an Dy - thr) * x                (K = D)
             G.gemm(G.EPI_GATE, Operand(ws.an16[l], False, D, M, H * D, z1=(H, D)), B_encv, M, Nh, D, ws.yn16[l],
-                   Z1=H, bn=128, aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr)
+                   Z1=H, bn=128, aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr_y)
             # m = yn E (split-K partials), v' = LN(v + LN(m))
             if peer is not None:
                 # decoder product with the reduce-scatter fused into its epilogue, then the

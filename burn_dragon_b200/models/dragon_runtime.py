@@ -207,15 +207,13 @@ class DragonRuntime(nn.Module):
             self.conn_first = _first_layer(cfg.block_attention_residual.last_layers, L)
         hd = cfg.hierarchical_dragon
         if hd.enabled and hd.weight_sharing == "split":
-            from .init import init_tensor
+            from .init import init_param
 
             H, Nh, N = cfg.n_head, cfg.latent_per_head, cfg.latent_total
-            depth = L * cfg.rollout_fast_steps_per_slow_step
-            mk = lambda role, shp, fi, fo: nn.Parameter(init_tensor(cfg.initialization, role, shp, fi, fo, depth, gen,
-                                                                    cfg.init_std, cfg.reservoir_density))
-            self.slow_encoder = mk("encoder", (H, D, Nh), D, Nh)
-            self.slow_encoder_v = mk("encoder_v", (H, D, Nh), D, Nh)
-            self.slow_decoder = mk("decoder", (N, D), N, D)
+            mk = lambda role, shp: nn.Parameter(init_param(cfg, role, shp, gen))  # noqa: E731
+            self.slow_encoder = mk("encoder", (H, D, Nh))
+            self.slow_encoder_v = mk("encoder_v", (H, D, Nh))
+            self.slow_decoder = mk("decoder", (N, D))
         lr = cfg.latent_reasoning
         if lr.enabled:
             hid = D * max(1, lr.refiner_hidden_multiplier)
@@ -325,7 +323,7 @@ class DragonRuntime(nn.Module):
     def _lowrank_step(self, v, ls, pos, fixed, *, slow_weights=False, slot="fast", x_inject=None, want_y=False):
         enc, enc_v, dec, p = self._weights(slow_weights)
         nf = self._norm(p)
-        thr = self.cfg.relu_threshold
+        thr, thr_y = self.cfg.thresholds()
         lm = self._latent_mask
         x = torch.relu(torch.einsum("btd,hdn->bhtn", v, enc) - thr)
         if lm is not None:
@@ -333,7 +331,7 @@ class DragonRuntime(nn.Module):
         if x_inject is not None:
             x = x + x_inject
         a = nf(self._attend(x, v, ls, pos, fixed, slot))
-        y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr)
+        y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr_y)
         if lm is not None:
             y = y * lm
         yn = x * y
@@ -416,7 +414,7 @@ class DragonRuntime(nn.Module):
         c = self.cfg.y_neuron_recurrence
         enc, enc_v, dec, p = self._weights()
         nf = self._norm(p)
-        thr = self.cfg.relu_threshold
+        thr, thr_y = self.cfg.thresholds()
         B, T, D = v.shape
         H, Nh = self.cfg.n_head, self.cfg.latent_per_head
         st = ls.y_state
@@ -433,7 +431,7 @@ class DragonRuntime(nn.Module):
                 x = x + st.unsqueeze(2) * c.carry_in_scale
             tok = v[:, s:e]
             a = nf(self._attend(x, tok, ls, start_pos if fixed else start_pos + s, fixed))
-            y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr)
+            y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr_y)
             if self._latent_mask is not None:
                 y = y * self._latent_mask
             yn = x * y

@@ -136,7 +136,8 @@ class Generator:
         N = H * Nh
         p32 = self.model.store.views(self.model.store.data)
         p16 = self.model.shadow_dict()
-        gam, bet, eps, thr = p32["norm_gamma"], p32["norm_beta"], cfg.norm_eps, cfg.relu_threshold
+        gam, bet, eps = p32["norm_gamma"], p32["norm_beta"], cfg.norm_eps
+        thr, thr_y = cfg.thresholds()
         if state.rhos is None:
             state.rhos = [torch.zeros(B, H, Nh, D, device=tokens.device) for _ in range(cfg.n_layer)]
         mod.ln_fwd(p32["embed"], tokens, B, D, gam, bet, eps, w.v32[0], w.v16[0], w.amean, w.arstd)
@@ -153,7 +154,7 @@ class Generator:
             mod.rho_step(state.rhos[l], q, N, v32, w.gamma, w.a32, B, H, Nh, D)
             mod.ln_fwd(w.a32, None, B * H, D, gam, bet, eps, None, w.an16, w.amean, w.arstd)
             G.gemm(G.EPI_GATE, Operand(w.an16, False, D, B, H * D, z1=(H, D)), B_encv, B, Nh, D, w.yn16, Z1=H,
-                   bn=128, aux0=w.x16, ld=N, sz1=Nh, thr=thr)
+                   bn=128, aux0=w.x16, ld=N, sz1=Nh, thr=thr_y)
             G.gemm(G.EPI_F32, Operand(w.yn16, False, N, B, N), Operand(p16["decoder"], True, D, N, D), B, D, N,
                    w.partial, splits=w.splits, ld=D, split_stride=B * D)
             nxt = 1 - cur

@@ -141,10 +141,11 @@ def layer_norm(x, gamma, beta, eps):
 
 
 def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, decay, rho0=None,
-              need_state=False, dropout=0.0, training=False, norm=None, pope=False, attention=None):
+              need_state=False, dropout=0.0, training=False, norm=None, pope=False, attention=None, thr_y=None):
     """One shared-weight BDH layer. v [B,T,D]; enc/enc_v [H,D,Nh]; dec [N,D].
     ``norm`` overrides the LayerNorm (other DragonNorm kinds); ``pope`` switches the
-    query embedding to PoPE (``freqs`` then holds the PoPE frequencies).
+    query embedding to PoPE (``freqs`` then holds the PoPE frequencies). ``thr`` is the
+    x ReLU threshold, ``thr_y`` the y one (default: the same).
 
     Returns (v', rho_T or None, aux dict of the intermediate activations).
     """
@@ -163,7 +164,7 @@ def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, de
     else:
         a, rho = linear_attention_dense(q, v[:, None], rho0=rho0, decay=decay, need_state=need_state)
     a = nf(a)  # [B,H,T,D]
-    y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - thr)
+    y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - (thr if thr_y is None else thr_y))
     yn = x * y
     if dropout > 0.0 and training:
         yn = F.dropout(yn, dropout, training=True)
@@ -200,7 +201,8 @@ def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state
         if streams > 1:
             v, R = MHC.layer_split(R, params["mhc_res"][layer], params["mhc_pre"][layer], cfg.mhc_tau, cfg.mhc_iters)
         v, rho, _ = bdh_layer(v, params["encoder"], params["encoder_v"], params["decoder"], gamma, beta,
-                              eps=cfg.norm_eps, thr=cfg.relu_threshold, freqs=freqs, positions=positions,
+                              eps=cfg.norm_eps, thr=cfg.thresholds()[0], thr_y=cfg.thresholds()[1], freqs=freqs,
+                              positions=positions,
                               decay=decay, rho0=r0, need_state=need_state, dropout=cfg.dropout,
                               training=training, norm=norm, pope=cfg.rotary_embedding == "pope")
         if streams > 1:

@@ -62,7 +62,7 @@ def cp_loss(model, tokens: torch.Tensor, targets: torch.Tensor, group=None) -> t
     attn = _attention(rank, world, decay, group)
     for _ in range(cfg.n_layer):
         v, _, _ = R.bdh_layer(v, p["encoder"], p["encoder_v"], p["decoder"], gamma, beta, eps=cfg.norm_eps,
-                              thr=cfg.relu_threshold, freqs=freqs, positions=pos, decay=decay, norm=norm,
+                              thr=cfg.thresholds()[0], thr_y=cfg.thresholds()[1], freqs=freqs, positions=pos, decay=decay, norm=norm,
                               attention=attn)
     head = p["embed"].t() if p.get("lm_head") is None else p["lm_head"]
     return R.cross_entropy(v @ head, targets) / world

@@ -164,7 +164,7 @@ class ReferenceStage:
         pos = torch.arange(T)
         for _ in range(self.l0, self.l1):
             v, _, _ = R.bdh_layer(v, params["encoder"], params["encoder_v"], params["decoder"], gamma, beta,
-                                  eps=cfg.norm_eps, thr=cfg.relu_threshold, freqs=freqs, positions=pos, decay=decay)
+                                  eps=cfg.norm_eps, thr=cfg.thresholds()[0], thr_y=cfg.thresholds()[1], freqs=freqs, positions=pos, decay=decay)
         loss = None
         if self.last:
             head = params["embed"].t() if params.get("lm_head") is None else params["lm_head"]

@@ -105,7 +105,7 @@ class ContinualBackprop:
         pos = torch.arange(T, device=v.device)
         for _ in range(cfg.n_layer):
             v, _, aux = R.bdh_layer(v, p["encoder"], p["encoder_v"], p["decoder"], p["norm_gamma"], p["norm_beta"],
-                                    eps=cfg.norm_eps, thr=cfg.relu_threshold, freqs=freqs, positions=pos, decay=decay,
+                                    eps=cfg.norm_eps, thr=cfg.thresholds()[0], thr_y=cfg.thresholds()[1], freqs=freqs, positions=pos, decay=decay,
                                     norm=norm, pope=cfg.rotary_embedding == "pope")
             self.record(aux["yn"])
 
@@ -201,19 +201,17 @@ class ContinualBackprop:
         return sel
 
     def reinitialize(self, model, optimizer, sel: list[int]) -> None:
-        from ..models.init import init_tensor
+        from ..models.init import init_param
 
         m = self.mcfg
         H, D, Nh, N = m.n_head, m.n_embd, m.latent_per_head, m.latent_total
         gen = torch.Generator().manual_seed(self.seed * 7919 + self.step)
-        depth = m.n_layer * m.rollout_fast_steps_per_slow_step
         idx = torch.tensor(sel, device=model.encoder.device)
         rows = (torch.arange(H, device=idx.device)[:, None] * Nh + idx[None, :]).reshape(-1)
         st = model.store
         with torch.no_grad():
             for name in ("encoder", "encoder_v"):
-                fresh = init_tensor(m.initialization, name, (H, D, Nh), D, Nh, depth, gen, m.init_std,
-                                    m.reservoir_density).to(idx.device)
+                fresh = init_param(m, name, (H, D, Nh), gen).to(idx.device)
                 p = getattr(model, name)
                 p[:, :, idx] = fresh[:, :, idx].to(p.dtype)
                 for buf in (optimizer.m, optimizer.v):

@@ -72,7 +72,7 @@ class _Stack:
     def layer(self, a, rho0=None, need_state=False):
         c = self.cfg
         out, rho, _ = R.bdh_layer(a, self.p["encoder"], self.p["encoder_v"], self.p["decoder"], self.p["norm_gamma"],
-                                  self.p["norm_beta"], eps=c.norm_eps, thr=c.relu_threshold, freqs=self.freqs,
+                                  self.p["norm_beta"], eps=c.norm_eps, thr=c.thresholds()[0], thr_y=c.thresholds()[1], freqs=self.freqs,
                                   positions=self.pos, decay=self.decay, rho0=rho0, need_state=need_state,
                                   norm=self.norm, pope=c.rotary_embedding == "pope")
         return out, rho

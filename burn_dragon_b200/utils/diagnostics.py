@@ -175,7 +175,7 @@ def neuron_activity(model, tokens: torch.Tensor) -> list[dict]:
         pos = torch.arange(tokens.shape[1], device=v.device)
         for i in range(cfg.n_layer):
             v, _, aux = R.bdh_layer(v, p["encoder"], p["encoder_v"], p["decoder"], p["norm_gamma"], p["norm_beta"],
-                                    eps=cfg.norm_eps, thr=cfg.relu_threshold, freqs=freqs, positions=pos, decay=decay,
+                                    eps=cfg.norm_eps, thr=cfg.thresholds()[0], thr_y=cfg.thresholds()[1], freqs=freqs, positions=pos, decay=decay,
                                     norm=norm)
             yn = aux["yn"]
             silent = (yn.reshape(-1, yn.shape[1], yn.shape[-1]) > 0).any(0).logical_not().double().mean()

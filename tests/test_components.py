@@ -1,4 +1,5 @@
 """Model components beyond the BDH-GPU defaults: norm kinds, PoPE, initialisers."""
+import copy
 import math
 
 import pytest
@@ -87,3 +88,42 @@ def test_mhc_sinkhorn_and_training():
     loss = model.loss(x, x)
     g = torch.autograd.grad(loss, [model.mhc_res, model.mhc_post, model.encoder], allow_unused=True)
     assert all(t is not None and torch.isfinite(t).all() for t in g)
+
+
+def test_initialization_sub_configs_follow_the_reference_rules():
+    from burn_dragon_b200.config import training_config_from_dict
+    from burn_dragon_b200.models.init import init_param, modular_bridges, projection_std
+
+    # no [model.initialization] table: simple_normal + depth-scaled + heavy-tailed gains
+    c = training_config_from_dict({"model": {"n_layer": 4, "n_embd": 32, "n_head": 2,
+                                             "mlp_internal_dim_multiplier": 8}}).model
+    assert (c.initialization, c.residual_scaling, c.neuron_gains) == ("simple_normal", "depth_scaled",
+                                                                       "heavy_tailed_log_normal")
+    assert abs(projection_std(c, "encoder", 32, 128) - 0.02 / 2) < 1e-12
+    assert projection_std(c, "lm_head", 32, 256) == 0.02
+    # a present table takes the sub-tables' own defaults (family_default, iid)
+    c2 = training_config_from_dict({"model": {"n_layer": 4, "n_embd": 32, "n_head": 2, "mlp_internal_dim_multiplier": 8,
+                                              "initialization": {"kind": "simple_normal"}}}).model
+    assert (c2.residual_scaling, c2.neuron_gains) == ("family_default", "iid")
+    assert projection_std(c2, "encoder", 32, 128) == 0.02
+    g = torch.Generator().manual_seed(0)
+    w = init_param(c, "encoder", (2, 32, 128), g)
+    col_rms = w.pow(2).mean(1).sqrt()  # per (head, neuron)
+    assert float(col_rms.max() / col_rms.min()) > 3.0  # heavy-tailed neuron gains
+    # modular bridges: unit RMS, bridge tail on the latent axis
+    c3 = copy.deepcopy(c2)
+    c3.topology_prior = "modular_bridges"
+    m = modular_bridges(c3, 8, 20, "cols")
+    assert abs(float(m.pow(2).mean().sqrt()) - 1.0) < 1e-6
+    assert torch.allclose(m[:, -1], m[0, -1].expand(8))  # bridge column is constant
+
+
+def test_firing_target_thresholds():
+    from burn_dragon_b200.config import DragonConfig
+
+    c = DragonConfig(n_layer=2, n_embd=64, n_head=2, mlp_internal_dim_multiplier=4, firing_targets="gaussian_estimate")
+    x, y = c.thresholds()
+    assert 0 < x < y  # a rarer y target sits further out in the tail
+    c.firing_targets = "explicit_thresholds"
+    c.x_firing_threshold, c.y_firing_threshold = 0.1, 0.2
+    assert c.thresholds() == (0.1, 0.2)
