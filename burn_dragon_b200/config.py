@@ -532,6 +532,28 @@ class AutoBatchSizeConfig:
 
 
 @dataclass
+class NeuronScalingStabilizationConfig:
+    freeze_base_steps: int = 256
+    unfreeze_ramp_steps: int = 256
+    new_slice_lr_scale: float = 1.0
+    base_lr_scale_after_ramp: float = 1.0
+
+
+@dataclass
+class NeuronScalingConfig:
+    """Latent-width doubling on a validation plateau (schema.rs:151-300; defaults there)."""
+
+    enabled: bool = False
+    max_latent_total: int = 8192
+    growth: str = "double"
+    min_steps_between_scales: int = 2000
+    max_scale_events: int = 4
+    capacity_patience_epochs: int = 2
+    require_live_source_selection: bool = True
+    stabilization: NeuronScalingStabilizationConfig = field(default_factory=NeuronScalingStabilizationConfig)
+
+
+@dataclass
 class TrainingSection:
     block_size: int = 512
     batch_size: int = 32
@@ -546,6 +568,7 @@ class TrainingSection:
     validation_interval_iters: int | None = None
     continual_backprop: ContinualBackpropConfig = field(default_factory=ContinualBackpropConfig)
     auto_batch_size: AutoBatchSizeConfig = field(default_factory=AutoBatchSizeConfig)
+    neuron_scaling: NeuronScalingConfig = field(default_factory=NeuronScalingConfig)
     target_effective_batch_size: int | None = None
     # initialise the weights from this run directory's newest checkpoint (a fresh run only)
     init_checkpoint_path: str | None = None

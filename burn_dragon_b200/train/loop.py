@@ -83,6 +83,11 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         cfg.parallel.tensor["micro_batches"] = res.gradient_accumulation_steps
         if rank == 0:
             run.write_json("auto_batch_size.json", vars(res))
+    ns_path = os.path.join(run.path, "neuron_scaling.json")
+    if resume and t.neuron_scaling.enabled and os.path.exists(ns_path):
+        import json
+
+        cfg.model.mlp_internal_dim_multiplier = int(json.load(open(ns_path))["mlp_internal_dim_multiplier"])
     extended = cfg.model.uses_extended_runtime()
     if extended and mode not in ("single", "ddp", "fsdp"):
         raise ValueError(f"parallel mode {mode!r} does not support the layer-loop variants this model enables")
@@ -108,6 +113,15 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     pc = t.algorithm == "predictive_coding"
     if pc and (extended or mode not in ("single", "ddp", "fsdp")):
         raise ValueError("predictive_coding training needs the plain BDH model in single / ddp mode")
+    scaler = None
+    if t.neuron_scaling.enabled:
+        if extended or pc or mode not in ("single", "ddp", "fsdp") or getattr(trainer, "comm", None) is not None:
+            raise ValueError("neuron_scaling needs the plain BDH model without the NVLink communicator")
+        if not t.validation_interval_iters:
+            raise ValueError("neuron_scaling triggers on validation plateaus: set training.validation_interval_iters")
+        from .neuron_scaling import NeuronScaler
+
+        scaler = NeuronScaler(t.neuron_scaling)
     objective = None
     if t.objective.get("type", "next_token") != "next_token":
         from . import objectives as OBJ
@@ -232,10 +246,14 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 trainer.step_idx += 1
                 prof.stop("forward_backward")
             else:
+                if scaler is not None:
+                    scaler.before_step(trainer.model, step)
                 sample = cbp is not None and cbp.should_sample()
                 if sample and not getattr(trainer, "fused", False):
                     cbp.record_reference(trainer.model, x.to(dev))
                 loss = trainer.step(x, y)
+                if scaler is not None:
+                    scaler.after_step(step)
                 prof.stop("forward_backward")
                 if cbp is not None:
                     if sample and getattr(trainer, "fused", False):
@@ -255,6 +273,17 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 with torch.no_grad():
                     vl = float(trainer.model.loss(vx.to(dev), vy.to(dev)))  # fresh state per window
                 log.log(step + 1, valid_loss=vl, force=True)
+                if scaler is not None:
+                    scaler.observe_validation(vl)
+                    if scaler.should_scale(step + 1, trainer.model.cfg):
+                        scaler.scale(trainer, step + 1)
+                        cfg.model = trainer.model.cfg
+                        log.log(step + 1, neuron_scale_event=scaler.events,
+                                latent_total=trainer.model.cfg.latent_total, force=True)
+                        if rank == 0:
+                            run.write_json("neuron_scaling.json", {
+                                "mlp_internal_dim_multiplier": trainer.model.cfg.mlp_internal_dim_multiplier,
+                                "events": scaler.events, "step": step + 1})
             if t.checkpoint_interval_iters and (step + 1) % t.checkpoint_interval_iters == 0 and rank == 0:
                 rt = None
                 if state is not None and not extended and state.rhos is not None:
