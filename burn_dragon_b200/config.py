@@ -569,6 +569,10 @@ class TrainingSection:
     continual_backprop: ContinualBackpropConfig = field(default_factory=ContinualBackpropConfig)
     auto_batch_size: AutoBatchSizeConfig = field(default_factory=AutoBatchSizeConfig)
     neuron_scaling: NeuronScalingConfig = field(default_factory=NeuronScalingConfig)
+    # batches from the native prefetching loader (csrc/host/loader.cpp) instead of the
+    # Python generators
+    native_loader: bool = True
+    loader_workers: int = 2
     target_effective_batch_size: int | None = None
     # initialise the weights from this run directory's newest checkpoint (a fresh run only)
     init_checkpoint_path: str | None = None

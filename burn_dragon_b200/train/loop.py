@@ -166,14 +166,34 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     if mode == "hybrid_2d":
         tp_size = int(cfg.parallel.tensor.get("size", 8))
         data_rank, data_world = rank // tp_size, world // tp_size
+    native = None
+    if t.native_loader and not streaming:
+        try:
+            from .native_data import NativeBytes
+
+            if cfg.dataset.type == "file":
+                native = NativeBytes("file", t.batch_size, t.block_size, path=cfg.dataset.path, seed=t.seed,
+                                     rank=data_rank, world=data_world, ratio=cfg.dataset.train_split_ratio,
+                                     workers=t.loader_workers, start_step=start)
+            else:
+                native = NativeBytes("random", t.batch_size, t.block_size, seed=t.seed, rank=data_rank,
+                                     world=data_world, vocab=cfg.model.vocab_size, workers=t.loader_workers,
+                                     start_step=start)
+        except Exception as e:  # no host toolchain: the Python generators below
+            import warnings
+
+            warnings.warn(f"native loader unavailable ({e}); using the Python batch generators", stacklevel=2)
+            native = None
     if streaming:
         chunk = t.tbptt_chunk_size or t.block_size
         data = StreamingBytes(t.batch_size, t.block_size, chunk, seed=t.seed, rank=data_rank)
         data.pos = (start * chunk) % max(1, t.block_size - chunk + 1) if t.block_size > chunk else 0
-    elif cfg.dataset.type == "file":
+    elif cfg.dataset.type == "file" and native is None:
         data = FileBytes(cfg.dataset.path, t.batch_size, t.block_size, "train", cfg.dataset.train_split_ratio,
                          seed=t.seed, rank=data_rank, world=data_world)
         data.step = start
+    elif native is not None:
+        data = native
     else:
         data = RandomBytes(t.batch_size, t.block_size, seed=t.seed, rank=data_rank, world=data_world)
         data.step = start
@@ -261,6 +281,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                     lr_now = getattr(trainer.opt, "_lr_now", o.learning_rate)
                     if cbp.after_optimizer_step(trainer.model, trainer.opt, lr_now):
                         log.log(step + 1, cbp_replaced=cbp.last.replacement_count, force=True)
+            if native is not None:
+                native.mark_consumed()  # its buffer is refilled only after these copies ran
             prof.tokens += x.numel() * (world if mode in ("ddp", "fsdp") else 1)
             if (step + 1) % t.log_frequency == 0 or step + 1 == t.max_iters:
                 lv = float(loss)
@@ -299,6 +321,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         raise
     finally:
         log.close()
+        if native is not None:
+            native.close()
         if hb is not None:
             hb.stop()
     summary = prof.summary() if prof.enabled else {}
