@@ -15,8 +15,11 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("rotary", ["rope", "alibi"])
 def test_fused_step_matches_reference(rotary):
+    # iid neurons: the x5 weights below on top of heavy-tailed neuron gains push a few
+    # neurons far enough that bf16 activations alone move the encoder_v gradient ~9%
     cfg = DragonConfig(n_layer=2, n_embd=64, n_head=2, mlp_internal_dim_multiplier=8, dropout=0.0,
-                       rotary_embedding=rotary)
+                       rotary_embedding=rotary, initialization="near_critical", residual_scaling="family_default",
+                       neuron_gains="iid")
     model = BDH(cfg, device="cuda", seed=5)
     # larger weights than N(0, .02) so that every path carries signal in bf16
     with torch.no_grad():
