@@ -208,7 +208,9 @@ class FusedBDH:
                    T=T, pos0=pos0, Nh=Nh)
             # S = tril_{-1}(q q^T) (* gamma^(i-j))      (K = Nh), upper tiles skipped
             qop = Operand(ws.q16[l], False, Nh, T, N, z1=(H, Nh), z2=(B, T * N))
-            G.gemm(G.EPI_SCORES, qop, qop, T, T, Nh, ws.S16[l], Z1=H, Z2=B, bn=256 if T % 256 == 0 else 128,
+            # 256-row CTA-pair tiles x 128 columns: finer causal skipping than 256 x 256
+            # (6 of 8 tiles vs 3 of 4 at T = 512), 8% faster measured at BDH-GPU batch 32
+            G.gemm(G.EPI_SCORES, qop, qop, T, T, Nh, ws.S16[l], Z1=H, Z2=B, bn=128,
                    causal_skip=True, ld=T, sz1=T * T, sz2=H * T * T, log2_decay=ws.log2_decay)
             # a = S V                                   (K = T), V shared by the heads
             G.gemm(G.EPI_F32, Operand(ws.S16[l], False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),

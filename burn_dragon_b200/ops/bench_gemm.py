@@ -11,6 +11,7 @@ drive ncu captures of a single kernel on a small case.
 from __future__ import annotations
 
 import argparse
+import os
 import json
 
 import torch
@@ -34,7 +35,8 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
     if case == "scores":
         q, S = r(M, N), r(B, H, T, T)
         op = Operand(q, False, Nh, T, N, z1=(H, Nh), z2=(B, T * N))
-        call = lambda: G.gemm(G.EPI_SCORES, op, op, T, T, Nh, S, Z1=H, Z2=B, bn=256, causal_skip=True,  # noqa: E731
+        bn = int(os.environ.get("BDH_BENCH_BN", "256"))
+        call = lambda: G.gemm(G.EPI_SCORES, op, op, T, T, Nh, S, Z1=H, Z2=B, bn=bn, causal_skip=True,  # noqa: E731
                               ld=T, sz1=T * T, sz2=H * T * T)
         return call, B * H * T * T * Nh, (M * N + B * H * T * T) * 2
     if case == "gate":
