@@ -1,0 +1,67 @@
+"""Stateful-TBPTT training benchmark (the long-context BDH-GPU configuration).
+
+  python -m burn_dragon_b200.cli.bench_tbptt [--batch 16] [--stream 8192] [--chunk 512]
+
+BDH-GPU (d=256, n=32768, h=4, L=6, RoPE), random-init weights, seeded random-byte
+streams. Every step trains the next ``chunk`` tokens of each stream with the recurrent
+state carried (detached) from the previous chunk — the fused forward takes the state as
+rho0 and returns the new one — and AdamW updates the weights. After a warm-up over one
+full stream, one full stream (stream / chunk steps) is timed with CUDA events; prints one
+JSON line (tokens/s over the batch).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from ..config import DragonConfig
+from ..models.state import ModelState
+from ..ops.gemm import check_errors
+from ..train.trainer import Trainer
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--stream", type=int, default=8192)
+    ap.add_argument("--chunk", type=int, default=512)
+    ap.add_argument("--layers", type=int, default=6)
+    a = ap.parse_args()
+    cfg = DragonConfig.bdh_gpu()
+    cfg.n_layer = a.layers
+    dev = torch.device("cuda", 0)
+    tr = Trainer(cfg, dev, lr=1e-3, weight_decay=0.0)
+    gen = torch.Generator().manual_seed(20260729)
+    data = torch.randint(0, 256, (a.batch, a.stream + 1), generator=gen).pin_memory()
+    steps = a.stream // a.chunk
+
+    def one_stream():
+        st = ModelState.empty()
+        loss = None
+        for k in range(steps):
+            s = k * a.chunk
+            loss = tr.step_stream(data[:, s:s + a.chunk], data[:, s + 1:s + a.chunk + 1], st)
+        return loss
+
+    one_stream()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    loss = one_stream()
+    e1.record()
+    torch.cuda.synchronize()
+    check_errors(dev)
+    ms = e0.elapsed_time(e1)
+    print(json.dumps({
+        "metric": "stateful TBPTT train tokens/s (device-timed) BDH-GPU",
+        "batch": a.batch, "stream": a.stream, "chunk": a.chunk, "steps": steps,
+        "tokens_per_s": round(a.batch * a.stream / (ms / 1e3), 1), "ms_per_chunk_step": round(ms / steps, 3),
+        "final_loss": float(loss),
+    }))
+
+
+if __name__ == "__main__":
+    main()
