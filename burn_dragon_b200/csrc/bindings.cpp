@@ -60,6 +60,8 @@ void reduce_adamw(std::vector<int64_t> grad, std::vector<int64_t> param, std::ve
                   const c10::optional<at::Tensor>& hyper);
 void tp_reduce_gather(const at::Tensor& slots, std::vector<int64_t> dst, int64_t rank, int64_t rows, int64_t M,
                       int64_t D, int64_t slot_stride);
+void tp_scatter_rows(const at::Tensor& src, std::vector<int64_t> slots, int64_t rank, int64_t rows, int64_t M,
+                     int64_t D, int64_t slot_stride);
 void reduce_mean(std::vector<int64_t> grad, std::vector<int64_t> flags, int64_t rank, int64_t lo, int64_t hi,
                  const at::Tensor& err);
 void percentile_thresholds(const at::Tensor& values, double q, const at::Tensor& out);
@@ -91,5 +93,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("reduce_adamw", &bd::reduce_adamw);
   m.def("reduce_mean", &bd::reduce_mean);
   m.def("tp_reduce_gather", &bd::tp_reduce_gather);
+  m.def("tp_scatter_rows", &bd::tp_scatter_rows);
   m.def("percentile_thresholds", &bd::percentile_thresholds);
 }

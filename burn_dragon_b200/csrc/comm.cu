@@ -186,6 +186,20 @@ __global__ void tp_reduce_gather_kernel(const float* __restrict__ slots, DstPtrs
   }
 }
 
+// Row scatter for a tensor-parallel sum of an [M, D] partial that is already in local
+// memory: row r goes to owner r / rows, into slot `rank` of that owner (P2P stores).
+__global__ void tp_scatter_rows_kernel(const float* __restrict__ src, DstPtrs slots, int rank, long long rows,
+                                       long long M, int D, long long slot_stride) {
+  const long long n4 = M * D / 4;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const long long e = 4 * i;
+    const long long r = e / D;
+    const int owner = (int)(r / rows);
+    const float4 x = *reinterpret_cast<const float4*>(src + e);
+    *reinterpret_cast<float4*>(slots.dst[owner] + rank * slot_stride + (r - owner * rows) * D + (e - r * D)) = x;
+  }
+}
+
 PeerPtrs make_ptrs(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
                    const std::vector<int64_t>& shadow, const std::vector<int64_t>& flags) {
   PeerPtrs pp;
@@ -286,6 +300,21 @@ void tp_reduce_gather(const at::Tensor& slots, std::vector<int64_t> dst, int64_t
   auto st = at::cuda::getCurrentCUDAStream(slots.get_device()).stream();
   tp_reduce_gather_kernel<<<148 * 2, 256, 0, st>>>(slots.data_ptr<float>(), dp, world, (int)rank, rows, valid,
                                                    (int)D, slot_stride);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void tp_scatter_rows(const at::Tensor& src, std::vector<int64_t> slots, int64_t rank, int64_t rows, int64_t M,
+                     int64_t D, int64_t slot_stride) {
+  const int world = (int)slots.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks && rows * world >= M, "1..8 ranks covering the rows");
+  TORCH_CHECK(src.scalar_type() == at::kFloat && src.is_contiguous() && src.numel() >= M * D && D % 4 == 0,
+              "fp32 contiguous [M, D] source, D % 4 == 0");
+  DstPtrs dp;
+  memset(&dp, 0, sizeof(dp));
+  for (int r = 0; r < world; ++r) dp.dst[r] = reinterpret_cast<float*>(slots[r]);
+  auto st = at::cuda::getCurrentCUDAStream(src.get_device()).stream();
+  tp_scatter_rows_kernel<<<148 * 2, 256, 0, st>>>(src.data_ptr<float>(), dp, (int)rank, rows, M, (int)D,
+                                                  slot_stride);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -372,7 +372,10 @@ class FusedBDH:
             dv_next = ws.dv[1] if dv is ws.dv[0] else ws.dv[0]
             if tp is not None:
                 mod.sum_rows(dv_next, None, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)
-                tp.all_reduce(dv_next)
+                if tp.peer is not None and tp.peer.M == M and tp.peer.D == D:
+                    tp.peer.all_reduce_rows(dv_next)  # P2P scatter / owner sum / P2P gather
+                else:
+                    tp.all_reduce(dv_next)
                 dv_next.add_(ws.dv_res)
             else:
                 mod.sum_rows(dv_next, ws.dv_res, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)

@@ -33,6 +33,9 @@ def hybrid_layout(world: int, tp: int) -> tuple[list[list[int]], list[list[int]]
 class PeerSum:
     """The per-layer decoder sum of tensor parallelism over NVLink peer memory.
 
+    Backward: the residual-gradient partials are summed the same way (``all_reduce_rows``:
+    row scatter by P2P stores, owner sums, all-gather by P2P stores).
+
     The decoder GEMM of every rank stores each output row straight into the slot of the
     rank that owns that row (``EPI_F32_SCATTER``: the reduce-scatter happens in the
     GEMM epilogue, tile by tile, while the tensor cores keep running); after a peer
@@ -54,7 +57,8 @@ class PeerSum:
         self.tp, self.M, self.D, self.L = tp, M, D, L
         self.rows = M // W
         self.dev = device.index if device.index is not None else torch.cuda.current_device()
-        sizes = {"slots": W * self.rows * D * 4, "sum": L * M * D * 4, "flags": self.FLAG_WORDS * 4}
+        sizes = {"slots": W * self.rows * D * 4, "sum": L * M * D * 4, "bsum": M * D * 4,
+                 "flags": self.FLAG_WORDS * 4}
         self._own = {k: mod.sym_alloc(b, self.dev) for k, b in sizes.items()}
         handles = {k: mod.ipc_handle(v, self.dev) for k, v in self._own.items()}
         gathered: list = [None] * W
@@ -72,6 +76,7 @@ class PeerSum:
         self.slots = mod.wrap_ptr(self._own["slots"], W * self.rows * D, 0, self.dev)
         sums = mod.wrap_ptr(self._own["sum"], L * M * D, 0, self.dev).view(L, M, D)
         self.sum_views = [sums[l] for l in range(L)]
+        self.bsum = mod.wrap_ptr(self._own["bsum"], M * D, 0, self.dev).view(M, D)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         dist.barrier(group=tp.group)
 
@@ -95,6 +100,20 @@ class PeerSum:
         dst = [b + layer * self.M * self.D * 4 for b in base]
         _ext.load().tp_reduce_gather(self.slots, dst, self.tp.rank, self.rows, self.M, self.D, self.rows * self.D)
         self._barrier(1)
+
+    def all_reduce_rows(self, t: torch.Tensor) -> None:
+        """In-place sum over the group of a local fp32 [M, D] tensor (the backward's
+        residual-gradient partials): rows scattered to their owners by P2P stores, owners
+        sum and all-gather into the symmetric ``bsum`` buffer, then copied back."""
+        from .. import _ext
+
+        mod = _ext.load()
+        mod.tp_scatter_rows(t, self.ptrs["slots"], self.tp.rank, self.rows, self.M, self.D, self.rows * self.D)
+        self._barrier(0)
+        mod.tp_reduce_gather(self.slots, self.ptrs["bsum"], self.tp.rank, self.rows, self.M, self.D,
+                             self.rows * self.D)
+        self._barrier(1)
+        t.view(self.M, self.D).copy_(self.bsum)
 
     def check(self) -> None:
         if int(self.err.item()):
