@@ -586,10 +586,13 @@ class TrainingSection:
 
 @dataclass
 class DatasetConfig:
+    # synthetic_bytes | file (a byte file) | jsonl | parquet | text (a corpus tokenised
+    # once into cache_dir, then read like a file)
     type: str = "synthetic_bytes"
     cache_dir: str = "data"
     train_split_ratio: float = 0.9
     path: str | None = None
+    text_field: str = "text"
 
 
 @dataclass

@@ -1,0 +1,84 @@
+"""Text corpora -> a prepared byte-token file the loaders read.
+
+The reference reads Hugging Face corpora (parquet / jsonl shards) and prepared token
+chunks (burn_dragon_language/src/dataset/{huggingface,prepared_chunks}.rs). Here a
+corpus directory or file of ``.jsonl`` (one JSON object per line, text under
+``text_field``), ``.parquet`` (a ``text_field`` column, read with pyarrow) or ``.txt``
+documents is tokenised once — UTF-8 bytes, documents separated by ``separator`` — into
+``<cache_dir>/<name>.bin`` (uint8, the byte vocabulary of the BDH configurations), with
+a ``.json`` manifest of the source files, sizes and modification times. A matching
+manifest makes later runs reuse the file. The training loop then reads windows of it
+(``dataset.type = "file"`` semantics: memory-mapped, train / valid split by ratio).
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+
+import numpy as np
+
+
+def _files(path: str) -> list[str]:
+    if os.path.isfile(path):
+        return [path]
+    out = []
+    for root, _, names in os.walk(path):
+        for n in sorted(names):
+            if n.endswith((".jsonl", ".parquet", ".txt")):
+                out.append(os.path.join(root, n))
+    return sorted(out)
+
+
+def _documents(f: str, text_field: str):
+    if f.endswith(".jsonl"):
+        with open(f, encoding="utf-8") as fh:
+            for line in fh:
+                line = line.strip()
+                if line:
+                    t = json.loads(line).get(text_field)
+                    if isinstance(t, str):
+                        yield t
+    elif f.endswith(".parquet"):
+        import pyarrow.parquet as pq
+
+        for batch in pq.ParquetFile(f).iter_batches(columns=[text_field]):
+            for t in batch.column(0).to_pylist():
+                if isinstance(t, str):
+                    yield t
+    else:
+        with open(f, encoding="utf-8", errors="replace") as fh:
+            yield fh.read()
+
+
+def prepare_corpus(path: str, cache_dir: str, text_field: str = "text", separator: bytes = b"\n\n") -> str:
+    """Tokenise the corpus at ``path`` into a byte file; returns its path."""
+    files = _files(path)
+    if not files:
+        raise FileNotFoundError(f"no .jsonl / .parquet / .txt files under {path}")
+    sig = [[f, os.path.getsize(f), int(os.path.getmtime(f))] for f in files]
+    key = hashlib.sha256(json.dumps([sig, text_field, separator.hex()]).encode()).hexdigest()[:16]
+    os.makedirs(cache_dir, exist_ok=True)
+    out = os.path.join(cache_dir, f"corpus-{key}.bin")
+    man = out[:-4] + ".json"
+    if os.path.exists(out) and os.path.exists(man):
+        return out
+    tmp = out + ".tmp"
+    n_docs = 0
+    with open(tmp, "wb") as fh:
+        for f in files:
+            for doc in _documents(f, text_field):
+                if n_docs:
+                    fh.write(separator)
+                fh.write(doc.encode("utf-8"))
+                n_docs += 1
+    os.replace(tmp, out)
+    with open(man, "w") as fh:
+        json.dump({"sources": sig, "text_field": text_field, "documents": n_docs,
+                   "bytes": os.path.getsize(out), "vocab": "bytes"}, fh, indent=2)
+    return out
+
+
+def corpus_bytes(path: str) -> np.ndarray:
+    return np.memmap(path, dtype=np.uint8, mode="r")

@@ -74,6 +74,15 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         # the residual stream is replicated across the tensor-parallel group; the sum is an
         # all-reduce of [M, D] per layer (a reduce-scatter + all-gather moves the same bytes)
         pass
+    if cfg.dataset.type in ("jsonl", "parquet", "text"):
+        from .datasets import prepare_corpus
+
+        if rank == 0:
+            prepared = prepare_corpus(cfg.dataset.path, cfg.dataset.cache_dir, cfg.dataset.text_field)
+        if world > 1 and dist.is_initialized():
+            dist.barrier()
+        prepared = prepare_corpus(cfg.dataset.path, cfg.dataset.cache_dir, cfg.dataset.text_field)
+        cfg.dataset.type, cfg.dataset.path = "file", prepared
     if t.auto_batch_size.enabled:
         from .autotune import choose_batch_size
 

@@ -1,0 +1,40 @@
+"""Text corpora (jsonl / parquet / txt) prepared into a byte file and trained on (CPU)."""
+
+import json
+import os
+
+import numpy as np
+
+from burn_dragon_b200.cli.train import main
+from burn_dragon_b200.train.datasets import corpus_bytes, prepare_corpus
+
+CFG = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu.toml")
+
+
+def test_prepare_jsonl_parquet_and_cache(tmp_path):
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    src = tmp_path / "corpus"
+    src.mkdir()
+    (src / "a.jsonl").write_text("\n".join(json.dumps({"text": t, "id": i}) for i, t in enumerate(["héllo", "world"])))
+    pq.write_table(pa.table({"text": ["third doc"]}), src / "b.parquet")
+    out = prepare_corpus(str(src), str(tmp_path / "cache"))
+    data = bytes(corpus_bytes(out))
+    assert data == "héllo\n\nworld\n\nthird doc".encode()
+    man = json.load(open(out[:-4] + ".json"))
+    assert man["documents"] == 3 and man["bytes"] == len(data)
+    mtime = os.path.getmtime(out)
+    assert prepare_corpus(str(src), str(tmp_path / "cache")) == out and os.path.getmtime(out) == mtime
+
+
+def test_training_on_a_text_corpus(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    src = tmp_path / "c.jsonl"
+    rng = np.random.default_rng(0)
+    src.write_text("\n".join(json.dumps({"body": "abc " * int(rng.integers(50, 200))}) for _ in range(40)))
+    main(["--config", CFG, "--set", 'dataset.type="jsonl"', "--set", f'dataset.path="{src}"',
+          "--set", f'dataset.cache_dir="{tmp_path / "cache"}"', "--set", 'dataset.text_field="body"',
+          "--set", "training.max_iters=4", "--set", "training.block_size=64", "--run-name", "txt"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None and res["final_loss"] < 5.5  # "abc " is far below ln 256
