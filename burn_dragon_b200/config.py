@@ -593,6 +593,7 @@ class DatasetConfig:
     train_split_ratio: float = 0.9
     path: str | None = None
     text_field: str = "text"
+    tokenizer: str | None = None  # a tokenizer.json (BPE) for jsonl / parquet / text corpora
 
 
 @dataclass

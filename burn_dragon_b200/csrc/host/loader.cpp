@@ -6,8 +6,9 @@
 //   random  uniform tokens from a counter-based generator: token (b, t) of step s for
 //           rank r is a pure function of (seed, s, r, b, t) (SplitMix64 finaliser over a
 //           Weyl sequence), so batches do not depend on thread scheduling
-//   file    windows of T + 1 bytes of a memory-mapped byte file (a train / valid split at
-//           `ratio`), window starts drawn from the same counter-based generator
+//   file    windows of T + 1 tokens of a memory-mapped token file — uint8 (bytes) or
+//           little-endian uint16 (a BPE vocabulary) — split train / valid at `ratio`,
+//           window starts drawn from the same counter-based generator
 //   stream  consecutive chunks of `batch` independent streams (stateful TBPTT): stream b
 //           of the split is the contiguous range [b * len, (b + 1) * len); chunk k covers
 //           positions [k * chunk, k * chunk + chunk + 1) and wraps to 0 at the end
@@ -51,10 +52,11 @@ class Loader {
  public:
   Loader(const std::string& mode, const std::string& path, int64_t batch, int64_t block, int64_t vocab,
          int64_t seed, int64_t rank, int64_t world, double ratio, bool valid_split, int64_t chunk,
-         std::vector<at::Tensor> buffers, int64_t workers, int64_t start_step)
-      : mode_(mode), batch_(batch), block_(block), vocab_(vocab), seed_(seed), rank_(rank), world_(world),
+         std::vector<at::Tensor> buffers, int64_t workers, int64_t start_step, int64_t elem_bytes)
+      : esize_(elem_bytes), mode_(mode), batch_(batch), block_(block), vocab_(vocab), seed_(seed), rank_(rank), world_(world),
         chunk_(chunk), bufs_(std::move(buffers)), next_issue_(start_step), next_take_(start_step) {
     if (mode_ != "random" && mode_ != "file" && mode_ != "stream") throw std::invalid_argument("unknown mode " + mode_);
+    if (esize_ != 1 && esize_ != 2) throw std::invalid_argument("token files hold 1- or 2-byte tokens");
     if (batch_ <= 0 || block_ <= 0 || bufs_.empty()) throw std::invalid_argument("batch, block > 0 and >= 1 buffer");
     for (auto& b : bufs_) {
       TORCH_CHECK(b.scalar_type() == at::kLong && b.is_contiguous() && !b.is_cuda(), "buffers: contiguous int64 host");
@@ -121,14 +123,21 @@ class Loader {
     map_ = map_len_ ? mmap(nullptr, map_len_, PROT_READ, MAP_PRIVATE, fd, 0) : nullptr;
     ::close(fd);
     if (map_ == MAP_FAILED) throw std::runtime_error("mmap failed for " + path);
-    const size_t cut = (size_t)((double)map_len_ * ratio);
-    base_ = static_cast<const uint8_t*>(map_) + (valid_split ? cut : 0);
-    split_len_ = valid_split ? map_len_ - cut : cut;
+    const size_t n = map_len_ / (size_t)esize_;  // tokens in the file
+    const size_t cut = (size_t)((double)n * ratio);
+    base_ = static_cast<const uint8_t*>(map_) + (valid_split ? cut : 0) * (size_t)esize_;
+    split_len_ = valid_split ? n - cut : cut;
     if (mode_ == "file" && split_len_ <= (size_t)block_ + 1) throw std::runtime_error("split shorter than a window");
     if (mode_ == "stream") {
       stream_len_ = split_len_ / (size_t)batch_;
       if (chunk_ <= 0 || stream_len_ < (size_t)chunk_ + 1) throw std::runtime_error("streams shorter than a chunk");
     }
+  }
+
+  // token i of the split
+  inline int64_t tok(size_t i) const {
+    if (esize_ == 1) return base_[i];
+    return (int64_t)base_[2 * i] | ((int64_t)base_[2 * i + 1] << 8);
   }
 
   int find_ready(int64_t step) const {
@@ -148,14 +157,14 @@ class Loader {
       const uint64_t span = split_len_ - (size_t)W;
       for (int64_t b = 0; b < batch_; ++b) {
         const uint64_t s = draw(seed_, (uint64_t)step, (uint64_t)(rank_ + world_ * 7919), (uint64_t)b) % span;
-        for (int64_t t = 0; t < W; ++t) out[b * W + t] = base_[s + t];
+        for (int64_t t = 0; t < W; ++t) out[b * W + t] = tok(s + (size_t)t);
       }
     } else {  // stream
       const int64_t per = (int64_t)((stream_len_ - 1) / (size_t)chunk_);  // whole chunks per stream
       const int64_t k = step % per;
       for (int64_t b = 0; b < batch_; ++b) {
-        const uint8_t* src = base_ + (size_t)b * stream_len_ + (size_t)(k * chunk_);
-        for (int64_t t = 0; t < W; ++t) out[b * W + t] = src[t];
+        const size_t s0 = (size_t)b * stream_len_ + (size_t)(k * chunk_);
+        for (int64_t t = 0; t < W; ++t) out[b * W + t] = tok(s0 + (size_t)t);
       }
     }
   }
@@ -187,6 +196,7 @@ class Loader {
     }
   }
 
+  int64_t esize_;
   std::string mode_;
   int64_t batch_, block_, vocab_, seed_, rank_, world_, chunk_;
   std::vector<at::Tensor> bufs_;
@@ -209,7 +219,7 @@ class Loader {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   pybind11::class_<Loader>(m, "Loader")
       .def(pybind11::init<const std::string&, const std::string&, int64_t, int64_t, int64_t, int64_t, int64_t,
-                          int64_t, double, bool, int64_t, std::vector<at::Tensor>, int64_t, int64_t>())
+                          int64_t, double, bool, int64_t, std::vector<at::Tensor>, int64_t, int64_t, int64_t>())
       .def("take", &Loader::take, pybind11::call_guard<pybind11::gil_scoped_release>())
       .def("release", &Loader::release)
       .def("split_len", &Loader::split_len)

@@ -57,14 +57,19 @@ class StreamingBytes:
 
 
 class FileBytes:
-    """Random [B, T+1] windows of a byte file (memory-mapped), split into train / valid
-    by ``train_split_ratio`` (the reference's file-backed corpora, dataset/mod.rs)."""
+    """Random [B, T+1] windows of a token file (memory-mapped; uint8 bytes, or uint16 ids
+    when ``token_bytes`` = 2), split into train / valid by ``train_split_ratio`` (the
+    reference's file-backed corpora, dataset/mod.rs)."""
 
     def __init__(self, path: str, batch: int, block: int, split: str = "train", ratio: float = 0.9,
-                 seed: int = 1337, rank: int = 0, world: int = 1):
+                 seed: int = 1337, rank: int = 0, world: int = 1, token_bytes: int | None = None):
         import numpy as np
 
-        data = np.memmap(path, dtype=np.uint8, mode="r")
+        if token_bytes is None:
+            from .datasets import token_bytes as tb
+
+            token_bytes = tb(path)
+        data = np.memmap(path, dtype=np.uint8 if token_bytes == 1 else np.dtype("<u2"), mode="r")
         cut = int(len(data) * ratio)
         self.data = data[:cut] if split == "train" else data[cut:]
         if len(self.data) <= block + 1:

@@ -78,10 +78,12 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         from .datasets import prepare_corpus
 
         if rank == 0:
-            prepared = prepare_corpus(cfg.dataset.path, cfg.dataset.cache_dir, cfg.dataset.text_field)
+            prepare_corpus(cfg.dataset.path, cfg.dataset.cache_dir, cfg.dataset.text_field,
+                           tokenizer=cfg.dataset.tokenizer)
         if world > 1 and dist.is_initialized():
             dist.barrier()
-        prepared = prepare_corpus(cfg.dataset.path, cfg.dataset.cache_dir, cfg.dataset.text_field)
+        prepared = prepare_corpus(cfg.dataset.path, cfg.dataset.cache_dir, cfg.dataset.text_field,
+                                  tokenizer=cfg.dataset.tokenizer)
         cfg.dataset.type, cfg.dataset.path = "file", prepared
     if t.auto_batch_size.enabled:
         from .autotune import choose_batch_size
@@ -181,9 +183,12 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
             from .native_data import NativeBytes
 
             if cfg.dataset.type == "file":
+                from .datasets import token_bytes
+
                 native = NativeBytes("file", t.batch_size, t.block_size, path=cfg.dataset.path, seed=t.seed,
                                      rank=data_rank, world=data_world, ratio=cfg.dataset.train_split_ratio,
-                                     workers=t.loader_workers, start_step=start)
+                                     workers=t.loader_workers, start_step=start,
+                                     token_bytes=token_bytes(cfg.dataset.path))
             else:
                 native = NativeBytes("random", t.batch_size, t.block_size, seed=t.seed, rank=data_rank,
                                      world=data_world, vocab=cfg.model.vocab_size, workers=t.loader_workers,

@@ -33,7 +33,9 @@ def _load():
 class NativeBytes:
     def __init__(self, mode: str, batch: int, block: int, *, path: str = "", vocab: int = 256, seed: int = 1337,
                  rank: int = 0, world: int = 1, split: str = "train", ratio: float = 0.9, chunk: int = 0,
-                 depth: int = 4, workers: int = 2, start_step: int = 0, pin: bool | None = None):
+                 depth: int = 4, workers: int = 2, start_step: int = 0, pin: bool | None = None,
+                 token_bytes: int = 1):
+        """``token_bytes``: 1 for byte files, 2 for uint16 token files (BPE vocabularies)."""
         mod = _load()
         if mode == "stream" and chunk <= 0:
             raise ValueError("stream mode needs chunk > 0")
@@ -42,7 +44,7 @@ class NativeBytes:
         self.bufs = [torch.empty(batch, width, dtype=torch.int64, pin_memory=pin) for _ in range(max(2, depth))]
         self.width = width
         self._l = mod.Loader(mode, path, batch, width - 1, vocab, seed, rank, world, ratio, split == "valid",
-                             chunk, self.bufs, workers, start_step)
+                             chunk, self.bufs, workers, start_step, token_bytes)
         self.mode = mode
         self._held: int | None = None
         self._event = None

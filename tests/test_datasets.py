@@ -38,3 +38,33 @@ def test_training_on_a_text_corpus(tmp_path, monkeypatch, capsys):
           "--set", "training.max_iters=4", "--set", "training.block_size=64", "--run-name", "txt"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res["final_loss"] is not None and res["final_loss"] < 5.5  # "abc " is far below ln 256
+
+
+def test_bpe_corpus_uint16_tokens_through_both_loaders(tmp_path):
+    import torch
+
+    from burn_dragon_b200.train.data import FileBytes
+    from burn_dragon_b200.train.datasets import token_bytes
+    from burn_dragon_b200.train.native_data import NativeBytes
+    from burn_dragon_b200.utils.tokenizer import BPETokenizer
+
+    texts = ["the cat sat on the mat " * 20, "the dog sat on the log " * 20]
+    tok = BPETokenizer().train(texts, 300)
+    tp = tmp_path / "tokenizer.json"
+    tp.write_text(json.dumps(tok.to_json()))
+    src = tmp_path / "c.txt"
+    src.write_text(texts[0] + texts[1])
+    out = prepare_corpus(str(src), str(tmp_path / "cache"), tokenizer=str(tp))
+    assert token_bytes(out) == 2
+    ids = np.fromfile(out, dtype="<u2")
+    assert ids.max() >= 256 and ids.tolist() == tok.encode(texts[0] + texts[1])
+    fb = FileBytes(out, 2, 8, ratio=1.0)
+    x, y = fb.next()
+    assert int(x.max()) < 300 and torch.equal(x[:, 1:], y[:, :-1])
+    nb = NativeBytes("file", 2, 8, path=out, ratio=1.0, token_bytes=2)
+    x2, _ = nb.next()
+    nb.close()
+    # every native window is a run of consecutive ids of the file
+    flat = ids.tolist()
+    for row in x2.tolist():
+        assert any(flat[i:i + 8] == row for i in range(len(flat) - 8))
