@@ -1,4 +1,5 @@
-"""Generation CLI: load a run's newest checkpoint and continue byte prompts.
+"""Generation CLI: load a run's newest checkpoint and continue prompts, encoded and
+decoded with the run's ``tokenizer.json`` (bytes or BPE).
 
   python -m burn_dragon_b200.cli.generate --run runs/cuda/NAME --prompt "hello" [--max-tokens 64]
          [--temperature 0.8 --top-k 40] [--batch 1]
@@ -15,6 +16,7 @@ from ..config import training_config_from_dict
 from ..models.bdh import BDH
 from ..models.generate import Generator
 from ..train.checkpoint import RunDir
+from ..utils.tokenizer import load_tokenizer
 
 
 def main(argv=None) -> None:
@@ -33,11 +35,13 @@ def main(argv=None) -> None:
     model = BDH(cfg.model, device=dev)
     if run.latest() is not None:
         run.load(None, model)
-    prompt = list(a.prompt.encode()) or [0]
+    tp = os.path.join(a.run, "tokenizer.json")
+    tok = load_tokenizer(tp) if os.path.exists(tp) else load_tokenizer({"type": "byte"})
+    prompt = tok.encode(a.prompt) or [0]
     x = torch.tensor([prompt] * a.batch, dtype=torch.long, device=dev)
     out = Generator(model).generate(x, a.max_tokens, temperature=a.temperature, top_k=a.top_k, seed=a.seed)
     for row in out.tolist():
-        print(bytes(prompt + row).decode("utf-8", errors="replace"))
+        print(tok.decode(prompt + row))
 
 
 if __name__ == "__main__":

@@ -167,7 +167,12 @@ class RunDir:
             "state_layout": {"rho": "[B, H, Nh, D] fp32 per layer"},
         })
         self.write_json("training_config.json", train_cfg)
-        self.write_json("tokenizer.json", {"type": "byte", "vocab_size": train_cfg.model.vocab_size})
+        tok = getattr(train_cfg.dataset, "tokenizer", None)
+        if tok:
+            with open(tok) as f:
+                self.write_json("tokenizer.json", json.load(f))
+        else:
+            self.write_json("tokenizer.json", {"type": "byte", "vocab_size": train_cfg.model.vocab_size})
 
     # ---- checkpoints
     def _p(self, kind: str, step: int) -> str:

@@ -73,7 +73,7 @@ class FileBytes:
         cut = int(len(data) * ratio)
         self.data = data[:cut] if split == "train" else data[cut:]
         if len(self.data) <= block + 1:
-            raise ValueError(f"{path}: {split} split has only {len(self.data)} bytes for block {block}")
+            raise ValueError(f"{path}: {split} split has only {len(self.data)} tokens for block {block}")
         self.batch, self.block = batch, block
         self.seed, self.rank, self.world = seed, rank, world
         self.step = 0

@@ -68,3 +68,24 @@ def test_bpe_corpus_uint16_tokens_through_both_loaders(tmp_path):
     flat = ids.tolist()
     for row in x2.tolist():
         assert any(flat[i:i + 8] == row for i in range(len(flat) - 8))
+
+
+def test_bpe_run_then_generate_cli(tmp_path, monkeypatch, capsys):
+    from burn_dragon_b200.cli.generate import main as gen_main
+    from burn_dragon_b200.utils.tokenizer import BPETokenizer
+
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    texts = ["hello there friend " * 30]
+    tok = BPETokenizer().train(texts, 280)
+    tp = tmp_path / "tokenizer.json"
+    tp.write_text(json.dumps(tok.to_json()))
+    src = tmp_path / "c.txt"
+    src.write_text(" ".join(f"{texts[0]} {i}" for i in range(40)))
+    main(["--config", CFG, "--set", 'dataset.type="text"', "--set", f'dataset.path="{src}"',
+          "--set", f'dataset.cache_dir="{tmp_path / "cache"}"', "--set", f'dataset.tokenizer="{tp}"',
+          "--set", "model.vocab_size=288", "--set", "training.max_iters=2", "--set", "training.block_size=32",
+          "--set", "training.checkpoint_interval_iters=2", "--run-name", "bpe"])
+    run_dir = json.loads(capsys.readouterr().out.strip().splitlines()[-1])["run_dir"]
+    assert json.load(open(os.path.join(run_dir, "tokenizer.json")))["type"] == "bpe"
+    gen_main(["--run", run_dir, "--prompt", "hello there", "--max-tokens", "5"])
+    assert capsys.readouterr().out.startswith("hello there")
