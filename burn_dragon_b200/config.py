@@ -554,6 +554,27 @@ class NeuronScalingConfig:
 
 
 @dataclass
+class CausalInputCorruptionConfig:
+    """Replace input tokens (never targets) at a ramped probability (schema.rs:321-339)."""
+
+    enabled: bool = False
+    probability: float = 0.0
+    warmup_steps: int = 0
+    ramp_steps: int = 0
+    replacement_token_id: int | None = None
+
+    def probability_at(self, step: int) -> float:
+        """0 before warm-up, then linear over ``ramp_steps`` to ``probability``
+        (burn_dragon_language/src/train/steps.rs:3368-3388)."""
+        p = min(max(self.probability, 0.0), 1.0)
+        if not self.enabled or p <= 1.1920929e-07 or step < self.warmup_steps:
+            return 0.0
+        if self.ramp_steps == 0:
+            return p
+        return p * min(max((step - self.warmup_steps + 1) / self.ramp_steps, 0.0), 1.0)
+
+
+@dataclass
 class TrainingSection:
     block_size: int = 512
     batch_size: int = 32
@@ -569,6 +590,7 @@ class TrainingSection:
     continual_backprop: ContinualBackpropConfig = field(default_factory=ContinualBackpropConfig)
     auto_batch_size: AutoBatchSizeConfig = field(default_factory=AutoBatchSizeConfig)
     neuron_scaling: NeuronScalingConfig = field(default_factory=NeuronScalingConfig)
+    input_corruption: CausalInputCorruptionConfig = field(default_factory=CausalInputCorruptionConfig)
     # batches from the native prefetching loader (csrc/host/loader.cpp) instead of the
     # Python generators
     native_loader: bool = True

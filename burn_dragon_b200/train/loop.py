@@ -240,6 +240,10 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
             else:
                 x, y = data.next()
             prof.stop("dataloader")
+            if t.input_corruption.enabled:
+                from .corruption import corrupt_inputs
+
+                x = corrupt_inputs(x, t.input_corruption, step, cfg.model.vocab_size, t.seed, rank)
             t0 = time.perf_counter()
             prof.start("forward_backward")
             if runner is not None:

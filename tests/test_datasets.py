@@ -89,3 +89,21 @@ def test_bpe_run_then_generate_cli(tmp_path, monkeypatch, capsys):
     assert json.load(open(os.path.join(run_dir, "tokenizer.json")))["type"] == "bpe"
     gen_main(["--run", run_dir, "--prompt", "hello there", "--max-tokens", "5"])
     assert capsys.readouterr().out.startswith("hello there")
+
+
+def test_causal_input_corruption_schedule_and_targets():
+    import torch
+
+    from burn_dragon_b200.config import CausalInputCorruptionConfig
+    from burn_dragon_b200.train.corruption import corrupt_inputs
+
+    c = CausalInputCorruptionConfig(enabled=True, probability=0.5, warmup_steps=2, ramp_steps=4)
+    assert [c.probability_at(s) for s in (0, 1, 2, 3, 5, 9)] == [0.0, 0.0, 0.125, 0.25, 0.5, 0.5]
+    x = torch.arange(4000).reshape(40, 100) % 200 + 10
+    assert torch.equal(corrupt_inputs(x, c, 0, 256), x)
+    y = corrupt_inputs(x, c, 9, 256, seed=1)
+    frac = float((y != x).float().mean())
+    assert 0.4 < frac < 0.52  # a random replacement can equal the original token
+    c.replacement_token_id = 0
+    z = corrupt_inputs(x, c, 9, 256, seed=1)
+    assert set(z[z != x].tolist()) == {0} and torch.equal(z, corrupt_inputs(x, c, 9, 256, seed=1))
