@@ -169,8 +169,15 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         if rt and rt.get("rhos") is not None and not extended:
             state = ModelState(rt["rhos"], int(rt.get("position", 0)))
     if start == 0 and t.init_checkpoint_path:
+        target = trainer.core if extended else trainer.model
+        fresh = {n: getattr(target, n).detach().clone() for n in target.store.shapes}
         src = C.RunDir(t.init_checkpoint_path)
-        src.load(None, trainer.core if extended else trainer.model, None, device=dev)
+        src.load(None, target, None, device=dev)
+        if t.init_transfer:
+            from ..config import _fill
+            from .init_transfer import InitTransferConfig, apply_init_transfer
+
+            apply_init_transfer(target, fresh, _fill(InitTransferConfig, dict(t.init_transfer), {}, ""), device=dev)
     streaming = t.sequence_batching == "streaming" or t.tbptt_persist_across_steps
     data_rank = 0 if mode in ("tensor_parallel_neuron", "pipeline") else rank
     data_world = 1 if mode in ("tensor_parallel_neuron", "pipeline") else world
