@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import tomllib
 
 from ..config import load_training_config
 
@@ -23,7 +24,10 @@ def parse_set(items: list[str]) -> dict:
         try:
             val = json.loads(raw)
         except json.JSONDecodeError:
-            val = raw
+            try:  # a TOML value: inline tables / arrays of tables, single-quoted strings
+                val = tomllib.loads("v = " + raw)["v"]
+            except tomllib.TOMLDecodeError:
+                val = raw
         d = out
         parts = key.split(".")
         for p in parts[:-1]:

@@ -591,7 +591,9 @@ class TrainingSection:
     auto_batch_size: AutoBatchSizeConfig = field(default_factory=AutoBatchSizeConfig)
     neuron_scaling: NeuronScalingConfig = field(default_factory=NeuronScalingConfig)
     input_corruption: CausalInputCorruptionConfig = field(default_factory=CausalInputCorruptionConfig)
-    init_transfer: dict[str, Any] = field(default_factory=dict)  # train.init_transfer.InitTransferConfig keys
+    init_transfer: dict[str, Any] = field(default_factory=dict)
+    # [{target, scale, schedule = {final_scale, start_fraction, end_fraction}}] (train.module_lr)
+    module_lr_scales: list[dict[str, Any]] = field(default_factory=list)  # train.init_transfer.InitTransferConfig keys
     # batches from the native prefetching loader (csrc/host/loader.cpp) instead of the
     # Python generators
     native_loader: bool = True

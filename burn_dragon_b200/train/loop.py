@@ -133,6 +133,13 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         from .neuron_scaling import NeuronScaler
 
         scaler = NeuronScaler(t.neuron_scaling)
+    mlr = None
+    if t.module_lr_scales:
+        if extended or mode not in ("single", "ddp", "fsdp") or getattr(trainer, "comm", None) is not None:
+            raise ValueError("module_lr_scales needs the plain BDH model without the NVLink communicator")
+        from .module_lr import ModuleLrScales
+
+        mlr = ModuleLrScales(t.module_lr_scales, t.max_iters)
     objective = None
     if t.objective.get("type", "next_token") != "next_token":
         from . import objectives as OBJ
@@ -293,12 +300,16 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
             else:
                 if scaler is not None:
                     scaler.before_step(trainer.model, step)
+                if mlr is not None:
+                    mlr.before_step(trainer.model, step)
                 sample = cbp is not None and cbp.should_sample()
                 if sample and not getattr(trainer, "fused", False):
                     cbp.record_reference(trainer.model, x.to(dev))
                 loss = trainer.step(x, y)
                 if scaler is not None:
                     scaler.after_step(step)
+                if mlr is not None:
+                    mlr.after_step(step)
                 prof.stop("forward_backward")
                 if cbp is not None:
                     if sample and getattr(trainer, "fused", False):
