@@ -554,6 +554,66 @@ class NeuronScalingConfig:
 
 
 @dataclass
+class LogitEntropyFloorConfig:
+    """Entropy / marginal-entropy floors and target coverage on the predicted
+    distribution (schema.rs:340-371)."""
+
+    enabled: bool = False
+    weight: float = 0.0
+    target_entropy_bits: float = 0.0
+    marginal_weight: float = 0.0
+    target_marginal_entropy_bits: float = 0.0
+    target_coverage_weight: float = 0.0
+    target_coverage_epsilon: float = 1e-8
+    warmup_steps: int = 0
+    ramp_steps: int = 0
+    every_steps: int = 1
+
+    def validate(self) -> None:
+        if not self.enabled:
+            return
+        for k in ("weight", "marginal_weight", "target_coverage_weight", "target_entropy_bits",
+                  "target_marginal_entropy_bits"):
+            v = getattr(self, k)
+            if not (v >= 0.0 and v != float("inf")):
+                raise ValueError(f"training.logit_entropy_floor.{k} must be finite and >= 0")
+        if not 0.0 < self.target_coverage_epsilon < 1.0:
+            raise ValueError("training.logit_entropy_floor.target_coverage_epsilon must be finite and in (0, 1)")
+        if self.every_steps == 0:
+            raise ValueError("training.logit_entropy_floor.every_steps must be > 0")
+
+
+@dataclass
+class RepeatUnlikelihoodConfig:
+    """Unlikelihood of repeating recent input tokens (schema.rs:372-407)."""
+
+    enabled: bool = False
+    weight: float = 0.0
+    cycle_weight: float = 0.0
+    cycle_margin_weight: float = 0.0
+    cycle_margin: float = 0.0
+    cycle_min_lag: int = 2
+    cycle_max_lag: int = 64
+    cycle_lags_per_step: int = 8
+    warmup_steps: int = 0
+    ramp_steps: int = 0
+    every_steps: int = 1
+    history_lags: list[int] = field(default_factory=list)
+    epsilon: float = 1e-4
+
+    def validate(self) -> None:
+        if not self.enabled:
+            return
+        for k in ("weight", "cycle_weight", "cycle_margin_weight"):
+            if not getattr(self, k) >= 0.0:
+                raise ValueError(f"training.repeat_unlikelihood.{k} must be finite and >= 0")
+        if not 0.0 < self.epsilon < 1.0:
+            raise ValueError("training.repeat_unlikelihood.epsilon must be in (0, 1)")
+        if self.every_steps == 0:
+            raise ValueError("training.repeat_unlikelihood.every_steps must be > 0")
+
+
+@dataclass
 class CausalInputCorruptionConfig:
     """Replace input tokens (never targets) at a ramped probability (schema.rs:321-339)."""
 
@@ -593,7 +653,9 @@ class TrainingSection:
     input_corruption: CausalInputCorruptionConfig = field(default_factory=CausalInputCorruptionConfig)
     init_transfer: dict[str, Any] = field(default_factory=dict)
     # [{target, scale, schedule = {final_scale, start_fraction, end_fraction}}] (train.module_lr)
-    module_lr_scales: list[dict[str, Any]] = field(default_factory=list)  # train.init_transfer.InitTransferConfig keys
+    module_lr_scales: list[dict[str, Any]] = field(default_factory=list)
+    logit_entropy_floor: LogitEntropyFloorConfig = field(default_factory=LogitEntropyFloorConfig)
+    repeat_unlikelihood: RepeatUnlikelihoodConfig = field(default_factory=RepeatUnlikelihoodConfig)  # train.init_transfer.InitTransferConfig keys
     # batches from the native prefetching loader (csrc/host/loader.cpp) instead of the
     # Python generators
     native_loader: bool = True

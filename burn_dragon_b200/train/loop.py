@@ -140,6 +140,16 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         from .module_lr import ModuleLrScales
 
         mlr = ModuleLrScales(t.module_lr_scales, t.max_iters)
+    regs = None
+    if t.logit_entropy_floor.enabled or t.repeat_unlikelihood.enabled:
+        t.logit_entropy_floor.validate()
+        t.repeat_unlikelihood.validate()
+        if extended or pc or mode not in ("single", "ddp", "fsdp") or getattr(trainer, "comm", None) is not None:
+            raise ValueError("logit_entropy_floor / repeat_unlikelihood need the plain BDH model without the "
+                             "NVLink communicator")
+        from .logit_regularizers import LogitRegularizers
+
+        regs = LogitRegularizers(t.logit_entropy_floor, t.repeat_unlikelihood)
     objective = None
     if t.objective.get("type", "next_token") != "next_token":
         from . import objectives as OBJ
@@ -273,19 +283,18 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 prof.stop("forward_backward")
             elif objective is not None:
                 from . import objectives as OBJ
-                from .optim import lr_at
 
                 oc, teacher = objective
                 m = trainer.model
                 lo = OBJ.window_objective_loss(m, teacher.model, x.to(dev), y.to(dev), oc)
-                gr = torch.autograd.grad(lo, list(m.parameters()), allow_unused=True)
-                for (n, _), g in zip(m.named_parameters(), gr):
-                    view = m.store.view(m.store.grad, n)
-                    view.zero_() if g is None else view.copy_(g)
-                trainer.opt.prepare(lr_at(trainer.step_idx, trainer.base_lr, trainer.lr_schedule, trainer.max_iters))
-                trainer._update()
-                trainer.step_idx += 1
+                _autograd_step(trainer, lo)
                 teacher.update(m)
+                loss = lo.detach()
+                prof.stop("forward_backward")
+            elif regs is not None and regs.active(step):
+                xd, yd = x.to(dev), y.to(dev)
+                lo = regs.loss(trainer.model(xd), yd, xd, step)
+                _autograd_step(trainer, lo)
                 loss = lo.detach()
                 prof.stop("forward_backward")
             elif pc:
@@ -363,3 +372,18 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
             hb.stop()
     summary = prof.summary() if prof.enabled else {}
     return {"final_loss": last_loss, "steps": t.max_iters - start, "run_dir": run.path, "profile": summary}
+
+
+def _autograd_step(trainer, loss) -> None:
+    """Gradients of ``loss`` by autograd over the PyTorch path of a plain ``BDH``
+    model, written into its flat gradient buffer, then the fused AdamW step."""
+    from .optim import lr_at
+
+    m = trainer.model
+    gr = torch.autograd.grad(loss, list(m.parameters()), allow_unused=True)
+    for (n, _), g in zip(m.named_parameters(), gr):
+        view = m.store.view(m.store.grad, n)
+        view.zero_() if g is None else view.copy_(g)
+    trainer.opt.prepare(lr_at(trainer.step_idx, trainer.base_lr, trainer.lr_schedule, trainer.max_iters))
+    trainer._update()
+    trainer.step_idx += 1
