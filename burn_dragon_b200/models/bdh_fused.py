@@ -31,6 +31,23 @@ from ..ops.gemm import Operand
 from .reference import rope_freqs
 
 
+def fused_unsupported(cfg) -> str | None:
+    """The first model option the fused kernels do not implement, or None: they
+    implement dropout 0 (as the BDH-GPU profiles use), LayerNorm, RoPE / ALiBi / no
+    rotation, one residual stream and an untied output head."""
+    if cfg.dropout != 0.0:
+        return "dropout > 0"
+    if getattr(cfg, "norm_kind", "layer_norm") != "layer_norm":
+        return f"norm_kind {cfg.norm_kind!r}"
+    if cfg.rotary_embedding == "pope":
+        return "PoPE"
+    if getattr(cfg, "mhc_streams", 1) > 1:
+        return "mHC streams"
+    if cfg.tie_input_output_embeddings:
+        return "a tied lm_head"
+    return None
+
+
 class FusedWorkspace:
     """Activation and gradient buffers for one (B, T) shape, allocated once."""
 
@@ -143,13 +160,9 @@ class FusedBDH:
         rank's heads only and the decoder / residual-gradient partials are summed over
         the tensor-parallel group."""
         self.tp = tp
-        if cfg.dropout != 0.0:
-            raise ValueError("the fused path implements dropout = 0 (as the BDH-GPU profiles use)")
-        if getattr(cfg, "norm_kind", "layer_norm") != "layer_norm" or cfg.rotary_embedding == "pope" \
-                or getattr(cfg, "mhc_streams", 1) > 1:
-            raise ValueError("the fused path implements LayerNorm and RoPE / ALiBi (use the PyTorch path)")
-        if cfg.tie_input_output_embeddings:
-            raise ValueError("the fused path needs an untied lm_head")
+        why = fused_unsupported(cfg)
+        if why is not None:
+            raise ValueError(f"the fused path does not implement {why} (use the PyTorch path)")
         self.cfg = cfg
         self.ws = ws
         self.mod = _ext.load()

@@ -14,6 +14,7 @@ buffer instead of one per parameter tensor.
 from __future__ import annotations
 
 import os
+import warnings
 
 import torch
 import torch.distributed as dist
@@ -86,6 +87,14 @@ class Trainer:
         else:
             self.world = 1 if self.tp is not None else (dist.get_world_size() if dist.is_initialized() else 1)
         self.fused = self.device.type == "cuda"
+        if self.fused:
+            from ..models.bdh_fused import fused_unsupported
+
+            why = fused_unsupported(cfg)
+            if why is not None:
+                # autograd over the PyTorch path (cuBLAS / ATen kernels), same step semantics
+                warnings.warn(f"fused BDH kernels do not implement {why}; training through the PyTorch path")
+                self.fused = False
         # comm: None / "nccl" (all-reduce + full AdamW on every rank) or "nvlink"
         # (symmetric-memory reduce-scatter + sharded AdamW + all-gather, parallel.ddp)
         self.comm = None
