@@ -554,6 +554,24 @@ class NeuronScalingConfig:
 
 
 @dataclass
+class ValidationConfig:
+    """Teacher-forced validation (schema.rs:1088-1160): ``fixed_holdout`` evaluates the
+    same windows every time (drawn with ``seed``, independent of the training seed);
+    ``live_source_selection`` draws fresh windows; ``external_evaluator`` leaves
+    validation to a separate process reading the checkpoints."""
+
+    execution: str = "local"  # local | external_evaluator
+    sampling: str = "fixed_holdout"  # fixed_holdout | live_source_selection
+    seed: int = 0xD12A60A5
+
+    def validate(self) -> None:
+        if self.execution not in ("local", "external_evaluator"):
+            raise ValueError(f"training.validation.execution {self.execution!r}")
+        if self.sampling not in ("fixed_holdout", "live_source_selection"):
+            raise ValueError(f"training.validation.sampling {self.sampling!r}")
+
+
+@dataclass
 class LogitEntropyFloorConfig:
     """Entropy / marginal-entropy floors and target coverage on the predicted
     distribution (schema.rs:340-371)."""
@@ -654,6 +672,7 @@ class TrainingSection:
     init_transfer: dict[str, Any] = field(default_factory=dict)
     # [{target, scale, schedule = {final_scale, start_fraction, end_fraction}}] (train.module_lr)
     module_lr_scales: list[dict[str, Any]] = field(default_factory=list)
+    validation: ValidationConfig = field(default_factory=ValidationConfig)
     logit_entropy_floor: LogitEntropyFloorConfig = field(default_factory=LogitEntropyFloorConfig)
     repeat_unlikelihood: RepeatUnlikelihoodConfig = field(default_factory=RepeatUnlikelihoodConfig)  # train.init_transfer.InitTransferConfig keys
     # batches from the native prefetching loader (csrc/host/loader.cpp) instead of the
@@ -685,10 +704,26 @@ class DatasetConfig:
 
 @dataclass
 class GenerationConfig:
+    prompt: str = ""
     max_tokens: int = 256
+    max_chars: int | None = None
     temperature: float = 1.0
     top_k: int | None = None
     device_buffer_tokens: int = 64
+    output_format: str = "auto"  # auto | decoded_text | token_ids (burn_dragon_language/src/config/core.rs:18-60)
+
+
+@dataclass
+class RunLayoutConfig:
+    """Where runs live (burn_dragon_train/src/config/run_layout.rs:6-35; path rules in
+    burn_dragon_train/src/train/pipeline/run_dirs.rs:46-141)."""
+
+    base_dir: str | None = None
+    category: str | None = None
+    mirror_config_path: bool = True
+    bundle: str | None = None
+    stage: str | None = None
+    variant: str | None = None
 
 
 @dataclass
@@ -699,10 +734,15 @@ class TrainingConfig:
     optimizer: OptimizerConfig = field(default_factory=OptimizerConfig)
     parallel: ParallelConfig = field(default_factory=ParallelConfig)
     generation: GenerationConfig = field(default_factory=GenerationConfig)
+    run_layout: RunLayoutConfig = field(default_factory=RunLayoutConfig)
+    config_paths: list[str] = field(default_factory=list)
     extras: dict[str, Any] = field(default_factory=dict)
 
     def validate(self) -> None:
         self.model.validate()
+        self.training.validation.validate()
+        if self.generation.output_format not in ("auto", "decoded_text", "token_ids"):
+            raise ValueError(f"generation.output_format {self.generation.output_format!r}")
         p = self.parallel.mode
         if p not in ("single", "ddp", "fsdp", "tensor_parallel_neuron", "hybrid_2d", "pipeline"):
             raise ValueError(f"unknown parallel.mode {p!r}")
@@ -788,6 +828,11 @@ def _model_table(table: dict) -> dict:
             t["norm_alpha_init"] = norm["alpha_init"]
         if norm.get("shift_init") is not None:
             t["norm_shift_init"] = norm["shift_init"]
+    head = t.pop("language_head", None)
+    if isinstance(head, dict) and head.get("type", "standard_token_classification") != "standard_token_classification":
+        # the factorized NCA patch head serves the NCA universality data, which is not built here
+        raise ValueError(f"model.language_head type {head.get('type')!r} is not implemented "
+                         "(standard_token_classification is)")
     mhc = t.pop("mhc", None)
     if isinstance(mhc, dict) and mhc.get("enabled"):
         t["mhc_streams"] = int(mhc.get("num_streams", 4))
@@ -845,13 +890,17 @@ def training_config_from_dict(data: dict) -> TrainingConfig:
     cfg = TrainingConfig()
     for section, cls in (("dataset", DatasetConfig), ("training", TrainingSection),
                          ("optimizer", OptimizerConfig), ("parallel", ParallelConfig),
-                         ("generation", GenerationConfig)):
+                         ("generation", GenerationConfig), ("run_layout", RunLayoutConfig)):
         if section in data:
             setattr(cfg, section, _fill(cls, data[section], extras, f"{section}."))
     if "model" in data:
         cfg.model = _fill(DragonConfig, _model_table(data["model"]), extras, "model.")
     for k, v in data.items():
-        if k not in ("dataset", "training", "optimizer", "parallel", "generation", "model"):
+        if k == "config_paths":  # written back by a run directory's training_config.json
+            cfg.config_paths = list(v)
+        elif k == "extras":
+            extras.update(v or {})
+        elif k not in ("dataset", "training", "optimizer", "parallel", "generation", "model", "run_layout"):
             extras[k] = v
     cfg.extras = extras
     if extras:
@@ -869,4 +918,6 @@ def load_training_config(paths: list[str] | str, overrides: dict | None = None) 
         merged = merge_tables(merged, load_toml_with_extends(p))
     if overrides:
         merged = merge_tables(merged, overrides)
-    return training_config_from_dict(merged)
+    cfg = training_config_from_dict(merged)
+    cfg.config_paths = [str(p) for p in paths]
+    return cfg

@@ -124,12 +124,78 @@ def load_parts(path: str, device=None) -> dict[str, torch.Tensor]:
 
 
 # ------------------------------------------------------------------ run directories
-def resolve_run_dir(backend: str = "cuda", run_name: str | None = None, root: str | None = None) -> str:
+def _rel(p) -> str | None:
+    """A relative path with empty, '.' and '..' parts dropped, or None if nothing is left."""
+    if not p:
+        return None
+    parts = [x for x in str(p).replace("\\", "/").split("/") if x not in ("", ".", "..")]
+    return os.path.join(*parts) if parts else None
+
+
+def category_from_config_path(domain: str, path: str) -> str | None:
+    """``.../config/<domain>/a/b/name.toml`` -> ``a/b/name``; ``.../config/local/[<domain>/]a/
+    name.toml`` -> ``local/a/name`` (run_dirs.rs:83-141)."""
+    comps = [c for c in os.path.normpath(path).split(os.sep) if c]
+    stem = os.path.splitext(comps[-1])[0] if comps else None
+    cfg_root = local_root = None
+    for i in range(len(comps) - 1):
+        if comps[i] == "config" and comps[i + 1] == domain:
+            cfg_root = i
+        if comps[i] == "config" and comps[i + 1] == "local":
+            local_root = i
+    if stem is None:
+        return None
+    if cfg_root is not None:
+        return _rel("/".join(comps[cfg_root + 2:-1] + [stem]))
+    if local_root is None:
+        return None
+    rest = comps[local_root + 2:-1]
+    if rest and rest[0] == domain:
+        rest = rest[1:]
+    return _rel("/".join(["local"] + rest + [stem]))
+
+
+def run_root_for(layout=None, config_paths=(), domain: str = "language", base: str | None = None) -> str:
+    """``<base>/<domain>/[<category>]/[bundles/<b>]/[stages/<s>]/[variants/<v>]``; the
+    category is ``layout.category`` or, with ``mirror_config_path``, derived from the last
+    config path that sits under ``config/<domain>`` or ``config/local`` (run_dirs.rs:46-81)."""
+    base = (layout.base_dir if layout is not None and layout.base_dir else None) or base or "runs"
+    root = os.path.join(base, domain)
+    if layout is None:
+        return root
+    cat = _rel(layout.category)
+    if cat is None and layout.mirror_config_path:
+        cat = next((c for c in (category_from_config_path(domain, p) for p in reversed(list(config_paths))) if c),
+                   None)
+    for prefix, part in (("", cat), ("bundles", _rel(layout.bundle)), ("stages", _rel(layout.stage)),
+                         ("variants", _rel(layout.variant))):
+        if part:
+            root = os.path.join(root, prefix, part) if prefix else os.path.join(root, part)
+    return root
+
+
+def resolve_run_dir(backend: str = "cuda", run_name: str | None = None, root: str | None = None,
+                    layout=None, config_paths=()) -> str:
+    """``BURN_DRAGON_RUN_DIR`` if set; else ``<run root>/<backend>/<name>`` where the run
+    root follows ``layout`` (base directory: ``layout.base_dir``, else ``root``, else
+    ``BURN_DRAGON_RUN_ROOT``, else ``runs``). With a layout, the run root's ``latest`` file
+    names the newest run (run_dirs.rs:196-212)."""
     if os.environ.get("BURN_DRAGON_RUN_DIR"):
         return os.environ["BURN_DRAGON_RUN_DIR"]
-    root = root or os.environ.get("BURN_DRAGON_RUN_ROOT", "runs")
+    base = root or os.environ.get("BURN_DRAGON_RUN_ROOT", "runs")
     name = run_name or os.environ.get("BURN_DRAGON_RUN_NAME") or "run"
-    return os.path.join(root, backend, name)
+    if layout is None:
+        return os.path.join(base, backend, name)
+    run_root = os.path.join(run_root_for(layout, config_paths, base=base), backend)
+    return os.path.join(run_root, name)
+
+
+def write_latest_run(run_dir: str) -> None:
+    """Record ``run_dir``'s name in its run root's ``latest`` file."""
+    root = os.path.dirname(os.path.abspath(run_dir))
+    os.makedirs(root, exist_ok=True)
+    with open(os.path.join(root, "latest"), "w") as f:
+        f.write(os.path.basename(os.path.abspath(run_dir)))
 
 
 def _jsonable(x):

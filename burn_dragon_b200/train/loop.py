@@ -48,7 +48,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     t = cfg.training
     mode = cfg.parallel.mode
     torch.manual_seed(t.seed + rank)
-    run = C.RunDir(C.resolve_run_dir(dev.type, run_name))
+    run = C.RunDir(C.resolve_run_dir(dev.type, run_name, layout=cfg.run_layout, config_paths=cfg.config_paths))
+    if rank == 0 and not os.environ.get("BURN_DRAGON_RUN_DIR"):
+        C.write_latest_run(run.path)
     if rank == 0:
         run.write_run_config(cfg)
         if cfg.model.random_scaffold.enabled:
@@ -235,11 +237,15 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     else:
         data = RandomBytes(t.batch_size, t.block_size, seed=t.seed, rank=data_rank, world=data_world)
         data.step = start
+    # validation windows: drawn with their own seed (identical across training seeds); a
+    # fixed holdout rewinds to the same windows at every validation
+    vseed = t.validation.seed % (2**31)
     if cfg.dataset.type == "file":
         valid = FileBytes(cfg.dataset.path, t.batch_size, t.block_size, "valid", cfg.dataset.train_split_ratio,
-                          seed=t.seed + 7919, rank=data_rank, world=data_world)
+                          seed=vseed, rank=data_rank, world=data_world)
     else:
-        valid = RandomBytes(t.batch_size, t.block_size, seed=t.seed + 7919, rank=data_rank, world=data_world)
+        valid = RandomBytes(t.batch_size, t.block_size, seed=vseed, rank=data_rank, world=data_world)
+    validate_here = t.validation.execution == "local"
 
     log = MetricsLogger(run.path, rank, every=t.log_frequency)
     prof = StageProfiler(dev)
@@ -335,7 +341,10 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 log.log(step + 1, loss=lv, lr=trainer.opt._lr_now if hasattr(trainer.opt, "_lr_now") else o.learning_rate,
                         step_ms=(time.perf_counter() - t0) * 1e3, force=True)
                 last_loss = lv
-            if t.validation_interval_iters and (step + 1) % t.validation_interval_iters == 0 and runner is None:
+            if validate_here and t.validation_interval_iters and (step + 1) % t.validation_interval_iters == 0 \
+                    and runner is None:
+                if t.validation.sampling == "fixed_holdout":
+                    valid.step = 0
                 vx, vy = valid.next()
                 with torch.no_grad():
                     vl = float(trainer.model.loss(vx.to(dev), vy.to(dev)))  # fresh state per window
