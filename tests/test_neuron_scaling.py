@@ -56,7 +56,9 @@ def test_training_loop_scales_on_plateau(tmp_path, monkeypatch, capsys):
           "--set", "training.neuron_scaling.min_steps_between_scales=0",
           "--set", "training.neuron_scaling.capacity_patience_epochs=1",
           "--set", "training.neuron_scaling.max_scale_events=1",
-          "--set", "training.neuron_scaling.max_latent_total=100000", "--run-name", "ns"])
+          "--set", "training.neuron_scaling.max_latent_total=100000",
+          # fresh validation windows each time: their noise makes the plateau the trigger needs
+          "--set", 'training.validation.sampling="live_source_selection"', "--run-name", "ns"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     ev = [json.loads(l) for l in open(os.path.join(res["run_dir"], "events", "metrics.jsonl"))]
     scale = [e for e in ev if "neuron_scale_event" in e]
