@@ -511,6 +511,9 @@ class LocalPredictiveCodingConfig:
     prediction_precision: float = 1.0
     factor_reduction: str = "sum"  # sum | mean
     sync_diagnostics: bool = False
+    # parameters learn once the activities have settled; the reference accepts only this
+    # schedule for Dragon (validate.rs:3610-3618)
+    learning_schedule: str = "equilibrium"
 
 
 @dataclass
@@ -569,6 +572,30 @@ class ValidationConfig:
             raise ValueError(f"training.validation.execution {self.execution!r}")
         if self.sampling not in ("fixed_holdout", "live_source_selection"):
             raise ValueError(f"training.validation.sampling {self.sampling!r}")
+
+
+@dataclass
+class DynamicsAnchorConfig:
+    """Self-distillation anchor to an EMA teacher of the student (schema.rs, DynamicsAnchorConfig)."""
+
+    enabled: bool = False
+    weight: float = 0.0
+    teacher_update_rate: float = 0.01
+    kl: str = "jensen_shannon"  # forward | reverse | jensen_shannon
+    mask: str = "all_tokens"  # all_tokens | context_tokens | target_tokens
+    warmup_steps: int = 0
+    ramp_steps: int = 0
+    every_steps: int = 1
+
+    def validate(self) -> None:
+        if not self.enabled:
+            return
+        if self.kl not in ("forward", "reverse", "jensen_shannon"):
+            raise ValueError(f"training.dynamics_anchor.kl {self.kl!r}")
+        if self.mask not in ("all_tokens", "context_tokens", "target_tokens"):
+            raise ValueError(f"training.dynamics_anchor.mask {self.mask!r}")
+        if not self.weight >= 0.0 or self.every_steps == 0:
+            raise ValueError("training.dynamics_anchor.weight must be >= 0 and every_steps > 0")
 
 
 @dataclass
@@ -674,6 +701,7 @@ class TrainingSection:
     module_lr_scales: list[dict[str, Any]] = field(default_factory=list)
     validation: ValidationConfig = field(default_factory=ValidationConfig)
     logit_entropy_floor: LogitEntropyFloorConfig = field(default_factory=LogitEntropyFloorConfig)
+    dynamics_anchor: DynamicsAnchorConfig = field(default_factory=DynamicsAnchorConfig)
     repeat_unlikelihood: RepeatUnlikelihoodConfig = field(default_factory=RepeatUnlikelihoodConfig)  # train.init_transfer.InitTransferConfig keys
     # batches from the native prefetching loader (csrc/host/loader.cpp) instead of the
     # Python generators

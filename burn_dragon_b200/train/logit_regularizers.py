@@ -15,6 +15,11 @@ burn_dragon_language/src/config/train/schema.rs:340-410.
   ``[cycle_min_lag, cycle_max_lag]``, and the cycle margin adds
   ``softplus(logit[history] - mean logit + margin)`` on those positions.
 
+* dynamics anchor: ``w * masked_mean_t D(student_t, teacher_t)`` with D the forward /
+  reverse / Jensen-Shannon self-distillation divergence and the teacher an EMA of the
+  student's weights (steps.rs:3502-3554); the mask keeps all tokens, the supervised
+  (target) tokens or the unsupervised (context) ones.
+
 Every weight is 0 before ``warmup_steps``, ramps linearly over ``ramp_steps`` and is
 active only on steps that are multiples of ``every_steps``, so the trainer runs its
 fused CE step on every step where all weights are 0.
@@ -27,7 +32,7 @@ import math
 import torch
 import torch.nn.functional as F
 
-from ..config import LogitEntropyFloorConfig, RepeatUnlikelihoodConfig
+from ..config import DynamicsAnchorConfig, LogitEntropyFloorConfig, RepeatUnlikelihoodConfig
 
 _EPS = 1.1920929e-07  # f32 machine epsilon, the reference's "weight is off" threshold
 
@@ -142,22 +147,45 @@ def repeat_unlikelihood_loss(logits, log_probs, targets, inputs, cfg: RepeatUnli
     return total
 
 
+def anchor_mask(cfg: DynamicsAnchorConfig, loss_mask):
+    if cfg.mask == "all_tokens" or loss_mask is None:
+        return None
+    return loss_mask if cfg.mask == "target_tokens" else (loss_mask == 0)
+
+
+def dynamics_anchor_loss(student_lp, teacher_logits, cfg: DynamicsAnchorConfig, step: int,
+                         loss_mask=None) -> torch.Tensor | None:
+    from .objectives import masked_token_mean, self_distillation_per_token
+
+    w = _w(cfg, cfg.weight, step)
+    if w <= _EPS:
+        return None
+    per = self_distillation_per_token(student_lp, F.log_softmax(teacher_logits.detach().float(), -1), cfg.kl)
+    return w * masked_token_mean(per, anchor_mask(cfg, loss_mask))
+
+
 class LogitRegularizers:
     """The configured auxiliary terms of one training run."""
 
-    def __init__(self, entropy: LogitEntropyFloorConfig, repeat: RepeatUnlikelihoodConfig):
+    def __init__(self, entropy: LogitEntropyFloorConfig, repeat: RepeatUnlikelihoodConfig,
+                 anchor: DynamicsAnchorConfig | None = None):
         self.entropy, self.repeat = entropy, repeat
+        self.anchor = anchor or DynamicsAnchorConfig()
 
     def enabled(self) -> bool:
-        return self.entropy.enabled or self.repeat.enabled
+        return self.entropy.enabled or self.repeat.enabled or self.anchor.enabled
+
+    def anchor_active(self, step: int) -> bool:
+        return _w(self.anchor, self.anchor.weight, step) > _EPS
 
     def active(self, step: int) -> bool:
         e, r = self.entropy, self.repeat
-        return any(x > _EPS for x in (_w(e, e.weight, step), _w(e, e.marginal_weight, step),
-                                      _w(e, e.target_coverage_weight, step), _w(r, r.weight, step),
-                                      _w(r, r.cycle_weight, step), _w(r, r.cycle_margin_weight, step)))
+        return self.anchor_active(step) or any(
+            x > _EPS for x in (_w(e, e.weight, step), _w(e, e.marginal_weight, step),
+                               _w(e, e.target_coverage_weight, step), _w(r, r.weight, step),
+                               _w(r, r.cycle_weight, step), _w(r, r.cycle_margin_weight, step)))
 
-    def loss(self, logits, targets, inputs, step: int, mask=None) -> torch.Tensor:
+    def loss(self, logits, targets, inputs, step: int, mask=None, teacher_logits=None) -> torch.Tensor:
         """Next-token CE plus the active auxiliary terms."""
         lp = F.log_softmax(logits.float(), -1)
         nll = -lp.gather(-1, targets.unsqueeze(-1)).squeeze(-1)
@@ -166,8 +194,11 @@ class LogitRegularizers:
         else:
             mk = mask.to(nll.dtype)
             loss = (nll * mk).sum() / mk.sum().clamp_min(1.0)
-        for aux in (repeat_unlikelihood_loss(logits, lp, targets, inputs, self.repeat, step),
-                    entropy_floor_loss(lp, targets, self.entropy, step)):
+        terms = [repeat_unlikelihood_loss(logits, lp, targets, inputs, self.repeat, step),
+                 entropy_floor_loss(lp, targets, self.entropy, step)]
+        if teacher_logits is not None:
+            terms.append(dynamics_anchor_loss(lp, teacher_logits, self.anchor, step, mask))
+        for aux in terms:
             if aux is not None:
                 loss = loss + aux
         return loss

@@ -142,16 +142,21 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         from .module_lr import ModuleLrScales
 
         mlr = ModuleLrScales(t.module_lr_scales, t.max_iters)
-    regs = None
-    if t.logit_entropy_floor.enabled or t.repeat_unlikelihood.enabled:
+    regs = anchor_teacher = None
+    if t.logit_entropy_floor.enabled or t.repeat_unlikelihood.enabled or t.dynamics_anchor.enabled:
         t.logit_entropy_floor.validate()
         t.repeat_unlikelihood.validate()
+        t.dynamics_anchor.validate()
         if extended or pc or mode not in ("single", "ddp", "fsdp") or getattr(trainer, "comm", None) is not None:
             raise ValueError("logit_entropy_floor / repeat_unlikelihood need the plain BDH model without the "
                              "NVLink communicator")
         from .logit_regularizers import LogitRegularizers
 
-        regs = LogitRegularizers(t.logit_entropy_floor, t.repeat_unlikelihood)
+        regs = LogitRegularizers(t.logit_entropy_floor, t.repeat_unlikelihood, t.dynamics_anchor)
+        if t.dynamics_anchor.enabled and t.dynamics_anchor.weight > 0:
+            from .objectives import EMATeacher
+
+            anchor_teacher = EMATeacher(trainer.model, min(max(t.dynamics_anchor.teacher_update_rate, 0.0), 1.0))
     objective = None
     if t.objective.get("type", "next_token") != "next_token":
         from . import objectives as OBJ
@@ -299,7 +304,11 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 prof.stop("forward_backward")
             elif regs is not None and regs.active(step):
                 xd, yd = x.to(dev), y.to(dev)
-                lo = regs.loss(trainer.model(xd), yd, xd, step)
+                tl = None
+                if anchor_teacher is not None and regs.anchor_active(step):
+                    with torch.no_grad():
+                        tl = anchor_teacher.model(xd)
+                lo = regs.loss(trainer.model(xd), yd, xd, step, teacher_logits=tl)
                 _autograd_step(trainer, lo)
                 loss = lo.detach()
                 prof.stop("forward_backward")
@@ -332,6 +341,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                     lr_now = getattr(trainer.opt, "_lr_now", o.learning_rate)
                     if cbp.after_optimizer_step(trainer.model, trainer.opt, lr_now):
                         log.log(step + 1, cbp_replaced=cbp.last.replacement_count, force=True)
+            if anchor_teacher is not None:
+                anchor_teacher.update(trainer.model)
             if native is not None:
                 native.mark_consumed()  # its buffer is refilled only after these copies ran
             prof.tokens += x.numel() * (world if mode in ("ddp", "fsdp") else 1)

@@ -103,6 +103,8 @@ def _sgd(a, g, inf: PCInferenceConfig):
 def local_pc_step(model, tokens, targets, cfg: LocalPredictiveCodingConfig, mask=None, rho0s=None):
     """One PC step on a ``BDH`` model: writes every parameter's ``.grad`` (the flat
     gradient buffer) and returns (feed-forward loss, report)."""
+    if cfg.learning_schedule != "equilibrium":
+        raise ValueError("local predictive coding supports only learning_schedule = \"equilibrium\"")
     L = model.cfg.n_layer
     scale = 1.0 if cfg.factor_reduction == "sum" else 1.0 / (L + 1)
     prec = cfg.prediction_precision

@@ -107,3 +107,34 @@ def test_training_loop_with_regularizers(tmp_path, monkeypatch, capsys):
           "--run-name", "regs"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res["final_loss"] is not None and math.isfinite(res["final_loss"])
+
+
+def test_dynamics_anchor_value_and_masks():
+    from burn_dragon_b200.config import DynamicsAnchorConfig
+    from burn_dragon_b200.train.logit_regularizers import dynamics_anchor_loss
+
+    torch.manual_seed(3)
+    s, t = torch.randn(2, 4, 6), torch.randn(2, 4, 6)
+    slp, tlp = F.log_softmax(s, -1), F.log_softmax(t, -1)
+    cfg = DynamicsAnchorConfig(enabled=True, weight=2.0, kl="forward")
+    kl = (tlp.exp() * (tlp - slp)).sum(-1)
+    assert abs(float(dynamics_anchor_loss(slp, t, cfg, 0)) - 2.0 * float(kl.mean())) < 1e-5
+    m = torch.tensor([[1, 0, 1, 0], [0, 0, 1, 1]])
+    cfg.mask = "context_tokens"
+    want = 2.0 * float((kl * (m == 0)).sum() / (m == 0).sum())
+    assert abs(float(dynamics_anchor_loss(slp, t, cfg, 0, m)) - want) < 1e-5
+    cfg.kl = "jensen_shannon"
+    cfg.mask = "all_tokens"
+    assert float(dynamics_anchor_loss(slp, s, cfg, 0)) < 1e-6  # identical distributions
+
+
+def test_training_loop_with_dynamics_anchor(tmp_path, monkeypatch, capsys):
+    from burn_dragon_b200.cli.train import main
+
+    cfg = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu.toml")
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", cfg, "--set", "training.max_iters=3",
+          "--set", "training.dynamics_anchor={enabled=true, weight=0.5, teacher_update_rate=0.1}",
+          "--run-name", "anchor"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert math.isfinite(res["final_loss"])
