@@ -599,6 +599,47 @@ class DynamicsAnchorConfig:
 
 
 @dataclass
+class GreedyRolloutUnlikelihoodConfig:
+    """Unlikelihood on short greedy rollouts (schema.rs, GreedyRolloutUnlikelihoodConfig)."""
+
+    enabled: bool = False
+    # only while the dynamics monitor reports a recovery; that monitor belongs to the
+    # absent event crate, so a recovery-only rollout never runs here
+    recovery_only: bool = False
+    weight: float = 0.0
+    margin_weight: float = 0.0
+    margin: float = 0.0
+    recovery_weight: float = 0.0
+    sequence_recovery_weight: float = 0.0
+    entropy_floor_weight: float = 0.0
+    target_entropy_bits: float = 0.0
+    cycle_weight: float = 0.0
+    cycle_margin_weight: float = 0.0
+    cycle_min_lag: int = 2
+    cycle_max_lag: int = 64
+    warmup_steps: int = 0
+    ramp_steps: int = 0
+    every_steps: int = 128
+    prompt_tokens: int = 32
+    rollout_tokens: int = 8
+    history_tokens: int = 8
+    batch_prompts: int = 1
+    epsilon: float = 1e-4
+
+    def validate(self) -> None:
+        if not self.enabled:
+            return
+        if self.every_steps == 0:
+            raise ValueError("training.greedy_rollout_unlikelihood.every_steps must be > 0")
+        if not 0.0 < self.epsilon < 1.0:
+            raise ValueError("training.greedy_rollout_unlikelihood.epsilon must be in (0, 1)")
+        for k in ("weight", "margin_weight", "recovery_weight", "sequence_recovery_weight", "entropy_floor_weight",
+                  "target_entropy_bits", "cycle_weight", "cycle_margin_weight"):
+            if not getattr(self, k) >= 0.0:
+                raise ValueError(f"training.greedy_rollout_unlikelihood.{k} must be finite and >= 0")
+
+
+@dataclass
 class LogitEntropyFloorConfig:
     """Entropy / marginal-entropy floors and target coverage on the predicted
     distribution (schema.rs:340-371)."""
@@ -702,6 +743,8 @@ class TrainingSection:
     validation: ValidationConfig = field(default_factory=ValidationConfig)
     logit_entropy_floor: LogitEntropyFloorConfig = field(default_factory=LogitEntropyFloorConfig)
     dynamics_anchor: DynamicsAnchorConfig = field(default_factory=DynamicsAnchorConfig)
+    greedy_rollout_unlikelihood: GreedyRolloutUnlikelihoodConfig = field(
+        default_factory=GreedyRolloutUnlikelihoodConfig)
     repeat_unlikelihood: RepeatUnlikelihoodConfig = field(default_factory=RepeatUnlikelihoodConfig)  # train.init_transfer.InitTransferConfig keys
     # batches from the native prefetching loader (csrc/host/loader.cpp) instead of the
     # Python generators

@@ -143,16 +143,19 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
 
         mlr = ModuleLrScales(t.module_lr_scales, t.max_iters)
     regs = anchor_teacher = None
-    if t.logit_entropy_floor.enabled or t.repeat_unlikelihood.enabled or t.dynamics_anchor.enabled:
+    if t.logit_entropy_floor.enabled or t.repeat_unlikelihood.enabled or t.dynamics_anchor.enabled \
+            or t.greedy_rollout_unlikelihood.enabled:
         t.logit_entropy_floor.validate()
         t.repeat_unlikelihood.validate()
         t.dynamics_anchor.validate()
+        t.greedy_rollout_unlikelihood.validate()
         if extended or pc or mode not in ("single", "ddp", "fsdp") or getattr(trainer, "comm", None) is not None:
             raise ValueError("logit_entropy_floor / repeat_unlikelihood need the plain BDH model without the "
                              "NVLink communicator")
         from .logit_regularizers import LogitRegularizers
 
-        regs = LogitRegularizers(t.logit_entropy_floor, t.repeat_unlikelihood, t.dynamics_anchor)
+        regs = LogitRegularizers(t.logit_entropy_floor, t.repeat_unlikelihood, t.dynamics_anchor,
+                                 t.greedy_rollout_unlikelihood)
         if t.dynamics_anchor.enabled and t.dynamics_anchor.weight > 0:
             from .objectives import EMATeacher
 
@@ -275,6 +278,7 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
             else:
                 x, y = data.next()
             prof.stop("dataloader")
+            x_clean = x
             if t.input_corruption.enabled:
                 from .corruption import corrupt_inputs
 
@@ -308,7 +312,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
                 if anchor_teacher is not None and regs.anchor_active(step):
                     with torch.no_grad():
                         tl = anchor_teacher.model(xd)
-                lo = regs.loss(trainer.model(xd), yd, xd, step, teacher_logits=tl)
+                lo = regs.loss(trainer.model(xd), yd, xd, step, teacher_logits=tl, model=trainer.model,
+                               clean_inputs=x_clean.to(dev))
                 _autograd_step(trainer, lo)
                 loss = lo.detach()
                 prof.stop("forward_backward")

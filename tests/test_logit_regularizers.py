@@ -138,3 +138,65 @@ def test_training_loop_with_dynamics_anchor(tmp_path, monkeypatch, capsys):
           "--run-name", "anchor"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert math.isfinite(res["final_loss"])
+
+
+def test_greedy_rollout_prompt_start():
+    from burn_dragon_b200.train.logit_regularizers import rollout_prompt_start
+
+    assert rollout_prompt_start(0, 1, 8, 4) == 4  # no span: the window right after one prompt length
+    assert [rollout_prompt_start(s, 2, 64, 8) for s in (0, 2, 4, 14)] == [8, 16, 24, 8 + (7 * 8) % 49]
+    assert rollout_prompt_start(0, 1, 4, 8) == 0
+
+
+def test_greedy_rollout_unlikelihood_matches_a_hand_rollout():
+    from burn_dragon_b200.config import GreedyRolloutUnlikelihoodConfig
+    from burn_dragon_b200.train.logit_regularizers import greedy_rollout_loss
+
+    torch.manual_seed(4)
+    V = 5
+    W = torch.randn(V, V, requires_grad=True)
+
+    def bigram(tokens, state=None):  # logits of the next token from the current one
+        return W[tokens]
+
+    x = torch.tensor([[0, 1, 2, 3, 4, 0, 1, 2], [4, 3, 2, 1, 0, 4, 3, 2]])
+    cfg = GreedyRolloutUnlikelihoodConfig(enabled=True, weight=1.0, margin_weight=0.5, margin=0.2, every_steps=1,
+                                          prompt_tokens=3, rollout_tokens=4, history_tokens=2, batch_prompts=2,
+                                          cycle_min_lag=2, cycle_max_lag=1)
+    got = greedy_rollout_loss(bigram, x, cfg, 0)
+    # by hand: prompt = x[:, 3:6] (avail 5, min start 3, span 2, step 0)
+    u_num = m_num = hits = 0.0
+    for b in range(2):
+        hist = [int(x[b, 5]), int(x[b, 4])]
+        cur = int(x[b, 5])
+        for _ in range(4):
+            lg = W[cur].detach()
+            nxt = int(lg.argmax())
+            if nxt in hist:
+                p = min(float(torch.softmax(lg, -1)[nxt]), 1 - 1e-4)
+                u_num += -math.log(max(1 - p, 1e-4))
+                m_num += float(F.softplus(lg[nxt] - lg.mean() + 0.2))
+                hits += 1
+            hist = [nxt] + hist[:1]
+            cur = nxt
+    want = (u_num + 0.5 * m_num) / max(hits, 1)
+    assert hits > 0 and abs(float(got.detach()) - want) < 1e-5
+    got.backward()
+    assert W.grad is not None and float(W.grad.abs().sum()) > 0
+    assert greedy_rollout_loss(bigram, x, cfg, 1) is not None  # every step
+    cfg.every_steps = 4
+    assert greedy_rollout_loss(bigram, x, cfg, 2) is None
+
+
+def test_training_loop_with_greedy_rollout(tmp_path, monkeypatch, capsys):
+    from burn_dragon_b200.cli.train import main
+
+    cfg = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu.toml")
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", cfg, "--set", "training.max_iters=2",
+          "--set", "training.greedy_rollout_unlikelihood={enabled=true, weight=0.5, recovery_weight=0.1, "
+                   "sequence_recovery_weight=0.1, entropy_floor_weight=0.1, target_entropy_bits=2.0, every_steps=1, "
+                   "prompt_tokens=8, rollout_tokens=3}",
+          "--run-name", "rollout"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert math.isfinite(res["final_loss"])
