@@ -727,7 +727,9 @@ class TrainingSection:
     max_iters: int = 1000
     tbptt_chunk_size: int | None = None
     tbptt_persist_across_steps: bool = False
-    sequence_batching: str = "random"  # random | streaming
+    # auto: streaming when rho persists across steps, random windows otherwise (schema.rs,
+    # SequenceBatchingMode)
+    sequence_batching: str = "auto"  # auto | random | streaming
     gradient_accumulation_steps: int = 1
     seed: int = 1337
     log_frequency: int = 10
@@ -819,8 +821,11 @@ class TrainingConfig:
             raise ValueError(f"unknown parallel.mode {p!r}")
         if p == "pipeline" and self.training.tbptt_chunk_size:
             raise ValueError("pipeline parallelism does not support TBPTT chunking")
-        if self.training.tbptt_persist_across_steps and self.training.sequence_batching != "streaming":
-            raise ValueError("tbptt_persist_across_steps requires sequence_batching = \"streaming\"")
+        if self.training.sequence_batching not in ("auto", "random", "streaming"):
+            raise ValueError(f"training.sequence_batching {self.training.sequence_batching!r}")
+        if self.training.tbptt_persist_across_steps and self.training.sequence_batching == "random":
+            raise ValueError("training.sequence_batching=random is incompatible with "
+                             "training.tbptt_persist_across_steps=true")
         if self.training.tbptt_chunk_size is not None:
             if self.training.tbptt_chunk_size <= 0 or self.training.block_size % self.training.tbptt_chunk_size:
                 raise ValueError("tbptt_chunk_size must divide block_size")
