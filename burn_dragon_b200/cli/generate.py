@@ -1,7 +1,7 @@
 """Generation CLI: load a run's newest checkpoint and continue prompts, encoded and
 decoded with the run's ``tokenizer.json`` (bytes or BPE). Flags left unset take the
 run's ``[generation]`` values (prompt, max_tokens, max_chars, temperature, top_k,
-output_format: ``decoded_text`` prints text, ``token_ids`` prints the ids as JSON, ``auto``
+context_strategy, output_format: ``decoded_text`` prints text, ``token_ids`` prints the ids as JSON, ``auto``
 is decoded text); burn_dragon_language/src/config/core.rs:18-60.
 
   python -m burn_dragon_b200.cli.generate --run runs/language/cuda/NAME --prompt "hello" [--max-tokens 64]
@@ -52,6 +52,9 @@ def main(argv=None) -> None:
     tp = os.path.join(a.run, "tokenizer.json")
     tok = load_tokenizer(tp) if os.path.exists(tp) else load_tokenizer({"type": "byte"})
     prompt = tok.encode(prompt_text) or [0]
+    window = g.sliding_window(cfg.training.block_size)
+    if window is not None and len(prompt) > window:
+        prompt = prompt[-window:]  # the recurrent state carries the rest; nothing to trim later
     x = torch.tensor([prompt] * a.batch, dtype=torch.long, device=dev)
     out = Generator(model).generate(x, max_tokens, temperature=temperature, top_k=top_k, seed=a.seed)
     for row in out.tolist():

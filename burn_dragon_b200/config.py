@@ -784,6 +784,18 @@ class GenerationConfig:
     top_k: int | None = None
     device_buffer_tokens: int = 64
     output_format: str = "auto"  # auto | decoded_text | token_ids (burn_dragon_language/src/config/core.rs:18-60)
+    # {type = "infinite"} or {type = "sliding", window = W}; window 0 means block_size
+    # (core.rs:60-68, generation.rs:1317-1332)
+    context_strategy: dict[str, Any] = field(default_factory=lambda: {"type": "infinite"})
+
+    def sliding_window(self, block_size: int) -> int | None:
+        kind = self.context_strategy.get("type", "infinite")
+        if kind == "infinite":
+            return None
+        if kind != "sliding":
+            raise ValueError(f"generation.context_strategy type {kind!r}")
+        w = int(self.context_strategy.get("window", 0))
+        return w if w > 0 else max(block_size, 1)
 
 
 @dataclass
@@ -816,6 +828,7 @@ class TrainingConfig:
         self.training.validation.validate()
         if self.generation.output_format not in ("auto", "decoded_text", "token_ids"):
             raise ValueError(f"generation.output_format {self.generation.output_format!r}")
+        self.generation.sliding_window(self.training.block_size)
         p = self.parallel.mode
         if p not in ("single", "ddp", "fsdp", "tensor_parallel_neuron", "hybrid_2d", "pipeline"):
             raise ValueError(f"unknown parallel.mode {p!r}")

@@ -84,3 +84,14 @@ def test_language_head_and_generation_keys(tmp_path, monkeypatch, capsys):
     gen(["--run", run_dir, "--prompt", "ab", "--temperature", "0"])
     ids = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert len(ids) == 3 and all(0 <= i < 256 for i in ids)
+
+
+def test_generation_context_strategy():
+    cfg = training_config_from_dict({"training": {"block_size": 64},
+                                     "generation": {"context_strategy": {"type": "sliding", "window": 0}}})
+    assert cfg.generation.sliding_window(64) == 64
+    cfg.generation.context_strategy = {"type": "sliding", "window": 5}
+    assert cfg.generation.sliding_window(64) == 5
+    assert training_config_from_dict({}).generation.sliding_window(64) is None
+    with pytest.raises(ValueError):
+        training_config_from_dict({"generation": {"context_strategy": {"type": "ring"}}})
