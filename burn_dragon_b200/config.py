@@ -250,6 +250,11 @@ class DragonConfig:
     mlp_internal_dim_multiplier: int = 4
     vocab_size: int = 256
     n_expert: int = 1
+    # {type = "late_layer", base_latent_total, last_layers} | {type = "geometric",
+    # min_latent_total}: layer l uses the first latent_total_for_layer(l) / n_head neurons
+    # of every head of the shared weights (burn_dragon_core/src/model/config.rs:584-592,
+    # 1125-1260; dragon.rs:1855-1880)
+    latent_fanout_schedule: dict | None = None
     tie_input_output_embeddings: bool = False
     rollout_fast_steps_per_slow_step: int = 1
     # FusedKernelConfig fields that change the math
@@ -328,6 +333,53 @@ class DragonConfig:
             raise ValueError("latent size must be divisible by the number of heads")
         return total // self.n_head
 
+    def _latent_quantum(self) -> int:
+        return math.lcm(max(self.n_embd, 1), max(self.n_head, 1) * max(self.n_expert, 1))
+
+    def latent_total_for_layer(self, layer: int) -> int:
+        full = self.latent_total
+        f = self.latent_fanout_schedule
+        if not f:
+            return full
+        if f.get("type") == "late_layer":
+            first_full = max(max(self.n_layer, 1) - max(int(f["last_layers"]), 1), 0)
+            return full if layer >= first_full else int(f["base_latent_total"])
+        lo = int(f["min_latent_total"])
+        if self.n_layer <= 1 or layer + 1 >= self.n_layer:
+            return full
+        if layer == 0:
+            return lo
+        raw = round(lo * (full / lo) ** (layer / (self.n_layer - 1)))
+        q = self._latent_quantum()
+        c = min(max(raw, lo), full)
+        lower = max((c // q) * q, lo)
+        upper = min(lower + q, full)
+        if upper < lo:
+            return lo
+        return lower if c - lower <= upper - c else upper
+
+    def latent_per_head_for_layer(self, layer: int) -> int:
+        return self.latent_total_for_layer(layer) // self.n_head
+
+    def uniform_latent_fanout(self) -> bool:
+        return all(self.latent_total_for_layer(i) == self.latent_total for i in range(self.n_layer))
+
+    def _validate_fanout(self) -> None:
+        f = self.latent_fanout_schedule
+        if not f:
+            return
+        kind = f.get("type")
+        keys = {"late_layer": ("base_latent_total",), "geometric": ("min_latent_total",)}.get(kind)
+        if keys is None:
+            raise ValueError(f"model.latent_fanout_schedule type {kind!r}")
+        for k in keys:
+            t = int(f.get(k, 0))
+            if t <= 0 or t > self.latent_total or t % self._latent_quantum():
+                raise ValueError(f"model.latent_fanout_schedule.{k} must be in (0, latent_total] and divisible by "
+                                 f"lcm(n_embd, n_head*n_expert) (got {t})")
+        if kind == "late_layer" and int(f.get("last_layers", 0)) <= 0:
+            raise ValueError("model.latent_fanout_schedule.last_layers must be > 0")
+
     def residual_depth(self) -> int:
         return max(self.n_layer, 1) * max(self.rollout_fast_steps_per_slow_step, 1)
 
@@ -384,6 +436,10 @@ class DragonConfig:
         if self.rotary_embedding == "rope" and self.latent_per_head % 2:
             raise ValueError("RoPE needs an even latent per head")
         _ = self.latent_per_head
+        self._validate_fanout()
+        if self.latent_fanout_schedule and self.uses_extended_runtime():
+            raise ValueError("model.latent_fanout_schedule is implemented on the BDH layer path, not with the "
+                             "layer-loop variants")
         if self.residual_connector not in ("vanilla", "mhc", "attention_residual", "block_attention_residual"):
             raise ValueError(f"unknown residual_connector {self.residual_connector!r}")
         self.latent_reasoning.validate()

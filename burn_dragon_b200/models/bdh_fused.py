@@ -45,6 +45,8 @@ def fused_unsupported(cfg) -> str | None:
         return "mHC streams"
     if cfg.tie_input_output_embeddings:
         return "a tied lm_head"
+    if getattr(cfg, "latent_fanout_schedule", None) and not cfg.uniform_latent_fanout():
+        return "a latent fan-out schedule"
     return None
 
 

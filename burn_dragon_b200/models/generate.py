@@ -72,6 +72,10 @@ class Generator:
         self.prefill_chunk = prefill_chunk
         self._dws: _DecodeWorkspace | None = None
         self._pws = None
+        from .bdh_fused import fused_unsupported
+
+        # options the fused prefill / decode kernels do not implement run on the PyTorch path
+        self._fused_ok = fused_unsupported(self.cfg) is None
 
     # ---------------------------------------------------------------- prefill
     @torch.no_grad()
@@ -80,7 +84,7 @@ class Generator:
         state = state or ModelState.empty()
         B, T = prompt.shape
         dev = prompt.device
-        fused_ok = dev.type == "cuda" and self.cfg.dropout == 0.0 and not self.cfg.tie_input_output_embeddings
+        fused_ok = dev.type == "cuda" and self._fused_ok
         chunk = self.prefill_chunk if fused_ok else T
         main = (T // 128) * 128 if fused_ok else 0
         if fused_ok and 0 < main < T:
@@ -121,7 +125,7 @@ class Generator:
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, state: ModelState) -> torch.Tensor:
         """One token per sequence: tokens [B] -> logits [B, V]; advances ``state``."""
-        if tokens.device.type != "cuda":
+        if tokens.device.type != "cuda" or not self._fused_ok:
             logits = self.model(tokens[:, None], state=state)
             state.detach_in_place()
             return logits[:, -1].float()

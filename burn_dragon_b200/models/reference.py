@@ -174,6 +174,20 @@ def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, de
     return v_next, rho, {"x": x, "q": q, "a": a, "y": y, "yn": yn}
 
 
+def layer_weights(params: dict, cfg, layer: int, freqs):
+    """The shared projections a layer uses: all of them, or under a latent fan-out
+    schedule the first ``nh`` neurons of every head (encoder / encoder_v columns, the
+    head's first ``nh`` decoder rows) with the RoPE / PoPE table cut to ``nh``."""
+    enc, enc_v, dec = params["encoder"], params["encoder_v"], params["decoder"]
+    nh = cfg.latent_per_head_for_layer(layer) if getattr(cfg, "latent_fanout_schedule", None) else enc.shape[-1]
+    cap = enc.shape[-1]
+    if nh == cap:
+        return enc, enc_v, dec, freqs
+    H = enc.shape[0]
+    dec = dec.reshape(H, cap, -1)[:, :nh].reshape(H * nh, -1)
+    return enc[..., :nh], enc_v[..., :nh], dec, None if freqs is None else freqs[:nh]
+
+
 def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state=False, training=False):
     """Full BDH forward (logits). params: embed [V,D], encoder, encoder_v, decoder,
     lm_head [D,V] (or None for tied), norm_gamma, norm_beta."""
@@ -200,8 +214,9 @@ def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state
         r0 = rho0s[layer] if rho0s is not None else None
         if streams > 1:
             v, R = MHC.layer_split(R, params["mhc_res"][layer], params["mhc_pre"][layer], cfg.mhc_tau, cfg.mhc_iters)
-        v, rho, _ = bdh_layer(v, params["encoder"], params["encoder_v"], params["decoder"], gamma, beta,
-                              eps=cfg.norm_eps, thr=cfg.thresholds()[0], thr_y=cfg.thresholds()[1], freqs=freqs,
+        enc, enc_v, dec, fq = layer_weights(params, cfg, layer, freqs)
+        v, rho, _ = bdh_layer(v, enc, enc_v, dec, gamma, beta,
+                              eps=cfg.norm_eps, thr=cfg.thresholds()[0], thr_y=cfg.thresholds()[1], freqs=fq,
                               positions=positions,
                               decay=decay, rho0=r0, need_state=need_state, dropout=cfg.dropout,
                               training=training, norm=norm, pope=cfg.rotary_embedding == "pope")

@@ -102,6 +102,13 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
 
         cfg.model.mlp_internal_dim_multiplier = int(json.load(open(ns_path))["mlp_internal_dim_multiplier"])
     extended = cfg.model.uses_extended_runtime()
+    if not cfg.model.uniform_latent_fanout() and (
+            mode not in ("single", "ddp", "fsdp") or t.algorithm == "predictive_coding"
+            or t.continual_backprop.enabled or t.neuron_scaling.enabled):
+        # as in the reference, local PC needs uniform fan-out; the sharded / pipelined
+        # paths and the neuron surgery work on full-width layers
+        raise ValueError("model.latent_fanout_schedule needs single / ddp mode without predictive coding, "
+                         "continual backprop or neuron scaling")
     if extended and mode not in ("single", "ddp", "fsdp"):
         raise ValueError(f"parallel mode {mode!r} does not support the layer-loop variants this model enables")
     if extended:
