@@ -32,7 +32,7 @@ from ..models.state import ModelState
 from ..parallel.fault import Heartbeat, NonFiniteGuard, PeerFailure
 from . import checkpoint as C
 from .data import FileBytes, RandomBytes, StreamingBytes
-from .metrics import MetricsLogger, StageProfiler
+from .metrics import MetricsLogger, StageProfiler, theoretical_forward_flops
 from .trainer import Trainer, init_distributed
 
 
@@ -263,6 +263,17 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     validate_here = t.validation.execution == "local"
 
     log = MetricsLogger(run.path, rank, every=t.log_frequency)
+    # which step implementation this run takes, and its forward FLOP estimate (the
+    # reference logs the same "training path fingerprint" and theoretical profile)
+    path = ("pipeline" if runner is not None else mode if mode in ("tensor_parallel_neuron", "hybrid_2d")
+            else "runtime_variants" if extended else "predictive_coding" if pc
+            else "self_distillation" if objective is not None
+            else "fused_sm100" if getattr(trainer, "fused", False) else "pytorch")
+    fl = theoretical_forward_flops(cfg.model, t.batch_size, t.block_size)
+    if rank == 0:
+        run.write_json("run_info.json", {
+            "training_path": path, "world": world, "mode": mode, "comm": comm, "aux_losses": regs is not None,
+            "start_step": start, "approx_forward_flops": fl})
     prof = StageProfiler(dev)
     guard = NonFiniteGuard(every=t.log_frequency)
     hb = Heartbeat(timeout=float(os.environ.get("BDH_HEARTBEAT_TIMEOUT", "60"))) if world > 1 else None

@@ -9,7 +9,13 @@
   profile.rs:1-576). Its summary reports ``wall_tokens_per_second``,
   ``model_tokens_per_second`` = tokens / (forward + backward + optimizer) and
   ``model_duty_fraction`` (backend.rs:1807-1915). Multi-GPU figures take the max over
-  ranks of each phase's time.
+  ranks of each phase's time. On CUDA each phase is also an NVTX range, so a timeline
+  profiler shows the phases.
+* ``theoretical_forward_flops``: the reference's forward FLOP terms per step
+  (burn_dragon_language/src/train/utils.rs:130-154: encoder, attention scores, attention
+  values, decoder; backward about twice the forward), summed over the layers (its log
+  line counts one layer's worth), plus the terms it leaves out (the y projection and the
+  output head) under separate keys.
 """
 
 from __future__ import annotations
@@ -38,6 +44,7 @@ class StageProfiler:
         self.tokens = 0
         self._wall0 = time.perf_counter()
         self._pending: list[tuple[str, object, object]] = []
+        self._nvtx: dict[str, int] = {}
 
     def start(self, phase: str) -> None:
         if not self.enabled:
@@ -46,6 +53,7 @@ class StageProfiler:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
             self._open[phase] = e
+            self._nvtx[phase] = torch.cuda.nvtx.range_start(phase)
         else:
             self._open[phase] = time.perf_counter()
 
@@ -57,6 +65,8 @@ class StageProfiler:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
             self._pending.append((phase, s, e))
+            if phase in self._nvtx:
+                torch.cuda.nvtx.range_end(self._nvtx.pop(phase))
         else:
             self.ms[phase] += (time.perf_counter() - s) * 1e3
         self.calls[phase] += 1
@@ -84,6 +94,24 @@ class StageProfiler:
             out["model_tokens_per_second"] = self.tokens / (model_ms / 1e3)
             out["model_duty_fraction"] = (model_ms / 1e3) / wall if wall > 0 else 0.0
         return out
+
+
+def theoretical_forward_flops(cfg, batch: int, block: int) -> dict:
+    """Forward FLOPs of one step of ``batch`` x ``block`` tokens."""
+    bt = batch * block
+    D, N, H, Nh, V = cfg.n_embd, cfg.latent_total, cfg.n_head, cfg.latent_per_head, cfg.vocab_size
+    L = cfg.n_layer
+    enc = 2 * bt * D * N * L
+    scores = 2 * batch * H * block * block * Nh * L
+    value = 2 * batch * H * block * block * D * L
+    dec = 2 * bt * N * D * L
+    out = {"encoder": enc, "attn_scores": scores, "attn_value": value, "decoder": dec,
+           "total": enc + scores + value + dec}
+    # not in the reference's estimate: the y projection (a @ encoder_v per head) and the head
+    out["encoder_v"] = 2 * bt * H * D * Nh * L
+    out["lm_head"] = 2 * bt * D * V
+    out["total_with_y_and_head"] = out["total"] + out["encoder_v"] + out["lm_head"]
+    return out
 
 
 class MetricsLogger:

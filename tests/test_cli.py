@@ -123,3 +123,19 @@ def test_self_distillation_objective_training_run(tmp_path, monkeypatch, capsys)
           "--set", "training.block_size=32", "--set", 'training.objective.type="sdft_sdpo"', "--run-name", "sd"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res["final_loss"] is not None
+
+
+def test_run_logs_training_path_and_flop_estimate(tmp_path, monkeypatch, capsys):
+    from burn_dragon_b200.config import load_training_config
+    from burn_dragon_b200.train.metrics import theoretical_forward_flops
+
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.max_iters=1", "--run-name", "fp"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    info = json.load(open(os.path.join(res["run_dir"], "run_info.json")))
+    assert info["training_path"] == "pytorch" and info["mode"] == "single"
+    tc = load_training_config(os.path.join(CFG, "tiny_cpu.toml"))
+    m, bt = tc.model, tc.training.batch_size * tc.training.block_size
+    fl = theoretical_forward_flops(m, tc.training.batch_size, tc.training.block_size)
+    assert fl["encoder"] == 2 * bt * m.n_embd * m.latent_total * m.n_layer
+    assert info["approx_forward_flops"] == fl
