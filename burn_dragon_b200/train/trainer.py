@@ -13,6 +13,7 @@ buffer instead of one per parameter tensor.
 
 from __future__ import annotations
 
+import datetime
 import os
 import warnings
 
@@ -33,7 +34,10 @@ def init_distributed() -> tuple[int, int, int]:
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-        dist.init_process_group(backend=backend)
+        # a rank that dies or stalls ends the others' next collective with an error after
+        # this long instead of hanging them (BDH_PG_TIMEOUT_S, seconds)
+        timeout = datetime.timedelta(seconds=float(os.environ.get("BDH_PG_TIMEOUT_S", "600")))
+        dist.init_process_group(backend=backend, timeout=timeout)
     return rank, world, local
 
 
