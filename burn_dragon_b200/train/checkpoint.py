@@ -32,6 +32,7 @@ import os
 import re
 import shutil
 import struct
+import threading
 from dataclasses import asdict, is_dataclass
 
 import torch
@@ -208,11 +209,34 @@ def _jsonable(x):
     return x
 
 
+def _host_copy(t: torch.Tensor) -> torch.Tensor:
+    return t.detach().to("cpu", copy=True)
+
+
 class RunDir:
-    def __init__(self, path: str):
+    """``async_write``: ``save`` copies the tensors to host memory on the calling thread
+    (the device work is ordered and finished before it returns) and writes the files on a
+    background thread, so training continues during the disk writes; the next ``save``,
+    ``load`` or ``wait`` waits for the previous write. The ``latest`` marker is written
+    after the files it names (``[parallel.checkpoint] async_write``,
+    burn_dragon_train/src/config/core.rs:217-222)."""
+
+    def __init__(self, path: str, async_write: bool = False):
         self.path = path
         self.ckpt = os.path.join(path, "checkpoint")
         os.makedirs(self.ckpt, exist_ok=True)
+        self.async_write = async_write
+        self._writer: threading.Thread | None = None
+        self._write_error: BaseException | None = None
+
+    def wait(self) -> None:
+        """Block until a background checkpoint write has finished; re-raise its error."""
+        if self._writer is not None:
+            self._writer.join()
+            self._writer = None
+        if self._write_error is not None:
+            e, self._write_error = self._write_error, None
+            raise RuntimeError("background checkpoint write failed") from e
 
     def write_json(self, name: str, obj) -> None:
         with open(os.path.join(self.path, name), "w") as f:
@@ -250,24 +274,45 @@ class RunDir:
         their optimizer moments), stored as ``extra-<step>.bin``."""
         from ..models.bdh import record_name
 
-        params = {record_name(n): t.detach() for n, t in model.store.views(model.store.data).items()}
-        save_tensors(self._p("model", step), params, {"schema_version": SCHEMA_VERSION, "step": step})
+        self.wait()
+        snap = _host_copy if self.async_write else (lambda t: t.detach())
+        params = {record_name(n): snap(t) for n, t in model.store.views(model.store.data).items()}
+        optim = None
         if optimizer is not None:
-            save_tensors(self._p("optim", step), {"m": optimizer.m, "v": optimizer.v},
-                         {"t": optimizer.t, "lr": optimizer.lr})
-        with open(self._p("scheduler", step), "w") as f:
-            json.dump(scheduler or {}, f)
+            optim = ({"m": snap(optimizer.m), "v": snap(optimizer.v)}, {"t": optimizer.t, "lr": optimizer.lr})
+        rt = meta = None
         if runtime is not None:
-            rt = {}
             meta = {k: v for k, v in runtime.items() if k != "rhos"}
-            for i, r in enumerate(runtime.get("rhos") or []):
-                rt[f"rho.{i}"] = r
-            save_tensors(self._p("runtime-state", step), rt, meta)
-        if extra:
-            save_tensors(self._p("extra", step), extra, {"schema_version": SCHEMA_VERSION})
-        with open(os.path.join(self.path, "latest"), "w") as f:
-            f.write(str(step))
-        self._retain(keep_last, best_step)
+            rt = {f"rho.{i}": snap(r) for i, r in enumerate(runtime.get("rhos") or [])}
+        extra = {k: snap(v) for k, v in extra.items()} if extra else None
+        scheduler = dict(scheduler or {})
+
+        def write():
+            save_tensors(self._p("model", step), params, {"schema_version": SCHEMA_VERSION, "step": step})
+            if optim is not None:
+                save_tensors(self._p("optim", step), *optim)
+            with open(self._p("scheduler", step), "w") as f:
+                json.dump(scheduler, f)
+            if rt is not None:
+                save_tensors(self._p("runtime-state", step), rt, meta)
+            if extra:
+                save_tensors(self._p("extra", step), extra, {"schema_version": SCHEMA_VERSION})
+            with open(os.path.join(self.path, "latest"), "w") as f:
+                f.write(str(step))
+            self._retain(keep_last, best_step)
+
+        if not self.async_write:
+            write()
+            return
+
+        def run():
+            try:
+                write()
+            except BaseException as e:  # surfaced by the next wait()
+                self._write_error = e
+
+        self._writer = threading.Thread(target=run, name=f"checkpoint-{step}", daemon=False)
+        self._writer.start()
 
     def steps(self) -> list[int]:
         out = []
@@ -299,6 +344,7 @@ class RunDir:
         """Restore model (and optimizer) state; returns {'scheduler', 'runtime'}."""
         from ..models.bdh import record_name
 
+        self.wait()
         step = self.latest() if step is None else step
         if step is None:
             raise FileNotFoundError(f"no checkpoint in {self.ckpt}")

@@ -48,7 +48,11 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
     t = cfg.training
     mode = cfg.parallel.mode
     torch.manual_seed(t.seed + rank)
-    run = C.RunDir(C.resolve_run_dir(dev.type, run_name, layout=cfg.run_layout, config_paths=cfg.config_paths))
+    ck = cfg.parallel.checkpoint or {}
+    if ck.get("format", "unsharded_v1") != "unsharded_v1":
+        raise ValueError("parallel.checkpoint.format: checkpoints are written unsharded by rank 0 (unsharded_v1)")
+    run = C.RunDir(C.resolve_run_dir(dev.type, run_name, layout=cfg.run_layout, config_paths=cfg.config_paths),
+                   async_write=bool(ck.get("async_write", False)))
     if rank == 0 and not os.environ.get("BURN_DRAGON_RUN_DIR"):
         C.write_latest_run(run.path)
     if rank == 0:
@@ -414,6 +418,7 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True)
         if hb is not None:
             hb.stop()
     summary = prof.summary() if prof.enabled else {}
+    run.wait()
     return {"final_loss": last_loss, "steps": t.max_iters - start, "run_dir": run.path, "profile": summary}
 
 

@@ -70,3 +70,41 @@ def test_retention_keeps_last_two_and_best(tmp_path):
         run.save(s, model, best_step=1)
     assert run.steps() == [1, 3, 4]
     assert run.latest() == 4
+
+
+def test_async_write_snapshots_before_training_continues(tmp_path):
+    cfg = DragonConfig(n_layer=1, n_embd=32, n_head=2, mlp_internal_dim_multiplier=2, dropout=0.0, vocab_size=64)
+    model = BDH(cfg, seed=5)
+    opt = FusedAdamW(model.store, lr=1e-2)
+    run = C.RunDir(os.path.join(str(tmp_path), "a"), async_write=True)
+    want = model.store.data.clone()
+    run.save(1, model, opt, {"step": 1})
+    model.store.data.add_(1.0)  # training goes on while the files are written
+    run.save(2, model, opt, {"step": 2})
+    run.wait()
+    assert run.latest() == 2 and run.steps() == [1, 2]
+    m2 = BDH(cfg, seed=6)
+
+    def params(buf):  # the parameter views (the flat store also holds alignment padding)
+        return m2.store.views(buf)
+
+    run.load(1, m2)
+    for n, v in params(m2.store.data).items():
+        torch.testing.assert_close(v, params(want)[n])
+    run.load(2, m2)
+    for n, v in params(m2.store.data).items():
+        torch.testing.assert_close(v, params(want)[n] + 1.0)
+
+
+def test_training_with_async_checkpoints(tmp_path, monkeypatch, capsys):
+    import json
+
+    from burn_dragon_b200.cli.train import main
+
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    cfg = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu.toml")
+    main(["--config", cfg, "--set", "training.max_iters=4", "--set", "training.checkpoint_interval_iters=2",
+          "--set", "parallel.checkpoint={async_write=true}", "--run-name", "aw"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "model-4.bin"))
+    assert open(os.path.join(res["run_dir"], "latest")).read().strip() == "4"
