@@ -136,6 +136,42 @@ def linear_attention_dense(q, v, rho0=None, decay=None, need_state: bool = True)
     return c, rho
 
 
+def linear_attention_dense_vjp(q, v, dc, rho0=None, decay=None, drho=None):
+    """Analytic backward of ``linear_attention_dense``: the data flow the fused backward
+    runs on tensor cores (dense_causal_attention/backward_runtime.rs:36-148 in the
+    reference). With S = (Q Q^T) . Gamma and P = dC V^T:
+
+        dV    = sum_h S^T dC                      (+ (Q . g^(T-i))^T-side of drho)
+        dS    = P . Gamma                         (strictly causal, decayed)
+        dQ    = (dS + dS^T) Q                     (Q is both query and key)
+                + (dC . g^i) rho0^T + (V drho^T) . g^(T-i)
+        drho0 = Q^T (dC . g^i) + drho g^T
+
+    ``v`` [B,1|H,T,D] (a broadcast value gets its head-sum); returns (dq, dv, drho0)."""
+    B, H, T, N = q.shape
+    D = v.shape[-1]
+    ve = v.expand(B, H, T, D)
+    gam, pow_i, pow_ti = _decay_powers(T, decay, q.device, q.dtype)
+    s = torch.matmul(q, q.transpose(-1, -2)) * gam[None]
+    dv = torch.matmul(s.transpose(-1, -2), dc)
+    ds = torch.matmul(dc, ve.transpose(-1, -2)) * gam[None]
+    dq = torch.matmul(ds + ds.transpose(-1, -2), q)
+    drho0 = None
+    if rho0 is not None:
+        dci = dc * pow_i[None, :, :, None] if pow_i is not None else dc
+        dq = dq + torch.matmul(dci, rho0.transpose(-1, -2))
+        drho0 = torch.matmul(q.transpose(-1, -2), dci)
+    if drho is not None:
+        wt = pow_ti[None, :, :, None] if pow_ti is not None else 1.0
+        dq = dq + torch.matmul(ve, drho.transpose(-1, -2)) * wt
+        dv = dv + torch.matmul(q * wt, drho)
+        if rho0 is not None:
+            drho0 = drho0 + drho * (decay.view(1, H, 1, 1) ** T if decay is not None else 1.0)
+    if v.shape[1] == 1 and H > 1:
+        dv = dv.sum(1, keepdim=True)
+    return dq, dv, drho0
+
+
 def layer_norm(x, gamma, beta, eps):
     return F.layer_norm(x, (x.shape[-1],), gamma, beta, eps)
 
