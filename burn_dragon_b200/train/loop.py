@@ -36,13 +36,18 @@ from .metrics import MetricsLogger, StageProfiler, theoretical_forward_flops
 from .trainer import Trainer, init_distributed
 
 
-def _device(local: int) -> torch.device:
+def _device(local: int, backend: str | None = None) -> torch.device:
+    """``backend="cpu"`` keeps a run on the host even where a GPU is present."""
+    if backend == "cpu":
+        return torch.device("cpu")
+    if backend == "cuda" and not torch.cuda.is_available():
+        raise RuntimeError("backend cuda requested but no CUDA device is visible")
     return torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
 
 
-def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True) -> dict:
+def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True, backend: str | None = None) -> dict:
     rank, world, local = init_distributed()
-    dev = _device(local)
+    dev = _device(local, backend)
     if dev.type == "cuda":
         torch.cuda.set_device(dev)
     t = cfg.training

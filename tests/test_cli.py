@@ -139,3 +139,15 @@ def test_run_logs_training_path_and_flop_estimate(tmp_path, monkeypatch, capsys)
     fl = theoretical_forward_flops(m, tc.training.batch_size, tc.training.block_size)
     assert fl["encoder"] == 2 * bt * m.n_embd * m.latent_total * m.n_layer
     assert info["approx_forward_flops"] == fl
+
+
+def test_train_shorthand_flags(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--training-config", os.path.join(CFG, "tiny_cpu.toml"), "--backend", "cpu", "--seed", "7",
+          "--n-layer", "1", "--latent-total", "512", "--batch-size", "2", "--block-size", "16", "--max-iters", "2",
+          "--run-name", "sh"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    tc = json.load(open(os.path.join(res["run_dir"], "training_config.json")))
+    assert tc["training"]["seed"] == 7 and tc["model"]["n_layer"] == 1
+    assert tc["training"]["batch_size"] == 2 and tc["training"]["block_size"] == 16
+    assert tc["model"]["mlp_internal_dim_multiplier"] * tc["model"]["n_embd"] == 512
