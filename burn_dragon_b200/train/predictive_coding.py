@@ -30,6 +30,7 @@ tensors, so no gradient crosses a factor boundary.
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
@@ -206,3 +207,57 @@ def _write(model, grads):
             view.zero_()
         else:
             view.copy_(g)
+
+
+# ------------------------------------------------------------------ gradient fidelity
+def _stats(pc: torch.Tensor, ref: torch.Tensor, family: str, present: bool | None) -> dict:
+    """Agreement of a PC derivative with the exact gradient (cosine, norm ratio, relative
+    L2 error, least-squares scale, sign agreement) as in the reference's diagnostics
+    (burn_dragon_language/src/train/local_predictive_coding/diagnostics.rs:16-120)."""
+    p, r = pc.double().reshape(-1), ref.double().reshape(-1)
+    return _finish({"elements": p.numel(), "dot": float(p @ r), "pc2": float(p @ p), "ref2": float(r @ r),
+                    "err2": float((p - r).pow(2).sum()), "nonneg": float((p * r >= 0).double().sum())},
+                   family, present)
+
+
+def _finish(raw: dict, family: str, present: bool | None) -> dict:
+    def ratio(a, b):
+        return a / b if abs(b) > 1e-30 and math.isfinite(a / b) else None
+
+    pn, rn = math.sqrt(max(raw["pc2"], 0.0)), math.sqrt(max(raw["ref2"], 0.0))
+    return {"parameter_family": family, "elements": raw["elements"], "reference_gradient_present": present,
+            "dot_product": raw["dot"], "pc_norm": pn, "reference_norm": rn, "cosine": ratio(raw["dot"], pn * rn),
+            "pc_to_reference_norm_ratio": ratio(pn, rn),
+            "relative_l2_error": ratio(math.sqrt(max(raw["err2"], 0.0)), rn),
+            "least_squares_scale": ratio(raw["dot"], raw["pc2"]),
+            "nonnegative_product_fraction": raw["nonneg"] / raw["elements"] if raw["elements"] else 0.0,
+            "_raw": raw}
+
+
+def pc_gradient_fidelity(model, tokens, targets, cfg: LocalPredictiveCodingConfig, mask=None, rho0s=None) -> dict:
+    """One local-PC derivative step against exact backpropagation of the same masked
+    next-token loss (an offline diagnostic: it runs one global backward)."""
+    loss_pc, report = local_pc_step(model, tokens, targets, cfg, mask=mask, rho0s=rho0s)
+    pc = {n: model.store.view(model.store.grad, n).clone() for n, _ in model.named_parameters()}
+    names = [n for n, _ in model.named_parameters()]
+    params = [p for _, p in model.named_parameters()]
+    from ..models.state import ModelState
+
+    st = None if rho0s is None else ModelState([r.detach() for r in rho0s], 0)
+    ref_loss = R.cross_entropy(model(tokens, state=st), targets, mask)
+    ref = torch.autograd.grad(ref_loss, params, allow_unused=True)
+    fams, tot = [], None
+    for n, p, g in zip(names, params, ref):
+        f = _stats(pc[n], torch.zeros_like(p) if g is None else g, n, g is not None)
+        fams.append(f)
+        raw = f["_raw"]
+        tot = dict(raw) if tot is None else {k: tot[k] + raw[k] for k in tot}
+    glob = _finish(tot, "global", None)
+    for f in fams + [glob]:
+        f.pop("_raw")
+    lp, lr = float(loss_pc), float(ref_loss.detach())
+    return {"pc_loss": lp, "reference_loss": lr, "loss_absolute_error": abs(lp - lr), "reference_backward_calls": 1,
+            "pc_step": {"solver": report.solver, "inference_steps": report.inference_steps,
+                        "factors": report.factors, "local_vjp_calls": report.local_vjp_calls,
+                        "global_backward_calls": report.global_backward_calls},
+            "global": glob, "parameter_families": fams}

@@ -67,3 +67,20 @@ def test_derivatives_invariant_to_batch_duplication():
     m2 = model()
     local_pc_step(m2, torch.cat([x, x]), torch.cat([y, y]), cfg)
     torch.testing.assert_close(m2.store.grad, g1, rtol=1e-4, atol=1e-7)
+
+
+def test_gradient_fidelity_report():
+    from burn_dragon_b200.cli.pc_gradient_fidelity import main as fidelity
+
+    small = ["--n-layer", "2", "--n-embd", "16", "--n-head", "2", "--latent-total", "64", "--vocab-size", "32",
+             "--batch-size", "2", "--block-size", "8"]
+    out = fidelity(small + ["--solver", "fixed_prediction"])
+    g = out["arms"][0]["report"]["global"]
+    # fixed prediction chains the factor VJPs: exactly backpropagation
+    assert abs(g["cosine"] - 1.0) < 1e-5 and g["relative_l2_error"] < 1e-4
+    out = fidelity(small + ["--inference-steps", "1,2", "--step-sizes", "0.05"])
+    assert len(out["arms"]) == 2
+    for arm in out["arms"]:
+        r = arm["report"]
+        assert r["reference_backward_calls"] == 1 and -1.0 <= r["global"]["cosine"] <= 1.0
+        assert {f["parameter_family"] for f in r["parameter_families"]} >= {"encoder", "decoder", "embed"}
