@@ -513,6 +513,26 @@ class OptimizerConfig:
     eps: float = 1e-8
     grad_clip_norm: float | None = None
     lr_schedule: dict[str, Any] = field(default_factory=lambda: {"type": "constant"})
+    # name = "eggroll": {sigma, population = {population_size (members, antithetic pairs
+    # x 2), population_chunk_size (pairs per batched forward), rank}}
+    # (burn_dragon_train/src/config/optimizer.rs:239-310)
+    eggroll: dict[str, Any] = field(default_factory=dict)
+
+    def eggroll_settings(self) -> dict:
+        e = dict(self.eggroll)
+        pop = dict(e.get("population", {}))
+        out = {"sigma": float(e.get("sigma", 0.01)), "members": int(pop.get("population_size", 16)),
+               "chunk": pop.get("population_chunk_size"), "rank": int(pop.get("rank", 4))}
+        if not out["sigma"] > 0:
+            raise ValueError("optimizer.eggroll.sigma must be > 0")
+        if out["members"] < 2 or out["members"] % 2:
+            raise ValueError("optimizer.eggroll.population.population_size must be an even number >= 2 "
+                             "(antithetic pairs)")
+        if out["rank"] <= 0:
+            raise ValueError("optimizer.eggroll.population.rank must be > 0")
+        if self.grad_clip_norm is not None:
+            raise ValueError("optimizer.name = eggroll does not use gradients: grad clipping is not supported")
+        return out
 
 
 @dataclass

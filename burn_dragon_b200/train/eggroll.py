@@ -54,18 +54,34 @@ def population_losses(model, tokens, targets, noises: dict, sigma: float) -> tor
 
 @torch.no_grad()
 def es_step(model, tokens, targets, population: int = 8, sigma: float = 0.01, lr: float = 0.01, rank: int = 4,
-            seed: int = 0) -> dict:
-    """One antithetic ES update of the three shared projections; returns diagnostics."""
+            seed: int = 0, chunk: int | None = None, weight_decay: float = 0.0, reduce=None) -> dict:
+    """One antithetic ES update of the three shared projections; returns diagnostics.
+
+    ``population`` antithetic pairs (2 x population members), evaluated ``chunk`` pairs
+    per batched forward; ``weight_decay`` is decoupled (W *= 1 - lr * wd before the ES
+    step); ``reduce`` maps this rank's member losses to the data-parallel mean, so every
+    rank (same ``seed``, hence the same perturbations) applies the same update."""
     gen = torch.Generator().manual_seed(seed)
     params = model.param_dict()
     noises = {n: torch.stack([_noise(params[n].shape, rank, gen, tokens.device) for _ in range(population)])
               for n in MATRIX}
-    losses = population_losses(model, tokens, targets, noises, sigma)
+    step = max(1, min(chunk or population, population))
+    plus, minus = [], []
+    for c in range(0, population, step):
+        part = population_losses(model, tokens, targets, {n: noises[n][c:c + step] for n in MATRIX}, sigma)
+        k = part.shape[0] // 2
+        plus.append(part[:k])
+        minus.append(part[k:])
+    losses = torch.cat(plus + minus)
+    if reduce is not None:
+        losses = reduce(losses)
     fp, fm = -losses[:population], -losses[population:]
     coef = (fp - fm) / (2 * population * sigma)
     for n in MATRIX:
-        upd = torch.tensordot(coef, noises[n], dims=1)
-        getattr(model, n).add_(lr * upd)
+        w = getattr(model, n)
+        if weight_decay:
+            w.mul_(1.0 - lr * weight_decay)
+        w.add_(lr * torch.tensordot(coef, noises[n], dims=1))
     model.store.refresh_shadow()
     return {"mean_loss": float(losses.mean()), "best_loss": float(losses.min())}
 

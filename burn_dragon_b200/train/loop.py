@@ -74,7 +74,7 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                 S.write_manifest(man_path, cfg.model)
     o = cfg.optimizer
     comm = None
-    if mode in ("ddp", "fsdp") and world > 1 and dev.type == "cuda":
+    if mode in ("ddp", "fsdp") and world > 1 and dev.type == "cuda" and o.name != "eggroll":
         comm = "nvlink" if o.grad_clip_norm is None else "nccl"
     micro = int(cfg.parallel.tensor.get("micro_batches", t.gradient_accumulation_steps))
     tp_arg: bool | int = mode == "tensor_parallel_neuron"
@@ -140,6 +140,11 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
         runner = PipelineRunner(trainer.model, pl, rank, t.batch_size // pl.micro, t.block_size)
 
     pc = t.algorithm == "predictive_coding"
+    egg = None
+    if o.name == "eggroll" or t.algorithm == "eggroll":
+        if extended or pc or mode not in ("single", "ddp", "fsdp") or getattr(trainer, "comm", None) is not None:
+            raise ValueError("EGGROLL training needs the plain BDH model in single / ddp mode (NCCL path)")
+        egg = o.eggroll_settings()
     if pc and (extended or mode not in ("single", "ddp", "fsdp")):
         raise ValueError("predictive_coding training needs the plain BDH model in single / ddp mode")
     scaler = None
@@ -275,7 +280,7 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     # which step implementation this run takes, and its forward FLOP estimate (the
     # reference logs the same "training path fingerprint" and theoretical profile)
     path = ("pipeline" if runner is not None else mode if mode in ("tensor_parallel_neuron", "hybrid_2d")
-            else "runtime_variants" if extended else "predictive_coding" if pc
+            else "runtime_variants" if extended else "predictive_coding" if pc else "eggroll" if egg is not None
             else "self_distillation" if objective is not None
             else "fused_sm100" if getattr(trainer, "fused", False) else "pytorch")
     fl = theoretical_forward_flops(cfg.model, t.batch_size, t.block_size)
@@ -343,6 +348,23 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                                clean_inputs=x_clean.to(dev))
                 _autograd_step(trainer, lo)
                 loss = lo.detach()
+                prof.stop("forward_backward")
+            elif egg is not None:
+                from .eggroll import es_step
+                from .optim import lr_at
+
+                lr_now = lr_at(step, o.learning_rate, o.lr_schedule, t.max_iters)
+                red = None
+                if world > 1:
+                    def red(ls):
+                        dist.all_reduce(ls)
+                        return ls / world
+                rep = es_step(trainer.model, x.to(dev), y.to(dev), population=egg["members"] // 2,
+                              sigma=egg["sigma"], lr=lr_now, rank=egg["rank"], seed=t.seed * 1_000_003 + step,
+                              chunk=None if egg["chunk"] is None else int(egg["chunk"]),
+                              weight_decay=o.weight_decay, reduce=red)
+                trainer.step_idx += 1
+                loss = torch.tensor(rep["mean_loss"])
                 prof.stop("forward_backward")
             elif pc:
                 from .optim import lr_at

@@ -67,3 +67,41 @@ init_from = "pretrain"
     out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert out["stages"] == ["pretrain:completed", "finetune:completed"]
     assert os.path.exists(tmp_path / "out" / "stages" / "00_pretrain" / "run" / "checkpoint" / "model-3.bin")
+
+
+def test_adamw_then_eggroll_phases(tmp_path, capsys):
+    """The reference's AdamW-warmup -> EGGROLL continuation (burn_dragon_language/src/train/
+    phased.rs) as a two-stage bundle."""
+    spec = tmp_path / "phases.toml"
+    spec.write_text(f'''
+[bundle]
+name = "adamw_eggroll"
+output_dir = "{tmp_path / 'out'}"
+
+[[stages]]
+name = "adamw"
+configs = ["{os.path.abspath(CFG)}"]
+overrides = {{ training = {{ max_iters = 2, checkpoint_interval_iters = 2, block_size = 32 }} }}
+
+[[stages]]
+name = "eggroll"
+configs = ["{os.path.abspath(CFG)}"]
+init_from = "adamw"
+
+[stages.overrides.training]
+max_iters = 2
+block_size = 32
+
+[stages.overrides.optimizer]
+name = "eggroll"
+learning_rate = 0.01
+
+[stages.overrides.optimizer.eggroll]
+sigma = 0.02
+population = {{ population_size = 4, rank = 2 }}
+''')
+    main([str(spec)])
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert out["stages"] == ["adamw:completed", "eggroll:completed"]
+    info = json.load(open(tmp_path / "out" / "stages" / "01_eggroll" / "run" / "run_info.json"))
+    assert info["training_path"] == "eggroll"

@@ -80,3 +80,34 @@ def test_hybrid_layout():
 
     tp, dp = hybrid_layout(8, 4)
     assert tp == [[0, 1, 2, 3], [4, 5, 6, 7]] and dp == [[0, 4], [1, 5], [2, 6], [3, 7]]
+
+
+def test_eggroll_chunking_and_decay_match_one_batch():
+    import copy
+
+    from burn_dragon_b200.models.bdh import BDH
+    from burn_dragon_b200.train.eggroll import es_step
+
+    cfg = DragonConfig(n_layer=1, n_embd=16, n_head=2, mlp_internal_dim_multiplier=4, vocab_size=32, dropout=0.0)
+    m1 = BDH(cfg, seed=2)
+    m2 = copy.deepcopy(m1)
+    x = torch.randint(0, 32, (2, 8))
+    es_step(m1, x, x, population=4, sigma=0.05, lr=0.1, rank=2, seed=9, weight_decay=0.1)
+    es_step(m2, x, x, population=4, sigma=0.05, lr=0.1, rank=2, seed=9, weight_decay=0.1, chunk=1)
+    for n in ("encoder", "encoder_v", "decoder"):
+        torch.testing.assert_close(getattr(m1, n), getattr(m2, n), atol=1e-6, rtol=1e-5)
+
+
+def test_training_loop_with_the_eggroll_optimizer(tmp_path, monkeypatch, capsys):
+    import json
+
+    from burn_dragon_b200.cli.train import main
+
+    cfg = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu.toml")
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", cfg, "--set", "training.max_iters=2", "--set", 'optimizer.name="eggroll"',
+          "--set", "optimizer.eggroll={sigma=0.02, population={population_size=4, population_chunk_size=1, rank=2}}",
+          "--run-name", "egg"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None
+    assert json.load(open(os.path.join(res["run_dir"], "run_info.json")))["training_path"] == "eggroll"
