@@ -512,6 +512,11 @@ class OptimizerConfig:
     beta2: float = 0.999
     eps: float = 1e-8
     grad_clip_norm: float | None = None
+    # element-wise gradient clamp, used when grad_clip_norm is unset
+    # (burn_dragon_train/src/train/pipeline/optimizer.rs:225-240)
+    grad_clip_value: float | None = None
+    # validated and recorded; the reference applies no schedule from it either
+    weight_decay_final: float | None = None
     lr_schedule: dict[str, Any] = field(default_factory=lambda: {"type": "constant"})
     # name = "eggroll": {sigma, population = {population_size (members, antithetic pairs
     # x 2), population_chunk_size (pairs per batched forward), rank}}
@@ -902,6 +907,11 @@ class TrainingConfig:
     def validate(self) -> None:
         self.model.validate()
         self.training.validation.validate()
+        o = self.optimizer
+        if o.weight_decay_final is not None and o.weight_decay_final < 0:
+            raise ValueError("optimizer.weight_decay_final must be >= 0")
+        if o.grad_clip_value is not None and not o.grad_clip_value > 0:
+            raise ValueError("optimizer.grad_clip_value must be > 0")
         if self.generation.output_format not in ("auto", "decoded_text", "token_ids"):
             raise ValueError(f"generation.output_format {self.generation.output_format!r}")
         self.generation.sliding_window(self.training.block_size)

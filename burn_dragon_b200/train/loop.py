@@ -75,12 +75,13 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     o = cfg.optimizer
     comm = None
     if mode in ("ddp", "fsdp") and world > 1 and dev.type == "cuda" and o.name != "eggroll":
-        comm = "nvlink" if o.grad_clip_norm is None else "nccl"
+        comm = "nvlink" if o.grad_clip_norm is None and o.grad_clip_value is None else "nccl"
     micro = int(cfg.parallel.tensor.get("micro_batches", t.gradient_accumulation_steps))
     tp_arg: bool | int = mode == "tensor_parallel_neuron"
     if mode == "hybrid_2d":
         tp_arg = int(cfg.parallel.tensor.get("size", 8))
-        comm = "nvlink" if o.grad_clip_norm is None and dev.type == "cuda" else None
+        plain = o.grad_clip_norm is None and o.grad_clip_value is None
+        comm = "nvlink" if plain and dev.type == "cuda" else None
     if cfg.parallel.tensor.get("sequence_parallel"):
         # the residual stream is replicated across the tensor-parallel group; the sum is an
         # all-reduce of [M, D] per layer (a reduce-scatter + all-gather moves the same bytes)
@@ -124,11 +125,13 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
         from .runtime_trainer import RuntimeTrainer
 
         trainer = RuntimeTrainer(cfg.model, dev, lr=o.learning_rate, weight_decay=o.weight_decay,
-                                 betas=(o.beta1, o.beta2), eps=o.eps, grad_clip_norm=o.grad_clip_norm, seed=t.seed,
+                                 betas=(o.beta1, o.beta2), eps=o.eps, grad_clip_norm=o.grad_clip_norm,
+                                 grad_clip_value=o.grad_clip_value, seed=t.seed,
                                  lr_schedule=o.lr_schedule, max_iters=t.max_iters)
     else:
         trainer = Trainer(cfg.model, dev, lr=o.learning_rate, weight_decay=o.weight_decay,
-                          betas=(o.beta1, o.beta2), eps=o.eps, grad_clip_norm=o.grad_clip_norm, seed=t.seed,
+                          betas=(o.beta1, o.beta2), eps=o.eps, grad_clip_norm=o.grad_clip_norm,
+                          grad_clip_value=o.grad_clip_value, seed=t.seed,
                           lr_schedule=o.lr_schedule, max_iters=t.max_iters, comm=comm, tensor_parallel=tp_arg,
                           micro_batches=micro if mode != "pipeline" else 1)
     runner = None

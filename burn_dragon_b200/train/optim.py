@@ -1,7 +1,7 @@
 """Fused AdamW over the flat parameter store, plus learning-rate schedules.
 
 AdamW with decoupled weight decay, beta (0.9, 0.999) defaults and optional global
-grad-norm clipping (burn_dragon_train/src/config/optimizer.rs:6-460). On CUDA one kernel
+grad-norm clipping or, when no norm is set, element-wise value clipping (burn_dragon_train/src/config/optimizer.rs:6-460). On CUDA one kernel
 updates the fp32 master weights, both moments and the bf16 GEMM shadow in a single
 pass over the flat buffers; the clipping coefficient stays on the device.
 LR schedules mirror burn_dragon_train/src/train/pipeline/schedule.rs:6-392.
@@ -48,8 +48,9 @@ class FusedAdamW:
     """AdamW over ``ParamStore`` flat buffers (a boolean mask selects trainable elements)."""
 
     def __init__(self, store, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.1,
-                 grad_clip_norm: float | None = None):
+                 grad_clip_norm: float | None = None, grad_clip_value: float | None = None):
         self.store = store
+        self.clip_value = grad_clip_value if grad_clip_norm is None else None
         self.lr = lr
         self.b1, self.b2 = betas
         self.eps = eps
@@ -90,6 +91,8 @@ class FusedAdamW:
     def apply(self) -> None:
         """The update itself (device work only on CUDA; safe to capture in a CUDA graph)."""
         s = self.store
+        if self.clip_value is not None:  # burn's GradientClipping::Value: clamp every element
+            s.grad.clamp_(-self.clip_value, self.clip_value)
         if s.data.is_cuda:
             mod = _ext.load()
             gscale = None

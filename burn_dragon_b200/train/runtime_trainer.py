@@ -21,13 +21,14 @@ from .optim import FusedAdamW, lr_at
 
 class RuntimeTrainer:
     def __init__(self, cfg: DragonConfig, device, lr=1e-3, weight_decay=0.1, betas=(0.9, 0.999), eps=1e-8,
-                 grad_clip_norm=None, seed=1337, lr_schedule=None, max_iters=1000, rollout_mode: str = "fused"):
+                 grad_clip_norm=None, seed=1337, lr_schedule=None, max_iters=1000, rollout_mode: str = "fused",
+                 grad_clip_value=None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = DragonRuntime(cfg, device=self.device, seed=seed, rollout_mode=rollout_mode)
         self.core = self.model.core
         self.opt = FusedAdamW(self.core.store, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
-                              grad_clip_norm=grad_clip_norm)
+                              grad_clip_norm=grad_clip_norm, grad_clip_value=grad_clip_value)
         core_ids = {id(p) for p in self.core.parameters()}
         self.extra_params = [p for p in self.model.parameters() if id(p) not in core_ids]
         self.extra_names = [n for n, p in self.model.named_parameters() if id(p) not in core_ids]
@@ -71,6 +72,9 @@ class RuntimeTrainer:
         if self.extra_opt is not None:
             for g in self.extra_opt.param_groups:
                 g["lr"] = lr
+            if self.opt.clip_value is not None:
+                for p in self.extra_params:
+                    p.grad.clamp_(-self.opt.clip_value, self.opt.clip_value)
             self.extra_opt.step()
         self.step_idx += 1
 

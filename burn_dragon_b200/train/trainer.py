@@ -43,7 +43,7 @@ def init_distributed() -> tuple[int, int, int]:
 
 class Trainer:
     def __init__(self, cfg: DragonConfig, device, lr=1e-3, weight_decay=0.1, betas=(0.9, 0.999), eps=1e-8,
-                 grad_clip_norm=None, seed=1337, lr_schedule=None, max_iters=1000, comm=None,
+                 grad_clip_norm=None, seed=1337, lr_schedule=None, max_iters=1000, comm=None, grad_clip_value=None,
                  tensor_parallel: bool = False, micro_batches: int = 1):
         self.cfg = cfg
         self.device = torch.device(device)
@@ -80,7 +80,7 @@ class Trainer:
         else:
             self.model = BDH(cfg, device=self.device, seed=seed)
         self.opt = FusedAdamW(self.model.store, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
-                              grad_clip_norm=grad_clip_norm)
+                              grad_clip_norm=grad_clip_norm, grad_clip_value=grad_clip_value)
         self.lr_schedule = lr_schedule
         self.max_iters = max_iters
         self.base_lr = lr

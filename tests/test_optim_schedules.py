@@ -1,0 +1,35 @@
+"""Optimizer options (CPU): element-wise gradient clipping, weight_decay_final checks."""
+
+import pytest
+import torch
+
+from burn_dragon_b200.config import DragonConfig, training_config_from_dict
+from burn_dragon_b200.models.bdh import BDH
+from burn_dragon_b200.train.optim import FusedAdamW
+
+
+def _model():
+    return BDH(DragonConfig(n_layer=1, n_embd=16, n_head=2, mlp_internal_dim_multiplier=4, vocab_size=32,
+                            dropout=0.0), seed=4)
+
+
+def test_grad_clip_value_clamps_every_element():
+    a, b = _model(), _model()
+    g = 10 * torch.randn_like(a.store.grad)
+    for m in (a, b):
+        m.store.grad.copy_(g)
+    FusedAdamW(a.store, lr=1e-2, grad_clip_value=0.5).step()
+    b.store.grad.copy_(g.clamp(-0.5, 0.5))
+    FusedAdamW(b.store, lr=1e-2).step()
+    torch.testing.assert_close(a.store.data, b.store.data)
+    # a norm, when set, takes precedence (the reference checks the norm first)
+    assert FusedAdamW(a.store, grad_clip_norm=1.0, grad_clip_value=0.5).clip_value is None
+
+
+def test_optimizer_key_validation():
+    cfg = training_config_from_dict({"optimizer": {"weight_decay_final": 0.01, "grad_clip_value": 1.0}})
+    assert cfg.optimizer.weight_decay_final == 0.01 and not cfg.extras
+    with pytest.raises(ValueError):
+        training_config_from_dict({"optimizer": {"weight_decay_final": -0.1}})
+    with pytest.raises(ValueError):
+        training_config_from_dict({"optimizer": {"grad_clip_value": 0.0}})
