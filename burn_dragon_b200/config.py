@@ -908,6 +908,12 @@ class TrainingConfig:
         self.model.validate()
         self.training.validation.validate()
         o = self.optimizer
+        if o.name == "predictive_coding":
+            # burn_dragon_train/src/train/pipeline/optimizer.rs:250-256
+            raise ValueError("optimizer.name=predictive_coding is retired; predictive coding is a training "
+                             "algorithm: use training.algorithm=predictive_coding with an ordinary update")
+        if o.name not in ("adamw", "eggroll"):
+            raise ValueError(f"optimizer.name {o.name!r} (adamw | eggroll)")
         if o.weight_decay_final is not None and o.weight_decay_final < 0:
             raise ValueError("optimizer.weight_decay_final must be >= 0")
         if o.grad_clip_value is not None and not o.grad_clip_value > 0:

@@ -33,3 +33,10 @@ def test_optimizer_key_validation():
         training_config_from_dict({"optimizer": {"weight_decay_final": -0.1}})
     with pytest.raises(ValueError):
         training_config_from_dict({"optimizer": {"grad_clip_value": 0.0}})
+
+
+def test_predictive_coding_optimizer_name_is_retired():
+    with pytest.raises(ValueError, match="retired"):
+        training_config_from_dict({"optimizer": {"name": "predictive_coding"}})
+    with pytest.raises(ValueError):
+        training_config_from_dict({"optimizer": {"name": "lion"}})
