@@ -823,6 +823,21 @@ class TrainingSection:
     init_transfer: dict[str, Any] = field(default_factory=dict)
     # [{target, scale, schedule = {final_scale, start_fraction, end_fraction}}] (train.module_lr)
     module_lr_scales: list[dict[str, Any]] = field(default_factory=list)
+    # run control (schema.rs TrainingHyperparameters; run_dirs.rs:13-19, 236-290):
+    # epochs: when set, max_iters = epochs x the dataset's steps per epoch
+    epochs: int | None = None
+    # None: resume the named run if it has a checkpoint. fresh | resume_exact_run (needs
+    # resume_run_dir) | resume_latest_checkpoint_if_present (the run root's latest run) |
+    # init_from_checkpoint (needs init_checkpoint_path)
+    launch_mode: str | None = None
+    resume_run_dir: str | None = None
+    resume_checkpoint_epoch: int | None = None  # which checkpoint to resume (default newest)
+    init_checkpoint_epoch: int | None = None  # which checkpoint of init_checkpoint_path
+    # streaming documents are at least this long (rounded up to block_size multiples)
+    min_logical_block_size: int | None = None
+    # the reference's ablation switch to keep an unused terminal state; the fused step
+    # writes the state only when it is consumed, so this changes nothing here
+    retain_ephemeral_terminal_sequence_state: bool = False
     validation: ValidationConfig = field(default_factory=ValidationConfig)
     logit_entropy_floor: LogitEntropyFloorConfig = field(default_factory=LogitEntropyFloorConfig)
     dynamics_anchor: DynamicsAnchorConfig = field(default_factory=DynamicsAnchorConfig)
@@ -907,6 +922,22 @@ class TrainingConfig:
     def validate(self) -> None:
         self.model.validate()
         self.training.validation.validate()
+        t = self.training
+        if t.launch_mode not in (None, "fresh", "resume_exact_run", "resume_latest_checkpoint_if_present",
+                                 "init_from_checkpoint"):
+            raise ValueError(f"training.launch_mode {t.launch_mode!r}")
+        if t.launch_mode in ("fresh", "init_from_checkpoint", "resume_latest_checkpoint_if_present") \
+                and t.resume_run_dir:
+            raise ValueError(f"training.launch_mode = \"{t.launch_mode}\" cannot be combined with "
+                             "training.resume_run_dir")
+        if t.launch_mode == "resume_exact_run" and not t.resume_run_dir:
+            raise ValueError("training.launch_mode = \"resume_exact_run\" requires training.resume_run_dir")
+        if t.launch_mode == "init_from_checkpoint" and not t.init_checkpoint_path:
+            raise ValueError("training.launch_mode = \"init_from_checkpoint\" requires training.init_checkpoint_path")
+        if t.min_logical_block_size is not None and t.min_logical_block_size <= 0:
+            raise ValueError("training.min_logical_block_size must be > 0 when set")
+        if t.epochs is not None and t.epochs <= 0:
+            raise ValueError("training.epochs must be > 0 when set")
         o = self.optimizer
         if o.name == "predictive_coding":
             # burn_dragon_train/src/train/pipeline/optimizer.rs:250-256

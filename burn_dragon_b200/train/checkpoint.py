@@ -191,6 +191,16 @@ def resolve_run_dir(backend: str = "cuda", run_name: str | None = None, root: st
     return os.path.join(run_root, name)
 
 
+def latest_run_dir(run_root: str) -> str | None:
+    """The run named by ``<run_root>/latest``, if that directory exists."""
+    p = os.path.join(run_root, "latest")
+    if not os.path.isfile(p):
+        return None
+    name = open(p).read().strip()
+    d = os.path.join(run_root, name)
+    return d if name and os.path.isdir(d) else None
+
+
 def write_latest_run(run_dir: str) -> None:
     """Record ``run_dir``'s name in its run root's ``latest`` file."""
     root = os.path.dirname(os.path.abspath(run_dir))

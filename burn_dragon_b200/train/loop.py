@@ -56,8 +56,32 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     ck = cfg.parallel.checkpoint or {}
     if ck.get("format", "unsharded_v1") != "unsharded_v1":
         raise ValueError("parallel.checkpoint.format: checkpoints are written unsharded by rank 0 (unsharded_v1)")
-    run = C.RunDir(C.resolve_run_dir(dev.type, run_name, layout=cfg.run_layout, config_paths=cfg.config_paths),
-                   async_write=bool(ck.get("async_write", False)))
+    lm = t.launch_mode
+    if lm in ("fresh", "init_from_checkpoint"):
+        resume = False
+    if lm == "resume_exact_run":
+        if not os.path.isdir(t.resume_run_dir):
+            raise ValueError(f"training.resume_run_dir does not exist or is not a directory: {t.resume_run_dir}")
+        run_path = t.resume_run_dir
+    else:
+        if lm in ("fresh", "init_from_checkpoint") and not run_name and not os.environ.get("BURN_DRAGON_RUN_NAME"):
+            # a fresh launch gets a run directory of its own (run_dirs.rs:143-160); rank 0
+            # names it and the others take that name
+            base = f"run-{time.strftime('%Y%m%d-%H%M%S')}-{os.getpid()}"
+            name, i = [base], 1
+            while os.path.exists(C.resolve_run_dir(dev.type, name[0], layout=cfg.run_layout,
+                                                   config_paths=cfg.config_paths)):
+                i += 1
+                name = [f"{base}-{i}"]
+            if world > 1:
+                dist.broadcast_object_list(name, src=0)
+            run_name = name[0]
+        run_path = C.resolve_run_dir(dev.type, run_name, layout=cfg.run_layout, config_paths=cfg.config_paths)
+        if lm == "resume_latest_checkpoint_if_present" and not run_name:
+            prev = C.latest_run_dir(os.path.dirname(os.path.abspath(run_path)))
+            if prev is not None and C.RunDir(prev).steps():
+                run_path = prev
+    run = C.RunDir(run_path, async_write=bool(ck.get("async_write", False)))
     if rank == 0 and not os.environ.get("BURN_DRAGON_RUN_DIR"):
         C.write_latest_run(run.path)
     if rank == 0:
@@ -111,6 +135,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
         import json
 
         cfg.model.mlp_internal_dim_multiplier = int(json.load(open(ns_path))["mlp_internal_dim_multiplier"])
+    if t.epochs is not None:
+        t.max_iters = t.epochs * _steps_per_epoch(cfg, 1 if mode in ("tensor_parallel_neuron", "pipeline") else world)
     extended = cfg.model.uses_extended_runtime()
     if not cfg.model.uniform_latent_fanout() and (
             mode not in ("single", "ddp", "fsdp") or t.algorithm == "predictive_coding"
@@ -211,7 +237,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     start = 0
     state = None
     if resume and run.latest() is not None:
-        info = run.load(None, trainer.core if extended else trainer.model, trainer.opt, device=dev)
+        info = run.load(t.resume_checkpoint_epoch, trainer.core if extended else trainer.model, trainer.opt,
+                        device=dev)
         start = info["step"]
         trainer.step_idx = start
         if extended and info.get("extra"):
@@ -223,7 +250,7 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
         target = trainer.core if extended else trainer.model
         fresh = {n: getattr(target, n).detach().clone() for n in target.store.shapes}
         src = C.RunDir(t.init_checkpoint_path)
-        src.load(None, target, None, device=dev)
+        src.load(t.init_checkpoint_epoch, target, None, device=dev)
         if t.init_transfer:
             from ..config import _fill
             from .init_transfer import InitTransferConfig, apply_init_transfer
@@ -258,7 +285,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
             native = None
     if streaming:
         chunk = t.tbptt_chunk_size or t.block_size
-        data = StreamingBytes(t.batch_size, t.block_size, chunk, seed=t.seed, rank=data_rank)
+        # a stream (document) is min_logical_block_size tokens rounded up to whole blocks
+        doc = -(-max(t.min_logical_block_size or t.block_size, t.block_size) // t.block_size) * t.block_size
+        data = StreamingBytes(t.batch_size, doc, chunk, seed=t.seed, rank=data_rank)
         data.pos = (start * chunk) % max(1, t.block_size - chunk + 1) if t.block_size > chunk else 0
     elif cfg.dataset.type == "file" and native is None:
         data = FileBytes(cfg.dataset.path, t.batch_size, t.block_size, "train", cfg.dataset.train_split_ratio,
@@ -465,3 +494,17 @@ def _autograd_step(trainer, loss) -> None:
     trainer.opt.prepare(lr_at(trainer.step_idx, trainer.base_lr, trainer.lr_schedule, trainer.max_iters))
     trainer._update()
     trainer.step_idx += 1
+
+
+def _steps_per_epoch(cfg: TrainingConfig, data_world: int) -> int:
+    """One pass over the train split of a file dataset in [batch, block] windows per
+    data-parallel rank; a synthetic stream has no end, so its epoch is the checkpoint
+    interval (the reference's fallback, burn_dragon_language/src/train/backend.rs:61-72)."""
+    t = cfg.training
+    if cfg.dataset.type == "file":
+        from .datasets import token_bytes
+
+        n = os.path.getsize(cfg.dataset.path) // token_bytes(cfg.dataset.path)
+        train = int(n * cfg.dataset.train_split_ratio)
+        return max(1, train // (t.batch_size * t.block_size * max(data_world, 1)))
+    return max(1, min(t.checkpoint_interval_iters or t.max_iters, t.max_iters))
