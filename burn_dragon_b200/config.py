@@ -838,6 +838,9 @@ class TrainingSection:
     # the reference's ablation switch to keep an unused terminal state; the fused step
     # writes the state only when it is consumed, so this changes nothing here
     retain_ephemeral_terminal_sequence_state: bool = False
+    # {enabled, paired_batches, max_rho_slots}: stream-warm validation with a warm / cold
+    # carry probe (train.state_probe)
+    sequence_state_probe: dict[str, Any] = field(default_factory=dict)
     validation: ValidationConfig = field(default_factory=ValidationConfig)
     logit_entropy_floor: LogitEntropyFloorConfig = field(default_factory=LogitEntropyFloorConfig)
     dynamics_anchor: DynamicsAnchorConfig = field(default_factory=DynamicsAnchorConfig)

@@ -307,6 +307,13 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     else:
         valid = RandomBytes(t.batch_size, t.block_size, seed=vseed, rank=data_rank, world=data_world)
     validate_here = t.validation.execution == "local"
+    probe = None
+    if t.sequence_state_probe.get("enabled"):
+        from .state_probe import SequenceStateProbeConfig
+
+        if not streaming or extended:
+            raise ValueError("training.sequence_state_probe needs streaming batches on the plain BDH model")
+        probe = SequenceStateProbeConfig(**dict(t.sequence_state_probe))
 
     log = MetricsLogger(run.path, rank, every=t.log_frequency)
     # which step implementation this run takes, and its forward FLOP estimate (the
@@ -440,6 +447,16 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                 last_loss = lv
             if validate_here and t.validation_interval_iters and (step + 1) % t.validation_interval_iters == 0 \
                     and runner is None:
+                if probe is not None:
+                    from .state_probe import stream_warm_validation
+
+                    chunk_v = t.tbptt_chunk_size or t.block_size
+                    vstream = StreamingBytes(t.batch_size, doc, chunk_v, vocab=cfg.model.vocab_size, seed=vseed,
+                                             rank=data_rank)
+                    rep = stream_warm_validation(trainer.model, vstream, max(doc // chunk_v, 1) * 2, probe, dev)
+                    log.log(step + 1, **{f"stream_{k}": v for k, v in rep.items() if k != "state"}, force=True)
+                    if rank == 0:
+                        run.write_json("sequence_state_probe.json", {"step": step + 1, **rep})
                 if t.validation.sampling == "fixed_holdout":
                     valid.step = 0
                 vx, vy = valid.next()

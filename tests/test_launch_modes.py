@@ -81,3 +81,17 @@ def test_min_logical_block_size_lengthens_streams(tmp_path, monkeypatch, capsys)
     _run(capsys, "--set", 'training.sequence_batching="streaming"', "--set", "training.tbptt_chunk_size=16",
          "--set", "training.min_logical_block_size=70", "--set", "training.max_iters=2", "--run-name", "ml")
     assert seen["len"] == 96  # 70 rounded up to whole 32-token blocks
+
+
+def test_sequence_state_probe_reports_warm_and_cold(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    res = _run(capsys, "--set", 'training.sequence_batching="streaming"', "--set", "training.tbptt_chunk_size=16",
+               "--set", "training.max_iters=2", "--set", "training.validation_interval_iters=2",
+               "--set", "training.sequence_state_probe={enabled=true, paired_batches=2, max_rho_slots=1}",
+               "--run-name", "probe")
+    rep = json.load(open(os.path.join(res["run_dir"], "sequence_state_probe.json")))
+    assert rep["paired_batches"] == 2 and rep["warm_loss"] > 0
+    assert abs(rep["carry_nll_gain"] - (rep["paired_cold_loss"] - rep["paired_warm_loss"])) < 1e-9
+    assert len(rep["state"]) == 1 and rep["state"][0]["present"]
+    ev = [json.loads(x) for x in open(os.path.join(res["run_dir"], "events", "metrics.jsonl"))]
+    assert any("stream_carry_nll_gain" in e for e in ev)
