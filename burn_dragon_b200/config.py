@@ -841,6 +841,12 @@ class TrainingSection:
     # {enabled, paired_batches, max_rho_slots}: stream-warm validation with a warm / cold
     # carry probe (train.state_probe)
     sequence_state_probe: dict[str, Any] = field(default_factory=dict)
+    # a [model.sequence_kernel] table that replaces the model's for training (applied by
+    # the loader; burn_dragon_language/src/train/backend.rs:755-770)
+    sequence_kernel_override: dict[str, Any] | None = None
+    # context strategy of generation done during training ({type = "infinite"} |
+    # {type = "sliding", window}), checked like generation.context_strategy
+    context_strategy: dict[str, Any] = field(default_factory=lambda: {"type": "infinite"})
     validation: ValidationConfig = field(default_factory=ValidationConfig)
     logit_entropy_floor: LogitEntropyFloorConfig = field(default_factory=LogitEntropyFloorConfig)
     dynamics_anchor: DynamicsAnchorConfig = field(default_factory=DynamicsAnchorConfig)
@@ -955,6 +961,8 @@ class TrainingConfig:
         if self.generation.output_format not in ("auto", "decoded_text", "token_ids"):
             raise ValueError(f"generation.output_format {self.generation.output_format!r}")
         self.generation.sliding_window(self.training.block_size)
+        GenerationConfig(context_strategy=dict(self.training.context_strategy)).sliding_window(
+            self.training.block_size)
         p = self.parallel.mode
         if p not in ("single", "ddp", "fsdp", "tensor_parallel_neuron", "hybrid_2d", "pipeline"):
             raise ValueError(f"unknown parallel.mode {p!r}")
@@ -1108,6 +1116,10 @@ def training_config_from_dict(data: dict) -> TrainingConfig:
                          ("generation", GenerationConfig), ("run_layout", RunLayoutConfig)):
         if section in data:
             setattr(cfg, section, _fill(cls, data[section], extras, f"{section}."))
+    sko = (data.get("training") or {}).get("sequence_kernel_override")
+    if sko is not None:
+        data = dict(data)
+        data["model"] = {**dict(data.get("model") or {}), "sequence_kernel": sko}
     if "model" in data:
         cfg.model = _fill(DragonConfig, _model_table(data["model"]), extras, "model.")
     for k, v in data.items():

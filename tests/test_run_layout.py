@@ -95,3 +95,12 @@ def test_generation_context_strategy():
     assert training_config_from_dict({}).generation.sliding_window(64) is None
     with pytest.raises(ValueError):
         training_config_from_dict({"generation": {"context_strategy": {"type": "ring"}}})
+
+
+def test_training_sequence_kernel_override_and_context_strategy():
+    cfg = training_config_from_dict({"model": {"sequence_kernel": {"memory_system": "linear_attention"}},
+                                     "training": {"sequence_kernel_override": {"memory_system": "gated_deltanet2",
+                                                                               "executor": "reference"}}})
+    assert cfg.model.sequence_memory_system == "gated_deltanet2" and not cfg.extras
+    with pytest.raises(ValueError):
+        training_config_from_dict({"training": {"context_strategy": {"type": "ring"}}})
