@@ -841,6 +841,8 @@ class TrainingSection:
     # {enabled, paired_batches, max_rho_slots}: stream-warm validation with a warm / cold
     # carry probe (train.state_probe)
     sequence_state_probe: dict[str, Any] = field(default_factory=dict)
+    # recurrent-state predictive coding (train.state_pc.RecurrentStatePCConfig keys)
+    predictive_coding: dict[str, Any] = field(default_factory=dict)
     # a [model.sequence_kernel] table that replaces the model's for training (applied by
     # the loader; burn_dragon_language/src/train/backend.rs:755-770)
     sequence_kernel_override: dict[str, Any] | None = None

@@ -307,6 +307,16 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     else:
         valid = RandomBytes(t.batch_size, t.block_size, seed=vseed, rank=data_rank, world=data_world)
     validate_here = t.validation.execution == "local"
+    spc = None
+    if t.predictive_coding.get("enabled"):
+        from .state_pc import RecurrentStatePCConfig
+
+        spc = RecurrentStatePCConfig(**dict(t.predictive_coding))
+        spc.validate()
+        if not streaming or extended or mode not in ("single", "ddp", "fsdp") \
+                or getattr(trainer, "comm", None) is not None:
+            raise ValueError("training.predictive_coding (recurrent-state inference) needs streaming TBPTT "
+                             "batches on the plain BDH model in single / ddp mode")
     probe = None
     if t.sequence_state_probe.get("enabled"):
         from .state_probe import SequenceStateProbeConfig
@@ -364,6 +374,16 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                 trainer.step_idx += 1
                 prof.stop("optimizer")
                 loss = loss if loss is not None else torch.zeros(())
+            elif streaming and spc is not None:
+                from .state_pc import state_pc_chunk_loss
+
+                if state.rhos is not None:
+                    state.rhos = [r.detach() for r in state.rhos]
+                lo, state, _ = state_pc_chunk_loss(trainer.model, x.to(dev), y.to(dev), state, spc, step)
+                _autograd_step(trainer, lo)
+                state.detach_in_place()
+                loss = lo.detach()
+                prof.stop("forward_backward")
             elif streaming:
                 loss = trainer.step_stream(x, y, state)
                 prof.stop("forward_backward")
