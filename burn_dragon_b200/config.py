@@ -843,6 +843,8 @@ class TrainingSection:
     sequence_state_probe: dict[str, Any] = field(default_factory=dict)
     # recurrent-state predictive coding (train.state_pc.RecurrentStatePCConfig keys)
     predictive_coding: dict[str, Any] = field(default_factory=dict)
+    # training-side latent reasoning (train.latent_reasoning.LatentReasoningTraining keys)
+    latent_reasoning: dict[str, Any] = field(default_factory=dict)
     # a [model.sequence_kernel] table that replaces the model's for training (applied by
     # the loader; burn_dragon_language/src/train/backend.rs:755-770)
     sequence_kernel_override: dict[str, Any] | None = None

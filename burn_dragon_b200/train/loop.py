@@ -307,6 +307,13 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     else:
         valid = RandomBytes(t.batch_size, t.block_size, seed=vseed, rank=data_rank, world=data_world)
     validate_here = t.validation.execution == "local"
+    if t.latent_reasoning.get("enabled"):
+        if not (extended and cfg.model.latent_reasoning.enabled):
+            raise ValueError("training.latent_reasoning needs model.latent_reasoning.enabled (its JEPA predictor)")
+        from .latent_reasoning import LatentReasoningTraining
+
+        trainer.latent_training = LatentReasoningTraining(t.latent_reasoning, cfg.model)
+        trainer.latent_training.attach_teacher(trainer.model)
     spc = None
     if t.predictive_coding.get("enabled"):
         from .state_pc import RecurrentStatePCConfig

@@ -15,6 +15,7 @@ import torch
 import torch.distributed as dist
 
 from ..config import DragonConfig
+from ..models import reference as R
 from ..models.dragon_runtime import DragonRuntime, RuntimeState
 from .optim import FusedAdamW, lr_at
 
@@ -81,9 +82,20 @@ class RuntimeTrainer:
     def step(self, tokens, targets, mask=None, event_mask=None) -> torch.Tensor:
         tokens = tokens.to(self.device, non_blocking=True)
         targets = targets.to(self.device, non_blocking=True)
-        loss = self.model.loss(tokens, targets, mask, event_mask=event_mask)
+        lrt = getattr(self, "latent_training", None)
+        if lrt is not None and lrt.active(self.step_idx):
+            # the training-side latent-reasoning terms read the final hidden states
+            h = self.model.forward_hidden(tokens, event_mask=event_mask)
+            loss = R.cross_entropy(self.model.logits_from_hidden(h), targets, mask)
+            aux = lrt.loss(self.model, h, tokens, self.step_idx)
+            if aux is not None:
+                loss = loss + aux
+        else:
+            loss = self.model.loss(tokens, targets, mask, event_mask=event_mask)
         self._grads(loss)
         self._update()
+        if lrt is not None and lrt.teacher is not None:
+            lrt.teacher.update(self.model)
         return loss.detach()
 
     def step_stream(self, tokens, targets, state: RuntimeState) -> torch.Tensor:

@@ -1,0 +1,65 @@
+"""Training-side latent reasoning (CPU): SigReg and JEPA terms against direct
+computations, the schedule, rejected options and a training run."""
+
+import json
+import os
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from burn_dragon_b200.config import DragonConfig
+from burn_dragon_b200.train.latent_reasoning import LatentReasoningTraining
+
+CFG = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu_variants.toml")
+
+
+def _mc():
+    return DragonConfig(n_layer=1, n_embd=8, n_head=2, mlp_internal_dim_multiplier=4, vocab_size=16, dropout=0.0)
+
+
+def test_schedule_and_rejections():
+    lr = LatentReasoningTraining({"enabled": True, "jepa_every_steps": 2, "constraint_balancer":
+                                  {"normalized_aux_scale": 2.0, "start_after_steps": 1, "warmup_steps": 4},
+                                  "sigreg": {"enabled": False}}, _mc())
+    assert lr._scale(0, 2, None) is None  # step 1 is not after start 1
+    assert lr._scale(2, 2, None) is None  # step 3 is odd
+    assert lr._scale(1, 2, None) is not None and abs(lr._scale(3, 2, None) - 2.0 * 3 / 4) < 1e-9
+    with pytest.raises(ValueError):
+        LatentReasoningTraining({"next_latent": {"enabled": True}}, _mc())
+    with pytest.raises(ValueError):
+        LatentReasoningTraining({"start_after_capability_gate_passed": True}, _mc())
+
+
+def test_sigreg_and_jepa_values():
+    torch.manual_seed(0)
+    h = torch.randn(2, 6, 8) * 0.3 + 0.2
+    lr = LatentReasoningTraining({"jepa_future_offsets": [2], "sigreg": {"min_variance": 0.2,
+                                                                         "mean_tolerance": 0.05}}, _mc())
+    mean = h.mean((0, 1))
+    var = ((h - mean) ** 2).mean((0, 1))
+    want = ((0.2 - var).clamp_min(0) ** 2).mean() + ((mean.abs() - 0.05).clamp_min(0) ** 2).mean()
+    torch.testing.assert_close(lr.sigreg(h), want)
+
+    class M:
+        @staticmethod
+        def latent_jepa_prediction(x):
+            return 0.5 * x
+
+    got = lr.loss(M(), h, None, 0)
+    pred, tgt = 0.5 * h[:, :4], h[:, 2:]
+    neg = torch.cat([tgt[1:], tgt[:1]], 0)
+    pos = ((pred - tgt) ** 2).mean()
+    jepa = pos + F.softplus(pos - ((pred - neg) ** 2).mean() + 1.0)
+    torch.testing.assert_close(got, (jepa + want) / 2)
+
+
+def test_training_run_with_latent_terms(tmp_path, monkeypatch, capsys):
+    from burn_dragon_b200.cli.train import main
+
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", CFG, "--set", "training.max_iters=2",
+          "--set", 'training.latent_reasoning={enabled=true, target_encoder="ema_teacher", jepa_future_offsets=[1, 2]}',
+          "--run-name", "lrt"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None
