@@ -11,6 +11,12 @@ negatives, SigReg); config schema.rs:780-1080 (LatentReasoningTrainingConfig).
   to the target and E- to a shifted negative (the batch rolled by one, or time rolled by
   one when the batch has one row). Targets are the detached student hiddens, or an EMA
   teacher's (``target_encoder = "ema_teacher"``).
+* next latent (steps.rs:9847-9927, helpers train/next_latent.rs:7-32): the model's
+  transition predicts the hidden at t + 1 from the hidden at t and the embedding of
+  token t + 1 (detached by default), rolled out ``horizon`` steps on its own
+  predictions; each step adds ``regression_weight`` x smooth-L1(beta) to the target
+  hidden and ``token_kl_weight`` x forward KL between the head's distributions of the
+  target and the prediction; the sum is averaged over its terms.
 * SigReg on the hidden: ``mean relu(min_variance - var_d)^2 + mean relu(|mean_d| -
   mean_tolerance)^2`` over feature dims d (statistics over batch and time).
 * Each term is scaled by ``constraint_balancer.normalized_aux_scale`` (ramped over its
@@ -18,7 +24,7 @@ negatives, SigReg); config schema.rs:780-1080 (LatentReasoningTrainingConfig).
   and after its ``start_after_steps``; the total is divided by the number of active
   terms and added to the next-token CE.
 
-Not built here: the next-latent transition, Dragon-state consistency, energy-model and
+Not built here: Dragon-state consistency, energy-model and
 step-contract terms, SigReg on rho memory slots, and starts gated on the capability gate
 of the event crate (the reference's ``burn_ecs``, absent from its repository); enabling
 one of them is an error rather than a silent no-op.
@@ -59,7 +65,17 @@ class LatentReasoningTraining:
                 for p in (c.get("jepa_start_policy"), sg.get("start_policy"))):
             raise ValueError("latent-reasoning starts gated on the capability gate need the event crate's gate, "
                              "which is not built here")
-        for k in ("next_latent", "dragon_state", "energy_model", "step_contract"):
+        nl = dict(c.get("next_latent", {}))
+        self.nl_enabled = bool(nl.get("enabled", False))
+        self.nl_every, self.nl_start = nl.get("every_steps"), nl.get("start_after_steps")
+        self.nl_horizon = int(nl.get("horizon", 1))
+        self.nl_reg = max(float(nl.get("regression_weight", 1.0)), 0.0)
+        self.nl_kl = max(float(nl.get("token_kl_weight", 0.0)), 0.0)
+        self.nl_beta = float(nl.get("smooth_l1_beta", 1.0))
+        self.nl_detach = bool(nl.get("detach_action_embedding", True))
+        if self.nl_enabled and not model_cfg.next_latent_transition.enabled:
+            raise ValueError("training.latent_reasoning.next_latent needs model.next_latent_transition.enabled")
+        for k in ("dragon_state", "energy_model", "step_contract"):
             if dict(c.get(k, {})).get("enabled"):
                 raise ValueError(f"training.latent_reasoning.{k} is not implemented here")
         if self.sg_enabled and self.sg_target != "hidden":
@@ -86,6 +102,8 @@ class LatentReasoningTraining:
         return s if s > _EPS else None
 
     def active(self, step: int) -> bool:
+        if self.nl_enabled and self._scale(step, self.nl_every, self.nl_start) is not None:
+            return True
         return self._scale(step, self.jepa_every, self.jepa_start) is not None or (
             self.sg_enabled and self._scale(step, self.sg_every, self.sg_start) is not None)
 
@@ -97,6 +115,42 @@ class LatentReasoningTraining:
             return torch.cat([t[:, 1:], t[:, :1]], 1)
         return t
 
+    @staticmethod
+    def smooth_l1(pred, target, beta: float) -> torch.Tensor:
+        beta = max(beta, 1e-8)
+        a = (pred - target).abs()
+        lin = (a - beta).clamp_min(0.0)
+        quad = a - lin
+        return (quad.pow(2) * (0.5 / beta) + lin).mean()
+
+    def next_latent(self, model, hidden, target, tokens) -> torch.Tensor | None:
+        from .objectives import self_distillation_per_token
+
+        B, T, _ = hidden.shape
+        if T < 2 or (self.nl_reg <= _EPS and self.nl_kl <= _EPS):
+            return None
+        embed = model.core.param_dict()["embed"]
+        roll, total, n = hidden, None, 0
+        for i in range(min(self.nl_horizon, T - 1)):
+            rt = T - (i + 1)
+            act = embed[tokens[:, i + 1:]]
+            if self.nl_detach:
+                act = act.detach()
+            pred = model.next_latent_prediction(roll[:, :rt], act)
+            if pred is None:
+                break
+            tgt = target[:, i + 1:].detach()
+            if self.nl_reg > _EPS:
+                term = self.nl_reg * self.smooth_l1(pred, tgt, self.nl_beta)
+                total, n = (term if total is None else total + term), n + 1
+            if self.nl_kl > _EPS:
+                s_lp = F.log_softmax(model.logits_from_hidden(pred).float(), -1)
+                t_lp = F.log_softmax(model.logits_from_hidden(tgt).detach().float(), -1)
+                term = self.nl_kl * self_distillation_per_token(s_lp, t_lp, "forward").mean()
+                total, n = (term if total is None else total + term), n + 1
+            roll = pred
+        return None if total is None else total / max(n, 1)
+
     def sigreg(self, h: torch.Tensor) -> torch.Tensor:
         mean = h.mean(dim=(0, 1))
         var = (h - mean).pow(2).mean(dim=(0, 1))
@@ -105,14 +159,21 @@ class LatentReasoningTraining:
     def loss(self, model, hidden: torch.Tensor, tokens: torch.Tensor, step: int) -> torch.Tensor | None:
         js = self._scale(step, self.jepa_every, self.jepa_start)
         ss = self._scale(step, self.sg_every, self.sg_start) if self.sg_enabled else None
+        ns = self._scale(step, self.nl_every, self.nl_start) if self.nl_enabled else None
         total, n = None, 0
         B, T, _ = hidden.shape
-        if js is not None:
+        target = None
+        if js is not None or ns is not None:
             if self.teacher is not None:
                 with torch.no_grad():
                     target = self.teacher.model.forward_hidden(tokens).detach()
             else:
                 target = hidden.detach()
+        if ns is not None:
+            term = self.next_latent(model, hidden, target, tokens)
+            if term is not None:
+                total, n = ns * term, 1
+        if js is not None:
             for k in (k for k in self.offsets if 0 < k < T):
                 pred = model.latent_jepa_prediction(hidden[:, :T - k])
                 tgt = target[:, k:]

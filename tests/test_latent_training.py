@@ -63,3 +63,39 @@ def test_training_run_with_latent_terms(tmp_path, monkeypatch, capsys):
           "--run-name", "lrt"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res["final_loss"] is not None
+
+
+def test_smooth_l1_fixture_and_next_latent_run(tmp_path, monkeypatch, capsys):
+    got = LatentReasoningTraining.smooth_l1(torch.tensor([[[0.5], [3.0]]]), torch.tensor([[[0.0], [1.0]]]), 1.0)
+    assert abs(float(got) - 0.8125) < 1e-6  # (0.125 + 1.5) / 2
+    with pytest.raises(ValueError, match="next_latent_transition"):
+        LatentReasoningTraining({"next_latent": {"enabled": True}}, _mc())
+    from burn_dragon_b200.cli.train import main
+
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", CFG, "--set", "training.max_iters=2", "--set", "model.next_latent_transition={enabled=true}",
+          "--set", "training.latent_reasoning={enabled=true, sigreg={enabled=false}, jepa_future_offsets=[], "
+                   "next_latent={enabled=true, horizon=2, token_kl_weight=0.5}}",
+          "--run-name", "nl"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None
+
+
+def test_next_latent_term_matches_a_direct_rollout():
+    from burn_dragon_b200.models.dragon_runtime import DragonRuntime
+
+    mc = _mc()
+    mc.latent_reasoning.enabled = True
+    mc.next_latent_transition.enabled = True
+    mc.next_latent_transition.zero_init_output = False
+    m = DragonRuntime(mc, seed=1)
+    tok = torch.randint(0, 16, (2, 5))
+    h = m.forward_hidden(tok)
+    lr = LatentReasoningTraining({"sigreg": {"enabled": False}, "jepa_future_offsets": [],
+                                  "next_latent": {"enabled": True, "horizon": 2}}, mc)
+    got = lr.next_latent(m, h, h.detach(), tok)
+    emb = m.core.param_dict()["embed"]
+    p1 = m.next_latent_prediction(h[:, :4], emb[tok[:, 1:]].detach())
+    p2 = m.next_latent_prediction(p1[:, :3], emb[tok[:, 2:]].detach())
+    want = (lr.smooth_l1(p1, h[:, 1:].detach(), 1.0) + lr.smooth_l1(p2, h[:, 2:].detach(), 1.0)) / 2
+    torch.testing.assert_close(got, want)
