@@ -17,6 +17,12 @@ negatives, SigReg); config schema.rs:780-1080 (LatentReasoningTrainingConfig).
   predictions; each step adds ``regression_weight`` x smooth-L1(beta) to the target
   hidden and ``token_kl_weight`` x forward KL between the head's distributions of the
   target and the prediction; the sum is averaged over its terms.
+* energy model (steps.rs:9929-10010, :1015-1054): over the first
+  ``max_rollout_steps_for_loss`` refinement steps of the model's latent reasoning on the
+  hidden, ``contrastive_weight`` x softplus(E_step - E(negative) + margin),
+  ``monotonic_weight`` x relu(E_step - E_prev(detached) - tolerance) and
+  ``contractive_weight`` x relu(rms(step - target) / rms(target) - trust_radius),
+  averaged over its terms (E from the model's energy head).
 * SigReg on the hidden: ``mean relu(min_variance - var_d)^2 + mean relu(|mean_d| -
   mean_tolerance)^2`` over feature dims d (statistics over batch and time).
 * Each term is scaled by ``constraint_balancer.normalized_aux_scale`` (ramped over its
@@ -24,8 +30,7 @@ negatives, SigReg); config schema.rs:780-1080 (LatentReasoningTrainingConfig).
   and after its ``start_after_steps``; the total is divided by the number of active
   terms and added to the next-token CE.
 
-Not built here: Dragon-state consistency, energy-model and
-step-contract terms, SigReg on rho memory slots, and starts gated on the capability gate
+Not built here: Dragon-state consistency and step-contract terms, SigReg on rho memory slots, and starts gated on the capability gate
 of the event crate (the reference's ``burn_ecs``, absent from its repository); enabling
 one of them is an error rather than a silent no-op.
 """
@@ -75,7 +80,16 @@ class LatentReasoningTraining:
         self.nl_detach = bool(nl.get("detach_action_embedding", True))
         if self.nl_enabled and not model_cfg.next_latent_transition.enabled:
             raise ValueError("training.latent_reasoning.next_latent needs model.next_latent_transition.enabled")
-        for k in ("dragon_state", "energy_model", "step_contract"):
+        em = dict(c.get("energy_model", {}))
+        self.em_enabled = bool(em.get("enabled", False))
+        self.em_every, self.em_start = em.get("every_steps"), em.get("start_after_steps")
+        self.em = {k: float(em.get(k, d)) for k, d in (("contrastive_weight", 1.0), ("monotonic_weight", 0.25),
+                                                         ("contractive_weight", 0.05), ("margin", 1.0),
+                                                         ("monotonic_tolerance", 0.0), ("trust_radius", 1.0))}
+        self.em_steps = int(em.get("max_rollout_steps_for_loss", 4))
+        if self.em_enabled and not model_cfg.latent_reasoning.energy_head:
+            raise ValueError("training.latent_reasoning.energy_model needs model.latent_reasoning.energy_head")
+        for k in ("dragon_state", "step_contract"):
             if dict(c.get(k, {})).get("enabled"):
                 raise ValueError(f"training.latent_reasoning.{k} is not implemented here")
         if self.sg_enabled and self.sg_target != "hidden":
@@ -102,6 +116,8 @@ class LatentReasoningTraining:
         return s if s > _EPS else None
 
     def active(self, step: int) -> bool:
+        if self.em_enabled and self._scale(step, self.em_every, self.em_start) is not None:
+            return True
         if self.nl_enabled and self._scale(step, self.nl_every, self.nl_start) is not None:
             return True
         return self._scale(step, self.jepa_every, self.jepa_start) is not None or (
@@ -151,6 +167,33 @@ class LatentReasoningTraining:
             roll = pred
         return None if total is None else total / max(n, 1)
 
+    def energy_model(self, model, hidden, target) -> torch.Tensor | None:
+        e = self.em
+        prev = model.latent_energy(hidden)
+        out = model.reason_hidden(hidden)
+        if prev is None or not out.step_hiddens or not out.energies:
+            return None
+        target = target.detach()
+        neg_e = model.latent_energy(self.shifted_negative(target).detach())
+        tscale = target.pow(2).mean().sqrt().detach().clamp_min(1e-6)
+        total, n = None, 0
+        for st, en in list(zip(out.step_hiddens, out.energies))[:self.em_steps]:
+            terms = []
+            if e["contrastive_weight"] > _EPS and neg_e is not None:
+                terms.append(e["contrastive_weight"] * F.softplus(en - neg_e + max(e["margin"], 0.0)).mean())
+            if e["monotonic_weight"] > _EPS:
+                terms.append(e["monotonic_weight"] * (en - prev.detach() - max(e["monotonic_tolerance"], 0.0))
+                             .clamp_min(0.0).mean())
+            if e["contractive_weight"] > _EPS:
+                # clamped: a zero-initialised refiner starts exactly on the target, where
+                # the square root's derivative is undefined
+                rms = (st - target).pow(2).mean().clamp_min(1e-12).sqrt()
+                terms.append(e["contractive_weight"] * (rms / tscale - max(e["trust_radius"], 0.0)).clamp_min(0.0))
+            for t in terms:
+                total, n = (t if total is None else total + t), n + 1
+            prev = en
+        return None if total is None else total / max(n, 1)
+
     def sigreg(self, h: torch.Tensor) -> torch.Tensor:
         mean = h.mean(dim=(0, 1))
         var = (h - mean).pow(2).mean(dim=(0, 1))
@@ -160,10 +203,11 @@ class LatentReasoningTraining:
         js = self._scale(step, self.jepa_every, self.jepa_start)
         ss = self._scale(step, self.sg_every, self.sg_start) if self.sg_enabled else None
         ns = self._scale(step, self.nl_every, self.nl_start) if self.nl_enabled else None
+        es = self._scale(step, self.em_every, self.em_start) if self.em_enabled else None
         total, n = None, 0
         B, T, _ = hidden.shape
         target = None
-        if js is not None or ns is not None:
+        if js is not None or ns is not None or es is not None:
             if self.teacher is not None:
                 with torch.no_grad():
                     target = self.teacher.model.forward_hidden(tokens).detach()
@@ -173,6 +217,10 @@ class LatentReasoningTraining:
             term = self.next_latent(model, hidden, target, tokens)
             if term is not None:
                 total, n = ns * term, 1
+        if es is not None:
+            term = self.energy_model(model, hidden, target)
+            if term is not None:
+                total, n = (es * term if total is None else total + es * term), n + 1
         if js is not None:
             for k in (k for k in self.offsets if 0 < k < T):
                 pred = model.latent_jepa_prediction(hidden[:, :T - k])

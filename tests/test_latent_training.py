@@ -99,3 +99,34 @@ def test_next_latent_term_matches_a_direct_rollout():
     p2 = m.next_latent_prediction(p1[:, :3], emb[tok[:, 2:]].detach())
     want = (lr.smooth_l1(p1, h[:, 1:].detach(), 1.0) + lr.smooth_l1(p2, h[:, 2:].detach(), 1.0)) / 2
     torch.testing.assert_close(got, want)
+
+
+def test_energy_model_term_and_run(tmp_path, monkeypatch, capsys):
+    from burn_dragon_b200.models.dragon_runtime import DragonRuntime
+
+    mc = _mc()
+    mc.latent_reasoning.enabled = True
+    mc.latent_reasoning.energy_head = True
+    mc.latent_reasoning.max_steps = 2
+    m = DragonRuntime(mc, seed=2)
+    tok = torch.randint(0, 16, (2, 5))
+    h = m.forward_hidden(tok)
+    lr = LatentReasoningTraining({"sigreg": {"enabled": False}, "jepa_future_offsets": [],
+                                  "energy_model": {"enabled": True, "trust_radius": 0.0}}, mc)
+    got = lr.energy_model(m, h, h.detach())
+    out = m.reason_hidden(h)
+    tgt = h.detach()
+    neg_e = m.latent_energy(torch.cat([tgt[1:], tgt[:1]], 0))
+    prev, terms = m.latent_energy(h), []
+    for st, en in zip(out.step_hiddens, out.energies):
+        terms += [F.softplus(en - neg_e + 1.0).mean(), 0.25 * (en - prev.detach()).clamp_min(0).mean(),
+                  0.05 * ((st - tgt).pow(2).mean().sqrt() / tgt.pow(2).mean().sqrt())]
+        prev = en
+    torch.testing.assert_close(got, sum(terms) / len(terms))
+    from burn_dragon_b200.cli.train import main
+
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", CFG, "--set", "training.max_iters=2", "--set", "model.latent_reasoning.energy_head=true",
+          "--set", "training.latent_reasoning={enabled=true, energy_model={enabled=true}}", "--run-name", "em"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None
