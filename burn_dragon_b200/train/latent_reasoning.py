@@ -23,6 +23,12 @@ negatives, SigReg); config schema.rs:780-1080 (LatentReasoningTrainingConfig).
   ``monotonic_weight`` x relu(E_step - E_prev(detached) - tolerance) and
   ``contractive_weight`` x relu(rms(step - target) / rms(target) - trust_radius),
   averaged over its terms (E from the model's energy head).
+* step contract (steps.rs, latent_step_contract_auxiliary_loss): over the first
+  ``max_rollout_steps_for_loss`` refinement steps, ``ce_weight`` x the step's CE (its
+  step-conditioned logits), ``monotonic_ce_weight`` x relu(CE_step - CE_prev(detached) -
+  ce_tolerance) (CE_0 from the hidden itself), ``token_kl_weight`` x forward KL to the
+  final reasoned logits (detached) and ``contractive_weight`` x relu(rms(step - prev) /
+  rms(prev) - trust_radius), averaged over its terms.
 * SigReg on the hidden: ``mean relu(min_variance - var_d)^2 + mean relu(|mean_d| -
   mean_tolerance)^2`` over feature dims d (statistics over batch and time).
 * Each term is scaled by ``constraint_balancer.normalized_aux_scale`` (ramped over its
@@ -30,7 +36,7 @@ negatives, SigReg); config schema.rs:780-1080 (LatentReasoningTrainingConfig).
   and after its ``start_after_steps``; the total is divided by the number of active
   terms and added to the next-token CE.
 
-Not built here: Dragon-state consistency and step-contract terms, SigReg on rho memory slots, and starts gated on the capability gate
+Not built here: the Dragon-state consistency term, SigReg on rho memory slots, and starts gated on the capability gate
 of the event crate (the reference's ``burn_ecs``, absent from its repository); enabling
 one of them is an error rather than a silent no-op.
 """
@@ -89,7 +95,14 @@ class LatentReasoningTraining:
         self.em_steps = int(em.get("max_rollout_steps_for_loss", 4))
         if self.em_enabled and not model_cfg.latent_reasoning.energy_head:
             raise ValueError("training.latent_reasoning.energy_model needs model.latent_reasoning.energy_head")
-        for k in ("dragon_state", "step_contract"):
+        sc = dict(c.get("step_contract", {}))
+        self.sc_enabled = bool(sc.get("enabled", False))
+        self.sc_every, self.sc_start = sc.get("every_steps"), sc.get("start_after_steps")
+        self.sc = {k: float(sc.get(k, d)) for k, d in (("ce_weight", 0.0), ("token_kl_weight", 0.0),
+                                                         ("monotonic_ce_weight", 1.0), ("contractive_weight", 0.05),
+                                                         ("ce_tolerance", 0.0), ("trust_radius", 1.0))}
+        self.sc_steps = max(int(sc.get("max_rollout_steps_for_loss", 4)), 1)
+        for k in ("dragon_state",):
             if dict(c.get(k, {})).get("enabled"):
                 raise ValueError(f"training.latent_reasoning.{k} is not implemented here")
         if self.sg_enabled and self.sg_target != "hidden":
@@ -116,6 +129,8 @@ class LatentReasoningTraining:
         return s if s > _EPS else None
 
     def active(self, step: int) -> bool:
+        if self.sc_enabled and self._scale(step, self.sc_every, self.sc_start) is not None:
+            return True
         if self.em_enabled and self._scale(step, self.em_every, self.em_start) is not None:
             return True
         if self.nl_enabled and self._scale(step, self.nl_every, self.nl_start) is not None:
@@ -194,12 +209,56 @@ class LatentReasoningTraining:
             prev = en
         return None if total is None else total / max(n, 1)
 
+    @staticmethod
+    def _contract(state, ref, trust):
+        scale = ref.pow(2).mean().sqrt().detach().clamp_min(1e-6)
+        rms = (state - ref).pow(2).mean().clamp_min(1e-12).sqrt()
+        return (rms / scale - max(trust, 0.0)).clamp_min(0.0)
+
+    def step_contract(self, model, hidden, targets, mask=None) -> torch.Tensor | None:
+        from ..models import reference as R
+        from .objectives import self_distillation_per_token
+
+        c = self.sc
+        out = model.reason_hidden(hidden)
+        if not out.step_hiddens:
+            return None
+        prev_h = hidden.detach()
+        prev_ce = None if targets is None else R.cross_entropy(model.logits_from_hidden(hidden, 0), targets,
+                                                               mask).detach()
+        ref = None
+        if c["token_kl_weight"] > _EPS:
+            ref = F.log_softmax(model.logits_from_hidden(out.final_hidden, out.steps_used).detach().float(), -1)
+        total, n = None, 0
+
+        def add(t):
+            nonlocal total, n
+            total, n = (t if total is None else total + t), n + 1
+
+        for i, st in enumerate(out.step_hiddens[:self.sc_steps]):
+            lg = model.logits_from_hidden(st, i + 1)
+            ce = None if targets is None else R.cross_entropy(lg, targets, mask)
+            if c["ce_weight"] > _EPS and ce is not None:
+                add(c["ce_weight"] * ce)
+            if c["monotonic_ce_weight"] > _EPS and ce is not None and prev_ce is not None:
+                add(c["monotonic_ce_weight"] * (ce - (prev_ce + max(c["ce_tolerance"], 0.0))).clamp_min(0.0))
+            if ref is not None:
+                add(c["token_kl_weight"] * self_distillation_per_token(F.log_softmax(lg.float(), -1), ref,
+                                                                        "forward").mean())
+            if c["contractive_weight"] > _EPS:
+                add(c["contractive_weight"] * self._contract(st, prev_h, c["trust_radius"]))
+            prev_h = st.detach()
+            if ce is not None:
+                prev_ce = ce.detach()
+        return None if total is None else total / max(n, 1)
+
     def sigreg(self, h: torch.Tensor) -> torch.Tensor:
         mean = h.mean(dim=(0, 1))
         var = (h - mean).pow(2).mean(dim=(0, 1))
         return (self.min_var - var).clamp_min(0.0).pow(2).mean() + (mean.abs() - self.mean_tol).clamp_min(0.0).pow(2).mean()
 
-    def loss(self, model, hidden: torch.Tensor, tokens: torch.Tensor, step: int) -> torch.Tensor | None:
+    def loss(self, model, hidden: torch.Tensor, tokens: torch.Tensor, step: int, targets=None,
+             mask=None) -> torch.Tensor | None:
         js = self._scale(step, self.jepa_every, self.jepa_start)
         ss = self._scale(step, self.sg_every, self.sg_start) if self.sg_enabled else None
         ns = self._scale(step, self.nl_every, self.nl_start) if self.nl_enabled else None
@@ -217,6 +276,11 @@ class LatentReasoningTraining:
             term = self.next_latent(model, hidden, target, tokens)
             if term is not None:
                 total, n = ns * term, 1
+        sc = self._scale(step, self.sc_every, self.sc_start) if self.sc_enabled else None
+        if sc is not None:
+            term = self.step_contract(model, hidden, targets, mask)
+            if term is not None:
+                total, n = (sc * term if total is None else total + sc * term), n + 1
         if es is not None:
             term = self.energy_model(model, hidden, target)
             if term is not None:

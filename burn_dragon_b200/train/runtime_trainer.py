@@ -87,7 +87,7 @@ class RuntimeTrainer:
             # the training-side latent-reasoning terms read the final hidden states
             h = self.model.forward_hidden(tokens, event_mask=event_mask)
             loss = R.cross_entropy(self.model.logits_from_hidden(h), targets, mask)
-            aux = lrt.loss(self.model, h, tokens, self.step_idx)
+            aux = lrt.loss(self.model, h, tokens, self.step_idx, targets=targets, mask=mask)
             if aux is not None:
                 loss = loss + aux
         else:

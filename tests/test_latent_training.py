@@ -130,3 +130,37 @@ def test_energy_model_term_and_run(tmp_path, monkeypatch, capsys):
           "--set", "training.latent_reasoning={enabled=true, energy_model={enabled=true}}", "--run-name", "em"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res["final_loss"] is not None
+
+
+def test_step_contract_term_and_run(tmp_path, monkeypatch, capsys):
+    from burn_dragon_b200.models import reference as R
+    from burn_dragon_b200.models.dragon_runtime import DragonRuntime
+
+    mc = _mc()
+    mc.latent_reasoning.enabled = True
+    mc.latent_reasoning.max_steps = 2
+    m = DragonRuntime(mc, seed=4)
+    with torch.no_grad():  # a non-zero refiner, so steps move
+        m.refiner_out.weight.normal_(0, 0.1)
+    tok = torch.randint(0, 16, (2, 5))
+    y = torch.randint(0, 16, (2, 5))
+    h = m.forward_hidden(tok)
+    lr = LatentReasoningTraining({"sigreg": {"enabled": False}, "jepa_future_offsets": [],
+                                  "step_contract": {"enabled": True, "ce_weight": 0.5, "trust_radius": 0.0}}, mc)
+    got = lr.step_contract(m, h, y)
+    out = m.reason_hidden(h)
+    prev_h, prev_ce, terms = h.detach(), R.cross_entropy(m.logits_from_hidden(h, 0), y).detach(), []
+    for i, st in enumerate(out.step_hiddens):
+        ce = R.cross_entropy(m.logits_from_hidden(st, i + 1), y)
+        terms += [0.5 * ce, (ce - prev_ce).clamp_min(0),
+                  0.05 * (st - prev_h).pow(2).mean().sqrt() / prev_h.pow(2).mean().sqrt()]
+        prev_h, prev_ce = st.detach(), ce.detach()
+    torch.testing.assert_close(got, sum(terms) / len(terms))
+    from burn_dragon_b200.cli.train import main
+
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", CFG, "--set", "training.max_iters=2",
+          "--set", "training.latent_reasoning={enabled=true, step_contract={enabled=true, token_kl_weight=0.1}}",
+          "--run-name", "sc"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None
