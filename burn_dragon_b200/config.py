@@ -845,6 +845,8 @@ class TrainingSection:
     predictive_coding: dict[str, Any] = field(default_factory=dict)
     # training-side latent reasoning (train.latent_reasoning.LatentReasoningTraining keys)
     latent_reasoning: dict[str, Any] = field(default_factory=dict)
+    # legacy: enabling it is rejected in favour of training.objective (validate.rs:2854-2860)
+    gdpo: dict[str, Any] | None = None
     # a [model.sequence_kernel] table that replaces the model's for training (applied by
     # the loader; burn_dragon_language/src/train/backend.rs:755-770)
     sequence_kernel_override: dict[str, Any] | None = None
@@ -936,6 +938,9 @@ class TrainingConfig:
         self.model.validate()
         self.training.validation.validate()
         t = self.training
+        if t.gdpo and t.gdpo.get("enabled"):
+            raise ValueError("training.gdpo.enabled is a legacy objective flag; use training.objective.type = "
+                             "\"sdpo\" for self-distilled policy optimization")
         if t.launch_mode not in (None, "fresh", "resume_exact_run", "resume_latest_checkpoint_if_present",
                                  "init_from_checkpoint"):
             raise ValueError(f"training.launch_mode {t.launch_mode!r}")

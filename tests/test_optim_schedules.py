@@ -40,3 +40,9 @@ def test_predictive_coding_optimizer_name_is_retired():
         training_config_from_dict({"optimizer": {"name": "predictive_coding"}})
     with pytest.raises(ValueError):
         training_config_from_dict({"optimizer": {"name": "lion"}})
+
+
+def test_legacy_gdpo_flag_is_rejected():
+    with pytest.raises(ValueError, match="training.gdpo.enabled"):
+        training_config_from_dict({"training": {"gdpo": {"enabled": True}}})
+    assert not training_config_from_dict({"training": {"gdpo": {"enabled": False}}}).extras
