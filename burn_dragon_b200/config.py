@@ -884,6 +884,10 @@ class DatasetConfig:
     path: str | None = None
     text_field: str = "text"
     tokenizer: str | None = None  # a tokenizer.json (BPE) for jsonl / parquet / text corpora
+    # a separate held-out source: {type = file | jsonl | parquet | text, path, text_field,
+    # cache_dir, train_split_ratio (default 0: the whole source is validation data)}
+    # (schema.rs:13-35, ValidationDatasetConfig)
+    validation: dict[str, Any] | None = None
 
 
 @dataclass

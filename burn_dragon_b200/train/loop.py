@@ -121,6 +121,22 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
         prepared = prepare_corpus(cfg.dataset.path, cfg.dataset.cache_dir, cfg.dataset.text_field,
                                   tokenizer=cfg.dataset.tokenizer)
         cfg.dataset.type, cfg.dataset.path = "file", prepared
+    vsrc = None
+    if cfg.dataset.validation:
+        vd = dict(cfg.dataset.validation)
+        vtype, vpath = vd.get("type", "file"), vd.get("path")
+        if vtype not in ("file", "jsonl", "parquet", "text") or not vpath:
+            raise ValueError("dataset.validation needs type = file | jsonl | parquet | text and a path")
+        if vtype != "file":
+            from .datasets import prepare_corpus
+
+            args = (vpath, vd.get("cache_dir", cfg.dataset.cache_dir), vd.get("text_field", cfg.dataset.text_field))
+            if rank == 0:
+                prepare_corpus(*args, tokenizer=cfg.dataset.tokenizer)
+            if world > 1 and dist.is_initialized():
+                dist.barrier()
+            vpath = prepare_corpus(*args, tokenizer=cfg.dataset.tokenizer)
+        vsrc = (vpath, float(vd.get("train_split_ratio", 0.0)))
     if t.auto_batch_size.enabled:
         from .autotune import choose_batch_size
 
@@ -301,7 +317,10 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     # validation windows: drawn with their own seed (identical across training seeds); a
     # fixed holdout rewinds to the same windows at every validation
     vseed = t.validation.seed % (2**31)
-    if cfg.dataset.type == "file":
+    if vsrc is not None:
+        valid = FileBytes(vsrc[0], t.batch_size, t.block_size, "valid", vsrc[1], seed=vseed, rank=data_rank,
+                          world=data_world)
+    elif cfg.dataset.type == "file":
         valid = FileBytes(cfg.dataset.path, t.batch_size, t.block_size, "valid", cfg.dataset.train_split_ratio,
                           seed=vseed, rank=data_rank, world=data_world)
     else:
