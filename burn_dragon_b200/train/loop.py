@@ -180,8 +180,7 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     if mode == "pipeline":
         from ..parallel.pipeline import PipelineRunner, plan
 
-        pp = cfg.parallel.pipeline
-        pl = plan(cfg.model.n_layer, world, int(pp.get("micro_batches", 4)), pp.get("schedule", "1f1b"))
+        pl = plan(cfg.model.n_layer, world, *_pipeline_settings(cfg.parallel.pipeline, world))
         runner = PipelineRunner(trainer.model, pl, rank, t.batch_size // pl.micro, t.block_size)
 
     pc = t.algorithm == "predictive_coding"
@@ -571,3 +570,20 @@ def _steps_per_epoch(cfg: TrainingConfig, data_world: int) -> int:
         train = int(n * cfg.dataset.train_split_ratio)
         return max(1, train // (t.batch_size * t.block_size * max(data_world, 1)))
     return max(1, min(t.checkpoint_interval_iters or t.max_iters, t.max_iters))
+
+
+def _pipeline_settings(pp: dict, world: int) -> tuple[int, str, int]:
+    """(micro-batches, schedule, virtual stages per rank) from ``[parallel.pipeline]``:
+    the reference's keys ``microbatches``, ``schedule`` (``gpipe`` | ``interleaved_1f1b``;
+    ``1f1b`` also accepted), ``virtual_stages_per_rank`` and ``stage_count``, which must be
+    the world size (burn_dragon_train/src/config/core.rs:95-282); ``micro_batches`` is an
+    alias of ``microbatches``."""
+    micro = int(pp.get("microbatches", pp.get("micro_batches", 4)))
+    kind = {"interleaved_1f1b": "interleaved"}.get(pp.get("schedule", "1f1b"), pp.get("schedule", "1f1b"))
+    virtual = int(pp.get("virtual_stages_per_rank", 1))
+    if "stage_count" in pp and int(pp["stage_count"]) != world:
+        raise ValueError(f"parallel.pipeline.stage_count = {pp['stage_count']} but the job has {world} ranks "
+                         "(one stage per rank)")
+    if micro <= 0 or virtual <= 0:
+        raise ValueError("parallel.pipeline.microbatches and virtual_stages_per_rank must be > 0")
+    return micro, kind, virtual

@@ -91,3 +91,13 @@ def test_two_stage_pipeline_matches_full_model(kind):
     assert torch.allclose(out[0][0], out[1][0])
     assert torch.allclose(out[0][0], flat, atol=1e-6, rtol=1e-4)
     assert abs(out[1][1] - float(loss)) < 1e-5
+
+
+def test_pipeline_settings_take_the_reference_keys():
+    from burn_dragon_b200.train.loop import _pipeline_settings
+
+    assert _pipeline_settings({"microbatches": 8, "schedule": "interleaved_1f1b", "virtual_stages_per_rank": 2,
+                               "stage_count": 4}, 4) == (8, "interleaved", 2)
+    assert _pipeline_settings({"micro_batches": 6, "schedule": "gpipe"}, 2) == (6, "gpipe", 1)
+    with pytest.raises(ValueError, match="stage_count"):
+        _pipeline_settings({"stage_count": 2}, 4)
