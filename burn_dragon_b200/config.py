@@ -979,6 +979,25 @@ class TrainingConfig:
         p = self.parallel.mode
         if p not in ("single", "ddp", "fsdp", "tensor_parallel_neuron", "hybrid_2d", "pipeline"):
             raise ValueError(f"unknown parallel.mode {p!r}")
+        if p in ("tensor_parallel_neuron", "hybrid_2d"):
+            tpc = self.parallel.tensor
+            if tpc.get("axis", "neuron") != "neuron":
+                raise ValueError("parallel.tensor.axis: only the neuron axis exists")
+            part = tpc.get("partition", "contiguous")
+            if part not in ("contiguous", "head_aligned"):
+                raise ValueError(f"parallel.tensor.partition {part!r}")
+            size = tpc.get("size")
+            if size is not None:
+                size = int(size)
+                if part == "head_aligned" and size > self.model.n_head:
+                    raise ValueError(f"parallel.tensor.partition=head_aligned requires parallel.tensor.size <= "
+                                     f"model.n_head (got tensor_size={size} n_head={self.model.n_head})")
+                # the decoder rows are head-major, so contiguous neuron ranges are whole heads
+                # exactly when the size divides the head count; a split inside a head would
+                # cut a head's attention across ranks, which this implementation keeps local
+                if self.model.n_head % size:
+                    raise ValueError(f"parallel.tensor.size {size} must divide model.n_head {self.model.n_head} "
+                                     "(shards are whole heads)")
         if p == "pipeline" and self.training.tbptt_chunk_size:
             raise ValueError("pipeline parallelism does not support TBPTT chunking")
         if self.training.sequence_batching not in ("auto", "random", "streaming"):

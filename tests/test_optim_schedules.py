@@ -46,3 +46,19 @@ def test_legacy_gdpo_flag_is_rejected():
     with pytest.raises(ValueError, match="training.gdpo.enabled"):
         training_config_from_dict({"training": {"gdpo": {"enabled": True}}})
     assert not training_config_from_dict({"training": {"gdpo": {"enabled": False}}}).extras
+
+
+def test_tensor_parallel_partition_rules():
+    base = {"model": {"n_head": 4, "n_embd": 32}, "parallel": {"mode": "tensor_parallel_neuron"}}
+
+    def cfg(tensor):
+        return training_config_from_dict({**base, "parallel": {**base["parallel"], "tensor": tensor}})
+
+    cfg({"size": 2, "partition": "contiguous"})
+    cfg({"size": 4, "partition": "head_aligned"})
+    with pytest.raises(ValueError, match="head_aligned requires"):
+        cfg({"size": 8, "partition": "head_aligned"})
+    with pytest.raises(ValueError, match="must divide"):
+        cfg({"size": 3})
+    with pytest.raises(ValueError):
+        cfg({"axis": "embedding"})
