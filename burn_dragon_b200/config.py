@@ -522,6 +522,50 @@ class OptimizerConfig:
     # x 2), population_chunk_size (pairs per batched forward), rank}}
     # (burn_dragon_train/src/config/optimizer.rs:239-310)
     eggroll: dict[str, Any] = field(default_factory=dict)
+    # {enabled, min_population_size 8, max_population_size 4096, population_per_batch 128,
+    # population_chunk_size, prefer_power_of_two true}: population size from the batch size
+    # (burn_dragon_train/src/config/optimizer.rs:108-135, 276-310, 382-406)
+    eggroll_auto_population: dict[str, Any] = field(default_factory=dict)
+    # {backend = auto | reference | cuda | factorized, perturbation_scope =
+    # dragon_core_projection}: the population always runs as one batched (vmapped) forward
+    # over the shared projections here, so every backend value takes that path
+    eggroll_population_execution: dict[str, Any] = field(default_factory=dict)
+    # the retired predictive-coding update transforms (only meaningful with the retired
+    # optimizer.name = "predictive_coding", which is rejected)
+    predictive_coding: dict[str, Any] = field(default_factory=dict)
+    # the reference's only schedule mode
+    schedule_mode: str = "dragon_reference"
+
+    def apply_auto_eggroll_population(self, batch_size: int) -> dict | None:
+        a = dict(self.eggroll_auto_population)
+        if self.name != "eggroll" or not a.get("enabled"):
+            return None
+
+        def even(v):
+            return max(v - v % 2, 2)
+
+        pop = dict(dict(self.eggroll).get("population", {}))
+        conf_size = int(pop.get("population_size", 16))
+        conf_chunk = pop.get("population_chunk_size")
+        lo = even(int(a.get("min_population_size", 8)))
+        hi = even(max(int(a.get("max_population_size", 4096)), lo))
+        req = max(conf_size, int(a.get("min_population_size", 8)),
+                  max(batch_size, 1) * int(a.get("population_per_batch", 128)))
+        req = min(max(even(req), lo), hi)
+        size = req
+        if a.get("prefer_power_of_two", True):
+            nxt = 1 << (req - 1).bit_length()
+            if lo <= nxt <= hi:
+                size = nxt
+            elif (1 << (req.bit_length() - 1)) >= lo:
+                size = 1 << (req.bit_length() - 1)
+        chunk = a.get("population_chunk_size", conf_chunk)
+        chunk = size if chunk is None else int(chunk)
+        chunk = min(even(max(min(chunk, size), 2)), size)
+        pop.update(population_size=size, population_chunk_size=chunk)
+        self.eggroll = {**dict(self.eggroll), "population": pop}
+        return {"configured_population_size": conf_size, "resolved_population_size": size,
+                "resolved_population_chunk_size": chunk, "batch_size": batch_size}
 
     def eggroll_settings(self) -> dict:
         e = dict(self.eggroll)
@@ -965,6 +1009,12 @@ class TrainingConfig:
             # burn_dragon_train/src/train/pipeline/optimizer.rs:250-256
             raise ValueError("optimizer.name=predictive_coding is retired; predictive coding is a training "
                              "algorithm: use training.algorithm=predictive_coding with an ordinary update")
+        ex = dict(o.eggroll_population_execution)
+        if ex.get("backend", "auto") not in ("auto", "reference", "cuda", "factorized") or \
+                ex.get("perturbation_scope", "dragon_core_projection") != "dragon_core_projection":
+            raise ValueError(f"optimizer.eggroll_population_execution {ex}")
+        if o.schedule_mode != "dragon_reference":
+            raise ValueError(f"optimizer.schedule_mode {o.schedule_mode!r}")
         if o.name not in ("adamw", "eggroll"):
             raise ValueError(f"optimizer.name {o.name!r} (adamw | eggroll)")
         if o.weight_decay_final is not None and o.weight_decay_final < 0:

@@ -188,6 +188,7 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     if o.name == "eggroll" or t.algorithm == "eggroll":
         if extended or pc or mode not in ("single", "ddp", "fsdp") or getattr(trainer, "comm", None) is not None:
             raise ValueError("EGGROLL training needs the plain BDH model in single / ddp mode (NCCL path)")
+        o.apply_auto_eggroll_population(t.batch_size)
         egg = o.eggroll_settings()
     if pc and (extended or mode not in ("single", "ddp", "fsdp")):
         raise ValueError("predictive_coding training needs the plain BDH model in single / ddp mode")

@@ -62,3 +62,20 @@ def test_tensor_parallel_partition_rules():
         cfg({"size": 3})
     with pytest.raises(ValueError):
         cfg({"axis": "embedding"})
+
+
+def test_eggroll_auto_population():
+    from burn_dragon_b200.config import OptimizerConfig
+
+    o = OptimizerConfig(name="eggroll", eggroll={"population": {"population_size": 64, "population_chunk_size": 16,
+                                                                 "rank": 2}},
+                        eggroll_auto_population={"enabled": True, "population_per_batch": 96})
+    r = o.apply_auto_eggroll_population(6)  # 6 x 96 = 576 -> the next power of two, 1024
+    assert r["resolved_population_size"] == 1024 and r["resolved_population_chunk_size"] == 16
+    assert o.eggroll["population"]["population_size"] == 1024 and o.eggroll["population"]["rank"] == 2
+    o = OptimizerConfig(name="eggroll", eggroll_auto_population={
+        "enabled": True, "min_population_size": 8, "max_population_size": 256, "population_per_batch": 1024,
+        "population_chunk_size": 32, "prefer_power_of_two": False})
+    r = o.apply_auto_eggroll_population(8)
+    assert (r["resolved_population_size"], r["resolved_population_chunk_size"]) == (256, 32)
+    assert OptimizerConfig(eggroll_auto_population={"enabled": True}).apply_auto_eggroll_population(4) is None
