@@ -1,6 +1,7 @@
 """Generation CLI: load a run's newest checkpoint and continue prompts, encoded and
 decoded with the run's ``tokenizer.json`` (bytes or BPE). Flags left unset take the
 run's ``[generation]`` values (prompt, max_tokens, max_chars, temperature, top_k,
+prompt_tokenizer / decode_tokenizer (the run's tokenizer, or one named in the config),
 context_strategy, output_format: ``decoded_text`` prints text, ``token_ids`` prints the ids as JSON, ``auto``
 is decoded text); burn_dragon_language/src/config/core.rs:18-60.
 
@@ -50,7 +51,16 @@ def main(argv=None) -> None:
     if run.latest() is not None:
         run.load(None, model)
     tp = os.path.join(a.run, "tokenizer.json")
-    tok = load_tokenizer(tp) if os.path.exists(tp) else load_tokenizer({"type": "byte"})
+    run_tok = load_tokenizer(tp) if os.path.exists(tp) else load_tokenizer({"type": "byte"})
+
+    def pick_tok(src: dict):
+        if src.get("source", "dataset") == "dataset":
+            return run_tok
+        if src.get("path"):
+            return load_tokenizer(src["path"])
+        return load_tokenizer({k: v for k, v in src.items() if k not in ("source", "cache_dir")})
+
+    tok, out_tok = pick_tok(g.prompt_tokenizer), pick_tok(g.decode_tokenizer)
     prompt = tok.encode(prompt_text) or [0]
     window = g.sliding_window(cfg.training.block_size)
     if window is not None and len(prompt) > window:
@@ -61,7 +71,7 @@ def main(argv=None) -> None:
         if fmt == "token_ids":
             print(json.dumps(row))
         else:
-            text = tok.decode(prompt + row)
+            text = out_tok.decode(prompt + row)
             print(text[:len(prompt_text) + max_chars] if max_chars is not None else text)
 
 if __name__ == "__main__":

@@ -946,6 +946,10 @@ class GenerationConfig:
     # {type = "infinite"} or {type = "sliding", window = W}; window 0 means block_size
     # (core.rs:60-68, generation.rs:1317-1332)
     context_strategy: dict[str, Any] = field(default_factory=lambda: {"type": "infinite"})
+    # {source = "dataset"} (the run's tokenizer.json) or {source = "config", path = a
+    # tokenizer.json | type = "byte"} (core.rs:40-52)
+    prompt_tokenizer: dict[str, Any] = field(default_factory=lambda: {"source": "dataset"})
+    decode_tokenizer: dict[str, Any] = field(default_factory=lambda: {"source": "dataset"})
 
     def sliding_window(self, block_size: int) -> int | None:
         kind = self.context_strategy.get("type", "infinite")

@@ -104,3 +104,16 @@ def test_training_sequence_kernel_override_and_context_strategy():
     assert cfg.model.sequence_memory_system == "gated_deltanet2" and not cfg.extras
     with pytest.raises(ValueError):
         training_config_from_dict({"training": {"context_strategy": {"type": "ring"}}})
+
+
+def test_generation_tokenizer_sources(tmp_path, monkeypatch, capsys):
+    from burn_dragon_b200.cli.generate import main as gen
+    from burn_dragon_b200.cli.train import main
+
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    main(["--config", CFG, "--set", "training.max_iters=1", "--set", "generation.max_tokens=3",
+          "--set", 'generation.decode_tokenizer={source="config", type="byte"}', "--run-name", "tk"])
+    run_dir = json.loads(capsys.readouterr().out.strip().splitlines()[-1])["run_dir"]
+    gen(["--run", run_dir, "--prompt", "ab", "--temperature", "0"])
+    text = capsys.readouterr().out.strip().splitlines()[-1]
+    assert text.startswith("ab")
