@@ -17,6 +17,7 @@ Two execution paths share these parameters:
 
 from __future__ import annotations
 
+import copy
 import math
 
 import torch
@@ -204,6 +205,21 @@ class BDH(nn.Module):
         g = getattr(self, f"{name}_gain") if self.cfg.random_scaffold.trainable_gain else \
             torch.ones(1, device=a.device, dtype=a.dtype)
         return a, b, g
+
+    def __deepcopy__(self, memo):
+        """A copy whose parameters are views of its own copied flat store (a plain deep
+        copy would give them separate storage, and an optimizer stepping the copy's store
+        would then miss them)."""
+        new = self.__class__.__new__(self.__class__)
+        memo[id(self)] = new
+        for k, v in self.__dict__.items():
+            new.__dict__[k] = copy.deepcopy(v, memo)
+        st = new.store
+        with torch.no_grad():
+            for name in st.shapes:  # the copied parameters hold the current values
+                st.view(st.data, name).copy_(getattr(self, name).detach())
+        new.attach_buffers(st.data, st.grad, st.shadow)
+        return new
 
     def attach_buffers(self, data: torch.Tensor, grad: torch.Tensor, shadow: torch.Tensor | None) -> None:
         """Re-home parameters, grads and the bf16 shadow (see ``ParamStore.rebind``)."""

@@ -53,14 +53,37 @@ def population_losses(model, tokens, targets, noises: dict, sigma: float) -> tor
 
 
 @torch.no_grad()
+def normalize_fitness(f: torch.Tensor, kind: str) -> torch.Tensor:
+    """``none``; ``center`` (minus the population mean); ``rank``: centred ranks in
+    [-0.5, 0.5] (the usual ES rank transform; ties broken by order). The reference names
+    these modes (burn_dragon_eggroll/src/lib.rs:139-175) but defines them in the
+    ``burn_eggroll`` crate, which is not in its repository, so these are the standard forms."""
+    if kind == "none":
+        return f
+    if kind == "center":
+        return f - f.mean()
+    if kind == "rank":
+        n = f.numel()
+        r = torch.empty_like(f)
+        r[torch.argsort(f)] = torch.arange(n, dtype=f.dtype, device=f.device)
+        return r / max(n - 1, 1) - 0.5
+    raise ValueError(f"unknown fitness normalization {kind!r}")
+
+
+@torch.no_grad()
 def es_step(model, tokens, targets, population: int = 8, sigma: float = 0.01, lr: float = 0.01, rank: int = 4,
-            seed: int = 0, chunk: int | None = None, weight_decay: float = 0.0, reduce=None) -> dict:
+            seed: int = 0, chunk: int | None = None, weight_decay: float = 0.0, reduce=None,
+            fitness_normalization: str = "none", coefficient_clip: float | None = None,
+            max_delta_rms: float | None = None) -> dict:
     """One antithetic ES update of the three shared projections; returns diagnostics.
 
     ``population`` antithetic pairs (2 x population members), evaluated ``chunk`` pairs
     per batched forward; ``weight_decay`` is decoupled (W *= 1 - lr * wd before the ES
     step); ``reduce`` maps this rank's member losses to the data-parallel mean, so every
-    rank (same ``seed``, hence the same perturbations) applies the same update."""
+    rank (same ``seed``, hence the same perturbations) applies the same update.
+    ``fitness_normalization`` transforms the 2P fitnesses before the pair coefficients,
+    ``coefficient_clip`` clamps each pair's coefficient and ``max_delta_rms`` rescales a
+    matrix's update so its RMS stays under that bound."""
     gen = torch.Generator().manual_seed(seed)
     params = model.param_dict()
     noises = {n: torch.stack([_noise(params[n].shape, rank, gen, tokens.device) for _ in range(population)])
@@ -75,13 +98,21 @@ def es_step(model, tokens, targets, population: int = 8, sigma: float = 0.01, lr
     losses = torch.cat(plus + minus)
     if reduce is not None:
         losses = reduce(losses)
-    fp, fm = -losses[:population], -losses[population:]
+    fit = normalize_fitness(-losses, fitness_normalization)
+    fp, fm = fit[:population], fit[population:]
     coef = (fp - fm) / (2 * population * sigma)
+    if coefficient_clip is not None:
+        coef = coef.clamp(-coefficient_clip, coefficient_clip)
     for n in MATRIX:
         w = getattr(model, n)
         if weight_decay:
             w.mul_(1.0 - lr * weight_decay)
-        w.add_(lr * torch.tensordot(coef, noises[n], dims=1))
+        upd = lr * torch.tensordot(coef, noises[n], dims=1)
+        if max_delta_rms is not None:
+            rms = float(upd.pow(2).mean().sqrt())
+            if rms > max_delta_rms:
+                upd = upd * (max_delta_rms / rms)
+        w.add_(upd)
     model.store.refresh_shadow()
     return {"mean_loss": float(losses.mean()), "best_loss": float(losses.min())}
 
