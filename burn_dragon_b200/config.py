@@ -570,8 +570,14 @@ class OptimizerConfig:
     def eggroll_settings(self) -> dict:
         e = dict(self.eggroll)
         pop = dict(e.get("population", {}))
+        upd = dict(e.get("update", {}))
         out = {"sigma": float(e.get("sigma", 0.01)), "members": int(pop.get("population_size", 16)),
-               "chunk": pop.get("population_chunk_size"), "rank": int(pop.get("rank", 4))}
+               "chunk": pop.get("population_chunk_size"), "rank": int(pop.get("rank", 4)),
+               "fitness_normalization": str(e.get("fitness_normalization", "none")),
+               "coefficient_clip": e.get("coefficient_clip"),
+               "max_delta_rms": upd.get("max_delta_rms", e.get("max_delta_rms"))}
+        if out["fitness_normalization"] not in ("none", "center", "rank"):
+            raise ValueError(f"optimizer.eggroll.fitness_normalization {out['fitness_normalization']!r}")
         if not out["sigma"] > 0:
             raise ValueError("optimizer.eggroll.sigma must be > 0")
         if out["members"] < 2 or out["members"] % 2:

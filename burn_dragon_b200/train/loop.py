@@ -447,7 +447,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                 rep = es_step(trainer.model, x.to(dev), y.to(dev), population=egg["members"] // 2,
                               sigma=egg["sigma"], lr=lr_now, rank=egg["rank"], seed=t.seed * 1_000_003 + step,
                               chunk=None if egg["chunk"] is None else int(egg["chunk"]),
-                              weight_decay=o.weight_decay, reduce=red)
+                              weight_decay=o.weight_decay, reduce=red,
+                              fitness_normalization=egg["fitness_normalization"],
+                              coefficient_clip=egg["coefficient_clip"], max_delta_rms=egg["max_delta_rms"])
                 trainer.step_idx += 1
                 loss = torch.tensor(rep["mean_loss"])
                 prof.stop("forward_backward")

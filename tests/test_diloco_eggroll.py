@@ -106,7 +106,8 @@ def test_training_loop_with_the_eggroll_optimizer(tmp_path, monkeypatch, capsys)
     cfg = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu.toml")
     monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
     main(["--config", cfg, "--set", "training.max_iters=2", "--set", 'optimizer.name="eggroll"',
-          "--set", "optimizer.eggroll={sigma=0.02, population={population_size=4, population_chunk_size=1, rank=2}}",
+          "--set", "optimizer.eggroll={sigma=0.02, fitness_normalization=\"rank\", coefficient_clip=10.0, "
+                   "update={max_delta_rms=0.1}, population={population_size=4, population_chunk_size=1, rank=2}}",
           "--run-name", "egg"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res["final_loss"] is not None
