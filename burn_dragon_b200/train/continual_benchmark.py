@@ -172,3 +172,33 @@ def run_sequential(trainer, spec: ContextRecurrenceSpec, tasks=("a", "b", "c", "
         matrix.append({t: evaluate(trainer.model, t, spec, holdout_seed) for t in tasks})
     forgetting = {t: matrix[-1][t]["accuracy"] - max(row[t]["accuracy"] for row in matrix) for t in tasks}
     return {"after_phase": matrix, "forgetting": forgetting}
+
+
+def acquisition(before: dict, after: dict) -> dict:
+    """A task's acquisition over a phase: loss reduction and accuracy gain."""
+    return {"loss_reduction": before["loss"] - after["loss"], "accuracy_gain": after["accuracy"] - before["accuracy"]}
+
+
+def acquisition_gate(baseline: list[dict], candidate: list[dict], loss_floor_ratio: float = 0.9,
+                     accuracy_tolerance: float = 0.0, minimum_baseline_loss_reduction: float = 0.0,
+                     minimum_baseline_accuracy_gain: float = 0.0) -> dict:
+    """Does a candidate method acquire every task as well as the baseline did
+    (continual_benchmark.rs:439-520)? A task counts only if the baseline acquired it
+    (loss reduction and accuracy gain at least the minimums); the candidate must keep at
+    least ``loss_floor_ratio`` of the baseline's loss reduction and its accuracy gain
+    within ``accuracy_tolerance``."""
+    if not baseline or len(baseline) != len(candidate):
+        raise ValueError("continual acquisition vectors must be non-empty and equally sized")
+    if not 0.0 <= loss_floor_ratio <= 1.0 or min(accuracy_tolerance, minimum_baseline_loss_reduction,
+                                                  minimum_baseline_accuracy_gain) < 0:
+        raise ValueError("continual acquisition thresholds must be non-negative, loss_floor_ratio in [0, 1]")
+    matched, acquired, ratios, deltas = True, [], [], []
+    for b, c in zip(baseline, candidate):
+        ok = b["loss_reduction"] >= minimum_baseline_loss_reduction and \
+            b["accuracy_gain"] >= minimum_baseline_accuracy_gain
+        ratios.append(c["loss_reduction"] / b["loss_reduction"] if abs(b["loss_reduction"]) > 1e-12 else 0.0)
+        deltas.append(c["accuracy_gain"] - b["accuracy_gain"])
+        matched &= ok and c["loss_reduction"] >= b["loss_reduction"] * loss_floor_ratio \
+            and c["accuracy_gain"] + accuracy_tolerance >= b["accuracy_gain"]
+        acquired.append(ok)
+    return {"matched": matched, "baseline_acquired": acquired, "loss_ratios": ratios, "accuracy_deltas": deltas}

@@ -47,3 +47,16 @@ def test_sequential_run_reports_a_forgetting_matrix():
     rep = run_sequential(Trainer(cfg, "cpu", lr=1e-2, seed=0), spec, tasks=("a", "b"), steps_per_task=3)
     assert len(rep["after_phase"]) == 2 and set(rep["forgetting"]) == {"a", "b"}
     assert all(v <= 0 for v in rep["forgetting"].values())
+
+
+def test_acquisition_gate():
+    from burn_dragon_b200.train.continual_benchmark import acquisition, acquisition_gate
+
+    base = [acquisition({"loss": 2.0, "accuracy": 0.1}, {"loss": 1.0, "accuracy": 0.6}),
+            {"loss_reduction": 0.5, "accuracy_gain": 0.2}]
+    good = [{"loss_reduction": 0.95, "accuracy_gain": 0.5}, {"loss_reduction": 0.5, "accuracy_gain": 0.2}]
+    bad = [{"loss_reduction": 0.5, "accuracy_gain": 0.5}, {"loss_reduction": 0.5, "accuracy_gain": 0.2}]
+    g = acquisition_gate(base, good, loss_floor_ratio=0.9)
+    assert g["matched"] and abs(g["loss_ratios"][0] - 0.95) < 1e-12
+    assert not acquisition_gate(base, bad, loss_floor_ratio=0.9)["matched"]
+    assert not acquisition_gate(base, good, minimum_baseline_accuracy_gain=0.3)["matched"]
