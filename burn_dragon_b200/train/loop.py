@@ -272,6 +272,11 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
             from .init_transfer import InitTransferConfig, apply_init_transfer
 
             apply_init_transfer(target, fresh, _fill(InitTransferConfig, dict(t.init_transfer), {}, ""), device=dev)
+    if rank == 0:
+        from .manifest import write_experiment_manifest
+
+        write_experiment_manifest(cfg, run.path, os.path.basename(os.path.abspath(run.path)), dev.type,
+                                  start if start > 0 else None)
     streaming = t.sequence_batching == "streaming" or t.tbptt_persist_across_steps
     data_rank = 0 if mode in ("tensor_parallel_neuron", "pipeline") else rank
     data_world = 1 if mode in ("tensor_parallel_neuron", "pipeline") else world

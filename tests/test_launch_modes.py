@@ -95,3 +95,17 @@ def test_sequence_state_probe_reports_warm_and_cold(tmp_path, monkeypatch, capsy
     assert len(rep["state"]) == 1 and rep["state"][0]["present"]
     ev = [json.loads(x) for x in open(os.path.join(res["run_dir"], "events", "metrics.jsonl"))]
     assert any("stream_carry_nll_gain" in e for e in ev)
+
+
+def test_experiment_manifest_records_each_launch(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    a = _run(capsys, "--set", "training.max_iters=2", "--set", "training.checkpoint_interval_iters=1",
+             "--run-name", "man")
+    _run(capsys, "--set", "training.max_iters=3", "--set", "training.checkpoint_interval_iters=1", "--run-name", "man")
+    man = json.load(open(os.path.join(a["run_dir"], "experiment_manifest.json")))
+    assert man["schema_version"] == 2 and man["run_name"] == "man" and man["backend"] == "cpu"
+    first, second = man["launches"]
+    assert first["resume_checkpoint_epoch"] is None and second["resume_checkpoint_epoch"] == 2
+    assert any(x["file_name"] == "model-2.bin" and x["bytes"] > 0 for x in second["checkpoint_artifacts"])
+    assert second["contract_changed"]  # max_iters grew from 2 to 3
+    assert len(first["effective_config_sha256"]) == 64
