@@ -279,7 +279,7 @@ class RunDir:
         return os.path.join(self.ckpt, f"{kind}-{step}.bin")
 
     def save(self, step: int, model, optimizer=None, scheduler: dict | None = None, runtime: dict | None = None,
-             keep_last: int = 2, best_step: int | None = None, extra: dict | None = None) -> None:
+             keep_last: int = 2, best_step: int | None = None, extra: dict | None = None, teacher=None) -> None:
         """``extra``: further named tensors (the optional modules of ``DragonRuntime`` and
         their optimizer moments), stored as ``extra-<step>.bin``."""
         from ..models.bdh import record_name
@@ -295,6 +295,10 @@ class RunDir:
             meta = {k: v for k, v in runtime.items() if k != "rhos"}
             rt = {f"rho.{i}": snap(r) for i, r in enumerate(runtime.get("rhos") or [])}
         extra = {k: snap(v) for k, v in extra.items()} if extra else None
+        # an EMA teacher (self-distillation, dynamics anchor, latent targets) is part of the
+        # run's state: ``teacher-model-<step>.bin`` (burn_dragon_language/src/train/
+        # runtime_checkpoint.rs:13-14)
+        teach = {k: snap(v) for k, v in teacher.state_dict().items()} if teacher is not None else None
         scheduler = dict(scheduler or {})
 
         def write():
@@ -307,6 +311,8 @@ class RunDir:
                 save_tensors(self._p("runtime-state", step), rt, meta)
             if extra:
                 save_tensors(self._p("extra", step), extra, {"schema_version": SCHEMA_VERSION})
+            if teach:
+                save_tensors(self._p("teacher-model", step), teach, {"schema_version": SCHEMA_VERSION})
             with open(os.path.join(self.path, "latest"), "w") as f:
                 f.write(str(step))
             self._retain(keep_last, best_step)
@@ -345,10 +351,21 @@ class RunDir:
         for s in steps:
             if s in keep:
                 continue
-            for kind in ("model", "optim", "scheduler", "runtime-state", "extra"):
+            for kind in ("model", "optim", "scheduler", "runtime-state", "extra", "teacher-model"):
                 p = self._p(kind, s)
                 if os.path.exists(p):
                     os.remove(p)
+
+    def load_teacher(self, step: int, teacher) -> bool:
+        """Restore an EMA teacher saved with ``save(..., teacher=)``; False if absent."""
+        self.wait()
+        p = self._p("teacher-model", step)
+        if not os.path.exists(p):
+            return False
+        sd, _ = load_tensors(p)
+        teacher.load_state_dict({k: v.to(t.device, t.dtype) for (k, v), t in
+                                 zip(sd.items(), [teacher.state_dict()[k] for k in sd])}, strict=False)
+        return True
 
     def load(self, step: int | None, model, optimizer=None, device=None) -> dict:
         """Restore model (and optimizer) state; returns {'scheduler', 'runtime'}."""

@@ -272,6 +272,13 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
             from .init_transfer import InitTransferConfig, apply_init_transfer
 
             apply_init_transfer(target, fresh, _fill(InitTransferConfig, dict(t.init_transfer), {}, ""), device=dev)
+    def _teacher():
+        for tch in ((objective[1] if objective is not None else None), anchor_teacher,
+                    getattr(getattr(trainer, "latent_training", None), "teacher", None)):
+            if tch is not None:
+                return tch.model
+        return None
+
     if rank == 0:
         from .manifest import write_experiment_manifest
 
@@ -338,6 +345,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
 
         trainer.latent_training = LatentReasoningTraining(t.latent_reasoning, cfg.model)
         trainer.latent_training.attach_teacher(trainer.model)
+    if start > 0 and _teacher() is not None:
+        run.load_teacher(start, _teacher())
     spc = None
     if t.predictive_coding.get("enabled"):
         from .state_pc import RecurrentStatePCConfig
@@ -532,10 +541,10 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                 if state is not None and not extended and state.rhos is not None:
                     rt = {"position": state.position, "rhos": [r.detach() for r in state.rhos]}
                 run.save(step + 1, trainer.core if extended else trainer.model, trainer.opt, {"step": step + 1}, rt,
-                         extra=trainer.extra_state() if extended else None)
+                         extra=trainer.extra_state() if extended else None, teacher=_teacher())
         if rank == 0 and t.checkpoint_interval_iters:
             run.save(t.max_iters, trainer.core if extended else trainer.model, trainer.opt, {"step": t.max_iters},
-                     extra=trainer.extra_state() if extended else None)
+                     extra=trainer.extra_state() if extended else None, teacher=_teacher())
     except PeerFailure:
         if hb is not None:
             hb.stop()

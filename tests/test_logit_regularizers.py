@@ -200,3 +200,27 @@ def test_training_loop_with_greedy_rollout(tmp_path, monkeypatch, capsys):
           "--run-name", "rollout"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert math.isfinite(res["final_loss"])
+
+
+def test_anchor_teacher_is_checkpointed_and_restored(tmp_path, monkeypatch, capsys):
+    import torch as T
+
+    from burn_dragon_b200.cli.train import main
+    from burn_dragon_b200.train import checkpoint as C
+
+    cfg = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu.toml")
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    args = ["--config", cfg, "--set", "training.checkpoint_interval_iters=2",
+            "--set", "training.dynamics_anchor={enabled=true, weight=0.5, teacher_update_rate=0.5}"]
+    main(args + ["--set", "training.max_iters=2", "--run-name", "tch"])
+    run_dir = json.loads(capsys.readouterr().out.strip().splitlines()[-1])["run_dir"]
+    sd, _ = C.load_tensors(os.path.join(run_dir, "checkpoint", "teacher-model-2.bin"))
+    assert "encoder" in sd and T.isfinite(sd["encoder"]).all()
+    main(args + ["--set", "training.max_iters=3", "--run-name", "tch"])  # resumes and restores the teacher
+    assert os.path.exists(os.path.join(run_dir, "checkpoint", "teacher-model-3.bin"))
+    from burn_dragon_b200.config import load_training_config
+    from burn_dragon_b200.models.bdh import BDH
+
+    fresh = BDH(load_training_config(cfg).model, seed=99)
+    assert C.RunDir(run_dir).load_teacher(2, fresh)
+    T.testing.assert_close(dict(fresh.named_parameters())["encoder"].detach(), sd["encoder"])
