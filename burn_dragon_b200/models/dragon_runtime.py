@@ -75,6 +75,32 @@ class RuntimeState:
         for ls in self.layers:
             ls.detach()
 
+    def to_tensors(self) -> dict[str, torch.Tensor]:
+        """Flat ``<layer>.<field>[.<key>]`` tensors for a runtime-state checkpoint."""
+        out = {}
+        for i, ls in enumerate(self.layers):
+            for k, v in vars(ls).items():
+                if isinstance(v, torch.Tensor):
+                    out[f"{i}.{k}"] = v.detach()
+                elif isinstance(v, dict):
+                    out.update({f"{i}.{k}.{n}": t.detach() for n, t in v.items()})
+        return out
+
+    @staticmethod
+    def from_tensors(n_layer: int, tensors: dict[str, torch.Tensor], position: int = 0) -> "RuntimeState":
+        st = RuntimeState.new(n_layer)
+        for name, t in tensors.items():
+            parts = name.split(".")
+            ls = st.layers[int(parts[0])]
+            if len(parts) == 2:
+                setattr(ls, parts[1], t)
+            else:
+                d = getattr(ls, parts[1]) or {}
+                d[parts[2]] = t
+                setattr(ls, parts[1], d)
+        st.position = position
+        return st
+
 
 def _applies(last_layers: int | None, layer: int, n_layer: int) -> bool:
     if last_layers is None:

@@ -292,8 +292,10 @@ class RunDir:
             optim = ({"m": snap(optimizer.m), "v": snap(optimizer.v)}, {"t": optimizer.t, "lr": optimizer.lr})
         rt = meta = None
         if runtime is not None:
-            meta = {k: v for k, v in runtime.items() if k != "rhos"}
+            meta = {k: v for k, v in runtime.items() if k not in ("rhos", "state_tensors")}
             rt = {f"rho.{i}": snap(r) for i, r in enumerate(runtime.get("rhos") or [])}
+            # the layer-loop variants' auxiliary memories, ``state.<layer>.<field>[.<key>]``
+            rt.update({f"state.{k}": snap(v) for k, v in (runtime.get("state_tensors") or {}).items()})
         extra = {k: snap(v) for k, v in extra.items()} if extra else None
         # an EMA teacher (self-distillation, dynamics anchor, latent targets) is part of the
         # run's state: ``teacher-model-<step>.bin`` (burn_dragon_language/src/train/
@@ -401,9 +403,13 @@ class RunDir:
         rp = self._p("runtime-state", step)
         if os.path.exists(rp):
             rt, rmeta = load_tensors(rp, device)
-            rhos = [rt[f"rho.{i}"] for i in range(len(rt))] or None
+            nrho = sum(1 for k in rt if k.startswith("rho."))
+            rhos = [rt[f"rho.{i}"] for i in range(nrho)] or None
             runtime = dict(rmeta)
             runtime["rhos"] = rhos
+            st = {k[len("state."):]: v for k, v in rt.items() if k.startswith("state.")}
+            if st:
+                runtime["state_tensors"] = st
             out["runtime"] = runtime
         return out
 

@@ -262,6 +262,10 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
         rt = info.get("runtime")
         if rt and rt.get("rhos") is not None and not extended:
             state = ModelState(rt["rhos"], int(rt.get("position", 0)))
+        elif rt and rt.get("state_tensors") and extended:
+            from ..models.dragon_runtime import RuntimeState
+
+            state = RuntimeState.from_tensors(cfg.model.n_layer, rt["state_tensors"], int(rt.get("position", 0)))
     if start == 0 and t.init_checkpoint_path:
         target = trainer.core if extended else trainer.model
         fresh = {n: getattr(target, n).detach().clone() for n in target.store.shapes}
@@ -540,6 +544,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                 rt = None
                 if state is not None and not extended and state.rhos is not None:
                     rt = {"position": state.position, "rhos": [r.detach() for r in state.rhos]}
+                elif state is not None and extended:
+                    rt = {"position": state.position, "state_tensors": state.to_tensors()}
                 run.save(step + 1, trainer.core if extended else trainer.model, trainer.opt, {"step": step + 1}, rt,
                          extra=trainer.extra_state() if extended else None, teacher=_teacher())
         if rank == 0 and t.checkpoint_interval_iters:

@@ -108,3 +108,22 @@ def test_training_with_async_checkpoints(tmp_path, monkeypatch, capsys):
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "model-4.bin"))
     assert open(os.path.join(res["run_dir"], "latest")).read().strip() == "4"
+
+
+def test_runtime_state_with_auxiliary_memories_round_trips(tmp_path):
+    from burn_dragon_b200.models.dragon_runtime import LayerState, RuntimeState
+
+    st = RuntimeState([LayerState(rho=torch.randn(1, 2, 4, 8), y_state=torch.randn(1, 2, 4)),
+                       LayerState(summary_hidden=torch.randn(1, 1, 8), mamba={"ssm": torch.randn(1, 2, 3)})], 17)
+    cfg = DragonConfig(n_layer=2, n_embd=8, n_head=2, mlp_internal_dim_multiplier=2, dropout=0.0, vocab_size=16)
+    run = C.RunDir(os.path.join(str(tmp_path), "r"))
+    run.save(1, BDH(cfg, seed=1), None, {"step": 1},
+             {"position": st.position, "state_tensors": st.to_tensors()})
+    info = run.load(1, BDH(cfg, seed=2))
+    back = RuntimeState.from_tensors(2, info["runtime"]["state_tensors"], int(info["runtime"]["position"]))
+    assert back.position == 17 and back.layers[0].clocked_hidden is None
+    torch.testing.assert_close(back.layers[0].rho, st.layers[0].rho)
+    torch.testing.assert_close(back.layers[0].y_state, st.layers[0].y_state)
+    torch.testing.assert_close(back.layers[1].summary_hidden, st.layers[1].summary_hidden)
+    torch.testing.assert_close(back.layers[1].mamba["ssm"], st.layers[1].mamba["ssm"])
+    assert info["runtime"]["rhos"] is None
