@@ -60,3 +60,14 @@ def test_acquisition_gate():
     assert g["matched"] and abs(g["loss_ratios"][0] - 0.95) < 1e-12
     assert not acquisition_gate(base, bad, loss_floor_ratio=0.9)["matched"]
     assert not acquisition_gate(base, good, minimum_baseline_accuracy_gain=0.3)["matched"]
+
+
+def test_benchmark_clis():
+    from burn_dragon_b200.cli.continual_benchmark import main as cb
+    from burn_dragon_b200.cli.optimizer_dynamics import main as od
+
+    out = cb(["--tasks", "ab", "--steps-per-task", "2", "--batch-size", "4", "--block-size", "16", "--n-layer", "1",
+              "--n-embd", "16", "--n-head", "2", "--latent-total", "64"])
+    assert len(out["after_phase"]) == 2 and set(out["forgetting"]) == {"a", "b"}
+    out = od(["--max-iters", "2", "--population", "4", "--rank", "2", "--n-embd", "16"])
+    assert out["adamw"]["train_steps"] == out["eggroll"]["train_steps"] == 2
