@@ -418,6 +418,22 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                 trainer.step_idx += 1
                 prof.stop("optimizer")
                 loss = loss if loss is not None else torch.zeros(())
+            elif streaming and pc:
+                # layer-local PC on a chunk that continues the carried rho; the state then
+                # advances through the chunk with the updated weights, detached
+                from .optim import lr_at
+                from .predictive_coding import local_pc_step
+
+                xd, yd = x.to(dev), y.to(dev)
+                rho0s = None if state.rhos is None else [r.detach() for r in state.rhos]
+                loss, _ = local_pc_step(trainer.model, xd, yd, t.local_predictive_coding, rho0s=rho0s)
+                trainer.opt.prepare(lr_at(trainer.step_idx, trainer.base_lr, trainer.lr_schedule, trainer.max_iters))
+                trainer._update()
+                trainer.step_idx += 1
+                with torch.no_grad():
+                    trainer.model(xd, state=state)
+                state.detach_in_place()
+                prof.stop("forward_backward")
             elif streaming and spc is not None:
                 from .state_pc import state_pc_chunk_loss
 

@@ -84,3 +84,28 @@ def test_gradient_fidelity_report():
         r = arm["report"]
         assert r["reference_backward_calls"] == 1 and -1.0 <= r["global"]["cosine"] <= 1.0
         assert {f["parameter_family"] for f in r["parameter_families"]} >= {"encoder", "decoder", "embed"}
+
+
+def test_local_pc_runs_on_tbptt_streams(tmp_path, monkeypatch, capsys):
+    import json
+    import os
+
+    from burn_dragon_b200.cli.train import main
+    from burn_dragon_b200.train import predictive_coding as P
+
+    calls = []
+    real = P.local_pc_step
+
+    def spy(model, x, y, cfg, mask=None, rho0s=None):
+        calls.append(rho0s is not None)
+        return real(model, x, y, cfg, mask=mask, rho0s=rho0s)
+
+    monkeypatch.setattr(P, "local_pc_step", spy)
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    cfg = os.path.join(os.path.dirname(__file__), "..", "burn_dragon_b200", "configs", "tiny_cpu.toml")
+    main(["--config", cfg, "--set", "training.block_size=32", "--set", 'training.algorithm="predictive_coding"',
+          "--set", "training.tbptt_chunk_size=16", "--set", "training.tbptt_persist_across_steps=true",
+          "--set", "training.max_iters=3", "--run-name", "pcs"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res["final_loss"] is not None
+    assert calls == [False, True, False]  # a new stream, its continuation, a new stream
