@@ -289,6 +289,16 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
         write_experiment_manifest(cfg, run.path, os.path.basename(os.path.abspath(run.path)), dev.type,
                                   start if start > 0 else None)
     streaming = t.sequence_batching == "streaming" or t.tbptt_persist_across_steps
+    if streaming:
+        # the stream step (plain, recurrent-state PC or local PC) does not run these
+        lost = [name for name, on in (("training.objective", objective is not None),
+                                      ("logit regularizers / dynamics anchor / greedy rollout", regs is not None),
+                                      ("optimizer.name = eggroll", egg is not None),
+                                      ("training.module_lr_scales", mlr is not None),
+                                      ("training.neuron_scaling", scaler is not None),
+                                      ("training.continual_backprop", cbp is not None)) if on]
+        if lost:
+            raise ValueError(f"{', '.join(lost)} not implemented with streaming TBPTT batches")
     data_rank = 0 if mode in ("tensor_parallel_neuron", "pipeline") else rank
     data_world = 1 if mode in ("tensor_parallel_neuron", "pipeline") else world
     if mode == "hybrid_2d":

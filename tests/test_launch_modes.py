@@ -109,3 +109,10 @@ def test_experiment_manifest_records_each_launch(tmp_path, monkeypatch, capsys):
     assert any(x["file_name"] == "model-2.bin" and x["bytes"] > 0 for x in second["checkpoint_artifacts"])
     assert second["contract_changed"]  # max_iters grew from 2 to 3
     assert len(first["effective_config_sha256"]) == 64
+
+
+def test_streaming_rejects_step_features_it_does_not_run(tmp_path, monkeypatch, capsys):
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    with pytest.raises(ValueError, match="module_lr_scales"):
+        _run(capsys, "--set", 'training.sequence_batching="streaming"', "--set", "training.tbptt_chunk_size=16",
+             "--set", 'training.module_lr_scales=[{target="embedding", scale=0.5}]', "--run-name", "bad")
