@@ -64,6 +64,16 @@ void tp_scatter_rows(const at::Tensor& src, std::vector<int64_t> slots, int64_t 
                      int64_t D, int64_t slot_stride);
 void reduce_mean(std::vector<int64_t> grad, std::vector<int64_t> flags, int64_t rank, int64_t lo, int64_t hi,
                  const at::Tensor& err);
+void ddp_step(std::vector<int64_t> grad, std::vector<int64_t> shadow, bool grad_bf16, int64_t rank, int64_t lo,
+              int64_t hi, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1, double b2,
+              double eps, double wd, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef);
+void ddp_reduce(std::vector<int64_t> grad, std::vector<int64_t> shadow, bool grad_bf16, int64_t rank, int64_t lo,
+                int64_t hi, const at::Tensor& gred, const at::Tensor& sumsq);
+void ddp_apply(std::vector<int64_t> grad, std::vector<int64_t> shadow, int64_t rank, int64_t lo, int64_t hi,
+               const at::Tensor& gred, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1,
+               double b2, double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef);
+void ddp_norm_exchange(std::vector<int64_t> flags, int64_t rank, const at::Tensor& sumsq, double max_norm,
+                       const at::Tensor& out, const at::Tensor& err);
 void percentile_thresholds(const at::Tensor& values, double q, const at::Tensor& out);
 }  // namespace bd
 
@@ -94,5 +104,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("reduce_mean", &bd::reduce_mean);
   m.def("tp_reduce_gather", &bd::tp_reduce_gather);
   m.def("tp_scatter_rows", &bd::tp_scatter_rows);
+  m.def("ddp_step", &bd::ddp_step);
+  m.def("ddp_reduce", &bd::ddp_reduce);
+  m.def("ddp_apply", &bd::ddp_apply);
+  m.def("ddp_norm_exchange", &bd::ddp_norm_exchange);
   m.def("percentile_thresholds", &bd::percentile_thresholds);
 }

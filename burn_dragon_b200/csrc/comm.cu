@@ -22,6 +22,7 @@
 #include <torch/extension.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <vector>
 
 namespace bd {
@@ -200,6 +201,230 @@ __global__ void tp_scatter_rows_kernel(const float* __restrict__ src, DstPtrs sl
   }
 }
 
+
+// ---------------------------------------------------------------------------------------
+// The data-parallel optimizer step over NVLink, bf16 transport (ddp_step):
+//
+//   every rank   casts its fp32 gradients into its symmetric bf16 gradient buffer
+//   barrier(0)
+//   rank r       owns elements [lo_r, hi_r): sums that slice of every peer's bf16 gradient
+//                (fp32 accumulation, peers loaded together so their latencies overlap),
+//                applies AdamW to its fp32 master slice (kept only here) and its moment
+//                shard, and stores the new bf16 weights into every peer's shadow buffer
+//   barrier(1)
+//
+// Bytes over NVLink per rank: (W-1)/W * P * 2 in and the same out (P = parameters), a
+// third of the fp32-gradient, fp32-master step. With global-norm clipping the sum runs
+// first into a local fp32 shard (ddp_reduce), the ranks exchange their shard's sum of
+// squares (ddp_norm_exchange), and the update reads the clipped local shard (ddp_apply).
+struct DdpPtrs {
+  const void* grad[kMaxRanks];  // bf16 (or fp32) gradient buffer of every rank
+  __nv_bfloat16* shadow[kMaxRanks];
+};
+
+template <typename GT>
+struct Vec8 {
+  static __device__ __forceinline__ void load(const GT* p, float (&o)[8]);
+};
+template <>
+struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float (&o)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+};
+template <>
+struct Vec8<float> {
+  static __device__ __forceinline__ void load(const float* p, float (&o)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+  }
+};
+
+// Sum of the W ranks' gradients for 8 elements at i, every peer's load issued before any
+// is used (the loop bound is a template constant, so the loads are not serialized behind
+// the adds of earlier peers).
+template <int W, typename GT>
+__device__ __forceinline__ void peer_sum8(const DdpPtrs& pp, int rank, long long i, float (&g)[8]) {
+  float x[W][8];
+#pragma unroll
+  for (int r = 0; r < W; ++r) {
+    int src = rank + r;
+    if (src >= W) src -= W;  // stagger the peer each rank starts with
+    Vec8<GT>::load(reinterpret_cast<const GT*>(pp.grad[src]) + i, x[r]);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float a = 0.f;
+#pragma unroll
+    for (int r = 0; r < W; ++r) a += x[r][k];
+    g[k] = a;
+  }
+}
+
+__device__ __forceinline__ float block_sum(float v) {
+  __shared__ float red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (w == 0) {
+    t = l < (int)(blockDim.x / 32) ? red[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  }
+  return t;  // valid in thread 0
+}
+
+// AdamW on 8 elements of the owned slice (hyper = {lr, 1 - b1^t, 1 - b2^t}): the fp32
+// master at flat index i, the moments at shard index s; then the new weights as bf16
+// into every rank's shadow at i.
+template <int W>
+__device__ __forceinline__ void adamw8_gather(const DdpPtrs& pp, int rank, long long i, long long s, float (&g)[8],
+                                              float* __restrict__ master, float* __restrict__ m,
+                                              float* __restrict__ v, float lr, float b1, float b2, float eps,
+                                              float wd, float bc1, float bc2) {
+  float pv[8], mv[8], vv[8];
+  Vec8<float>::load(master + i, pv);
+  Vec8<float>::load(m + s, mv);
+  Vec8<float>::load(v + s, vv);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    mv[k] = b1 * mv[k] + (1.f - b1) * g[k];
+    vv[k] = b2 * vv[k] + (1.f - b2) * g[k] * g[k];
+    pv[k] = pv[k] * (1.f - lr * wd) - lr * (mv[k] / bc1) / (sqrtf(vv[k] / bc2) + eps);
+  }
+  *reinterpret_cast<float4*>(master + i) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+  *reinterpret_cast<float4*>(master + i + 4) = make_float4(pv[4], pv[5], pv[6], pv[7]);
+  *reinterpret_cast<float4*>(m + s) = make_float4(mv[0], mv[1], mv[2], mv[3]);
+  *reinterpret_cast<float4*>(m + s + 4) = make_float4(mv[4], mv[5], mv[6], mv[7]);
+  *reinterpret_cast<float4*>(v + s) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+  *reinterpret_cast<float4*>(v + s + 4) = make_float4(vv[4], vv[5], vv[6], vv[7]);
+  uint4 hb;
+  __nv_bfloat162 h;
+  h = __floats2bfloat162_rn(pv[0], pv[1]); hb.x = *reinterpret_cast<unsigned int*>(&h);
+  h = __floats2bfloat162_rn(pv[2], pv[3]); hb.y = *reinterpret_cast<unsigned int*>(&h);
+  h = __floats2bfloat162_rn(pv[4], pv[5]); hb.z = *reinterpret_cast<unsigned int*>(&h);
+  h = __floats2bfloat162_rn(pv[6], pv[7]); hb.w = *reinterpret_cast<unsigned int*>(&h);
+#pragma unroll
+  for (int r = 0; r < W; ++r) {
+    int dst = rank + r;
+    if (dst >= W) dst -= W;
+    *reinterpret_cast<uint4*>(pp.shadow[dst] + i) = hb;
+  }
+}
+
+// Fused (no clipping): peer sum + AdamW + shadow all-gather in one pass. `master` is
+// this rank's full fp32 buffer (the slice [lo, hi) is updated); m / v are shard-local.
+template <int W, typename GT>
+__global__ void __launch_bounds__(256) ddp_step_kernel(DdpPtrs pp, int rank, long long lo, long long hi,
+                                                       float* __restrict__ master, float* __restrict__ m,
+                                                       float* __restrict__ v, float b1, float b2, float eps,
+                                                       float wd, const float* __restrict__ hyper,
+                                                       const float* __restrict__ coef) {
+  const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
+  const float scale = (1.0f / W) * (coef ? coef[0] : 1.0f);
+  for (long long i = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
+       i += 8ll * (long long)gridDim.x * blockDim.x) {
+    float g[8];
+    peer_sum8<W, GT>(pp, rank, i, g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] *= scale;
+    adamw8_gather<W>(pp, rank, i, i - lo, g, master, m, v, lr, b1, b2, eps, wd, bc1, bc2);
+  }
+}
+
+// Clipping, pass 1: the owned slice's mean gradient into a local fp32 shard, and its
+// sum of squares into sumsq[0] (zeroed by the caller's stream before this launch).
+template <int W, typename GT>
+__global__ void __launch_bounds__(256) ddp_reduce_kernel(DdpPtrs pp, int rank, long long lo, long long hi,
+                                                         float* __restrict__ gred, float* __restrict__ sumsq) {
+  float acc = 0.f;
+  for (long long i = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
+       i += 8ll * (long long)gridDim.x * blockDim.x) {
+    float g[8];
+    peer_sum8<W, GT>(pp, rank, i, g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      g[k] *= 1.0f / W;
+      acc += g[k] * g[k];
+    }
+    float* o = gred + (i - lo);
+    *reinterpret_cast<float4*>(o) = make_float4(g[0], g[1], g[2], g[3]);
+    *reinterpret_cast<float4*>(o + 4) = make_float4(g[4], g[5], g[6], g[7]);
+  }
+  const float t = block_sum(acc);
+  if (threadIdx.x == 0) atomicAdd(sumsq, t);
+}
+
+// Clipping, pass 2: AdamW from the local reduced shard, scaled by coef[0].
+template <int W>
+__global__ void __launch_bounds__(256) ddp_apply_kernel(DdpPtrs pp, int rank, long long lo, long long hi,
+                                                        const float* __restrict__ gred, float* __restrict__ master,
+                                                        float* __restrict__ m, float* __restrict__ v, float b1,
+                                                        float b2, float eps, float wd,
+                                                        const float* __restrict__ hyper,
+                                                        const float* __restrict__ coef) {
+  const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
+  const float c = coef[0];
+  for (long long i = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
+       i += 8ll * (long long)gridDim.x * blockDim.x) {
+    float g[8];
+    Vec8<float>::load(gred + (i - lo), g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] *= c;
+    adamw8_gather<W>(pp, rank, i, i - lo, g, master, m, v, lr, b1, b2, eps, wd, bc1, bc2);
+  }
+}
+
+// Global gradient norm across the ranks: each rank publishes its shard's sum of squares
+// into every peer's flag page (value, then an epoch flag with release semantics), waits
+// (bounded) for all W values of this epoch, and writes {clip coefficient, norm} to out.
+// The epoch is the step counter the phase-0 barrier advanced.
+__global__ void ddp_norm_exchange_kernel(PeerPtrs pp, int rank, int world, const float* __restrict__ sumsq,
+                                         float max_norm, float* __restrict__ out, int* err) {
+  const int t = threadIdx.x;
+  __shared__ float vals[kMaxRanks];
+  const unsigned int epoch = *(volatile unsigned int*)(pp.flags[rank] + 2 * kMaxRanks);
+  const float mine = *sumsq;
+  if (t < world) {
+    pp.flags[t][4 * kMaxRanks + rank] = __float_as_uint(mine);
+    __threadfence_system();
+    st_release_sys(pp.flags[t] + 3 * kMaxRanks + rank, epoch);
+    const unsigned long long t0 = gtimer();
+    float val = 0.f;
+    while (true) {
+      if (ld_acquire_sys(pp.flags[rank] + 3 * kMaxRanks + t) >= epoch) {
+        val = __uint_as_float(*(volatile unsigned int*)(pp.flags[rank] + 4 * kMaxRanks + t));
+        break;
+      }
+      if (gtimer() - t0 > kPeerWaitNs) {
+        atomicCAS(err, 0, 110);
+        break;
+      }
+    }
+    vals[t] = val;
+  }
+  __syncthreads();
+  if (t == 0) {
+    float tot = 0.f;
+    for (int r = 0; r < world; ++r) tot += vals[r];
+    const float norm = sqrtf(tot);
+    out[0] = fminf(1.0f, max_norm / (norm + 1e-6f));
+    out[1] = norm;
+  }
+}
+
 PeerPtrs make_ptrs(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
                    const std::vector<int64_t>& shadow, const std::vector<int64_t>& flags) {
   PeerPtrs pp;
@@ -315,6 +540,115 @@ void tp_scatter_rows(const at::Tensor& src, std::vector<int64_t> slots, int64_t 
   auto st = at::cuda::getCurrentCUDAStream(src.get_device()).stream();
   tp_scatter_rows_kernel<<<148 * 2, 256, 0, st>>>(src.data_ptr<float>(), dp, (int)rank, rows, M, (int)D,
                                                   slot_stride);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+
+namespace {
+DdpPtrs make_ddp_ptrs(const std::vector<int64_t>& grad, const std::vector<int64_t>& shadow) {
+  DdpPtrs pp;
+  memset(&pp, 0, sizeof(pp));
+  TORCH_CHECK(grad.size() >= 1 && grad.size() <= kMaxRanks && shadow.size() == grad.size(),
+              "one gradient and one shadow pointer per rank (<= 8)");
+  for (size_t r = 0; r < grad.size(); ++r) {
+    pp.grad[r] = reinterpret_cast<const void*>(grad[r]);
+    pp.shadow[r] = reinterpret_cast<__nv_bfloat16*>(shadow[r]);
+    TORCH_CHECK(grad[r] % 16 == 0 && shadow[r] % 16 == 0, "peer buffers must be 16-byte aligned");
+  }
+  return pp;
+}
+
+template <typename F>
+void dispatch_world(int world, F&& f) {
+  switch (world) {
+    case 1: f(std::integral_constant<int, 1>{}); break;
+    case 2: f(std::integral_constant<int, 2>{}); break;
+    case 3: f(std::integral_constant<int, 3>{}); break;
+    case 4: f(std::integral_constant<int, 4>{}); break;
+    case 5: f(std::integral_constant<int, 5>{}); break;
+    case 6: f(std::integral_constant<int, 6>{}); break;
+    case 7: f(std::integral_constant<int, 7>{}); break;
+    case 8: f(std::integral_constant<int, 8>{}); break;
+    default: TORCH_CHECK(false, "1..8 ranks");
+  }
+}
+
+int ddp_grid(long long n8) {
+  // enough 8-element work items in flight to cover NVLink latency, never more blocks
+  // than work
+  const long long blocks = (n8 + 255) / 256;
+  return (int)std::max<long long>(1, std::min<long long>(blocks, 148 * 4));
+}
+}  // namespace
+
+// One fused data-parallel optimizer step (no clipping): see ddp_step_kernel.
+void ddp_step(std::vector<int64_t> grad, std::vector<int64_t> shadow, bool grad_bf16, int64_t rank, int64_t lo,
+              int64_t hi, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1, double b2,
+              double eps, double wd, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef) {
+  DdpPtrs pp = make_ddp_ptrs(grad, shadow);
+  TORCH_CHECK(lo % 8 == 0 && hi % 8 == 0 && hi >= lo, "shard bounds must be multiples of 8");
+  TORCH_CHECK(master.scalar_type() == at::kFloat && master.numel() >= hi, "fp32 master covering the shard");
+  TORCH_CHECK(m.numel() >= hi - lo && v.numel() >= hi - lo, "moment shards too small");
+  auto st = at::cuda::getCurrentCUDAStream(m.get_device()).stream();
+  const int grid = ddp_grid((hi - lo) / 8);
+  const float* cp = coef ? coef->data_ptr<float>() : nullptr;
+  dispatch_world((int)grad.size(), [&](auto W) {
+    if (grad_bf16)
+      ddp_step_kernel<W(), __nv_bfloat16><<<grid, 256, 0, st>>>(
+          pp, (int)rank, lo, hi, master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), (float)b1,
+          (float)b2, (float)eps, (float)wd, hyper.data_ptr<float>(), cp);
+    else
+      ddp_step_kernel<W(), float><<<grid, 256, 0, st>>>(pp, (int)rank, lo, hi, master.data_ptr<float>(),
+                                                        m.data_ptr<float>(), v.data_ptr<float>(), (float)b1,
+                                                        (float)b2, (float)eps, (float)wd, hyper.data_ptr<float>(), cp);
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Clipping pass 1: peer sum of the owned slice into gred, its sum of squares into sumsq[0].
+void ddp_reduce(std::vector<int64_t> grad, std::vector<int64_t> shadow, bool grad_bf16, int64_t rank, int64_t lo,
+                int64_t hi, const at::Tensor& gred, const at::Tensor& sumsq) {
+  DdpPtrs pp = make_ddp_ptrs(grad, shadow);
+  TORCH_CHECK(lo % 8 == 0 && hi % 8 == 0 && gred.numel() >= hi - lo, "shard bounds / reduced shard size");
+  auto st = at::cuda::getCurrentCUDAStream(gred.get_device()).stream();
+  C10_CUDA_CHECK(cudaMemsetAsync(sumsq.data_ptr<float>(), 0, sizeof(float), st));
+  const int grid = ddp_grid((hi - lo) / 8);
+  dispatch_world((int)grad.size(), [&](auto W) {
+    if (grad_bf16)
+      ddp_reduce_kernel<W(), __nv_bfloat16><<<grid, 256, 0, st>>>(pp, (int)rank, lo, hi, gred.data_ptr<float>(),
+                                                                  sumsq.data_ptr<float>());
+    else
+      ddp_reduce_kernel<W(), float><<<grid, 256, 0, st>>>(pp, (int)rank, lo, hi, gred.data_ptr<float>(),
+                                                          sumsq.data_ptr<float>());
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Clipping pass 2: AdamW from the reduced shard scaled by coef[0], shadow all-gather.
+void ddp_apply(std::vector<int64_t> grad, std::vector<int64_t> shadow, int64_t rank, int64_t lo, int64_t hi,
+               const at::Tensor& gred, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1,
+               double b2, double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef) {
+  DdpPtrs pp = make_ddp_ptrs(grad, shadow);
+  TORCH_CHECK(lo % 8 == 0 && hi % 8 == 0 && gred.numel() >= hi - lo, "shard bounds / reduced shard size");
+  auto st = at::cuda::getCurrentCUDAStream(gred.get_device()).stream();
+  const int grid = ddp_grid((hi - lo) / 8);
+  dispatch_world((int)grad.size(), [&](auto W) {
+    ddp_apply_kernel<W()><<<grid, 256, 0, st>>>(pp, (int)rank, lo, hi, gred.data_ptr<float>(),
+                                                master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                                                (float)b1, (float)b2, (float)eps, (float)wd, hyper.data_ptr<float>(),
+                                                coef.data_ptr<float>());
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Cross-rank global norm: see ddp_norm_exchange_kernel. out = {coef, norm}.
+void ddp_norm_exchange(std::vector<int64_t> flags, int64_t rank, const at::Tensor& sumsq, double max_norm,
+                       const at::Tensor& out, const at::Tensor& err) {
+  std::vector<int64_t> z(flags.size(), 0);
+  PeerPtrs pp = make_ptrs(z, z, z, flags);
+  auto st = at::cuda::getCurrentCUDAStream(out.get_device()).stream();
+  ddp_norm_exchange_kernel<<<1, 32, 0, st>>>(pp, (int)rank, (int)flags.size(), sumsq.data_ptr<float>(),
+                                             (float)max_norm, out.data_ptr<float>(), err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

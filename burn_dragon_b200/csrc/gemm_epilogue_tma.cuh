@@ -1,5 +1,5 @@
 // gemm_epilogue_tma.cuh — asynchronous epilogue for the memory-bound BDH modes
-// (x-projection + RoPE, gate, decoder backward, dQ), tile N = 128.
+// (x-projection + RoPE, gate, decoder backward, dQ), tile N = 128 or 256.
 //
 // Each epilogue warp owns a 32-row x CW-column chunk of every tile: CW = 64 with 8
 // warps (128-byte rows, 128B swizzle) or CW = 32 with 16 warps (64-byte rows, 64B
@@ -129,6 +129,12 @@ __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoor
 // The epilogue warps' loop over this CTA's tiles (tile t0, t0 + tstep, ...). PAIR: the
 // tiles are CTA-pair tiles (rows shifted by row_shift for this CTA) and the accumulator
 // is released on the leader CTA's tmem-empty barrier.
+//
+// Warp ew owns TMEM lane quadrant (warp % 4) and column group ew / 4 of width
+// GW = BN / (NEPI / 4); it walks its group in chunks of CW columns (CH = GW / CW chunks
+// per tile: 1 for BN = 128, 2 for BN = 256). Each chunk is one unit of the per-warp
+// buffer ring: the aux tiles of the next unit are fetched while this one is computed.
+// The accumulator is handed back after the tile's last chunk has been read from TMEM.
 template <int BN, int EPI, int KIND, bool PAIR>
 __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total, int t0, int tstep, int row_shift,
                                                   uint8_t* sEpi, uint64_t (*aux_bar)[3], uint64_t* tfull_bar,
@@ -136,7 +142,11 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
                                                   uint32_t leader_tempty1, bool leader, uint32_t tmem_base,
                                                   volatile int* abort_flag, int warp, int lane) {
   constexpr int NAUX = epi_naux<EPI>();
-  constexpr int CW = KIND == 3 ? 32 : 64;  // columns per warp
+  constexpr int CW = KIND == 3 ? 32 : 64;  // columns per chunk
+  constexpr int NEPI = KIND == 3 ? 16 : 8;
+  constexpr int GW = BN / (NEPI / 4);      // columns per warp and tile
+  constexpr int CH = GW / CW;              // chunks per warp and tile
+  static_assert(CH >= 1 && GW % CW == 0, "tile N must be a multiple of the warp column group");
   constexpr int kTmaTileBytes = 32 * CW * 2;
   constexpr int NBUF = KIND == 4 ? 3 : 2;  // ring of tile buffers
   constexpr int TENS = KIND == 4 ? 1 : 2;  // tensors per buffer
@@ -144,7 +154,7 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
   const int quad = warp & 3;  // TMEM lane quadrant this warp may access
   const int r_local = quad * 32 + lane;
   uint8_t* wbuf = sEpi + ew * NBUF * TENS * kTmaTileBytes;  // [buffer][tensor] tiles
-  const int col_off = (ew >> 2) * CW;
+  const int grp_off = (ew >> 2) * GW;
   auto tile = [&](int t) {
     if constexpr (PAIR) {
       TileCoord c = decode_tile_pair(p, t, BN);
@@ -157,7 +167,8 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
   // Per-buffer issue / wait counters keep the mbarrier parities exact (uniform across
   // the warp; only lane 0 issues).
   int n_issued[3] = {0, 0, 0}, n_waited[3] = {0, 0, 0};
-  auto issue_aux = [&](int t, int b) {
+  // aux fetch of chunk c of tile t into buffer b (no zero tiles in these modes)
+  auto issue_aux = [&](int t, int c, int b) {
     if constexpr (NAUX > 0) {
       if (t >= total) return;
       const TileCoord n = tile(t);
@@ -165,67 +176,86 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
       ++n_issued[b];
       if (lane != 0) return;
       uint8_t* dst = wbuf + b * TENS * kTmaTileBytes;
+      const int col = n.n0 + grp_off + c * CW;
       fence_proxy_async_smem();
       mbar_arrive_expect_tx(&aux_bar[ew][b], NAUX * kTmaTileBytes);
-      tma_load_4d(dst, &p.tx0, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1, n.z2);
+      tma_load_4d(dst, &p.tx0, &aux_bar[ew][b], col, n.m0 + quad * 32, n.z1, n.z2);
       if constexpr (NAUX > 1)
-        tma_load_4d(dst + kTmaTileBytes, &p.tx1, &aux_bar[ew][b], n.n0 + col_off, n.m0 + quad * 32, n.z1, n.z2);
+        tma_load_4d(dst + kTmaTileBytes, &p.tx1, &aux_bar[ew][b], col, n.m0 + quad * 32, n.z1, n.z2);
     }
   };
-  issue_aux(t0, 0);
+  issue_aux(t0, 0, 0);
   int acc = 0;
   uint32_t acc_phase = 0;
   int it = 0;
-  for (int t = t0; t < total; t += tstep, ++it) {
+  bool ok = true;
+  for (int t = t0; t < total && ok; t += tstep) {
     const TileCoord tc = tile(t);
-    const int b = it % NBUF;
-    const int bn = (it + 1) % NBUF;
-    uint8_t* b0 = wbuf + b * TENS * kTmaTileBytes;
-    uint8_t* b1 = TENS > 1 ? b0 + kTmaTileBytes : b0;
-    // the next buffer was last read by this warp's stores NBUF - 1 tiles ago; with no aux
-    // prefetch (x-projection) only this tile's buffer, stored two tiles ago, must be
-    // free, so the previous tile's store may still be reading
-    if (lane == 0) {
-      if constexpr (NBUF == 3 || NAUX == 0)
-        bulk_wait_group_read1();
-      else
-        bulk_wait_group_read0();
-    }
-    __syncwarp();
-    issue_aux(t + tstep, bn);
     if (tc.zero) continue;  // (no zero tiles in these modes unless K is empty)
-    if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) break;
-    tc_fence_after();
-    float v[CW];
-    if constexpr (CW == 32)
-      tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
-    else
-      tmem_ld64(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      if (!PAIR || leader)
-        mbar_arrive(&tempty_bar[acc]);
+#pragma unroll 1
+    for (int c = 0; c < CH; ++c, ++it) {
+      const int b = it % NBUF;
+      const int bn = (it + 1) % NBUF;
+      uint8_t* b0 = wbuf + b * TENS * kTmaTileBytes;
+      uint8_t* b1 = TENS > 1 ? b0 + kTmaTileBytes : b0;
+      // the next buffer was last read by this warp's stores NBUF - 1 units ago; with no
+      // aux prefetch (x-projection) only this unit's buffer, stored two units ago, must be
+      // free, so the previous unit's store may still be reading
+      if (lane == 0) {
+        if constexpr (NBUF == 3 || NAUX == 0)
+          bulk_wait_group_read1();
+        else
+          bulk_wait_group_read0();
+      }
+      __syncwarp();
+      if (c + 1 < CH)
+        issue_aux(t, c + 1, bn);
       else
-        mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
-    }
-    if (++acc == 2) {
-      acc = 0;
-      acc_phase ^= 1;
-    }
-    if constexpr (NAUX > 0) {
-      if (!mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
-      ++n_waited[b];
-    }
-    tma_epi_math<EPI, CW>(p, tc, v, tc.m0 + r_local, tc.n0 + col_off, b0, b1, lane);
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      const int c0 = tc.n0 + col_off, c1 = tc.m0 + quad * 32;
-      tma_store_4d(&p.to0, b0, c0, c1, tc.z1, tc.z2);
-      if (EPI == EPI_DEC_BWD || (EPI == EPI_RELU_ROPE && p.e.freq != nullptr))
-        tma_store_4d(&p.to1, b1, c0, c1, tc.z1, tc.z2);
-      bulk_commit_group();
+        issue_aux(t + tstep, 0, bn);
+      if (c == 0) {
+        if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      const int col_off = grp_off + c * CW;
+      float v[CW];
+      if constexpr (CW == 32)
+        tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
+      else
+        tmem_ld64(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + col_off, v);
+      if (c == CH - 1) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (!PAIR || leader)
+            mbar_arrive(&tempty_bar[acc]);
+          else
+            mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+        }
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if constexpr (NAUX > 0) {
+        if (!mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, abort_flag, p.err, kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        ++n_waited[b];
+      }
+      tma_epi_math<EPI, CW>(p, tc, v, tc.m0 + r_local, tc.n0 + col_off, b0, b1, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int c0 = tc.n0 + col_off, c1 = tc.m0 + quad * 32;
+        tma_store_4d(&p.to0, b0, c0, c1, tc.z1, tc.z2);
+        if (EPI == EPI_DEC_BWD || (EPI == EPI_RELU_ROPE && p.e.freq != nullptr))
+          tma_store_4d(&p.to1, b1, c0, c1, tc.z1, tc.z2);
+        bulk_commit_group();
+      }
     }
   }
   if (lane == 0) {

@@ -107,9 +107,9 @@ int num_sms_of(int dev) { return num_sms(dev); }
 
 namespace {
 const Entry* find_entry(int bn, bool a_mn, bool b_mn, int epi, bool pair) {
-  const Entry* tables[4] = {kGemmTableA, kGemmTableB, kGemmTableC, kGemmTableD};
-  const int sizes[4] = {kGemmTableASize, kGemmTableBSize, kGemmTableCSize, kGemmTableDSize};
-  for (int t = 0; t < 4; ++t)
+  const Entry* tables[5] = {kGemmTableA, kGemmTableB, kGemmTableC, kGemmTableD, kGemmTableE};
+  const int sizes[5] = {kGemmTableASize, kGemmTableBSize, kGemmTableCSize, kGemmTableDSize, kGemmTableESize};
+  for (int t = 0; t < 5; ++t)
     for (int i = 0; i < sizes[t]; ++i) {
       const Entry& en = tables[t][i];
       if (en.bn == bn && en.a_mn == a_mn && en.b_mn == b_mn && en.epi == epi && en.pair == pair) return &en;
@@ -212,7 +212,8 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   if (epi == EPI_DEC_BWD) TORCH_CHECK(e.aux0 && e.aux1 && e.out1, "decoder backward epilogue needs x, yn, out1");
   if (epi == EPI_DQ) TORCH_CHECK(e.aux0, "dq epilogue needs dx_part (carrying the x mask)");
   if (epi == EPI_RELU_ROPE || epi == EPI_GATE || epi == EPI_DEC_BWD || epi == EPI_DQ) {
-    TORCH_CHECK(bn == 128, "TMA-epilogue modes use tile N = 128");
+    TORCH_CHECK(bn == 128 || bn == 256, "TMA-epilogue modes use tile N = 128 or 256");
+    TORCH_CHECK(!causal_skip, "TMA-epilogue modes have no zero tiles");
     // columns per epilogue warp: 32 for the 16-warp x-projection epilogue, else 64
     const uint32_t cw = epi == EPI_RELU_ROPE ? 32 : 64;
     p.to0 = encode_out_map(e.out0, N, M, ld, Z1, sz1, Z2, sz2, cw);

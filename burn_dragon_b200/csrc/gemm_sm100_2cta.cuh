@@ -14,10 +14,11 @@
 //   both CTAs  warps 2-9  epilogue on their own 128 rows; release the accumulator on
 //                         the leader's tmem-empty barrier (one arrival per epilogue warp of both CTAs)
 // All epilogue kinds: fp32, staged bf16 and the TMA epilogues (each CTA runs the same
-// per-warp TMA epilogue loop as the 1-CTA kernel on its own 128 rows). The TMA-epilogue
-// modes are not instantiated on pairs: measured at BDH-GPU batch 32 they ran 25-45%
-// slower than the 1-CTA kernel (the pair couples two CTAs' epilogues through the shared
-// accumulator release, and these modes are bound by the epilogue, not operand bytes).
+// per-warp TMA epilogue loop as the 1-CTA kernel on its own 128 rows). For the
+// TMA-epilogue modes the pair runs 256 x 256 tiles (each CTA 128 x 256, two 64-column
+// chunks per epilogue warp): per output element a CTA then stages half the operand bytes
+// of a 1-CTA 128 x 128 tile. (256 x 128 pair tiles measured 25-45% slower than the 1-CTA
+// kernel: the saving is smaller and the pair couples two CTAs' epilogues.)
 // Bounded waits as in the 1-CTA kernel.
 #pragma once
 
@@ -31,8 +32,10 @@ struct Gemm2Cfg {
   // TMA-epilogue kinds: the 1-CTA kernel's warp counts and tile buffers (GemmCfg)
   static constexpr int NEPI = GemmCfg<BN, KIND>::NEPI;
   static constexpr int EPI_BYTES = KIND >= 2 ? GemmCfg<BN, KIND>::EPI_BYTES : (KIND == 1 ? 8 * 2 * 4096 : 0);
-  static constexpr int STAGES = KIND == 4   ? 5
-                                : KIND >= 2 ? 4
+  // TMA-epilogue kinds with BN = 256 stage 32 KB per CTA per k-block: one stage fewer
+  // keeps the ring plus the epilogue tile buffers inside 227 KB
+  static constexpr int STAGES = KIND == 4   ? (BN == 256 ? 4 : 5)
+                                : KIND >= 2 ? (BN == 256 ? 3 : 4)
                                 : KIND == 1 ? (BN == 256 ? 5 : 6)
                                             : (BN == 256 ? 6 : 8);
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
@@ -44,7 +47,7 @@ template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(Gemm2Cfg<BN, epi_kind<EPI>()>::THREADS, 1)
     gemm_sm100_2cta_kernel(const __grid_constant__ GemmParams p) {
   constexpr int KIND = epi_kind<EPI>();
-  static_assert(KIND < 2 || BN == 128, "the TMA epilogue is built for tile N = 128");
+  static_assert(KIND < 2 || BN == 128 || BN == 256, "the TMA epilogue is built for tile N = 128 / 256");
   constexpr bool STAGED = KIND == 1;
   using Cfg = Gemm2Cfg<BN, KIND>;
   constexpr int STAGES = Cfg::STAGES;

@@ -9,7 +9,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, epi_kind<EPI>()>::THREADS, 1)
     gemm_sm100_kernel(const __grid_constant__ GemmParams p) {
   constexpr int KIND = epi_kind<EPI>();
   constexpr bool STAGED = KIND == 1;
-  static_assert(KIND < 2 || BN == 128, "the TMA epilogue is built for tile N = 128");
+  static_assert(KIND < 2 || BN == 128 || BN == 256, "the TMA epilogue is built for tile N = 128 / 256");
   using Cfg = GemmCfg<BN, KIND>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];

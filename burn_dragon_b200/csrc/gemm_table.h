@@ -1,5 +1,5 @@
 // gemm_table.h — the instantiation table of the tcgen05 GEMM engine. The kernel
-// template is instantiated in three translation units (gemm_inst_{a,b,c}.cu) so nvcc
+// template is instantiated in five translation units (gemm_inst_{a..e}.cu) so nvcc
 // compiles them in parallel; gemm_host.cu looks a launch function up by its
 // (tile N, A major, B major, epilogue) key.
 #pragma once
@@ -28,5 +28,7 @@ extern const Entry kGemmTableC[];
 extern const int kGemmTableCSize;
 extern const Entry kGemmTableD[];
 extern const int kGemmTableDSize;
+extern const Entry kGemmTableE[];
+extern const int kGemmTableESize;
 
 }  // namespace bd

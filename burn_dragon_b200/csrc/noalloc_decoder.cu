@@ -36,6 +36,7 @@
 #include <cstring>
 #include <exception>
 
+#include "bdh_noalloc.h"
 #include "gemm_sm100.cuh"
 #include "gemm_table.h"
 
@@ -49,16 +50,9 @@ constexpr int kMaxDevices = 64;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
 int* g_err_ptr[kMaxDevices] = {nullptr};
 
-enum : int {
-  BDH_NOALLOC_OK = 0,
-  BDH_NOALLOC_ERR_ARGS = 1,
-  BDH_NOALLOC_ERR_TOO_LARGE = 2,
-  BDH_NOALLOC_ERR_SETUP = 3,
-  BDH_NOALLOC_ERR_CUDA = 4,
-  BDH_NOALLOC_ERR_KERNEL_TIMEOUT = 5,
-};
-
 // Per-device set-up: resolve the device addresses of the scratch array and error word.
+// Two host threads making their first call on one device at once both resolve the same
+// addresses and store the same values, so the unsynchronized cache is benign.
 int setup_device(int dev) {
   if (g_scratch_ptr[dev] != nullptr) return BDH_NOALLOC_OK;
   void* s = nullptr;
@@ -160,14 +154,23 @@ const char* bdh_noalloc_error_string(int code) {
 // Bytes of built-in scratch available to bdh_decoder_merge_noalloc.
 size_t bdh_noalloc_scratch_bytes(void) { return kScratchBytes; }
 
+// Device address of the current device's error word, for callers that pass check == 0.
+int* bdh_noalloc_error_word(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (setup_device(dev) != BDH_NOALLOC_OK) return nullptr;
+  return g_err_ptr[dev];
+}
+
 // v_out = LN(v + LN(yn @ dec)) with one shared LayerNorm (gamma, beta, eps).
 //   yn    [M, N]  bf16, row-major      dec   [N, D] bf16, row-major
 //   v     [M, D]  fp32                 gamma, beta [D] fp32
 //   v_out [M, D]  fp32                 v_out_bf16 [M, D] bf16 or NULL
 // `splits` divides the K = N reduction across CTAs (1..N/64); the partial products live
-// in the built-in scratch. Enqueued on `stream`; returns 0 or a code of
-// bdh_noalloc_error_string. The device error word is read back only when `check` != 0
-// (that read synchronizes the stream).
+// in the built-in scratch. Enqueued on `stream` (a stream of the current device); returns
+// 0 or a code of bdh_noalloc_error_string. The device error word is read back only when
+// `check` != 0 (that read synchronizes the stream); with check == 0 a GEMM timeout is
+// not reported here, and the caller reads bdh_noalloc_error_word() later instead.
 int bdh_decoder_merge_noalloc(const void* yn, const void* dec, const float* v, const float* gamma,
                               const float* beta, float* v_out, void* v_out_bf16, int M, int N, int D, int splits,
                               float eps, int check, cudaStream_t stream) {
@@ -179,8 +182,17 @@ int bdh_decoder_merge_noalloc(const void* yn, const void* dec, const float* v, c
   const int per = (KB + splits - 1) / splits;
   const int real_splits = (KB + per - 1) / per;
   if ((size_t)real_splits * (size_t)M * (size_t)D * sizeof(float) > kScratchBytes) return BDH_NOALLOC_ERR_TOO_LARGE;
+  // an error left by the caller's earlier work is not this call's: drain it first
+  (void)cudaGetLastError();
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return BDH_NOALLOC_ERR_CUDA;
+#if CUDART_VERSION >= 12080
+  if (stream != nullptr) {
+    int sdev = -1;
+    if (cudaStreamGetDevice(stream, &sdev) != cudaSuccess) return BDH_NOALLOC_ERR_CUDA;
+    if (sdev != dev) return BDH_NOALLOC_ERR_ARGS;
+  }
+#endif
   int rc = setup_device(dev);
   if (rc != BDH_NOALLOC_OK) return rc;
   float* scratch = g_scratch_ptr[dev];

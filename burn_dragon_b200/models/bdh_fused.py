@@ -30,6 +30,10 @@ from ..ops import gemm as G
 from ..ops.gemm import Operand
 from .reference import rope_freqs
 
+# The forward stores x = relu(v Dx) next to q = rope(x) (the gate and the decoder
+# backward read x); the step roofline counts its bytes.
+STORES_X = True
+
 
 def fused_unsupported(cfg) -> str | None:
     """The first model option the fused kernels do not implement, or None: they
@@ -218,7 +222,7 @@ class FusedBDH:
         for l in range(L):
             v16 = ws.v16[l]
             # x = relu(v Dx - thr), q = rope(x)       (K = D)
-            G.gemm(G.EPI_RELU_ROPE, Operand(v16, False, D, M, D), B_enc, M, Nh, D, ws.x16[l], Z1=H, bn=128,
+            G.gemm(G.EPI_RELU_ROPE, Operand(v16, False, D, M, D), B_enc, M, Nh, D, ws.x16[l], Z1=H, bn=G.tma_bn(M, Nh),
                    out1=ws.q16[l] if ws.freq is not None else None, ld=N, sz1=Nh, thr=thr, freq=ws.freq,
                    T=T, pos0=pos0, Nh=Nh)
             # S = tril_{-1}(q q^T) (* gamma^(i-j))      (K = Nh), upper tiles skipped
@@ -264,7 +268,7 @@ class FusedBDH:
                        ws.amean[l], ws.arstd[l])
             # yn = relu(an Dy - thr) * x                (K = D)
             G.gemm(G.EPI_GATE, Operand(ws.an16[l], False, D, M, H * D, z1=(H, D)), B_encv, M, Nh, D, ws.yn16[l],
-                   Z1=H, bn=128, aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr_y)
+                   Z1=H, bn=G.tma_bn(M, Nh), aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr_y)
             # m = yn E (split-K partials), v' = LN(v + LN(m))
             if peer is not None:
                 # decoder product with the reduce-scatter fused into its epilogue, then the
@@ -343,7 +347,7 @@ class FusedBDH:
             v16 = ws.v16[l]
             parts.append(mod.tail_bwd(dv, ws.v32[l], ws.m32[l], ws.tst[l], M, D, gam, bet, ws.dm16, ws.dv_res))
             # d(yn) = dm E^T -> dx_part = d(yn)*y, dy_pre = d(yn)*x*[y>0]
-            G.gemm(G.EPI_DEC_BWD, Operand(ws.dm16, False, D, M, D), Operand(dec, False, D, N, D), M, N, D, ws.dx16, bn=128,
+            G.gemm(G.EPI_DEC_BWD, Operand(ws.dm16, False, D, M, D), Operand(dec, False, D, N, D), M, N, D, ws.dx16, bn=G.tma_bn(M, N),
                    out1=ws.dy16, aux0=ws.x16[l], aux1=ws.yn16[l], ld=N)
             # dE += yn^T dm
             G.gemm(G.EPI_F32, Operand(ws.yn16[l], True, N, M, N), Operand(ws.dm16, True, D, M, D), N, D, M,
@@ -366,12 +370,12 @@ class FusedBDH:
             # dx_pre = (dx_part + rope^T(G q)) * [x > 0]   (in place over dx_part, which
             # carries the x <= 0 mask as -0.0 from the decoder backward)
             G.gemm(G.EPI_DQ, Operand(ws.G16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
-                   Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B, bn=128,
+                   Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B, bn=G.tma_bn(T, Nh),
                    aux0=ws.dx16, ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh)
             if ws.has_rho0:
                 # + rope^T(gamma^t dC rho0^T) (the carried state is detached: no grad to rho0)
                 G.gemm(G.EPI_DQ, dcop, Operand(ws.rho16[l], False, D, Nh, D, z1=(H, Nh * D), z2=(B, H * Nh * D)),
-                       T, Nh, D, ws.dx16, Z1=H, Z2=B, bn=128, aux0=ws.dx16, ld=N, sz1=Nh,
+                       T, Nh, D, ws.dx16, Z1=H, Z2=B, bn=G.tma_bn(T, Nh), aux0=ws.dx16, ld=N, sz1=Nh,
                        sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh, log2_decay=ws.log2_decay,
                        row_decay=ws.log2_decay is not None)
             # dV = sum_h S_h^T dC_h  (K = (h, i))

@@ -26,10 +26,12 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
     bf = torch.bfloat16
     r = lambda *s: (torch.randn(*s, device=dev) * 0.5).to(bf)  # noqa: E731
     freq = torch.rand(Nh, device=dev) * 0.1
+    if os.environ.get("BDH_BENCH_NOROPE"):
+        freq = None  # the epilogue without the rotation (cost split of the RoPE math)
     if case == "xproj":
         v, enc, x, q = r(M, D), r(H, D, Nh), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_RELU_ROPE, Operand(v, False, D, M, D),  # noqa: E731
-                              Operand(enc, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, x, Z1=H, bn=128, out1=q, ld=N,
+                              Operand(enc, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, x, Z1=H, bn=G.tma_bn(M, Nh), out1=q, ld=N,
                               sz1=Nh, freq=freq, T=T, Nh=Nh)
         return call, 2 * M * N * D, (M * D + D * N + 2 * M * N) * 2
     if case == "scores":
@@ -42,18 +44,18 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
     if case == "gate":
         an, encv, x, yn = r(M, H, D), r(H, D, Nh), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_GATE, Operand(an, False, D, M, H * D, z1=(H, D)),  # noqa: E731
-                              Operand(encv, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, yn, Z1=H, bn=128, aux0=x, ld=N,
+                              Operand(encv, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, yn, Z1=H, bn=G.tma_bn(M, Nh), aux0=x, ld=N,
                               sz1=Nh)
         return call, 2 * M * N * D, (M * H * D + D * N + 2 * M * N) * 2
     if case == "dec_bwd":
         dm, dec, x, yn, dx, dy = r(M, D), r(N, D), r(M, N), r(M, N), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_DEC_BWD, Operand(dm, False, D, M, D), Operand(dec, False, D, N, D),  # noqa: E731
-                              M, N, D, dx, bn=128, out1=dy, aux0=x, aux1=yn, ld=N)
+                              M, N, D, dx, bn=G.tma_bn(M, N), out1=dy, aux0=x, aux1=yn, ld=N)
         return call, 2 * M * N * D, (M * D + N * D + 4 * M * N) * 2
     if case == "dq":
         g16, q, dx = r(B, H, T, T), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_DQ, Operand(g16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),  # noqa: E731
-                              Operand(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B, bn=128,
+                              Operand(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B, bn=G.tma_bn(T, Nh),
                               aux0=dx, ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh)
         return call, 2 * B * H * T * T * Nh, (B * H * T * T + 3 * M * N) * 2
     if case == "wgrad":
@@ -69,6 +71,16 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
         call = lambda: G.gemm(G.EPI_F32, Operand(yn, False, N, M, N), Operand(dec, True, D, N, D), M, D, N,  # noqa: E731
                               part, splits=splits, ld=D, split_stride=M * D)
         return call, 2 * M * N * D, M * N * 2 + splits * M * D * 4
+    if case == "plain":
+        # square K-major GEMM with an fp32 output: tile shape / CTA-pair comparison
+        # (BDH_BENCH_BN, BDH_BENCH_PAIR); M = N = batch * 1024, K = seq * 16
+        Mp, Kp = B * 1024, T * 16
+        a, b, out = r(Mp, Kp), r(Mp, Kp), torch.empty(Mp, Mp, device=dev)
+        bn = int(os.environ.get("BDH_BENCH_BN", "256"))
+        pair = os.environ.get("BDH_BENCH_PAIR", "1") != "0"
+        call = lambda: G.gemm(G.EPI_F32, Operand(a, False, Kp, Mp, Kp), Operand(b, False, Kp, Mp, Kp),  # noqa: E731
+                              Mp, Mp, Kp, out, bn=bn, ld=Mp, pair=pair)
+        return call, 2 * Mp * Mp * Kp, (2 * Mp * Kp) * 2 + Mp * Mp * 4
     raise ValueError(case)
 
 

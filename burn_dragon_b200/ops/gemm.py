@@ -58,6 +58,19 @@ def check_errors(device: torch.device) -> None:
         raise RuntimeError(f"tcgen05 GEMM engine reported a bounded-wait timeout (code {code})")
 
 
+# Tile N of the TMA-epilogue modes (x-projection, gate, decoder backward, dQ): 256 runs
+# them on CTA pairs with 256 x 256 tiles where M >= 256 (BDH_TMA_BN=128 selects the
+# 1-CTA 128 x 128 kernel).
+TMA_BN = int(os.environ.get("BDH_TMA_BN", "256"))
+
+
+def tma_bn(M: int, N: int) -> int:
+    """Tile N for a TMA-epilogue GEMM of M x N outputs (per batch matrix)."""
+    if TMA_BN == 256 and PAIR and M >= 256 and N % 256 == 0:
+        return 256
+    return 128
+
+
 def pick_bn(n: int) -> int:
     for bn in (256, 128, 64):
         if n % bn == 0:

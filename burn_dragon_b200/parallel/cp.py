@@ -1,6 +1,6 @@
 """Context parallelism over the sequence by an exact prefix of the recurrent state.
 
-The reference scales context only through the recurrent state and TBPTT (SURVEY: no
+The reference scales context only through the recurrent state and TBPTT (it has no
 ring attention); linearity of the state makes an exact split possible: rank r holds
 tokens [r*Tc, (r+1)*Tc). Per layer each rank computes its chunk's attention from a zero
 state plus its chunk state ``rho_r = sum_t gamma^(Tc-t) q_t v_t``; the states are

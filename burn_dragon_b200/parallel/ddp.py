@@ -1,15 +1,30 @@
-"""Data parallelism: the NVLink peer-memory gradient step and the NCCL baseline.
+"""Data parallelism: the NVLink peer-memory optimizer step and the NCCL baseline.
 
-``NVLinkDDP`` puts the model's flat parameter / gradient / bf16-shadow buffers in
-symmetric device memory shared through CUDA IPC, then runs each optimizer step as
-barrier -> fused reduce-scatter + AdamW-on-own-shard + all-gather-by-stores -> barrier
-(``csrc/comm.cu``). Every rank keeps the full fp32 master and bf16 shadow (the next
-forward needs them) but only its shard of the AdamW moments, so optimizer-state memory
-and optimizer math are divided by the world size (a partitioned optimizer, the
-reference's intended ZeRO-style mode: burn_dragon_train/src/config/core.rs:87-94).
+``NVLinkDDP`` shares, through CUDA IPC, one symmetric region per rank holding the bf16
+gradient buffer (or fp32 with ``grad_dtype="fp32"``), the bf16 weight shadow the GEMMs
+read, and a page of flags. Each optimizer step is
+
+    cast fp32 grads -> bf16 (local) -> barrier -> ddp_step -> barrier
+
+where ``ddp_step`` (``csrc/comm.cu``) is one kernel: rank r sums its slice [lo_r, hi_r)
+of every peer's gradient with plain P2P loads (a reduce-scatter, fp32 accumulation),
+runs AdamW on its fp32 master slice and moment shard, and stores the new bf16 weights
+into every peer's shadow (an all-gather by P2P stores). A rank keeps the fp32 master
+current only on its own slice (ZeRO-1 style: optimizer state and master updates are
+partitioned, the reference's intended FSDP mode, burn_dragon_train/src/config/core.rs:
+87-94); ``sync_master()`` all-gathers the full fp32 master when a caller needs it
+(checkpoints, the PyTorch path, evaluation in fp32).
+
+Global-norm clipping: the peer sum runs first into a local fp32 shard while summing its
+squares, the ranks exchange those sums over the flag page (``ddp_norm_exchange``), and
+the update applies the common clip coefficient (``ddp_apply``).
+
+Bytes over NVLink per rank and step: (W-1)/W * P * 2 in and out (P parameters, bf16),
+against (W-1)/W * P * 4 in and * 6 out for an fp32-gradient, fp32-master step.
 
 The NCCL path (``Trainer.allreduce_grads`` without a communicator) mirrors the reference's
-process-group DDP: gradient mean over ranks, then a full AdamW on every rank.
+process-group DDP: gradient mean over ranks, then a full AdamW on every rank
+(burn_dragon_language/src/train/schedule.rs:10348-10457).
 """
 
 from __future__ import annotations
@@ -25,9 +40,11 @@ class NVLinkDDP:
 
     FLAG_WORDS = 64
 
-    def __init__(self, numel: int, device: torch.device, group=None):
+    def __init__(self, numel: int, device: torch.device, group=None, grad_dtype: str = "bf16"):
         if not dist.is_initialized():
             raise RuntimeError("NVLinkDDP needs an initialised process group")
+        if grad_dtype not in ("bf16", "fp32"):
+            raise ValueError("grad_dtype must be 'bf16' or 'fp32'")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -35,13 +52,15 @@ class NVLinkDDP:
             raise ValueError("NVLinkDDP supports up to 8 ranks on one NVSwitch node")
         self.device = device
         self.dev = device.index if device.index is not None else torch.cuda.current_device()
+        self.grad_bf16 = grad_dtype == "bf16"
         mod = _ext.load()
-        unit = 4 * self.world
+        unit = 8 * self.world
         self.numel = -(-numel // unit) * unit
         self.shard = self.numel // self.world
         self.lo = self.rank * self.shard
         self.hi = self.lo + self.shard
-        sizes = {"grad": self.numel * 4, "param": self.numel * 4, "shadow": self.numel * 2, "flags": self.FLAG_WORDS * 4}
+        gbytes = self.numel * (2 if self.grad_bf16 else 4)
+        sizes = {"gsym": gbytes, "shadow": self.numel * 2, "flags": self.FLAG_WORDS * 4}
         self._own = {k: mod.sym_alloc(b, self.dev) for k, b in sizes.items()}
         handles = {k: mod.ipc_handle(p, self.dev) for k, p in self._own.items()}
         gathered: list = [None] * self.world
@@ -56,40 +75,76 @@ class NVLinkDDP:
                     p = mod.ipc_open(gathered[r][k], self.dev)
                     self._opened.append(p)
                     self.ptrs[k].append(p)
-        self.grad = mod.wrap_ptr(self._own["grad"], self.numel, 0, self.dev)
-        self.param = mod.wrap_ptr(self._own["param"], self.numel, 0, self.dev)
+        # local fp32 gradient (written by the backward) and fp32 master (current on [lo, hi))
+        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
+        self.param = torch.zeros(self.numel, dtype=torch.float32, device=device)
         self.shadow = mod.wrap_ptr(self._own["shadow"], self.numel, 1, self.dev)
+        self.gsym = mod.wrap_ptr(self._own["gsym"], self.numel, 1 if self.grad_bf16 else 0, self.dev)
         self.m = torch.zeros(self.shard, dtype=torch.float32, device=device)
         self.v = torch.zeros(self.shard, dtype=torch.float32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self._gred = None
+        self._sumsq = torch.zeros(1, dtype=torch.float32, device=device)
+        self.norm_out = torch.zeros(2, dtype=torch.float32, device=device)  # {clip coef, grad norm}
+        self.master_synced = True
         dist.barrier(group=group)
 
-    def _args(self):
-        return self.ptrs["grad"], self.ptrs["param"], self.ptrs["shadow"], self.ptrs["flags"]
+    def _barrier_args(self):
+        f = self.ptrs["flags"]
+        return f, f, f, f
 
     def barrier(self, phase: int) -> None:
-        _ext.load().peer_barrier(*self._args(), self.rank, phase, self.err)
+        _ext.load().peer_barrier(*self._barrier_args(), self.rank, phase, self.err)
+
+    def _stage_grads(self) -> None:
+        if self.grad_bf16:
+            _ext.load().cast_bf16(self.grad, self.gsym)
+        else:
+            self.gsym.copy_(self.grad)
 
     def step_adamw(self, opt) -> None:
-        """Reduce-scatter + AdamW on this rank's shard + all-gather of the new weights.
-        ``opt`` supplies the hyper-parameters and the device-resident {lr, bc1, bc2}."""
+        """Reduce-scatter + AdamW on this rank's shard + all-gather of the new bf16 weights.
+        ``opt`` supplies the hyper-parameters, the device-resident {lr, bc1, bc2} and the
+        global-norm clip (``opt.clip``)."""
         mod = _ext.load()
+        self._stage_grads()
         self.barrier(0)
-        mod.reduce_adamw(*self._args(), self.rank, self.lo, self.hi, self.m, self.v, 0.0, opt.b1, opt.b2, opt.eps,
-                         opt.wd, 1.0, 1.0, opt._hyper)
+        g, sh = self.ptrs["gsym"], self.ptrs["shadow"]
+        if opt.clip is None:
+            mod.ddp_step(g, sh, self.grad_bf16, self.rank, self.lo, self.hi, self.param, self.m, self.v, opt.b1,
+                         opt.b2, opt.eps, opt.wd, opt._hyper, None)
+        else:
+            if self._gred is None:
+                self._gred = torch.empty(self.shard, dtype=torch.float32, device=self.device)
+            mod.ddp_reduce(g, sh, self.grad_bf16, self.rank, self.lo, self.hi, self._gred, self._sumsq)
+            mod.ddp_norm_exchange(self.ptrs["flags"], self.rank, self._sumsq, float(opt.clip), self.norm_out, self.err)
+            mod.ddp_apply(g, sh, self.rank, self.lo, self.hi, self._gred, self.param, self.m, self.v, opt.b1, opt.b2,
+                          opt.eps, opt.wd, opt._hyper, self.norm_out)
+            opt._scratch[1:2].copy_(self.norm_out[1:2])
         self.barrier(1)
+        self.master_synced = False
 
-    def allreduce_mean(self, grad: torch.Tensor | None = None) -> None:
-        """Gradient mean in place over the symmetric gradient buffer (no optimizer)."""
-        mod = _ext.load()
-        self.barrier(0)
-        mod.reduce_mean(self.ptrs["grad"], self.ptrs["flags"], self.rank, self.lo, self.hi, self.err)
-        self.barrier(1)
+    def sync_master(self) -> None:
+        """All-gather the fp32 master slices so every rank holds the full current master."""
+        if self.master_synced:
+            return
+        if self.world > 1:
+            shards = list(self.param.split(self.shard))
+            mine = shards[self.rank].clone()
+            dist.all_gather(shards, mine, group=self.group)
+        self.master_synced = True
+
+    def allreduce_mean(self) -> None:
+        """Gradient mean in place over the local fp32 gradient (NCCL; no optimizer)."""
+        op = dist.ReduceOp.AVG if dist.get_backend(self.group) == "nccl" else dist.ReduceOp.SUM
+        dist.all_reduce(self.grad, op=op, group=self.group)
+        if op == dist.ReduceOp.SUM:
+            self.grad.div_(self.world)
 
     def check(self) -> None:
         code = int(self.err.item())
         if code:
-            raise RuntimeError(f"NVLinkDDP: a peer barrier timed out (code {code})")
+            raise RuntimeError(f"NVLinkDDP: a peer wait timed out (code {code})")
 
     def state_dict(self) -> dict:
         return {"m": self.m, "v": self.v, "lo": self.lo, "hi": self.hi}

@@ -99,17 +99,17 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     o = cfg.optimizer
     comm = None
     if mode in ("ddp", "fsdp") and world > 1 and dev.type == "cuda" and o.name != "eggroll":
-        comm = "nvlink" if o.grad_clip_norm is None and o.grad_clip_value is None else "nccl"
+        # the NVLink step implements global-norm clipping; element-wise value clipping of the
+        # mean gradient runs on the NCCL path
+        comm = "nvlink" if o.grad_clip_value is None else "nccl"
     micro = int(cfg.parallel.tensor.get("micro_batches", t.gradient_accumulation_steps))
     tp_arg: bool | int = mode == "tensor_parallel_neuron"
     if mode == "hybrid_2d":
         tp_arg = int(cfg.parallel.tensor.get("size", 8))
-        plain = o.grad_clip_norm is None and o.grad_clip_value is None
-        comm = "nvlink" if plain and dev.type == "cuda" else None
-    if cfg.parallel.tensor.get("sequence_parallel"):
-        # the residual stream is replicated across the tensor-parallel group; the sum is an
-        # all-reduce of [M, D] per layer (a reduce-scatter + all-gather moves the same bytes)
-        pass
+        comm = "nvlink" if o.grad_clip_value is None and dev.type == "cuda" else None
+    if cfg.parallel.tensor.get("sequence_parallel") and not tp_arg:
+        raise ValueError("parallel.tensor.sequence_parallel needs a tensor-parallel mode "
+                         "(tensor_parallel_neuron or hybrid_2d)")
     if cfg.dataset.type in ("jsonl", "parquet", "text"):
         from .datasets import prepare_corpus
 
@@ -539,6 +539,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                 last_loss = lv
             if validate_here and t.validation_interval_iters and (step + 1) % t.validation_interval_iters == 0 \
                     and runner is None:
+                if hasattr(trainer, "sync_params"):
+                    trainer.sync_params()  # the PyTorch path reads the full fp32 master
                 if probe is not None:
                     from .state_probe import stream_warm_validation
 
@@ -566,6 +568,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                             run.write_json("neuron_scaling.json", {
                                 "mlp_internal_dim_multiplier": trainer.model.cfg.mlp_internal_dim_multiplier,
                                 "events": scaler.events, "step": step + 1})
+            if t.checkpoint_interval_iters and (step + 1) % t.checkpoint_interval_iters == 0 \
+                    and hasattr(trainer, "sync_params"):
+                trainer.sync_params()  # every rank: gathers sharded master / moments
             if t.checkpoint_interval_iters and (step + 1) % t.checkpoint_interval_iters == 0 and rank == 0:
                 rt = None
                 if state is not None and not extended and state.rhos is not None:
@@ -574,6 +579,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                     rt = {"position": state.position, "state_tensors": state.to_tensors()}
                 run.save(step + 1, trainer.core if extended else trainer.model, trainer.opt, {"step": step + 1}, rt,
                          extra=trainer.extra_state() if extended else None, teacher=_teacher())
+        if t.checkpoint_interval_iters and hasattr(trainer, "sync_params"):
+            trainer.sync_params()
         if rank == 0 and t.checkpoint_interval_iters:
             run.save(t.max_iters, trainer.core if extended else trainer.model, trainer.opt, {"step": t.max_iters},
                      extra=trainer.extra_state() if extended else None, teacher=_teacher())

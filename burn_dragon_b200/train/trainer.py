@@ -105,13 +105,28 @@ class Trainer:
         if comm == "nvlink" and self.world > 1:
             from ..parallel.ddp import NVLinkDDP
 
-            if grad_clip_norm is not None:
-                raise ValueError("the NVLink DDP step does not implement global-norm clipping; use comm='nccl'")
-            self.comm = NVLinkDDP(self.model.store.numel, self.device, group=self.dp_group)
+            if grad_clip_value is not None:
+                raise ValueError("the NVLink DDP step clips by global norm only; use comm='nccl' for "
+                                 "element-wise value clipping")
+            self.comm = NVLinkDDP(self.model.store.numel, self.device, group=self.dp_group,
+                                  grad_dtype=os.environ.get("BDH_DDP_GRAD_DTYPE", "bf16"))
             self.model.attach_buffers(self.comm.param, self.comm.grad, self.comm.shadow)
         self._graph = None
         self._graph_shape = None
         self._graph_launches = 0
+
+    def sync_params(self) -> None:
+        """Make the full fp32 master and the optimizer moments current on every rank (the
+        NVLink step keeps them sharded). A collective: every data-parallel rank calls it."""
+        if self.comm is None:
+            return
+        self.comm.sync_master()
+        if self.world > 1:
+            n = self.comm.numel
+            for full, shard in ((self.opt.m, self.comm.m), (self.opt.v, self.comm.v)):
+                buf = torch.empty(n, dtype=torch.float32, device=self.device)
+                dist.all_gather(list(buf.split(self.comm.shard)), shard.contiguous(), group=self.dp_group)
+                full.copy_(buf[:full.numel()])
 
     def enable_cuda_graph(self, tokens: torch.Tensor, targets: torch.Tensor, warmup: int = 2) -> None:
         """Capture forward + backward + all-reduce + AdamW of one step into a CUDA graph.

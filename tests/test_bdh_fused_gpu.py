@@ -101,3 +101,41 @@ def test_fused_stateful_chunks_match_reference(rotary):
         assert r < 0.08, f"{n}: rel err {r:.3e}"
     for r_ref, r_got in zip(rhos2, st.rhos):
         assert _rel(r_got, r_ref.detach()) < 0.03
+
+
+def test_fused_step_at_bench_shape_default_init():
+    """The BDH-GPU layer shape the benchmark runs (d=256, h=4, Nh=8192, T=512; B=2, L=2)
+    with the default initialisation (heavy-tailed neuron gains), against the fp32
+    PyTorch oracle on the same bf16-rounded weights. Exercises K = 8192 reductions, the
+    CTA-pair kernels and the 256 x 256 TMA-epilogue tiles."""
+    cfg = DragonConfig.bdh_gpu()
+    cfg.n_layer = 2
+    model = BDH(cfg, device="cuda", seed=11)
+    torch.manual_seed(2)
+    B, T = 2, 512
+    tokens = torch.randint(0, 256, (B, T), device="cuda")
+    targets = torch.randint(0, 256, (B, T), device="cuda")
+    ref_params = {}
+    for n, p in model.param_dict().items():
+        if p is None:
+            ref_params[n] = None
+            continue
+        q = p.detach().clone()
+        if n in ("encoder", "encoder_v", "decoder", "lm_head"):
+            q = q.bfloat16().float()
+        ref_params[n] = q.requires_grad_(True)
+    logits, _ = R.bdh_forward(tokens, ref_params, cfg)
+    ref_loss = R.cross_entropy(logits, targets)
+    ref_loss.backward()
+    loss = model.fused_step(tokens, targets)
+    torch.cuda.synchronize()
+    from burn_dragon_b200.ops.gemm import check_errors
+
+    check_errors(torch.device("cuda"))
+    assert abs(loss.item() - ref_loss.item()) < 1e-2 * abs(ref_loss.item())
+    grads = model.grad_dict()
+    errs = {n: _rel(grads[n], ref_params[n].grad) for n in
+            ("lm_head", "decoder", "encoder_v", "encoder", "embed", "norm_gamma", "norm_beta")}
+    print("bench-shape relative gradient errors:", {k: f"{v:.3e}" for k, v in errs.items()})
+    for n, r in errs.items():
+        assert r < 0.08, f"{n}: rel err {r:.3e}"

@@ -1,4 +1,4 @@
-"""Config loading and the CPU training CLI on BASELINE config 1 (tiny BDH, 20 steps)."""
+"""Config loading and the CPU training CLI on the tiny BDH config (d64 n2048 h4 L2, 8 x 128, 20 steps)."""
 import json
 import os
 

@@ -114,3 +114,63 @@ def test_cta_pair_causal_scores():
         outs.append(S)
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1])
+
+
+def _tma_case(case, B=2, T=256, D=64, H=2, Nh=512, seed=0):
+    """Operands of one TMA-epilogue BDH contraction (the layouts of the fused step) and a
+    call that runs it with a given tile N; returns (call, outputs)."""
+    G = _ops()
+    Op = G.Operand
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    r = lambda *s: (torch.randn(*s, device="cuda", generator=g) * 0.5).bfloat16()  # noqa: E731
+    N, M = H * Nh, B * T
+    freq = torch.rand(Nh, device="cuda", generator=g) * 0.1
+    if case == "xproj":
+        v, enc = r(M, D), r(H, D, Nh)
+        outs = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+        call = lambda bn: G.gemm(G.EPI_RELU_ROPE, Op(v, False, D, M, D), Op(enc, True, Nh, D, Nh, z1=(H, D * Nh)),  # noqa: E731
+                                 M, Nh, D, outs[0], Z1=H, bn=bn, out1=outs[1], ld=N, sz1=Nh, thr=0.1, freq=freq, T=T,
+                                 Nh=Nh)
+    elif case == "gate":
+        an, encv, x = r(M, H, D), r(H, D, Nh), torch.relu(r(M, N).float()).bfloat16()
+        outs = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16)]
+        call = lambda bn: G.gemm(G.EPI_GATE, Op(an, False, D, M, H * D, z1=(H, D)),  # noqa: E731
+                                 Op(encv, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, outs[0], Z1=H, bn=bn, aux0=x,
+                                 ld=N, sz1=Nh, thr=0.05)
+    elif case == "dec_bwd":
+        dm, dec = r(M, D), r(N, D)
+        x = torch.relu(r(M, N).float()).bfloat16()
+        yn = (torch.relu(r(M, N).float()) * x.float()).bfloat16()
+        outs = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+        call = lambda bn: G.gemm(G.EPI_DEC_BWD, Op(dm, False, D, M, D), Op(dec, False, D, N, D), M, N, D,  # noqa: E731
+                                 outs[0], bn=bn, out1=outs[1], aux0=x, aux1=yn, ld=N)
+    else:  # dq: dx_part carries the x <= 0 mask as -0.0
+        g16, q = r(B, H, T, T), r(M, N)
+        dx0 = r(M, N)
+        dx0 = torch.where(torch.rand(M, N, device="cuda", generator=g) < 0.3, torch.full_like(dx0, -0.0), dx0)
+        outs = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16)]
+
+        def call(bn):
+            outs[0].copy_(dx0)
+            G.gemm(G.EPI_DQ, Op(g16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
+                   Op(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, outs[0], Z1=H, Z2=B, bn=bn,
+                   aux0=outs[0], ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh)
+    return call, outs
+
+
+@pytest.mark.parametrize("case", ["xproj", "gate", "dec_bwd", "dq"])
+def test_tma_epilogue_pair256_matches_single_cta128(case):
+    """The CTA-pair 256 x 256 TMA-epilogue kernel (two 64-column chunks per epilogue warp)
+    against the 1-CTA 128 x 128 kernel on the same operands: same per-element math, so
+    the outputs agree to the bf16 rounding of the accumulator."""
+    G = _ops()
+    call, outs = _tma_case(case)
+    call(128)
+    ref = [o.float().clone() for o in outs]
+    call(256)
+    torch.cuda.synchronize()
+    G.check_errors(torch.device("cuda"))
+    for got, r in zip(outs, ref):
+        _close(got, r, tol=1e-2)
+        # the masked (-0.0) / zero pattern is identical
+        assert torch.equal(got == 0, r == 0)
