@@ -7,22 +7,26 @@ Run layout (burn_dragon_language/src/checkpoint.rs:27-85,712-735; run_dirs.rs:37
         training_config.json            the resolved training configuration
         tokenizer.json                  byte tokenizer description
         random_scaffold_manifest.json   (random-scaffold runs only)
-        checkpoint/model-<step>.bin     parameters
-        checkpoint/optim-<step>.bin     optimizer moments + step
-        checkpoint/scheduler-<step>.bin learning-rate schedule position
-        checkpoint/runtime-state-<step>.bin  streaming rho state, position, ...
+        checkpoint/model-<step>.bpk     parameters
+        checkpoint/optim-<step>.bpk     optimizer moments + step
+        checkpoint/scheduler-<step>.bin learning-rate schedule position (JSON)
+        checkpoint/runtime-state-<step>.bpk  streaming rho state, position, ...
         latest                          name of the newest checkpoint step
 
 The root comes from ``BURN_DRAGON_RUN_ROOT`` (default ``runs``); ``BURN_DRAGON_RUN_DIR``
 overrides the whole path and ``BURN_DRAGON_RUN_NAME`` the run name.
 
-Tensor payloads use the safetensors container (8-byte little-endian header length, a
-JSON header of ``{name: {dtype, shape, data_offsets}}`` plus ``__metadata__``, then the
-raw little-endian data), implemented here. Record names mirror the reference's Burn
-record paths (``encoder``, ``embed.weight``, ``norm.gamma``, ...). Large files can be
-split into parts with a manifest (burn_dragon_checkpoint/src/parts.rs) and exported at
-reduced precision (f16 / bf16; burn_dragon_checkpoint/src/precision.rs). Retention keeps
-the newest two checkpoints plus the best-validation one (schedule.rs:25,848-900).
+Tensor records are burnpack files (``train/burnpack.py``: the reference's container,
+magic 0x4255524E, CBOR metadata, 256-byte aligned payloads), so a model record loads in
+the reference's burnpack loaders and the reverse. The reference's own training
+checkpoints are Burn ``BinFileRecorder`` records (``.bin``); those are not read here.
+Records written by earlier versions of this package (``.bin`` in the safetensors
+container: 8-byte little-endian header length, a JSON header, raw data) still load:
+``load_tensors`` tells the two apart by the burnpack magic. Record names mirror the
+reference's Burn record paths (``encoder``, ``embed.weight``, ``norm.gamma``, ...). Large
+files split into burnpack parts with a SHA-256 manifest (burn_dragon_checkpoint/src/
+parts.rs) and export at f16 (precision.rs). Retention keeps the newest two checkpoints
+plus the best-validation one (schedule.rs:25,848-900).
 """
 
 from __future__ import annotations
@@ -37,7 +41,10 @@ from dataclasses import asdict, is_dataclass
 
 import torch
 
+from . import burnpack as BP
+
 SCHEMA_VERSION = 4  # burn_dragon_core/src/lib.rs:7
+RECORD_EXT = ".bpk"
 
 _DT = {
     torch.float32: "F32", torch.float16: "F16", torch.bfloat16: "BF16", torch.int64: "I64",
@@ -48,6 +55,11 @@ _DT_INV = {v: k for k, v in _DT.items()}
 
 # ------------------------------------------------------------------ tensor files
 def save_tensors(path: str, tensors: dict[str, torch.Tensor], metadata: dict | None = None) -> None:
+    """A ``.bpk`` path gets a burnpack file (metadata values JSON-encoded as text), any
+    other path the safetensors container."""
+    if path.endswith(".bpk"):
+        BP.save_burnpack(path, tensors, {k: json.dumps(v) for k, v in (metadata or {}).items()})
+        return
     header: dict = {}
     blobs = []
     off = 0
@@ -70,7 +82,24 @@ def save_tensors(path: str, tensors: dict[str, torch.Tensor], metadata: dict | N
     os.replace(tmp, path)
 
 
+def _is_burnpack(path: str) -> bool:
+    with open(path, "rb") as f:
+        head = f.read(4)
+    return len(head) == 4 and struct.unpack("<I", head)[0] == BP.MAGIC
+
+
+def _meta_value(v: str):
+    try:
+        return json.loads(v)
+    except (TypeError, ValueError):
+        return v
+
+
 def load_tensors(path: str, device=None) -> tuple[dict[str, torch.Tensor], dict]:
+    """Tensors and metadata of a burnpack or safetensors record (told apart by the magic)."""
+    if _is_burnpack(path):
+        t, meta = BP.load_burnpack(path, device)
+        return t, {k: _meta_value(v) for k, v in meta.items()}
     with open(path, "rb") as f:
         n = struct.unpack("<Q", f.read(8))[0]
         header = json.loads(f.read(n))
@@ -92,9 +121,58 @@ def convert_precision(tensors: dict[str, torch.Tensor], dtype: torch.dtype) -> d
     return {k: (v.to(dtype) if v.is_floating_point() else v) for k, v in tensors.items()}
 
 
+def export_burnpack(model, path: str, f16: bool = False, part_mib: int | None = None,
+                    metadata: dict | None = None) -> str:
+    """Write the model's parameters under their record names as a burnpack deployment file
+    (``<stem>.bpk``, or ``<stem>_f16.bpk`` with ``f16``), optionally split into parts of
+    ``part_mib`` MiB with a ``.parts.json`` manifest. Returns the file path."""
+    from ..models.bdh import record_name
+
+    out = BP.precision_path(path, f16)
+    tensors = {record_name(n): t.detach() for n, t in model.store.views(model.store.data).items()}
+    if f16:
+        tensors = {k: v.half() for k, v in tensors.items()}
+    meta = {"schema_version": str(SCHEMA_VERSION), "producer": "burn_dragon_b200"}
+    if f16:
+        meta["precision"] = "f16"
+    meta.update({k: str(v) for k, v in (metadata or {}).items()})
+    BP.save_burnpack(out, tensors, meta)
+    if part_mib:
+        BP.write_parts(out, part_mib)
+    return out
+
+
+def load_model_burnpack(model, path: str, prefer_f16: bool = False) -> str:
+    """Load a burnpack deployment file (or its parts manifest, or the preferred precision
+    variant that exists) into the model's parameters; returns the file that was read."""
+    from ..models.bdh import record_name
+
+    cands = [path] if path.endswith(".parts.json") else BP.candidate_paths(path, prefer_f16)
+    for c in cands:
+        man = c if c.endswith(".parts.json") else BP.parts_manifest_path(c)
+        if os.path.isfile(c) or os.path.isfile(man):
+            tensors = BP.load_parts(man)[0] if os.path.isfile(man) and not os.path.isfile(c) else \
+                (BP.load_parts(man)[0] if c.endswith(".parts.json") else BP.load_burnpack(c)[0])
+            views = model.store.views(model.store.data)
+            with torch.no_grad():
+                for n, v in views.items():
+                    src = tensors[record_name(n)]
+                    if tuple(src.shape) != tuple(v.shape):
+                        raise ValueError(f"{record_name(n)}: shape {tuple(src.shape)} != {tuple(v.shape)}")
+                    v.copy_(src.to(v.device, v.dtype))
+            model.store.refresh_shadow()
+            return c
+    raise FileNotFoundError(f"no burnpack at {path} (tried {cands})")
+
+
 def save_parts(path: str, tensors: dict[str, torch.Tensor], max_part_bytes: int, metadata=None) -> dict:
-    """Split a record over ``<path>.part-<i>`` files of at most ``max_part_bytes`` each
-    (a tensor larger than the limit gets a part of its own) plus ``<path>.parts.json``."""
+    """A ``.bpk`` path: one burnpack file split into burnpack parts of at most
+    ``max_part_bytes`` (rounded up to whole MiB) with the SHA-256 manifest
+    ``<path>.parts.json``. Any other path: safetensors parts ``<path>.part-<i>`` with a
+    name list in ``<path>.parts.json`` (the earlier container)."""
+    if path.endswith(".bpk"):
+        save_tensors(path, tensors, metadata)
+        return BP.write_parts(path, max(1, -(-max_part_bytes // (1 << 20))))
     parts: list[list[str]] = [[]]
     size = 0
     for name in sorted(tensors):
@@ -115,6 +193,8 @@ def save_parts(path: str, tensors: dict[str, torch.Tensor], max_part_bytes: int,
 
 
 def load_parts(path: str, device=None) -> dict[str, torch.Tensor]:
+    if path.endswith(".bpk"):
+        return BP.load_parts(BP.parts_manifest_path(path), device)[0]
     with open(path + ".parts.json") as f:
         manifest = json.load(f)
     out: dict[str, torch.Tensor] = {}
@@ -275,8 +355,16 @@ class RunDir:
             self.write_json("tokenizer.json", {"type": "byte", "vocab_size": train_cfg.model.vocab_size})
 
     # ---- checkpoints
-    def _p(self, kind: str, step: int) -> str:
-        return os.path.join(self.ckpt, f"{kind}-{step}.bin")
+    def _p(self, kind: str, step: int, write: bool = False) -> str:
+        """Record path: ``.bpk`` (burnpack); for reading, an earlier ``.bin`` record when
+        no ``.bpk`` exists. The scheduler record is JSON in ``.bin``."""
+        if kind == "scheduler":
+            return os.path.join(self.ckpt, f"{kind}-{step}.bin")
+        new = os.path.join(self.ckpt, f"{kind}-{step}{RECORD_EXT}")
+        if write or os.path.exists(new):
+            return new
+        old = os.path.join(self.ckpt, f"{kind}-{step}.bin")
+        return old if os.path.exists(old) else new
 
     def save(self, step: int, model, optimizer=None, scheduler: dict | None = None, runtime: dict | None = None,
              keep_last: int = 2, best_step: int | None = None, extra: dict | None = None, teacher=None) -> None:
@@ -304,17 +392,17 @@ class RunDir:
         scheduler = dict(scheduler or {})
 
         def write():
-            save_tensors(self._p("model", step), params, {"schema_version": SCHEMA_VERSION, "step": step})
+            save_tensors(self._p("model", step, True), params, {"schema_version": SCHEMA_VERSION, "step": step})
             if optim is not None:
-                save_tensors(self._p("optim", step), *optim)
+                save_tensors(self._p("optim", step, True), *optim)
             with open(self._p("scheduler", step), "w") as f:
                 json.dump(scheduler, f)
             if rt is not None:
-                save_tensors(self._p("runtime-state", step), rt, meta)
+                save_tensors(self._p("runtime-state", step, True), rt, meta)
             if extra:
-                save_tensors(self._p("extra", step), extra, {"schema_version": SCHEMA_VERSION})
+                save_tensors(self._p("extra", step, True), extra, {"schema_version": SCHEMA_VERSION})
             if teach:
-                save_tensors(self._p("teacher-model", step), teach, {"schema_version": SCHEMA_VERSION})
+                save_tensors(self._p("teacher-model", step, True), teach, {"schema_version": SCHEMA_VERSION})
             with open(os.path.join(self.path, "latest"), "w") as f:
                 f.write(str(step))
             self._retain(keep_last, best_step)
@@ -335,10 +423,10 @@ class RunDir:
     def steps(self) -> list[int]:
         out = []
         for fn in os.listdir(self.ckpt):
-            m = re.fullmatch(r"model-(\d+)\.bin", fn)
+            m = re.fullmatch(r"model-(\d+)\.(?:bin|bpk)", fn)
             if m:
                 out.append(int(m.group(1)))
-        return sorted(out)
+        return sorted(set(out))
 
     def latest(self) -> int | None:
         p = os.path.join(self.path, "latest")
@@ -354,9 +442,10 @@ class RunDir:
             if s in keep:
                 continue
             for kind in ("model", "optim", "scheduler", "runtime-state", "extra", "teacher-model"):
-                p = self._p(kind, s)
-                if os.path.exists(p):
-                    os.remove(p)
+                for ext in (".bin", RECORD_EXT):
+                    p = os.path.join(self.ckpt, f"{kind}-{s}{ext}")
+                    if os.path.exists(p):
+                        os.remove(p)
 
     def load_teacher(self, step: int, teacher) -> bool:
         """Restore an EMA teacher saved with ``save(..., teacher=)``; False if absent."""

@@ -16,7 +16,7 @@ Sequence batching: ``random`` windows, or ``streaming`` with stateful TBPTT
 (``tbptt_chunk_size``, ``tbptt_persist_across_steps``): every step trains the next chunk
 of each stream with the linear-attention state carried (detached) from the previous
 chunk, reset at stream starts (burn_dragon_language/src/train/steps.rs:2698-2731,
-11860-11960); the state is saved in ``runtime-state-<step>.bin``.
+11860-11960); the state is saved in ``runtime-state-<step>.bpk``.
 """
 
 from __future__ import annotations

@@ -79,7 +79,7 @@ def write_experiment_manifest(cfg, run_dir: str, run_name: str, backend: str, re
     if resumed_step is not None:
         ck = os.path.join(run_dir, "checkpoint")
         for fn in sorted(os.listdir(ck)):
-            if fn.endswith(f"-{resumed_step}.bin") or fn.endswith(f"-{resumed_step}.json"):
+            if any(fn.endswith(f"-{resumed_step}{e}") for e in (".bin", ".bpk", ".json")):
                 arts.append({"file_name": fn, "bytes": os.path.getsize(os.path.join(ck, fn))})
     launch = {"unix_time_ms": int(time.time() * 1000), "command": list(sys.argv), "effective_config_sha256": _sha(cfg),
               "training_contract_sha256": contract, "launch_mode": cfg.training.launch_mode,

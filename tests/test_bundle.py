@@ -66,7 +66,7 @@ init_from = "pretrain"
     main([str(spec)])
     out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert out["stages"] == ["pretrain:completed", "finetune:completed"]
-    assert os.path.exists(tmp_path / "out" / "stages" / "00_pretrain" / "run" / "checkpoint" / "model-3.bin")
+    assert os.path.exists(tmp_path / "out" / "stages" / "00_pretrain" / "run" / "checkpoint" / "model-3.bpk")
 
 
 def test_adamw_then_eggroll_phases(tmp_path, capsys):

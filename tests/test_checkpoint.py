@@ -106,7 +106,7 @@ def test_training_with_async_checkpoints(tmp_path, monkeypatch, capsys):
     main(["--config", cfg, "--set", "training.max_iters=4", "--set", "training.checkpoint_interval_iters=2",
           "--set", "parallel.checkpoint={async_write=true}", "--run-name", "aw"])
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
-    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "model-4.bin"))
+    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "model-4.bpk"))
     assert open(os.path.join(res["run_dir"], "latest")).read().strip() == "4"
 
 
@@ -127,3 +127,100 @@ def test_runtime_state_with_auxiliary_memories_round_trips(tmp_path):
     torch.testing.assert_close(back.layers[1].summary_hidden, st.layers[1].summary_hidden)
     torch.testing.assert_close(back.layers[1].mamba["ssm"], st.layers[1].mamba["ssm"])
     assert info["runtime"]["rhos"] is None
+
+
+def _burnpack_vector(tmp_path):
+    """A burnpack file assembled byte by byte from the format's definition (header of
+    magic 0x4255524E, u16 version, u32 CBOR size; CBOR {"tensors", "metadata"}; data at
+    the next 256-byte boundary, each payload 256-aligned), independent of the writer."""
+    import struct
+
+    a = torch.arange(6, dtype=torch.float32).reshape(2, 3)
+    b = torch.tensor([1, -2], dtype=torch.int64)
+
+    def text(s):
+        raw = s.encode()
+        assert len(raw) < 24
+        return bytes([0x60 | len(raw)]) + raw
+
+    def uint(n):
+        return bytes([n]) if n < 24 else (bytes([0x18, n]) if n < 256 else bytes([0x19]) + struct.pack(">H", n))
+
+    def arr(items):
+        return bytes([0x80 | len(items)]) + b"".join(items)
+
+    def desc(dtype, shape, lo, hi):
+        return (bytes([0xA3]) + text("dtype") + text(dtype) + text("shape") + arr([uint(s) for s in shape])
+                + text("data_offsets") + arr([uint(lo), uint(hi)]))
+
+    cbor = (bytes([0xA2]) + text("tensors") + bytes([0xA2]) + text("a") + desc("F32", [2, 3], 0, 24)
+            + text("b") + desc("I64", [2], 256, 272) + text("metadata") + bytes([0xA1]) + text("k") + text("v"))
+    head = struct.pack("<IHI", 0x4255524E, 1, len(cbor))
+    start = -(-(len(head) + len(cbor)) // 256) * 256
+    data = bytearray(start + 272)
+    data[:len(head)] = head
+    data[len(head):len(head) + len(cbor)] = cbor
+    data[start:start + 24] = a.numpy().tobytes()
+    data[start + 256:start + 272] = b.numpy().tobytes()
+    p = tmp_path / "vec.bpk"
+    p.write_bytes(bytes(data))
+    return str(p), a, b
+
+
+def test_burnpack_reader_parses_a_spec_test_vector(tmp_path):
+    from burn_dragon_b200.train import burnpack as BP
+
+    p, a, b = _burnpack_vector(tmp_path)
+    t, meta = BP.load_burnpack(p)
+    assert meta == {"k": "v"}
+    assert torch.equal(t["a"], a) and torch.equal(t["b"], b)
+    # the writer lays the same tensors out identically (same offsets, same payload bytes)
+    q = str(tmp_path / "out.bpk")
+    BP.save_burnpack(q, {"a": a, "b": b}, {"k": "v"})
+    _, _, md = BP.read_header(q)
+    assert md["tensors"]["a"]["data_offsets"] == [0, 24] and md["tensors"]["b"]["data_offsets"] == [256, 272]
+    assert open(q, "rb").read() == open(p, "rb").read()
+
+
+def test_burnpack_round_trip_parts_and_f16(tmp_path):
+    from burn_dragon_b200.train import burnpack as BP
+
+    t = {f"w{i}": torch.randn(300, 512) for i in range(5)}  # 600 KiB each
+    t["ids"] = torch.arange(10)
+    t["h"] = torch.randn(7).bfloat16()
+    p = str(tmp_path / "model.bpk")
+    BP.save_burnpack(p, t, {"step": "3"})
+    back, meta = BP.load_burnpack(p)
+    assert meta == {"step": "3"} and all(torch.equal(back[k], t[k]) for k in t)
+    man = BP.write_parts(p, max_part_mib=1)
+    assert len(man["parts"]) == 5 and sum(e["tensors"] for e in man["parts"]) == len(t)
+    assert all(len(e["sha256"]) == 64 and e["path"].endswith(".bpk") for e in man["parts"])
+    back2, _ = BP.load_parts(BP.parts_manifest_path(p))
+    assert all(torch.equal(back2[k], t[k]) for k in t)
+    # a corrupted part is refused
+    part = tmp_path / man["parts"][0]["path"]
+    raw = bytearray(part.read_bytes())
+    raw[-1] ^= 0xFF
+    part.write_bytes(bytes(raw))
+    import pytest
+
+    with pytest.raises(ValueError):
+        BP.load_parts(BP.parts_manifest_path(p))
+    # f16 variant: floats converted, integers kept, precision recorded
+    h = BP.convert_precision(p, BP.precision_path(p, True), "f16")
+    assert h.endswith("model_f16.bpk")
+    th, mh = BP.load_burnpack(h)
+    assert mh["precision"] == "f16" and th["w0"].dtype == torch.float16 and th["ids"].dtype == torch.int64
+
+
+def test_model_burnpack_export_and_load(tmp_path):
+    cfg = _cfg()
+    m1, m2 = BDH(cfg, seed=1), BDH(cfg, seed=2)
+    out = C.export_burnpack(m1, str(tmp_path / "deploy"), part_mib=1)
+    assert out.endswith("deploy.bpk")
+    C.load_model_burnpack(m2, out)
+    assert torch.equal(m1.store.data, m2.store.data)
+    f16 = C.export_burnpack(m1, str(tmp_path / "deploy"), f16=True)
+    m3 = BDH(cfg, seed=3)
+    assert C.load_model_burnpack(m3, str(tmp_path / "deploy.bpk"), prefer_f16=True) == f16
+    assert torch.allclose(m3.store.data, m1.store.data, atol=1e-3)

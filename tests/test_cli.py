@@ -39,7 +39,7 @@ def test_tiny_cpu_training_run_and_resume(tmp_path, monkeypatch, capsys):
 
     # uniform random bytes: the loss stays at the entropy floor ln(256)
     assert len(losses) == 4 and all(abs(v - math.log(256)) < 0.05 for v in losses)
-    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "model-20.bin"))
+    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "model-20.bpk"))
     # resume: nothing left to do at max_iters
     main(["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.checkpoint_interval_iters=10",
           "--run-name", "tiny"])
@@ -84,7 +84,7 @@ def test_layer_loop_variants_train_checkpoint_resume(tmp_path, monkeypatch, caps
     main(args)
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res["final_loss"] is not None and res["steps"] == 4
-    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "extra-4.bin"))
+    assert os.path.exists(os.path.join(res["run_dir"], "checkpoint", "extra-4.bpk"))
     main(args[:3] + ["training.max_iters=6", "--run-name", "var"])
     res2 = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert res2["steps"] == 2

@@ -106,7 +106,7 @@ def test_experiment_manifest_records_each_launch(tmp_path, monkeypatch, capsys):
     assert man["schema_version"] == 2 and man["run_name"] == "man" and man["backend"] == "cpu"
     first, second = man["launches"]
     assert first["resume_checkpoint_epoch"] is None and second["resume_checkpoint_epoch"] == 2
-    assert any(x["file_name"] == "model-2.bin" and x["bytes"] > 0 for x in second["checkpoint_artifacts"])
+    assert any(x["file_name"] == "model-2.bpk" and x["bytes"] > 0 for x in second["checkpoint_artifacts"])
     assert second["contract_changed"]  # max_iters grew from 2 to 3
     assert len(first["effective_config_sha256"]) == 64
 

@@ -214,10 +214,10 @@ def test_anchor_teacher_is_checkpointed_and_restored(tmp_path, monkeypatch, caps
             "--set", "training.dynamics_anchor={enabled=true, weight=0.5, teacher_update_rate=0.5}"]
     main(args + ["--set", "training.max_iters=2", "--run-name", "tch"])
     run_dir = json.loads(capsys.readouterr().out.strip().splitlines()[-1])["run_dir"]
-    sd, _ = C.load_tensors(os.path.join(run_dir, "checkpoint", "teacher-model-2.bin"))
+    sd, _ = C.load_tensors(os.path.join(run_dir, "checkpoint", "teacher-model-2.bpk"))
     assert "encoder" in sd and T.isfinite(sd["encoder"]).all()
     main(args + ["--set", "training.max_iters=3", "--run-name", "tch"])  # resumes and restores the teacher
-    assert os.path.exists(os.path.join(run_dir, "checkpoint", "teacher-model-3.bin"))
+    assert os.path.exists(os.path.join(run_dir, "checkpoint", "teacher-model-3.bpk"))
     from burn_dragon_b200.config import load_training_config
     from burn_dragon_b200.models.bdh import BDH
 
