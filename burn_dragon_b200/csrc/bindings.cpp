@@ -11,7 +11,9 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           const c10::optional<at::Tensor>& aux1, int64_t ld, int64_t sz1, int64_t sz2, int64_t split_stride,
           double alpha, double thr, const c10::optional<at::Tensor>& freq,
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh, bool accumulate,
-          bool row_decay, int64_t pair, const at::Tensor& err, const c10::optional<std::vector<int64_t>>& scatter);
+          bool row_decay, int64_t pair, const at::Tensor& err, const c10::optional<std::vector<int64_t>>& scatter,
+          const c10::optional<at::Tensor>& acc_src, int64_t src_decay_T, const c10::optional<at::Tensor>& rope_tab);
+void rope_table(const at::Tensor& freq, int64_t pos0, int64_t T, const at::Tensor& out);
 void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_t rows, int64_t D,
             const at::Tensor& gamma, const at::Tensor& beta, double eps, const c10::optional<at::Tensor>& y32,
             const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd);
@@ -44,8 +46,14 @@ void rho_step(const at::Tensor& rho, const at::Tensor& q, int64_t q_row_stride, 
 void scaffold_effective(int64_t key, double stdv, int64_t dist, int64_t rows, int64_t I, int64_t O, int64_t R,
                         const c10::optional<at::Tensor>& A, const c10::optional<at::Tensor>& B,
                         const c10::optional<at::Tensor>& gain, double scale, const c10::optional<at::Tensor>& out16,
-                        const c10::optional<at::Tensor>& out32, const c10::optional<at::Tensor>& base32);
+                        const c10::optional<at::Tensor>& out32, const c10::optional<at::Tensor>& base32,
+                        const c10::optional<at::Tensor>& base_in);
 void scaffold_gain_grad(int64_t key, double stdv, int64_t dist, const at::Tensor& dW, const at::Tensor& out);
+void scaffold_adapter_grad(int64_t key, double stdv, int64_t dist, int64_t Hm, int64_t I, int64_t O, int64_t R,
+                           const at::Tensor& dW, const at::Tensor& A, const at::Tensor& B,
+                           const c10::optional<at::Tensor>& base32, double scale, const at::Tensor& dA,
+                           const at::Tensor& dB, const c10::optional<at::Tensor>& gain_out, const at::Tensor& work);
+int64_t scaffold_adapter_work(int64_t Hm, int64_t I, int64_t O, int64_t R);
 int64_t sym_alloc(int64_t bytes, int64_t device);
 void sym_free(int64_t ptr, int64_t device);
 std::vector<int64_t> ipc_handle(int64_t ptr, int64_t device);
@@ -74,12 +82,15 @@ void ddp_apply(std::vector<int64_t> grad, std::vector<int64_t> shadow, int64_t r
                double b2, double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef);
 void ddp_norm_exchange(std::vector<int64_t> flags, int64_t rank, const at::Tensor& sumsq, double max_norm,
                        const at::Tensor& out, const at::Tensor& err);
+void ddp_epoch_advance(const at::Tensor& flags_local);
+void ddp_slot_barrier(std::vector<int64_t> flags, int64_t rank, int64_t slot, const at::Tensor& err);
 void percentile_thresholds(const at::Tensor& values, double q, const at::Tensor& out);
 }  // namespace bd
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "burn_dragon_b200 sm_100a kernels (tcgen05 GEMM engine + row kernels)";
   m.def("gemm", &bd::gemm);
+  m.def("rope_table", &bd::rope_table);
   m.def("ln_fwd", &bd::ln_fwd);
   m.def("ln_bwd", &bd::ln_bwd);
   m.def("tail_fwd", &bd::tail_fwd);
@@ -93,6 +104,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rho_step", &bd::rho_step);
   m.def("scaffold_effective", &bd::scaffold_effective);
   m.def("scaffold_gain_grad", &bd::scaffold_gain_grad);
+  m.def("scaffold_adapter_grad", &bd::scaffold_adapter_grad);
+  m.def("scaffold_adapter_work", &bd::scaffold_adapter_work);
   m.def("sym_alloc", &bd::sym_alloc);
   m.def("sym_free", &bd::sym_free);
   m.def("ipc_handle", &bd::ipc_handle);
@@ -108,5 +121,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ddp_reduce", &bd::ddp_reduce);
   m.def("ddp_apply", &bd::ddp_apply);
   m.def("ddp_norm_exchange", &bd::ddp_norm_exchange);
+  m.def("ddp_epoch_advance", &bd::ddp_epoch_advance);
+  m.def("ddp_slot_barrier", &bd::ddp_slot_barrier);
   m.def("percentile_thresholds", &bd::percentile_thresholds);
 }

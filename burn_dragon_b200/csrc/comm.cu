@@ -387,25 +387,34 @@ __global__ void __launch_bounds__(256) ddp_apply_kernel(DdpPtrs pp, int rank, lo
   }
 }
 
-// Global gradient norm across the ranks: each rank publishes its shard's sum of squares
-// into every peer's flag page (value, then an epoch flag with release semantics), waits
-// (bounded) for all W values of this epoch, and writes {clip coefficient, norm} to out.
-// The epoch is the step counter the phase-0 barrier advanced.
+// Flag page of the data-parallel step (DDP_FLAG_WORDS words per rank, symmetric): slot s
+// of the per-bucket barriers uses words [8 s, 8 s + 8) (one word per source rank), the
+// norm exchange its flag words at kDdpNormFlag and values at kDdpNormVal, and
+// kDdpEpoch holds this rank's step counter (ddp_epoch_advance, once per step).
+constexpr int kDdpNormFlag = 480;
+constexpr int kDdpNormVal = 488;
+constexpr int kDdpEpoch = 500;
+constexpr int kDdpSlots = 60;
+
+// Global gradient norm across the ranks: each rank publishes its sum of squares into
+// every peer's flag page (value, then an epoch flag with release semantics), waits
+// (bounded) for all W values of this step's epoch, and writes {clip coefficient, norm}
+// to out.
 __global__ void ddp_norm_exchange_kernel(PeerPtrs pp, int rank, int world, const float* __restrict__ sumsq,
                                          float max_norm, float* __restrict__ out, int* err) {
   const int t = threadIdx.x;
   __shared__ float vals[kMaxRanks];
-  const unsigned int epoch = *(volatile unsigned int*)(pp.flags[rank] + 2 * kMaxRanks);
+  const unsigned int epoch = *(volatile unsigned int*)(pp.flags[rank] + kDdpEpoch);
   const float mine = *sumsq;
   if (t < world) {
-    pp.flags[t][4 * kMaxRanks + rank] = __float_as_uint(mine);
+    pp.flags[t][kDdpNormVal + rank] = __float_as_uint(mine);
     __threadfence_system();
-    st_release_sys(pp.flags[t] + 3 * kMaxRanks + rank, epoch);
+    st_release_sys(pp.flags[t] + kDdpNormFlag + rank, epoch);
     const unsigned long long t0 = gtimer();
     float val = 0.f;
     while (true) {
-      if (ld_acquire_sys(pp.flags[rank] + 3 * kMaxRanks + t) >= epoch) {
-        val = __uint_as_float(*(volatile unsigned int*)(pp.flags[rank] + 4 * kMaxRanks + t));
+      if (ld_acquire_sys(pp.flags[rank] + kDdpNormFlag + t) >= epoch) {
+        val = __uint_as_float(*(volatile unsigned int*)(pp.flags[rank] + kDdpNormVal + t));
         break;
       }
       if (gtimer() - t0 > kPeerWaitNs) {
@@ -423,6 +432,33 @@ __global__ void ddp_norm_exchange_kernel(PeerPtrs pp, int rank, int world, const
     out[0] = fminf(1.0f, max_norm / (norm + 1e-6f));
     out[1] = norm;
   }
+}
+
+// Advance this rank's step epoch (one thread; ordered before the step's barriers by the
+// stream, or by the event the side stream waits on).
+__global__ void ddp_epoch_advance_kernel(unsigned int* flags_local) { flags_local[kDdpEpoch] += 1; }
+
+// Barrier of slot `slot` for this step's epoch: release-store the epoch into every peer's
+// word [8 slot + rank], then wait (bounded, error code 120 + slot) until every peer has
+// stored it into ours. Orders this rank's earlier writes (its bf16 gradients) before the
+// peers' loads, and the peers' writes before ours.
+__global__ void ddp_slot_barrier_kernel(PeerPtrs pp, int rank, int world, int slot, int* err) {
+  const int t = threadIdx.x;
+  const unsigned int epoch = *(volatile unsigned int*)(pp.flags[rank] + kDdpEpoch);
+  __threadfence_system();
+  __syncwarp();
+  if (t < world) st_release_sys(pp.flags[t] + 8 * slot + rank, epoch);
+  if (t < world) {
+    const unsigned int* mine = pp.flags[rank] + 8 * slot + t;
+    const unsigned long long t0 = gtimer();
+    while (ld_acquire_sys(mine) < epoch) {
+      if (gtimer() - t0 > kPeerWaitNs) {
+        atomicCAS(err, 0, 120 + slot);
+        break;
+      }
+    }
+  }
+  __syncwarp();
 }
 
 PeerPtrs make_ptrs(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
@@ -638,6 +674,22 @@ void ddp_apply(std::vector<int64_t> grad, std::vector<int64_t> shadow, int64_t r
                                                 (float)b1, (float)b2, (float)eps, (float)wd, hyper.data_ptr<float>(),
                                                 coef.data_ptr<float>());
   });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ddp_epoch_advance(const at::Tensor& flags_local) {
+  TORCH_CHECK(flags_local.numel() > kDdpEpoch, "flag page too small");
+  auto st = at::cuda::getCurrentCUDAStream(flags_local.get_device()).stream();
+  ddp_epoch_advance_kernel<<<1, 1, 0, st>>>(reinterpret_cast<unsigned int*>(flags_local.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ddp_slot_barrier(std::vector<int64_t> flags, int64_t rank, int64_t slot, const at::Tensor& err) {
+  TORCH_CHECK(slot >= 0 && slot < kDdpSlots, "barrier slot out of range");
+  std::vector<int64_t> z(flags.size(), 0);
+  PeerPtrs pp = make_ptrs(z, z, z, flags);
+  auto st = at::cuda::getCurrentCUDAStream(err.get_device()).stream();
+  ddp_slot_barrier_kernel<<<1, 32, 0, st>>>(pp, (int)rank, (int)flags.size(), (int)slot, err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -3,7 +3,8 @@
 // For each (b, h): a[b,h,:] = rho[b,h]^T q[b,h,:]   (read BEFORE the update)
 //                  rho[b,h] <- (rho[b,h] + q[b,h,:] (x) v[b,:]) * gamma_h
 // (burn_dragon_core/src/model/sequence/linear.rs:18-60 with T = 1). The state is the
-// whole cost of a decode token: it is read and written exactly once here, in place.
+// whole cost of a decode token: it is read and written at most once here, in place, and
+// without decay only the rows whose q is nonzero are touched.
 // Grid: (row chunks of Nh, B*H); 256 threads = 64 column groups of 4 floats x 4 row
 // phases; the 4 phases reduce through smem and one atomicAdd per column lands in `a`
 // (which the caller zeroes).
@@ -44,6 +45,10 @@ __global__ void rho_step_kernel(float* __restrict__ rho, const QT* __restrict__ 
       vv = reinterpret_cast<const float4*>(v + (size_t)b * D)[c];
       for (int j = j0 + ph; j < min(j0 + kRows, Nh); j += 4) {
         const float qj = to_f(qb[j]);
+        // a latent row whose q is 0 neither changes rho (without decay) nor adds to a: its
+        // read and write are skipped (exact; q is ReLU-sparse, so many rows are 0). The
+        // branch is uniform over a warp (all its lanes share the row phase).
+        if (qj == 0.0f && g == 1.0f) continue;
         float4 r = R[(size_t)j * D4 + c];
         acc.x += qj * r.x;
         acc.y += qj * r.y;

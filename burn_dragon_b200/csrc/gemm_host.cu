@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -127,7 +128,8 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
           double alpha, double thr, const c10::optional<at::Tensor>& freq,
           const c10::optional<at::Tensor>& log2_decay, int64_t T, int64_t pos0, int64_t Nh,
           bool accumulate, bool row_decay, int64_t pair, const at::Tensor& err,
-          const c10::optional<std::vector<int64_t>>& scatter) {
+          const c10::optional<std::vector<int64_t>>& scatter, const c10::optional<at::Tensor>& acc_src,
+          int64_t src_decay_T, const c10::optional<at::Tensor>& rope_tab) {
   // pair: 0 = 1-CTA kernel, 1 = CTA-pair kernel when instantiated and M >= 256
   const Entry* hit = nullptr;
   if (pair && M >= 256) hit = find_entry((int)bn, a_mn, b_mn, (int)epi, true);
@@ -180,12 +182,33 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   e.alpha = (float)alpha;
   e.thr = (float)thr;
   e.freq = freq ? freq->data_ptr<float>() : nullptr;
+  e.rope_tab = nullptr;
+  if (rope_tab && e.freq) {
+    TORCH_CHECK(rope_tab->scalar_type() == at::kInt && rope_tab->numel() >= T * (Nh / 2) && Nh % 8 == 0,
+                "rope_tab: int32 (half2) table of T x Nh/2 phases");
+    e.rope_tab = reinterpret_cast<const uint32_t*>(rope_tab->data_ptr());
+  }
   e.log2_decay = log2_decay ? log2_decay->data_ptr<float>() : nullptr;
   e.T = (int)T;
   e.pos0 = (int)pos0;
   e.Nh = (int)Nh;
   e.accumulate = accumulate ? 1 : 0;
   e.row_decay = row_decay ? 1 : 0;
+  e.acc_src = acc_src ? acc_src->data_ptr<float>() : nullptr;
+  e.src_decay_T = (int)src_decay_T;
+  if (acc_src) {
+    TORCH_CHECK(epi == EPI_F32 && accumulate && acc_src->scalar_type() == at::kFloat && splits == 1,
+                "acc_src: fp32 source of an accumulating EPI_F32 GEMM without split-K");
+    TORCH_CHECK(acc_src->numel() == out0.numel(), "acc_src must have out0's size and layout");
+  }
+  if (src_decay_T > 0) TORCH_CHECK(e.log2_decay != nullptr && acc_src, "src_decay_T needs log2_decay and acc_src");
+  {
+    static const int probe = [] {
+      const char* v = std::getenv("BDH_GEMM_PROBE");
+      return v ? std::atoi(v) : 0;
+    }();
+    e.probe = probe;
+  }
   if (row_decay) TORCH_CHECK(e.log2_decay != nullptr, "row_decay needs log2_decay");
   if (epi == EPI_F32_SCATTER) {
     // scatter = [world, rows per owner, this rank, slot stride (elements), slot pointer per rank]
@@ -204,6 +227,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
     }
   } else if (epi == EPI_F32) {
     TORCH_CHECK(out0.scalar_type() == at::kFloat, "EPI_F32 output must be fp32");
+    if (e.out1) TORCH_CHECK(out1->scalar_type() == at::kBFloat16, "EPI_F32 out1 (the copy) must be bf16");
   } else {
     TORCH_CHECK(out0.scalar_type() == at::kBFloat16, "bf16 epilogue output must be bf16");
   }
@@ -214,7 +238,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   if (epi == EPI_RELU_ROPE || epi == EPI_GATE || epi == EPI_DEC_BWD || epi == EPI_DQ) {
     TORCH_CHECK(bn == 128 || bn == 256, "TMA-epilogue modes use tile N = 128 or 256");
     TORCH_CHECK(!causal_skip, "TMA-epilogue modes have no zero tiles");
-    // columns per epilogue warp: 32 for the 16-warp x-projection epilogue, else 64
+    // columns per epilogue chunk: 32 for the 16-warp x-projection epilogue, else 64
     const uint32_t cw = epi == EPI_RELU_ROPE ? 32 : 64;
     p.to0 = encode_out_map(e.out0, N, M, ld, Z1, sz1, Z2, sz2, cw);
     if (e.out1) p.to1 = encode_out_map(e.out1, N, M, ld, Z1, sz1, Z2, sz2, cw);
@@ -222,6 +246,32 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
     if (e.aux1) p.tx1 = encode_out_map(e.aux1, N, M, ld, Z1, sz1, Z2, sz2, cw);
   }
   hit->fn(p, at::cuda::getCurrentCUDAStream(dev).stream(), dev);
+}
+
+namespace {
+// (cos, sin) of the RoPE phase 2*pi*frac(pos * freq[2j]) as half2, pos = pos0 + t.
+__global__ void rope_table_kernel(const float* __restrict__ freq, int pos0, int T, int half_nh,
+                                  uint32_t* __restrict__ out) {
+  const long long n = (long long)T * half_nh;
+  for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(k / half_nh), j = (int)(k % half_nh);
+    float c, s;
+    rope_cs((float)(pos0 + t), freq[2 * j], c, s);
+    const __half2 h = __floats2half2_rn(c, s);
+    out[k] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+}  // namespace
+
+// Fill the half2 RoPE table [T, Nh/2] read by the x-projection and dQ epilogues.
+void rope_table(const at::Tensor& freq, int64_t pos0, int64_t T, const at::Tensor& out) {
+  TORCH_CHECK(freq.scalar_type() == at::kFloat && out.scalar_type() == at::kInt, "fp32 freq, int32 table");
+  const int64_t half_nh = freq.numel() / 2;
+  TORCH_CHECK(out.numel() >= T * half_nh, "rope table too small");
+  c10::cuda::CUDAGuard guard(freq.get_device());
+  rope_table_kernel<<<148 * 4, 256, 0, at::cuda::getCurrentCUDAStream(freq.get_device()).stream()>>>(
+      freq.data_ptr<float>(), (int)pos0, (int)T, (int)half_nh, reinterpret_cast<uint32_t*>(out.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 }  // namespace bd

@@ -21,13 +21,15 @@
 // (burn_dragon_kernel/src/relu_lowrank.wgsl:40-82, dense_causal_attention.wgsl:53-106)
 // or Burn library matmuls (burn_dragon_core/src/model/dragon/residual_stream.rs:309-321).
 #pragma once
+#include <cuda_fp16.h>
+
 #include "sm100_ptx.cuh"
 
 namespace bd {
 
 enum EpiMode : int {
   EPI_BF16 = 0,       // out0 = alpha*acc (bf16)
-  EPI_F32 = 1,        // out0 (+)= alpha*acc (fp32); split-K partials
+  EPI_F32 = 1,        // out0 (+)= alpha*acc (fp32); split-K partials; out1: bf16 copy of out0
   EPI_RELU_ROPE = 2,  // x = relu(acc - thr) -> out0; q = rope(x, pos) -> out1
   EPI_SCORES = 3,     // strictly-causal masked (and decayed) scores -> out0 (bf16)
   EPI_GATE = 4,       // yn = relu(acc - thr) * x(aux0) -> out0 (bf16)
@@ -49,12 +51,19 @@ struct EpiParams {
   float alpha;
   float thr;
   const float* freq;       // RoPE frequency per latent column (cycles / position), or null
+  const uint32_t* rope_tab;  // or null: (cos, sin) as half2 per (row % T, column pair), row
+                             // stride Nh / 2, phases of positions pos0 + (row % T)
   const float* log2_decay; // per-z1 log2(gamma) for decayed scores, or null
   int T;                   // rows per sequence (position = pos0 + row % T)
   int pos0;
   int Nh;                  // latent per head (column -> in-head index for RoPE)
   int accumulate;          // EPI_F32: add into the existing output
   int row_decay;           // EPI_F32 / EPI_DQ: scale row r by 2^(r * log2_decay[z1])
+  const float* acc_src;    // EPI_F32 with accumulate: add this fp32 tensor (same layout as out0)
+                           // instead of out0's old contents (out0 = alpha*acc + src*src_scale)
+  int src_decay_T;         // > 0: src_scale = 2^(src_decay_T * log2_decay[z1]) (state decay)
+  int probe;               // measurement only (BDH_GEMM_PROBE): 1 = TMA-epilogue modes read the
+                           // accumulator and release it, skipping aux loads, math and stores
   // EPI_F32_SCATTER: row r belongs to rank r / scatter_rows; it is stored at
   // peer[owner] + scatter_rank * slot_stride + (r % scatter_rows) * ld + col, where
   // peer[] are the (IPC-mapped) slot buffers of every rank. Plain st.global over NVLink.
@@ -96,6 +105,11 @@ constexpr int epi_kind() {
                                                  : 1;
 }
 
+// Epilogue warps of the TMA kinds: 16 (four per TMEM lane quadrant, 32-column chunks)
+// for the x-projection, else 8 (64-column chunks). (16 warps on 256-wide tiles measured
+// slower at BDH-GPU batch 32: twice the TMA operations of half the size.)
+constexpr int tma_nepi(int KIND, int BN) { return KIND == 3 ? 16 : 8; }
+
 template <int BN, int KIND = 0>
 struct GemmCfg {
   static constexpr bool STAGED = KIND != 0;
@@ -109,7 +123,7 @@ struct GemmCfg {
                                          : ((BN == 256) ? 4 : (BN == 128 ? 6 : 8)));
   // epilogue warps: kind 3 runs 16 (four per TMEM lane quadrant, 32 columns each),
   // the others 8 (two per quadrant, 64 columns each)
-  static constexpr int NEPI = KIND == 3 ? 16 : 8;
+  static constexpr int NEPI = KIND >= 2 ? tma_nepi(KIND, BN) : 8;
   // kinds 2 / 3: warps x 2 tile buffers x 2 tensors x (32 rows x columns-per-warp bf16)
   static constexpr int EPI_BYTES = KIND == 4 ? 96 * 1024 : KIND >= 2 ? 128 * 1024 : (STAGED ? 8 * 2 * 4096 : 0);
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024;
@@ -196,14 +210,27 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const TileCo
     float* o = reinterpret_cast<float*>(e.out0) + off + (long long)tc.split * e.split_stride;
     float4* o4 = reinterpret_cast<float4*>(o);
     const float a = e.row_decay ? e.alpha * exp2f((float)row * e.log2_decay[tc.z1]) : e.alpha;
+    // out1 (optional): a bf16 copy of the stored fp32 values (the state GEMM's next-chunk
+    // operand), so no separate conversion pass reads the fp32 result back
+    __nv_bfloat162* o16 = e.out1 ? reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(e.out1) + off +
+                                                                     (long long)tc.split * e.split_stride)
+                                 : nullptr;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       float4 w = make_float4(a * v[4 * q], a * v[4 * q + 1], a * v[4 * q + 2], a * v[4 * q + 3]);
       if (e.accumulate) {
-        float4 old = o4[q];
+        float4 old = e.acc_src ? reinterpret_cast<const float4*>(e.acc_src + off)[q] : o4[q];
+        if (e.src_decay_T > 0) {
+          const float sc = exp2f((float)e.src_decay_T * e.log2_decay[tc.z1]);
+          old.x *= sc; old.y *= sc; old.z *= sc; old.w *= sc;
+        }
         w.x += old.x; w.y += old.y; w.z += old.z; w.w += old.w;
       }
       o4[q] = w;
+      if (o16) {
+        o16[2 * q] = __floats2bfloat162_rn(w.x, w.y);
+        o16[2 * q + 1] = __floats2bfloat162_rn(w.z, w.w);
+      }
     }
     return;
   } else {
@@ -260,11 +287,17 @@ __device__ __forceinline__ void epilogue_zero_chunk(const GemmParams& p, const T
   if constexpr (EPI == EPI_F32_SCATTER) {
     return;  // the scattered GEMM has no zero tiles (no causal skip, K > 0)
   } else if constexpr (EPI == EPI_F32) {
-    if (e.accumulate) return;
+    if (e.accumulate) return;  // (a zero tile leaves an accumulated output, and its copy, as it is)
     float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out0) + off +
                                            (long long)tc.split * e.split_stride);
 #pragma unroll
     for (int q = 0; q < 8; ++q) o4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (e.out1) {
+      uint4* o16 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(e.out1) + off +
+                                            (long long)tc.split * e.split_stride);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) o16[q] = make_uint4(0u, 0u, 0u, 0u);
+    }
   } else {
     store_bf16x32(reinterpret_cast<__nv_bfloat16*>(e.out0) + off, v);
   }

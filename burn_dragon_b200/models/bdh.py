@@ -183,6 +183,12 @@ class BDH(nn.Module):
                                                      rs.distribution)
         self._eff16 = None
         self._geff = None
+        self._scaffold_work = None
+        # BDH_SCAFFOLD_CACHE_BASE=1 keeps W_seed in device memory (fp32) instead of
+        # regenerating it from the seed in the fold and gain-gradient kernels every step
+        import os as _os
+
+        self.scaffold_cache_base = device.type == "cuda" and _os.environ.get("BDH_SCAFFOLD_CACHE_BASE", "0") == "1"
 
     def scaffold_base(self, name: str) -> torch.Tensor:
         """W_seed of a projection (fp32), regenerated on the device when needed."""
@@ -195,7 +201,7 @@ class BDH(nn.Module):
             rows = shp[0] * shp[1] if len(shp) == 3 else shp[0]
             _ext.load().scaffold_effective(self.scaffold_keys[name], self.cfg.init_std, self.scaffold_dist, rows,
                                            shp[-2] if len(shp) == 3 else rows, shp[-1], 0, None, None, None, 0.0,
-                                           None, None, out)
+                                           None, None, out, None)
             self._bases[name] = out
         return self._bases[name]
 
@@ -308,40 +314,49 @@ class BDH(nn.Module):
             a, b, g = self._scaffold_parts(n)
             rows = shp[0] * shp[1] if len(shp) == 3 else shp[0]
             I = shp[1] if len(shp) == 3 else shp[0]
+            base = self.scaffold_base(n) if self.scaffold_cache_base else None
             mod.scaffold_effective(self.scaffold_keys[n], self.cfg.init_std, self.scaffold_dist, rows, I, shp[-1], r,
-                                   a.detach().reshape(rows, r), b.detach(), g.detach(), s, self._eff16[n], None, None)
+                                   a.detach().reshape(rows, r), b.detach(), g.detach(), s, self._eff16[n], None, None,
+                                   base)
             p16[n] = self._eff16[n]
             g32[n] = self._geff[n]
 
     def _scaffold_backward(self, g32: dict) -> None:
-        """Adapter grads from d(W_eff): dA = s dW B^T, dB = s A^T dW, dgain = sum(dW * W_seed)."""
+        """Adapter grads from d(W_eff), one pass over dW per projection on the device
+        (``scaffold_adapter_grad``): dA = s dW B^T, dB = s A^T dW, dgain = sum(dW * W_seed)
+        with W_seed regenerated from the seed (or read from the cached base)."""
         from .. import _ext
+        from .scaffold import base_shape
 
         mod = _ext.load()
         s = self.cfg.random_scaffold.adapter_scale()
+        r = self.cfg.random_scaffold.rank
         for n in ("encoder", "encoder_v", "decoder"):
             dW = self._geff[n]
             a, b, _ = self._scaffold_parts(n)
+            shp = base_shape(self.cfg, n)
+            Hm, I, O = (shp[0], shp[1], shp[2]) if len(shp) == 3 else (1, shp[0], shp[1])
             ga = self.store.view(self.store.grad, f"{n}_a")
             gb = self.store.view(self.store.grad, f"{n}_b")
-            torch.matmul(dW, b.detach().transpose(-1, -2), out=ga)
-            ga.mul_(s)
-            torch.matmul(a.detach().transpose(-1, -2), dW, out=gb)
-            gb.mul_(s)
-            if self.cfg.random_scaffold.trainable_gain:
-                gg = self.store.view(self.store.grad, f"{n}_gain")
-                gg.zero_()
-                mod.scaffold_gain_grad(self.scaffold_keys[n], self.cfg.init_std, self.scaffold_dist, dW, gg)
+            need = mod.scaffold_adapter_work(Hm, I, O, r)
+            if self._scaffold_work is None or self._scaffold_work.numel() < need:
+                self._scaffold_work = torch.empty(need, device=dW.device)
+            gg = self.store.view(self.store.grad, f"{n}_gain") if self.cfg.random_scaffold.trainable_gain else None
+            mod.scaffold_adapter_grad(self.scaffold_keys[n], self.cfg.init_std, self.scaffold_dist, Hm, I, O, r, dW,
+                                      a.detach(), b.detach(), self.scaffold_base(n) if self.scaffold_cache_base else None,
+                                      s, ga, gb, gg, self._scaffold_work)
 
     # ---------------------------------------------------------------- fused path
     def fused_step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None, state=None,
-                   accumulate: bool = False, loss_scale: float = 1.0) -> torch.Tensor:
+                   accumulate: bool = False, loss_scale: float = 1.0, grad_ready=None) -> torch.Tensor:
         """Forward + CE + backward on the sm_100a kernels. Writes ``.grad`` of every
         parameter (the flat grad buffer) and returns the loss as a device scalar.
 
         With a ``ModelState`` the chunk continues that state (stateful TBPTT: the state
         enters detached and leaves detached, burn_dragon_language/src/train/steps.rs:
-        2698-2731) and the state is advanced in place."""
+        2698-2731) and the state is advanced in place. ``grad_ready(name)`` is called on the
+        current stream as soon as a shared projection's gradient is final (data-parallel
+        overlap)."""
         from .bdh_fused import FusedBDH, FusedWorkspace
 
         B, T = tokens.shape
@@ -359,7 +374,7 @@ class BDH(nn.Module):
         rho0s = state.rhos if state is not None else None
         outs = f.forward(p16, p32, tokens, pos0=pos0, rho0s=rho0s, want_state=state is not None)
         loss = f.loss(targets, mask, scale=loss_scale)
-        f.backward(p16, p32, g32, tokens, pos0=pos0, accumulate=accumulate)
+        f.backward(p16, p32, g32, tokens, pos0=pos0, accumulate=accumulate, grad_ready=grad_ready)
         if self.scaffold:
             self._scaffold_backward(g32)
         if state is not None:

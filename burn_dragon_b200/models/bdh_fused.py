@@ -22,6 +22,7 @@ loop), dragon/residual_stream.rs:323-572 (layer), dragon/language_head.rs:549-57
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -33,6 +34,7 @@ from .reference import rope_freqs
 # The forward stores x = relu(v Dx) next to q = rope(x) (the gate and the decoder
 # backward read x); the step roofline counts its bytes.
 STORES_X = True
+ROPE_TABLE = os.environ.get("BDH_ROPE_TABLE", "0") == "1"
 
 
 def fused_unsupported(cfg) -> str | None:
@@ -51,6 +53,9 @@ def fused_unsupported(cfg) -> str | None:
         return "a tied lm_head"
     if getattr(cfg, "latent_fanout_schedule", None) and not cfg.uniform_latent_fanout():
         return "a latent fan-out schedule"
+    rs = getattr(cfg, "random_scaffold", None)
+    if rs is not None and rs.enabled and rs.rank not in (4, 8, 16, 32):
+        return f"random-scaffold rank {rs.rank} (the adapter-gradient kernel has ranks 4, 8, 16, 32)"
     return None
 
 
@@ -104,6 +109,8 @@ class FusedWorkspace:
         if inference:
             self.rho16 = None
             self.rho_sets = None
+            self.rho16_sets = None
+            self.rho16_valid = [False, False]
             self.rho_flip = 0
             self.has_rho0 = False
             self.qscaled = None
@@ -135,23 +142,48 @@ class FusedWorkspace:
         # copy of the incoming state and two ping-pong sets of outgoing fp32 states
         self.rho16: list[torch.Tensor] | None = None
         self.rho_sets: list[list[torch.Tensor]] | None = None
+        self.rho16_sets: list[list[torch.Tensor]] | None = None
+        self.rho16_valid = [False, False]
         self.rho_flip = 0
         self.has_rho0 = False
         self.qscaled: torch.Tensor | None = None
 
+    def rope_tab(self, pos0: int):
+        """The half2 (cos, sin) table of this workspace's positions pos0 .. pos0 + T - 1
+        (rebuilt only when pos0 changes), or None without RoPE or unless BDH_ROPE_TABLE=1
+        (the epilogues evaluate the phases themselves by default: the table's loads
+        measured slower at BDH-GPU batch 32)."""
+        if self.freq is None or not ROPE_TABLE:
+            return None
+        if getattr(self, "_rope_tab", None) is None:
+            self._rope_tab = torch.empty(self.T, self.Nh // 2, dtype=torch.int32, device=self.freq.device)
+            self._rope_pos0 = None
+        if self._rope_pos0 != pos0:
+            G.rope_table(self.freq, pos0, self.T, self._rope_tab)
+            self._rope_pos0 = pos0
+        return self._rope_tab
+
     def ensure_state_buffers(self) -> None:
+        """Training: two ping-pong sets of outgoing fp32 states with their bf16 operand
+        copies (written by the state GEMM's epilogue, so the next chunk reads its incoming
+        state as a GEMM operand without a conversion pass). Inference: one bf16 operand
+        buffer, the outgoing state overwriting the incoming one."""
         if self.rho16 is not None:
             return
         B, H, Nh, D, L = self.B, self.H, self.Nh, self.D, self.L
         dev = self.v32[0].device
-        one16 = torch.empty(B, H, Nh, D, dtype=torch.bfloat16, device=dev) if self.inference else None
-        self.rho16 = [one16 if self.inference else torch.empty(B, H, Nh, D, dtype=torch.bfloat16, device=dev)
-                      for _ in range(L)]
         if self.inference:
-            self.rho_sets = None  # inference: outgoing state overwrites the incoming one
+            one16 = torch.empty(B, H, Nh, D, dtype=torch.bfloat16, device=dev)
+            self.rho16 = [one16] * L
+            self.rho_sets = None
+            self.rho16_sets = None
         else:
             self.rho_sets = [[torch.empty(B, H, Nh, D, dtype=torch.float32, device=dev) for _ in range(L)]
                              for _ in range(2)]
+            self.rho16_sets = [[torch.empty(B, H, Nh, D, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+                               for _ in range(2)]
+            self.rho16 = list(self.rho16_sets[0])
+        self.rho16_valid = [False, False]
 
 
 def _bn(n: int) -> int:
@@ -187,8 +219,24 @@ class FusedBDH:
         decay = ws.log2_decay is not None
         ws.has_rho0 = rho0s is not None
         out_states = None
+        out16 = None
+        in16 = None  # bf16 operand copies of the incoming states, when a state GEMM wrote them
         if rho0s is not None or want_state:
             ws.ensure_state_buffers()
+        if not ws.inference and ws.rho_sets is not None:
+            cur = ws.rho_flip
+            prev = cur ^ 1
+            if rho0s is not None:
+                if ws.rho16_valid[prev] and all(r.data_ptr() == s.data_ptr() for r, s in zip(rho0s, ws.rho_sets[prev])):
+                    in16 = ws.rho16_sets[prev]
+                else:
+                    # a state from elsewhere (checkpoint, probe): its operand copy goes into the
+                    # set this step does not write
+                    for l in range(ws.L):
+                        ws.rho16_sets[prev][l].copy_(rho0s[l])
+                    ws.rho16_valid[prev] = False
+                    in16 = ws.rho16_sets[prev]
+                ws.rho16 = list(in16)
         if want_state:
             if ws.inference:
                 if rho0s is None:
@@ -198,7 +246,11 @@ class FusedBDH:
                     out_states = list(rho0s)  # updated in place
             else:
                 out_states = ws.rho_sets[ws.rho_flip]
+                out16 = ws.rho16_sets[ws.rho_flip]
+                ws.rho16_valid[ws.rho_flip] = True
                 ws.rho_flip ^= 1
+        elif not ws.inference and ws.rho_sets is not None:
+            ws.rho16_valid = [False, False]
         B, T, D, H, Nh, N, M, L = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L
         peer = None
         if self.tp is not None and self.tp.world > 1 and not ws.inference:
@@ -224,7 +276,7 @@ class FusedBDH:
             # x = relu(v Dx - thr), q = rope(x)       (K = D)
             G.gemm(G.EPI_RELU_ROPE, Operand(v16, False, D, M, D), B_enc, M, Nh, D, ws.x16[l], Z1=H, bn=G.tma_bn(M, Nh),
                    out1=ws.q16[l] if ws.freq is not None else None, ld=N, sz1=Nh, thr=thr, freq=ws.freq,
-                   T=T, pos0=pos0, Nh=Nh)
+                   T=T, pos0=pos0, Nh=Nh, rope_tab=ws.rope_tab(pos0))
             # S = tril_{-1}(q q^T) (* gamma^(i-j))      (K = Nh), upper tiles skipped
             qop = Operand(ws.q16[l], False, Nh, T, N, z1=(H, Nh), z2=(B, T * N))
             # 256-row CTA-pair tiles x 128 columns: finer causal skipping than 256 x 256
@@ -237,7 +289,8 @@ class FusedBDH:
                    ld=H * D, sz1=D, sz2=T * H * D)
             if rho0s is not None:
                 # a += gamma^t q rho0                    (K = Nh)
-                ws.rho16[l].copy_(rho0s[l])
+                if in16 is None:
+                    ws.rho16[l].copy_(rho0s[l])
                 G.gemm(G.EPI_F32, qop, Operand(ws.rho16[l], True, D, Nh, D, z1=(H, Nh * D), z2=(B, H * Nh * D)),
                        T, D, Nh, ws.a32[l], Z1=H, Z2=B, ld=H * D, sz1=D, sz2=T * H * D, accumulate=True,
                        log2_decay=ws.log2_decay, row_decay=decay)
@@ -254,16 +307,14 @@ class FusedBDH:
                     qv = ws.q16[l].view(B, T, H, Nh).float() * sc[None, :, :, None]
                     ws.qscaled.view(B, T, H, Nh).copy_(qv)
                     qsrc = ws.qscaled
-                if rho0s is not None:
-                    gT = torch.exp2(ws.log2_decay * T).view(1, H, 1, 1) if decay else 1.0
-                    if ro.data_ptr() == rho0s[l].data_ptr():
-                        if decay:
-                            ro.mul_(gT)
-                    else:
-                        ro.copy_(rho0s[l] * gT)
+                # the carried state enters through the epilogue (decayed by gamma^T per
+                # head), and the bf16 operand copy for the next chunk leaves with it
+                src = rho0s[l] if rho0s is not None else None
                 G.gemm(G.EPI_F32, Operand(qsrc, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)),
                        Operand(v16, True, D, T, D, z2=(B, T * D)), Nh, D, T, ro, Z1=H, Z2=B, ld=D, sz1=Nh * D,
-                       sz2=H * Nh * D, accumulate=rho0s is not None)
+                       sz2=H * Nh * D, accumulate=src is not None, acc_src=src,
+                       src_decay_T=T if (decay and src is not None) else 0, log2_decay=ws.log2_decay,
+                       out1=out16[l] if out16 is not None else None)
             mod.ln_fwd(ws.a32[l], None, M * H, D, p32["norm_gamma"], p32["norm_beta"], eps, None, ws.an16[l],
                        ws.amean[l], ws.arstd[l])
             # yn = relu(an Dy - thr) * x                (K = D)
@@ -315,13 +366,18 @@ class FusedBDH:
 
     # ---------------------------------------------------------------- backward
     def backward(self, p16: dict, p32: dict, g32: dict, tokens: torch.Tensor | None, pos0: int = 0,
-                 accumulate: bool = False, dv_out: torch.Tensor | None = None, with_embed: bool = True):
+                 accumulate: bool = False, dv_out: torch.Tensor | None = None, with_embed: bool = True,
+                 grad_ready=None):
         """Writes parameter gradients into g32 (``accumulate``: adds to them, for
         gradient accumulation over micro-batches).
 
         Pipeline stages: ``dv_out`` ([M, D] fp32, the gradient of this stage's output)
         replaces the LM head / CE backward; ``with_embed=False`` stops at this stage's
-        input and returns its gradient (a view of a workspace buffer)."""
+        input and returns its gradient (a view of a workspace buffer).
+
+        ``grad_ready(name)``: called as soon as the weights are shared across the layers
+        and layer 0 has added its last term to ``decoder`` / ``encoder_v`` / ``encoder``."""
+        ready = grad_ready if grad_ready is not None else (lambda name: None)
         ws, cfg, mod = self.ws, self.cfg, self.mod
         B, T, D, H, Nh, N, M, L, V = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L, ws.V
         gam, bet = p32["norm_gamma"], p32["norm_beta"]
@@ -352,10 +408,14 @@ class FusedBDH:
             # dE += yn^T dm
             G.gemm(G.EPI_F32, Operand(ws.yn16[l], True, N, M, N), Operand(ws.dm16, True, D, M, D), N, D, M,
                    g32["decoder"], ld=D, accumulate=True)
+            if l == 0:
+                ready("decoder")
             # dDy_h += an_h^T dy_h
             G.gemm(G.EPI_F32, Operand(ws.an16[l], True, D, M, H * D, z1=(H, D)),
                    Operand(ws.dy16, True, Nh, M, N, z1=(H, Nh)), D, Nh, M, g32["encoder_v"], Z1=H, ld=Nh,
                    sz1=D * Nh, accumulate=True)
+            if l == 0:
+                ready("encoder_v")
             # d(an)_h = dy_h Dy_h^T
             G.gemm(G.EPI_F32, Operand(ws.dy16, False, Nh, M, N, z1=(H, Nh)),
                    Operand(encv, False, Nh, D, Nh, z1=(H, D * Nh)), M, D, Nh, ws.dan32, Z1=H, ld=H * D, sz1=D)
@@ -371,12 +431,14 @@ class FusedBDH:
             # carries the x <= 0 mask as -0.0 from the decoder backward)
             G.gemm(G.EPI_DQ, Operand(ws.G16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
                    Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B, bn=G.tma_bn(T, Nh),
-                   aux0=ws.dx16, ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh)
+                   aux0=ws.dx16, ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh,
+                   rope_tab=ws.rope_tab(pos0))
             if ws.has_rho0:
                 # + rope^T(gamma^t dC rho0^T) (the carried state is detached: no grad to rho0)
                 G.gemm(G.EPI_DQ, dcop, Operand(ws.rho16[l], False, D, Nh, D, z1=(H, Nh * D), z2=(B, H * Nh * D)),
-                       T, Nh, D, ws.dx16, Z1=H, Z2=B, bn=G.tma_bn(T, Nh), aux0=ws.dx16, ld=N, sz1=Nh,
+                       T, Nh, D, ws.dx16, Z1=H, Z2=B, bn=128, aux0=ws.dx16, ld=N, sz1=Nh,
                        sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh, log2_decay=ws.log2_decay,
+                       rope_tab=ws.rope_tab(pos0),
                        row_decay=ws.log2_decay is not None)
             # dV = sum_h S_h^T dC_h  (K = (h, i))
             G.gemm(G.EPI_F32, Operand(ws.S16[l], True, T, H * T, T, z2=(B, H * T * T)),
@@ -385,6 +447,8 @@ class FusedBDH:
             # dDx_h += v^T dx_h
             G.gemm(G.EPI_F32, Operand(v16, True, D, M, D), Operand(ws.dx16, True, Nh, M, N, z1=(H, Nh)), D, Nh, M,
                    g32["encoder"], Z1=H, ld=Nh, sz1=D * Nh, accumulate=True)
+            if l == 0:
+                ready("encoder")
             # dv_x per head = dx_h Dx_h^T
             G.gemm(G.EPI_F32, Operand(ws.dx16, False, Nh, M, N, z1=(H, Nh)),
                    Operand(enc, False, Nh, D, Nh, z1=(H, D * Nh)), M, D, Nh, ws.dvx32, Z1=H, ld=D, sz1=M * D)

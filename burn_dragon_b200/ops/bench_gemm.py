@@ -28,11 +28,14 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
     freq = torch.rand(Nh, device=dev) * 0.1
     if os.environ.get("BDH_BENCH_NOROPE"):
         freq = None  # the epilogue without the rotation (cost split of the RoPE math)
+    tab = None
+    if freq is not None and os.environ.get("BDH_BENCH_ROPE_TABLE", "0") == "1":
+        tab = G.rope_table(freq, 0, T)  # the half2 phase table the fused step passes
     if case == "xproj":
         v, enc, x, q = r(M, D), r(H, D, Nh), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_RELU_ROPE, Operand(v, False, D, M, D),  # noqa: E731
                               Operand(enc, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, x, Z1=H, bn=G.tma_bn(M, Nh), out1=q, ld=N,
-                              sz1=Nh, freq=freq, T=T, Nh=Nh)
+                              sz1=Nh, freq=freq, T=T, Nh=Nh, rope_tab=tab)
         return call, 2 * M * N * D, (M * D + D * N + 2 * M * N) * 2
     if case == "scores":
         q, S = r(M, N), r(B, H, T, T)
@@ -56,7 +59,7 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
         g16, q, dx = r(B, H, T, T), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_DQ, Operand(g16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),  # noqa: E731
                               Operand(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B, bn=G.tma_bn(T, Nh),
-                              aux0=dx, ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh)
+                              aux0=dx, ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh, rope_tab=tab)
         return call, 2 * B * H * T * T * Nh, (B * H * T * T + 3 * M * N) * 2
     if case == "wgrad":
         a, dy, out = r(M, D), r(M, N), torch.zeros(H, D, Nh, device=dev)
@@ -71,6 +74,12 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
         call = lambda: G.gemm(G.EPI_F32, Operand(yn, False, N, M, N), Operand(dec, True, D, N, D), M, D, N,  # noqa: E731
                               part, splits=splits, ld=D, split_stride=M * D)
         return call, 2 * M * N * D, M * N * 2 + splits * M * D * 4
+    if case == "k256":
+        # the x-projection's operands with a plain bf16 output (no ReLU / RoPE, one tensor)
+        v, enc, x = r(M, D), r(H, D, Nh), r(M, N)
+        call = lambda: G.gemm(G.EPI_BF16, Operand(v, False, D, M, D),  # noqa: E731
+                              Operand(enc, True, Nh, D, Nh, z1=(H, D * Nh)), M, Nh, D, x, Z1=H, bn=128, ld=N, sz1=Nh)
+        return call, 2 * M * N * D, (M * D + D * N + M * N) * 2
     if case == "plain":
         # square K-major GEMM with an fp32 output: tile shape / CTA-pair comparison
         # (BDH_BENCH_BN, BDH_BENCH_PAIR); M = N = batch * 1024, K = seq * 16

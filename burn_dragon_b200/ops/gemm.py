@@ -58,10 +58,11 @@ def check_errors(device: torch.device) -> None:
         raise RuntimeError(f"tcgen05 GEMM engine reported a bounded-wait timeout (code {code})")
 
 
-# Tile N of the TMA-epilogue modes (x-projection, gate, decoder backward, dQ): 256 runs
-# them on CTA pairs with 256 x 256 tiles where M >= 256 (BDH_TMA_BN=128 selects the
-# 1-CTA 128 x 128 kernel).
-TMA_BN = int(os.environ.get("BDH_TMA_BN", "256"))
+# Tile N of the TMA-epilogue modes (x-projection, gate, decoder backward, dQ): 128 runs
+# the 1-CTA 128 x 128 kernel; 256 runs CTA pairs with 256 x 256 tiles where M >= 256
+# (their mainloops are about twice as fast, but at BDH-GPU batch 32 the epilogue bounds
+# both and the pair measured 2-15% slower, so 128 is the default).
+TMA_BN = int(os.environ.get("BDH_TMA_BN", "128"))
 
 
 def tma_bn(M: int, N: int) -> int:
@@ -90,14 +91,32 @@ def gemm(epi: int, a: Operand, b: Operand, M: int, N: int, K: int, out0: torch.T
          out1=None, aux0=None, aux1=None, ld: int, sz1: int = 0, sz2: int = 0, split_stride: int = 0,
          alpha: float = 1.0, thr: float = 0.0, freq=None, log2_decay=None, T: int = 1, pos0: int = 0,
          Nh: int = 1, accumulate: bool = False, row_decay: bool = False, pair: bool | None = None,
-         scatter: list[int] | None = None) -> None:
+         scatter: list[int] | None = None, acc_src: torch.Tensor | None = None, src_decay_T: int = 0,
+         rope_tab: torch.Tensor | None = None) -> None:
     """``scatter`` (EPI_F32_SCATTER): [world, rows per owner, rank, slot stride, slot
-    pointer of every rank] — rows go straight to their owner's slot over NVLink."""
+    pointer of every rank] — rows go straight to their owner's slot over NVLink.
+
+    EPI_F32 extras: ``out1`` a bf16 copy of the stored values; ``acc_src`` with
+    ``accumulate``: out0 = alpha * acc + acc_src (* 2^(src_decay_T * log2_decay[z1]) when
+    ``src_decay_T`` > 0) instead of adding out0's old contents.
+
+    ``rope_tab`` (x-projection / dQ with ``freq``): the half2 (cos, sin) table of
+    ``rope_table`` for this call's positions pos0 .. pos0 + T - 1."""
     mod = _ext.load()
     bn = bn or pick_bn(N)
     mod.gemm(epi, bn, a.t, a.mn, a.geom(), b.t, b.mn, b.geom(), M, N, K, Z1, Z2, splits, causal_skip,
              out0, out1, aux0, aux1, ld, sz1, sz2, split_stride, alpha, thr, freq, log2_decay, T, pos0, Nh,
-             accumulate, row_decay, int(PAIR if pair is None else pair), error_word(out0.device), scatter)
+             accumulate, row_decay, int(PAIR if pair is None else pair), error_word(out0.device), scatter,
+             acc_src, src_decay_T, rope_tab)
+
+
+def rope_table(freq: torch.Tensor, pos0: int, T: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """(cos, sin) half2 pairs of the RoPE phases for positions pos0 .. pos0 + T - 1 and the
+    latent pairs of ``freq`` ([T, Nh / 2] int32), the table the epilogues read."""
+    if out is None:
+        out = torch.empty(T, freq.numel() // 2, dtype=torch.int32, device=freq.device)
+    _ext.load().rope_table(freq, pos0, T, out)
+    return out
 
 
 def matmul(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.float32, a_t: bool = False,

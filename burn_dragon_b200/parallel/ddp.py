@@ -6,6 +6,9 @@ read, and a page of flags. Each optimizer step is
 
     cast fp32 grads -> bf16 (local) -> barrier -> ddp_step -> barrier
 
+per bucket of the flat store (``buckets``), each on a side stream as soon as the
+backward has finished that bucket's gradients (``overlap``), then a closing barrier
+
 where ``ddp_step`` (``csrc/comm.cu``) is one kernel: rank r sums its slice [lo_r, hi_r)
 of every peer's gradient with plain P2P loads (a reduce-scatter, fp32 accumulation),
 runs AdamW on its fp32 master slice and moment shard, and stores the new bf16 weights
@@ -36,11 +39,19 @@ from .. import _ext
 
 
 class NVLinkDDP:
-    """Symmetric-memory communicator for one flat parameter store of ``numel`` elements."""
+    """Symmetric-memory communicator for one flat parameter store of ``numel`` elements.
 
-    FLAG_WORDS = 64
+    ``buckets``: contiguous [start, end) ranges of the flat store that become final at
+    different points of the backward (default: one bucket). Every rank owns an 8-aligned
+    1/W slice of every bucket. With ``overlap`` the backward calls ``bucket_ready(b)`` as
+    soon as bucket b's gradients are final, and that bucket's cast, barrier and fused
+    reduce-scatter + AdamW + all-gather run on a side stream beside the rest of the
+    backward; ``step_adamw`` then launches what is left and joins."""
 
-    def __init__(self, numel: int, device: torch.device, group=None, grad_dtype: str = "bf16"):
+    FLAG_WORDS = 512
+
+    def __init__(self, numel: int, device: torch.device, group=None, grad_dtype: str = "bf16",
+                 buckets: list[tuple[int, int]] | None = None):
         if not dist.is_initialized():
             raise RuntimeError("NVLinkDDP needs an initialised process group")
         if grad_dtype not in ("bf16", "fp32"):
@@ -54,11 +65,26 @@ class NVLinkDDP:
         self.dev = device.index if device.index is not None else torch.cuda.current_device()
         self.grad_bf16 = grad_dtype == "bf16"
         mod = _ext.load()
-        unit = 8 * self.world
-        self.numel = -(-numel // unit) * unit
-        self.shard = self.numel // self.world
-        self.lo = self.rank * self.shard
-        self.hi = self.lo + self.shard
+        self.numel = -(-numel // 64) * 64
+        buckets = buckets or [(0, self.numel)]
+        if buckets[0][0] != 0 or buckets[-1][1] < numel or any(a[1] != b[0] for a, b in zip(buckets, buckets[1:])):
+            raise ValueError("buckets must tile [0, numel) in order")
+        buckets = [(a, b) for a, b in buckets[:-1]] + [(buckets[-1][0], self.numel)]
+        if any(a % 8 for a, _ in buckets) or len(buckets) > 50:
+            raise ValueError("bucket starts must be multiples of 8 (at most 50 buckets)")
+        # every rank's slice of every bucket: [lo, hi), 8-aligned, the last one clipped
+        self.buckets = []
+        moff = 0
+        for a, b in buckets:
+            c = -(-(b - a) // (8 * self.world)) * 8
+            lo = min(a + self.rank * c, b)
+            hi = min(lo + c, b)
+            self.buckets.append({"start": a, "end": b, "lo": lo, "hi": hi, "moff": moff})
+            moff += hi - lo
+        self.shard_total = moff
+        # kept for callers of the one-bucket layout
+        self.lo, self.hi = self.buckets[0]["lo"], self.buckets[0]["hi"]
+        self.shard = -(-self.numel // self.world)
         gbytes = self.numel * (2 if self.grad_bf16 else 4)
         sizes = {"gsym": gbytes, "shadow": self.numel * 2, "flags": self.FLAG_WORDS * 4}
         self._own = {k: mod.sym_alloc(b, self.dev) for k, b in sizes.items()}
@@ -75,53 +101,100 @@ class NVLinkDDP:
                     p = mod.ipc_open(gathered[r][k], self.dev)
                     self._opened.append(p)
                     self.ptrs[k].append(p)
-        # local fp32 gradient (written by the backward) and fp32 master (current on [lo, hi))
+        # local fp32 gradient (written by the backward) and fp32 master (current on the
+        # owned slices)
         self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
         self.param = torch.zeros(self.numel, dtype=torch.float32, device=device)
         self.shadow = mod.wrap_ptr(self._own["shadow"], self.numel, 1, self.dev)
         self.gsym = mod.wrap_ptr(self._own["gsym"], self.numel, 1 if self.grad_bf16 else 0, self.dev)
-        self.m = torch.zeros(self.shard, dtype=torch.float32, device=device)
-        self.v = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        self.flags_local = mod.wrap_ptr(self._own["flags"], self.FLAG_WORDS, 2, self.dev)
+        self.m = torch.zeros(max(1, moff), dtype=torch.float32, device=device)
+        self.v = torch.zeros(max(1, moff), dtype=torch.float32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self._gred = None
         self._sumsq = torch.zeros(1, dtype=torch.float32, device=device)
         self.norm_out = torch.zeros(2, dtype=torch.float32, device=device)  # {clip coef, grad norm}
         self.master_synced = True
+        self.side = torch.cuda.Stream(device)
+        self._launched: set[int] = set()
+        self._opt = None
         dist.barrier(group=group)
 
-    def _barrier_args(self):
-        f = self.ptrs["flags"]
-        return f, f, f, f
+    # ---------------------------------------------------------------- per-step protocol
+    def begin_step(self, opt) -> None:
+        """Start a step on the current stream: advance the step epoch. ``opt`` supplies
+        the hyper-parameters (its device scalars must be staged for this step)."""
+        _ext.load().ddp_epoch_advance(self.flags_local)
+        self._launched = set()
+        self._opt = opt
+        if opt.clip is not None and self._gred is None:
+            self._gred = torch.empty(max(1, self.shard_total), dtype=torch.float32, device=self.device)
+        if opt.clip is not None:
+            self._sumsq.zero_()
 
-    def barrier(self, phase: int) -> None:
-        _ext.load().peer_barrier(*self._barrier_args(), self.rank, phase, self.err)
-
-    def _stage_grads(self) -> None:
+    def _bucket_work(self, b: int) -> None:
+        mod = _ext.load()
+        bk = self.buckets[b]
+        a, e, lo, hi = bk["start"], bk["end"], bk["lo"], bk["hi"]
+        opt = self._opt
         if self.grad_bf16:
-            _ext.load().cast_bf16(self.grad, self.gsym)
+            mod.cast_bf16(self.grad[a:e], self.gsym[a:e])
         else:
-            self.gsym.copy_(self.grad)
+            self.gsym[a:e].copy_(self.grad[a:e])
+        mod.ddp_slot_barrier(self.ptrs["flags"], self.rank, b, self.err)
+        if hi <= lo:
+            return
+        g, sh = self.ptrs["gsym"], self.ptrs["shadow"]
+        mo, n = bk["moff"], hi - lo
+        if opt.clip is None:
+            mod.ddp_step(g, sh, self.grad_bf16, self.rank, lo, hi, self.param, self.m[mo:mo + n], self.v[mo:mo + n],
+                         opt.b1, opt.b2, opt.eps, opt.wd, opt._hyper, None)
+        else:
+            # sums of squares accumulate into _sumsq over the buckets (ddp_reduce zeroes its
+            # target, so each bucket reduces into a scratch word first)
+            part = self._bucket_sumsq(b)
+            mod.ddp_reduce(g, sh, self.grad_bf16, self.rank, lo, hi, self._gred[mo:mo + n], part)
+            self._sumsq.add_(part)
+
+    def _bucket_sumsq(self, b: int) -> torch.Tensor:
+        if not hasattr(self, "_bsum"):
+            self._bsum = torch.zeros(len(self.buckets), dtype=torch.float32, device=self.device)
+        return self._bsum[b:b + 1]
+
+    def bucket_ready(self, b: int) -> None:
+        """Bucket b's gradients are final on the current stream: run its communication on
+        the side stream from here on."""
+        if b in self._launched:
+            return
+        self._launched.add(b)
+        cur = torch.cuda.current_stream(self.device)
+        self.side.wait_stream(cur)
+        with torch.cuda.stream(self.side):
+            self._bucket_work(b)
 
     def step_adamw(self, opt) -> None:
-        """Reduce-scatter + AdamW on this rank's shard + all-gather of the new bf16 weights.
-        ``opt`` supplies the hyper-parameters, the device-resident {lr, bc1, bc2} and the
-        global-norm clip (``opt.clip``)."""
+        """Finish the step: launch the buckets not yet launched, join the side stream, and
+        (with global-norm clipping) exchange the norm and apply the clipped update; then
+        the closing barrier after which every rank's shadow holds the new weights."""
         mod = _ext.load()
-        self._stage_grads()
-        self.barrier(0)
-        g, sh = self.ptrs["gsym"], self.ptrs["shadow"]
-        if opt.clip is None:
-            mod.ddp_step(g, sh, self.grad_bf16, self.rank, self.lo, self.hi, self.param, self.m, self.v, opt.b1,
-                         opt.b2, opt.eps, opt.wd, opt._hyper, None)
-        else:
-            if self._gred is None:
-                self._gred = torch.empty(self.shard, dtype=torch.float32, device=self.device)
-            mod.ddp_reduce(g, sh, self.grad_bf16, self.rank, self.lo, self.hi, self._gred, self._sumsq)
+        if self._opt is None:
+            self.begin_step(opt)
+        for b in range(len(self.buckets)):
+            self.bucket_ready(b)
+        cur = torch.cuda.current_stream(self.device)
+        cur.wait_stream(self.side)
+        if opt.clip is not None:
             mod.ddp_norm_exchange(self.ptrs["flags"], self.rank, self._sumsq, float(opt.clip), self.norm_out, self.err)
-            mod.ddp_apply(g, sh, self.rank, self.lo, self.hi, self._gred, self.param, self.m, self.v, opt.b1, opt.b2,
-                          opt.eps, opt.wd, opt._hyper, self.norm_out)
+            g, sh = self.ptrs["gsym"], self.ptrs["shadow"]
+            for bk in self.buckets:
+                lo, hi, mo = bk["lo"], bk["hi"], bk["moff"]
+                if hi > lo:
+                    n = hi - lo
+                    mod.ddp_apply(g, sh, self.rank, lo, hi, self._gred[mo:mo + n], self.param, self.m[mo:mo + n],
+                                  self.v[mo:mo + n], opt.b1, opt.b2, opt.eps, opt.wd, opt._hyper, self.norm_out)
             opt._scratch[1:2].copy_(self.norm_out[1:2])
-        self.barrier(1)
+        mod.ddp_slot_barrier(self.ptrs["flags"], self.rank, len(self.buckets), self.err)
+        self._opt = None
         self.master_synced = False
 
     def sync_master(self) -> None:
@@ -129,17 +202,33 @@ class NVLinkDDP:
         if self.master_synced:
             return
         if self.world > 1:
-            shards = list(self.param.split(self.shard))
-            mine = shards[self.rank].clone()
-            dist.all_gather(shards, mine, group=self.group)
+            for bk in self.buckets:
+                a, e = bk["start"], bk["end"]
+                c = -(-(e - a) // (8 * self.world)) * 8
+                full = torch.zeros(c * self.world, dtype=torch.float32, device=self.device)
+                mine = torch.zeros(c, dtype=torch.float32, device=self.device)
+                mine[:bk["hi"] - bk["lo"]].copy_(self.param[bk["lo"]:bk["hi"]])
+                dist.all_gather_into_tensor(full, mine, group=self.group)
+                self.param[a:e].copy_(full[:e - a])
         self.master_synced = True
 
-    def allreduce_mean(self) -> None:
-        """Gradient mean in place over the local fp32 gradient (NCCL; no optimizer)."""
-        op = dist.ReduceOp.AVG if dist.get_backend(self.group) == "nccl" else dist.ReduceOp.SUM
-        dist.all_reduce(self.grad, op=op, group=self.group)
-        if op == dist.ReduceOp.SUM:
-            self.grad.div_(self.world)
+    def gather_moments(self, m_full: torch.Tensor, v_full: torch.Tensor) -> None:
+        """Assemble the full AdamW moments from every rank's slices (a collective)."""
+        for src, dst in ((self.m, m_full), (self.v, v_full)):
+            for bk in self.buckets:
+                a, e = bk["start"], bk["end"]
+                c = -(-(e - a) // (8 * self.world)) * 8
+                full = torch.zeros(c * self.world, dtype=torch.float32, device=self.device)
+                mine = torch.zeros(c, dtype=torch.float32, device=self.device)
+                n = bk["hi"] - bk["lo"]
+                mine[:n].copy_(src[bk["moff"]:bk["moff"] + n])
+                if self.world > 1:
+                    dist.all_gather_into_tensor(full, mine, group=self.group)
+                else:
+                    full.copy_(mine)
+                lim = min(e, dst.numel())
+                if lim > a:
+                    dst[a:lim].copy_(full[:lim - a])
 
     def check(self) -> None:
         code = int(self.err.item())
@@ -147,7 +236,7 @@ class NVLinkDDP:
             raise RuntimeError(f"NVLinkDDP: a peer wait timed out (code {code})")
 
     def state_dict(self) -> dict:
-        return {"m": self.m, "v": self.v, "lo": self.lo, "hi": self.hi}
+        return {"m": self.m, "v": self.v, "buckets": [dict(b) for b in self.buckets]}
 
     def close(self) -> None:
         mod = _ext.load()

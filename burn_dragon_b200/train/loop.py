@@ -107,9 +107,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     if mode == "hybrid_2d":
         tp_arg = int(cfg.parallel.tensor.get("size", 8))
         comm = "nvlink" if o.grad_clip_value is None and dev.type == "cuda" else None
-    if cfg.parallel.tensor.get("sequence_parallel") and not tp_arg:
-        raise ValueError("parallel.tensor.sequence_parallel needs a tensor-parallel mode "
-                         "(tensor_parallel_neuron or hybrid_2d)")
+    if cfg.parallel.tensor.get("sequence_parallel"):
+        raise ValueError("parallel.tensor.sequence_parallel is not implemented: the residual stream is "
+                         "replicated across the tensor-parallel group (unset the key)")
     if cfg.dataset.type in ("jsonl", "parquet", "text"):
         from .datasets import prepare_corpus
 

@@ -108,12 +108,37 @@ class Trainer:
             if grad_clip_value is not None:
                 raise ValueError("the NVLink DDP step clips by global norm only; use comm='nccl' for "
                                  "element-wise value clipping")
+            self._bucket_of, buckets = self._ddp_buckets()
             self.comm = NVLinkDDP(self.model.store.numel, self.device, group=self.dp_group,
-                                  grad_dtype=os.environ.get("BDH_DDP_GRAD_DTYPE", "bf16"))
+                                  grad_dtype=os.environ.get("BDH_DDP_GRAD_DTYPE", "bf16"), buckets=buckets)
             self.model.attach_buffers(self.comm.param, self.comm.grad, self.comm.shadow)
+            # overlap the per-bucket gradient exchange with the rest of the backward
+            # (BDH_DDP_OVERLAP=0: one exchange after the backward)
+            self.overlap = (os.environ.get("BDH_DDP_OVERLAP", "1") != "0" and self.fused
+                            and not self.model.scaffold and micro_batches == 1)
         self._graph = None
         self._graph_shape = None
         self._graph_launches = 0
+        if self.comm is None:
+            self.overlap = False
+
+    def _ddp_buckets(self):
+        """Buckets of the flat store in the order the fused backward finishes them: the
+        three shared projections (final after layer 0's dE / dDy / dDx contractions), then
+        everything else (final at the end of the backward). One bucket for layouts
+        without the three projections (random scaffold)."""
+        st = self.model.store
+        names = list(st.shapes)
+        if names[:3] != ["encoder", "encoder_v", "decoder"]:
+            return {}, None
+        cuts = [st.offsets["encoder"], st.offsets["encoder_v"], st.offsets["decoder"], st.offsets[names[3]]]
+        buckets = [(cuts[i], cuts[i + 1]) for i in range(3)] + [(cuts[3], st.numel)]
+        return {"encoder": 0, "encoder_v": 1, "decoder": 2}, buckets
+
+    def _grad_ready(self, name: str) -> None:
+        b = self._bucket_of.get(name)
+        if b is not None:
+            self.comm.bucket_ready(b)
 
     def sync_params(self) -> None:
         """Make the full fp32 master and the optimizer moments current on every rank (the
@@ -121,12 +146,7 @@ class Trainer:
         if self.comm is None:
             return
         self.comm.sync_master()
-        if self.world > 1:
-            n = self.comm.numel
-            for full, shard in ((self.opt.m, self.comm.m), (self.opt.v, self.comm.v)):
-                buf = torch.empty(n, dtype=torch.float32, device=self.device)
-                dist.all_gather(list(buf.split(self.comm.shard)), shard.contiguous(), group=self.dp_group)
-                full.copy_(buf[:full.numel()])
+        self.comm.gather_moments(self.opt.m, self.opt.v)
 
     def enable_cuda_graph(self, tokens: torch.Tensor, targets: torch.Tensor, warmup: int = 2) -> None:
         """Capture forward + backward + all-reduce + AdamW of one step into a CUDA graph.
@@ -153,12 +173,18 @@ class Trainer:
         self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
         before = _ext.launch_count()
         with torch.cuda.graph(g):
+            self._begin_update()
             self._sloss = self.compute_grads(self._sx, self._sy)
             self._update()
         self._graph_launches = _ext.launch_count() - before
         self.opt.t -= 1  # the capture itself did not update anything
         self._graph = g
         self._graph_shape = (tuple(tokens.shape), tuple(targets.shape))
+
+    def _begin_update(self) -> None:
+        """Before the backward (after ``opt.prepare``): open the overlapped exchange."""
+        if self.overlap:
+            self.comm.begin_step(self.opt)
 
     def _update(self) -> None:
         """Gradient reduction + optimizer update (device work only; capturable)."""
@@ -169,8 +195,9 @@ class Trainer:
             self.opt.apply()
 
     def _eager_device_step(self, tokens, targets, mask=None) -> torch.Tensor:
-        loss = self.compute_grads(tokens, targets, mask)
         self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
+        self._begin_update()
+        loss = self.compute_grads(tokens, targets, mask)
         self._update()
         self.step_idx += 1
         return loss
@@ -189,7 +216,8 @@ class Trainer:
                 total = li if total is None else total + li
             return total
         if self.fused:
-            return self.model.fused_step(tokens, targets, mask)
+            return self.model.fused_step(tokens, targets, mask,
+                                         grad_ready=self._grad_ready if self.overlap else None)
         self.model.zero_grad(set_to_none=False)
         loss = self.model.loss(tokens, targets, mask)
         grads = torch.autograd.grad(loss, [p for p in self.model.parameters()], allow_unused=True)
@@ -248,8 +276,9 @@ class Trainer:
         targets = targets.to(self.device, non_blocking=True)
         if mask is not None:
             mask = mask.to(self.device, non_blocking=True)
-        loss = self.compute_grads(tokens, targets, mask)
         self.opt.prepare(lr_at(self.step_idx, self.base_lr, self.lr_schedule, self.max_iters))
+        self._begin_update()
+        loss = self.compute_grads(tokens, targets, mask)
         self._update()
         self.step_idx += 1
         return loss

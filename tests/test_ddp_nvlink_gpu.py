@@ -36,14 +36,20 @@ def _worker(rank, world, port, out):
     batches = [(torch.randint(0, 256, (2, 128), generator=g), torch.randint(0, 256, (2, 128), generator=g))
                for _ in range(3)]
     res = {}
-    for comm in ("nccl", "nvlink"):
-        tr = Trainer(cfg, dev, lr=1e-3, seed=3, comm=comm)
+    arms = [("nccl", "nccl", None, "bf16"), ("nvlink_fp32", "nvlink", None, "fp32"), ("nvlink", "nvlink", None, "bf16"),
+            ("nccl_clip", "nccl", 0.05, "bf16"), ("nvlink_clip", "nvlink", 0.05, "bf16")]
+    for name, comm, clip, gdt in arms:
+        os.environ["BDH_DDP_GRAD_DTYPE"] = gdt
+        tr = Trainer(cfg, dev, lr=1e-3, seed=3, comm=comm, grad_clip_norm=clip)
         for x, y in batches:
             tr.step(x.to(dev), y.to(dev))
         torch.cuda.synchronize()
         if tr.comm is not None:
             tr.comm.check()
-        res[comm] = tr.model.store.data[:tr.model.store.numel].cpu().clone()
+        tr.sync_params()  # the NVLink step keeps the fp32 master sharded
+        res[name] = tr.model.store.data[:tr.model.store.numel].cpu().clone()
+        res[name + "_norm"] = float(tr.opt.grad_norm()) if clip else 0.0
+        res[name + "_shadow"] = tr.model.store.shadow[:tr.model.store.numel].float().cpu().clone()
         if tr.comm is not None:
             tr.comm.close()
     out[rank] = res
@@ -56,5 +62,16 @@ def test_nvlink_step_matches_nccl_step():
     out = mp.Manager().dict()
     mp.spawn(_worker, args=(2, _port(), out), nprocs=2, join=True)
     a, b = out[0], out[1]
-    assert torch.equal(a["nvlink"], b["nvlink"])  # replicas identical
-    assert torch.allclose(a["nvlink"], a["nccl"], atol=1e-6, rtol=1e-5)
+    for arm in ("nvlink", "nvlink_fp32", "nvlink_clip"):
+        assert torch.equal(a[arm], b[arm])  # replicas identical after the master all-gather
+        assert torch.equal(a[arm + "_shadow"], b[arm + "_shadow"])
+        assert torch.equal(a[arm + "_shadow"], a[arm].bfloat16().float())  # shadow = bf16(master)
+    # fp32 transport: the same sums as NCCL up to summation order
+    assert torch.allclose(a["nvlink_fp32"], a["nccl"], atol=1e-6, rtol=1e-5)
+    # bf16 transport: each rank's gradient rounded to bf16 before the fp32 sum; AdamW's
+    # normalised update moves a weight by at most ~lr per step, so the drift stays far
+    # below lr * steps
+    assert (a["nvlink"] - a["nccl"]).abs().max().item() < 2e-4
+    # global-norm clipping: same norm, same clipped update
+    assert abs(a["nvlink_clip_norm"] - a["nccl_clip_norm"]) < 1e-2 * a["nccl_clip_norm"]
+    assert (a["nvlink_clip"] - a["nccl_clip"]).abs().max().item() < 2e-4

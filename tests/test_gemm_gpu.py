@@ -116,7 +116,7 @@ def test_cta_pair_causal_scores():
     assert torch.equal(outs[0], outs[1])
 
 
-def _tma_case(case, B=2, T=256, D=64, H=2, Nh=512, seed=0):
+def _tma_case(case, B=2, T=256, D=64, H=2, Nh=512, seed=0, table=False):
     """Operands of one TMA-epilogue BDH contraction (the layouts of the fused step) and a
     call that runs it with a given tile N; returns (call, outputs)."""
     G = _ops()
@@ -125,12 +125,13 @@ def _tma_case(case, B=2, T=256, D=64, H=2, Nh=512, seed=0):
     r = lambda *s: (torch.randn(*s, device="cuda", generator=g) * 0.5).bfloat16()  # noqa: E731
     N, M = H * Nh, B * T
     freq = torch.rand(Nh, device="cuda", generator=g) * 0.1
+    tab = G.rope_table(freq, 0, T) if table else None
     if case == "xproj":
         v, enc = r(M, D), r(H, D, Nh)
         outs = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
         call = lambda bn: G.gemm(G.EPI_RELU_ROPE, Op(v, False, D, M, D), Op(enc, True, Nh, D, Nh, z1=(H, D * Nh)),  # noqa: E731
                                  M, Nh, D, outs[0], Z1=H, bn=bn, out1=outs[1], ld=N, sz1=Nh, thr=0.1, freq=freq, T=T,
-                                 Nh=Nh)
+                                 Nh=Nh, rope_tab=tab)
     elif case == "gate":
         an, encv, x = r(M, H, D), r(H, D, Nh), torch.relu(r(M, N).float()).bfloat16()
         outs = [torch.empty(M, N, device="cuda", dtype=torch.bfloat16)]
@@ -154,7 +155,7 @@ def _tma_case(case, B=2, T=256, D=64, H=2, Nh=512, seed=0):
             outs[0].copy_(dx0)
             G.gemm(G.EPI_DQ, Op(g16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
                    Op(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, outs[0], Z1=H, Z2=B, bn=bn,
-                   aux0=outs[0], ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh)
+                   aux0=outs[0], ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh, rope_tab=tab)
     return call, outs
 
 
@@ -174,3 +175,18 @@ def test_tma_epilogue_pair256_matches_single_cta128(case):
         _close(got, r, tol=1e-2)
         # the masked (-0.0) / zero pattern is identical
         assert torch.equal(got == 0, r == 0)
+
+
+@pytest.mark.parametrize("case", ["xproj", "dq"])
+def test_rope_table_matches_evaluated_phases(case):
+    """The half2 (cos, sin) table path of the RoPE epilogues against the per-element
+    evaluation of the same phases (fp16 phase values: agreement to the bf16 output)."""
+    G = _ops()
+    c0, o0 = _tma_case(case, table=False)
+    c1, o1 = _tma_case(case, table=True)
+    c0(256)
+    c1(256)
+    torch.cuda.synchronize()
+    G.check_errors(torch.device("cuda"))
+    for a, b in zip(o0, o1):
+        _close(b, a.float(), tol=1e-2)
