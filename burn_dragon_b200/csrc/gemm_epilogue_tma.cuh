@@ -183,17 +183,25 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
       return decode_tile(p, t, BN);
     }
   };
-  // Per-buffer issue / wait counters keep the mbarrier parities exact (uniform across
-  // the warp; only lane 0 issues).
-  int n_issued[3] = {0, 0, 0}, n_waited[3] = {0, 0, 0};
+  // Unit u (a chunk of a tile) uses aux buffer u % NBUF for the (u / NBUF)-th time, so its
+  // mbarrier parity is (u / NBUF) & 1; `issued_upto` / `waited_upto` (uniform across the
+  // warp; only lane 0 issues) bound the loads still landing when the loop ends early.
+  int issued_upto = -1, waited_upto = -1;
   // aux fetch of chunk c of tile t into buffer b (no zero tiles in these modes)
-  const bool probe = p.e.probe != 0;
-  auto issue_aux = [&](int t, int c, int b) {
+  // measurement switches (BDH_GEMM_PROBE bits): 1 = read and release the accumulator
+  // only; 2 = store the results with coalesced st.global from the staging tile instead
+  // of TMA; 4 = load the aux tiles with coalesced ld.global at use instead of TMA
+  // prefetch (2 and 4 apply to the 64-column kinds)
+  const bool probe = (p.e.probe & 1) != 0;
+  const bool dstore = CW == 64 && (p.e.probe & 2) != 0;
+  const bool dload = CW == 64 && (p.e.probe & 4) != 0;
+  auto issue_aux = [&](int t, int c, int u) {
     if constexpr (NAUX > 0) {
-      if (t >= total || probe) return;
+      if (t >= total || probe || dload) return;
       const TileCoord n = tile(t);
       if (n.zero) return;
-      ++n_issued[b];
+      issued_upto = u;
+      const int b = u % NBUF;
       if (lane != 0) return;
       uint8_t* dst = wbuf + b * TENS * kTmaTileBytes;
       const int col = n.n0 + grp_off + c * CW;
@@ -204,7 +212,7 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
         tma_load_4d(dst + kTmaTileBytes, &p.tx1, &aux_bar[ew][b], col, n.m0 + quad * 32, n.z1, n.z2);
     }
   };
-  issue_aux(t0, 0, 0);
+  issue_aux(t0, 0, 0);  // unit 0
   int acc = 0;
   uint32_t acc_phase = 0;
   int it = 0;
@@ -215,7 +223,6 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
 #pragma unroll 1
     for (int c = 0; c < CH; ++c, ++it) {
       const int b = it % NBUF;
-      const int bn = (it + 1) % NBUF;
       uint8_t* b0 = wbuf + b * TENS * kTmaTileBytes;
       uint8_t* b1 = TENS > 1 ? b0 + kTmaTileBytes : b0;
       // the next buffer was last read by this warp's stores NBUF - 1 units ago; with no
@@ -229,9 +236,9 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
       }
       __syncwarp();
       if (c + 1 < CH)
-        issue_aux(t, c + 1, bn);
+        issue_aux(t, c + 1, it + 1);
       else
-        issue_aux(t + tstep, 0, bn);
+        issue_aux(t + tstep, 0, it + 1);
       if (c == 0) {
         if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, abort_flag, p.err, kErrTimeoutEpilogue)) {
           ok = false;
@@ -264,14 +271,32 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
         if (v[0] == 1.2345e-30f && p.e.alpha == -7.0f) *reinterpret_cast<float*>(p.e.out0) = v[1];
         continue;
       }
+      const long long goff = (long long)tc.z2 * p.e.sz2 + (long long)tc.z1 * p.e.sz1 +
+                             (long long)(tc.m0 + quad * 32) * p.e.ld + tc.n0 + col_off;
+      const int rows_ok = min(32, p.M - (tc.m0 + quad * 32)), cols_ok = min(CW, p.N - (tc.n0 + col_off));
       if constexpr (NAUX > 0) {
-        if (!mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, abort_flag, p.err, kErrTimeoutEpilogue)) {
-          ok = false;
-          break;
+        if (dload) {
+          coop_load(p.e.aux0 + goff, p.e.ld, rows_ok, cols_ok, b0, lane);
+          if constexpr (NAUX > 1) coop_load(p.e.aux1 + goff, p.e.ld, rows_ok, cols_ok, b1, lane);
+          __syncwarp();
+        } else {
+          if (!mbar_wait_bounded(&aux_bar[ew][b], (uint32_t)((it / NBUF) & 1), abort_flag, p.err,
+                                 kErrTimeoutEpilogue)) {
+            ok = false;
+            break;
+          }
+          waited_upto = it;
         }
-        ++n_waited[b];
       }
       tma_epi_math<EPI, CW>(p, tc, v, tc.m0 + r_local, tc.n0 + col_off, b0, b1, lane);
+      if (dstore) {
+        __syncwarp();
+        coop_store(reinterpret_cast<__nv_bfloat16*>(p.e.out0) + goff, p.e.ld, rows_ok, cols_ok, b0, lane);
+        if (EPI == EPI_DEC_BWD)
+          coop_store(reinterpret_cast<__nv_bfloat16*>(p.e.out1) + goff, p.e.ld, rows_ok, cols_ok, b1, lane);
+        __syncwarp();
+        continue;
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -287,11 +312,9 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
     bulk_wait_group0();
     // On an abort, loads may still be landing in smem: wait for them (bounded).
     int dummy_abort = 0;
-    for (int b = 0; b < NBUF; ++b)
-      while (n_waited[b] < n_issued[b]) {
-        mbar_wait_bounded(&aux_bar[ew][b], n_waited[b] & 1, (volatile int*)&dummy_abort, p.err, kErrTimeoutDrain);
-        ++n_waited[b];
-      }
+    for (int u = waited_upto + 1; u <= issued_upto; ++u)
+      mbar_wait_bounded(&aux_bar[ew][u % NBUF], (uint32_t)((u / NBUF) & 1), (volatile int*)&dummy_abort, p.err,
+                        kErrTimeoutDrain);
   }
   __syncwarp();
 }

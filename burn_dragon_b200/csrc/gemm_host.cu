@@ -239,7 +239,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
     TORCH_CHECK(bn == 128 || bn == 256, "TMA-epilogue modes use tile N = 128 or 256");
     TORCH_CHECK(!causal_skip, "TMA-epilogue modes have no zero tiles");
     // columns per epilogue chunk: 32 for the 16-warp x-projection epilogue, else 64
-    const uint32_t cw = epi == EPI_RELU_ROPE ? 32 : 64;
+    const uint32_t cw = (epi == EPI_RELU_ROPE || bn == 256) ? 32 : 64;
     p.to0 = encode_out_map(e.out0, N, M, ld, Z1, sz1, Z2, sz2, cw);
     if (e.out1) p.to1 = encode_out_map(e.out1, N, M, ld, Z1, sz1, Z2, sz2, cw);
     if (e.aux0) p.tx0 = encode_out_map(e.aux0, N, M, ld, Z1, sz1, Z2, sz2, cw);

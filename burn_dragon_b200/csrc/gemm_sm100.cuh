@@ -108,7 +108,7 @@ constexpr int epi_kind() {
 // Epilogue warps of the TMA kinds: 16 (four per TMEM lane quadrant, 32-column chunks)
 // for the x-projection, else 8 (64-column chunks). (16 warps on 256-wide tiles measured
 // slower at BDH-GPU batch 32: twice the TMA operations of half the size.)
-constexpr int tma_nepi(int KIND, int BN) { return KIND == 3 ? 16 : 8; }
+constexpr int tma_nepi(int KIND, int BN) { return (KIND == 3 || (KIND >= 2 && BN == 256)) ? 16 : 8; }
 
 template <int BN, int KIND = 0>
 struct GemmCfg {
@@ -183,11 +183,11 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float (&v
 
 // cos/sin of the RoPE phase 2*pi*frac(pos*freq) (phase wrapped as in
 // burn_dragon_core/src/model/attention.rs:540-550), evaluated with CUDA's __sincosf on
-// the argument reduced to [-pi, pi).
+// the argument reduced to [-pi, pi]: raw - rint(raw) is the phase in revolutions, already
+// centred (one rounding instruction in place of floor, compare and subtract).
 __device__ __forceinline__ void rope_cs(float pos, float freq, float& c, float& s) {
-  float raw = pos * freq;
-  float ph = (raw - floorf(raw)) * 6.283185307179586f;
-  if (ph > 3.14159265358979f) ph -= 6.283185307179586f;
+  const float raw = pos * freq;
+  const float ph = (raw - rintf(raw)) * 6.283185307179586f;
   __sincosf(ph, &s, &c);
 }
 

@@ -430,7 +430,8 @@ class FusedBDH:
             # dx_pre = (dx_part + rope^T(G q)) * [x > 0]   (in place over dx_part, which
             # carries the x <= 0 mask as -0.0 from the decoder backward)
             G.gemm(G.EPI_DQ, Operand(ws.G16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
-                   Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B, bn=G.tma_bn(T, Nh),
+                   Operand(ws.q16[l], True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, ws.dx16, Z1=H, Z2=B,
+                   bn=G.tma_bn(T, Nh, "dq"),
                    aux0=ws.dx16, ld=N, sz1=Nh, sz2=T * N, freq=ws.freq, pos0=pos0, T=T, Nh=Nh,
                    rope_tab=ws.rope_tab(pos0))
             if ws.has_rho0:

@@ -58,7 +58,7 @@ def build(case: str, B: int, T: int, D: int, H: int, Nh: int):
     if case == "dq":
         g16, q, dx = r(B, H, T, T), r(M, N), r(M, N)
         call = lambda: G.gemm(G.EPI_DQ, Operand(g16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),  # noqa: E731
-                              Operand(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B, bn=G.tma_bn(T, Nh),
+                              Operand(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B, bn=G.tma_bn(T, Nh, "dq"),
                               aux0=dx, ld=N, sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh, rope_tab=tab)
         return call, 2 * B * H * T * T * Nh, (B * H * T * T + 3 * M * N) * 2
     if case == "wgrad":

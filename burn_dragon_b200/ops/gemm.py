@@ -59,15 +59,19 @@ def check_errors(device: torch.device) -> None:
 
 
 # Tile N of the TMA-epilogue modes (x-projection, gate, decoder backward, dQ): 128 runs
-# the 1-CTA 128 x 128 kernel; 256 runs CTA pairs with 256 x 256 tiles where M >= 256
-# (their mainloops are about twice as fast, but at BDH-GPU batch 32 the epilogue bounds
-# both and the pair measured 2-15% slower, so 128 is the default).
-TMA_BN = int(os.environ.get("BDH_TMA_BN", "128"))
+# the 1-CTA 128 x 128 kernel, 256 a CTA pair with 256 x 256 tiles and 16 epilogue warps
+# (where M >= 256). Measured at BDH-GPU batch 32 (CUDA events): the pair's mainloop is
+# about twice as fast, which pays for dQ (K = T = 512: 841 vs 895 us) but not for the
+# K = 256 modes, whose epilogues bound both (x-projection 596 vs 587, gate 539 vs 476,
+# decoder backward 1190 vs 880 us). ``BDH_TMA_BN`` = 128 / 256 forces one tile for all.
+TMA_BN = os.environ.get("BDH_TMA_BN")
+_TMA_BN_DEFAULT = {"dq": 256}
 
 
-def tma_bn(M: int, N: int) -> int:
+def tma_bn(M: int, N: int, mode: str = "") -> int:
     """Tile N for a TMA-epilogue GEMM of M x N outputs (per batch matrix)."""
-    if TMA_BN == 256 and PAIR and M >= 256 and N % 256 == 0:
+    want = int(TMA_BN) if TMA_BN else _TMA_BN_DEFAULT.get(mode, 128)
+    if want == 256 and PAIR and M >= 256 and N % 256 == 0:
         return 256
     return 128
 

@@ -265,33 +265,49 @@ class PipelineRunner:
             self.stage.first_backward = True
         else:
             self.model.store.grad.zero_()
-        outs: dict[int, torch.Tensor] = {}
         losses = []
         sends = []
-        for kind, mb, _ in self.plan.events[self.rank]:
+        events = self.plan.events[self.rank]
+        pending: dict[int, tuple] = {}
+
+        def post_recv(k: int) -> None:
+            # The activation (F) or gradient (B) this event consumes, received without
+            # blocking the host: the wait is a stream dependency, so the host keeps
+            # enqueueing and the transfer overlaps the compute already queued. Posted only
+            # after the previous event's send, which keeps every rank pair's NCCL
+            # operations in the same order on both sides.
+            if k >= len(events) or k in pending:
+                return
+            kind = events[k][0]
+            if kind == "F" and not self.first:
+                buf = torch.empty(b, T, self.D, device=dev)
+                pending[k] = (dist.irecv(buf, src=self.ranks[self.rank - 1], group=self.group), buf)
+            elif kind != "F" and not self.last:
+                buf = torch.empty(b, T, self.D, device=dev)
+                pending[k] = (dist.irecv(buf, src=self.ranks[self.rank + 1], group=self.group), buf)
+
+        post_recv(0)
+        for k, (kind, mb, _) in enumerate(events):
             sl = slice(mb * b, (mb + 1) * b)
+            got = None
+            if k in pending:
+                work, got = pending.pop(k)
+                work.wait()
             if kind == "F":
-                v_in = None
-                if not self.first:
-                    v_in = torch.empty(b, T, self.D, device=dev)
-                    dist.recv(v_in, src=self.ranks[self.rank - 1], group=self.group)
                 if isinstance(self.stage, FusedStage):
                     self.stage._tokens[mb] = tokens[sl]
-                v_out, loss = self.stage.forward(mb, tokens[sl], targets[sl], v_in, 1.0 / m)
+                v_out, loss = self.stage.forward(mb, tokens[sl], targets[sl], got, 1.0 / m)
                 if loss is not None:
                     losses.append(loss)
                 if not self.last:
                     buf = v_out.reshape(b, T, self.D).clone()  # the workspace slot is reused
                     sends.append((dist.isend(buf, dst=self.ranks[self.rank + 1], group=self.group), buf))
             else:
-                dv_out = None
-                if not self.last:
-                    dv_out = torch.empty(b, T, self.D, device=dev)
-                    dist.recv(dv_out, src=self.ranks[self.rank + 1], group=self.group)
-                dv_in = self.stage.backward(mb, dv_out)
+                dv_in = self.stage.backward(mb, got)
                 if not self.first:
                     buf = dv_in.reshape(b, T, self.D).clone()
                     sends.append((dist.isend(buf, dst=self.ranks[self.rank - 1], group=self.group), buf))
+            post_recv(k + 1)
         for h, _ in sends:
             h.wait()
         dist.all_reduce(self.model.store.grad, group=self.group)

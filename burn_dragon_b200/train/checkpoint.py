@@ -367,16 +367,18 @@ class RunDir:
         return old if os.path.exists(old) else new
 
     def save(self, step: int, model, optimizer=None, scheduler: dict | None = None, runtime: dict | None = None,
-             keep_last: int = 2, best_step: int | None = None, extra: dict | None = None, teacher=None) -> None:
+             keep_last: int = 2, best_step: int | None = None, extra: dict | None = None, teacher=None,
+             sharded: bool = False) -> None:
         """``extra``: further named tensors (the optional modules of ``DragonRuntime`` and
-        their optimizer moments), stored as ``extra-<step>.bin``."""
+        their optimizer moments), stored as ``extra-<step>.bpk``. ``sharded``: the model
+        and optimizer records were written per rank by ``save_shard``; write the rest."""
         from ..models.bdh import record_name
 
         self.wait()
         snap = _host_copy if self.async_write else (lambda t: t.detach())
-        params = {record_name(n): snap(t) for n, t in model.store.views(model.store.data).items()}
+        params = {} if sharded else {record_name(n): snap(t) for n, t in model.store.views(model.store.data).items()}
         optim = None
-        if optimizer is not None:
+        if optimizer is not None and not sharded:
             optim = ({"m": snap(optimizer.m), "v": snap(optimizer.v)}, {"t": optimizer.t, "lr": optimizer.lr})
         rt = meta = None
         if runtime is not None:
@@ -392,8 +394,9 @@ class RunDir:
         scheduler = dict(scheduler or {})
 
         def write():
-            save_tensors(self._p("model", step, True), params, {"schema_version": SCHEMA_VERSION, "step": step})
-            if optim is not None:
+            if not sharded:
+                save_tensors(self._p("model", step, True), params, {"schema_version": SCHEMA_VERSION, "step": step})
+            if optim is not None and not sharded:
                 save_tensors(self._p("optim", step, True), *optim)
             with open(self._p("scheduler", step), "w") as f:
                 json.dump(scheduler, f)
@@ -420,10 +423,61 @@ class RunDir:
         self._writer = threading.Thread(target=run, name=f"checkpoint-{step}", daemon=False)
         self._writer.start()
 
+    # ---- sharded records (``[parallel.checkpoint] format = "sharded_v2"``)
+    def save_shard(self, step: int, rank: int, world: int, slices: list[tuple[int, int]], master: torch.Tensor,
+                   m: torch.Tensor, v: torch.Tensor, numel: int, t: int) -> None:
+        """One data-parallel rank's record of its own slices of the flat store: the fp32
+        master and both AdamW moments (``model-<step>.shard-<r>-of-<W>.bpk``). Every rank
+        writes its own file, in parallel, without gathering anything; ``load`` assembles
+        them for any world size."""
+        self.wait()
+        vals = master.detach().reshape(-1)
+        take = torch.cat([vals[a:b] for a, b in slices]) if slices else vals[:0]
+        meta = {"schema_version": SCHEMA_VERSION, "step": step, "rank": rank, "world": world, "numel": numel,
+                "t": t, "slices": [[int(a), int(b)] for a, b in slices]}
+        save_tensors(os.path.join(self.ckpt, f"model-{step}.shard-{rank}-of-{world}{RECORD_EXT}"),
+                     {"master": take, "m": m.detach().reshape(-1)[:take.numel()],
+                      "v": v.detach().reshape(-1)[:take.numel()]}, meta)
+
+    def shard_files(self, step: int) -> list[str]:
+        pat = re.compile(rf"model-{step}\.shard-(\d+)-of-(\d+)\.bpk")
+        return sorted((os.path.join(self.ckpt, fn) for fn in os.listdir(self.ckpt) if pat.fullmatch(fn)))
+
+    def load_shards(self, step: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, int] | None:
+        """(master, m, v, optimizer step) assembled from every shard file of ``step``, or
+        None when the step has none. Checks that the shards cover the store exactly."""
+        files = self.shard_files(step)
+        if not files:
+            return None
+        full = mm = vv = None
+        covered = 0
+        t = 0
+        worlds = set()
+        for f in files:
+            ten, meta = load_tensors(f)
+            worlds.add(int(meta["world"]))
+            n = int(meta["numel"])
+            if full is None:
+                full, mm, vv = torch.zeros(n), torch.zeros(n), torch.zeros(n)
+            off = 0
+            for a, b in meta["slices"]:
+                k = b - a
+                full[a:b] = ten["master"][off:off + k]
+                mm[a:b] = ten["m"][off:off + k]
+                vv[a:b] = ten["v"][off:off + k]
+                off += k
+                covered += k
+            t = int(meta["t"])
+        if len(worlds) != 1 or len(files) != next(iter(worlds)):
+            raise ValueError(f"checkpoint step {step}: incomplete shard set {files}")
+        if covered != full.numel():
+            raise ValueError(f"checkpoint step {step}: shards cover {covered} of {full.numel()} elements")
+        return full, mm, vv, t
+
     def steps(self) -> list[int]:
         out = []
         for fn in os.listdir(self.ckpt):
-            m = re.fullmatch(r"model-(\d+)\.(?:bin|bpk)", fn)
+            m = re.fullmatch(r"model-(\d+)(?:\.shard-0-of-\d+)?\.(?:bin|bpk)", fn)
             if m:
                 out.append(int(m.group(1)))
         return sorted(set(out))
@@ -446,6 +500,8 @@ class RunDir:
                     p = os.path.join(self.ckpt, f"{kind}-{s}{ext}")
                     if os.path.exists(p):
                         os.remove(p)
+            for p in self.shard_files(s):
+                os.remove(p)
 
     def load_teacher(self, step: int, teacher) -> bool:
         """Restore an EMA teacher saved with ``save(..., teacher=)``; False if absent."""
@@ -466,18 +522,32 @@ class RunDir:
         step = self.latest() if step is None else step
         if step is None:
             raise FileNotFoundError(f"no checkpoint in {self.ckpt}")
-        tensors, meta = load_tensors(self._p("model", step))
-        if int(meta.get("schema_version", SCHEMA_VERSION)) != SCHEMA_VERSION:
-            raise ValueError("checkpoint schema version mismatch")
-        views = model.store.views(model.store.data)
-        with torch.no_grad():
-            for n, v in views.items():
-                src = tensors[record_name(n)]
-                if tuple(src.shape) != tuple(v.shape):
-                    raise ValueError(f"{record_name(n)}: checkpoint shape {tuple(src.shape)} != {tuple(v.shape)}")
-                v.copy_(src.to(v.device, v.dtype))
-        model.store.refresh_shadow()
-        if optimizer is not None and os.path.exists(self._p("optim", step)):
+        shards = None if os.path.exists(self._p("model", step)) else self.load_shards(step)
+        if shards is not None:
+            full, mm, vv, t = shards
+            n = model.store.numel
+            if full.numel() < n:
+                raise ValueError(f"sharded checkpoint holds {full.numel()} elements, the model {n}")
+            with torch.no_grad():
+                model.store.data[:n].copy_(full[:n].to(model.store.data.device))
+            model.store.refresh_shadow()
+            if optimizer is not None:
+                optimizer.m[:n].copy_(mm[:n].to(optimizer.m.device))
+                optimizer.v[:n].copy_(vv[:n].to(optimizer.v.device))
+                optimizer.t = t
+        else:
+            tensors, meta = load_tensors(self._p("model", step))
+            if int(meta.get("schema_version", SCHEMA_VERSION)) != SCHEMA_VERSION:
+                raise ValueError("checkpoint schema version mismatch")
+            views = model.store.views(model.store.data)
+            with torch.no_grad():
+                for n, v in views.items():
+                    src = tensors[record_name(n)]
+                    if tuple(src.shape) != tuple(v.shape):
+                        raise ValueError(f"{record_name(n)}: checkpoint shape {tuple(src.shape)} != {tuple(v.shape)}")
+                    v.copy_(src.to(v.device, v.dtype))
+            model.store.refresh_shadow()
+        if shards is None and optimizer is not None and os.path.exists(self._p("optim", step)):
             o, ometa = load_tensors(self._p("optim", step))
             optimizer.m.copy_(o["m"].to(optimizer.m.device))
             optimizer.v.copy_(o["v"].to(optimizer.v.device))

@@ -54,8 +54,9 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     mode = cfg.parallel.mode
     torch.manual_seed(t.seed + rank)
     ck = cfg.parallel.checkpoint or {}
-    if ck.get("format", "unsharded_v1") != "unsharded_v1":
-        raise ValueError("parallel.checkpoint.format: checkpoints are written unsharded by rank 0 (unsharded_v1)")
+    ck_format = ck.get("format", "unsharded_v1")
+    if ck_format not in ("unsharded_v1", "sharded_v2"):
+        raise ValueError(f"parallel.checkpoint.format {ck_format!r}: unsharded_v1 or sharded_v2")
     lm = t.launch_mode
     if lm in ("fresh", "init_from_checkpoint"):
         resume = False
@@ -257,6 +258,8 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                         device=dev)
         start = info["step"]
         trainer.step_idx = start
+        if hasattr(trainer, "after_load"):
+            trainer.after_load()
         if extended and info.get("extra"):
             trainer.load_extra_state(info["extra"])
         rt = info.get("runtime")
@@ -568,22 +571,24 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                             run.write_json("neuron_scaling.json", {
                                 "mlp_internal_dim_multiplier": trainer.model.cfg.mlp_internal_dim_multiplier,
                                 "events": scaler.events, "step": step + 1})
-            if t.checkpoint_interval_iters and (step + 1) % t.checkpoint_interval_iters == 0 \
-                    and hasattr(trainer, "sync_params"):
+            ck_now = bool(t.checkpoint_interval_iters) and (step + 1) % t.checkpoint_interval_iters == 0
+            sharded = ck_now and _save_shards(run, trainer, step + 1, ck_format, extended)
+            if ck_now and not sharded and hasattr(trainer, "sync_params"):
                 trainer.sync_params()  # every rank: gathers sharded master / moments
-            if t.checkpoint_interval_iters and (step + 1) % t.checkpoint_interval_iters == 0 and rank == 0:
+            if ck_now and rank == 0:
                 rt = None
                 if state is not None and not extended and state.rhos is not None:
                     rt = {"position": state.position, "rhos": [r.detach() for r in state.rhos]}
                 elif state is not None and extended:
                     rt = {"position": state.position, "state_tensors": state.to_tensors()}
                 run.save(step + 1, trainer.core if extended else trainer.model, trainer.opt, {"step": step + 1}, rt,
-                         extra=trainer.extra_state() if extended else None, teacher=_teacher())
-        if t.checkpoint_interval_iters and hasattr(trainer, "sync_params"):
+                         extra=trainer.extra_state() if extended else None, teacher=_teacher(), sharded=sharded)
+        sharded = bool(t.checkpoint_interval_iters) and _save_shards(run, trainer, t.max_iters, ck_format, extended)
+        if t.checkpoint_interval_iters and not sharded and hasattr(trainer, "sync_params"):
             trainer.sync_params()
         if rank == 0 and t.checkpoint_interval_iters:
             run.save(t.max_iters, trainer.core if extended else trainer.model, trainer.opt, {"step": t.max_iters},
-                     extra=trainer.extra_state() if extended else None, teacher=_teacher())
+                     extra=trainer.extra_state() if extended else None, teacher=_teacher(), sharded=sharded)
     except PeerFailure:
         if hb is not None:
             hb.stop()
@@ -597,6 +602,22 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     summary = prof.summary() if prof.enabled else {}
     run.wait()
     return {"final_loss": last_loss, "steps": t.max_iters - start, "run_dir": run.path, "profile": summary}
+
+
+def _save_shards(run, trainer, step: int, ck_format: str, extended: bool) -> bool:
+    """``sharded_v2``: every data-parallel rank writes its own slices of the fp32 master and
+    AdamW moments (no gather); returns True when it did (the other records follow from
+    rank 0). Falls back to the unsharded records for trainers without the flat DP layout."""
+    if ck_format != "sharded_v2" or extended or not hasattr(trainer, "dp_shard") or trainer.tp is not None:
+        return False
+    world = trainer.world if trainer.comm is not None else 1
+    rank = trainer.comm.rank if trainer.comm is not None else 0
+    if trainer.comm is not None or (not dist.is_initialized() or dist.get_rank() == 0):
+        slices, master, m, v = trainer.dp_shard()
+        run.save_shard(step, rank, world, slices, master, m, v, trainer.model.store.numel, trainer.opt.t)
+    if dist.is_initialized():
+        dist.barrier()
+    return True
 
 
 def _autograd_step(trainer, loss) -> None:

@@ -148,6 +148,28 @@ class Trainer:
         self.comm.sync_master()
         self.comm.gather_moments(self.opt.m, self.opt.v)
 
+    def dp_shard(self) -> tuple[list[tuple[int, int]], torch.Tensor, torch.Tensor, torch.Tensor]:
+        """This rank's slices of the flat store with the fp32 master and the AdamW moments of
+        those slices (concatenated in slice order): the sharded checkpoint record."""
+        if self.comm is None:
+            n = self.model.store.numel
+            return [(0, n)], self.model.store.data, self.opt.m, self.opt.v
+        sl = [(b["lo"], b["hi"]) for b in self.comm.buckets if b["hi"] > b["lo"]]
+        return sl, self.comm.param, self.comm.m, self.comm.v
+
+    def after_load(self) -> None:
+        """After a checkpoint load into the model and the full optimizer moments: hand this
+        rank's slices of the moments to the NVLink communicator."""
+        if self.comm is None:
+            return
+        for b in self.comm.buckets:
+            lo, hi, mo = b["lo"], b["hi"], b["moff"]
+            n = min(hi, self.opt.m.numel()) - lo
+            if n > 0:
+                self.comm.m[mo:mo + n].copy_(self.opt.m[lo:lo + n])
+                self.comm.v[mo:mo + n].copy_(self.opt.v[lo:lo + n])
+        self.comm.master_synced = True
+
     def enable_cuda_graph(self, tokens: torch.Tensor, targets: torch.Tensor, warmup: int = 2) -> None:
         """Capture forward + backward + all-reduce + AdamW of one step into a CUDA graph.
 

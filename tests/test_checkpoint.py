@@ -224,3 +224,34 @@ def test_model_burnpack_export_and_load(tmp_path):
     m3 = BDH(cfg, seed=3)
     assert C.load_model_burnpack(m3, str(tmp_path / "deploy.bpk"), prefer_f16=True) == f16
     assert torch.allclose(m3.store.data, m1.store.data, atol=1e-3)
+
+
+def test_sharded_v2_records_reassemble_for_any_world(tmp_path):
+    """Two ranks each write their own slices of master / moments (sharded_v2); a load
+    assembles the full store and moments, and refuses an incomplete shard set."""
+    import pytest
+
+    cfg = _cfg()
+    model = BDH(cfg, seed=3)
+    opt = FusedAdamW(model.store, lr=1e-2)
+    n = model.store.numel
+    opt.m.copy_(torch.randn(n))
+    opt.v.copy_(torch.rand(n))
+    opt.t = 5
+    run = C.RunDir(str(tmp_path / "r"))
+    # rank r owns two interleaved slices (the NVLink step's per-bucket layout)
+    half, q = n // 2, n // 4
+    owned = {0: [(0, q), (half, half + q)], 1: [(q, half), (half + q, n)]}
+    for r, sl in owned.items():
+        cat = lambda t: torch.cat([t[a:b] for a, b in sl])  # noqa: E731
+        run.save_shard(4, r, 2, sl, model.store.data, cat(opt.m), cat(opt.v), n, opt.t)
+    run.save(4, model, opt, {"step": 4}, sharded=True)
+    assert run.latest() == 4 and run.steps() == [4]
+    m2 = BDH(cfg, seed=99)
+    o2 = FusedAdamW(m2.store, lr=1e-2)
+    run.load(None, m2, o2)
+    assert torch.equal(m2.store.data, model.store.data)
+    assert torch.equal(o2.m, opt.m) and torch.equal(o2.v, opt.v) and o2.t == 5
+    os.remove(run.shard_files(4)[1])
+    with pytest.raises(ValueError):
+        run.load(4, m2, o2)

@@ -151,3 +151,20 @@ def test_train_shorthand_flags(tmp_path, monkeypatch, capsys):
     assert tc["training"]["seed"] == 7 and tc["model"]["n_layer"] == 1
     assert tc["training"]["batch_size"] == 2 and tc["training"]["block_size"] == 16
     assert tc["model"]["mlp_internal_dim_multiplier"] * tc["model"]["n_embd"] == 512
+
+
+def test_sharded_v2_checkpoint_run_and_resume(tmp_path, monkeypatch, capsys):
+    """``[parallel.checkpoint] format = "sharded_v2"``: the model / optimizer records are
+    written as per-rank shard files (one rank here) and a resumed run continues from them."""
+    monkeypatch.setenv("BURN_DRAGON_RUN_ROOT", str(tmp_path))
+    args = ["--config", os.path.join(CFG, "tiny_cpu.toml"), "--set", "training.checkpoint_interval_iters=2",
+            "--set", 'parallel.checkpoint={format="sharded_v2"}', "--run-name", "sh"]
+    main(args + ["--set", "training.max_iters=4"])
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    ck = os.path.join(res["run_dir"], "checkpoint")
+    assert os.path.exists(os.path.join(ck, "model-4.shard-0-of-1.bpk"))
+    assert not os.path.exists(os.path.join(ck, "model-4.bpk"))
+    main(args + ["--set", "training.max_iters=6"])
+    res2 = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert res2["steps"] == 2
+    assert os.path.exists(os.path.join(ck, "model-6.shard-0-of-1.bpk"))
