@@ -296,6 +296,9 @@ class DragonConfig:
     mhc_streams: int = 1
     mhc_tau: float = 1.0
     mhc_iters: int = 10
+    # coefficient policy (mhc/config.rs:9-24): "static_sinkhorn" (learned constants) or
+    # "dynamic_positive" (a per-token stream controller)
+    mhc_policy: str = "static_sinkhorn"
     # latent block pattern (kernel/block_sparse.rs): None = dense; otherwise the active
     # latent blocks (of latent_block_size neurons within each head)
     latent_block_size: int = 64
@@ -442,6 +445,8 @@ class DragonConfig:
                              "layer-loop variants")
         if self.residual_connector not in ("vanilla", "mhc", "attention_residual", "block_attention_residual"):
             raise ValueError(f"unknown residual_connector {self.residual_connector!r}")
+        if self.mhc_policy not in ("static_sinkhorn", "dynamic_positive"):
+            raise ValueError(f"unknown mHC coefficient policy {self.mhc_policy!r}")
         self.latent_reasoning.validate()
         ok = {("linear_attention", "reference"), ("linear_attention", "dense_score_short_context"),
               ("mamba3_state_space_duality", "reference"), ("gated_deltanet2", "reference"),
@@ -1153,6 +1158,7 @@ def _model_table(table: dict) -> dict:
         t["mhc_streams"] = int(mhc.get("num_streams", 4))
         t["mhc_tau"] = float(mhc.get("mhc_tau", 1.0))
         t["mhc_iters"] = int(mhc.get("mhc_iters", 10))
+        t["mhc_policy"] = str(mhc.get("coefficient_policy", "static_sinkhorn"))
     sk = t.pop("sequence_kernel", None)
     if isinstance(sk, str):
         sk = {"memory_system": sk}

@@ -62,6 +62,10 @@ def param_shapes(cfg: DragonConfig) -> dict[str, tuple[int, ...]]:
     if cfg.mhc_streams > 1:
         S, L = cfg.mhc_streams, cfg.n_layer
         shapes.update({"mhc_res": (L, S, S), "mhc_pre": (L, 1, S), "mhc_post": (L, 1, S)})
+        if cfg.mhc_policy == "dynamic_positive":
+            from .mhc import dynamic_shapes
+
+            shapes.update(dynamic_shapes(L, S, D))
     return shapes
 
 
@@ -150,7 +154,12 @@ class BDH(nn.Module):
         rs = cfg.random_scaffold
         for name, shp in self.store.shapes.items():
             view = self.store.view(self.store.data, name)
-            if name == "norm_gamma" or name.endswith("_gain"):
+            if name.startswith("mhc_"):
+                from .mhc import init_logits
+
+                view.copy_(init_logits(cfg.n_layer, cfg.mhc_streams, dim=cfg.n_embd,
+                                       dynamic=cfg.mhc_policy == "dynamic_positive")[name])
+            elif name == "norm_gamma" or name.endswith("_gain"):
                 view.fill_(1.0)
             elif name == "norm_alpha":
                 view.fill_(cfg.norm_alpha())
@@ -158,10 +167,6 @@ class BDH(nn.Module):
                 view.fill_(cfg.norm_shift_init)
             elif name == "norm_beta" or name.endswith("_b"):
                 view.zero_()
-            elif name.startswith("mhc_"):
-                from .mhc import init_logits
-
-                view.copy_(init_logits(cfg.n_layer, cfg.mhc_streams)[name])
             elif name.endswith("_a") and rs.enabled:
                 proj = name[:-2]
                 fan_in = shp[-2]
@@ -242,6 +247,7 @@ class BDH(nn.Module):
         d = {n: getattr(self, n) for n in ("embed", "lm_head", "norm_gamma", "norm_beta", "norm_alpha", "norm_shift",
                                            "mhc_res", "mhc_pre", "mhc_post")
              if n in self.store.shapes}
+        d.update({n: getattr(self, n) for n in self.store.shapes if n.startswith("mhc_")})
         if self.scaffold:
             from .scaffold import effective_weight
 

@@ -503,16 +503,19 @@ class DragonRuntime(nn.Module):
         conn = self.connector
         history = [cur] if conn in ("attention_residual", "block_attention_residual") else None
         streams = cfg.mhc_streams if conn == "mhc" else 1
+        dyn = streams > 1 and cfg.mhc_policy == "dynamic_positive"
         if streams > 1:
             from . import mhc as MHC
 
-            Rs = cur[:, None].expand(cur.shape[0], streams, *cur.shape[1:])
+            Rs = MHC.bootstrap(cur, streams, p["mhc_boot"] if dyn else None)
         yrec = cfg.y_neuron_recurrence.enabled
         for li in range(cfg.n_layer):
             ls = state.layers[li]
             before = cur
             use_conn = history is not None and li >= self.conn_first
-            if streams > 1:
+            if dyn:
+                branch, Rs, w_out = MHC.dynamic_split(Rs, p, li, cfg.mhc_tau, cfg.mhc_iters)
+            elif streams > 1:
                 branch, Rs = MHC.layer_split(Rs, p["mhc_res"][li], p["mhc_pre"][li], cfg.mhc_tau, cfg.mhc_iters)
             elif use_conn:
                 branch = self.attn_res.attend(cur, history)
@@ -541,7 +544,7 @@ class DragonRuntime(nn.Module):
                     ls.hier_slow = ls.slow_rho = None
                     out = self._lowrank_step(branch, ls, start_pos, fixed)
             if streams > 1:
-                Rs = MHC.layer_merge(Rs, out, p["mhc_post"][li])
+                Rs = MHC.dynamic_merge(Rs, out, w_out) if dyn else MHC.layer_merge(Rs, out, p["mhc_post"][li])
                 cur = out
             elif use_conn:
                 cur = nf(cur + out)

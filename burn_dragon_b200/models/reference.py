@@ -242,13 +242,16 @@ def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state
     positions = torch.arange(pos0, pos0 + T, device=v.device)
     rhos = []
     streams = getattr(cfg, "mhc_streams", 1)
+    dyn = streams > 1 and getattr(cfg, "mhc_policy", "static_sinkhorn") == "dynamic_positive"
     if streams > 1:
         from . import mhc as MHC
 
-        R = v[:, None].expand(B, streams, T, v.shape[-1])
+        R = MHC.bootstrap(v, streams, params["mhc_boot"] if dyn else None)
     for layer in range(cfg.n_layer):
         r0 = rho0s[layer] if rho0s is not None else None
-        if streams > 1:
+        if dyn:
+            v, R, w_out = MHC.dynamic_split(R, params, layer, cfg.mhc_tau, cfg.mhc_iters)
+        elif streams > 1:
             v, R = MHC.layer_split(R, params["mhc_res"][layer], params["mhc_pre"][layer], cfg.mhc_tau, cfg.mhc_iters)
         enc, enc_v, dec, fq = layer_weights(params, cfg, layer, freqs)
         v, rho, _ = bdh_layer(v, enc, enc_v, dec, gamma, beta,
@@ -256,7 +259,9 @@ def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state
                               positions=positions,
                               decay=decay, rho0=r0, need_state=need_state, dropout=cfg.dropout,
                               training=training, norm=norm, pope=cfg.rotary_embedding == "pope")
-        if streams > 1:
+        if dyn:
+            R = MHC.dynamic_merge(R, v, w_out)
+        elif streams > 1:
             R = MHC.layer_merge(R, v, params["mhc_post"][layer])
         rhos.append(rho)
     if streams > 1:

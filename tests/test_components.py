@@ -90,6 +90,36 @@ def test_mhc_sinkhorn_and_training():
     assert all(t is not None and torch.isfinite(t).all() for t in g)
 
 
+def test_mhc_dynamic_positive_controller():
+    """dynamic_positive: per-token coefficients from the streams (positive sigmoids, a
+    batched Sinkhorn), reference initialisation (zero controller weights, gates at
+    sigmoid(-4.59512), carry bias = static h_res logits, bootstrap bias), gradients reach
+    the controller, and the TOML key selects it."""
+    from burn_dragon_b200.config import training_config_from_dict
+    from burn_dragon_b200.models import mhc as MHC
+
+    c = training_config_from_dict({"model": {"n_layer": 2, "n_embd": 32, "n_head": 2,
+                                             "mlp_internal_dim_multiplier": 4,
+                                             "mhc": {"enabled": True, "num_streams": 3,
+                                                     "coefficient_policy": "dynamic_positive"}}}).model
+    assert c.mhc_policy == "dynamic_positive" and c.mhc_streams == 3
+    cfg = DragonConfig(n_layer=2, n_embd=32, n_head=2, mlp_internal_dim_multiplier=4, dropout=0.0,
+                       rotary_embedding="rope", mhc_streams=3, mhc_policy="dynamic_positive")
+    model = BDH(cfg, seed=1)
+    assert torch.all(model.mhc_alpha_w == 0) and torch.allclose(model.mhc_carry_gate, torch.tensor(-4.59512))
+    assert torch.equal(model.mhc_carry_b.view(2, 3, 3), model.mhc_res)
+    assert model.mhc_boot.abs().max() < 1e-3 and model.mhc_boot.abs().max() > 0
+    # per-token residual weights are doubly stochastic; branch weights positive
+    R = torch.randn(2, 3, 5, 32)
+    bi, mixed, w_out = MHC.dynamic_split(R, model.param_dict(), 0, cfg.mhc_tau, 30)
+    assert bi.shape == (2, 5, 32) and mixed.shape == R.shape and (w_out > 0).all()
+    x = torch.randint(0, 256, (2, 8))
+    loss = model.loss(x, x)
+    # the controller weights start at zero but are reachable through the gates
+    g = torch.autograd.grad(loss, [model.mhc_alpha_w, model.mhc_carry_w, model.mhc_beta_gate, model.encoder])
+    assert all(torch.isfinite(t).all() for t in g) and g[0].abs().sum() > 0 and g[1].abs().sum() > 0
+
+
 def test_initialization_sub_configs_follow_the_reference_rules():
     from burn_dragon_b200.config import training_config_from_dict
     from burn_dragon_b200.models.init import init_param, modular_bridges, projection_std
