@@ -354,7 +354,8 @@ class BDH(nn.Module):
 
     # ---------------------------------------------------------------- fused path
     def fused_step(self, tokens: torch.Tensor, targets: torch.Tensor, mask=None, state=None,
-                   accumulate: bool = False, loss_scale: float = 1.0, grad_ready=None) -> torch.Tensor:
+                   accumulate: bool = False, loss_scale: float = 1.0, grad_ready=None,
+                   grad16: dict | None = None) -> torch.Tensor:
         """Forward + CE + backward on the sm_100a kernels. Writes ``.grad`` of every
         parameter (the flat grad buffer) and returns the loss as a device scalar.
 
@@ -380,7 +381,7 @@ class BDH(nn.Module):
         rho0s = state.rhos if state is not None else None
         outs = f.forward(p16, p32, tokens, pos0=pos0, rho0s=rho0s, want_state=state is not None)
         loss = f.loss(targets, mask, scale=loss_scale)
-        f.backward(p16, p32, g32, tokens, pos0=pos0, accumulate=accumulate, grad_ready=grad_ready)
+        f.backward(p16, p32, g32, tokens, pos0=pos0, accumulate=accumulate, grad_ready=grad_ready, grad16=grad16)
         if self.scaffold:
             self._scaffold_backward(g32)
         if state is not None:

@@ -367,7 +367,7 @@ class FusedBDH:
     # ---------------------------------------------------------------- backward
     def backward(self, p16: dict, p32: dict, g32: dict, tokens: torch.Tensor | None, pos0: int = 0,
                  accumulate: bool = False, dv_out: torch.Tensor | None = None, with_embed: bool = True,
-                 grad_ready=None):
+                 grad_ready=None, grad16: dict | None = None):
         """Writes parameter gradients into g32 (``accumulate``: adds to them, for
         gradient accumulation over micro-batches).
 
@@ -375,9 +375,14 @@ class FusedBDH:
         replaces the LM head / CE backward; ``with_embed=False`` stops at this stage's
         input and returns its gradient (a view of a workspace buffer).
 
-        ``grad_ready(name)``: called as soon as the weights are shared across the layers
-        and layer 0 has added its last term to ``decoder`` / ``encoder_v`` / ``encoder``."""
+        ``grad_ready(name)``: called once layer 0 has added its last term to the shared
+        ``decoder`` / ``encoder_v`` / ``encoder`` gradient and the backward has finished
+        reading that projection's bf16 shadow (the data-parallel exchange may then
+        overwrite it). ``grad16``: bf16 destinations of those gradients; layer 0's weight
+        GEMMs write the final values there too (the exchange's transport copy, no
+        conversion pass)."""
         ready = grad_ready if grad_ready is not None else (lambda name: None)
+        g16 = grad16 or {}
         ws, cfg, mod = self.ws, self.cfg, self.mod
         B, T, D, H, Nh, N, M, L, V = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L, ws.V
         gam, bet = p32["norm_gamma"], p32["norm_beta"]
@@ -407,18 +412,19 @@ class FusedBDH:
                    out1=ws.dy16, aux0=ws.x16[l], aux1=ws.yn16[l], ld=N)
             # dE += yn^T dm
             G.gemm(G.EPI_F32, Operand(ws.yn16[l], True, N, M, N), Operand(ws.dm16, True, D, M, D), N, D, M,
-                   g32["decoder"], ld=D, accumulate=True)
+                   g32["decoder"], ld=D, accumulate=True, out1=g16.get("decoder") if l == 0 else None)
             if l == 0:
                 ready("decoder")
             # dDy_h += an_h^T dy_h
             G.gemm(G.EPI_F32, Operand(ws.an16[l], True, D, M, H * D, z1=(H, D)),
                    Operand(ws.dy16, True, Nh, M, N, z1=(H, Nh)), D, Nh, M, g32["encoder_v"], Z1=H, ld=Nh,
-                   sz1=D * Nh, accumulate=True)
-            if l == 0:
-                ready("encoder_v")
+                   sz1=D * Nh, accumulate=True, out1=g16.get("encoder_v") if l == 0 else None)
             # d(an)_h = dy_h Dy_h^T
             G.gemm(G.EPI_F32, Operand(ws.dy16, False, Nh, M, N, z1=(H, Nh)),
                    Operand(encv, False, Nh, D, Nh, z1=(H, D * Nh)), M, D, Nh, ws.dan32, Z1=H, ld=H * D, sz1=D)
+            if l == 0:
+                # after the last read of the encoder_v shadow: its new weights may land now
+                ready("encoder_v")
             # dC = LN^T(d an), written as [B,H,T,D]
             head_parts.append(mod.ln_bwd(ws.dan32, ws.a32[l], ws.amean[l], ws.arstd[l], M * H, D, gam, T, H, ws.dC16,
                                     None))
@@ -447,12 +453,14 @@ class FusedBDH:
                    sz2=T * D)
             # dDx_h += v^T dx_h
             G.gemm(G.EPI_F32, Operand(v16, True, D, M, D), Operand(ws.dx16, True, Nh, M, N, z1=(H, Nh)), D, Nh, M,
-                   g32["encoder"], Z1=H, ld=Nh, sz1=D * Nh, accumulate=True)
-            if l == 0:
-                ready("encoder")
+                   g32["encoder"], Z1=H, ld=Nh, sz1=D * Nh, accumulate=True,
+                   out1=g16.get("encoder") if l == 0 else None)
             # dv_x per head = dx_h Dx_h^T
             G.gemm(G.EPI_F32, Operand(ws.dx16, False, Nh, M, N, z1=(H, Nh)),
                    Operand(enc, False, Nh, D, Nh, z1=(H, D * Nh)), M, D, Nh, ws.dvx32, Z1=H, ld=D, sz1=M * D)
+            if l == 0:
+                # after the last read of the encoder shadow
+                ready("encoder")
             dv_next = ws.dv[1] if dv is ws.dv[0] else ws.dv[0]
             if tp is not None:
                 mod.sum_rows(dv_next, None, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)

@@ -132,12 +132,14 @@ class NVLinkDDP:
         if opt.clip is not None:
             self._sumsq.zero_()
 
-    def _bucket_work(self, b: int) -> None:
+    def _bucket_work(self, b: int, precast: bool = False) -> None:
         mod = _ext.load()
         bk = self.buckets[b]
         a, e, lo, hi = bk["start"], bk["end"], bk["lo"], bk["hi"]
         opt = self._opt
-        if self.grad_bf16:
+        if precast:
+            pass  # the backward wrote this bucket's transport copy itself
+        elif self.grad_bf16:
             mod.cast_bf16(self.grad[a:e], self.gsym[a:e])
         else:
             self.gsym[a:e].copy_(self.grad[a:e])
@@ -161,16 +163,18 @@ class NVLinkDDP:
             self._bsum = torch.zeros(len(self.buckets), dtype=torch.float32, device=self.device)
         return self._bsum[b:b + 1]
 
-    def bucket_ready(self, b: int) -> None:
-        """Bucket b's gradients are final on the current stream: run its communication on
-        the side stream from here on."""
+    def bucket_ready(self, b: int, precast: bool = False) -> None:
+        """Bucket b's gradients are final on the current stream and this rank no longer
+        reads its shadow weights before the step ends: run its communication on the side
+        stream from here on. ``precast``: the bucket's transport copy (bf16) is already in
+        the symmetric gradient buffer."""
         if b in self._launched:
             return
         self._launched.add(b)
         cur = torch.cuda.current_stream(self.device)
         self.side.wait_stream(cur)
         with torch.cuda.stream(self.side):
-            self._bucket_work(b)
+            self._bucket_work(b, precast)
 
     def step_adamw(self, opt) -> None:
         """Finish the step: launch the buckets not yet launched, join the side stream, and

@@ -138,7 +138,16 @@ class Trainer:
     def _grad_ready(self, name: str) -> None:
         b = self._bucket_of.get(name)
         if b is not None:
-            self.comm.bucket_ready(b)
+            self.comm.bucket_ready(b, precast=self.comm.grad_bf16)
+
+    def _grad16(self) -> dict | None:
+        """bf16 views of the symmetric gradient buffer for the three shared projections
+        (their final backward GEMMs write the transport copy directly)."""
+        if not self.comm.grad_bf16:
+            return None
+        st = self.model.store
+        return {n: self.comm.gsym[st.offsets[n]:st.offsets[n] + st.view(st.grad, n).numel()].view(st.shapes[n])
+                for n in self._bucket_of}
 
     def sync_params(self) -> None:
         """Make the full fp32 master and the optimizer moments current on every rank (the
@@ -239,7 +248,8 @@ class Trainer:
             return total
         if self.fused:
             return self.model.fused_step(tokens, targets, mask,
-                                         grad_ready=self._grad_ready if self.overlap else None)
+                                         grad_ready=self._grad_ready if self.overlap else None,
+                                         grad16=self._grad16() if self.overlap else None)
         self.model.zero_grad(set_to_none=False)
         loss = self.model.loss(tokens, targets, mask)
         grads = torch.autograd.grad(loss, [p for p in self.model.parameters()], allow_unused=True)
