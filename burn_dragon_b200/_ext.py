@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD_DIR = os.path.join(CSRC, "build")
 
-SOURCES = ["bindings.cpp", "gemm_host.cu", "gemm_inst_a.cu", "gemm_inst_b.cu", "gemm_inst_c.cu", "gemm_inst_d.cu", "gemm_inst_e.cu", "rowwise.cu", "noalloc_decoder.cu", "decode.cu", "scaffold.cu", "comm.cu", "gdpo.cu"]
+SOURCES = ["bindings.cpp", "gemm_host.cu", "gemm_inst_a.cu", "gemm_inst_b.cu", "gemm_inst_c.cu", "gemm_inst_d.cu", "gemm_inst_e.cu", "rowwise.cu", "noalloc_decoder.cu", "decode.cu", "scaffold.cu", "comm.cu", "gdpo.cu", "ssd_chunk.cu"]
 
 NVCC_FLAGS = [
     "-gencode=arch=compute_100a,code=sm_100a",

@@ -84,6 +84,14 @@ void ddp_norm_exchange(std::vector<int64_t> flags, int64_t rank, const at::Tenso
                        const at::Tensor& out, const at::Tensor& err);
 void ddp_epoch_advance(const at::Tensor& flags_local);
 void ddp_slot_barrier(std::vector<int64_t> flags, int64_t rank, int64_t slot, const at::Tensor& err);
+void ssd_chunk_fwd(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V, const at::Tensor& DA,
+                   const at::Tensor& S0, const at::Tensor& VS, const at::Tensor& KS, const at::Tensor& CF,
+                   int64_t chunk, const at::Tensor& Y, const at::Tensor& SF, const at::Tensor& SC);
+void ssd_chunk_bwd(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V, const at::Tensor& DA,
+                   const at::Tensor& VS, const at::Tensor& KS, const at::Tensor& CF, const at::Tensor& SC,
+                   const at::Tensor& DY, const at::Tensor& DSF, int64_t chunk, const at::Tensor& dQ,
+                   const at::Tensor& dK, const at::Tensor& dV, const at::Tensor& dDA, const at::Tensor& dS0,
+                   const at::Tensor& dVS, const at::Tensor& dKS, const at::Tensor& dCF);
 void percentile_thresholds(const at::Tensor& values, double q, const at::Tensor& out);
 }  // namespace bd
 
@@ -123,5 +131,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ddp_norm_exchange", &bd::ddp_norm_exchange);
   m.def("ddp_epoch_advance", &bd::ddp_epoch_advance);
   m.def("ddp_slot_barrier", &bd::ddp_slot_barrier);
+  m.def("ssd_chunk_fwd", &bd::ssd_chunk_fwd);
+  m.def("ssd_chunk_bwd", &bd::ssd_chunk_bwd);
   m.def("percentile_thresholds", &bd::percentile_thresholds);
 }

@@ -178,7 +178,11 @@ class Mamba3Params(nn.Module):
         return torch.cat((rot, x[..., 2 * n:]), -1)
 
     def forward(self, hidden: torch.Tensor, state: dict | None):
-        """hidden [B,T,D] -> (context [B,T,D], state dict ssm/angle/k/v)."""
+        """hidden [B,T,D] -> (context [B,T,D], state dict ssm/angle/k/v). On CUDA the chunk
+        scan runs in the ``ssd_chunk`` kernels (``forward_fused``); elsewhere in the chunk
+        loop below."""
+        if hidden.is_cuda and fused_ssd_ok(self):
+            return self.forward_fused(hidden, state)
         B, T, Dm = hidden.shape
         H, P, S, n = self.nheads, self.headdim, self.d_state, self.n_angles
         di, gs = self.d_inner, self.ngroups * S
@@ -230,3 +234,130 @@ class Mamba3Params(nn.Module):
             k_s = k_rot[:, -1]
             v_s = x[:, s1 - 1]
         return torch.cat(outs, 1), {"ssm": ssm, "angle": ang_s, "k": k_s, "v": v_s}
+
+
+# ----------------------------------------------------------------------- Mamba-3 on the device
+
+
+def fused_ssd_ok(m: "Mamba3Params") -> bool:
+    """The ``ssd_chunk`` kernels' limits: chunk <= 64, state <= 64, head dim <= 256."""
+    return m.chunk <= 64 and m.d_state <= 64 and m.headdim <= 256
+
+
+class SSDChunkScan(torch.autograd.Function):
+    """The chunk scan of the state-space duality on the device (``csrc/ssd_chunk.cu``).
+
+    Inputs (fp32, [BH, ...]): q, k [BH, T, S]; v [BH, T, P]; da [BH, T] (chunk-local
+    cumulative log decay); s0 [BH, P, S]; vs [BH, n, P], ks [BH, n, S], cf [BH, n] (the
+    trapezoid term of each chunk). Outputs: y [BH, T, P] (carried-state read + causal
+    intra-chunk term) and the final state [BH, P, S]."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, da, s0, vs, ks, cf, chunk: int):
+        from .. import _ext
+
+        BH, T, S = q.shape
+        P = v.shape[-1]
+        n = -(-T // chunk)
+        y = torch.empty(BH, T, P, device=q.device)
+        sf = torch.empty(BH, P, S, device=q.device)
+        sc = torch.empty(BH, n, P, S, device=q.device)
+        _ext.load().ssd_chunk_fwd(q, k, v, da, s0, vs, ks, cf, chunk, y, sf, sc)
+        ctx.save_for_backward(q, k, v, da, vs, ks, cf, sc)
+        ctx.chunk = chunk
+        return y, sf
+
+    @staticmethod
+    def backward(ctx, dy, dsf):
+        from .. import _ext
+
+        q, k, v, da, vs, ks, cf, sc = ctx.saved_tensors
+        dy = torch.zeros_like(v) if dy is None else dy.contiguous()
+        BH, T, S = q.shape
+        P = v.shape[-1]
+        dsf = torch.zeros(BH, P, S, device=q.device) if dsf is None else dsf.contiguous()
+        g = [torch.empty_like(t) for t in (q, k, v, da)]
+        ds0 = torch.empty(BH, P, S, device=q.device)
+        dvs, dks, dcf = torch.empty_like(vs), torch.empty_like(ks), torch.empty_like(cf)
+        _ext.load().ssd_chunk_bwd(q, k, v, da, vs, ks, cf, sc, dy, dsf, ctx.chunk, *g, ds0, dvs, dks, dcf)
+        return (*g, ds0, dvs, dks, dcf, None)
+
+
+def ssd_scan_reference(q, k, v, da, s0, vs, ks, cf, chunk: int):
+    """PyTorch restatement of ``SSDChunkScan`` (same inputs and outputs; the oracle)."""
+    BH, T, S = q.shape
+    st = s0
+    ys = []
+    for c, t0 in enumerate(range(0, T, chunk)):
+        t1 = min(t0 + chunk, T)
+        qc, kcc, vc, dc = q[:, t0:t1], k[:, t0:t1], v[:, t0:t1], da[:, t0:t1]
+        tl = st + cf[:, c, None, None] * vs[:, c, :, None] * ks[:, c, None, :]
+        dec = (dc[:, :, None] - dc[:, None, :]).clamp_max(0).exp()
+        ys.append((qc @ tl.transpose(-1, -2)) * dc.exp()[..., None]
+                  + torch.tril((qc @ kcc.transpose(-1, -2)) * dec, -1) @ vc)
+        last = dc[:, -1]
+        st = tl * last.exp()[:, None, None] + (vc * (last[:, None] - dc).exp()[..., None]).transpose(-1, -2) @ kcc
+    return torch.cat(ys, 1), st
+
+
+def _forward_fused(self, hidden: torch.Tensor, state: dict | None, scan=None):
+    """Mamba-3 SISO with the projections, norms and rotations vectorised over the whole
+    sequence and the chunk scan in ``SSDChunkScan`` (the same function as the chunk loop of
+    ``forward``: the rotary angle accumulates over the sequence, a token's key carries
+    its own gamma plus the next token's beta inside its chunk, and each chunk's first
+    token's beta enters through the trapezoid term on the previous token's key / value)."""
+    B, T, Dm = hidden.shape
+    H, P, S, n = self.nheads, self.headdim, self.d_state, self.n_angles
+    di, gs, C = self.d_inner, self.ngroups * S, self.chunk
+    pr = hidden @ self.in_proj
+    z = pr[..., :di].view(B, T, H, P)
+    x = pr[..., di:2 * di].view(B, T, H, P)
+    k_pre = self._bc(pr[..., 2 * di:2 * di + gs], self.b_norm_weight, self.b_bias)
+    q_pre = self._bc(pr[..., 2 * di + gs:2 * di + 2 * gs], self.c_norm_weight, self.c_bias)
+    o = 2 * di + 2 * gs
+    dt = F.softplus(self.dt_bias + pr[..., o:o + H])
+    a = (-F.softplus(pr[..., o + H:o + 2 * H])).clamp_max(-self.a_floor)
+    trap = torch.sigmoid(pr[..., o + 2 * H:o + 3 * H])
+    ang_proj = pr[..., o + 3 * H:].unsqueeze(2).expand(B, T, H, n)
+    gamma = dt * trap
+    beta = dt * (1 - trap)
+    st = state or {}
+    ssm = st.get("ssm", hidden.new_zeros(B, H, P, S))
+    ang_s = st.get("angle", hidden.new_zeros(B, H, n))
+    k_s = st.get("k", hidden.new_zeros(B, H, S))
+    v_s = st.get("v", hidden.new_zeros(B, H, P))
+    ang = (torch.tanh(ang_proj) * dt[..., None] * math.pi).cumsum(1) + ang_s[:, None]
+    q_rot = self._rotate(q_pre, ang, n)
+    k_rot = self._rotate(k_pre, ang, n)
+    qk_dot = (q_pre * k_pre).sum(-1) * gamma                         # [B,T,H]
+    t_idx = torch.arange(T, device=hidden.device)
+    chunk_end = ((t_idx + 1) % C == 0) | (t_idx == T - 1)
+    nxt = torch.cat((beta[:, 1:], beta.new_zeros(B, 1, H)), 1) * (~chunk_end)[None, :, None]
+    kc = k_rot * (gamma + nxt)[..., None]
+    nch = -(-T // C)
+    pad = nch * C - T
+    adt = F.pad(a * dt, (0, 0, 0, pad)).view(B, nch, C, H).cumsum(2).view(B, nch * C, H)[:, :T]
+    starts = torch.arange(nch, device=hidden.device) * C
+    cf = beta[:, starts]                                               # [B, n, H]
+    prev_idx = (starts - 1).clamp_min(0)
+    vs = x[:, prev_idx].clone()                                        # [B, n, H, P]
+    ks = k_rot[:, prev_idx].clone()
+    vs[:, 0] = v_s
+    ks[:, 0] = k_s
+    cdt = hidden.dtype if scan is not None else torch.float32  # the kernels run in fp32
+    scan = scan or SSDChunkScan.apply
+    bh = lambda t: t.transpose(1, 2).reshape(B * H, *t.shape[1:2], *t.shape[3:]).contiguous().to(cdt)  # noqa: E731
+    y, sf = scan(bh(q_rot), bh(kc), bh(x), adt.transpose(1, 2).reshape(B * H, T).contiguous().to(cdt),
+                 ssm.reshape(B * H, P, S).contiguous().to(cdt), bh(vs), bh(ks),
+                 cf.transpose(1, 2).reshape(B * H, nch).contiguous().to(cdt), C)
+    y = y.to(hidden.dtype)
+    sf = sf.to(hidden.dtype)
+    y = y.view(B, H, T, P)
+    v = x.transpose(1, 2)
+    y = y + (self.d_skip[None, :, None, None] + qk_dot.transpose(1, 2)[..., None]) * v
+    y = F.silu(z.transpose(1, 2)) * y
+    out = y.transpose(1, 2).reshape(B, T, di) @ self.out_proj
+    return out, {"ssm": sf.view(B, H, P, S), "angle": ang[:, -1], "k": k_rot[:, -1], "v": x[:, -1]}
+
+
+Mamba3Params.forward_fused = _forward_fused
