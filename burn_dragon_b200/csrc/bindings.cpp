@@ -74,12 +74,14 @@ void reduce_mean(std::vector<int64_t> grad, std::vector<int64_t> flags, int64_t 
                  const at::Tensor& err);
 void ddp_step(std::vector<int64_t> grad, std::vector<int64_t> shadow, bool grad_bf16, int64_t rank, int64_t lo,
               int64_t hi, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1, double b2,
-              double eps, double wd, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef);
+              double eps, double wd, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef,
+              std::vector<int64_t> gather_master);
 void ddp_reduce(std::vector<int64_t> grad, std::vector<int64_t> shadow, bool grad_bf16, int64_t rank, int64_t lo,
                 int64_t hi, const at::Tensor& gred, const at::Tensor& sumsq);
 void ddp_apply(std::vector<int64_t> grad, std::vector<int64_t> shadow, int64_t rank, int64_t lo, int64_t hi,
                const at::Tensor& gred, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1,
-               double b2, double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef);
+               double b2, double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef,
+               std::vector<int64_t> gather_master);
 void ddp_norm_exchange(std::vector<int64_t> flags, int64_t rank, const at::Tensor& sumsq, double max_norm,
                        const at::Tensor& out, const at::Tensor& err);
 void ddp_epoch_advance(const at::Tensor& flags_local);

@@ -220,6 +220,7 @@ __global__ void tp_scatter_rows_kernel(const float* __restrict__ src, DstPtrs sl
 struct DdpPtrs {
   const void* grad[kMaxRanks];  // bf16 (or fp32) gradient buffer of every rank
   __nv_bfloat16* shadow[kMaxRanks];
+  float* master[kMaxRanks];     // fp32 master of every rank, or null: not gathered
 };
 
 template <typename GT>
@@ -321,6 +322,12 @@ __device__ __forceinline__ void adamw8_gather(const DdpPtrs& pp, int rank, long 
     int dst = rank + r;
     if (dst >= W) dst -= W;
     *reinterpret_cast<uint4*>(pp.shadow[dst] + i) = hb;
+    // buckets whose fp32 master the forward reads (embedding, norms, adapters): the new
+    // master goes to every peer too (pp.master[rank] is this rank's own buffer)
+    if (pp.master[0] != nullptr && dst != rank) {
+      *reinterpret_cast<float4*>(pp.master[dst] + i) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+      *reinterpret_cast<float4*>(pp.master[dst] + i + 4) = make_float4(pv[4], pv[5], pv[6], pv[7]);
+    }
   }
 }
 
@@ -581,14 +588,17 @@ void tp_scatter_rows(const at::Tensor& src, std::vector<int64_t> slots, int64_t 
 
 
 namespace {
-DdpPtrs make_ddp_ptrs(const std::vector<int64_t>& grad, const std::vector<int64_t>& shadow) {
+DdpPtrs make_ddp_ptrs(const std::vector<int64_t>& grad, const std::vector<int64_t>& shadow,
+                      const std::vector<int64_t>& master = {}) {
   DdpPtrs pp;
   memset(&pp, 0, sizeof(pp));
   TORCH_CHECK(grad.size() >= 1 && grad.size() <= kMaxRanks && shadow.size() == grad.size(),
               "one gradient and one shadow pointer per rank (<= 8)");
+  TORCH_CHECK(master.empty() || master.size() == grad.size(), "one master pointer per rank, or none");
   for (size_t r = 0; r < grad.size(); ++r) {
     pp.grad[r] = reinterpret_cast<const void*>(grad[r]);
     pp.shadow[r] = reinterpret_cast<__nv_bfloat16*>(shadow[r]);
+    if (!master.empty()) pp.master[r] = reinterpret_cast<float*>(master[r]);
     TORCH_CHECK(grad[r] % 16 == 0 && shadow[r] % 16 == 0, "peer buffers must be 16-byte aligned");
   }
   return pp;
@@ -618,10 +628,13 @@ int ddp_grid(long long n8) {
 }  // namespace
 
 // One fused data-parallel optimizer step (no clipping): see ddp_step_kernel.
+// gather_master: every rank's fp32 master buffer (symmetric) to all-gather the new fp32
+// values into as well, or empty.
 void ddp_step(std::vector<int64_t> grad, std::vector<int64_t> shadow, bool grad_bf16, int64_t rank, int64_t lo,
               int64_t hi, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1, double b2,
-              double eps, double wd, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef) {
-  DdpPtrs pp = make_ddp_ptrs(grad, shadow);
+              double eps, double wd, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef,
+              std::vector<int64_t> gather_master) {
+  DdpPtrs pp = make_ddp_ptrs(grad, shadow, gather_master);
   TORCH_CHECK(lo % 8 == 0 && hi % 8 == 0 && hi >= lo, "shard bounds must be multiples of 8");
   TORCH_CHECK(master.scalar_type() == at::kFloat && master.numel() >= hi, "fp32 master covering the shard");
   TORCH_CHECK(m.numel() >= hi - lo && v.numel() >= hi - lo, "moment shards too small");
@@ -663,8 +676,9 @@ void ddp_reduce(std::vector<int64_t> grad, std::vector<int64_t> shadow, bool gra
 // Clipping pass 2: AdamW from the reduced shard scaled by coef[0], shadow all-gather.
 void ddp_apply(std::vector<int64_t> grad, std::vector<int64_t> shadow, int64_t rank, int64_t lo, int64_t hi,
                const at::Tensor& gred, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1,
-               double b2, double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef) {
-  DdpPtrs pp = make_ddp_ptrs(grad, shadow);
+               double b2, double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef,
+               std::vector<int64_t> gather_master) {
+  DdpPtrs pp = make_ddp_ptrs(grad, shadow, gather_master);
   TORCH_CHECK(lo % 8 == 0 && hi % 8 == 0 && gred.numel() >= hi - lo, "shard bounds / reduced shard size");
   auto st = at::cuda::getCurrentCUDAStream(gred.get_device()).stream();
   const int grid = ddp_grid((hi - lo) / 8);

@@ -12,8 +12,10 @@ backward has finished that bucket's gradients (``overlap``), then a closing barr
 where ``ddp_step`` (``csrc/comm.cu``) is one kernel: rank r sums its slice [lo_r, hi_r)
 of every peer's gradient with plain P2P loads (a reduce-scatter, fp32 accumulation),
 runs AdamW on its fp32 master slice and moment shard, and stores the new bf16 weights
-into every peer's shadow (an all-gather by P2P stores). A rank keeps the fp32 master
-current only on its own slice (ZeRO-1 style: optimizer state and master updates are
+into every peer's shadow (an all-gather by P2P stores). For the buckets whose fp32 master
+the model reads (the embedding, norms and scaffold adapters: ``master_buckets``) the new
+fp32 values are stored into every peer as well. For the shared projections a rank keeps
+the fp32 master current only on its own slice (ZeRO-1 style: optimizer state and master updates are
 partitioned, the reference's intended FSDP mode, burn_dragon_train/src/config/core.rs:
 87-94); ``sync_master()`` all-gathers the full fp32 master when a caller needs it
 (checkpoints, the PyTorch path, evaluation in fp32).
@@ -51,7 +53,10 @@ class NVLinkDDP:
     FLAG_WORDS = 512
 
     def __init__(self, numel: int, device: torch.device, group=None, grad_dtype: str = "bf16",
-                 buckets: list[tuple[int, int]] | None = None):
+                 buckets: list[tuple[int, int]] | None = None, master_buckets: set[int] | None = None):
+        """``master_buckets``: buckets whose fp32 master the model reads in its forward /
+        backward (embedding, norms, scaffold adapters); their new fp32 values are
+        all-gathered with the shadow. Default: every bucket."""
         if not dist.is_initialized():
             raise RuntimeError("NVLinkDDP needs an initialised process group")
         if grad_dtype not in ("bf16", "fp32"):
@@ -86,7 +91,7 @@ class NVLinkDDP:
         self.lo, self.hi = self.buckets[0]["lo"], self.buckets[0]["hi"]
         self.shard = -(-self.numel // self.world)
         gbytes = self.numel * (2 if self.grad_bf16 else 4)
-        sizes = {"gsym": gbytes, "shadow": self.numel * 2, "flags": self.FLAG_WORDS * 4}
+        sizes = {"gsym": gbytes, "shadow": self.numel * 2, "flags": self.FLAG_WORDS * 4, "param": self.numel * 4}
         self._own = {k: mod.sym_alloc(b, self.dev) for k, b in sizes.items()}
         handles = {k: mod.ipc_handle(p, self.dev) for k, p in self._own.items()}
         gathered: list = [None] * self.world
@@ -104,7 +109,8 @@ class NVLinkDDP:
         # local fp32 gradient (written by the backward) and fp32 master (current on the
         # owned slices)
         self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
-        self.param = torch.zeros(self.numel, dtype=torch.float32, device=device)
+        self.param = mod.wrap_ptr(self._own["param"], self.numel, 0, self.dev)
+        self.master_buckets = set(range(len(self.buckets))) if master_buckets is None else set(master_buckets)
         self.shadow = mod.wrap_ptr(self._own["shadow"], self.numel, 1, self.dev)
         self.gsym = mod.wrap_ptr(self._own["gsym"], self.numel, 1 if self.grad_bf16 else 0, self.dev)
         self.flags_local = mod.wrap_ptr(self._own["flags"], self.FLAG_WORDS, 2, self.dev)
@@ -148,9 +154,10 @@ class NVLinkDDP:
             return
         g, sh = self.ptrs["gsym"], self.ptrs["shadow"]
         mo, n = bk["moff"], hi - lo
+        gm = self.ptrs["param"] if b in self.master_buckets else []
         if opt.clip is None:
             mod.ddp_step(g, sh, self.grad_bf16, self.rank, lo, hi, self.param, self.m[mo:mo + n], self.v[mo:mo + n],
-                         opt.b1, opt.b2, opt.eps, opt.wd, opt._hyper, None)
+                         opt.b1, opt.b2, opt.eps, opt.wd, opt._hyper, None, gm)
         else:
             # sums of squares accumulate into _sumsq over the buckets (ddp_reduce zeroes its
             # target, so each bucket reduces into a scratch word first)
@@ -190,12 +197,13 @@ class NVLinkDDP:
         if opt.clip is not None:
             mod.ddp_norm_exchange(self.ptrs["flags"], self.rank, self._sumsq, float(opt.clip), self.norm_out, self.err)
             g, sh = self.ptrs["gsym"], self.ptrs["shadow"]
-            for bk in self.buckets:
+            for b, bk in enumerate(self.buckets):
                 lo, hi, mo = bk["lo"], bk["hi"], bk["moff"]
                 if hi > lo:
                     n = hi - lo
+                    gm = self.ptrs["param"] if b in self.master_buckets else []
                     mod.ddp_apply(g, sh, self.rank, lo, hi, self._gred[mo:mo + n], self.param, self.m[mo:mo + n],
-                                  self.v[mo:mo + n], opt.b1, opt.b2, opt.eps, opt.wd, opt._hyper, self.norm_out)
+                                  self.v[mo:mo + n], opt.b1, opt.b2, opt.eps, opt.wd, opt._hyper, self.norm_out, gm)
             opt._scratch[1:2].copy_(self.norm_out[1:2])
         mod.ddp_slot_barrier(self.ptrs["flags"], self.rank, len(self.buckets), self.err)
         self._opt = None
@@ -206,7 +214,9 @@ class NVLinkDDP:
         if self.master_synced:
             return
         if self.world > 1:
-            for bk in self.buckets:
+            for b, bk in enumerate(self.buckets):
+                if b in self.master_buckets:
+                    continue  # already current on every rank
                 a, e = bk["start"], bk["end"]
                 c = -(-(e - a) // (8 * self.world)) * 8
                 full = torch.zeros(c * self.world, dtype=torch.float32, device=self.device)

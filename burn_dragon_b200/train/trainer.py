@@ -109,8 +109,12 @@ class Trainer:
                 raise ValueError("the NVLink DDP step clips by global norm only; use comm='nccl' for "
                                  "element-wise value clipping")
             self._bucket_of, buckets = self._ddp_buckets()
+            # the forward reads the fp32 master of every bucket but the three shared
+            # projections (their bf16 shadow only): those buckets all-gather fp32 too
+            master_b = {len(buckets) - 1} if buckets else None
             self.comm = NVLinkDDP(self.model.store.numel, self.device, group=self.dp_group,
-                                  grad_dtype=os.environ.get("BDH_DDP_GRAD_DTYPE", "bf16"), buckets=buckets)
+                                  grad_dtype=os.environ.get("BDH_DDP_GRAD_DTYPE", "bf16"), buckets=buckets,
+                                  master_buckets=master_b)
             self.model.attach_buffers(self.comm.param, self.comm.grad, self.comm.shadow)
             # overlap the per-bucket gradient exchange with the rest of the backward
             # (BDH_DDP_OVERLAP=0: one exchange after the backward)
