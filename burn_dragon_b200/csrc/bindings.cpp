@@ -94,6 +94,9 @@ void ssd_chunk_bwd(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V
                    const at::Tensor& DY, const at::Tensor& DSF, int64_t chunk, const at::Tensor& dQ,
                    const at::Tensor& dK, const at::Tensor& dV, const at::Tensor& dDA, const at::Tensor& dS0,
                    const at::Tensor& dVS, const at::Tensor& dKS, const at::Tensor& dCF);
+void tp_sum_slots(const at::Tensor& slots, const at::Tensor& out, int64_t world, int64_t n, int64_t slot_stride,
+                  const c10::optional<at::Tensor>& add);
+void tp_gather_bytes(std::vector<int64_t> dst, int64_t rank, int64_t offset, int64_t nbytes, int64_t device);
 void percentile_thresholds(const at::Tensor& values, double q, const at::Tensor& out);
 }  // namespace bd
 
@@ -135,5 +138,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ddp_slot_barrier", &bd::ddp_slot_barrier);
   m.def("ssd_chunk_fwd", &bd::ssd_chunk_fwd);
   m.def("ssd_chunk_bwd", &bd::ssd_chunk_bwd);
+  m.def("tp_sum_slots", &bd::tp_sum_slots);
+  m.def("tp_gather_bytes", &bd::tp_gather_bytes);
   m.def("percentile_thresholds", &bd::percentile_thresholds);
 }

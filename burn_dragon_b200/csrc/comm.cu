@@ -468,6 +468,40 @@ __global__ void ddp_slot_barrier_kernel(PeerPtrs pp, int rank, int world, int sl
   __syncwarp();
 }
 
+
+// Sequence-parallel halves of the tensor-parallel sums. tp_sum_slots: the owner adds its
+// W slots (rows scattered to it by every rank) into its own rows, without gathering them.
+__global__ void tp_sum_slots_kernel(const float* __restrict__ slots, float* __restrict__ out, int world,
+                                    long long n4, long long slot_stride, const float* __restrict__ add) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const long long e = 4 * i;
+    float4 acc = add ? *reinterpret_cast<const float4*>(add + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < world; ++s) {
+      const float4 x = *reinterpret_cast<const float4*>(slots + s * slot_stride + e);
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+    *reinterpret_cast<float4*>(out + e) = acc;
+  }
+}
+
+// tp_gather_bytes: this rank's block of `nbytes` (16-byte multiples) at `offset` of its
+// own buffer is stored at the same offset of every peer's buffer (an all-gather by P2P
+// stores; the bf16 residual rows of sequence parallelism).
+__global__ void tp_gather_bytes_kernel(const uint4* __restrict__ src, DstPtrs dp, int world, int rank,
+                                       long long offset16, long long n16) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (long long)gridDim.x * blockDim.x) {
+    const uint4 x = src[offset16 + i];
+    for (int r = 1; r < world; ++r) {
+      int t = rank + r;
+      if (t >= world) t -= world;
+      reinterpret_cast<uint4*>(dp.dst[t])[offset16 + i] = x;
+    }
+  }
+}
+
 PeerPtrs make_ptrs(const std::vector<int64_t>& grad, const std::vector<int64_t>& param,
                    const std::vector<int64_t>& shadow, const std::vector<int64_t>& flags) {
   PeerPtrs pp;
@@ -715,6 +749,30 @@ void ddp_norm_exchange(std::vector<int64_t> flags, int64_t rank, const at::Tenso
   auto st = at::cuda::getCurrentCUDAStream(out.get_device()).stream();
   ddp_norm_exchange_kernel<<<1, 32, 0, st>>>(pp, (int)rank, (int)flags.size(), sumsq.data_ptr<float>(),
                                              (float)max_norm, out.data_ptr<float>(), err.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+
+// out[e] = (add[e]) + sum_s slots[s * slot_stride + e] for e < n (n % 4 == 0)
+void tp_sum_slots(const at::Tensor& slots, const at::Tensor& out, int64_t world, int64_t n, int64_t slot_stride,
+                  const c10::optional<at::Tensor>& add) {
+  TORCH_CHECK(n % 4 == 0 && slot_stride % 4 == 0 && out.numel() >= n, "tp_sum_slots: sizes");
+  auto st = at::cuda::getCurrentCUDAStream(out.get_device()).stream();
+  tp_sum_slots_kernel<<<148 * 2, 256, 0, st>>>(slots.data_ptr<float>(), out.data_ptr<float>(), (int)world, n / 4,
+                                               slot_stride, add ? add->data_ptr<float>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Store bytes [offset, offset + nbytes) of this rank's buffer (dst[rank]) into every peer's.
+void tp_gather_bytes(std::vector<int64_t> dst, int64_t rank, int64_t offset, int64_t nbytes, int64_t device) {
+  const int world = (int)dst.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks && offset % 16 == 0 && nbytes % 16 == 0, "tp_gather_bytes: 16-byte blocks");
+  DstPtrs dp;
+  memset(&dp, 0, sizeof(dp));
+  for (int r = 0; r < world; ++r) dp.dst[r] = reinterpret_cast<float*>(dst[r]);
+  auto st = at::cuda::getCurrentCUDAStream((c10::DeviceIndex)device).stream();
+  tp_gather_bytes_kernel<<<148 * 2, 256, 0, st>>>(reinterpret_cast<const uint4*>(dst[rank]), dp, world, (int)rank,
+                                                  offset / 16, nbytes / 16);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -32,7 +32,7 @@ struct SsdDims {
 
 // shared-memory carve-up, the same in forward and backward (floats)
 struct SsdSmem {
-  float *st, *tl, *q, *k, *v, *da, *A, *QK, *dy, *dst, *dtl, *red;
+  float *st, *tl, *q, *k, *v, *da, *A, *QK, *dy, *dst, *dtl, *U, *V2, *red;
 };
 
 __device__ __forceinline__ SsdSmem carve(float* base, const SsdDims& d, bool bwd) {
@@ -49,13 +49,15 @@ __device__ __forceinline__ SsdSmem carve(float* base, const SsdDims& d, bool bwd
   m.dy = bwd ? p : nullptr; if (bwd) p += d.C * d.P;
   m.dst = bwd ? p : nullptr; if (bwd) p += d.C * d.C;  // dA
   m.dtl = bwd ? p : nullptr; if (bwd) p += d.P * d.S;  // dtilde
+  m.U = bwd ? p : nullptr; if (bwd) p += d.C * d.S;    // U_i = tilde^T dy_i
+  m.V2 = bwd ? p : nullptr; if (bwd) p += d.C * d.P;   // V2_j = dS' k_j
   m.red = p; p += 4 * 64;      // small reductions
   return m;
 }
 
 size_t smem_floats(const SsdDims& d, bool bwd) {
   size_t f = 2 * d.P * d.S + 2 * d.C * d.S + d.C * d.P + 64 + 2 * d.C * d.C + 4 * 64;
-  if (bwd) f += d.C * d.P + d.C * d.C + d.P * d.S;
+  if (bwd) f += d.C * d.P + d.C * d.C + d.P * d.S + d.C * d.S + d.C * d.P;
   return f;
 }
 
@@ -203,6 +205,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_kernel(
       const int i = idx / d.S, s = idx % d.S;
       float a = 0.f;
       for (int p = 0; p < d.P; ++p) a += m.tl[p * d.S + s] * m.dy[i * d.P + p];
+      m.U[idx] = a;
       a *= __expf(m.da[i]);
       for (int j = 0; j < i; ++j)
         a += m.dst[i * d.C + j] * __expf(fminf(m.da[i] - m.da[j], 0.f)) * m.k[j * d.S + s];
@@ -225,20 +228,18 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_kernel(
       for (int i = j + 1; i < Cc; ++i) a += m.A[i * d.C + j] * m.dy[i * d.P + p];
       float b = 0.f;
       for (int s = 0; s < d.S; ++s) b += m.st[p * d.S + s] * m.k[j * d.S + s];
+      m.V2[idx] = b;
       gv[idx] = a + __expf(last - m.da[j]) * b;
     }
+    __syncthreads();
     // decay gradient, per token (thread i < Cc), plus the chunk-last terms
     float extra_last = 0.f;
     if ((int)threadIdx.x < Cc) {
       const int i = threadIdx.x;
       const float ei = __expf(m.da[i]);
-      // e^{da_i} dy_i . (tilde q_i)
+      // e^{da_i} dy_i . (tilde q_i) = e^{da_i} U_i . q_i
       float t1 = 0.f;
-      for (int p = 0; p < d.P; ++p) {
-        float tq = 0.f;
-        for (int s = 0; s < d.S; ++s) tq += m.tl[p * d.S + s] * m.q[i * d.S + s];
-        t1 += m.dy[i * d.P + p] * tq;
-      }
+      for (int s = 0; s < d.S; ++s) t1 += m.U[i * d.S + s] * m.q[i * d.S + s];
       float g = ei * t1;
       // intra-chunk decay: G_ij = dA_ij QK_ij L_ij where da_i - da_j <= 0
       for (int j = 0; j < i; ++j) {
@@ -251,11 +252,7 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_kernel(
       }
       // state write: R_i = w_i v_i^T dS' k_i enters with -1 here and +1 on the last token
       float r = 0.f;
-      for (int p = 0; p < d.P; ++p) {
-        float sk = 0.f;
-        for (int s = 0; s < d.S; ++s) sk += m.st[p * d.S + s] * m.k[i * d.S + s];
-        r += m.v[i * d.P + p] * sk;
-      }
+      for (int p = 0; p < d.P; ++p) r += m.v[i * d.P + p] * m.V2[i * d.P + p];
       r *= __expf(last - m.da[i]);
       g -= r;
       extra_last = r;

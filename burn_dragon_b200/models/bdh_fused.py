@@ -255,7 +255,12 @@ class FusedBDH:
         peer = None
         if self.tp is not None and self.tp.world > 1 and not ws.inference:
             peer = self.tp.attach_peer(M, D, L, ws.v32[0].device)
-            if peer is not None:
+            if peer is not None and self.tp.sequence_parallel:
+                # sequence parallel: the bf16 residual operands and the bf16 decoder
+                # gradient live in symmetric memory (rows gathered from their owners)
+                ws.v16 = peer.v16_views
+                ws.dm16 = peer.dm16
+            elif peer is not None:
                 ws.m32 = peer.sum_views  # the all-gathered decoder sums land here
         eps = cfg.norm_eps
         thr, thr_y = cfg.thresholds()
@@ -326,6 +331,11 @@ class FusedBDH:
                 # owners' sums all-gathered by peer stores (parallel.tp.PeerSum)
                 G.gemm(G.EPI_F32_SCATTER, Operand(ws.yn16[l], False, N, M, N), B_dec, M, D, N, ws.m32[l], ld=D,
                        scatter=peer.scatter_args())
+                if self.tp.sequence_parallel:
+                    # the owner merges its own rows and gathers their bf16 copies
+                    peer.sp_tail_forward(l, ws.v32[l], ws.v32[l + 1], ws.tst[l], p32["norm_gamma"],
+                                         p32["norm_beta"], eps)
+                    continue
                 peer.finish(l)
                 mod.tail_fwd(ws.m32[l], 1, M * D, ws.v32[l], M, D, p32["norm_gamma"], p32["norm_beta"], eps, None,
                              ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
@@ -404,9 +414,19 @@ class FusedBDH:
                 g32["lm_head"].zero_()
             dv.copy_(dv_out.reshape(M, D))
         enc, encv, dec = p16["encoder"], p16["encoder_v"], p16["decoder"]
+        sp = tp is not None and tp.sequence_parallel and tp.peer is not None
+        own = tp.peer.own_rows() if sp else None
         for l in reversed(range(L)):
             v16 = ws.v16[l]
-            parts.append(mod.tail_bwd(dv, ws.v32[l], ws.m32[l], ws.tst[l], M, D, gam, bet, ws.dm16, ws.dv_res))
+            if sp:
+                # residual-merge backward on this rank's rows; the bf16 decoder gradient rows
+                # are gathered, the LayerNorm partials summed over the group below
+                rows = own.stop - own.start
+                head_parts.append(mod.tail_bwd(dv[own], ws.v32[l][own], tp.peer.m_own[l], ws.tst[l][own], rows, D,
+                                               gam, bet, ws.dm16[own], ws.dv_res[own]))
+                tp.peer.sp_gather_dm()
+            else:
+                parts.append(mod.tail_bwd(dv, ws.v32[l], ws.m32[l], ws.tst[l], M, D, gam, bet, ws.dm16, ws.dv_res))
             # d(yn) = dm E^T -> dx_part = d(yn)*y, dy_pre = d(yn)*x*[y>0]
             G.gemm(G.EPI_DEC_BWD, Operand(ws.dm16, False, D, M, D), Operand(dec, False, D, N, D), M, N, D, ws.dx16, bn=G.tma_bn(M, N),
                    out1=ws.dy16, aux0=ws.x16[l], aux1=ws.yn16[l], ld=N)
@@ -462,7 +482,11 @@ class FusedBDH:
                 # after the last read of the encoder shadow
                 ready("encoder")
             dv_next = ws.dv[1] if dv is ws.dv[0] else ws.dv[0]
-            if tp is not None:
+            if sp:
+                # reduce-scatter only: the owner's rows get the group sum plus its residual
+                mod.sum_rows(dv_next, None, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)
+                tp.peer.sp_reduce_scatter(dv_next, ws.dv_res[own])
+            elif tp is not None:
                 mod.sum_rows(dv_next, None, ws.dvx32, H, M * D, ws.dva32, 1, 0, M * D)
                 if tp.peer is not None and tp.peer.M == M and tp.peer.D == D:
                     tp.peer.all_reduce_rows(dv_next)  # P2P scatter / owner sum / P2P gather
@@ -475,13 +499,22 @@ class FusedBDH:
         if with_embed:
             # embedding LayerNorm and gather
             demb = ws.dv_res  # reuse as fp32 [M, D] scratch
-            parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb))
             if not accumulate:
                 g32["embed"].zero_()
-            g32["embed"].index_add_(0, tokens.reshape(-1), demb)
+            if sp:
+                rows = own.stop - own.start
+                head_parts.append(mod.ln_bwd(dv[own], ws.emb_rows[own], ws.emean[own], ws.erstd[own], rows, D, gam,
+                                             0, 0, None, demb[own]))
+                ge = torch.zeros_like(g32["embed"])
+                ge.index_add_(0, tokens.reshape(-1)[own], demb[own])
+                tp.all_reduce(ge)  # every rank's own-row contributions
+                g32["embed"].add_(ge)
+            else:
+                parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb))
+                g32["embed"].index_add_(0, tokens.reshape(-1), demb)
         elif not accumulate:
             g32["embed"].zero_()
-        allp = torch.cat(parts, 0).sum(0)
+        allp = torch.cat(parts, 0).sum(0) if parts else 0.0
         hp = torch.cat(head_parts, 0).sum(0)
         if tp is not None:
             tp.all_reduce(hp)

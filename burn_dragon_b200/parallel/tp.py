@@ -51,14 +51,20 @@ class PeerSum:
         from .. import _ext
 
         W = tp.world
+        sp = tp.sequence_parallel
         if M % W:
             raise ValueError(f"token rows {M} must split evenly over {W} tensor-parallel ranks")
         mod = _ext.load()
         self.tp, self.M, self.D, self.L = tp, M, D, L
         self.rows = M // W
         self.dev = device.index if device.index is not None else torch.cuda.current_device()
-        sizes = {"slots": W * self.rows * D * 4, "sum": L * M * D * 4, "bsum": M * D * 4,
+        sizes = {"slots": W * self.rows * D * 4, "sum": (0 if sp else L) * M * D * 4 + 16, "bsum": M * D * 4,
                  "flags": self.FLAG_WORDS * 4}
+        if sp:
+            # sequence parallel: the bf16 residual operand of every layer and the bf16 decoder
+            # gradient are gathered by rows; the fp32 sums stay with their owner
+            sizes["v16"] = (L + 1) * M * D * 2
+            sizes["dm16"] = M * D * 2
         self._own = {k: mod.sym_alloc(b, self.dev) for k, b in sizes.items()}
         handles = {k: mod.ipc_handle(v, self.dev) for k, v in self._own.items()}
         gathered: list = [None] * W
@@ -74,8 +80,15 @@ class PeerSum:
                     self._opened.append(h)
                     self.ptrs[k].append(h)
         self.slots = mod.wrap_ptr(self._own["slots"], W * self.rows * D, 0, self.dev)
-        sums = mod.wrap_ptr(self._own["sum"], L * M * D, 0, self.dev).view(L, M, D)
-        self.sum_views = [sums[l] for l in range(L)]
+        if sp:
+            self.sum_views = None
+            v16 = mod.wrap_ptr(self._own["v16"], (L + 1) * M * D, 1, self.dev).view(L + 1, M, D)
+            self.v16_views = [v16[l] for l in range(L + 1)]
+            self.dm16 = mod.wrap_ptr(self._own["dm16"], M * D, 1, self.dev).view(M, D)
+            self.m_own = torch.empty(L, self.rows, D, device=device)
+        else:
+            sums = mod.wrap_ptr(self._own["sum"], L * M * D, 0, self.dev).view(L, M, D)
+            self.sum_views = [sums[l] for l in range(L)]
         self.bsum = mod.wrap_ptr(self._own["bsum"], M * D, 0, self.dev).view(M, D)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         dist.barrier(group=tp.group)
@@ -115,18 +128,75 @@ class PeerSum:
         self._barrier(1)
         t.view(self.M, self.D).copy_(self.bsum)
 
+    # ---- sequence parallel (``TensorParallel(sequence_parallel=True)``)
+    def own_rows(self) -> slice:
+        r0 = self.tp.rank * self.rows
+        return slice(r0, r0 + self.rows)
+
+    def sp_tail_forward(self, layer: int, v32_in, v32_out, tst, gamma, beta, eps: float) -> None:
+        """After the scattered decoder GEMM of ``layer``: the owner sums its rows' partials,
+        runs the residual merge v' = LN(v + LN(m)) on its rows only, and all-gathers the
+        bf16 rows of v' (the next GEMM operand) by P2P stores. The fp32 residual stays
+        with its owner."""
+        from .. import _ext
+
+        mod = _ext.load()
+        W, D, rows = self.tp.world, self.D, self.rows
+        own = self.own_rows()
+        self._barrier(0)
+        mod.tp_sum_slots(self.slots, self.m_own[layer], W, rows * D, rows * D, None)
+        v16 = self.v16_views[layer + 1]
+        mod.tail_fwd(self.m_own[layer], 1, rows * D, v32_in[own], rows, D, gamma, beta, eps, None, v32_out[own],
+                     v16[own], tst[own])
+        self._gather16(self.ptrs["v16"], (layer + 1) * self.M * D * 2 + own.start * D * 2, rows * D * 2)
+        self._barrier(1)
+
+    def _gather16(self, ptrs, offset: int, nbytes: int) -> None:
+        from .. import _ext
+
+        _ext.load().tp_gather_bytes(ptrs, self.tp.rank, offset, nbytes, self.dev)
+
+    def sp_gather_dm(self) -> None:
+        """All-gather this rank's rows of the bf16 decoder gradient (written into ``dm16``)."""
+        own = self.own_rows()
+        self._barrier(0)  # every rank has finished reading the previous layer's dm16
+        self._gather16(self.ptrs["dm16"], own.start * self.D * 2, self.rows * self.D * 2)
+        self._barrier(1)
+
+    def sp_reduce_scatter(self, t: torch.Tensor, add_own: torch.Tensor | None = None) -> None:
+        """Sum a local fp32 [M, D] partial over the group into this rank's rows of ``t``
+        only (rows scattered to their owners by P2P stores, the owner adds its slots and
+        ``add_own``); the other rows of ``t`` are left stale."""
+        from .. import _ext
+
+        mod = _ext.load()
+        W, D, rows, M = self.tp.world, self.D, self.rows, self.M
+        own = self.own_rows()
+        self._barrier(0)  # every owner has consumed the previous contents of its slots
+        mod.tp_scatter_rows(t, self.ptrs["slots"], self.tp.rank, rows, M, D, rows * D)
+        self._barrier(1)
+        mod.tp_sum_slots(self.slots, t.view(M, D)[own], W, rows * D, rows * D, add_own)
+
     def check(self) -> None:
         if int(self.err.item()):
             raise RuntimeError(f"tensor-parallel peer barrier timed out (code {int(self.err.item())})")
 
 
 class TensorParallel:
-    def __init__(self, group=None, fused_comm: bool | None = None):
+    def __init__(self, group=None, fused_comm: bool | None = None, sequence_parallel: bool = False):
         """``fused_comm``: run the forward decoder sums through ``PeerSum`` (default on
-        CUDA unless BDH_TP_FUSED=0); otherwise NCCL all-reduce."""
+        CUDA unless BDH_TP_FUSED=0); otherwise NCCL all-reduce.
+
+        ``sequence_parallel``: the residual stream between the tensor-parallel regions is
+        sharded by token rows (the reference's ``parallel.tensor.sequence_parallel``):
+        each rank owns M / P rows of the fp32 residual, runs the residual merge, the
+        LayerNorm backward of the merge and the embedding on those rows only, and the
+        ranks exchange bf16 rows (the GEMM operands) instead of fp32 sums. Needs the
+        peer-memory path and M divisible by P."""
         import os
 
         self.group = group
+        self.sequence_parallel = sequence_parallel
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if fused_comm is None:
@@ -138,6 +208,8 @@ class TensorParallel:
         """Symmetric buffers for a workspace shape (re-created when the shape changes)."""
         if not self.fused_comm:
             return None
+        if self.sequence_parallel and not self.fused_comm:
+            raise ValueError("sequence_parallel runs on the peer-memory tensor-parallel path (BDH_TP_FUSED=1, CUDA)")
         p = self.peer
         if p is None or (p.M, p.D, p.L) != (M, D, L):
             self.peer = PeerSum(self, M, D, L, device)

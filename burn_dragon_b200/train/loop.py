@@ -108,9 +108,10 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     if mode == "hybrid_2d":
         tp_arg = int(cfg.parallel.tensor.get("size", 8))
         comm = "nvlink" if o.grad_clip_value is None and dev.type == "cuda" else None
-    if cfg.parallel.tensor.get("sequence_parallel"):
-        raise ValueError("parallel.tensor.sequence_parallel is not implemented: the residual stream is "
-                         "replicated across the tensor-parallel group (unset the key)")
+    seq_par = bool(cfg.parallel.tensor.get("sequence_parallel", False))
+    if seq_par and not tp_arg:
+        raise ValueError("parallel.tensor.sequence_parallel needs a tensor-parallel mode "
+                         "(tensor_parallel_neuron or hybrid_2d)")
     if cfg.dataset.type in ("jsonl", "parquet", "text"):
         from .datasets import prepare_corpus
 
@@ -176,6 +177,7 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
                           betas=(o.beta1, o.beta2), eps=o.eps, grad_clip_norm=o.grad_clip_norm,
                           grad_clip_value=o.grad_clip_value, seed=t.seed,
                           lr_schedule=o.lr_schedule, max_iters=t.max_iters, comm=comm, tensor_parallel=tp_arg,
+                          sequence_parallel=seq_par,
                           micro_batches=micro if mode != "pipeline" else 1)
     runner = None
     if mode == "pipeline":

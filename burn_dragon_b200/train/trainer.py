@@ -44,10 +44,12 @@ def init_distributed() -> tuple[int, int, int]:
 class Trainer:
     def __init__(self, cfg: DragonConfig, device, lr=1e-3, weight_decay=0.1, betas=(0.9, 0.999), eps=1e-8,
                  grad_clip_norm=None, seed=1337, lr_schedule=None, max_iters=1000, comm=None, grad_clip_value=None,
-                 tensor_parallel: bool = False, micro_batches: int = 1):
+                 tensor_parallel: bool = False, micro_batches: int = 1, sequence_parallel: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.micro_batches = micro_batches
+        if sequence_parallel and not tensor_parallel:
+            raise ValueError("sequence_parallel shards the residual stream of a tensor-parallel group")
         self.tp = None
         self.dp_group = None
         dp_world = None
@@ -62,11 +64,11 @@ class Trainer:
                 pg_tp = [dist.new_group(g) for g in tp_groups]
                 pg_dp = [dist.new_group(g) for g in dp_groups]
                 r = dist.get_rank()
-                self.tp = TensorParallel(pg_tp[r // tp_size])
+                self.tp = TensorParallel(pg_tp[r // tp_size], sequence_parallel=sequence_parallel)
                 self.dp_group = pg_dp[r % tp_size]
                 dp_world = world_all // tp_size
             else:
-                self.tp = TensorParallel()
+                self.tp = TensorParallel(sequence_parallel=sequence_parallel)
             local = self.tp.local_config(cfg)
             self.model = BDH(local, device=self.device, seed=seed)
             # replicated tensors share the seed; each rank's heads get their own stream

@@ -29,7 +29,7 @@ def _worker(rank, world, port, out, fused="1"):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0", BDH_TP_FUSED=fused)
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0", BDH_TP_FUSED="0" if fused == "0" else "1")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world)
     from burn_dragon_b200.models.bdh import BDH
@@ -43,7 +43,7 @@ def _worker(rank, world, port, out, fused="1"):
     y = torch.randint(0, 256, (2, 128), generator=g).to(dev)
     loss_full = full.fused_step(x, y).item()
     gf = {k: v.clone() for k, v in full.grad_dict().items()}
-    tp = TensorParallel()
+    tp = TensorParallel(sequence_parallel=fused == "sp")
     local = BDH(tp.local_config(cfg), device=dev, seed=11)
     tp.shard_from_full(local, full.param_dict(), cfg)
     local.tp = tp
@@ -66,9 +66,11 @@ def _worker(rank, world, port, out, fused="1"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("fused", ["1", "0"])
+@pytest.mark.parametrize("fused", ["1", "0", "sp"])
 def test_tensor_parallel_matches_unsharded(fused):
-    """fused = "1": decoder sums through the scattered GEMM + peer all-gather; "0": NCCL."""
+    """fused = "1": decoder sums through the scattered GEMM + peer all-gather; "0": NCCL;
+    "sp": sequence parallel (residual rows sharded, bf16 rows gathered, reduce-scatter of
+    the residual gradient)."""
     out = mp.Manager().dict()
     mp.spawn(_worker, args=(2, _port(), out, fused), nprocs=2, join=True)
     for r in (0, 1):
