@@ -34,13 +34,16 @@ def main() -> None:
     ap.add_argument("--dim", type=int, default=1024)
     ap.add_argument("--neurons", type=int, default=262144)
     ap.add_argument("--heads", type=int, default=8)
+    ap.add_argument("--sequence-parallel", action="store_true",
+                    help="shard the residual stream by token rows between the tensor-parallel regions")
     a = ap.parse_args()
     rank, world, local = init_distributed()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     cfg = DragonConfig(n_layer=a.layers, n_embd=a.dim, n_head=a.heads, mlp_internal_dim_multiplier=a.neurons // a.dim,
                        dropout=0.0, rotary_embedding="rope")
-    tr = Trainer(cfg, dev, lr=1e-3, seed=7, tensor_parallel=world > 1, micro_batches=a.micro)
+    tr = Trainer(cfg, dev, lr=1e-3, seed=7, tensor_parallel=world > 1, micro_batches=a.micro,
+                 sequence_parallel=a.sequence_parallel and world > 1)
     data = RandomBytes(a.batch, a.seq, seed=20260729)  # identical on every TP rank
     x, y = (t.to(dev) for t in data.next())
     for _ in range(a.warmup):
@@ -63,7 +66,8 @@ def main() -> None:
                           "value": round(toks / (ms.item() / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
                           "ms_per_step": round(ms.item(), 2), "loss": float(loss.item()),
                           "config": {"d": a.dim, "n": a.neurons, "h": a.heads, "L": a.layers, "T": a.seq,
-                                     "global_batch": a.batch, "micro_batches": a.micro, "parallelism": f"tp{world}"}}),
+                                     "global_batch": a.batch, "micro_batches": a.micro, "parallelism": f"tp{world}",
+                                     "sequence_parallel": a.sequence_parallel}}),
               flush=True)
     if world > 1:
         dist.barrier()

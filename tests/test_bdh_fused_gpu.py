@@ -139,3 +139,21 @@ def test_fused_step_at_bench_shape_default_init():
     print("bench-shape relative gradient errors:", {k: f"{v:.3e}" for k, v in errs.items()})
     for n, r in errs.items():
         assert r < 0.08, f"{n}: rel err {r:.3e}"
+
+
+def test_fused_step_is_bitwise_reproducible():
+    """Race check: the fused step (split-K decoder partials in fixed slots, weight-gradient
+    accumulation in stream order, row-kernel partials in fixed slots, no atomics) gives
+    bitwise identical loss and gradients when run twice on the same inputs."""
+    cfg = DragonConfig(n_layer=2, n_embd=64, n_head=2, mlp_internal_dim_multiplier=8, dropout=0.0,
+                       rotary_embedding="rope")
+    model = BDH(cfg, device="cuda", seed=21)
+    torch.manual_seed(3)
+    x = torch.randint(0, 256, (4, 256), device="cuda")
+    y = torch.randint(0, 256, (4, 256), device="cuda")
+    l1 = model.fused_step(x, y).clone()
+    g1 = model.store.grad.clone()
+    l2 = model.fused_step(x, y).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(l1, l2)
+    assert torch.equal(g1, model.store.grad)
