@@ -32,7 +32,7 @@ struct SsdDims {
 
 // shared-memory carve-up, the same in forward and backward (floats)
 struct SsdSmem {
-  float *st, *tl, *q, *k, *v, *da, *A, *QK, *dy, *dst, *dtl, *U, *V2, *red;
+  float *st, *tl, *q, *k, *v, *da, *ex, *wx, *A, *QK, *dy, *dst, *dtl, *U, *V2, *red;
 };
 
 __device__ __forceinline__ SsdSmem carve(float* base, const SsdDims& d, bool bwd) {
@@ -44,6 +44,8 @@ __device__ __forceinline__ SsdSmem carve(float* base, const SsdDims& d, bool bwd
   m.k = p; p += d.C * d.S;
   m.v = p; p += d.C * d.P;
   m.da = p; p += 64;
+  m.ex = p; p += 64;           // e^{da_i}
+  m.wx = p; p += 64;           // e^{da_last - da_j}
   m.A = p; p += d.C * d.C;     // (q.k) L, masked
   m.QK = p; p += d.C * d.C;    // q.k (backward: the decay gradient needs it)
   m.dy = bwd ? p : nullptr; if (bwd) p += d.C * d.P;
@@ -56,7 +58,7 @@ __device__ __forceinline__ SsdSmem carve(float* base, const SsdDims& d, bool bwd
 }
 
 size_t smem_floats(const SsdDims& d, bool bwd) {
-  size_t f = 2 * d.P * d.S + 2 * d.C * d.S + d.C * d.P + 64 + 2 * d.C * d.C + 4 * 64;
+  size_t f = 2 * d.P * d.S + 2 * d.C * d.S + d.C * d.P + 3 * 64 + 2 * d.C * d.C + 4 * 64;
   if (bwd) f += d.C * d.P + d.C * d.C + d.P * d.S + d.C * d.S + d.C * d.P;
   return f;
 }
@@ -83,6 +85,15 @@ __device__ void load_chunk(const SsdSmem& m, const SsdDims& d, int Cc, const flo
   for (int idx = threadIdx.x; idx < Cc; idx += kThreads) m.da[idx] = da[t0 + idx];
 }
 
+// after load_chunk and a barrier: the per-token exponentials of the chunk
+__device__ void chunk_exps(const SsdSmem& m, int Cc) {
+  const float last = m.da[Cc - 1];
+  for (int i = threadIdx.x; i < Cc; i += kThreads) {
+    m.ex[i] = __expf(m.da[i]);
+    m.wx[i] = __expf(last - m.da[i]);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) ssd_fwd_kernel(SsdDims d, const float* __restrict__ Q,
                                                            const float* __restrict__ K, const float* __restrict__ V,
                                                            const float* __restrict__ DA, const float* __restrict__ S0,
@@ -106,6 +117,8 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_kernel(SsdDims d, const floa
     const float cf = CF[bh * d.n + c];
     const float* vs = VS + (bh * d.n + c) * d.P;
     const float* ks = KS + (bh * d.n + c) * d.S;
+    __syncthreads();
+    chunk_exps(m, Cc);
     for (int idx = threadIdx.x; idx < PS; idx += kThreads) {
       const int p = idx / d.S, s = idx % d.S;
       const float tl = m.st[idx] + cf * vs[p] * ks[s];
@@ -121,7 +134,7 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_kernel(SsdDims d, const floa
       const int i = idx / d.P, p = idx % d.P;
       float a = 0.f;
       for (int s = 0; s < d.S; ++s) a += m.tl[p * d.S + s] * m.q[i * d.S + s];
-      a *= __expf(m.da[i]);
+      a *= m.ex[i];
       for (int j = 0; j < i; ++j) a += m.A[i * d.C + j] * m.v[j * d.P + p];
       y[idx] = a;
     }
@@ -131,7 +144,7 @@ __global__ void __launch_bounds__(kThreads) ssd_fwd_kernel(SsdDims d, const floa
     for (int idx = threadIdx.x; idx < PS; idx += kThreads) {
       const int p = idx / d.S, s = idx % d.S;
       float a = E * m.tl[idx];
-      for (int j = 0; j < Cc; ++j) a += __expf(last - m.da[j]) * m.v[j * d.P + p] * m.k[j * d.S + s];
+      for (int j = 0; j < Cc; ++j) a += m.wx[j] * m.v[j * d.P + p] * m.k[j * d.S + s];
       m.st[idx] = a;
     }
   }
@@ -177,22 +190,26 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_kernel(
     for (int idx = threadIdx.x; idx < Cc * d.P; idx += kThreads) m.dy[idx] = dy[idx];
     for (int idx = threadIdx.x; idx < PS; idx += kThreads) m.tl[idx] = SC[(bh * d.n + c) * PS + idx];
     __syncthreads();
+    chunk_exps(m, Cc);
     chunk_scores(m, d, Cc);
-    // dA_ij = dy_i . v_j (j < i)
+    // DAL_ij = (dy_i . v_j) L_ij (j < i): the gradient of A_ij times its decay
     for (int idx = threadIdx.x; idx < Cc * Cc; idx += kThreads) {
       const int i = idx / Cc, j = idx % Cc;
       float s = 0.f;
-      if (j < i)
+      if (j < i) {
         for (int p = 0; p < d.P; ++p) s += m.dy[i * d.P + p] * m.v[j * d.P + p];
+        s *= __expf(fminf(m.da[i] - m.da[j], 0.f));
+      }
       m.dst[i * d.C + j] = s;
     }
+    __syncthreads();
     const float last = m.da[Cc - 1];
     const float E = __expf(last);
     // dtilde = E dS' + sum_i e^{da_i} dy_i q_i^T
     for (int idx = threadIdx.x; idx < PS; idx += kThreads) {
       const int p = idx / d.S, s = idx % d.S;
       float a = E * m.st[idx];
-      for (int i = 0; i < Cc; ++i) a += __expf(m.da[i]) * m.dy[i * d.P + p] * m.q[i * d.S + s];
+      for (int i = 0; i < Cc; ++i) a += m.ex[i] * m.dy[i * d.P + p] * m.q[i * d.S + s];
       m.dtl[idx] = a;
     }
     __syncthreads();
@@ -206,20 +223,18 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_kernel(
       float a = 0.f;
       for (int p = 0; p < d.P; ++p) a += m.tl[p * d.S + s] * m.dy[i * d.P + p];
       m.U[idx] = a;
-      a *= __expf(m.da[i]);
-      for (int j = 0; j < i; ++j)
-        a += m.dst[i * d.C + j] * __expf(fminf(m.da[i] - m.da[j], 0.f)) * m.k[j * d.S + s];
+      a *= m.ex[i];
+      for (int j = 0; j < i; ++j) a += m.dst[i * d.C + j] * m.k[j * d.S + s];
       gq[idx] = a;
     }
     // dk_j = sum_{i>j} dA_ij L_ij q_i + w_j dS'^T v_j
     for (int idx = threadIdx.x; idx < Cc * d.S; idx += kThreads) {
       const int j = idx / d.S, s = idx % d.S;
       float a = 0.f;
-      for (int i = j + 1; i < Cc; ++i)
-        a += m.dst[i * d.C + j] * __expf(fminf(m.da[i] - m.da[j], 0.f)) * m.q[i * d.S + s];
+      for (int i = j + 1; i < Cc; ++i) a += m.dst[i * d.C + j] * m.q[i * d.S + s];
       float b = 0.f;
       for (int p = 0; p < d.P; ++p) b += m.st[p * d.S + s] * m.v[j * d.P + p];
-      gk[idx] = a + __expf(last - m.da[j]) * b;
+      gk[idx] = a + m.wx[j] * b;
     }
     // dv_j = sum_{i>j} A_ij dy_i + w_j dS' k_j
     for (int idx = threadIdx.x; idx < Cc * d.P; idx += kThreads) {
@@ -229,31 +244,27 @@ __global__ void __launch_bounds__(kThreads) ssd_bwd_kernel(
       float b = 0.f;
       for (int s = 0; s < d.S; ++s) b += m.st[p * d.S + s] * m.k[j * d.S + s];
       m.V2[idx] = b;
-      gv[idx] = a + __expf(last - m.da[j]) * b;
+      gv[idx] = a + m.wx[j] * b;
     }
     __syncthreads();
     // decay gradient, per token (thread i < Cc), plus the chunk-last terms
     float extra_last = 0.f;
     if ((int)threadIdx.x < Cc) {
       const int i = threadIdx.x;
-      const float ei = __expf(m.da[i]);
+      const float ei = m.ex[i];
       // e^{da_i} dy_i . (tilde q_i) = e^{da_i} U_i . q_i
       float t1 = 0.f;
       for (int s = 0; s < d.S; ++s) t1 += m.U[i * d.S + s] * m.q[i * d.S + s];
       float g = ei * t1;
-      // intra-chunk decay: G_ij = dA_ij QK_ij L_ij where da_i - da_j <= 0
-      for (int j = 0; j < i; ++j) {
-        const float x = m.da[i] - m.da[j];
-        if (x <= 0.f) g += m.dst[i * d.C + j] * m.QK[i * d.C + j] * __expf(x);
-      }
-      for (int i2 = i + 1; i2 < Cc; ++i2) {
-        const float x = m.da[i2] - m.da[i];
-        if (x <= 0.f) g -= m.dst[i2 * d.C + i] * m.QK[i2 * d.C + i] * __expf(x);
-      }
+      // intra-chunk decay: G_ij = dA_ij L_ij QK_ij where da_i - da_j <= 0
+      for (int j = 0; j < i; ++j)
+        if (m.da[i] - m.da[j] <= 0.f) g += m.dst[i * d.C + j] * m.QK[i * d.C + j];
+      for (int i2 = i + 1; i2 < Cc; ++i2)
+        if (m.da[i2] - m.da[i] <= 0.f) g -= m.dst[i2 * d.C + i] * m.QK[i2 * d.C + i];
       // state write: R_i = w_i v_i^T dS' k_i enters with -1 here and +1 on the last token
       float r = 0.f;
       for (int p = 0; p < d.P; ++p) r += m.v[i * d.P + p] * m.V2[i * d.P + p];
-      r *= __expf(last - m.da[i]);
+      r *= m.wx[i];
       g -= r;
       extra_last = r;
       gda[i] = g;
