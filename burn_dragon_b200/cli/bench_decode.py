@@ -27,12 +27,13 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--layers", type=int, default=6)
+    ap.add_argument("--state-dtype", default="fp32", choices=["fp32", "bf16"])
     a = ap.parse_args()
     cfg = DragonConfig.bdh_gpu()
     cfg.n_layer = a.layers
     dev = torch.device("cuda", 0)
     model = BDH(cfg, device=dev, seed=1)
-    g = Generator(model, prefill_chunk=512)
+    g = Generator(model, prefill_chunk=512, state_dtype=a.state_dtype)
     gen = torch.Generator(device="cpu").manual_seed(20260729)
     prompt = torch.randint(0, 256, (a.batch, a.prompt), generator=gen).to(dev)
     # warm-up (compiles nothing; touches every kernel once)
@@ -53,10 +54,11 @@ def main() -> None:
     check_errors(dev)
     pre_ms = e[0].elapsed_time(e[1])
     dec_ms = e[2].elapsed_time(e[3])
-    state_bytes = cfg.n_layer * a.batch * cfg.n_head * cfg.latent_per_head * cfg.n_embd * 4
+    state_bytes = cfg.n_layer * a.batch * cfg.n_head * cfg.latent_per_head * cfg.n_embd * \
+        (2 if a.state_dtype == "bf16" else 4)
     print(json.dumps({
         "metric": "recurrent decode tokens/s (device-timed) BDH-GPU",
-        "batch": a.batch, "prompt": a.prompt, "decode_tokens": a.tokens,
+        "batch": a.batch, "prompt": a.prompt, "decode_tokens": a.tokens, "state_dtype": a.state_dtype,
         "prefill_tokens_per_s": round(a.batch * a.prompt / (pre_ms / 1e3), 1),
         "decode_tokens_per_s": round(a.batch * a.tokens / (dec_ms / 1e3), 1),
         "decode_ms_per_token": round(dec_ms / a.tokens, 3),

@@ -13,6 +13,8 @@
 #include <cuda_bf16.h>
 #include <torch/extension.h>
 
+#include <type_traits>
+
 namespace bd {
 namespace {
 
@@ -21,8 +23,25 @@ constexpr int kRows = 64;  // latent rows per CTA
 __device__ __forceinline__ float to_f(float x) { return x; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
 
-template <typename QT>
-__global__ void rho_step_kernel(float* __restrict__ rho, const QT* __restrict__ q, long long q_row_stride,
+// 4 state values: fp32 (16 bytes) or bf16 (8 bytes, rounded to nearest on store)
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void st4(__nv_bfloat16* p, float4 v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<unsigned int*>(&a);
+  u.y = *reinterpret_cast<unsigned int*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+template <typename QT, typename RT>
+__global__ void rho_step_kernel(RT* __restrict__ rho, const QT* __restrict__ q, long long q_row_stride,
                                 const float* __restrict__ v, const float* __restrict__ gamma, float* __restrict__ a,
                                 int H, int Nh, int D) {
   __shared__ float4 red[4][64];
@@ -32,7 +51,7 @@ __global__ void rho_step_kernel(float* __restrict__ rho, const QT* __restrict__ 
   const int c4 = threadIdx.x & 63;  // column group (4 floats)
   const int ph = threadIdx.x >> 6;  // row phase 0..3
   const float g = gamma ? gamma[h] : 1.0f;
-  float4* R = reinterpret_cast<float4*>(rho + ((size_t)bh * Nh) * D);
+  RT* R = rho + ((size_t)bh * Nh) * D;
   const QT* qb = q + (size_t)b * q_row_stride + (size_t)h * Nh;
   float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -49,7 +68,7 @@ __global__ void rho_step_kernel(float* __restrict__ rho, const QT* __restrict__ 
         // read and write are skipped (exact; q is ReLU-sparse, so many rows are 0). The
         // branch is uniform over a warp (all its lanes share the row phase).
         if (qj == 0.0f && g == 1.0f) continue;
-        float4 r = R[(size_t)j * D4 + c];
+        float4 r = ld4(R + ((size_t)j * D4 + c) * 4);
         acc.x += qj * r.x;
         acc.y += qj * r.y;
         acc.z += qj * r.z;
@@ -58,7 +77,7 @@ __global__ void rho_step_kernel(float* __restrict__ rho, const QT* __restrict__ 
         r.y = (r.y + qj * vv.y) * g;
         r.z = (r.z + qj * vv.z) * g;
         r.w = (r.w + qj * vv.w) * g;
-        R[(size_t)j * D4 + c] = r;
+        st4(R + ((size_t)j * D4 + c) * 4, r);
       }
     }
     red[ph][c4] = acc;
@@ -84,29 +103,34 @@ __global__ void rho_step_kernel(float* __restrict__ rho, const QT* __restrict__ 
 
 }  // namespace
 
-// rho [B,H,Nh,D] fp32 (updated in place); q rows [B, >= H*Nh] (bf16 or fp32, row stride
+// rho [B,H,Nh,D] fp32 or bf16 (updated in place); q rows [B, >= H*Nh] (bf16 or fp32, row stride
 // q_row_stride elements); v [B,D] fp32; gamma [H] or None; a [B,H,D] fp32, pre-zeroed.
 void rho_step(const at::Tensor& rho, const at::Tensor& q, int64_t q_row_stride, const at::Tensor& v,
               const c10::optional<at::Tensor>& gamma, const at::Tensor& a, int64_t B, int64_t H, int64_t Nh,
               int64_t D) {
   c10::cuda::CUDAGuard g(rho.get_device());
-  TORCH_CHECK(rho.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat && a.scalar_type() == at::kFloat,
-              "rho_step: rho, v and a must be fp32");
+  TORCH_CHECK((rho.scalar_type() == at::kFloat || rho.scalar_type() == at::kBFloat16) &&
+                  v.scalar_type() == at::kFloat && a.scalar_type() == at::kFloat,
+              "rho_step: rho fp32 or bf16, v and a fp32");
   TORCH_CHECK(D % 4 == 0, "rho_step: D must be a multiple of 4");
   dim3 grid((unsigned)((Nh + kRows - 1) / kRows), (unsigned)(B * H));
   auto st = at::cuda::getCurrentCUDAStream(rho.get_device()).stream();
   const float* gp = gamma ? gamma->data_ptr<float>() : nullptr;
-  if (q.scalar_type() == at::kBFloat16) {
-    rho_step_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(rho.data_ptr<float>(),
-                                                         reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
-                                                         q_row_stride, v.data_ptr<float>(), gp, a.data_ptr<float>(),
-                                                         (int)H, (int)Nh, (int)D);
-  } else {
-    TORCH_CHECK(q.scalar_type() == at::kFloat, "rho_step: q must be bf16 or fp32");
-    rho_step_kernel<float><<<grid, 256, 0, st>>>(rho.data_ptr<float>(), q.data_ptr<float>(), q_row_stride,
-                                                 v.data_ptr<float>(), gp, a.data_ptr<float>(), (int)H, (int)Nh,
-                                                 (int)D);
-  }
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 || q.scalar_type() == at::kFloat, "rho_step: q must be bf16 or fp32");
+  auto go = [&](auto* r) {
+    using RT = std::remove_pointer_t<decltype(r)>;
+    if (q.scalar_type() == at::kBFloat16)
+      rho_step_kernel<__nv_bfloat16, RT><<<grid, 256, 0, st>>>(
+          r, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q_row_stride, v.data_ptr<float>(), gp,
+          a.data_ptr<float>(), (int)H, (int)Nh, (int)D);
+    else
+      rho_step_kernel<float, RT><<<grid, 256, 0, st>>>(r, q.data_ptr<float>(), q_row_stride, v.data_ptr<float>(), gp,
+                                                       a.data_ptr<float>(), (int)H, (int)Nh, (int)D);
+  };
+  if (rho.scalar_type() == at::kFloat)
+    go(rho.data_ptr<float>());
+  else
+    go(reinterpret_cast<__nv_bfloat16*>(rho.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -66,7 +66,14 @@ class _DecodeWorkspace:
 
 
 class Generator:
-    def __init__(self, model, prefill_chunk: int = 512):
+    def __init__(self, model, prefill_chunk: int = 512, state_dtype: str = "fp32"):
+        """``state_dtype`` "bf16": the decode steps keep the recurrent state rho in bf16
+        (half the state traffic, which is the whole cost of a decode token; each update is
+        computed in fp32 and rounded once when stored). The prefill still builds the state
+        in fp32; it is rounded to bf16 at the first decode step."""
+        if state_dtype not in ("fp32", "bf16"):
+            raise ValueError("state_dtype must be 'fp32' or 'bf16'")
+        self.state_dtype = state_dtype
         self.model = model
         self.cfg = model.cfg
         self.prefill_chunk = prefill_chunk
@@ -114,7 +121,10 @@ class Generator:
         p32 = self.model.store.views(self.model.store.data)
         p16 = self.model.shadow_dict()
         for s in range(0, T, chunk):
-            outs = f.forward(p16, p32, prompt[:, s:s + chunk], pos0=state.position, rho0s=state.rhos,
+            rho0s = state.rhos
+            if rho0s is not None and rho0s[0].dtype != torch.float32:
+                rho0s = [r.float() for r in rho0s]  # the prefill carries its state in fp32
+            outs = f.forward(p16, p32, prompt[:, s:s + chunk], pos0=state.position, rho0s=rho0s,
                              want_state=True)
             state.rhos = outs
             state.position += chunk
@@ -142,8 +152,11 @@ class Generator:
         p16 = self.model.shadow_dict()
         gam, bet, eps = p32["norm_gamma"], p32["norm_beta"], cfg.norm_eps
         thr, thr_y = cfg.thresholds()
+        sdt = torch.bfloat16 if self.state_dtype == "bf16" else torch.float32
         if state.rhos is None:
-            state.rhos = [torch.zeros(B, H, Nh, D, device=tokens.device) for _ in range(cfg.n_layer)]
+            state.rhos = [torch.zeros(B, H, Nh, D, device=tokens.device, dtype=sdt) for _ in range(cfg.n_layer)]
+        elif state.rhos[0].dtype != sdt:
+            state.rhos = [r.to(sdt) for r in state.rhos]
         mod.ln_fwd(p32["embed"], tokens, B, D, gam, bet, eps, w.v32[0], w.v16[0], w.amean, w.arstd)
         B_enc = Operand(p16["encoder"], True, Nh, D, Nh, z1=(H, D * Nh))
         B_encv = Operand(p16["encoder_v"], True, Nh, D, Nh, z1=(H, D * Nh))

@@ -62,7 +62,10 @@ def test_rho_step_kernel_matches_recurrence():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("rotary", ["rope", "alibi"])
-def test_gpu_prefill_and_decode_match_reference(rotary):
+@pytest.mark.parametrize("state_dtype", ["fp32", "bf16"])
+def test_gpu_prefill_and_decode_match_reference(rotary, state_dtype):
+    """Prefill + decode against the fp32 teacher-forced oracle; with a bf16 decode state
+    the bound is the same (the state is rounded once per update)."""
     cfg = _cfg(rotary)
     model = BDH(cfg, device="cuda", seed=6)
     with torch.no_grad():
@@ -75,7 +78,7 @@ def test_gpu_prefill_and_decode_match_reference(rotary):
     B, T = 2, 256
     toks = torch.randint(0, 256, (B, T + 4), device="cuda")
     full, _ = R.bdh_forward(toks, params, cfg)
-    g = Generator(model, prefill_chunk=128)
+    g = Generator(model, prefill_chunk=128, state_dtype=state_dtype)
     logits, st = g.prefill(toks[:, :T])
 
     def rel(a, b):
@@ -85,6 +88,8 @@ def test_gpu_prefill_and_decode_match_reference(rotary):
     for i in range(T, T + 4):
         logits = g.decode_step(toks[:, i], st)
         assert rel(logits, full[:, i]) < 0.03, i
+    if state_dtype == "bf16":
+        assert st.rhos[0].dtype == torch.bfloat16
 
 
 def test_ragged_batch_matches_serial_greedy():
