@@ -40,6 +40,8 @@ void adamw(const at::Tensor& p, const at::Tensor& g, const at::Tensor& m, const 
            const c10::optional<at::Tensor>& hyper);
 void grad_clip_coef(const at::Tensor& g, const at::Tensor& scratch3, double max_norm);
 void cast_bf16(const at::Tensor& x, const at::Tensor& y);
+void embed_grad(const at::Tensor& tokens, const at::Tensor& g, int64_t rows, int64_t D, const at::Tensor& out,
+                bool accumulate, const c10::optional<at::Tensor>& perm, const c10::optional<at::Tensor>& seg);
 void rho_step(const at::Tensor& rho, const at::Tensor& q, int64_t q_row_stride, const at::Tensor& v,
               const c10::optional<at::Tensor>& gamma, const at::Tensor& a, int64_t B, int64_t H, int64_t Nh,
               int64_t D);
@@ -106,6 +108,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_table", &bd::rope_table);
   m.def("ln_fwd", &bd::ln_fwd);
   m.def("ln_bwd", &bd::ln_bwd);
+  m.def("embed_grad", &bd::embed_grad);
   m.def("tail_fwd", &bd::tail_fwd);
   m.def("tail_bwd", &bd::tail_bwd);
   m.def("sum_rows", &bd::sum_rows);

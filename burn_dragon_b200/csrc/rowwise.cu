@@ -334,6 +334,51 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
+// Embedding-table gradient: out[v, :] (+)= the sum of g[r, :] over the rows r whose token
+// is v, added in increasing r (no atomics, so two runs give bitwise equal gradients).
+// Block (v, column slab of 256). Without `seg` the block scans every token (the cheap
+// choice for byte-sized vocabularies); with `seg` (offsets of a stable token sort, [V + 1])
+// it walks only its own rows `perm[seg[v] .. seg[v + 1])`.
+__global__ void __launch_bounds__(256) embed_grad_kernel(const int64_t* __restrict__ tokens,
+                                                         const int64_t* __restrict__ perm,
+                                                         const int64_t* __restrict__ seg,
+                                                         const float* __restrict__ g, long long rows, int D,
+                                                         float* __restrict__ out, int accumulate) {
+  __shared__ int idx[256];
+  __shared__ int wcount[8];
+  const int v = blockIdx.x;
+  const int col = blockIdx.y * 256 + threadIdx.x;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float acc = 0.f;
+  if (seg != nullptr) {
+    if (col < D)
+      for (long long i = seg[v]; i < seg[v + 1]; ++i) acc += g[perm[i] * D + col];
+  } else {
+    for (long long base = 0; base < rows; base += 256) {
+      const long long r = base + threadIdx.x;
+      const bool hit = r < rows && tokens[r] == v;
+      const unsigned m = __ballot_sync(0xffffffffu, hit);
+      if (lane == 0) wcount[warp] = __popc(m);
+      __syncthreads();
+      int off = 0, total = 0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        off += w < warp ? wcount[w] : 0;
+        total += wcount[w];
+      }
+      if (hit) idx[off + __popc(m & ((1u << lane) - 1u))] = (int)(r - base);
+      __syncthreads();
+      if (col < D)
+        for (int i = 0; i < total; ++i) acc += g[(base + idx[i]) * D + col];
+      __syncthreads();
+    }
+  }
+  if (col < D) {
+    float* o = out + (size_t)v * D + col;
+    *o = accumulate ? *o + acc : acc;
+  }
+}
+
 __global__ void sumsq_kernel(const float* __restrict__ x, long long n, float* __restrict__ out) {
   float s = 0.f;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -534,6 +579,23 @@ void grad_clip_coef(const at::Tensor& g, const at::Tensor& scratch3, double max_
   C10_CUDA_CHECK(cudaMemsetAsync(scratch3.data_ptr(), 0, sizeof(float), cur_stream(g)));
   sumsq_kernel<<<148 * 4, 256, 0, cur_stream(g)>>>(g.data_ptr<float>(), g.numel(), scratch3.data_ptr<float>());
   clip_coef_kernel<<<1, 1, 0, cur_stream(g)>>>(scratch3.data_ptr<float>(), (float)max_norm);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void embed_grad(const at::Tensor& tokens, const at::Tensor& g, int64_t rows, int64_t D, const at::Tensor& out,
+                bool accumulate, const c10::optional<at::Tensor>& perm, const c10::optional<at::Tensor>& seg) {
+  c10::cuda::CUDAGuard gd(g.get_device());
+  TORCH_CHECK(tokens.is_contiguous() && g.is_contiguous() && out.is_contiguous(), "embed_grad: contiguous inputs");
+  TORCH_CHECK(tokens.scalar_type() == at::kLong && g.scalar_type() == at::kFloat && out.scalar_type() == at::kFloat,
+              "embed_grad: int64 tokens, fp32 gradient rows and table");
+  TORCH_CHECK(tokens.numel() >= rows && g.numel() >= rows * D && out.size(1) == D, "embed_grad: shapes");
+  TORCH_CHECK(!perm == !seg, "embed_grad: perm and seg go together");
+  const int64_t V = out.size(0);
+  if (seg) TORCH_CHECK(seg->numel() == V + 1 && perm->numel() >= rows, "embed_grad: seg needs V + 1 offsets");
+  dim3 grid((unsigned)V, (unsigned)((D + 255) / 256));
+  embed_grad_kernel<<<grid, 256, 0, cur_stream(g)>>>(tokens.data_ptr<int64_t>(), opt_ptr<const int64_t>(perm),
+                                                     opt_ptr<const int64_t>(seg), g.data_ptr<float>(), rows, (int)D,
+                                                     out.data_ptr<float>(), accumulate ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -37,6 +37,28 @@ STORES_X = True
 ROPE_TABLE = os.environ.get("BDH_ROPE_TABLE", "0") == "1"
 
 
+# Vocabularies up to this size take the scan form of the embedding-gradient kernel
+# (every block reads the token list); larger ones walk a stable token sort.
+EMBED_SCAN_MAX_V = 1024
+
+
+def embed_grad(mod, tokens: torch.Tensor, rows_grad: torch.Tensor, table_grad: torch.Tensor,
+               accumulate: bool) -> None:
+    """table_grad[v] (+)= sum of rows_grad[r] over rows with tokens[r] == v, in row order
+    (deterministic: no atomics). ``tokens`` int64 [R], ``rows_grad`` fp32 [R, D]."""
+    tok = tokens.reshape(-1)
+    if tok.dtype != torch.int64 or not tok.is_contiguous():
+        tok = tok.to(torch.int64).contiguous()
+    R, D = rows_grad.shape
+    V = table_grad.shape[0]
+    if V <= EMBED_SCAN_MAX_V:
+        mod.embed_grad(tok, rows_grad, R, D, table_grad, accumulate, None, None)
+        return
+    srt, perm = torch.sort(tok, stable=True)
+    seg = torch.searchsorted(srt, torch.arange(V + 1, device=tok.device, dtype=torch.int64))
+    mod.embed_grad(tok, rows_grad, R, D, table_grad, accumulate, perm, seg)
+
+
 def fused_unsupported(cfg) -> str | None:
     """The first model option the fused kernels do not implement, or None: they
     implement dropout 0 (as the BDH-GPU profiles use), LayerNorm, RoPE / ALiBi / no
@@ -499,19 +521,20 @@ class FusedBDH:
         if with_embed:
             # embedding LayerNorm and gather
             demb = ws.dv_res  # reuse as fp32 [M, D] scratch
-            if not accumulate:
-                g32["embed"].zero_()
             if sp:
                 rows = own.stop - own.start
                 head_parts.append(mod.ln_bwd(dv[own], ws.emb_rows[own], ws.emean[own], ws.erstd[own], rows, D, gam,
                                              0, 0, None, demb[own]))
-                ge = torch.zeros_like(g32["embed"])
-                ge.index_add_(0, tokens.reshape(-1)[own], demb[own])
+                ge = torch.empty_like(g32["embed"])
+                embed_grad(mod, tokens.reshape(-1)[own].contiguous(), demb[own], ge, accumulate=False)
                 tp.all_reduce(ge)  # every rank's own-row contributions
-                g32["embed"].add_(ge)
+                if accumulate:
+                    g32["embed"].add_(ge)
+                else:
+                    g32["embed"].copy_(ge)
             else:
                 parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb))
-                g32["embed"].index_add_(0, tokens.reshape(-1), demb)
+                embed_grad(mod, tokens.reshape(-1), demb, g32["embed"], accumulate=accumulate)
         elif not accumulate:
             g32["embed"].zero_()
         allp = torch.cat(parts, 0).sum(0) if parts else 0.0

@@ -157,3 +157,28 @@ def test_fused_step_is_bitwise_reproducible():
     torch.cuda.synchronize()
     assert torch.equal(l1, l2)
     assert torch.equal(g1, model.store.grad)
+
+
+@pytest.mark.parametrize("V,D,R", [(256, 256, 4096), (3000, 96, 1000)])
+def test_embed_grad_kernel_matches_index_add(V, D, R):
+    """The embedding-gradient kernel (scan form for small vocabularies, stable-sort form
+    for large ones) against an fp32 index_add_, and bitwise equal across two calls."""
+    from burn_dragon_b200 import _ext
+    from burn_dragon_b200.models.bdh_fused import embed_grad
+
+    mod = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    tok = torch.randint(0, V, (R,), device="cuda", generator=g)
+    rows = torch.randn(R, D, device="cuda", generator=g)
+    base = torch.randn(V, D, device="cuda", generator=g)
+    ref = base.double().index_add_(0, tok, rows.double()).float()
+    out1 = base.clone()
+    embed_grad(mod, tok, rows, out1, accumulate=True)
+    out2 = base.clone()
+    embed_grad(mod, tok, rows, out2, accumulate=True)
+    fresh = torch.full_like(base, 7.0)
+    embed_grad(mod, tok, rows, fresh, accumulate=False)
+    torch.cuda.synchronize()
+    assert torch.allclose(out1, ref, rtol=1e-5, atol=1e-4)
+    assert torch.equal(out1, out2)
+    assert torch.allclose(fresh, ref - base, rtol=1e-5, atol=1e-4)
