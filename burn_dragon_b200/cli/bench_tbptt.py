@@ -67,11 +67,24 @@ def main() -> None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms = float(ms_t.item())
     if rank == 0:
+        # the carried state adds three contractions per layer (state read, state update and
+        # its backward): the plain step's FLOPs at the same batch and their share explain
+        # the per-token gap to plain training
+        from ..models.bdh_fused import STORES_X
+        from ..train.roofline import step_totals
+
+        full = step_totals(cfg, a.batch, a.chunk, params=tr.model.store.numel, store_x=STORES_X, stateful=True)
+        plain = step_totals(cfg, a.batch, a.chunk, params=tr.model.store.numel, store_x=STORES_X)
+        step_s = ms / steps / 1e3
         print(json.dumps({
             "metric": "stateful TBPTT train tokens/s (device-timed, max over ranks) BDH-GPU",
             "n_gpus": world, "batch_per_gpu": a.batch, "stream": a.stream, "chunk": a.chunk, "steps": steps,
             "tokens_per_s": round(world * a.batch * a.stream / (ms / 1e3), 1),
             "ms_per_chunk_step": round(ms / steps, 3), "final_loss": float(loss),
+            "chunk_step_tflop": round(full["tflop"], 3), "plain_step_tflop": round(plain["tflop"], 3),
+            "state_flop_share": round(1 - plain["tflop"] / full["tflop"], 3),
+            "achieved_tflops": round(full["tflop"] / step_s, 1),
+            "frac_step_floor": round(full["floor_ms"] / (step_s * 1e3), 3),
         }), flush=True)
     if world > 1:
         if tr.comm is not None:

@@ -16,17 +16,21 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
 void rope_table(const at::Tensor& freq, int64_t pos0, int64_t T, const at::Tensor& out);
 void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_t rows, int64_t D,
             const at::Tensor& gamma, const at::Tensor& beta, double eps, const c10::optional<at::Tensor>& y32,
-            const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd);
+            const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd, int64_t norm_kind,
+            const c10::optional<at::Tensor>& norm_alpha, const c10::optional<at::Tensor>& norm_shift);
 at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
                   int64_t rows, int64_t D, const at::Tensor& gamma, int64_t remap_T, int64_t remap_H,
-                  const c10::optional<at::Tensor>& dx16, const c10::optional<at::Tensor>& dx32);
+                  const c10::optional<at::Tensor>& dx16, const c10::optional<at::Tensor>& dx32, int64_t norm_kind,
+            const c10::optional<at::Tensor>& norm_alpha, const c10::optional<at::Tensor>& norm_shift);
 void tail_fwd(const at::Tensor& partial, int64_t nsplit, int64_t split_stride, const at::Tensor& v, int64_t rows,
               int64_t D, const at::Tensor& gamma, const at::Tensor& beta, double eps,
               const c10::optional<at::Tensor>& m_out, const at::Tensor& vout32,
-              const c10::optional<at::Tensor>& vout16, const c10::optional<at::Tensor>& st);
+              const c10::optional<at::Tensor>& vout16, const c10::optional<at::Tensor>& st, int64_t norm_kind,
+            const c10::optional<at::Tensor>& norm_alpha, const c10::optional<at::Tensor>& norm_shift);
 at::Tensor tail_bwd(const at::Tensor& gin, const at::Tensor& v, const at::Tensor& m, const at::Tensor& st,
                     int64_t rows, int64_t D, const at::Tensor& gamma, const at::Tensor& beta, const at::Tensor& dm16,
-                    const at::Tensor& dv_res);
+                    const at::Tensor& dv_res, int64_t norm_kind,
+            const c10::optional<at::Tensor>& norm_alpha, const c10::optional<at::Tensor>& norm_shift);
 void sum_rows(const at::Tensor& out, const c10::optional<at::Tensor>& base, const at::Tensor& p0, int64_t n0,
               int64_t s0, const c10::optional<at::Tensor>& p1, int64_t n1, int64_t s1, int64_t total);
 void cross_entropy(const at::Tensor& logits, const at::Tensor& target, const c10::optional<at::Tensor>& mask,
@@ -106,11 +110,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "burn_dragon_b200 sm_100a kernels (tcgen05 GEMM engine + row kernels)";
   m.def("gemm", &bd::gemm);
   m.def("rope_table", &bd::rope_table);
-  m.def("ln_fwd", &bd::ln_fwd);
-  m.def("ln_bwd", &bd::ln_bwd);
+  // trailing norm arguments: kind 0 LayerNorm, 1 RMSNorm, 2 DynamicTanh, 3 Derf (alpha /
+  // shift: 1-element fp32 device tensors of the learnable scalars)
+  m.def("ln_fwd", &bd::ln_fwd, py::arg("x"), py::arg("tokens"), py::arg("rows"), py::arg("D"), py::arg("gamma"),
+        py::arg("beta"), py::arg("eps"), py::arg("y32"), py::arg("y16"), py::arg("mean"), py::arg("rstd"), py::arg("norm_kind") = 0, py::arg("norm_alpha") = py::none(), py::arg("norm_shift") = py::none());
+  m.def("ln_bwd", &bd::ln_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"), py::arg("rows"),
+        py::arg("D"), py::arg("gamma"), py::arg("remap_T"), py::arg("remap_H"), py::arg("dx16"), py::arg("dx32"),
+        py::arg("norm_kind") = 0, py::arg("norm_alpha") = py::none(), py::arg("norm_shift") = py::none());
   m.def("embed_grad", &bd::embed_grad);
-  m.def("tail_fwd", &bd::tail_fwd);
-  m.def("tail_bwd", &bd::tail_bwd);
+  m.def("tail_fwd", &bd::tail_fwd, py::arg("partial"), py::arg("nsplit"), py::arg("split_stride"), py::arg("v"),
+        py::arg("rows"), py::arg("D"), py::arg("gamma"), py::arg("beta"), py::arg("eps"), py::arg("m_out"),
+        py::arg("vout32"), py::arg("vout16"), py::arg("st"), py::arg("norm_kind") = 0, py::arg("norm_alpha") = py::none(), py::arg("norm_shift") = py::none());
+  m.def("tail_bwd", &bd::tail_bwd, py::arg("gin"), py::arg("v"), py::arg("m"), py::arg("st"), py::arg("rows"),
+        py::arg("D"), py::arg("gamma"), py::arg("beta"), py::arg("dm16"), py::arg("dv_res"), py::arg("norm_kind") = 0, py::arg("norm_alpha") = py::none(), py::arg("norm_shift") = py::none());
   m.def("sum_rows", &bd::sum_rows);
   m.def("cross_entropy", &bd::cross_entropy);
   m.def("symmetrize", &bd::symmetrize);

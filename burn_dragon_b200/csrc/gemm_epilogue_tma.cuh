@@ -24,12 +24,9 @@ constexpr int epi_naux() {
 }
 
 // The x > 0 mask rides in dx_part: the decoder backward writes -0.0 (bf16 0x8000) where
-// x <= 0 and flushes |value| < 1e-30 to +0.0 elsewhere, so no live entry carries the
-// 0x8000 pattern; dQ reads the mask from those bits instead of re-reading x, and keeps
-// the marker in its output for a second dQ pass over the same buffer.
-constexpr unsigned short kMaskedBits = 0x8000u;
-
-__device__ __forceinline__ float flush_live(float v) { return fabsf(v) < 1e-30f ? 0.0f : v; }
+// x <= 0 and never writes -0.0 elsewhere, so no live entry carries the 0x8000 pattern; dQ
+// reads the mask from those bits instead of re-reading x, and keeps the marker in its
+// output for a second dQ pass over the same buffer.
 
 // In-place math on the smem tiles b0 (and b1) for this thread's row.
 template <int CW>
@@ -63,6 +60,17 @@ __device__ __forceinline__ void rope_cs4(const EpiParams& e, float pos, int trow
   }
 }
 
+// cos / sin of four consecutive RoPE pairs from one 16-byte word of the staged half2 table.
+__device__ __forceinline__ void rope_cs4_word(uint4 u, float (&cs)[4], float (&sn)[4]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    cs[i] = f.x;
+    sn[i] = f.y;
+  }
+}
+
 template <int EPI, int CW>
 __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoord& tc, float (&v)[CW], int row,
                                              int col0, uint8_t* b0, uint8_t* b1, int lane) {
@@ -89,12 +97,17 @@ __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoor
     uint4* s0 = reinterpret_cast<uint4*>(b0 + epi_off<CW>(lane, c));
     uint4* s1 = reinterpret_cast<uint4*>(b1 + epi_off<CW>(lane, c));
     if constexpr (EPI == EPI_RELU_ROPE) {
+      // with a staged phase table, its word for these four pairs sits where x goes
+      const uint4 tw = e.rope_tma ? *s0 : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
       for (int i = 0; i < 8; ++i) w[i] = fmaxf(w[i] - e.thr, 0.0f);
       *s0 = pack8(w);
       if (e.freq) {
         float cs[4], sn[4];
-        rope_cs4(e, pos, trow, j0 + 8 * c, cs, sn);
+        if (e.rope_tma)
+          rope_cs4_word(tw, cs, sn);
+        else
+          rope_cs4(e, pos, trow, j0 + 8 * c, cs, sn);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float xe = w[2 * i], xo = w[2 * i + 1];
@@ -113,21 +126,22 @@ __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoor
       float xv[8], yv[8], dy[8];
       unpack8(*s0, xv);
       unpack8(*s1, yv);
+      // x >= 0 and yn = y x >= 0, so yn > 0 implies x > 0. dx_part = g yn / x on live
+      // entries: adding +0.0 turns an exact -0.0 quotient (g < 0, yn = 0) into +0.0, so a
+      // live entry never carries the mask pattern (a nonzero quotient keeps its sign and
+      // rounds to a nonzero bf16 unless its magnitude is below 1e-40).
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float g = w[i];
-        const bool live = xv[i] > 0.0f;
-        const float y = live ? __fdividef(yv[i], xv[i]) : 0.0f;
-        dy[i] = (yv[i] > 0.0f) ? g * xv[i] : 0.0f;
-        w[i] = live ? flush_live(g * y) : -0.0f;
+        dy[i] = yv[i] > 0.0f ? g * xv[i] : 0.0f;
+        const float dxp = __fdividef(g * yv[i], xv[i]) + 0.0f;
+        w[i] = xv[i] > 0.0f ? dxp : -0.0f;
       }
       *s0 = pack8(w);
       *s1 = pack8(dy);
     } else if constexpr (EPI == EPI_DQ) {
       float bv[8];
-      const uint4 raw = *s0;
-      const unsigned short* bits = reinterpret_cast<const unsigned short*>(&raw);
-      unpack8(raw, bv);
+      unpack8(*s0, bv);
       if (e.freq) {
         float cs[4], sn[4];
         rope_cs4(e, pos, trow, j0 + 8 * c, cs, sn);
@@ -138,8 +152,10 @@ __device__ __forceinline__ void tma_epi_math(const GemmParams& p, const TileCoor
           w[2 * i + 1] = go * cs[i] - ge * sn[i];
         }
       }
+      // a masked entry is exactly -0.0 (0x80000000 once widened); a live entry is never
+      // -0.0, and w + bv of a live entry is -0.0 only if both are, so the sum needs no flush
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = bits[i] == kMaskedBits ? -0.0f : flush_live(w[i] + bv[i]);
+      for (int i = 0; i < 8; ++i) w[i] = __float_as_uint(bv[i]) == 0x80000000u ? -0.0f : w[i] + bv[i];
       *s0 = pack8(w);
     }
   }
@@ -195,17 +211,28 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
   const bool probe = (p.e.probe & 1) != 0;
   const bool dstore = CW == 64 && (p.e.probe & 2) != 0;
   const bool dload = CW == 64 && (p.e.probe & 4) != 0;
+  // The x-projection's RoPE phases may come as a staged table: a [T, Nh/2] half2 (cos, sin)
+  // tensor whose 32-row x CW/2-pair box has the byte geometry of a bf16 output box, fetched
+  // into the buffer x is then written over.
+  const bool tab = EPI == EPI_RELU_ROPE && p.e.rope_tma != 0;
+  const bool has_aux = NAUX > 0 || tab;
   auto issue_aux = [&](int t, int c, int u) {
+    if (!has_aux) return;
+    if (t >= total || probe || dload) return;
+    const TileCoord n = tile(t);
+    if (n.zero) return;
+    issued_upto = u;
+    const int b = u % NBUF;
+    if (lane != 0) return;
+    uint8_t* dst = wbuf + b * TENS * kTmaTileBytes;
+    const int col = n.n0 + grp_off + c * CW;
+    fence_proxy_async_smem();
+    if (tab) {
+      mbar_arrive_expect_tx(&aux_bar[ew][b], kTmaTileBytes);
+      tma_load_4d(dst, &p.tx0, &aux_bar[ew][b], col >> 1, (n.m0 + quad * 32) % p.e.T, 0, 0);
+      return;
+    }
     if constexpr (NAUX > 0) {
-      if (t >= total || probe || dload) return;
-      const TileCoord n = tile(t);
-      if (n.zero) return;
-      issued_upto = u;
-      const int b = u % NBUF;
-      if (lane != 0) return;
-      uint8_t* dst = wbuf + b * TENS * kTmaTileBytes;
-      const int col = n.n0 + grp_off + c * CW;
-      fence_proxy_async_smem();
       mbar_arrive_expect_tx(&aux_bar[ew][b], NAUX * kTmaTileBytes);
       tma_load_4d(dst, &p.tx0, &aux_bar[ew][b], col, n.m0 + quad * 32, n.z1, n.z2);
       if constexpr (NAUX > 1)
@@ -229,7 +256,7 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
       // aux prefetch (x-projection) only this unit's buffer, stored two units ago, must be
       // free, so the previous unit's store may still be reading
       if (lane == 0) {
-        if constexpr (NBUF == 3 || NAUX == 0)
+        if (NBUF == 3 || !has_aux)
           bulk_wait_group_read1();
         else
           bulk_wait_group_read0();
@@ -274,8 +301,8 @@ __device__ __forceinline__ void tma_epilogue_loop(const GemmParams& p, int total
       const long long goff = (long long)tc.z2 * p.e.sz2 + (long long)tc.z1 * p.e.sz1 +
                              (long long)(tc.m0 + quad * 32) * p.e.ld + tc.n0 + col_off;
       const int rows_ok = min(32, p.M - (tc.m0 + quad * 32)), cols_ok = min(CW, p.N - (tc.n0 + col_off));
-      if constexpr (NAUX > 0) {
-        if (dload) {
+      if (has_aux) {
+        if (dload && NAUX > 0) {
           coop_load(p.e.aux0 + goff, p.e.ld, rows_ok, cols_ok, b0, lane);
           if constexpr (NAUX > 1) coop_load(p.e.aux1 + goff, p.e.ld, rows_ok, cols_ok, b1, lane);
           __syncwarp();

@@ -92,6 +92,25 @@ CUtensorMap encode_out_map(const void* ptr, int64_t N, int64_t M, int64_t ld, in
   return m;
 }
 
+// The RoPE phase table [T, Nh/2] of half2 (cos, sin) words as 32-row boxes of cols / 2
+// words: the byte geometry (and swizzle) of a 32 x cols bf16 output box, so chunk c of a
+// table box holds the phases of chunk c of the x / q boxes.
+CUtensorMap encode_table_map(const void* ptr, int64_t pairs, int64_t T, uint32_t cols) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "RoPE table must be 16-byte aligned");
+  cuuint64_t dims[4] = {(cuuint64_t)pairs, (cuuint64_t)T, 1, 1};
+  const cuuint64_t row = (cuuint64_t)pairs * 4;
+  cuuint64_t strides[3] = {row, row * (cuuint64_t)T, row * (cuuint64_t)T};
+  cuuint32_t box[4] = {cols / 2, 32, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMap m;
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (RoPE table map) failed with code ", (int)r);
+  return m;
+}
+
 int num_sms(int dev) {
   static int cached[64] = {0};
   if (cached[dev] == 0) {
@@ -183,10 +202,18 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
   e.thr = (float)thr;
   e.freq = freq ? freq->data_ptr<float>() : nullptr;
   e.rope_tab = nullptr;
+  e.rope_tma = 0;
   if (rope_tab && e.freq) {
     TORCH_CHECK(rope_tab->scalar_type() == at::kInt && rope_tab->numel() >= T * (Nh / 2) && Nh % 8 == 0,
                 "rope_tab: int32 (half2) table of T x Nh/2 phases");
-    e.rope_tab = reinterpret_cast<const uint32_t*>(rope_tab->data_ptr());
+    if (epi == EPI_RELU_ROPE) {
+      // staged by the epilogue's TMA ring (map encoded below with the output maps)
+      TORCH_CHECK(T % 32 == 0 && Nh % 64 == 0 && rope_tab->is_contiguous(),
+                  "staged RoPE table: T % 32 == 0, Nh % 64 == 0, contiguous");
+      e.rope_tma = 1;
+    } else {
+      e.rope_tab = reinterpret_cast<const uint32_t*>(rope_tab->data_ptr());
+    }
   }
   e.log2_decay = log2_decay ? log2_decay->data_ptr<float>() : nullptr;
   e.T = (int)T;
@@ -243,6 +270,7 @@ void gemm(int64_t epi, int64_t bn, const at::Tensor& a, bool a_mn, std::vector<i
     p.to0 = encode_out_map(e.out0, N, M, ld, Z1, sz1, Z2, sz2, cw);
     if (e.out1) p.to1 = encode_out_map(e.out1, N, M, ld, Z1, sz1, Z2, sz2, cw);
     if (e.aux0) p.tx0 = encode_out_map(e.aux0, N, M, ld, Z1, sz1, Z2, sz2, cw);
+    if (e.rope_tma) p.tx0 = encode_table_map(rope_tab->data_ptr(), Nh / 2, T, cw);
     if (e.aux1) p.tx1 = encode_out_map(e.aux1, N, M, ld, Z1, sz1, Z2, sz2, cw);
   }
   hit->fn(p, at::cuda::getCurrentCUDAStream(dev).stream(), dev);

@@ -53,6 +53,8 @@ struct EpiParams {
   const float* freq;       // RoPE frequency per latent column (cycles / position), or null
   const uint32_t* rope_tab;  // or null: (cos, sin) as half2 per (row % T, column pair), row
                              // stride Nh / 2, phases of positions pos0 + (row % T)
+  int rope_tma;            // EPI_RELU_ROPE: the phases come as a staged table (the half2
+                           // [T, Nh/2] table of positions pos0 + t, TMA map tx0), not rope_tab
   const float* log2_decay; // per-z1 log2(gamma) for decayed scores, or null
   int T;                   // rows per sequence (position = pos0 + row % T)
   int pos0;

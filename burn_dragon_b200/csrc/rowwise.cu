@@ -19,81 +19,161 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Normalisation kinds of the shared norm (burn_dragon_core/src/model/norm.rs:302-327),
+// every one followed by y = n * gamma + beta:
+//   0 LayerNorm    n = (x - mean) / sqrt(var + eps)
+//   1 RMSNorm      n = x / sqrt(mean(x^2) + eps)
+//   2 DynamicTanh  n = tanh(alpha x)
+//   3 Derf         n = erf(alpha x + shift)
+// alpha / shift are learnable scalars (device pointers). The statistics saved for the
+// backward are (mean, rstd) for kinds 0 / 1 and unused (0, 1) for the elementwise kinds.
+struct NormArgs {
+  int kind;
+  const float* alpha;
+  const float* shift;
+};
+
+// Rows of the gamma / beta (/ alpha / shift) gradient partials: the elementwise kinds add
+// per-column partials of the two scalar gradients (summed over the columns on the host).
+__host__ __device__ __forceinline__ int norm_part_rows(int kind) { return kind >= 2 ? 4 : 2; }
+
 template <int VPL>
-__device__ __forceinline__ void ln_stats(const float (&x)[VPL], int D, float eps, float& mean, float& rstd) {
-  float s = 0.f;
+__device__ __forceinline__ void norm_row(const float (&x)[VPL], int D, float eps, const NormArgs& na,
+                                         float (&n)[VPL], float& mean, float& rstd) {
+  if (na.kind <= 1) {
+    float s = 0.f;
+    if (na.kind == 0) {
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) s += x[i];
-  mean = warp_sum(s) / D;
-  float q = 0.f;
+      for (int i = 0; i < VPL; ++i) s += x[i];
+      mean = warp_sum(s) / D;
+    } else {
+      mean = 0.f;
+    }
+    float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const float d = x[i] - mean;
-    q += d * d;
+    for (int i = 0; i < VPL; ++i) {
+      const float d = x[i] - mean;
+      q += d * d;
+    }
+    rstd = rsqrtf(warp_sum(q) / D + eps);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) n[i] = (x[i] - mean) * rstd;
+  } else {
+    mean = 0.f;
+    rstd = 1.f;
+    const float a = *na.alpha;
+    const float sh = na.kind == 3 ? *na.shift : 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) n[i] = na.kind == 2 ? tanhf(a * x[i]) : erff(fmaf(a, x[i], sh));
   }
-  rstd = rsqrtf(warp_sum(q) / D + eps);
 }
 
-// dx of y = xhat*gamma + beta given dy; accumulates dgamma/dbeta lane partials.
+// The normalised row again from the raw input and the saved statistics.
 template <int VPL>
-__device__ __forceinline__ void ln_backward_row(const float (&g)[VPL], const float (&xhat)[VPL],
-                                                const float (&gam)[VPL], float rstd, int D, float (&dx)[VPL],
-                                                float (&dg)[VPL], float (&db)[VPL]) {
-  float s1 = 0.f, s2 = 0.f;
+__device__ __forceinline__ void norm_row_saved(const float (&x)[VPL], float mean, float rstd, const NormArgs& na,
+                                               float (&n)[VPL]) {
+  if (na.kind <= 1) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) n[i] = (x[i] - mean) * rstd;
+  } else {
+    const float a = *na.alpha;
+    const float sh = na.kind == 3 ? *na.shift : 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) n[i] = na.kind == 2 ? tanhf(a * x[i]) : erff(fmaf(a, x[i], sh));
+  }
+}
+
+// dx of y = n(x) * gamma + beta given dy = g (x raw, n its normalised row); accumulates the
+// lane partials of dgamma / dbeta and, for the elementwise kinds, of dalpha / dshift.
+template <int VPL>
+__device__ __forceinline__ void norm_backward_row(const float (&g)[VPL], const float (&x)[VPL], const float (&n)[VPL],
+                                                  const float (&gam)[VPL], float rstd, int D, const NormArgs& na,
+                                                  float (&dx)[VPL], float (&dg)[VPL], float (&db)[VPL],
+                                                  float (&da)[VPL], float (&ds)[VPL]) {
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    const float gy = g[i] * gam[i];
-    s1 += gy;
-    s2 += gy * xhat[i];
-    dg[i] += g[i] * xhat[i];
+    dg[i] += g[i] * n[i];
     db[i] += g[i];
   }
-  s1 = warp_sum(s1) / D;
-  s2 = warp_sum(s2) / D;
+  if (na.kind <= 1) {
+    float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) dx[i] = rstd * (g[i] * gam[i] - s1 - xhat[i] * s2);
+    for (int i = 0; i < VPL; ++i) {
+      const float gy = g[i] * gam[i];
+      s1 += gy;
+      s2 += gy * n[i];
+    }
+    s1 = na.kind == 0 ? warp_sum(s1) / D : 0.f;
+    s2 = warp_sum(s2) / D;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) dx[i] = rstd * (g[i] * gam[i] - s1 - n[i] * s2);
+  } else {
+    const float a = *na.alpha;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const float gy = g[i] * gam[i];
+      // d n / d(alpha x + shift): 1 - tanh^2, or (2 / sqrt(pi)) exp(-z^2)
+      float dn;
+      if (na.kind == 2) {
+        dn = 1.f - n[i] * n[i];
+      } else {
+        const float z = fmaf(a, x[i], *na.shift);
+        dn = 1.1283791670955126f * __expf(-z * z);
+      }
+      dx[i] = gy * dn * a;
+      da[i] += gy * dn * x[i];
+      ds[i] += na.kind == 3 ? gy * dn : 0.f;
+    }
+  }
 }
 
-// Reduce per-lane dgamma/dbeta partials over the block's warps and write one partial
-// row per block: part[block, 0, :] = dgamma, part[block, 1, :] = dbeta.
+// Reduce per-lane partials over the block's warps and write one partial block per CTA:
+// part[block, 0, :] = dgamma, part[block, 1, :] = dbeta (and rows 2, 3 = per-column
+// dalpha / dshift partials for the elementwise kinds).
 template <int VPL>
-__device__ void block_write_partials(const float (&dg)[VPL], const float (&db)[VPL], int D, float* part) {
-  extern __shared__ float sh[];  // [kWarps][2][D]
+__device__ void block_write_partials(const float (&dg)[VPL], const float (&db)[VPL], const float (&da)[VPL],
+                                     const float (&ds)[VPL], int D, int kind, float* part) {
+  extern __shared__ float sh[];  // [kWarps][rows][D]
+  const int R = norm_part_rows(kind);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
-    sh[(warp * 2 + 0) * D + lane + 32 * i] = dg[i];
-    sh[(warp * 2 + 1) * D + lane + 32 * i] = db[i];
+    sh[(warp * R + 0) * D + lane + 32 * i] = dg[i];
+    sh[(warp * R + 1) * D + lane + 32 * i] = db[i];
+    if (R == 4) {
+      sh[(warp * R + 2) * D + lane + 32 * i] = da[i];
+      sh[(warp * R + 3) * D + lane + 32 * i] = ds[i];
+    }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < 2 * D; c += blockDim.x) {
+  for (int c = threadIdx.x; c < R * D; c += blockDim.x) {
     const int which = c / D, col = c % D;
     float s = 0.f;
-    for (int w = 0; w < kWarps; ++w) s += sh[(w * 2 + which) * D + col];
-    part[(size_t)blockIdx.x * 2 * D + c] = s;
+    for (int w = 0; w < kWarps; ++w) s += sh[(w * R + which) * D + col];
+    part[(size_t)blockIdx.x * R * D + c] = s;
   }
 }
 
-// y = LN(x) for rows of x (fp32); optional fp32 / bf16 outputs and saved stats.
+// y = norm(x) for rows of x (fp32); optional fp32 / bf16 outputs and saved stats.
 // When `tokens` is given the row is gathered from an embedding table first.
 template <int VPL>
 __global__ void ln_fwd_kernel(const float* __restrict__ x, const int64_t* __restrict__ tokens, long long rows, int D,
                               const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
                               float* __restrict__ y32, __nv_bfloat16* __restrict__ y16, float* __restrict__ mean_out,
-                              float* __restrict__ rstd_out) {
+                              float* __restrict__ rstd_out, NormArgs na) {
   const int lane = threadIdx.x % 32;
   const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
   if (row >= rows) return;
   const float* src = tokens ? x + (size_t)tokens[row] * D : x + (size_t)row * D;
-  float v[VPL];
+  float v[VPL], n[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) v[i] = src[lane + 32 * i];
   float mean, rstd;
-  ln_stats<VPL>(v, D, eps, mean, rstd);
+  norm_row<VPL>(v, D, eps, na, n, mean, rstd);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int c = lane + 32 * i;
-    const float y = (v[i] - mean) * rstd * gamma[c] + beta[c];
+    const float y = n[i] * gamma[c] + beta[c];
     if (y32) y32[(size_t)row * D + c] = y;
     if (y16) y16[(size_t)row * D + c] = __float2bfloat16_rn(y);
   }
@@ -103,32 +183,33 @@ __global__ void ln_fwd_kernel(const float* __restrict__ x, const int64_t* __rest
   }
 }
 
-// dx = LN^T(dy), with an optional output row remap: input row r = m*H + h with
+// dx = norm^T(dy), with an optional output row remap: input row r = m*H + h with
 // m = b*T + t is written to row (b*H + h)*T + t (the [B,H,T,D] layout the attention
 // backward GEMMs read). Output bf16 and/or fp32.
 template <int VPL>
 __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                               const float* __restrict__ mean_in, const float* __restrict__ rstd_in, long long rows,
                               int D, const float* __restrict__ gamma, int remap_T, int remap_H,
-                              __nv_bfloat16* __restrict__ dx16, float* __restrict__ dx32, float* __restrict__ part) {
+                              __nv_bfloat16* __restrict__ dx16, float* __restrict__ dx32, float* __restrict__ part,
+                              NormArgs na) {
   const int lane = threadIdx.x % 32;
-  float gam[VPL], dg[VPL], db[VPL];
+  float gam[VPL], dg[VPL], db[VPL], da[VPL], ds[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     gam[i] = gamma[lane + 32 * i];
-    dg[i] = 0.f;
-    db[i] = 0.f;
+    dg[i] = db[i] = da[i] = ds[i] = 0.f;
   }
   for (long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32; row < rows;
        row += (long long)gridDim.x * kWarps) {
-    float g[VPL], xh[VPL], dx[VPL];
+    float g[VPL], xr[VPL], n[VPL], dx[VPL];
     const float mean = mean_in[row], rstd = rstd_in[row];
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       g[i] = dy[(size_t)row * D + lane + 32 * i];
-      xh[i] = (x[(size_t)row * D + lane + 32 * i] - mean) * rstd;
+      xr[i] = x[(size_t)row * D + lane + 32 * i];
     }
-    ln_backward_row<VPL>(g, xh, gam, rstd, D, dx, dg, db);
+    norm_row_saved<VPL>(xr, mean, rstd, na, n);
+    norm_backward_row<VPL>(g, xr, n, gam, rstd, D, na, dx, dg, db, da, ds);
     long long orow = row;
     if (remap_T > 0) {
       const long long m = row / remap_H, h = row % remap_H;
@@ -141,23 +222,23 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
       if (dx32) dx32[(size_t)orow * D + lane + 32 * i] = dx[i];
     }
   }
-  block_write_partials<VPL>(dg, db, D, part);
+  block_write_partials<VPL>(dg, db, da, ds, D, na.kind, part);
 }
 
 // Forward of the residual merge (burn_dragon_core/src/model/residual_stream.rs:511-535):
 //   m = sum_s partial[s]  (split-K / per-head partial products of yn @ E)
-//   u = LN(m);  v' = LN(v + u)
-// Saves m (fp32) and both LN statistics for the backward.
+//   u = norm(m);  v' = norm(v + u)
+// Saves m (fp32) and both norms' statistics for the backward.
 template <int VPL>
 __global__ void tail_fwd_kernel(const float* __restrict__ partial, int nsplit, long long split_stride,
                                 const float* __restrict__ v, long long rows, int D, const float* __restrict__ gamma,
                                 const float* __restrict__ beta, float eps, float* __restrict__ m_out,
                                 float* __restrict__ vout32, __nv_bfloat16* __restrict__ vout16,
-                                float* __restrict__ st) {
+                                float* __restrict__ st, NormArgs na) {
   const int lane = threadIdx.x % 32;
   const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
   if (row >= rows) return;
-  float m[VPL], z[VPL];
+  float m[VPL], z[VPL], n[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     float s = 0.f;
@@ -166,17 +247,17 @@ __global__ void tail_fwd_kernel(const float* __restrict__ partial, int nsplit, l
     if (m_out) m_out[(size_t)row * D + lane + 32 * i] = s;
   }
   float mean1, rstd1, mean2, rstd2;
-  ln_stats<VPL>(m, D, eps, mean1, rstd1);
+  norm_row<VPL>(m, D, eps, na, n, mean1, rstd1);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int c = lane + 32 * i;
-    z[i] = v[(size_t)row * D + c] + (m[i] - mean1) * rstd1 * gamma[c] + beta[c];
+    z[i] = v[(size_t)row * D + c] + n[i] * gamma[c] + beta[c];
   }
-  ln_stats<VPL>(z, D, eps, mean2, rstd2);
+  norm_row<VPL>(z, D, eps, na, n, mean2, rstd2);
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int c = lane + 32 * i;
-    const float y = (z[i] - mean2) * rstd2 * gamma[c] + beta[c];
+    const float y = n[i] * gamma[c] + beta[c];
     vout32[(size_t)row * D + c] = y;
     if (vout16) vout16[(size_t)row * D + c] = __float2bfloat16_rn(y);
   }
@@ -195,31 +276,32 @@ __global__ void tail_bwd_kernel(const float* __restrict__ g_in, const float* __r
                                 const float* __restrict__ m_in, const float* __restrict__ st, long long rows, int D,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 __nv_bfloat16* __restrict__ dm16, float* __restrict__ dv_res,
-                                float* __restrict__ part) {
+                                float* __restrict__ part, NormArgs na) {
   const int lane = threadIdx.x % 32;
-  float gam[VPL], bet[VPL], dg[VPL], db[VPL];
+  float gam[VPL], bet[VPL], dg[VPL], db[VPL], da[VPL], ds[VPL];
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     gam[i] = gamma[lane + 32 * i];
     bet[i] = beta[lane + 32 * i];
-    dg[i] = 0.f;
-    db[i] = 0.f;
+    dg[i] = db[i] = da[i] = ds[i] = 0.f;
   }
   for (long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32; row < rows;
        row += (long long)gridDim.x * kWarps) {
     const float mean1 = st[row * 4 + 0], rstd1 = st[row * 4 + 1];
     const float mean2 = st[row * 4 + 2], rstd2 = st[row * 4 + 3];
-    float g[VPL], mh[VPL], zh[VPL], dz[VPL], dm[VPL];
+    float g[VPL], mr[VPL], mh[VPL], z[VPL], zh[VPL], dz[VPL], dm[VPL];
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const size_t o = (size_t)row * D + lane + 32 * i;
       g[i] = g_in[o];
-      mh[i] = (m_in[o] - mean1) * rstd1;
-      const float z = v[o] + mh[i] * gam[i] + bet[i];
-      zh[i] = (z - mean2) * rstd2;
+      mr[i] = m_in[o];
     }
-    ln_backward_row<VPL>(g, zh, gam, rstd2, D, dz, dg, db);
-    ln_backward_row<VPL>(dz, mh, gam, rstd1, D, dm, dg, db);
+    norm_row_saved<VPL>(mr, mean1, rstd1, na, mh);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) z[i] = v[(size_t)row * D + lane + 32 * i] + mh[i] * gam[i] + bet[i];
+    norm_row_saved<VPL>(z, mean2, rstd2, na, zh);
+    norm_backward_row<VPL>(g, z, zh, gam, rstd2, D, na, dz, dg, db, da, ds);
+    norm_backward_row<VPL>(dz, mr, mh, gam, rstd1, D, na, dm, dg, db, da, ds);
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const size_t o = (size_t)row * D + lane + 32 * i;
@@ -227,7 +309,7 @@ __global__ void tail_bwd_kernel(const float* __restrict__ g_in, const float* __r
       dv_res[o] = dz[i];
     }
   }
-  block_write_partials<VPL>(dg, db, D, part);
+  block_write_partials<VPL>(dg, db, da, ds, D, na.kind, part);
 }
 
 // out[i] = base[i] (optional) + sum_k p0[k*s0 + i] + sum_k p1[k*s1 + i].
@@ -455,6 +537,14 @@ void allow_smem(K kern, size_t bytes) {
   if (bytes > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
 }
 
+NormArgs norm_args(int64_t kind, const c10::optional<at::Tensor>& alpha, const c10::optional<at::Tensor>& shift) {
+  TORCH_CHECK(kind >= 0 && kind <= 3, "norm kind must be 0 (layer), 1 (rms), 2 (dynamic tanh) or 3 (derf)");
+  if (kind >= 2) TORCH_CHECK(alpha && alpha->scalar_type() == at::kFloat && alpha->is_cuda(), "this norm kind needs alpha");
+  if (kind == 3) TORCH_CHECK(shift && shift->scalar_type() == at::kFloat && shift->is_cuda(), "derf needs shift");
+  return NormArgs{(int)kind, kind >= 2 ? alpha->data_ptr<float>() : nullptr,
+                  kind == 3 ? shift->data_ptr<float>() : nullptr};
+}
+
 int part_blocks(long long rows) {
   const long long need = (rows + kWarps - 1) / kWarps;
   return (int)std::min<long long>(need, 148 * 8);
@@ -464,15 +554,17 @@ int part_blocks(long long rows) {
 
 void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_t rows, int64_t D,
             const at::Tensor& gamma, const at::Tensor& beta, double eps, const c10::optional<at::Tensor>& y32,
-            const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd) {
+            const c10::optional<at::Tensor>& y16, const at::Tensor& mean, const at::Tensor& rstd, int64_t norm_kind, const c10::optional<at::Tensor>& norm_alpha,
+            const c10::optional<at::Tensor>& norm_shift) {
   c10::cuda::CUDAGuard g(x.get_device());
+  const NormArgs na = norm_args(norm_kind, norm_alpha, norm_shift);
   TORCH_CHECK(x.is_contiguous() && (!tokens || tokens->is_contiguous()), "ln_fwd: inputs must be contiguous");
   const int blocks = (int)((rows + kWarps - 1) / kWarps);
   dispatch_vpl((int)D, [&](auto vpl) {
     ln_fwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(x)>>>(
         x.data_ptr<float>(), tokens ? tokens->data_ptr<int64_t>() : nullptr, rows, (int)D, gamma.data_ptr<float>(),
         beta.data_ptr<float>(), (float)eps, opt_ptr<float>(y32), opt_ptr<__nv_bfloat16>(y16), mean.data_ptr<float>(),
-        rstd.data_ptr<float>());
+        rstd.data_ptr<float>(), na);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -480,16 +572,19 @@ void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_
 // Returns the [blocks, 2, D] dgamma/dbeta partials.
 at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
                   int64_t rows, int64_t D, const at::Tensor& gamma, int64_t remap_T, int64_t remap_H,
-                  const c10::optional<at::Tensor>& dx16, const c10::optional<at::Tensor>& dx32) {
+                  const c10::optional<at::Tensor>& dx16, const c10::optional<at::Tensor>& dx32, int64_t norm_kind, const c10::optional<at::Tensor>& norm_alpha,
+            const c10::optional<at::Tensor>& norm_shift) {
   c10::cuda::CUDAGuard g(x.get_device());
+  const NormArgs na = norm_args(norm_kind, norm_alpha, norm_shift);
   const int blocks = part_blocks(rows);
-  auto part = at::empty({blocks, 2, D}, x.options().dtype(at::kFloat));
+  const int R = norm_part_rows(na.kind);
+  auto part = at::empty({blocks, R, D}, x.options().dtype(at::kFloat));
   dispatch_vpl((int)D, [&](auto vpl) {
-    allow_smem(ln_bwd_kernel<decltype(vpl)::value>, kWarps * 2 * D * sizeof(float));
-    ln_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * 2 * D * sizeof(float), cur_stream(x)>>>(
+    allow_smem(ln_bwd_kernel<decltype(vpl)::value>, kWarps * R * D * sizeof(float));
+    ln_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * R * D * sizeof(float), cur_stream(x)>>>(
         dy.data_ptr<float>(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, (int)D,
         gamma.data_ptr<float>(), (int)remap_T, (int)remap_H, opt_ptr<__nv_bfloat16>(dx16), opt_ptr<float>(dx32),
-        part.data_ptr<float>());
+        part.data_ptr<float>(), na);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return part;
@@ -498,30 +593,35 @@ at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& m
 void tail_fwd(const at::Tensor& partial, int64_t nsplit, int64_t split_stride, const at::Tensor& v, int64_t rows,
               int64_t D, const at::Tensor& gamma, const at::Tensor& beta, double eps,
               const c10::optional<at::Tensor>& m_out, const at::Tensor& vout32,
-              const c10::optional<at::Tensor>& vout16, const c10::optional<at::Tensor>& st) {
+              const c10::optional<at::Tensor>& vout16, const c10::optional<at::Tensor>& st, int64_t norm_kind, const c10::optional<at::Tensor>& norm_alpha,
+            const c10::optional<at::Tensor>& norm_shift) {
   c10::cuda::CUDAGuard g(v.get_device());
+  const NormArgs na = norm_args(norm_kind, norm_alpha, norm_shift);
   const int blocks = (int)((rows + kWarps - 1) / kWarps);
   dispatch_vpl((int)D, [&](auto vpl) {
     tail_fwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(v)>>>(
         partial.data_ptr<float>(), (int)nsplit, split_stride, v.data_ptr<float>(), rows, (int)D,
         gamma.data_ptr<float>(), beta.data_ptr<float>(), (float)eps, opt_ptr<float>(m_out), vout32.data_ptr<float>(),
-        opt_ptr<__nv_bfloat16>(vout16), opt_ptr<float>(st));
+        opt_ptr<__nv_bfloat16>(vout16), opt_ptr<float>(st), na);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 at::Tensor tail_bwd(const at::Tensor& gin, const at::Tensor& v, const at::Tensor& m, const at::Tensor& st,
                     int64_t rows, int64_t D, const at::Tensor& gamma, const at::Tensor& beta, const at::Tensor& dm16,
-                    const at::Tensor& dv_res) {
+                    const at::Tensor& dv_res, int64_t norm_kind, const c10::optional<at::Tensor>& norm_alpha,
+            const c10::optional<at::Tensor>& norm_shift) {
   c10::cuda::CUDAGuard g(v.get_device());
+  const NormArgs na = norm_args(norm_kind, norm_alpha, norm_shift);
   const int blocks = part_blocks(rows);
-  auto part = at::empty({blocks, 2, D}, v.options().dtype(at::kFloat));
+  const int R = norm_part_rows(na.kind);
+  auto part = at::empty({blocks, R, D}, v.options().dtype(at::kFloat));
   dispatch_vpl((int)D, [&](auto vpl) {
-    allow_smem(tail_bwd_kernel<decltype(vpl)::value>, kWarps * 2 * D * sizeof(float));
-    tail_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * 2 * D * sizeof(float), cur_stream(v)>>>(
+    allow_smem(tail_bwd_kernel<decltype(vpl)::value>, kWarps * R * D * sizeof(float));
+    tail_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * R * D * sizeof(float), cur_stream(v)>>>(
         gin.data_ptr<float>(), v.data_ptr<float>(), m.data_ptr<float>(), st.data_ptr<float>(), rows, (int)D,
         gamma.data_ptr<float>(), beta.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dm16.data_ptr()),
-        dv_res.data_ptr<float>(), part.data_ptr<float>());
+        dv_res.data_ptr<float>(), part.data_ptr<float>(), na);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return part;

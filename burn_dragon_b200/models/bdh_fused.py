@@ -34,7 +34,14 @@ from .reference import rope_freqs
 # The forward stores x = relu(v Dx) next to q = rope(x) (the gate and the decoder
 # backward read x); the step roofline counts its bytes.
 STORES_X = True
+# RoPE phases from a half2 (cos, sin) table instead of evaluating them in the epilogue:
+# BDH_ROPE_TMA=1 stages the x-projection's table tiles through its epilogue's TMA ring,
+# BDH_ROPE_TABLE=1 has dQ read them with plain loads. Both off by default: at BDH-GPU batch
+# 32 the staged table took the x-projection from 597 to 765 us (the two-buffer ring must
+# drain a tile's stores before the next table tile may land) and the plain loads expose
+# their latency.
 ROPE_TABLE = os.environ.get("BDH_ROPE_TABLE", "0") == "1"
+ROPE_TMA = os.environ.get("BDH_ROPE_TMA", "0") == "1"
 
 
 # Vocabularies up to this size take the scan form of the embedding-gradient kernel
@@ -59,13 +66,26 @@ def embed_grad(mod, tokens: torch.Tensor, rows_grad: torch.Tensor, table_grad: t
     mod.embed_grad(tok, rows_grad, R, D, table_grad, accumulate, perm, seg)
 
 
+# Norm kinds of the row kernels (rowwise.cu NormArgs).
+NORM_KINDS = {"layer_norm": 0, "rms_norm": 1, "dynamic_tanh": 2, "derf": 3}
+
+
+def norm_kwargs(cfg, p32: dict) -> dict:
+    """The trailing norm arguments of the row kernels: the kind and, for the elementwise
+    kinds, the learnable alpha / shift scalars (1-element fp32 device tensors)."""
+    k = NORM_KINDS[getattr(cfg, "norm_kind", "layer_norm")]
+    return {"norm_kind": k, "norm_alpha": p32.get("norm_alpha") if k >= 2 else None,
+            "norm_shift": p32.get("norm_shift") if k == 3 else None}
+
+
 def fused_unsupported(cfg) -> str | None:
     """The first model option the fused kernels do not implement, or None: they
-    implement dropout 0 (as the BDH-GPU profiles use), LayerNorm, RoPE / ALiBi / no
-    rotation, one residual stream and an untied output head."""
+    implement dropout 0 (as the BDH-GPU profiles use), every norm kind (LayerNorm, RMSNorm,
+    DynamicTanh, Derf), RoPE / ALiBi / no rotation, one residual stream and an untied
+    output head."""
     if cfg.dropout != 0.0:
         return "dropout > 0"
-    if getattr(cfg, "norm_kind", "layer_norm") != "layer_norm":
+    if getattr(cfg, "norm_kind", "layer_norm") not in NORM_KINDS:
         return f"norm_kind {cfg.norm_kind!r}"
     if cfg.rotary_embedding == "pope":
         return "PoPE"
@@ -170,12 +190,12 @@ class FusedWorkspace:
         self.has_rho0 = False
         self.qscaled: torch.Tensor | None = None
 
-    def rope_tab(self, pos0: int):
+    def rope_tab(self, pos0: int, staged: bool = False):
         """The half2 (cos, sin) table of this workspace's positions pos0 .. pos0 + T - 1
-        (rebuilt only when pos0 changes), or None without RoPE or unless BDH_ROPE_TABLE=1
-        (the epilogues evaluate the phases themselves by default: the table's loads
-        measured slower at BDH-GPU batch 32)."""
-        if self.freq is None or not ROPE_TABLE:
+        (rebuilt only when pos0 changes), or None without RoPE. ``staged``: for the
+        x-projection, which fetches table tiles by TMA (only with BDH_ROPE_TMA=1); else for
+        dQ's plain loads (only with BDH_ROPE_TABLE=1)."""
+        if self.freq is None or not (ROPE_TMA if staged else ROPE_TABLE):
             return None
         if getattr(self, "_rope_tab", None) is None:
             self._rope_tab = torch.empty(self.T, self.Nh // 2, dtype=torch.int32, device=self.freq.device)
@@ -285,12 +305,13 @@ class FusedBDH:
             elif peer is not None:
                 ws.m32 = peer.sum_views  # the all-gathered decoder sums land here
         eps = cfg.norm_eps
+        nk = norm_kwargs(cfg, p32)
         thr, thr_y = cfg.thresholds()
         if v_in is None:
             tok = tokens.reshape(-1)
             torch.index_select(p32["embed"], 0, tok, out=ws.emb_rows)
             mod.ln_fwd(ws.emb_rows, None, M, D, p32["norm_gamma"], p32["norm_beta"], eps, ws.v32[0], ws.v16[0],
-                       ws.emean, ws.erstd)
+                       ws.emean, ws.erstd, **nk)
         else:
             ws.v32[0].copy_(v_in.reshape(M, D))
             ws.v16[0].copy_(ws.v32[0])
@@ -303,7 +324,7 @@ class FusedBDH:
             # x = relu(v Dx - thr), q = rope(x)       (K = D)
             G.gemm(G.EPI_RELU_ROPE, Operand(v16, False, D, M, D), B_enc, M, Nh, D, ws.x16[l], Z1=H, bn=G.tma_bn(M, Nh),
                    out1=ws.q16[l] if ws.freq is not None else None, ld=N, sz1=Nh, thr=thr, freq=ws.freq,
-                   T=T, pos0=pos0, Nh=Nh, rope_tab=ws.rope_tab(pos0))
+                   T=T, pos0=pos0, Nh=Nh, rope_tab=ws.rope_tab(pos0, staged=True))
             # S = tril_{-1}(q q^T) (* gamma^(i-j))      (K = Nh), upper tiles skipped
             qop = Operand(ws.q16[l], False, Nh, T, N, z1=(H, Nh), z2=(B, T * N))
             # 256-row CTA-pair tiles x 128 columns: finer causal skipping than 256 x 256
@@ -343,7 +364,7 @@ class FusedBDH:
                        src_decay_T=T if (decay and src is not None) else 0, log2_decay=ws.log2_decay,
                        out1=out16[l] if out16 is not None else None)
             mod.ln_fwd(ws.a32[l], None, M * H, D, p32["norm_gamma"], p32["norm_beta"], eps, None, ws.an16[l],
-                       ws.amean[l], ws.arstd[l])
+                       ws.amean[l], ws.arstd[l], **nk)
             # yn = relu(an Dy - thr) * x                (K = D)
             G.gemm(G.EPI_GATE, Operand(ws.an16[l], False, D, M, H * D, z1=(H, D)), B_encv, M, Nh, D, ws.yn16[l],
                    Z1=H, bn=G.tma_bn(M, Nh), aux0=ws.x16[l], ld=N, sz1=Nh, thr=thr_y)
@@ -356,11 +377,11 @@ class FusedBDH:
                 if self.tp.sequence_parallel:
                     # the owner merges its own rows and gathers their bf16 copies
                     peer.sp_tail_forward(l, ws.v32[l], ws.v32[l + 1], ws.tst[l], p32["norm_gamma"],
-                                         p32["norm_beta"], eps)
+                                         p32["norm_beta"], eps, nk)
                     continue
                 peer.finish(l)
                 mod.tail_fwd(ws.m32[l], 1, M * D, ws.v32[l], M, D, p32["norm_gamma"], p32["norm_beta"], eps, None,
-                             ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
+                             ws.v32[l + 1], ws.v16[l + 1], ws.tst[l], **nk)
                 continue
             G.gemm(G.EPI_F32, Operand(ws.yn16[l], False, N, M, N), B_dec, M, D, N, ws.partial,
                    splits=ws.dec_splits, ld=D, split_stride=M * D)
@@ -373,10 +394,10 @@ class FusedBDH:
                     ws.m32[l].copy_(msum)
                 self.tp.all_reduce(ws.m32[l])
                 mod.tail_fwd(ws.m32[l], 1, M * D, ws.v32[l], M, D, p32["norm_gamma"], p32["norm_beta"], eps, None,
-                             ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
+                             ws.v32[l + 1], ws.v16[l + 1], ws.tst[l], **nk)
             else:
                 mod.tail_fwd(ws.partial, ws.dec_splits, M * D, ws.v32[l], M, D, p32["norm_gamma"],
-                             p32["norm_beta"], eps, ws.m32[l], ws.v32[l + 1], ws.v16[l + 1], ws.tst[l])
+                             p32["norm_beta"], eps, ws.m32[l], ws.v32[l + 1], ws.v16[l + 1], ws.tst[l], **nk)
         if with_head:
             G.gemm(G.EPI_F32, Operand(ws.v16[L], False, D, M, D), Operand(p16["lm_head"], True, ws.V, D, ws.V),
                    M, ws.V, D, ws.logits, ld=ws.V)
@@ -418,6 +439,7 @@ class FusedBDH:
         ws, cfg, mod = self.ws, self.cfg, self.mod
         B, T, D, H, Nh, N, M, L, V = ws.B, ws.T, ws.D, ws.H, ws.Nh, ws.N, ws.M, ws.L, ws.V
         gam, bet = p32["norm_gamma"], p32["norm_beta"]
+        nk = norm_kwargs(cfg, p32)
         tp = self.tp if self.tp is not None and self.tp.world > 1 else None
         if not accumulate:
             for k in ("encoder", "encoder_v", "decoder"):
@@ -445,10 +467,10 @@ class FusedBDH:
                 # are gathered, the LayerNorm partials summed over the group below
                 rows = own.stop - own.start
                 head_parts.append(mod.tail_bwd(dv[own], ws.v32[l][own], tp.peer.m_own[l], ws.tst[l][own], rows, D,
-                                               gam, bet, ws.dm16[own], ws.dv_res[own]))
+                                               gam, bet, ws.dm16[own], ws.dv_res[own], **nk))
                 tp.peer.sp_gather_dm()
             else:
-                parts.append(mod.tail_bwd(dv, ws.v32[l], ws.m32[l], ws.tst[l], M, D, gam, bet, ws.dm16, ws.dv_res))
+                parts.append(mod.tail_bwd(dv, ws.v32[l], ws.m32[l], ws.tst[l], M, D, gam, bet, ws.dm16, ws.dv_res, **nk))
             # d(yn) = dm E^T -> dx_part = d(yn)*y, dy_pre = d(yn)*x*[y>0]
             G.gemm(G.EPI_DEC_BWD, Operand(ws.dm16, False, D, M, D), Operand(dec, False, D, N, D), M, N, D, ws.dx16, bn=G.tma_bn(M, N),
                    out1=ws.dy16, aux0=ws.x16[l], aux1=ws.yn16[l], ld=N)
@@ -469,7 +491,7 @@ class FusedBDH:
                 ready("encoder_v")
             # dC = LN^T(d an), written as [B,H,T,D]
             head_parts.append(mod.ln_bwd(ws.dan32, ws.a32[l], ws.amean[l], ws.arstd[l], M * H, D, gam, T, H, ws.dC16,
-                                    None))
+                                    None, **nk))
             # P = dC V^T ; G = mask(P) + mask(P)^T
             dcop = Operand(ws.dC16, False, D, T, D, z1=(H, T * D), z2=(B, H * T * D))
             G.gemm(G.EPI_F32, dcop, Operand(v16, False, D, T, D, z2=(B, T * D)), T, T, D, ws.P32, Z1=H, Z2=B,
@@ -524,7 +546,7 @@ class FusedBDH:
             if sp:
                 rows = own.stop - own.start
                 head_parts.append(mod.ln_bwd(dv[own], ws.emb_rows[own], ws.emean[own], ws.erstd[own], rows, D, gam,
-                                             0, 0, None, demb[own]))
+                                             0, 0, None, demb[own], **nk))
                 ge = torch.empty_like(g32["embed"])
                 embed_grad(mod, tokens.reshape(-1)[own].contiguous(), demb[own], ge, accumulate=False)
                 tp.all_reduce(ge)  # every rank's own-row contributions
@@ -533,7 +555,7 @@ class FusedBDH:
                 else:
                     g32["embed"].copy_(ge)
             else:
-                parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb))
+                parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb, **nk))
                 embed_grad(mod, tokens.reshape(-1), demb, g32["embed"], accumulate=accumulate)
         elif not accumulate:
             g32["embed"].zero_()
@@ -542,10 +564,16 @@ class FusedBDH:
         if tp is not None:
             tp.all_reduce(hp)
         allp = allp + hp
-        if accumulate:
-            g32["norm_gamma"].add_(allp[0])
-            g32["norm_beta"].add_(allp[1])
-        else:
-            g32["norm_gamma"].copy_(allp[0])
-            g32["norm_beta"].copy_(allp[1])
+        # rows: dgamma, dbeta (and per-column dalpha / dshift partials for the elementwise kinds)
+        grads = [("norm_gamma", allp[0]), ("norm_beta", allp[1])]
+        if nk["norm_kind"] >= 2:
+            grads += [("norm_alpha", allp[2].sum().reshape(1)), ("norm_shift", allp[3].sum().reshape(1))]
+        elif "norm_alpha" in g32 and not accumulate:
+            g32["norm_alpha"].zero_()
+            g32["norm_shift"].zero_()
+        for name, gv in grads:
+            if accumulate:
+                g32[name].add_(gv)
+            else:
+                g32[name].copy_(gv)
         return None if with_embed else dv

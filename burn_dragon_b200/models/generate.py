@@ -151,13 +151,16 @@ class Generator:
         p32 = self.model.store.views(self.model.store.data)
         p16 = self.model.shadow_dict()
         gam, bet, eps = p32["norm_gamma"], p32["norm_beta"], cfg.norm_eps
+        from .bdh_fused import norm_kwargs
+
+        nk = norm_kwargs(cfg, p32)
         thr, thr_y = cfg.thresholds()
         sdt = torch.bfloat16 if self.state_dtype == "bf16" else torch.float32
         if state.rhos is None:
             state.rhos = [torch.zeros(B, H, Nh, D, device=tokens.device, dtype=sdt) for _ in range(cfg.n_layer)]
         elif state.rhos[0].dtype != sdt:
             state.rhos = [r.to(sdt) for r in state.rhos]
-        mod.ln_fwd(p32["embed"], tokens, B, D, gam, bet, eps, w.v32[0], w.v16[0], w.amean, w.arstd)
+        mod.ln_fwd(p32["embed"], tokens, B, D, gam, bet, eps, w.v32[0], w.v16[0], w.amean, w.arstd, **nk)
         B_enc = Operand(p16["encoder"], True, Nh, D, Nh, z1=(H, D * Nh))
         B_encv = Operand(p16["encoder_v"], True, Nh, D, Nh, z1=(H, D * Nh))
         cur = 0
@@ -169,13 +172,13 @@ class Generator:
             q = w.q16 if w.freq is not None else w.x16
             w.a32.zero_()
             mod.rho_step(state.rhos[l], q, N, v32, w.gamma, w.a32, B, H, Nh, D)
-            mod.ln_fwd(w.a32, None, B * H, D, gam, bet, eps, None, w.an16, w.amean, w.arstd)
+            mod.ln_fwd(w.a32, None, B * H, D, gam, bet, eps, None, w.an16, w.amean, w.arstd, **nk)
             G.gemm(G.EPI_GATE, Operand(w.an16, False, D, B, H * D, z1=(H, D)), B_encv, B, Nh, D, w.yn16, Z1=H,
                    bn=128, aux0=w.x16, ld=N, sz1=Nh, thr=thr_y)
             G.gemm(G.EPI_F32, Operand(w.yn16, False, N, B, N), Operand(p16["decoder"], True, D, N, D), B, D, N,
                    w.partial, splits=w.splits, ld=D, split_stride=B * D)
             nxt = 1 - cur
-            mod.tail_fwd(w.partial, w.splits, B * D, v32, B, D, gam, bet, eps, None, w.v32[nxt], w.v16[nxt], None)
+            mod.tail_fwd(w.partial, w.splits, B * D, v32, B, D, gam, bet, eps, None, w.v32[nxt], w.v16[nxt], None, **nk)
             cur = nxt
         G.gemm(G.EPI_F32, Operand(w.v16[cur], False, D, B, D), Operand(p16["lm_head"], True, V, D, V), B, V, D,
                w.logits, ld=V)

@@ -105,7 +105,8 @@ def gemm(epi: int, a: Operand, b: Operand, M: int, N: int, K: int, out0: torch.T
     ``src_decay_T`` > 0) instead of adding out0's old contents.
 
     ``rope_tab`` (x-projection / dQ with ``freq``): the half2 (cos, sin) table of
-    ``rope_table`` for this call's positions pos0 .. pos0 + T - 1."""
+    ``rope_table`` for this call's positions pos0 .. pos0 + T - 1. The x-projection
+    stages its tiles through the epilogue's TMA ring; dQ reads it with plain loads."""
     mod = _ext.load()
     bn = bn or pick_bn(N)
     mod.gemm(epi, bn, a.t, a.mn, a.geom(), b.t, b.mn, b.geom(), M, N, K, Z1, Z2, splits, causal_skip,

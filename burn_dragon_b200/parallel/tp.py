@@ -133,7 +133,7 @@ class PeerSum:
         r0 = self.tp.rank * self.rows
         return slice(r0, r0 + self.rows)
 
-    def sp_tail_forward(self, layer: int, v32_in, v32_out, tst, gamma, beta, eps: float) -> None:
+    def sp_tail_forward(self, layer: int, v32_in, v32_out, tst, gamma, beta, eps: float, nk: dict | None = None) -> None:
         """After the scattered decoder GEMM of ``layer``: the owner sums its rows' partials,
         runs the residual merge v' = LN(v + LN(m)) on its rows only, and all-gathers the
         bf16 rows of v' (the next GEMM operand) by P2P stores. The fp32 residual stays
@@ -147,7 +147,7 @@ class PeerSum:
         mod.tp_sum_slots(self.slots, self.m_own[layer], W, rows * D, rows * D, None)
         v16 = self.v16_views[layer + 1]
         mod.tail_fwd(self.m_own[layer], 1, rows * D, v32_in[own], rows, D, gamma, beta, eps, None, v32_out[own],
-                     v16[own], tst[own])
+                     v16[own], tst[own], **(nk or {}))
         self._gather16(self.ptrs["v16"], (layer + 1) * self.M * D * 2 + own.start * D * 2, rows * D * 2)
         self._barrier(1)
 

@@ -47,11 +47,13 @@ def measured_peaks(path: str | None = None) -> dict:
         return out
 
 
-def fused_step_cost(cfg, B: int, T: int, store_x: bool = False) -> list[dict]:
+def fused_step_cost(cfg, B: int, T: int, store_x: bool = False, stateful: bool = False) -> list[dict]:
     """Per-kernel FLOPs / bytes of one fused step at batch ``B`` x ``T`` tokens.
 
     ``store_x``: the forward also stores x next to q (an older layout); by default x is
-    recovered from q = rope(x) and a one-bit positivity mask where it is read."""
+    recovered from q = rope(x) and a one-bit positivity mask where it is read.
+    ``stateful``: a TBPTT chunk step, which also reads the carried state rho0 [B,H,Nh,D]
+    (a += q rho0, dq += dC rho0^T) and writes the outgoing one (rho_T = q^T v + rho0)."""
     D, H, Nh, V, L = cfg.n_embd, cfg.n_head, cfg.latent_per_head, cfg.vocab_size, cfg.n_layer
     N = H * Nh
     M = B * T
@@ -99,15 +101,21 @@ def fused_step_cost(cfg, B: int, T: int, store_x: bool = False) -> list[dict]:
     k("dDx += v^T dx", mnd, MN + MD2)
     k("dv_x = dx Dx^T (per head)", mnd, MN + H * MD4)
     k("dv sum", 0, (H + 3) * MD4)
+    if stateful:
+        R4, R2 = B * H * Nh * D * f4, B * H * Nh * D * bf
+        k("state read a += q rho0", 2 * B * H * T * Nh * D, MN + R2 + M * H * D * f4 * 2)
+        k("state update rho_T = q^T v + rho0", 2 * B * H * Nh * T * D, MN + MD2 + R4 + R4 + R2)
+        k("state backward dq += rope^T(dC rho0^T)", 2 * B * H * T * D * Nh, M * H * D * bf + R2 + MN + MN)
     k("AdamW", 0, 0, per_layer=False)
     return rows
 
 
-def step_totals(cfg, B: int, T: int, params: int = 0, store_x: bool = False, peaks: dict | None = None) -> dict:
+def step_totals(cfg, B: int, T: int, params: int = 0, store_x: bool = False, peaks: dict | None = None,
+                stateful: bool = False) -> dict:
     """Summed FLOPs / bytes of a step and the floor time at the given peaks.
 
     ``params``: parameter count (AdamW reads p, g, m, v and writes p, m, v, bf16 shadow)."""
-    rows = fused_step_cost(cfg, B, T, store_x=store_x)
+    rows = fused_step_cost(cfg, B, T, store_x=store_x, stateful=stateful)
     for r in rows:
         if r["kernel"] == "AdamW":
             r["bytes"] = params * (4 * 4 + 3 * 4 + 2)

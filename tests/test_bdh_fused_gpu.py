@@ -182,3 +182,51 @@ def test_embed_grad_kernel_matches_index_add(V, D, R):
     assert torch.allclose(out1, ref, rtol=1e-5, atol=1e-4)
     assert torch.equal(out1, out2)
     assert torch.allclose(fresh, ref - base, rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("kind", ["rms_norm", "dynamic_tanh", "derf"])
+def test_fused_step_norm_kinds_match_reference(kind):
+    """RMSNorm / DynamicTanh / Derf in the row kernels (embedding norm, attention-output
+    norm, both residual-merge norms) against the fp32 PyTorch oracle, including the
+    gradients of the learnable alpha / shift scalars."""
+    cfg = DragonConfig(n_layer=2, n_embd=64, n_head=2, mlp_internal_dim_multiplier=8, dropout=0.0,
+                       rotary_embedding="rope", initialization="near_critical", residual_scaling="family_default",
+                       neuron_gains="iid", norm_kind=kind, norm_shift_init=0.1 if kind == "derf" else 0.0)
+    model = BDH(cfg, device="cuda", seed=11)
+    assert model._fused is None
+    with torch.no_grad():
+        for n in ("encoder", "encoder_v", "decoder"):
+            getattr(model, n).mul_(5.0)
+    model.store.refresh_shadow()
+    torch.manual_seed(2)
+    B, T = 2, 256
+    tokens = torch.randint(0, 256, (B, T), device="cuda")
+    targets = torch.randint(0, 256, (B, T), device="cuda")
+    ref_params = {}
+    for n, p in model.param_dict().items():
+        if p is None:
+            ref_params[n] = None
+            continue
+        q = p.detach().clone()
+        if n in ("encoder", "encoder_v", "decoder", "lm_head"):
+            q = q.bfloat16().float()
+        ref_params[n] = q.requires_grad_(True)
+    logits, _ = R.bdh_forward(tokens, ref_params, cfg)
+    ref_loss = R.cross_entropy(logits, targets)
+    ref_loss.backward()
+
+    loss = model.fused_step(tokens, targets)
+    torch.cuda.synchronize()
+    from burn_dragon_b200.ops.gemm import check_errors
+
+    check_errors(torch.device("cuda"))
+    assert abs(loss.item() - ref_loss.item()) < 2e-2 * abs(ref_loss.item())
+    grads = model.grad_dict()
+    names = ["lm_head", "decoder", "encoder_v", "encoder", "embed", "norm_gamma", "norm_beta"]
+    if kind != "rms_norm":
+        names.append("norm_alpha")
+    if kind == "derf":
+        names.append("norm_shift")
+    for n in names:
+        r = _rel(grads[n], ref_params[n].grad)
+        assert r < 0.08, f"{kind} {n}: rel err {r:.3e}"

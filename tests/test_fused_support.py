@@ -9,6 +9,7 @@ def test_fused_support_matrix():
     base = dict(n_layer=1, n_embd=64, n_head=2, mlp_internal_dim_multiplier=4, vocab_size=64)
     assert fused_unsupported(DragonConfig(**base, dropout=0.0)) is None
     assert fused_unsupported(DragonConfig(**base, dropout=0.1)) == "dropout > 0"
-    assert "rms_norm" in fused_unsupported(DragonConfig(**base, dropout=0.0, norm_kind="rms_norm"))
+    for kind in ("rms_norm", "dynamic_tanh", "derf"):
+        assert fused_unsupported(DragonConfig(**base, dropout=0.0, norm_kind=kind)) is None
     assert fused_unsupported(DragonConfig(**base, dropout=0.0, rotary_embedding="pope")) == "PoPE"
     assert fused_unsupported(DragonConfig(**base, dropout=0.0, tie_input_output_embeddings=True)) == "a tied lm_head"

@@ -184,9 +184,63 @@ def test_rope_table_matches_evaluated_phases(case):
     G = _ops()
     c0, o0 = _tma_case(case, table=False)
     c1, o1 = _tma_case(case, table=True)
-    c0(256)
-    c1(256)
+    # the x-projection stages table tiles through its TMA ring (both tile widths); dQ
+    # reads the table with plain loads
+    for bn in (128, 256):
+        c0(bn)
+        c1(bn)
+        torch.cuda.synchronize()
+        G.check_errors(torch.device("cuda"))
+        for a, b in zip(o0, o1):
+            _close(b, a.float(), tol=1e-2)
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_decoder_backward_and_dq_epilogues_match_fp32(bn):
+    """The decoder-backward epilogue (dx_part = g yn / x on x > 0, else the -0.0 mask
+    marker; dy = g x on yn > 0) and the dQ epilogue (dx = dx_part + rope^T(G q) on live
+    entries, the marker kept) against fp32 PyTorch on the same bf16 operands."""
+    from burn_dragon_b200.models.reference import rope_freqs
+
+    G = _ops()
+    Op = G.Operand
+    B, T, D, H, Nh = 2, 256, 64, 2, 512
+    N, M = H * Nh, B * T
+    g = torch.Generator(device="cuda").manual_seed(3)
+    r = lambda *s: (torch.randn(*s, device="cuda", generator=g) * 0.5).bfloat16()  # noqa: E731
+    dm, dec = r(M, D), r(N, D)
+    x = torch.relu(r(M, N).float()).bfloat16()
+    yn = (torch.relu(r(M, N).float()) * x.float()).bfloat16()
+    dxp, dy = (torch.empty(M, N, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    G.gemm(G.EPI_DEC_BWD, Op(dm, False, D, M, D), Op(dec, False, D, N, D), M, N, D, dxp, bn=bn, out1=dy, aux0=x,
+           aux1=yn, ld=N)
+    acc = dm.float() @ dec.float().t()
+    xf, yf = x.float(), yn.float()
+    ref_dy = torch.where(yf > 0, acc * xf, torch.zeros_like(acc))
+    ref_dxp = torch.where(xf > 0, acc * yf / xf.clamp_min(1e-30), torch.zeros_like(acc))
     torch.cuda.synchronize()
     G.check_errors(torch.device("cuda"))
-    for a, b in zip(o0, o1):
-        _close(b, a.float(), tol=1e-2)
+    _close(dy, ref_dy, tol=1e-2)
+    _close(dxp, ref_dxp, tol=1e-2)
+    marker = dxp.view(torch.int16) == -32768  # bf16 -0.0
+    assert torch.equal(marker, x.float() <= 0)
+
+    # dQ over the decoder-backward output
+    g16, q = r(B, H, T, T), r(M, N)
+    freq = rope_freqs(Nh, 10000.0, device="cuda")
+    dx = dxp.clone()
+    G.gemm(G.EPI_DQ, Op(g16, False, T, T, T, z1=(H, T * T), z2=(B, H * T * T)),
+           Op(q, True, Nh, T, N, z1=(H, Nh), z2=(B, T * N)), T, Nh, T, dx, Z1=H, Z2=B, bn=bn, aux0=dx, ld=N,
+           sz1=Nh, sz2=T * N, freq=freq, T=T, Nh=Nh)
+    gq = torch.einsum("bhts,bshj->bthj", g16.float(), q.float().view(B, T, H, Nh))  # [B, T, H, Nh]
+    pos = torch.arange(T, device="cuda", dtype=torch.float32)
+    raw = pos[:, None] * freq[0::2][None, :]
+    ph = (raw - torch.round(raw)) * (2 * torch.pi)
+    c, s = torch.cos(ph)[None, :, None, :], torch.sin(ph)[None, :, None, :]
+    ge, go = gq[..., 0::2], gq[..., 1::2]
+    rot = torch.stack((ge * c + go * s, go * c - ge * s), dim=-1).reshape(B, T, H, Nh).reshape(M, N)
+    ref_dx = torch.where(marker, torch.zeros_like(rot), rot + dxp.float())
+    torch.cuda.synchronize()
+    G.check_errors(torch.device("cuda"))
+    _close(dx, ref_dx, tol=1e-2)
+    assert torch.equal(dx.view(torch.int16) == -32768, marker)
