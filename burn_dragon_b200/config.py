@@ -932,8 +932,15 @@ class TrainingSection:
 @dataclass
 class DatasetConfig:
     # synthetic_bytes | file (a byte file) | jsonl | parquet | text (a corpus tokenised
-    # once into cache_dir, then read like a file)
+    # once into cache_dir, then read like a file) | nemotron_climb_mix (the reference's
+    # Hugging Face preset, schema.rs:37-52) | huggingface (a dataset repository of the local
+    # hub cache described by the ``huggingface`` table: repo_id, revision, format,
+    # train_files, auto_discover_train_files, validation_files, text_fields,
+    # sequence_field, field_separator, template, max_records; schema.rs:64-96)
     type: str = "synthetic_bytes"
+    revision: str | None = None      # nemotron_climb_mix
+    max_records: int | None = None   # nemotron_climb_mix
+    huggingface: dict[str, Any] | None = None
     cache_dir: str = "data"
     train_split_ratio: float = 0.9
     path: str | None = None

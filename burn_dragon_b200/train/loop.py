@@ -112,6 +112,25 @@ def train(cfg: TrainingConfig, run_name: str | None = None, resume: bool = True,
     if seq_par and not tp_arg:
         raise ValueError("parallel.tensor.sequence_parallel needs a tensor-parallel mode "
                          "(tensor_parallel_neuron or hybrid_2d)")
+    if cfg.dataset.type in ("huggingface", "nemotron_climb_mix"):
+        from .datasets import prepare_hf_dataset
+
+        if cfg.dataset.type == "huggingface":
+            spec = dict(cfg.dataset.huggingface or {})
+        else:
+            spec = {"type": "nemotron_climb_mix", "revision": cfg.dataset.revision,
+                    "max_records": cfg.dataset.max_records}
+        splits = ["train"] + (["validation"] if spec.get("validation_files") and not cfg.dataset.validation else [])
+        if rank == 0:
+            for sp in splits:
+                prepare_hf_dataset(spec, cfg.dataset.cache_dir, tokenizer=cfg.dataset.tokenizer, split=sp)
+        if world > 1 and dist.is_initialized():
+            dist.barrier()
+        prepared, *vp = [prepare_hf_dataset(spec, cfg.dataset.cache_dir, tokenizer=cfg.dataset.tokenizer, split=sp)
+                         for sp in splits]
+        if vp:
+            cfg.dataset.validation = {"type": "file", "path": vp[0]}
+        cfg.dataset.type, cfg.dataset.path = "file", prepared
     if cfg.dataset.type in ("jsonl", "parquet", "text"):
         from .datasets import prepare_corpus
 
