@@ -35,6 +35,11 @@ def main(argv=None) -> None:
     ap.add_argument("--output-format", choices=("auto", "decoded_text", "token_ids"), default=None)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--weights-url", default=None,
+                    help="base URL (http(s):// or file://) of burnpack weights: resolved from the local cache "
+                         "or fetched into it (parts first), then loaded in place of the run's checkpoint")
+    ap.add_argument("--weights-cache", default=None, help="cache root for --weights-url (default: "
+                    "$BURN_DRAGON_CACHE_DIR or ~/.cache/burn_dragon/models)")
     a = ap.parse_args(argv)
     run = RunDir(a.run)
     cfg = training_config_from_dict(run.read_json("training_config.json"))
@@ -48,7 +53,15 @@ def main(argv=None) -> None:
     fmt = pick(a.output_format, g.output_format)
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
     model = BDH(cfg.model, device=dev)
-    if run.latest() is not None:
+    if a.weights_url:
+        from ..train import burnpack as BP
+        from ..train.checkpoint import load_model_burnpack
+
+        name = a.weights_url.rstrip("/").rpartition("/")[2]
+        name = name[:-4] if name.endswith(".bpk") else name
+        path = BP.resolve_or_bootstrap(name, a.weights_url, cache_root=a.weights_cache)
+        load_model_burnpack(model, path)
+    elif run.latest() is not None:
         run.load(None, model)
     tp = os.path.join(a.run, "tokenizer.json")
     run_tok = load_tokenizer(tp) if os.path.exists(tp) else load_tokenizer({"type": "byte"})

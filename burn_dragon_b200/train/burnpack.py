@@ -367,3 +367,160 @@ def candidate_paths(path: str, prefer_f16: bool = False) -> list[str]:
     """Load order of the precision variants of ``path``."""
     a, b = precision_path(path, False), precision_path(path, True)
     return [b, a] if prefer_f16 else [a, b]
+
+
+# ------------------------------------------------------------------ bootstrap from a URL
+# Resolve a model's weights from a local cache, fetching them from a remote base URL when
+# the cache has neither a complete parts set nor a monolithic file (the reference's
+# bootstrap, burn_dragon_checkpoint/src/bootstrap.rs:19-330): for each precision variant in
+# the load order, a complete cached parts manifest wins, then a cached monolithic file,
+# then the remote parts manifest (<url>.parts.json) with every part fetched and checked
+# against its size / SHA-256, then the remote monolithic file. URLs are http(s):// or
+# file:// (urllib); writes are atomic (temporary file + rename).
+
+def default_cache_root() -> str:
+    """$BURN_DRAGON_CACHE_DIR, else ~/.cache/burn_dragon/models."""
+    env = os.environ.get("BURN_DRAGON_CACHE_DIR")
+    if env:
+        return env
+    return os.path.join(os.path.expanduser("~"), ".cache", "burn_dragon", "models")
+
+
+def _url_with_suffix(url: str, suffix: str) -> str:
+    head, _, tail = url.rpartition("/")
+    stem, dot, ext = tail.rpartition(".")
+    if dot and not stem.endswith(suffix):
+        tail = f"{stem}{suffix}.{ext}"
+    elif not dot and not tail.endswith(suffix):
+        tail = tail + suffix
+    return f"{head}/{tail}" if head else tail
+
+
+def candidate_urls(base_url: str, prefer_f16: bool = False) -> list[str]:
+    """The remote burnpack URLs in load order (``.bpk`` appended when missing)."""
+    f32 = base_url if base_url.endswith(".bpk") else base_url + ".bpk"
+    f16 = _url_with_suffix(f32, F16_SUFFIX)
+    if f16 == f32:
+        return [f32]
+    return [f16, f32] if prefer_f16 else [f32, f16]
+
+
+def _entry_url(manifest_url: str, entry: str) -> str:
+    if entry.startswith(("http://", "https://", "file://")):
+        return entry
+    base = manifest_url.rpartition("/")[0]
+    return f"{base.rstrip('/')}/{entry.lstrip('/')}" if base else entry.lstrip("/")
+
+
+def _fetch(url: str, timeout: float = 60.0) -> bytes | None:
+    """The body at ``url``, or None when it does not exist (HTTP 404 / missing file)."""
+    import urllib.error
+    import urllib.request
+
+    try:
+        with urllib.request.urlopen(url, timeout=timeout) as r:
+            return r.read()
+    except urllib.error.HTTPError as e:
+        if e.code == 404:
+            return None
+        raise
+    except urllib.error.URLError as e:
+        if isinstance(e.reason, FileNotFoundError) or "No such file" in str(e.reason):
+            return None
+        raise
+
+
+def _write_atomic(path: str, data: bytes) -> None:
+    os.makedirs(os.path.dirname(path) or ".", exist_ok=True)
+    tmp = f"{path}.tmp-{os.getpid()}"
+    with open(tmp, "wb") as f:
+        f.write(data)
+    os.replace(tmp, path)
+
+
+def _part_ok(path: str, entry: dict) -> bool:
+    if not os.path.isfile(path):
+        return False
+    if entry.get("bytes") and os.path.getsize(path) != int(entry["bytes"]):
+        return False
+    return not entry.get("sha256") or _sha256(path) == entry["sha256"]
+
+
+def manifest_complete(manifest_path: str) -> bool:
+    """Every part the manifest lists is present with its size and checksum."""
+    if not os.path.isfile(manifest_path):
+        return False
+    with open(manifest_path) as f:
+        man = json.load(f)
+    root = os.path.dirname(manifest_path)
+    parts = man.get("parts", [])
+    return bool(parts) and all(_part_ok(os.path.join(root, e["path"]), e) for e in parts)
+
+
+def resolve_or_bootstrap(local_base: str, remote_base_url: str, cache_root: str | None = None,
+                         prefer_parts: bool = True, verify_checksums: bool = True, prefer_f16: bool = False,
+                         progress=None) -> str:
+    """The local burnpack path to load (``load_parts`` on its ``.parts.json`` when that is
+    complete, else ``load_burnpack``), fetched from ``remote_base_url`` when not cached. A
+    relative ``local_base`` lives under ``cache_root`` (default ``default_cache_root()``)."""
+    say = progress or (lambda msg: None)
+    root = cache_root or default_cache_root()
+    os.makedirs(root, exist_ok=True)
+    base = local_base if os.path.isabs(local_base) else os.path.join(root, local_base)
+    last = None
+    for local, remote in zip(candidate_paths(base, prefer_f16), candidate_urls(remote_base_url, prefer_f16)):
+        man_path = parts_manifest_path(local)
+        if manifest_complete(man_path):
+            say(f"using cached multipart burnpack {man_path}")
+            return local
+        if os.path.isfile(local):
+            say(f"using cached monolithic burnpack {local}")
+            return local
+        if prefer_parts:
+            murl = remote + ".parts.json"
+            try:
+                body = _fetch(murl)
+            except OSError:
+                body = None
+            if body is not None:
+                _write_atomic(man_path, body)
+                man = json.loads(body)
+                ok = bool(man.get("parts"))
+                for i, e in enumerate(man.get("parts", [])):
+                    p = os.path.join(os.path.dirname(man_path), e["path"])
+                    if _part_ok(p, e):
+                        continue
+                    say(f"downloading burnpack part {i + 1}/{len(man['parts'])}")
+                    try:
+                        data = _fetch(_entry_url(murl, e["path"]))
+                    except OSError:
+                        data = None
+                    if data is None:
+                        ok = False
+                        break
+                    _write_atomic(p, data)
+                    if verify_checksums and not _part_ok(p, e):
+                        ok = False
+                        break
+                if ok and manifest_complete(man_path):
+                    return local
+        say(f"downloading monolithic burnpack {remote}")
+        try:
+            data = _fetch(remote)
+        except OSError as e:
+            last = str(e)
+            continue
+        if data is None:
+            last = f"{remote}: not found"
+            continue
+        _write_atomic(local, data)
+        return local
+    raise FileNotFoundError(last or f"failed to resolve burnpack weights for {base}")
+
+
+def load_resolved(path: str, device=None) -> tuple[dict[str, torch.Tensor], dict]:
+    """Load what ``resolve_or_bootstrap`` returned: its complete parts set, else the file."""
+    man = parts_manifest_path(path)
+    if manifest_complete(man):
+        return load_parts(man, device)
+    return load_burnpack(path, device)
