@@ -93,7 +93,7 @@ def main() -> None:
     ap.add_argument("--seq", type=int, default=512)
     ap.add_argument("--layers", type=int, default=6)
     ap.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per step")
-    ap.add_argument("--comm", default="nvlink", choices=["nccl", "nvlink"],
+    ap.add_argument("--comm", default="nvlink", choices=["nccl", "nvlink", "nvls"],
                     help="gradient step for N > 1: NCCL all-reduce + AdamW, or the NVLink peer-memory "
                          "reduce-scatter + sharded AdamW + all-gather kernel")
     args = ap.parse_args()

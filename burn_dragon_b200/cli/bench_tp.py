@@ -61,10 +61,33 @@ def main() -> None:
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     if rank == 0:
+        # roofline: each rank runs 1/W of the neuron-axis work (the embedding, norms, head and
+        # CE are replicated and counted in full), and per layer and micro-batch the decoder
+        # sum (forward) and the residual-gradient sum (backward) each reduce-scatter and
+        # all-gather an fp32 [M, D] block: 4 (W - 1) / W * M * D * 4 bytes per direction
+        from ..models.bdh_fused import STORES_X
+        from ..train.roofline import measured_peaks, step_totals
+
+        pk = measured_peaks()
+        mb = a.batch // a.micro
+        rows = step_totals(cfg, mb, a.seq, store_x=STORES_X, peaks=pk)["rows"]
+        shared = ("embed + LN", "lm head", "cross-entropy", "d lm head (weight + input)", "AdamW")
+        flop = sum(r["flop"] / (1 if r["kernel"] in shared else world) for r in rows) * a.micro
+        link = 4 * a.layers * (world - 1) / world * mb * a.seq * a.dim * 4 * a.micro
+        t_flop = flop / (pk["bf16_tflops_sustained"] * 1e12)
+        t_link = link / 770e9
+        step_s = ms.item() / 1e3
         toks = a.batch * a.seq
         print(json.dumps({"metric": "train tokens/sec (device-timed, max over ranks) BDH 0.8B neuron-TP",
                           "value": round(toks / (ms.item() / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
                           "ms_per_step": round(ms.item(), 2), "loss": float(loss.item()),
+                          "per_gpu_tflop_per_step": round(flop / 1e12, 3),
+                          "achieved_tflops_per_gpu": round(flop / step_s / 1e12, 1),
+                          "nvlink_gb_per_direction_per_step": round(link / 1e9, 2),
+                          "roofline_ms": round(max(t_flop, t_link) * 1e3, 1),
+                          "frac_roofline": round(max(t_flop, t_link) / step_s, 3),
+                          "peaks": {"bf16_tflops_sustained": pk["bf16_tflops_sustained"], "nvlink_gbs": 770.0,
+                                    "source": pk["source"]},
                           "config": {"d": a.dim, "n": a.neurons, "h": a.heads, "L": a.layers, "T": a.seq,
                                      "global_batch": a.batch, "micro_batches": a.micro, "parallelism": f"tp{world}",
                                      "sequence_parallel": a.sequence_parallel}}),

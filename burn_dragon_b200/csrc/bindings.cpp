@@ -103,6 +103,15 @@ void ssd_chunk_bwd(const at::Tensor& Q, const at::Tensor& K, const at::Tensor& V
 void tp_sum_slots(const at::Tensor& slots, const at::Tensor& out, int64_t world, int64_t n, int64_t slot_stride,
                   const c10::optional<at::Tensor>& add);
 void tp_gather_bytes(std::vector<int64_t> dst, int64_t rank, int64_t offset, int64_t nbytes, int64_t device);
+void ddp_step_nvls(int64_t mc_grad, int64_t mc_shadow, int64_t mc_master, bool grad_bf16, int64_t world, int64_t lo,
+                   int64_t hi, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1,
+                   double b2, double eps, double wd, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef);
+void ddp_reduce_nvls(int64_t mc_grad, bool grad_bf16, int64_t world, int64_t lo, int64_t hi, const at::Tensor& gred,
+                     const at::Tensor& sumsq);
+void ddp_apply_nvls(int64_t mc_shadow, int64_t mc_master, int64_t lo, int64_t hi, const at::Tensor& gred,
+                    const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1, double b2,
+                    double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef);
+void set_debug_bounds(int64_t device, const c10::optional<at::Tensor>& word);
 void percentile_thresholds(const at::Tensor& values, double q, const at::Tensor& out);
 }  // namespace bd
 
@@ -124,6 +133,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tail_bwd", &bd::tail_bwd, py::arg("gin"), py::arg("v"), py::arg("m"), py::arg("st"), py::arg("rows"),
         py::arg("D"), py::arg("gamma"), py::arg("beta"), py::arg("dm16"), py::arg("dv_res"), py::arg("norm_kind") = 0, py::arg("norm_alpha") = py::none(), py::arg("norm_shift") = py::none());
   m.def("sum_rows", &bd::sum_rows);
+  m.def("set_debug_bounds", &bd::set_debug_bounds);
   m.def("cross_entropy", &bd::cross_entropy);
   m.def("symmetrize", &bd::symmetrize);
   m.def("adamw", &bd::adamw);
@@ -146,6 +156,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce_gather", &bd::tp_reduce_gather);
   m.def("tp_scatter_rows", &bd::tp_scatter_rows);
   m.def("ddp_step", &bd::ddp_step);
+  m.def("ddp_step_nvls", &bd::ddp_step_nvls);
+  m.def("ddp_reduce_nvls", &bd::ddp_reduce_nvls);
+  m.def("ddp_apply_nvls", &bd::ddp_apply_nvls);
   m.def("ddp_reduce", &bd::ddp_reduce);
   m.def("ddp_apply", &bd::ddp_apply);
   m.def("ddp_norm_exchange", &bd::ddp_norm_exchange);

@@ -290,12 +290,10 @@ __device__ __forceinline__ float block_sum(float v) {
 // AdamW on 8 elements of the owned slice (hyper = {lr, 1 - b1^t, 1 - b2^t}): the fp32
 // master at flat index i, the moments at shard index s; then the new weights as bf16
 // into every rank's shadow at i.
-template <int W>
-__device__ __forceinline__ void adamw8_gather(const DdpPtrs& pp, int rank, long long i, long long s, float (&g)[8],
-                                              float* __restrict__ master, float* __restrict__ m,
-                                              float* __restrict__ v, float lr, float b1, float b2, float eps,
-                                              float wd, float bc1, float bc2) {
-  float pv[8], mv[8], vv[8];
+__device__ __forceinline__ void adamw8_local(long long i, long long s, const float (&g)[8], float* __restrict__ master,
+                                             float* __restrict__ m, float* __restrict__ v, float lr, float b1,
+                                             float b2, float eps, float wd, float bc1, float bc2, float (&pv)[8]) {
+  float mv[8], vv[8];
   Vec8<float>::load(master + i, pv);
   Vec8<float>::load(m + s, mv);
   Vec8<float>::load(v + s, vv);
@@ -311,12 +309,26 @@ __device__ __forceinline__ void adamw8_gather(const DdpPtrs& pp, int rank, long 
   *reinterpret_cast<float4*>(m + s + 4) = make_float4(mv[4], mv[5], mv[6], mv[7]);
   *reinterpret_cast<float4*>(v + s) = make_float4(vv[0], vv[1], vv[2], vv[3]);
   *reinterpret_cast<float4*>(v + s + 4) = make_float4(vv[4], vv[5], vv[6], vv[7]);
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&pv)[8]) {
   uint4 hb;
   __nv_bfloat162 h;
   h = __floats2bfloat162_rn(pv[0], pv[1]); hb.x = *reinterpret_cast<unsigned int*>(&h);
   h = __floats2bfloat162_rn(pv[2], pv[3]); hb.y = *reinterpret_cast<unsigned int*>(&h);
   h = __floats2bfloat162_rn(pv[4], pv[5]); hb.z = *reinterpret_cast<unsigned int*>(&h);
   h = __floats2bfloat162_rn(pv[6], pv[7]); hb.w = *reinterpret_cast<unsigned int*>(&h);
+  return hb;
+}
+
+template <int W>
+__device__ __forceinline__ void adamw8_gather(const DdpPtrs& pp, int rank, long long i, long long s, float (&g)[8],
+                                              float* __restrict__ master, float* __restrict__ m,
+                                              float* __restrict__ v, float lr, float b1, float b2, float eps,
+                                              float wd, float bc1, float bc2) {
+  float pv[8];
+  adamw8_local(i, s, g, master, m, v, lr, b1, b2, eps, wd, bc1, bc2, pv);
+  const uint4 hb = pack_bf16x8(pv);
 #pragma unroll
   for (int r = 0; r < W; ++r) {
     int dst = rank + r;
@@ -391,6 +403,120 @@ __global__ void __launch_bounds__(256) ddp_apply_kernel(DdpPtrs pp, int rank, lo
 #pragma unroll
     for (int k = 0; k < 8; ++k) g[k] *= c;
     adamw8_gather<W>(pp, rank, i, i - lo, g, master, m, v, lr, b1, b2, eps, wd, bc1, bc2);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// The same step through NVLink SHARP (NVLS) multicast addresses. The gradient, shadow and
+// (gathered) master buffers are bound to one multicast object per buffer across the ranks;
+// `multimem.ld_reduce` on a multicast address returns the sum of every rank's copy of those
+// words, reduced inside the NVSwitch (one read per element crosses this GPU's links instead
+// of W - 1), and `multimem.st` writes one copy that the switch delivers to every rank.
+// bf16 gradients are summed with fp32 accumulation in the switch (.acc::f32) and arrive
+// rounded to bf16 once; fp32 gradients are summed in fp32.
+__device__ __forceinline__ void mc_sum8(const __nv_bfloat16* mc, float (&g)[8]) {
+  uint32_t r[4];
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "l"(mc)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    g[2 * i] = __uint_as_float(r[i] << 16);
+    g[2 * i + 1] = __uint_as_float(r[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ void mc_sum8(const float* mc, float (&g)[8]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(g[4 * h]), "=f"(g[4 * h + 1]), "=f"(g[4 * h + 2]), "=f"(g[4 * h + 3])
+                 : "l"(mc + 4 * h)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mc_store16(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// AdamW on 8 elements from the summed gradient g; the new bf16 weights (and, for a gathered
+// master, the fp32 values) leave through multicast stores.
+__device__ __forceinline__ void adamw8_multicast(long long i, long long s, const float (&g)[8],
+                                                 __nv_bfloat16* mc_shadow, float* mc_master,
+                                                 float* __restrict__ master, float* __restrict__ m,
+                                                 float* __restrict__ v, float lr, float b1, float b2, float eps,
+                                                 float wd, float bc1, float bc2) {
+  float pv[8];
+  adamw8_local(i, s, g, master, m, v, lr, b1, b2, eps, wd, bc1, bc2, pv);
+  mc_store16(mc_shadow + i, pack_bf16x8(pv));
+  if (mc_master != nullptr) {
+    mc_store16(mc_master + i, make_uint4(__float_as_uint(pv[0]), __float_as_uint(pv[1]), __float_as_uint(pv[2]),
+                                         __float_as_uint(pv[3])));
+    mc_store16(mc_master + i + 4, make_uint4(__float_as_uint(pv[4]), __float_as_uint(pv[5]), __float_as_uint(pv[6]),
+                                             __float_as_uint(pv[7])));
+  }
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(256) ddp_step_nvls_kernel(const GT* mc_grad, __nv_bfloat16* mc_shadow,
+                                                            float* mc_master, float inv_world, long long lo,
+                                                            long long hi, float* __restrict__ master,
+                                                            float* __restrict__ m, float* __restrict__ v, float b1,
+                                                            float b2, float eps, float wd,
+                                                            const float* __restrict__ hyper,
+                                                            const float* __restrict__ coef) {
+  const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
+  const float scale = inv_world * (coef ? coef[0] : 1.0f);
+  for (long long i = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
+       i += 8ll * (long long)gridDim.x * blockDim.x) {
+    float g[8];
+    mc_sum8(mc_grad + i, g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] *= scale;
+    adamw8_multicast(i, i - lo, g, mc_shadow, mc_master, master, m, v, lr, b1, b2, eps, wd, bc1, bc2);
+  }
+}
+
+template <typename GT>
+__global__ void __launch_bounds__(256) ddp_reduce_nvls_kernel(const GT* mc_grad, float inv_world, long long lo,
+                                                              long long hi, float* __restrict__ gred,
+                                                              float* __restrict__ sumsq) {
+  float acc = 0.f;
+  for (long long i = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
+       i += 8ll * (long long)gridDim.x * blockDim.x) {
+    float g[8];
+    mc_sum8(mc_grad + i, g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      g[k] *= inv_world;
+      acc += g[k] * g[k];
+    }
+    float* o = gred + (i - lo);
+    *reinterpret_cast<float4*>(o) = make_float4(g[0], g[1], g[2], g[3]);
+    *reinterpret_cast<float4*>(o + 4) = make_float4(g[4], g[5], g[6], g[7]);
+  }
+  const float t = block_sum(acc);
+  if (threadIdx.x == 0) atomicAdd(sumsq, t);
+}
+
+__global__ void __launch_bounds__(256) ddp_apply_nvls_kernel(__nv_bfloat16* mc_shadow, float* mc_master, long long lo,
+                                                             long long hi, const float* __restrict__ gred,
+                                                             float* __restrict__ master, float* __restrict__ m,
+                                                             float* __restrict__ v, float b1, float b2, float eps,
+                                                             float wd, const float* __restrict__ hyper,
+                                                             const float* __restrict__ coef) {
+  const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
+  const float c = coef[0];
+  for (long long i = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
+       i += 8ll * (long long)gridDim.x * blockDim.x) {
+    float g[8];
+    Vec8<float>::load(gred + (i - lo), g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] *= c;
+    adamw8_multicast(i, i - lo, g, mc_shadow, mc_master, master, m, v, lr, b1, b2, eps, wd, bc1, bc2);
   }
 }
 
@@ -782,6 +908,64 @@ void reduce_mean(std::vector<int64_t> grad, std::vector<int64_t> flags, int64_t 
   PeerPtrs pp = make_ptrs(grad, z, z, flags);
   auto st = at::cuda::getCurrentCUDAStream(err.get_device()).stream();
   reduce_mean_kernel<<<148 * 4, 256, 0, st>>>(pp, (int)rank, (int)grad.size(), lo, hi, 1.0f / (float)grad.size());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+
+// NVLS forms of ddp_step / ddp_reduce / ddp_apply: mc_* are multicast addresses of the
+// gradient, shadow and (0: not gathered) master buffers; the rest as in the P2P forms.
+void ddp_step_nvls(int64_t mc_grad, int64_t mc_shadow, int64_t mc_master, bool grad_bf16, int64_t world, int64_t lo,
+                   int64_t hi, const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1,
+                   double b2, double eps, double wd, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef) {
+  TORCH_CHECK(mc_grad != 0 && mc_shadow != 0, "multicast addresses of the gradient and shadow buffers");
+  TORCH_CHECK(lo % 8 == 0 && hi % 8 == 0 && hi >= lo && world >= 1, "shard bounds must be multiples of 8");
+  TORCH_CHECK(master.scalar_type() == at::kFloat && master.numel() >= hi, "fp32 master covering the shard");
+  TORCH_CHECK(m.numel() >= hi - lo && v.numel() >= hi - lo, "moment shards too small");
+  auto st = at::cuda::getCurrentCUDAStream(m.get_device()).stream();
+  const int grid = ddp_grid((hi - lo) / 8);
+  const float* cp = coef ? coef->data_ptr<float>() : nullptr;
+  auto* sh = reinterpret_cast<__nv_bfloat16*>(mc_shadow);
+  auto* mm = reinterpret_cast<float*>(mc_master);
+  if (grad_bf16)
+    ddp_step_nvls_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(mc_grad), sh, mm, 1.0f / (float)world, lo, hi, master.data_ptr<float>(),
+        m.data_ptr<float>(), v.data_ptr<float>(), (float)b1, (float)b2, (float)eps, (float)wd, hyper.data_ptr<float>(),
+        cp);
+  else
+    ddp_step_nvls_kernel<float><<<grid, 256, 0, st>>>(
+        reinterpret_cast<const float*>(mc_grad), sh, mm, 1.0f / (float)world, lo, hi, master.data_ptr<float>(),
+        m.data_ptr<float>(), v.data_ptr<float>(), (float)b1, (float)b2, (float)eps, (float)wd, hyper.data_ptr<float>(),
+        cp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ddp_reduce_nvls(int64_t mc_grad, bool grad_bf16, int64_t world, int64_t lo, int64_t hi, const at::Tensor& gred,
+                     const at::Tensor& sumsq) {
+  TORCH_CHECK(mc_grad != 0 && lo % 8 == 0 && hi % 8 == 0 && gred.numel() >= hi - lo, "shard bounds / reduced shard");
+  auto st = at::cuda::getCurrentCUDAStream(gred.get_device()).stream();
+  C10_CUDA_CHECK(cudaMemsetAsync(sumsq.data_ptr<float>(), 0, sizeof(float), st));
+  const int grid = ddp_grid((hi - lo) / 8);
+  if (grad_bf16)
+    ddp_reduce_nvls_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(mc_grad),
+                                                                1.0f / (float)world, lo, hi, gred.data_ptr<float>(),
+                                                                sumsq.data_ptr<float>());
+  else
+    ddp_reduce_nvls_kernel<float><<<grid, 256, 0, st>>>(reinterpret_cast<const float*>(mc_grad), 1.0f / (float)world,
+                                                        lo, hi, gred.data_ptr<float>(), sumsq.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ddp_apply_nvls(int64_t mc_shadow, int64_t mc_master, int64_t lo, int64_t hi, const at::Tensor& gred,
+                    const at::Tensor& master, const at::Tensor& m, const at::Tensor& v, double b1, double b2,
+                    double eps, double wd, const at::Tensor& hyper, const at::Tensor& coef) {
+  TORCH_CHECK(mc_shadow != 0 && lo % 8 == 0 && hi % 8 == 0, "multicast shadow address / shard bounds");
+  auto st = at::cuda::getCurrentCUDAStream(m.get_device()).stream();
+  const int grid = ddp_grid((hi - lo) / 8);
+  ddp_apply_nvls_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(mc_shadow),
+                                              reinterpret_cast<float*>(mc_master), lo, hi, gred.data_ptr<float>(),
+                                              master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                                              (float)b1, (float)b2, (float)eps, (float)wd, hyper.data_ptr<float>(),
+                                              coef.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -13,6 +13,21 @@ namespace {
 
 constexpr int kWarps = 8;
 
+// Bounds checks of the data-dependent indices (token ids, targets), on only while a debug
+// word is registered for the device (set_debug_bounds; DRAGON_DEBUG_BOUNDS=1 at the Python
+// layer): a token or target outside [0, V) records its code in the word (first one wins)
+// and the access is skipped, so a bad batch is reported instead of faulting.
+constexpr int kBoundsGather = 201;  // ln_fwd embedding gather: token id outside the table
+constexpr int kBoundsTarget = 202;  // cross-entropy target outside the vocabulary
+constexpr int kBoundsEmbedGrad = 203;  // embedding-gradient token id outside the table
+int* g_debug_word[64] = {nullptr};
+
+__device__ __forceinline__ bool in_vocab(int64_t t, long long V, int* dbg, int code) {
+  if (dbg == nullptr || (t >= 0 && t < V)) return true;
+  atomicCAS(dbg, 0, code);
+  return false;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -160,10 +175,11 @@ template <int VPL>
 __global__ void ln_fwd_kernel(const float* __restrict__ x, const int64_t* __restrict__ tokens, long long rows, int D,
                               const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
                               float* __restrict__ y32, __nv_bfloat16* __restrict__ y16, float* __restrict__ mean_out,
-                              float* __restrict__ rstd_out, NormArgs na) {
+                              float* __restrict__ rstd_out, NormArgs na, long long table_rows, int* dbg) {
   const int lane = threadIdx.x % 32;
   const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
   if (row >= rows) return;
+  if (tokens && !in_vocab(tokens[row], table_rows, dbg, kBoundsGather)) return;
   const float* src = tokens ? x + (size_t)tokens[row] * D : x + (size_t)row * D;
   float v[VPL], n[VPL];
 #pragma unroll
@@ -330,10 +346,11 @@ __global__ void sum_rows_kernel(float* __restrict__ out, const float* __restrict
 template <int VPL>
 __global__ void ce_kernel(const float* __restrict__ logits, const int64_t* __restrict__ target,
                           const float* __restrict__ mask, const float* __restrict__ inv_count, long long rows, int V,
-                          float* __restrict__ loss_rows, __nv_bfloat16* __restrict__ dlogits) {
+                          float* __restrict__ loss_rows, __nv_bfloat16* __restrict__ dlogits, int* dbg) {
   const int lane = threadIdx.x % 32;
   const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
   if (row >= rows) return;
+  if (lane == 0) in_vocab(target[row], V, dbg, kBoundsTarget);
   float z[VPL];
   float mx = -INFINITY;
 #pragma unroll
@@ -425,7 +442,9 @@ __global__ void __launch_bounds__(256) embed_grad_kernel(const int64_t* __restri
                                                          const int64_t* __restrict__ perm,
                                                          const int64_t* __restrict__ seg,
                                                          const float* __restrict__ g, long long rows, int D,
-                                                         float* __restrict__ out, int accumulate) {
+                                                         float* __restrict__ out, int accumulate, int V, int* dbg) {
+  if (dbg != nullptr && blockIdx.x == 0 && blockIdx.y == 0)
+    for (long long r = threadIdx.x; r < rows; r += blockDim.x) in_vocab(tokens[r], V, dbg, kBoundsEmbedGrad);
   __shared__ int idx[256];
   __shared__ int wcount[8];
   const int v = blockIdx.x;
@@ -564,7 +583,7 @@ void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_
     ln_fwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(x)>>>(
         x.data_ptr<float>(), tokens ? tokens->data_ptr<int64_t>() : nullptr, rows, (int)D, gamma.data_ptr<float>(),
         beta.data_ptr<float>(), (float)eps, opt_ptr<float>(y32), opt_ptr<__nv_bfloat16>(y16), mean.data_ptr<float>(),
-        rstd.data_ptr<float>(), na);
+        rstd.data_ptr<float>(), na, tokens ? x.size(0) : 0, tokens ? g_debug_word[x.get_device()] : nullptr);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -645,7 +664,8 @@ void cross_entropy(const at::Tensor& logits, const at::Tensor& target, const c10
   dispatch_vpl((int)V, [&](auto vpl) {
     ce_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, 0, cur_stream(logits)>>>(
         logits.data_ptr<float>(), target.data_ptr<int64_t>(), opt_ptr<const float>(mask), inv_count.data_ptr<float>(),
-        rows, (int)V, loss_rows.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dlogits.data_ptr()));
+        rows, (int)V, loss_rows.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dlogits.data_ptr()),
+        g_debug_word[logits.get_device()]);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -695,8 +715,17 @@ void embed_grad(const at::Tensor& tokens, const at::Tensor& g, int64_t rows, int
   dim3 grid((unsigned)V, (unsigned)((D + 255) / 256));
   embed_grad_kernel<<<grid, 256, 0, cur_stream(g)>>>(tokens.data_ptr<int64_t>(), opt_ptr<const int64_t>(perm),
                                                      opt_ptr<const int64_t>(seg), g.data_ptr<float>(), rows, (int)D,
-                                                     out.data_ptr<float>(), accumulate ? 1 : 0);
+                                                     out.data_ptr<float>(), accumulate ? 1 : 0, (int)V,
+                                                     g_debug_word[g.get_device()]);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Register (or with None clear) the int32 word the bounds checks of `device` report into.
+void set_debug_bounds(int64_t device, const c10::optional<at::Tensor>& word) {
+  TORCH_CHECK(device >= 0 && device < 64, "device index");
+  if (word) TORCH_CHECK(word->scalar_type() == at::kInt && word->is_cuda() && word->get_device() == device,
+                        "debug word: an int32 tensor on that device");
+  g_debug_word[device] = word ? word->data_ptr<int>() : nullptr;
 }
 
 void cast_bf16(const at::Tensor& x, const at::Tensor& y) {

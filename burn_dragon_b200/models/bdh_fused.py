@@ -246,6 +246,7 @@ class FusedBDH:
         self.cfg = cfg
         self.ws = ws
         self.mod = _ext.load()
+        G.error_word(ws.v32[0].device)  # (registers the bounds-check word under DRAGON_DEBUG_BOUNDS=1)
 
     # ---------------------------------------------------------------- forward
     def forward(self, p16: dict, p32: dict, tokens: torch.Tensor | None, pos0: int = 0, rho0s=None,

@@ -41,20 +41,43 @@ _ERR: dict[int, torch.Tensor] = {}
 PAIR = os.environ.get("BDH_GEMM_PAIR", "1") != "0"
 
 
+# Bounds checks of data-dependent indices (token ids, CE targets) in the row kernels:
+# DRAGON_DEBUG_BOUNDS=1 registers the device's error word with them, so an id outside the
+# vocabulary is recorded (codes 201-203) and skipped instead of read out of bounds.
+DEBUG_BOUNDS = os.environ.get("DRAGON_DEBUG_BOUNDS", "0") == "1"
+BOUNDS_CODES = {201: "embedding gather: token id outside the table",
+                202: "cross-entropy: target outside the vocabulary",
+                203: "embedding gradient: token id outside the table"}
+
+
 def error_word(device: torch.device) -> torch.Tensor:
-    """Per-device int32 the kernels set when a bounded wait times out (0 = healthy)."""
+    """Per-device int32 the kernels set when a bounded wait times out or (with
+    DRAGON_DEBUG_BOUNDS=1) a bounds check fails (0 = healthy)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     if idx not in _ERR:
-        _ERR[idx] = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[idx] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        if DEBUG_BOUNDS:
+            set_debug_bounds(torch.device("cuda", idx), True)
     return _ERR[idx]
 
 
+def set_debug_bounds(device: torch.device, on: bool) -> None:
+    """Turn the row kernels' bounds checks on `device` on (reporting into its error word)
+    or off."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    word = error_word(device) if on else None
+    _ext.load().set_debug_bounds(idx, word)
+
+
 def check_errors(device: torch.device) -> None:
-    """Raise if any engine launch on `device` recorded a timeout (synchronizes)."""
+    """Raise if any launch on `device` recorded a timeout or a failed bounds check
+    (synchronizes)."""
     e = error_word(device)
     code = int(e.item())
     if code:
         e.zero_()
+        if code in BOUNDS_CODES:
+            raise IndexError(f"bounds check failed (code {code}): {BOUNDS_CODES[code]}")
         raise RuntimeError(f"tcgen05 GEMM engine reported a bounded-wait timeout (code {code})")
 
 

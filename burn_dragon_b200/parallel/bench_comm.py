@@ -5,7 +5,8 @@
 
 Times, with CUDA events on each rank and the max over ranks, (a) the whole NVLinkDDP
 step (bf16 cast, barrier, fused reduce-scatter + AdamW + shadow all-gather, barrier),
-(b) the same with global-norm clipping, and (c) the NCCL baseline: all-reduce (mean) of
+(b) the same with global-norm clipping (``--transport nvls``: both through NVLink multicast
+objects), and (c) the NCCL baseline: all-reduce (mean) of
 the fp32 gradients followed by the fused AdamW on every rank. Reports the NVLink bytes
 each rank moves and the achieved fraction of the roofline: (W-1)/W * P * 2 bytes in
 each direction at 770 GB/s per direction (the measured peer-copy rate of this machine
@@ -45,6 +46,8 @@ def main() -> None:
     ap.add_argument("--params", type=int, default=25_300_000)
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--grad-dtype", default="bf16", choices=["bf16", "fp32"])
+    ap.add_argument("--transport", default="p2p", choices=["p2p", "nvls"],
+                    help="peer loads / stores, or NVLink multicast (in-switch sum, multicast stores)")
     a = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -59,7 +62,7 @@ def main() -> None:
         _scratch = torch.zeros(4, device="cuda")
 
     dev = torch.device("cuda", local)
-    ddp = NVLinkDDP(a.params, dev, grad_dtype=a.grad_dtype)
+    ddp = NVLinkDDP(a.params, dev, grad_dtype=a.grad_dtype, transport=a.transport)
     ddp.grad.normal_()
     ddp.param.normal_()
     opt = _Opt()
@@ -83,7 +86,7 @@ def main() -> None:
     link_bytes = (world - 1) / world * ddp.numel * max(esz, 2)  # per direction, the larger of in / out
     roof_us = link_bytes / (LINK_GBS * 1e9) * 1e6
     if rank == 0:
-        print(json.dumps({"world": world, "params": ddp.numel, "grad_dtype": a.grad_dtype,
+        print(json.dumps({"world": world, "params": ddp.numel, "grad_dtype": a.grad_dtype, "transport": a.transport,
                           "nvlink_step_us": round(us_step, 1), "nvlink_step_clip_us": round(us_clip, 1),
                           "nccl_allreduce_adamw_us": round(us_nccl, 1),
                           "link_bytes_per_direction_mb": round(link_bytes / 1e6, 1),

@@ -53,10 +53,18 @@ class NVLinkDDP:
     FLAG_WORDS = 512
 
     def __init__(self, numel: int, device: torch.device, group=None, grad_dtype: str = "bf16",
-                 buckets: list[tuple[int, int]] | None = None, master_buckets: set[int] | None = None):
+                 buckets: list[tuple[int, int]] | None = None, master_buckets: set[int] | None = None,
+                 transport: str = "p2p"):
         """``master_buckets``: buckets whose fp32 master the model reads in its forward /
         backward (embedding, norms, scaffold adapters); their new fp32 values are
-        all-gathered with the shadow. Default: every bucket."""
+        all-gathered with the shadow. Default: every bucket.
+
+        ``transport``: "p2p" (CUDA-IPC buffers; the owner loads every peer's gradient and
+        stores into every peer's shadow) or "nvls" (the buffers come from torch's symmetric
+        memory with one NVLink multicast object each: the owner's gradient sum is one
+        ``multimem.ld_reduce`` reduced inside the NVSwitch, its new weights one
+        ``multimem.st`` delivered to every rank). The barriers use plain peer stores in
+        both."""
         if not dist.is_initialized():
             raise RuntimeError("NVLinkDDP needs an initialised process group")
         if grad_dtype not in ("bf16", "fp32"):
@@ -92,20 +100,28 @@ class NVLinkDDP:
         self.shard = -(-self.numel // self.world)
         gbytes = self.numel * (2 if self.grad_bf16 else 4)
         sizes = {"gsym": gbytes, "shadow": self.numel * 2, "flags": self.FLAG_WORDS * 4, "param": self.numel * 4}
-        self._own = {k: mod.sym_alloc(b, self.dev) for k, b in sizes.items()}
-        handles = {k: mod.ipc_handle(p, self.dev) for k, p in self._own.items()}
-        gathered: list = [None] * self.world
-        dist.all_gather_object(gathered, handles, group=group)
+        if transport not in ("p2p", "nvls"):
+            raise ValueError("transport must be 'p2p' or 'nvls'")
+        self.transport = transport
         self.ptrs: dict[str, list[int]] = {k: [] for k in sizes}
         self._opened: list[int] = []
-        for r in range(self.world):
-            for k in sizes:
-                if r == self.rank:
-                    self.ptrs[k].append(self._own[k])
-                else:
-                    p = mod.ipc_open(gathered[r][k], self.dev)
-                    self._opened.append(p)
-                    self.ptrs[k].append(p)
+        self.mc: dict[str, int] = {}
+        self._symm: dict = {}
+        if transport == "nvls":
+            self._own = self._nvls_alloc(sizes, group)
+        else:
+            self._own = {k: mod.sym_alloc(b, self.dev) for k, b in sizes.items()}
+            handles = {k: mod.ipc_handle(p, self.dev) for k, p in self._own.items()}
+            gathered: list = [None] * self.world
+            dist.all_gather_object(gathered, handles, group=group)
+            for r in range(self.world):
+                for k in sizes:
+                    if r == self.rank:
+                        self.ptrs[k].append(self._own[k])
+                    else:
+                        p = mod.ipc_open(gathered[r][k], self.dev)
+                        self._opened.append(p)
+                        self.ptrs[k].append(p)
         # local fp32 gradient (written by the backward) and fp32 master (current on the
         # owned slices)
         self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
@@ -125,6 +141,34 @@ class NVLinkDDP:
         self._launched: set[int] = set()
         self._opt = None
         dist.barrier(group=group)
+
+    def _nvls_alloc(self, sizes: dict, group) -> dict:
+        """Allocate every region from torch's symmetric memory and rendezvous it across the
+        group: the peers' addresses fill ``ptrs``, the multicast address ``mc``. Raises when
+        the system has no multicast support (no NVSwitch multicast objects)."""
+        import torch.distributed._symmetric_memory as symm
+
+        grp = group if group is not None else dist.group.WORLD
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            try:
+                symm.enable_symm_mem_for_group(grp.group_name)
+            except Exception:  # noqa: BLE001 - newer releases enable every group
+                pass
+        own = {}
+        for k, nbytes in sizes.items():
+            t = symm.empty(-(-nbytes // 16) * 16, dtype=torch.uint8, device=self.device)
+            t.zero_()
+            h = symm.rendezvous(t, grp)
+            if k != "flags":
+                mc = int(h.multicast_ptr)  # 0 where the device / driver has no multicast support
+                if mc == 0:
+                    raise RuntimeError("transport='nvls' needs NVLink multicast (NVSwitch) support on every rank")
+                self.mc[k] = mc
+            self._symm[k] = (t, h)
+            self.ptrs[k] = [int(x) for x in h.buffer_ptrs]
+            own[k] = int(t.data_ptr())
+        torch.cuda.synchronize(self.device)
+        return own
 
     # ---------------------------------------------------------------- per-step protocol
     def begin_step(self, opt) -> None:
@@ -155,6 +199,17 @@ class NVLinkDDP:
         g, sh = self.ptrs["gsym"], self.ptrs["shadow"]
         mo, n = bk["moff"], hi - lo
         gm = self.ptrs["param"] if b in self.master_buckets else []
+        if self.transport == "nvls":
+            mcm = self.mc["param"] if b in self.master_buckets else 0
+            if opt.clip is None:
+                mod.ddp_step_nvls(self.mc["gsym"], self.mc["shadow"], mcm, self.grad_bf16, self.world, lo, hi,
+                                  self.param, self.m[mo:mo + n], self.v[mo:mo + n], opt.b1, opt.b2, opt.eps, opt.wd,
+                                  opt._hyper, None)
+            else:
+                part = self._bucket_sumsq(b)
+                mod.ddp_reduce_nvls(self.mc["gsym"], self.grad_bf16, self.world, lo, hi, self._gred[mo:mo + n], part)
+                self._sumsq.add_(part)
+            return
         if opt.clip is None:
             mod.ddp_step(g, sh, self.grad_bf16, self.rank, lo, hi, self.param, self.m[mo:mo + n], self.v[mo:mo + n],
                          opt.b1, opt.b2, opt.eps, opt.wd, opt._hyper, None, gm)
@@ -199,7 +254,13 @@ class NVLinkDDP:
             g, sh = self.ptrs["gsym"], self.ptrs["shadow"]
             for b, bk in enumerate(self.buckets):
                 lo, hi, mo = bk["lo"], bk["hi"], bk["moff"]
-                if hi > lo:
+                if hi > lo and self.transport == "nvls":
+                    n = hi - lo
+                    mcm = self.mc["param"] if b in self.master_buckets else 0
+                    mod.ddp_apply_nvls(self.mc["shadow"], mcm, lo, hi, self._gred[mo:mo + n], self.param,
+                                       self.m[mo:mo + n], self.v[mo:mo + n], opt.b1, opt.b2, opt.eps, opt.wd,
+                                       opt._hyper, self.norm_out)
+                elif hi > lo:
                     n = hi - lo
                     gm = self.ptrs["param"] if b in self.master_buckets else []
                     mod.ddp_apply(g, sh, self.rank, lo, hi, self._gred[mo:mo + n], self.param, self.m[mo:mo + n],

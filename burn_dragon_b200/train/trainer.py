@@ -101,10 +101,12 @@ class Trainer:
                 # autograd over the PyTorch path (cuBLAS / ATen kernels), same step semantics
                 warnings.warn(f"fused BDH kernels do not implement {why}; training through the PyTorch path")
                 self.fused = False
-        # comm: None / "nccl" (all-reduce + full AdamW on every rank) or "nvlink"
-        # (symmetric-memory reduce-scatter + sharded AdamW + all-gather, parallel.ddp)
+        # comm: None / "nccl" (all-reduce + full AdamW on every rank), "nvlink"
+        # (symmetric-memory reduce-scatter + sharded AdamW + all-gather by peer loads and
+        # stores, parallel.ddp) or "nvls" (the same step through NVLink multicast objects:
+        # in-switch reduction and multicast stores)
         self.comm = None
-        if comm == "nvlink" and self.world > 1:
+        if comm in ("nvlink", "nvls") and self.world > 1:
             from ..parallel.ddp import NVLinkDDP
 
             if grad_clip_value is not None:
@@ -116,7 +118,7 @@ class Trainer:
             master_b = {len(buckets) - 1} if buckets else None
             self.comm = NVLinkDDP(self.model.store.numel, self.device, group=self.dp_group,
                                   grad_dtype=os.environ.get("BDH_DDP_GRAD_DTYPE", "bf16"), buckets=buckets,
-                                  master_buckets=master_b)
+                                  master_buckets=master_b, transport="nvls" if comm == "nvls" else "p2p")
             self.model.attach_buffers(self.comm.param, self.comm.grad, self.comm.shadow)
             # overlap the per-bucket gradient exchange with the rest of the backward
             # (BDH_DDP_OVERLAP=0: one exchange after the backward)
