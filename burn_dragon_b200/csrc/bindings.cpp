@@ -21,7 +21,8 @@ void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_
 at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
                   int64_t rows, int64_t D, const at::Tensor& gamma, int64_t remap_T, int64_t remap_H,
                   const c10::optional<at::Tensor>& dx16, const c10::optional<at::Tensor>& dx32, int64_t norm_kind,
-            const c10::optional<at::Tensor>& norm_alpha, const c10::optional<at::Tensor>& norm_shift);
+            const c10::optional<at::Tensor>& norm_alpha, const c10::optional<at::Tensor>& norm_shift,
+            const c10::optional<at::Tensor>& tokens);
 void tail_fwd(const at::Tensor& partial, int64_t nsplit, int64_t split_stride, const at::Tensor& v, int64_t rows,
               int64_t D, const at::Tensor& gamma, const at::Tensor& beta, double eps,
               const c10::optional<at::Tensor>& m_out, const at::Tensor& vout32,
@@ -125,7 +126,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("beta"), py::arg("eps"), py::arg("y32"), py::arg("y16"), py::arg("mean"), py::arg("rstd"), py::arg("norm_kind") = 0, py::arg("norm_alpha") = py::none(), py::arg("norm_shift") = py::none());
   m.def("ln_bwd", &bd::ln_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"), py::arg("rows"),
         py::arg("D"), py::arg("gamma"), py::arg("remap_T"), py::arg("remap_H"), py::arg("dx16"), py::arg("dx32"),
-        py::arg("norm_kind") = 0, py::arg("norm_alpha") = py::none(), py::arg("norm_shift") = py::none());
+        py::arg("norm_kind") = 0, py::arg("norm_alpha") = py::none(), py::arg("norm_shift") = py::none(),
+        py::arg("tokens") = py::none());
   m.def("embed_grad", &bd::embed_grad);
   m.def("tail_fwd", &bd::tail_fwd, py::arg("partial"), py::arg("nsplit"), py::arg("split_stride"), py::arg("v"),
         py::arg("rows"), py::arg("D"), py::arg("gamma"), py::arg("beta"), py::arg("eps"), py::arg("m_out"),

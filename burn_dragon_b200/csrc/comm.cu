@@ -460,6 +460,8 @@ __device__ __forceinline__ void adamw8_multicast(long long i, long long s, const
   }
 }
 
+constexpr int kNvlsUnroll = 4;
+
 template <typename GT>
 __global__ void __launch_bounds__(256) ddp_step_nvls_kernel(const GT* mc_grad, __nv_bfloat16* mc_shadow,
                                                             float* mc_master, float inv_world, long long lo,
@@ -470,13 +472,23 @@ __global__ void __launch_bounds__(256) ddp_step_nvls_kernel(const GT* mc_grad, _
                                                             const float* __restrict__ coef) {
   const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
   const float scale = inv_world * (coef ? coef[0] : 1.0f);
-  for (long long i = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
-       i += 8ll * (long long)gridDim.x * blockDim.x) {
-    float g[8];
-    mc_sum8(mc_grad + i, g);
+  // kNvlsUnroll switch reductions in flight per thread before the first is used (their
+  // round trip through the NVSwitch is the latency to cover)
+  const long long stride = 8ll * (long long)gridDim.x * blockDim.x;
+  for (long long i0 = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i0 < hi;
+       i0 += kNvlsUnroll * stride) {
+    float g[kNvlsUnroll][8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) g[k] *= scale;
-    adamw8_multicast(i, i - lo, g, mc_shadow, mc_master, master, m, v, lr, b1, b2, eps, wd, bc1, bc2);
+    for (int u = 0; u < kNvlsUnroll; ++u)
+      if (i0 + u * stride < hi) mc_sum8(mc_grad + i0 + u * stride, g[u]);
+#pragma unroll
+    for (int u = 0; u < kNvlsUnroll; ++u) {
+      const long long i = i0 + u * stride;
+      if (i >= hi) break;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) g[u][k] *= scale;
+      adamw8_multicast(i, i - lo, g[u], mc_shadow, mc_master, master, m, v, lr, b1, b2, eps, wd, bc1, bc2);
+    }
   }
 }
 
@@ -485,18 +497,26 @@ __global__ void __launch_bounds__(256) ddp_reduce_nvls_kernel(const GT* mc_grad,
                                                               long long hi, float* __restrict__ gred,
                                                               float* __restrict__ sumsq) {
   float acc = 0.f;
-  for (long long i = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i < hi;
-       i += 8ll * (long long)gridDim.x * blockDim.x) {
-    float g[8];
-    mc_sum8(mc_grad + i, g);
+  const long long stride = 8ll * (long long)gridDim.x * blockDim.x;
+  for (long long i0 = lo + 8ll * ((long long)blockIdx.x * blockDim.x + threadIdx.x); i0 < hi;
+       i0 += kNvlsUnroll * stride) {
+    float g[kNvlsUnroll][8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      g[k] *= inv_world;
-      acc += g[k] * g[k];
+    for (int u = 0; u < kNvlsUnroll; ++u)
+      if (i0 + u * stride < hi) mc_sum8(mc_grad + i0 + u * stride, g[u]);
+#pragma unroll
+    for (int u = 0; u < kNvlsUnroll; ++u) {
+      const long long i = i0 + u * stride;
+      if (i >= hi) break;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        g[u][k] *= inv_world;
+        acc += g[u][k] * g[u][k];
+      }
+      float* o = gred + (i - lo);
+      *reinterpret_cast<float4*>(o) = make_float4(g[u][0], g[u][1], g[u][2], g[u][3]);
+      *reinterpret_cast<float4*>(o + 4) = make_float4(g[u][4], g[u][5], g[u][6], g[u][7]);
     }
-    float* o = gred + (i - lo);
-    *reinterpret_cast<float4*>(o) = make_float4(g[0], g[1], g[2], g[3]);
-    *reinterpret_cast<float4*>(o + 4) = make_float4(g[4], g[5], g[6], g[7]);
   }
   const float t = block_sum(acc);
   if (threadIdx.x == 0) atomicAdd(sumsq, t);

@@ -207,7 +207,7 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
                               const float* __restrict__ mean_in, const float* __restrict__ rstd_in, long long rows,
                               int D, const float* __restrict__ gamma, int remap_T, int remap_H,
                               __nv_bfloat16* __restrict__ dx16, float* __restrict__ dx32, float* __restrict__ part,
-                              NormArgs na) {
+                              NormArgs na, const int64_t* __restrict__ tokens, long long table_rows, int* dbg) {
   const int lane = threadIdx.x % 32;
   float gam[VPL], dg[VPL], db[VPL], da[VPL], ds[VPL];
 #pragma unroll
@@ -219,10 +219,13 @@ __global__ void ln_bwd_kernel(const float* __restrict__ dy, const float* __restr
        row += (long long)gridDim.x * kWarps) {
     float g[VPL], xr[VPL], n[VPL], dx[VPL];
     const float mean = mean_in[row], rstd = rstd_in[row];
+    // with `tokens`, x is the embedding table and row r's input is its row tokens[r]
+    const bool ok = tokens == nullptr || in_vocab(tokens[row], table_rows, dbg, kBoundsGather);
+    const float* xrow = tokens ? x + (size_t)(ok ? tokens[row] : 0) * D : x + (size_t)row * D;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       g[i] = dy[(size_t)row * D + lane + 32 * i];
-      xr[i] = x[(size_t)row * D + lane + 32 * i];
+      xr[i] = xrow[lane + 32 * i];
     }
     norm_row_saved<VPL>(xr, mean, rstd, na, n);
     norm_backward_row<VPL>(g, xr, n, gam, rstd, D, na, dx, dg, db, da, ds);
@@ -592,7 +595,7 @@ void ln_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& tokens, int64_
 at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
                   int64_t rows, int64_t D, const at::Tensor& gamma, int64_t remap_T, int64_t remap_H,
                   const c10::optional<at::Tensor>& dx16, const c10::optional<at::Tensor>& dx32, int64_t norm_kind, const c10::optional<at::Tensor>& norm_alpha,
-            const c10::optional<at::Tensor>& norm_shift) {
+            const c10::optional<at::Tensor>& norm_shift, const c10::optional<at::Tensor>& tokens) {
   c10::cuda::CUDAGuard g(x.get_device());
   const NormArgs na = norm_args(norm_kind, norm_alpha, norm_shift);
   const int blocks = part_blocks(rows);
@@ -603,7 +606,8 @@ at::Tensor ln_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& m
     ln_bwd_kernel<decltype(vpl)::value><<<blocks, kWarps * 32, kWarps * R * D * sizeof(float), cur_stream(x)>>>(
         dy.data_ptr<float>(), x.data_ptr<float>(), mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, (int)D,
         gamma.data_ptr<float>(), (int)remap_T, (int)remap_H, opt_ptr<__nv_bfloat16>(dx16), opt_ptr<float>(dx32),
-        part.data_ptr<float>(), na);
+        part.data_ptr<float>(), na, tokens ? tokens->data_ptr<int64_t>() : nullptr, tokens ? x.size(0) : 0,
+        tokens ? g_debug_word[x.get_device()] : nullptr);
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return part;

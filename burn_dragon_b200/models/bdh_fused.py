@@ -137,7 +137,7 @@ class FusedWorkspace:
         self.yn16 = per_layer(lambda: e(M, N, dt=bf16))
         self.m32 = per_layer(lambda: e(M, D))
         self.tst = per_layer(lambda: e(M, 4))
-        self.emb_rows = e(M, D)
+        self._tok = None
         self.emean, self.erstd = e(M), e(M)
         self.logits = e(M, V)
         self.dlogits16 = e(M, V, dt=bf16)
@@ -189,6 +189,18 @@ class FusedWorkspace:
         self.rho_flip = 0
         self.has_rho0 = False
         self.qscaled: torch.Tensor | None = None
+
+    def token_ids(self, tokens: torch.Tensor) -> torch.Tensor:
+        """The step's token ids as a flat contiguous int64 tensor (the caller's tensor when it
+        already is one, else a copy into a workspace buffer, so a captured graph keeps one
+        address)."""
+        t = tokens.reshape(-1)
+        if t.dtype == torch.int64 and t.is_contiguous():
+            return t
+        if self._tok is None or self._tok.numel() != t.numel():
+            self._tok = torch.empty(t.numel(), dtype=torch.int64, device=t.device)
+        self._tok.copy_(t)
+        return self._tok
 
     def rope_tab(self, pos0: int, staged: bool = False):
         """The half2 (cos, sin) table of this workspace's positions pos0 .. pos0 + T - 1
@@ -309,9 +321,9 @@ class FusedBDH:
         nk = norm_kwargs(cfg, p32)
         thr, thr_y = cfg.thresholds()
         if v_in is None:
-            tok = tokens.reshape(-1)
-            torch.index_select(p32["embed"], 0, tok, out=ws.emb_rows)
-            mod.ln_fwd(ws.emb_rows, None, M, D, p32["norm_gamma"], p32["norm_beta"], eps, ws.v32[0], ws.v16[0],
+            # the embedding rows are gathered inside the norm kernel (and again in its backward)
+            tok = ws.token_ids(tokens)
+            mod.ln_fwd(p32["embed"], tok, M, D, p32["norm_gamma"], p32["norm_beta"], eps, ws.v32[0], ws.v16[0],
                        ws.emean, ws.erstd, **nk)
         else:
             ws.v32[0].copy_(v_in.reshape(M, D))
@@ -546,8 +558,9 @@ class FusedBDH:
             demb = ws.dv_res  # reuse as fp32 [M, D] scratch
             if sp:
                 rows = own.stop - own.start
-                head_parts.append(mod.ln_bwd(dv[own], ws.emb_rows[own], ws.emean[own], ws.erstd[own], rows, D, gam,
-                                             0, 0, None, demb[own], **nk))
+                tok = ws.token_ids(tokens)[own]
+                head_parts.append(mod.ln_bwd(dv[own], p32["embed"], ws.emean[own], ws.erstd[own], rows, D, gam,
+                                             0, 0, None, demb[own], **nk, tokens=tok))
                 ge = torch.empty_like(g32["embed"])
                 embed_grad(mod, tokens.reshape(-1)[own].contiguous(), demb[own], ge, accumulate=False)
                 tp.all_reduce(ge)  # every rank's own-row contributions
@@ -556,7 +569,8 @@ class FusedBDH:
                 else:
                     g32["embed"].copy_(ge)
             else:
-                parts.append(mod.ln_bwd(dv, ws.emb_rows, ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb, **nk))
+                parts.append(mod.ln_bwd(dv, p32["embed"], ws.emean, ws.erstd, M, D, gam, 0, 0, None, demb, **nk,
+                                        tokens=ws.token_ids(tokens)))
                 embed_grad(mod, tokens.reshape(-1), demb, g32["embed"], accumulate=accumulate)
         elif not accumulate:
             g32["embed"].zero_()
