@@ -66,6 +66,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The same test with a suspend-time hint: a thread whose phase has not completed sleeps
+// in the barrier (woken as soon as the phase completes, or after at most `hint_ns`)
+// instead of spinning, so waiting warps stop taking issue slots from the warps that compute.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Suspend hint of the bounded waits (ns). Each failed test sleeps at most this long, and
+// the deadline and abort flag are checked after every one.
+constexpr uint32_t kWaitSleepNs = 1000000u;
+
 // Bounded wait. Returns false (after recording `code`) when the deadline passes or when
 // another role of this CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
@@ -73,16 +92,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
                                                   int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitBudgetNs) {
-        *abort_flag = 1;
-        if (err_word) atomicCAS(err_word, 0, code);
-        return false;
-      }
+    if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitBudgetNs) {
+      *abort_flag = 1;
+      if (err_word) atomicCAS(err_word, 0, code);
+      return false;
     }
   }
 }
