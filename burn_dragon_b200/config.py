@@ -599,6 +599,8 @@ class OptimizerConfig:
 class ParallelConfig:
     mode: str = "single"  # single | ddp | fsdp | tensor_parallel_neuron | hybrid_2d | pipeline
     world_size: int | None = None
+    # data: shard-the-loader keys of the reference, plus transport = "p2p" | "nvls" (the
+    # NVLink data-parallel step's exchange: peer loads / stores or NVLink multicast)
     data: dict[str, Any] = field(default_factory=dict)
     tensor: dict[str, Any] = field(default_factory=dict)
     pipeline: dict[str, Any] = field(default_factory=dict)
@@ -1051,6 +1053,8 @@ class TrainingConfig:
         p = self.parallel.mode
         if p not in ("single", "ddp", "fsdp", "tensor_parallel_neuron", "hybrid_2d", "pipeline"):
             raise ValueError(f"unknown parallel.mode {p!r}")
+        if self.parallel.data.get("transport", "p2p") not in ("p2p", "nvls"):
+            raise ValueError("parallel.data.transport must be 'p2p' or 'nvls'")
         if p in ("tensor_parallel_neuron", "hybrid_2d"):
             tpc = self.parallel.tensor
             if tpc.get("axis", "neuron") != "neuron":

@@ -13,3 +13,14 @@ def test_fused_support_matrix():
         assert fused_unsupported(DragonConfig(**base, dropout=0.0, norm_kind=kind)) is None
     assert fused_unsupported(DragonConfig(**base, dropout=0.0, rotary_embedding="pope")) == "PoPE"
     assert fused_unsupported(DragonConfig(**base, dropout=0.0, tie_input_output_embeddings=True)) == "a tied lm_head"
+
+
+def test_data_transport_key_is_validated():
+    from burn_dragon_b200.config import training_config_from_dict
+
+    cfg = training_config_from_dict({"parallel": {"mode": "ddp", "data": {"transport": "nvls"}}})
+    cfg.validate()
+    import pytest
+
+    with pytest.raises(ValueError, match="transport"):
+        training_config_from_dict({"parallel": {"mode": "ddp", "data": {"transport": "ib"}}}).validate()
