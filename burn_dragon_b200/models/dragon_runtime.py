@@ -342,7 +342,8 @@ class DragonRuntime(nn.Module):
             setattr(ls, attr, S)
             return out * self.gdn2.output_scale
         q = self._rotate(x, pos, fixed)
-        a, rho = R.linear_attention_dense(q, v[:, None], rho0=rho0, decay=self._decay, need_state=True)
+        a, rho = R.linear_attention_chunked(q, v[:, None], rho0=rho0, decay=self._decay, need_state=True,
+                                            chunk=getattr(self.cfg, "dense_score_row_chunk", 0) or 0)
         setattr(ls, attr, rho)
         return a
 

@@ -136,6 +136,27 @@ def linear_attention_dense(q, v, rho0=None, decay=None, need_state: bool = True)
     return c, rho
 
 
+def linear_attention_chunked(q, v, rho0=None, decay=None, need_state: bool = True, chunk: int = 512):
+    """The dense-score form over row chunks of ``chunk`` positions with the state carried
+    between them: chunk c computes its causal scores against itself only and reads the
+    state that enters it (rho_c = gamma^c0 rho0 + sum_{j < c0} gamma^(c0-j) q_j^T v_j), so the
+    scores take O(T chunk) memory instead of O(T^2) and the result (and its autograd
+    gradient, which flows through the carried states) equals ``linear_attention_dense``.
+    The reference's dense executor chunks its rows the same way (``dense_score_row_chunk``,
+    burn_dragon_core/src/model/sequence/config.rs)."""
+    T = q.shape[2]
+    if chunk <= 0 or T <= chunk:
+        return linear_attention_dense(q, v, rho0=rho0, decay=decay, need_state=need_state)
+    outs, rho = [], rho0
+    for c0 in range(0, T, chunk):
+        c1 = min(T, c0 + chunk)
+        vc = v[:, :, c0:c1]
+        a, rho = linear_attention_dense(q[:, :, c0:c1], vc, rho0=rho, decay=decay,
+                                        need_state=need_state or c1 < T)
+        outs.append(a)
+    return torch.cat(outs, dim=2), (rho if need_state else None)
+
+
 def linear_attention_dense_vjp(q, v, dc, rho0=None, decay=None, drho=None):
     """Analytic backward of ``linear_attention_dense``: the data flow the fused backward
     runs on tensor cores (dense_causal_attention/backward_runtime.rs:36-148 in the
@@ -177,11 +198,15 @@ def layer_norm(x, gamma, beta, eps):
 
 
 def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, decay, rho0=None,
-              need_state=False, dropout=0.0, training=False, norm=None, pope=False, attention=None, thr_y=None):
+              need_state=False, dropout=0.0, training=False, norm=None, pope=False, attention=None, thr_y=None,
+              row_chunk: int = 0):
     """One shared-weight BDH layer. v [B,T,D]; enc/enc_v [H,D,Nh]; dec [N,D].
     ``norm`` overrides the LayerNorm (other DragonNorm kinds); ``pope`` switches the
     query embedding to PoPE (``freqs`` then holds the PoPE frequencies). ``thr`` is the
     x ReLU threshold, ``thr_y`` the y one (default: the same).
+
+    ``row_chunk`` > 0: the attention runs over row chunks of that many positions with
+    the state carried between them (``linear_attention_chunked``).
 
     Returns (v', rho_T or None, aux dict of the intermediate activations).
     """
@@ -198,7 +223,8 @@ def bdh_layer(v, enc, enc_v, dec, gamma, beta, *, eps, thr, freqs, positions, de
     if attention is not None:  # e.g. context parallelism: the sequence is split over ranks
         a, rho = attention(q, v[:, None])
     else:
-        a, rho = linear_attention_dense(q, v[:, None], rho0=rho0, decay=decay, need_state=need_state)
+        a, rho = linear_attention_chunked(q, v[:, None], rho0=rho0, decay=decay, need_state=need_state,
+                                          chunk=row_chunk)
     a = nf(a)  # [B,H,T,D]
     y = torch.relu(torch.einsum("bhtd,hdn->bhtn", a, enc_v) - (thr if thr_y is None else thr_y))
     yn = x * y
@@ -258,7 +284,8 @@ def bdh_forward(tokens, params: dict, cfg, rho0s=None, pos0: int = 0, need_state
                               eps=cfg.norm_eps, thr=cfg.thresholds()[0], thr_y=cfg.thresholds()[1], freqs=fq,
                               positions=positions,
                               decay=decay, rho0=r0, need_state=need_state, dropout=cfg.dropout,
-                              training=training, norm=norm, pope=cfg.rotary_embedding == "pope")
+                              training=training, norm=norm, pope=cfg.rotary_embedding == "pope",
+                              row_chunk=getattr(cfg, "dense_score_row_chunk", 0) or 0)
         if dyn:
             R = MHC.dynamic_merge(R, v, w_out)
         elif streams > 1:

@@ -48,3 +48,26 @@ def test_bdh_layer_gradcheck():
                            decay=None)[0]
 
     assert torch.autograd.gradcheck(f, (v, enc, enc_v, dec, gamma, beta), eps=1e-6, atol=1e-5)
+
+
+@pytest.mark.parametrize("decay", [False, True])
+@pytest.mark.parametrize("T,chunk", [(40, 16), (48, 16), (33, 7)])
+def test_row_chunked_attention_matches_dense(decay, T, chunk):
+    """Row-chunked dense scores with the state carried between chunks: same output, final
+    state and gradients (through the carried states) as the full dense form, in fp64."""
+    from burn_dragon_b200.models import reference as R
+
+    g = torch.Generator().manual_seed(T + chunk)
+    B, H, N, D = 2, 3, 8, 5
+    q = torch.randn(B, H, T, N, generator=g, dtype=torch.float64, requires_grad=True)
+    v = torch.randn(B, 1, T, D, generator=g, dtype=torch.float64, requires_grad=True)
+    rho0 = torch.randn(B, H, N, D, generator=g, dtype=torch.float64, requires_grad=True)
+    dec = torch.tensor([0.9, 0.97, 0.8], dtype=torch.float64) if decay else None
+    a1, r1 = R.linear_attention_dense(q, v, rho0=rho0, decay=dec)
+    a2, r2 = R.linear_attention_chunked(q, v, rho0=rho0, decay=dec, chunk=chunk)
+    assert torch.allclose(a1, a2, atol=1e-10) and torch.allclose(r1, r2, atol=1e-10)
+    w1, w2 = torch.randn_like(a1), torch.randn_like(r1)
+    g1 = torch.autograd.grad((a1 * w1).sum() + (r1 * w2).sum(), (q, v, rho0))
+    g2 = torch.autograd.grad((a2 * w1).sum() + (r2 * w2).sum(), (q, v, rho0))
+    for x, y in zip(g1, g2):
+        assert torch.allclose(x, y, atol=1e-9)
